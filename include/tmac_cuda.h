@@ -1,0 +1,144 @@
+/*
+ * tmac_cuda.h -- C ABI of libtmac_cuda.so, the B200 (sm_100a) replacement for
+ * the FPGA compute cores that liuwantao3/tmac-zynq-fpga drives from its host
+ * engine (sim/tmac_gguf.cpp) and models in sim/fpga_sim.hpp.
+ *
+ * Plain C: opaque handles, plain pointers, sizes and int status codes.  No
+ * CUDA runtime types appear here; streams are passed as `void*`
+ * (a cudaStream_t, NULL = the legacy default stream).
+ *
+ * Numerics: every GEMV reproduces the reference's CPU result bit for bit
+ * (int64 row / per-unit sums exact, fp32 outputs identical), including the
+ * per-call activation quantisation x_q = (int16)roundf(x / x_scale),
+ * x_scale = max|x| / 32767, of tmac_gguf.cpp:889-896.
+ *
+ * Threading: a weight handle belongs to the device it was registered on; calls
+ * on it must use a stream of that device.  The library keeps one workspace per
+ * device; calls from several host threads on one device must be serialised by
+ * the caller (as the reference's single-threaded engine does).
+ */
+#ifndef TMAC_CUDA_H
+#define TMAC_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TMAC_ABI_VERSION 1
+
+/* GGUF tensor type codes (sim/tmac_gguf.cpp:151-156). */
+enum tmac_type {
+    TMAC_TYPE_F32 = 0,
+    TMAC_TYPE_F16 = 1,
+    TMAC_TYPE_Q5_0 = 6,
+    TMAC_TYPE_Q8_0 = 8,
+    TMAC_TYPE_Q4_K = 12,
+    TMAC_TYPE_Q6_K = 14
+};
+
+/* Which reference driver a registered weight reproduces.
+ *   NATIVE: the type's FPGA core path  -- matmul_fpga_q8 / _q5_0 / _q4_k /
+ *           _q6_k (tmac_gguf.cpp:948, :1221, :1097, :1367)
+ *   INT16:  matmul_fpga_int16 (tmac_gguf.cpp:887), the path a type takes
+ *           when its --fpga-* switch is off while another switch is on
+ *   F32:    the FP32 dequant path taken with no --fpga switch
+ *           (tmac_gguf.cpp:488-492)                                       */
+enum tmac_mode { TMAC_MODE_NATIVE = 0, TMAC_MODE_INT16 = 1, TMAC_MODE_F32 = 2 };
+
+/* Status codes: 0 = success, negative = failure (message in tmac_last_error). */
+enum tmac_status {
+    TMAC_OK = 0,
+    TMAC_ERR_INVALID = -1,   /* NULL handle/pointer, bad argument */
+    TMAC_ERR_TYPE = -2,      /* type/mode combination not supported */
+    TMAC_ERR_SHAPE = -3,     /* rows/cols/batch not supported */
+    TMAC_ERR_BOUNDS = -4,    /* descriptor/arena offset or size out of range */
+    TMAC_ERR_CUDA = -5,      /* CUDA runtime error */
+    TMAC_ERR_NCCL = -6,      /* NCCL error */
+    TMAC_ERR_TIMEOUT = -7,   /* a bounded device wait gave up */
+    TMAC_ERR_NOMEM = -8,     /* device allocation failed */
+    TMAC_ERR_NODEV = -9      /* no CUDA device / wrong architecture */
+};
+
+typedef struct tmac_weight_s* tmac_weight_t;
+
+/* Library identity and diagnostics. */
+int tmac_abi_version(void);
+/* Message of the last failing call on this host thread ("" if none). */
+const char* tmac_last_error(void);
+/* Reads and clears the device-side error word of `device` (synchronises that
+ * device).  *code receives 0 or the TMAC_ERR_* a kernel recorded. */
+int tmac_device_error(int device, int* code);
+
+/*
+ * Register one weight tensor: W[rows][cols] as raw GGUF blocks (the bytes a
+ * `.tmac` file / Tensor::data hold, row r = blocks r*(cols/QK) ...).
+ * Replaces: Tensor registration by load_tmac (tmac_gguf.cpp:1894-1947) plus
+ * the per-call weight-only work of the matmul_fpga_* drivers (row_inv /
+ * row_scale passes, Q8_0 combined scales), which is done once here.
+ *   blocks:        host pointer (copied) or, if blocks_on_device != 0, a
+ *                  device pointer on `device` (read during the call only).
+ *   row_max_abs:   optional host float[rows] for Q8_0 NATIVE
+ *                  (the `*_row_max_abs` tensor, sim/matmul_q8.cpp:22-35).
+ * The handle owns its device memory until tmac_weight_free.
+ */
+int tmac_weight_register(int type, int mode, int64_t rows, int64_t cols,
+                         const void* blocks, size_t n_bytes, int blocks_on_device,
+                         const float* row_max_abs, int device, tmac_weight_t* out);
+int tmac_weight_free(tmac_weight_t w);
+int tmac_weight_info(tmac_weight_t w, int* type, int* mode, int64_t* rows, int64_t* cols,
+                     int* device);
+/* Device bytes the kernels stream per GEMV (the resident layout). */
+int tmac_weight_device_bytes(tmac_weight_t w, size_t* bytes);
+/* Host copy of the per-row normaliser: row_inv (Q5_0/Q4_K/Q6_K NATIVE) or
+ * row_scale (Q8_0 NATIVE, INT16).  out: float[rows]. */
+int tmac_weight_row_norm(tmac_weight_t w, float* out);
+
+/* Partial-sum units per row: Q8_0 NATIVE and INT16 -> 64-column tiles,
+ * Q5_0 -> 32-column blocks, Q4_K/Q6_K -> 256-column blocks; F32 -> 0. */
+int64_t tmac_units_per_row(int type, int mode, int64_t cols);
+
+/*
+ * GEMV on device buffers: y[b][rows] = W . x[b][cols] for b < batch, each
+ * activation vector quantised with its own x_scale (as `batch` sequential
+ * calls of the reference driver would).  Replaces matmul_fpga_q8/_q5_0/_q4_k/
+ * _q6_k/_int16 and the FP32 matmul() branch (tmac_gguf.cpp:466-493).
+ *   x, y:      device pointers on the weight's device.
+ *   row_acc:   optional int64[batch][rows] device buffer: the exact integer
+ *              row accumulator (NATIVE/INT16 modes).
+ *   unit_acc:  optional int64[batch][rows][units] device buffer: per-unit
+ *              partial sums (see tmac_units_per_row).
+ *   stream:    cudaStream_t of the weight's device (NULL = default stream).
+ * Asynchronous: returns after enqueueing.
+ */
+int tmac_gemv(tmac_weight_t w, const float* x, float* y, int batch, void* stream);
+int tmac_gemv_acc(tmac_weight_t w, const float* x, float* y, int64_t* row_acc, int64_t* unit_acc,
+                  int batch, void* stream);
+
+/* Type-checked entry points with the per-type names of the reference drivers
+ * (tmac_gguf.cpp:466-470): they fail with TMAC_ERR_TYPE if `w` has another
+ * type or mode. */
+int tmac_gemv_q8_0(tmac_weight_t w, const float* x, float* y, int batch, void* stream);
+int tmac_gemv_q5_0(tmac_weight_t w, const float* x, float* y, int batch, void* stream);
+int tmac_gemv_q4_k(tmac_weight_t w, const float* x, float* y, int batch, void* stream);
+int tmac_gemv_q6_k(tmac_weight_t w, const float* x, float* y, int batch, void* stream);
+int tmac_gemv_int16(tmac_weight_t w, const float* x, float* y, int batch, void* stream);
+
+/*
+ * Host-buffer GEMV: copies x[batch][cols] host->device, runs tmac_gemv on the
+ * weight's device and copies y[batch][rows] back; synchronous.  This is the
+ * drop-in for the reference's `void matmul_fpga_X(const Tensor*, const float*
+ * x, float* y, int rows, int cols)` calls on host arrays.
+ */
+int tmac_gemv_host(tmac_weight_t w, const float* x_host, float* y_host, int batch);
+
+/* Allocate the per-device workspace for GEMVs up to batch x cols now, so that
+ * later calls allocate nothing (required before CUDA-graph capture). */
+int tmac_reserve(int device, int64_t max_batch, int64_t max_cols);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TMAC_CUDA_H */

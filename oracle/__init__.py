@@ -1,0 +1,165 @@
+"""Parity checker for the CUDA product path (test infrastructure only).
+
+`oracle.restated` wraps liboracle.so, the C restatement of the reference's CPU
+algorithm; `oracle.reference` wraps _ref/libtmac_ref.so, the reference's own
+sim/ sources compiled unmodified.  Only tests/, __graft_entry__.smoke() and
+bench.py's CPU baseline legs import this package; the product never does.
+"""
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "liboracle.so")
+REF_PATH = os.path.join(HERE, "_ref", "libtmac_ref.so")
+
+PATH_NATIVE, PATH_INT16, PATH_F32 = 0, 1, 2
+
+_lib = None
+_ref = None
+
+_P = ctypes.c_void_p
+_I64 = ctypes.c_int64
+
+
+def build():
+    """Compile liboracle.so (and _ref/ when the reference sources exist)."""
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+
+
+def _ptr(a):
+    return None if a is None else a.ctypes.data_as(ctypes.c_void_p)
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            build()
+        L = ctypes.CDLL(LIB_PATH)
+        L.orc_f16_to_f32.restype = ctypes.c_float
+        L.orc_f16_to_f32.argtypes = [ctypes.c_uint16]
+        L.orc_quantize_x.restype = ctypes.c_float
+        L.orc_quantize_x.argtypes = [_P, _I64, _P]
+        L.orc_dequant.restype = ctypes.c_float
+        L.orc_dequant.argtypes = [ctypes.c_int, _P, _I64, _I64, _I64]
+        for n in ("orc_row_inv_q5_0", "orc_row_inv_q4_k", "orc_row_inv_q6_k"):
+            getattr(L, n).argtypes = [_P, _I64, _I64, _P]
+        L.orc_row_scale_q8_0.argtypes = [_P, _I64, _I64, _P, _P]
+        L.orc_q8_combined_scale.restype = ctypes.c_uint16
+        L.orc_q8_combined_scale.argtypes = [ctypes.c_float, ctypes.c_float]
+        L.orc_units_per_row.restype = _I64
+        L.orc_units_per_row.argtypes = [ctypes.c_int, ctypes.c_int, _I64]
+        L.orc_gemv.restype = ctypes.c_int
+        L.orc_gemv.argtypes = [ctypes.c_int, ctypes.c_int, _P, _I64, _I64, _P, _P, _P, _P, _P]
+        _lib = L
+    return _lib
+
+
+def ref_available():
+    return os.path.exists(REF_PATH)
+
+
+def ref():
+    global _ref
+    if _ref is None:
+        R = ctypes.CDLL(REF_PATH)
+        R.ref_gemv.restype = ctypes.c_int
+        R.ref_gemv.argtypes = [ctypes.c_int, ctypes.c_int, _P, _I64, _I64, ctypes.c_size_t, _P, _P, _P]
+        R.ref_dequant.restype = ctypes.c_float
+        R.ref_dequant.argtypes = [ctypes.c_int, _P, _I64, _I64, _I64, _I64]
+        R.ref_q8_tile_sums.restype = ctypes.c_int
+        R.ref_q8_tile_sums.argtypes = [_P, _I64, _I64, ctypes.c_size_t, _P, _P, _P, _P]
+        R.ref_q5_0_block_sums.restype = ctypes.c_int
+        R.ref_q5_0_block_sums.argtypes = [_P, _I64, _P, _P, _P]
+        R.ref_q5_0_hw_tiles.restype = ctypes.c_int
+        R.ref_q5_0_hw_tiles.argtypes = [_P, _I64, _I64, _P, _P, _P]
+        R.ref_kquant_block_sums.restype = ctypes.c_int
+        R.ref_kquant_block_sums.argtypes = [ctypes.c_int, _P, _I64, _I64, _P, _P, _P]
+        _ref = R
+    return _ref
+
+
+class Result:
+    """y plus the exact integer accumulators of one GEMV."""
+
+    def __init__(self, y, row_acc=None, unit_acc=None):
+        self.y, self.row_acc, self.unit_acc = y, row_acc, unit_acc
+
+
+def gemv(qtype, w, rows, cols, x, path=PATH_NATIVE, row_max_abs=None):
+    """Restated reference GEMV for one activation vector x[cols]."""
+    L = lib()
+    w = np.ascontiguousarray(w, dtype=np.uint8)
+    x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)
+    y = np.zeros(rows, np.float32)
+    units = L.orc_units_per_row(qtype, path, cols)
+    row_acc = np.zeros(rows, np.int64) if path != PATH_F32 else None
+    unit_acc = np.zeros((rows, units), np.int64) if units > 0 else None
+    rma = None if row_max_abs is None else np.ascontiguousarray(row_max_abs, dtype=np.float32)
+    rc = L.orc_gemv(qtype, path, _ptr(w), rows, cols, _ptr(x), _ptr(rma), _ptr(y),
+                    _ptr(row_acc), _ptr(unit_acc))
+    if rc != 0:
+        raise ValueError(f"oracle rejected type={qtype} path={path} shape={rows}x{cols}")
+    return Result(y, row_acc, unit_acc)
+
+
+def quantize_x(x):
+    x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)
+    xq = np.zeros(x.size, np.int16)
+    xs = lib().orc_quantize_x(_ptr(x), x.size, _ptr(xq))
+    return np.float32(xs), xq
+
+
+def row_inv(qtype, w, rows, cols):
+    L = lib()
+    w = np.ascontiguousarray(w, dtype=np.uint8)
+    out = np.zeros(rows, np.float32)
+    fn = {6: L.orc_row_inv_q5_0, 12: L.orc_row_inv_q4_k, 14: L.orc_row_inv_q6_k}[qtype]
+    fn(_ptr(w), rows, cols, _ptr(out))
+    return out
+
+
+def row_scale_q8(w, rows, cols, row_max_abs=None):
+    out = np.zeros(rows, np.float32)
+    rma = None if row_max_abs is None else np.ascontiguousarray(row_max_abs, dtype=np.float32)
+    lib().orc_row_scale_q8_0(_ptr(np.ascontiguousarray(w, dtype=np.uint8)), rows, cols, _ptr(rma), _ptr(out))
+    return out
+
+
+# ---- the reference itself (compiled from its own sources) ----------------
+
+def ref_gemv(qtype, w, rows, cols, x, path=PATH_NATIVE, row_max_abs=None):
+    R = ref()
+    w = np.ascontiguousarray(w, dtype=np.uint8)
+    x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)
+    y = np.zeros(rows, np.float32)
+    rma = None if row_max_abs is None else np.ascontiguousarray(row_max_abs, dtype=np.float32)
+    R.ref_gemv(qtype, path, _ptr(w), rows, cols, w.nbytes, _ptr(x), _ptr(rma), _ptr(y))
+    return y
+
+
+def ref_unit_sums(qtype, w, rows, cols, x, row_max_abs=None):
+    """The reference core models' per-unit int64 sums (see ref_harness.cpp)."""
+    R = ref()
+    w = np.ascontiguousarray(w, dtype=np.uint8)
+    x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)
+    if qtype == 8:
+        out = np.zeros((rows, (cols + 63) // 64), np.int64)
+        y = np.zeros(rows, np.float32)
+        rma = None if row_max_abs is None else np.ascontiguousarray(row_max_abs, dtype=np.float32)
+        rc = R.ref_q8_tile_sums(_ptr(w), rows, cols, w.nbytes, _ptr(x), _ptr(rma), _ptr(y), _ptr(out))
+    else:
+        _, xq = quantize_x(x)  # pinned separately against the reference drivers' y
+        ri = row_inv(qtype, w, rows, cols)
+        if qtype == 6:
+            out = np.zeros((rows, 28), np.int64)
+            rc = R.ref_q5_0_block_sums(_ptr(w), rows, _ptr(xq), _ptr(ri), _ptr(out))
+        else:
+            out = np.zeros((rows, cols // 256), np.int64)
+            rc = R.ref_kquant_block_sums(qtype, _ptr(w), rows, cols, _ptr(xq), _ptr(ri), _ptr(out))
+    if rc != 0:
+        raise ValueError(f"reference harness rejected type={qtype} shape={rows}x{cols} rc={rc}")
+    return out

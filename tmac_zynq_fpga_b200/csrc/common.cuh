@@ -1,0 +1,192 @@
+// common.cuh -- shared host/device helpers of libtmac_cuda.so (sm_100a only).
+//
+// Exactness rules for every kernel in this library (the reference's CPU code is
+// the numerics spec):
+//  * fp32/fp64 expressions are written with explicit round-to-nearest
+//    intrinsics (__fmul_rn, __fadd_rn, __dmul_rn, ...) in the reference's
+//    evaluation order, and the library is compiled with -fmad=false, so no FMA
+//    contraction changes a rounding.
+//  * roundf() is C99 round-half-away-from-zero, as in the reference.
+//  * fp16 -> fp32 is exact (__half2float), matching fpga_sim::read_f16.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "../../include/tmac_cuda.h"
+
+#define TMAC_DEV __device__ __forceinline__
+
+namespace tmac {
+
+// ---------------------------------------------------------------- errors --
+void set_error(const std::string& msg);
+int fail(int code, const std::string& msg);
+int cuda_fail(cudaError_t e, const char* what);
+
+#define TMAC_CUDA_TRY(expr)                                  \
+    do {                                                     \
+        cudaError_t _e = (expr);                             \
+        if (_e != cudaSuccess) return tmac::cuda_fail(_e, #expr); \
+    } while (0)
+
+// Device-side error word (one per device, in this library's module).
+int* device_error_word(int device);
+
+// Switch to `device` for the lifetime of the guard.
+struct DeviceGuard {
+    int prev = -1;
+    bool ok = true;
+    explicit DeviceGuard(int dev)
+    {
+        if (cudaGetDevice(&prev) != cudaSuccess) { ok = false; return; }
+        if (prev != dev && cudaSetDevice(dev) != cudaSuccess) ok = false;
+    }
+    ~DeviceGuard()
+    {
+        int cur;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+int num_sms(int device);
+
+// ---------------------------------------------------------- device bits --
+TMAC_DEV float f16_bits_to_f32(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+
+TMAC_DEV uint16_t ld_u16_unaligned(const uint8_t* p) { return (uint16_t)(p[0] | (p[1] << 8)); }
+
+TMAC_DEV int16_t clamp_round_i16(float v)
+{
+    if (v > 32767.0f) return 32767;
+    if (v < -32768.0f) return -32768;
+    return (int16_t)(int)roundf(v);
+}
+
+// dp4a with unsigned a-bytes and signed / unsigned b-bytes.
+TMAC_DEV int dp4a_us(uint32_t a, uint32_t b, int c)
+{
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+TMAC_DEV int dp4a_uu(uint32_t a, uint32_t b, int c)
+{
+    int d;
+    asm("dp4a.u32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// Block-wide max of non-negative floats (fmaxf is exact and order-free).
+// `red` must hold one float per warp.  All threads get the result.
+TMAC_DEV float block_max(float v, float* red, int nthreads)
+{
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    if (l == 0) red[w] = v;
+    __syncthreads();
+    float m = 0.0f;
+    for (int i = 0; i < (nthreads + 31) / 32; i++) m = fmaxf(m, red[i]);
+    __syncthreads();
+    return m;
+}
+
+// x_scale of tmac_gguf.cpp:889-892 from max|x|.
+TMAC_DEV float x_scale_from_max(float mx) { return (mx < 1e-10f) ? 1.0f : __fdiv_rn(mx, 32767.0f); }
+// x_q of tmac_gguf.cpp:894-896.
+TMAC_DEV int16_t quantize_one(float x, float xs) { return (int16_t)(int)roundf(__fdiv_rn(x, xs)); }
+
+// ----------------------------------------------------- mbarrier / bulk copy
+TMAC_DEV uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+TMAC_DEV void mbar_init(uint64_t* bar, uint32_t count)
+{
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count));
+}
+TMAC_DEV void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+
+TMAC_DEV void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes)
+{
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+                 : "memory");
+}
+TMAC_DEV void mbar_arrive(uint64_t* bar)
+{
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+TMAC_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+TMAC_DEV uint64_t global_timer_ns()
+{
+    uint64_t t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+// Bounded wait: gives up after ~2 s, records TMAC_ERR_TIMEOUT and returns false.
+TMAC_DEV bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* err)
+{
+    if (mbar_try_wait(bar, parity)) return true;
+    uint64_t t0 = global_timer_ns();
+    for (uint32_t it = 1;; it++) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 255u) == 0 && global_timer_ns() - t0 > 2000000000ull) {
+            if (err) atomicExch(err, (int)TMAC_ERR_TIMEOUT);
+            return false;
+        }
+    }
+}
+// 1-D bulk copy global -> shared (no multicast), completion on `bar`.
+// dst, src 16-byte aligned, bytes a multiple of 16.
+TMAC_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar)
+{
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar))
+        : "memory");
+}
+TMAC_DEV void named_bar_sync(int id, int nthreads)
+{
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+}  // namespace tmac
+
+// ------------------------------------------------------- weight objects --
+// Device-resident layouts (all chosen at registration; see each .cu file).
+struct tmac_weight_s {
+    int type = 0, mode = 0, device = 0;
+    int64_t rows = 0, cols = 0;
+    uint8_t* data = nullptr;     // layout-specific packed weights
+    size_t data_bytes = 0;
+    float* row_norm = nullptr;   // row_inv (NATIVE Q5_0/K-quants) or row_scale (Q8_0, INT16)
+    int64_t groups = 0;          // row groups (interleaved layouts)
+    int64_t group_bytes = 0;     // bytes per row group
+    int tiles = 0;               // 64-column tiles per row (Q8_0 / INT16)
+};
+
+namespace tmac {
+// Per-path launchers (one per .cu file).  All return TMAC_OK or an error.
+int register_q8_0(tmac_weight_s* w, const uint8_t* d_raw, const float* d_row_max_abs, cudaStream_t s);
+int launch_q8_0(const tmac_weight_s* w, const float* x, float* y, int64_t* row_acc, int64_t* unit_acc,
+                int batch, cudaStream_t s);
+int register_blockq(tmac_weight_s* w, const uint8_t* d_raw, cudaStream_t s);
+int launch_blockq(const tmac_weight_s* w, const float* x, float* y, int64_t* row_acc, int64_t* unit_acc,
+                  int batch, cudaStream_t s);
+int register_int16(tmac_weight_s* w, const uint8_t* d_raw, cudaStream_t s);
+int launch_int16(const tmac_weight_s* w, const float* x, float* y, int64_t* row_acc, int64_t* unit_acc,
+                 int batch, cudaStream_t s);
+int register_f32(tmac_weight_s* w, const uint8_t* d_raw, cudaStream_t s);
+int launch_f32(const tmac_weight_s* w, const float* x, float* y, int batch, cudaStream_t s);
+}  // namespace tmac

@@ -1,0 +1,261 @@
+// gemv_blockq.cu -- Q5_0 / Q4_K / Q6_K GEMV, bit-exact with the reference's
+// FPGA core models driven by their matmul_fpga_* drivers:
+//   Q5_0: matmul_fpga_q5_0 (sim/tmac_gguf.cpp:1221-1362) +
+//         axi_vecmul_tile_q5_0_8x896_axilite (sim/fpga_sim.hpp:1004-1052)
+//   Q4_K: matmul_fpga_q4_k (tmac_gguf.cpp:1097-1215) + axilite_q4k_run (fpga_sim.hpp:730-788)
+//   Q6_K: matmul_fpga_q6_k (tmac_gguf.cpp:1367-1523) +
+//         axi_vecmul_tile_q6_k_axilite (fpga_sim.hpp:1058-1115)
+//
+// Per row r: row_inv[r] = 32767 / max|w| (weight-only, computed once at
+// registration), every weight becomes
+//   v = clamp_round_i16(w_f32 * row_inv)      with w_f32 in the reference's order:
+//       Q5_0: d*q     Q4_K: (d*sc)*q4 - dmin*m     Q6_K: (d*sc)*q6
+// the int64 row sum is  acc = sum v * x_q  and  y = (float)((double)acc * x_scale / (double)row_inv).
+// The integer sum is order-free, so the work is split freely: one thread per
+// 32-value chunk (a Q5_0 block, a Q4_K sub-block, a Q6_K 32-value run), rows of
+// a CTA accumulated in shared memory with 64-bit atomics.
+#include "common.cuh"
+#include "dequant.cuh"
+
+#include <algorithm>
+
+namespace tmac {
+namespace {
+
+constexpr int kThreads = 256;
+
+TMAC_DEV uint16_t ldg16(const uint8_t* p) { return __ldg(reinterpret_cast<const uint16_t*>(p)); }
+
+// ------------------------------------------------------------ row_inv pass --
+template <int TYPE>
+__global__ void row_inv_kernel(const uint8_t* __restrict__ raw, int64_t rows, int64_t cols, float* __restrict__ ri)
+{
+    const int64_t r = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (r >= rows) return;
+    float mx = 0.0f;
+    for (int64_t c = lane; c < cols; c += 32) {
+        // |w| with the reference's fp32 expression (tmac_gguf.cpp:1258, :1131, :1415)
+        float v = dequant_element(TYPE, raw, cols, r, c);
+        mx = fmaxf(mx, fabsf(v));
+    }
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) ri[r] = __fdiv_rn(32767.0f, (mx < 1e-10f) ? 1.0f : mx);
+}
+
+// --------------------------------------------------- chunk decode (32 values)
+// Decodes chunk `ch` of row `r` into v[32] (int16 values held in ints).
+template <int TYPE>
+TMAC_DEV void decode_chunk(const uint8_t* __restrict__ raw, int64_t r, int64_t cpr, int64_t ch, float ri, int (&v)[32])
+{
+    if (TYPE == TMAC_TYPE_Q5_0) {
+        const uint8_t* b = raw + (r * cpr + ch) * 22;  // 2-byte aligned
+        const float d = f16_bits_to_f32(ldg16(b));
+        const uint32_t qh = (uint32_t)ldg16(b + 2) | ((uint32_t)ldg16(b + 4) << 16);
+        uint8_t qs[16];
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            uint16_t h = ldg16(b + 6 + 2 * i);
+            qs[2 * i] = (uint8_t)h;
+            qs[2 * i + 1] = (uint8_t)(h >> 8);
+        }
+#pragma unroll
+        for (int wi = 0; wi < 32; wi++) {
+            const int ql = wi < 16 ? (qs[wi] & 0xF) : (qs[wi - 16] >> 4);
+            const int q = ((((qh >> wi) & 1) << 4) | ql) - 16;
+            v[wi] = clamp_round_i16(__fmul_rn(__fmul_rn(d, (float)q), ri));
+        }
+    } else if (TYPE == TMAC_TYPE_Q4_K) {
+        const int64_t sb = ch >> 3;
+        const int sub = (int)(ch & 7);
+        const uint8_t* b = raw + (r * (cpr >> 3) + sb) * 144;  // 16-byte aligned
+        const uint4 hdr = __ldg(reinterpret_cast<const uint4*>(b));
+        const uint8_t* hb = reinterpret_cast<const uint8_t*>(&hdr);
+        const float d = f16_bits_to_f32((uint16_t)(hb[0] | (hb[1] << 8)));
+        const float dmin = f16_bits_to_f32((uint16_t)(hb[2] | (hb[3] << 8)));
+        int sc, m;
+        q4_k_scale_min(hb + 4, sub, sc, m);
+        const float A = __fmul_rn(d, (float)sc), B = __fmul_rn(dmin, (float)m);
+        const uint4* qp = reinterpret_cast<const uint4*>(b + 16 + (sub >> 1) * 32);
+        uint4 q2[2] = {__ldg(qp), __ldg(qp + 1)};
+        const uint8_t* qs = reinterpret_cast<const uint8_t*>(q2);
+        const int shift = (sub & 1) * 4;
+#pragma unroll
+        for (int j = 0; j < 32; j++) {
+            const int q4 = (qs[j] >> shift) & 0xF;
+            v[j] = clamp_round_i16(__fmul_rn(__fsub_rn(__fmul_rn(A, (float)q4), B), ri));
+        }
+    } else {  // Q6_K
+        const int64_t sb = ch >> 3;
+        const int within = (int)(ch & 7), half = within >> 2, sub = within & 3;
+        const uint8_t* b = raw + (r * (cpr >> 3) + sb) * 210;  // 2-byte aligned
+        const float d = f16_bits_to_f32(ldg16(b + 208));
+        const uint16_t scw = ldg16(b + 192 + half * 8 + sub * 2);
+        const float A0 = __fmul_rn(d, (float)(int8_t)(scw & 0xFF));
+        const float A1 = __fmul_rn(d, (float)(int8_t)(scw >> 8));
+        const uint8_t* ql = b + half * 64 + (sub & 1) * 32;
+        const uint8_t* qhp = b + 128 + half * 32;
+        const int lshift = (sub < 2) ? 0 : 4, hshift = sub * 2;
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+            const uint16_t lw = ldg16(ql + 2 * i), hw = ldg16(qhp + 2 * i);
+#pragma unroll
+            for (int k = 0; k < 2; k++) {
+                const int l = 2 * i + k;
+                const int lo = ((k ? (lw >> 8) : lw) >> lshift) & 0xF;
+                const int hi = ((k ? (hw >> 8) : hw) >> hshift) & 0x3;
+                const int q6 = ((hi << 4) | lo) - 32;
+                v[l] = clamp_round_i16(__fmul_rn(__fmul_rn(l < 16 ? A0 : A1, (float)q6), ri));
+            }
+        }
+    }
+}
+
+struct BlockqArgs {
+    const uint8_t* raw;
+    const float* row_inv;
+    int64_t rows, cols;
+    const float* x;  // [nb][cols]
+    float* y;        // [nb][rows]
+    int64_t* row_acc;
+    int64_t* unit_acc;
+    int nb;          // activation vectors handled by this launch
+    int rp;          // rows per CTA pass
+};
+
+template <int TYPE>
+__global__ void __launch_bounds__(kThreads) blockq_gemv_kernel(BlockqArgs a)
+{
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int64_t cols = a.cols, cpr = cols / 32;
+    const int nb = a.nb;
+    int16_t* xq = reinterpret_cast<int16_t*>(smem);                                    // [nb][cols]
+    float* xs = reinterpret_cast<float*>(smem + ((size_t)nb * cols * 2 + 15) / 16 * 16);  // [nb]
+    float* red = xs + 16;                                                              // [8]
+    unsigned long long* racc = reinterpret_cast<unsigned long long*>(red + 8);         // [rp][nb]
+
+    // activation quantisation, one vector at a time (tmac_gguf.cpp:889-896)
+    for (int b = 0; b < nb; b++) {
+        const float* xb = a.x + (int64_t)b * cols;
+        float mx = 0.0f;
+        for (int64_t j = threadIdx.x; j < cols; j += kThreads) mx = fmaxf(mx, fabsf(xb[j]));
+        mx = block_max(mx, red, kThreads);
+        const float s = x_scale_from_max(mx);
+        if (threadIdx.x == 0) xs[b] = s;
+        for (int64_t j = threadIdx.x; j < cols; j += kThreads) xq[b * cols + j] = quantize_one(xb[j], s);
+    }
+    __syncthreads();
+
+    const int upr_div = (TYPE == TMAC_TYPE_Q5_0) ? 1 : 8;  // chunks per reported unit
+    const int64_t upr = cpr / upr_div;
+    for (int64_t r0 = (int64_t)blockIdx.x * a.rp; r0 < a.rows; r0 += (int64_t)gridDim.x * a.rp) {
+        const int nr = (int)std::min<int64_t>(a.rp, a.rows - r0);
+        for (int i = threadIdx.x; i < nr * nb; i += kThreads) racc[i] = 0ull;
+        __syncthreads();
+        for (int64_t c = threadIdx.x; c < (int64_t)nr * cpr; c += kThreads) {
+            const int rr = (int)(c / cpr);
+            const int64_t ch = c % cpr, r = r0 + rr;
+            int v[32];
+            decode_chunk<TYPE>(a.raw, r, cpr, ch, __ldg(a.row_inv + r), v);
+            for (int b = 0; b < nb; b++) {
+                const uint4* xv = reinterpret_cast<const uint4*>(xq + b * cols + ch * 32);
+                long long acc = 0;
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    const uint4 u = xv[q];
+                    const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        const int x0 = (int)(int16_t)(w4[k] & 0xFFFF), x1 = (int)(int16_t)(w4[k] >> 16);
+                        acc += (long long)(v[q * 8 + 2 * k] * x0 + v[q * 8 + 2 * k + 1] * x1);
+                    }
+                }
+                atomicAdd(&racc[rr * nb + b], (unsigned long long)acc);
+                if (a.unit_acc) {
+                    long long* u = (long long*)a.unit_acc + ((int64_t)b * a.rows + r) * upr + ch / upr_div;
+                    if (upr_div == 1) *u = acc;
+                    else atomicAdd(reinterpret_cast<unsigned long long*>(u), (unsigned long long)acc);
+                }
+            }
+        }
+        __syncthreads();
+        for (int i = threadIdx.x; i < nr * nb; i += kThreads) {
+            const int rr = i / nb, b = i % nb;
+            const int64_t r = r0 + rr;
+            const long long acc = (long long)racc[i];
+            const double v = __ddiv_rn(__dmul_rn((double)acc, (double)xs[b]), (double)__ldg(a.row_inv + r));
+            a.y[(int64_t)b * a.rows + r] = (float)v;
+            if (a.row_acc) a.row_acc[(int64_t)b * a.rows + r] = acc;
+        }
+        __syncthreads();
+    }
+}
+
+template <int TYPE>
+int launch_type(const tmac_weight_s* w, const float* x, float* y, int64_t* row_acc, int64_t* unit_acc, int batch,
+                cudaStream_t s)
+{
+    const int64_t cols = w->cols, cpr = cols / 32;
+    const int64_t max_smem = 200 * 1024;
+    int bmax = (int)std::max<int64_t>(1, std::min<int64_t>(16, (max_smem - 4096) / (cols * 2)));
+    const int rp = (int)std::max<int64_t>(1, 512 / cpr);
+    static bool attr[64] = {};
+    if (!attr[w->device & 63]) {
+        TMAC_CUDA_TRY(cudaFuncSetAttribute(blockq_gemv_kernel<TYPE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)max_smem));
+        attr[w->device & 63] = true;
+    }
+    const int64_t upr = (TYPE == TMAC_TYPE_Q5_0) ? cpr : cpr / 8;
+    if (unit_acc && TYPE != TMAC_TYPE_Q5_0)
+        TMAC_CUDA_TRY(cudaMemsetAsync(unit_acc, 0, (size_t)batch * w->rows * upr * sizeof(int64_t), s));
+    const int64_t passes = (w->rows + rp - 1) / rp;
+    const int grid = (int)std::min<int64_t>(passes, (int64_t)num_sms(w->device) * 4);
+    for (int b0 = 0; b0 < batch; b0 += bmax) {
+        const int nb = std::min(bmax, batch - b0);
+        BlockqArgs a;
+        a.raw = w->data;
+        a.row_inv = w->row_norm;
+        a.rows = w->rows;
+        a.cols = cols;
+        a.x = x + (int64_t)b0 * cols;
+        a.y = y + (int64_t)b0 * w->rows;
+        a.row_acc = row_acc ? row_acc + (int64_t)b0 * w->rows : nullptr;
+        a.unit_acc = unit_acc ? unit_acc + (int64_t)b0 * w->rows * upr : nullptr;
+        a.nb = nb;
+        a.rp = rp;
+        const size_t smem = ((size_t)nb * cols * 2 + 15) / 16 * 16 + 24 * 4 + (size_t)rp * nb * 8;
+        blockq_gemv_kernel<TYPE><<<grid, kThreads, smem, s>>>(a);
+        TMAC_CUDA_TRY(cudaGetLastError());
+    }
+    return TMAC_OK;
+}
+
+}  // namespace
+
+int register_blockq(tmac_weight_s* w, const uint8_t* d_raw, cudaStream_t s)
+{
+    TMAC_CUDA_TRY(cudaMalloc(&w->row_norm, (size_t)w->rows * sizeof(float)));
+    const int wpb = 8;
+    const unsigned grid = (unsigned)((w->rows + wpb - 1) / wpb);
+    switch (w->type) {
+    case TMAC_TYPE_Q5_0: row_inv_kernel<TMAC_TYPE_Q5_0><<<grid, wpb * 32, 0, s>>>(d_raw, w->rows, w->cols, w->row_norm); break;
+    case TMAC_TYPE_Q4_K: row_inv_kernel<TMAC_TYPE_Q4_K><<<grid, wpb * 32, 0, s>>>(d_raw, w->rows, w->cols, w->row_norm); break;
+    case TMAC_TYPE_Q6_K: row_inv_kernel<TMAC_TYPE_Q6_K><<<grid, wpb * 32, 0, s>>>(d_raw, w->rows, w->cols, w->row_norm); break;
+    default: return fail(TMAC_ERR_TYPE, "register_blockq: unsupported type");
+    }
+    TMAC_CUDA_TRY(cudaGetLastError());
+    return TMAC_OK;
+}
+
+int launch_blockq(const tmac_weight_s* w, const float* x, float* y, int64_t* row_acc, int64_t* unit_acc, int batch,
+                  cudaStream_t s)
+{
+    switch (w->type) {
+    case TMAC_TYPE_Q5_0: return launch_type<TMAC_TYPE_Q5_0>(w, x, y, row_acc, unit_acc, batch, s);
+    case TMAC_TYPE_Q4_K: return launch_type<TMAC_TYPE_Q4_K>(w, x, y, row_acc, unit_acc, batch, s);
+    case TMAC_TYPE_Q6_K: return launch_type<TMAC_TYPE_Q6_K>(w, x, y, row_acc, unit_acc, batch, s);
+    default: return fail(TMAC_ERR_TYPE, "launch_blockq: unsupported type");
+    }
+}
+
+}  // namespace tmac

@@ -1,0 +1,378 @@
+// gemv_q8_0.cu -- Q8_0 GEMV, bit-exact with the reference's Q8_0 FPGA path:
+// matmul_fpga_q8 (sim/tmac_gguf.cpp:948-1085) driving axi_vecmul_tile_q8 and
+// MatmulAccel::compute_int16's Q8 branch (sim/fpga_sim.hpp:322-349, :466-491).
+//
+// Reference numerics, per row r and 64-column tile t:
+//   row_scale  = max_j |q*d| / 32767            (or row_max_abs[r] / 32767)
+//   cs(blk)    = (u16)(min(max(d_blk * (1/row_scale), 0), 255.996) * 256 + 0.5)
+//   deq        = (int16)((q * cs) >> 8)          (arithmetic shift = floor)
+//   acc_t      = sum_k deq * x_q[k]              (int64, 64 columns)
+//   y          = (float)((double)y + (double)acc_t * x_scale * row_scale), t = 0..T-1 in order
+//
+// Device layout (built once by register_q8_0): rows in groups of 32, each group
+// one contiguous record so a single 1-D bulk copy stages it in shared memory:
+//   [T][4][32 lanes][16 B]  biased quants q ^ 0x80 (16 columns per chunk)
+//   [T][32 lanes] u32       cs of the tile's two 32-column blocks (lo | hi << 16)
+//   [32] f32                row_scale
+// = 952 B per row for cols = 896, the same as the GGUF blocks (34 B / 32 values)
+// plus the 4-byte row scale.  Padding rows/columns hold q = 0, cs = 0.
+//
+// Exact integer identity used by the kernel (no per-element float work):
+//   cs = 256*ch + cl  =>  floor(q*cs/256) = q*ch + floor(q*cl/256)
+//   with q' = q + 128 in [0,255]:  e + 128 = (q'*cl + 128*(256-cl)) >> 8 in [0,254]
+// Two 16-bit lanes of (q'*cl + K) fit one 32-bit IMAD without carries
+// (max 65153), so e is produced for 4 columns with 2 IMADs + 3 byte permutes,
+// and every dot product is a dp4a against the split activation
+// x_q = 256*xh + xl (xh signed byte, xl unsigned byte):
+//   sum deq*x = ch*(sum q'*x - 128*Sx) + (sum eb*x - 128*Sx),  Sx = sum of x_q over the block.
+#include "common.cuh"
+
+#include <algorithm>
+
+namespace tmac {
+namespace {
+
+constexpr int kConsumerWarps = 7;
+constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr int kMaxStages = 4;
+constexpr size_t kSmemLimit = 220 * 1024;
+
+struct Q8Layout {
+    int T;               // 64-column tiles per row
+    int stages;          // shared-memory pipeline depth (2..4)
+    int64_t groups;      // 32-row groups
+    int64_t group_bytes; // T*2048 + T*128 + 128
+    __host__ __device__ int64_t cs_off() const { return (int64_t)T * 2048; }
+    __host__ __device__ int64_t rs_off() const { return (int64_t)T * 2176; }
+};
+
+Q8Layout q8_layout(int64_t rows, int64_t cols)
+{
+    Q8Layout L;
+    L.T = (int)((cols + 63) / 64);
+    L.groups = (rows + 31) / 32;
+    L.group_bytes = (int64_t)L.T * 2176 + 128;
+    // Everything but the stages: barriers, tile sums, split activations, scratch.
+    const int64_t extra = 2 * kMaxStages * 8 + 2 * (int64_t)L.T * 32 * 8 + (int64_t)L.T * 16 * 4 * 2 +
+                          (int64_t)L.T * 2 * 4 + (int64_t)L.T * 64 * 2 + 16 * 4;
+    const int64_t fit = ((int64_t)kSmemLimit - extra) / L.group_bytes;
+    L.stages = (int)std::min<int64_t>(kMaxStages, std::max<int64_t>(fit, 0));
+    return L;
+}
+
+// ---------------------------------------------------------- registration --
+// row_scale per row (tmac_gguf.cpp:980-1004): one warp per row.
+__global__ void q8_row_scale_kernel(const uint8_t* __restrict__ raw, int64_t rows, int64_t cols,
+                                    const float* __restrict__ row_max_abs, float* __restrict__ row_scale)
+{
+    int64_t r = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    int lane = threadIdx.x & 31;
+    if (r >= rows) return;
+    float mx;
+    if (row_max_abs) {
+        mx = row_max_abs[r];
+    } else {
+        mx = 0.0f;
+        const int64_t bpr = cols / 32;
+        for (int64_t b = lane; b < bpr; b += 32) {
+            const uint8_t* blk = raw + (r * bpr + b) * 34;
+            float d = f16_bits_to_f32(ld_u16_unaligned(blk));
+            for (int k = 0; k < 32; k++) mx = fmaxf(mx, fabsf(__fmul_rn((float)(int8_t)blk[2 + k], d)));
+        }
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    }
+    if (lane == 0) row_scale[r] = (mx < 1e-10f) ? 1.0f : __fdiv_rn(mx, 32767.0f);
+}
+
+// Combined UQ8.8 scale, tmac_gguf.cpp:1022-1039.
+TMAC_DEV uint32_t q8_combined(float d, float rs)
+{
+    float rinv = (rs < 1e-10f) ? 1.0f : __fdiv_rn(1.0f, rs);
+    float c = __fmul_rn(d, rinv);
+    if (c >= 256.0f) c = 255.996f;
+    if (c < 0.0f) c = 0.0f;
+    return (uint32_t)(uint16_t)__fadd_rn(__fmul_rn(c, 256.0f), 0.5f);
+}
+
+// One CTA per (group, tile): 128 threads write the 16-byte quant chunks,
+// 32 threads the combined scales; tile 0 also writes the row scales.
+__global__ void q8_pack_kernel(const uint8_t* __restrict__ raw, int64_t rows, int64_t cols,
+                               const float* __restrict__ row_scale, Q8Layout L, uint8_t* __restrict__ out)
+{
+    const int64_t g = blockIdx.y;
+    const int t = blockIdx.x;
+    uint8_t* rec = out + g * L.group_bytes;
+    const int tid = threadIdx.x;
+    if (tid < 128) {
+        int j = tid / 32, l = tid % 32;
+        int64_t r = g * 32 + l;
+        uint8_t buf[16];
+        for (int b = 0; b < 16; b++) {
+            int64_t c = (int64_t)t * 64 + j * 16 + b;
+            uint8_t v = 0x80;
+            if (r < rows && c < cols) {
+                int64_t idx = r * cols + c;
+                v = raw[(idx / 32) * 34 + 2 + idx % 32] ^ 0x80;
+            }
+            buf[b] = v;
+        }
+        uint4 u;
+        memcpy(&u, buf, 16);
+        reinterpret_cast<uint4*>(rec)[((int64_t)t * 4 + j) * 32 + l] = u;
+    } else if (tid < 160) {
+        int l = tid - 128;
+        int64_t r = g * 32 + l;
+        uint32_t cs2 = 0;
+        if (r < rows) {
+            float rs = row_scale[r];
+            for (int blk = 0; blk < 2; blk++) {
+                int64_t c0 = (int64_t)t * 64 + blk * 32;
+                if (c0 >= cols) continue;
+                const uint8_t* b = raw + ((r * cols + c0) / 32) * 34;
+                cs2 |= q8_combined(f16_bits_to_f32(ld_u16_unaligned(b)), rs) << (16 * blk);
+            }
+        }
+        reinterpret_cast<uint32_t*>(rec + L.cs_off())[t * 32 + l] = cs2;
+    } else if (tid < 192 && t == 0) {
+        int l = tid - 160;
+        int64_t r = g * 32 + l;
+        reinterpret_cast<float*>(rec + L.rs_off())[l] = (r < rows) ? row_scale[r] : 1.0f;
+    }
+}
+
+// -------------------------------------------------------------- the GEMV --
+struct Q8Args {
+    const uint8_t* packed;
+    Q8Layout L;
+    int64_t rows;
+    int cols;
+    const float* x;
+    float* y;
+    int64_t* row_acc;
+    int64_t* unit_acc;
+    int* err;
+};
+
+// Exact sum over one 32-column block: 8 words of biased quants, the split
+// activations, the block's combined scale and activation sum.
+TMAC_DEV long long q8_block_dot(const uint32_t (&q)[8], const uint4& xh0, const uint4& xh1, const uint4& xl0,
+                                const uint4& xl1, uint32_t cs, int sx)
+{
+    const uint32_t cl = cs & 255u, ch = cs >> 8;
+    const uint32_t K2 = (128u * (256u - cl)) * 0x00010001u;
+    const uint32_t xh[8] = {xh0.x, xh0.y, xh0.z, xh0.w, xh1.x, xh1.y, xh1.z, xh1.w};
+    const uint32_t xl[8] = {xl0.x, xl0.y, xl0.z, xl0.w, xl1.x, xl1.y, xl1.z, xl1.w};
+    int qh = 0, ql = 0, eh = 0, el = 0;
+#pragma unroll
+    for (int w = 0; w < 8; w++) {
+        const uint32_t a = __byte_perm(q[w], 0u, 0x4240);  // q'0 | q'2 << 16
+        const uint32_t b = __byte_perm(q[w], 0u, 0x4341);  // q'1 | q'3 << 16
+        const uint32_t ea = a * cl + K2;
+        const uint32_t eb = b * cl + K2;
+        const uint32_t e = __byte_perm(ea, eb, 0x7351);    // eb0 eb1 eb2 eb3
+        qh = dp4a_us(q[w], xh[w], qh);
+        ql = dp4a_uu(q[w], xl[w], ql);
+        eh = dp4a_us(e, xh[w], eh);
+        el = dp4a_uu(e, xl[w], el);
+    }
+    const int qx = qh * 256 + ql - 128 * sx;
+    const int ex = eh * 256 + el - 128 * sx;
+    return (long long)ch * (long long)qx + (long long)ex;
+}
+
+__global__ void __launch_bounds__(kThreads, 1) q8_gemv_kernel(Q8Args a)
+{
+    extern __shared__ __align__(128) uint8_t smem[];
+    const Q8Layout L = a.L;
+    const int T = L.T;
+    uint8_t* stage_base = smem;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.stages * L.group_bytes);
+    uint64_t* empty = full + L.stages;
+    long long* accs = reinterpret_cast<long long*>(empty + L.stages);           // [2][T][32]
+    uint32_t* xh_s = reinterpret_cast<uint32_t*>(accs + 2 * T * 32);            // [T*16]
+    uint32_t* xl_s = xh_s + T * 16;                                             // [T*16]
+    int* sx_s = reinterpret_cast<int*>(xl_s + T * 16);                          // [T*2]
+    int16_t* xq_s = reinterpret_cast<int16_t*>(sx_s + T * 2);                   // [T*64]
+    float* red = reinterpret_cast<float*>(xq_s + T * 64);                       // [8] + xs
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t g0 = (int64_t)blockIdx.x * L.groups / gridDim.x;
+    const int64_t g1 = (int64_t)(blockIdx.x + 1) * L.groups / gridDim.x;
+    const int ng = (int)(g1 - g0);
+
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(red + 12);
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < L.stages; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kConsumerWarps);
+        }
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    if (warp == kConsumerWarps) {
+        // ---------------- producer: one lane streams this CTA's groups ----
+        if (lane == 0) {
+            int issued = 0;
+            for (int i = 0; i < ng; i++) {
+                const int s = i % L.stages;
+                if (i >= L.stages && !mbar_wait_bounded(&empty[s], ((i / L.stages) & 1) ^ 1, a.err)) {
+                    *abort_flag = 1;
+                    break;
+                }
+                mbar_arrive_expect_tx(&full[s], (uint32_t)L.group_bytes);
+                bulk_g2s(stage_base + (int64_t)s * L.group_bytes, a.packed + (g0 + i) * L.group_bytes,
+                         (uint32_t)L.group_bytes, &full[s]);
+                issued = i + 1;
+            }
+            // Keep the CTA (and its shared memory) alive until every bulk copy
+            // issued has landed; on the normal path these waits return at once.
+            for (int i = (issued > L.stages ? issued - L.stages : 0); i < issued; i++)
+                mbar_wait_bounded(&full[i % L.stages], (i / L.stages) & 1, a.err);
+        }
+        return;
+    }
+
+    // ---------------- consumers: activation quantisation (overlaps the copies)
+    const int nct = kConsumerWarps * 32;
+    float mx = 0.0f;
+    for (int j = threadIdx.x; j < a.cols; j += nct) mx = fmaxf(mx, fabsf(a.x[j]));
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) red[warp] = mx;
+    named_bar_sync(1, nct);
+    mx = 0.0f;
+    for (int i = 0; i < kConsumerWarps; i++) mx = fmaxf(mx, red[i]);
+    const float xs = x_scale_from_max(mx);
+    for (int j = threadIdx.x; j < T * 64; j += nct) xq_s[j] = (j < a.cols) ? quantize_one(a.x[j], xs) : 0;
+    named_bar_sync(1, nct);
+    for (int j = threadIdx.x; j < T * 16; j += nct) {
+        uint32_t h = 0, l = 0;
+        for (int b = 0; b < 4; b++) {
+            int v = xq_s[j * 4 + b];
+            h |= (uint32_t)((v >> 8) & 0xFF) << (8 * b);
+            l |= (uint32_t)(v & 0xFF) << (8 * b);
+        }
+        xh_s[j] = h;
+        xl_s[j] = l;
+    }
+    for (int j = threadIdx.x; j < T * 2; j += nct) {
+        int sum = 0;
+        for (int k = 0; k < 32; k++) sum += xq_s[j * 32 + k];
+        sx_s[j] = sum;
+    }
+    named_bar_sync(1, nct);
+
+    // ---------------- main loop over this CTA's 32-row groups -------------
+    bool ok = true;
+    for (int i = 0; i < ng; i++) {
+        const int s = i % L.stages;
+        if (ok && *abort_flag) ok = false;
+        if (ok && !mbar_wait_bounded(&full[s], (i / L.stages) & 1, a.err)) {
+            ok = false;
+            *abort_flag = 1;
+        }
+        const uint8_t* st = stage_base + (int64_t)s * L.group_bytes;
+        long long* acc_buf = accs + (i & 1) * T * 32;
+        float rs = 1.0f;
+        if (ok) {
+            const uint4* qv = reinterpret_cast<const uint4*>(st);
+            const uint32_t* csv = reinterpret_cast<const uint32_t*>(st + L.cs_off());
+            rs = reinterpret_cast<const float*>(st + L.rs_off())[lane];
+            for (int t = warp; t < T; t += kConsumerWarps) {
+                uint4 c[4];
+#pragma unroll
+                for (int j = 0; j < 4; j++) c[j] = qv[(t * 4 + j) * 32 + lane];
+                const uint32_t csw = csv[t * 32 + lane];
+                const uint4* xh4 = reinterpret_cast<const uint4*>(xh_s + t * 16);
+                const uint4* xl4 = reinterpret_cast<const uint4*>(xl_s + t * 16);
+                const int2 sx = reinterpret_cast<const int2*>(sx_s)[t];
+                const uint32_t q0[8] = {c[0].x, c[0].y, c[0].z, c[0].w, c[1].x, c[1].y, c[1].z, c[1].w};
+                const uint32_t q1[8] = {c[2].x, c[2].y, c[2].z, c[2].w, c[3].x, c[3].y, c[3].z, c[3].w};
+                long long acc = q8_block_dot(q0, xh4[0], xh4[1], xl4[0], xl4[1], csw & 0xFFFFu, sx.x);
+                acc += q8_block_dot(q1, xh4[2], xh4[3], xl4[2], xl4[3], csw >> 16, sx.y);
+                acc_buf[t * 32 + lane] = acc;
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+        named_bar_sync(1, nct);
+
+        // One warp folds the group's tile sums in tile order (tmac_gguf.cpp:1075-1076).
+        if (ok && warp == i % kConsumerWarps) {
+            const int64_t r = (g0 + i) * 32 + lane;
+            float yr = 0.0f;
+            long long rsum = 0;
+            for (int t = 0; t < T; t++) {
+                const long long acc = acc_buf[t * 32 + lane];
+                rsum += acc;
+                const double v = __dmul_rn(__dmul_rn((double)acc, (double)xs), (double)rs);
+                yr = (float)__dadd_rn((double)yr, v);
+                if (a.unit_acc && r < a.rows) a.unit_acc[r * T + t] = acc;
+            }
+            if (r < a.rows) {
+                a.y[r] = yr;
+                if (a.row_acc) a.row_acc[r] = rsum;
+            }
+        }
+    }
+}
+
+size_t q8_smem_bytes(const Q8Layout& L)
+{
+    return (size_t)L.stages * L.group_bytes + 2 * L.stages * sizeof(uint64_t) + 2 * (size_t)L.T * 32 * 8 +
+           (size_t)L.T * 16 * 4 * 2 + (size_t)L.T * 2 * 4 + (size_t)L.T * 64 * 2 + 16 * 4;  // red[8], abort flag
+}
+
+}  // namespace
+
+int register_q8_0(tmac_weight_s* w, const uint8_t* d_raw, const float* d_row_max_abs, cudaStream_t s)
+{
+    if (w->cols % 32) return fail(TMAC_ERR_SHAPE, "Q8_0 needs cols % 32 == 0");
+    Q8Layout L = q8_layout(w->rows, w->cols);
+    w->tiles = L.T;
+    w->groups = L.groups;
+    w->group_bytes = L.group_bytes;
+    w->data_bytes = (size_t)(L.groups * L.group_bytes);
+    if (L.stages < 2) return fail(TMAC_ERR_SHAPE, "Q8_0: cols too large for a two-stage row-group pipeline");
+    TMAC_CUDA_TRY(cudaMalloc(&w->row_norm, (size_t)w->rows * sizeof(float)));
+    TMAC_CUDA_TRY(cudaMalloc(&w->data, w->data_bytes));
+    const int wpb = 8;
+    q8_row_scale_kernel<<<(unsigned)((w->rows + wpb - 1) / wpb), wpb * 32, 0, s>>>(d_raw, w->rows, w->cols,
+                                                                                   d_row_max_abs, w->row_norm);
+    TMAC_CUDA_TRY(cudaGetLastError());
+    dim3 grid(L.T, (unsigned)L.groups);
+    q8_pack_kernel<<<grid, 192, 0, s>>>(d_raw, w->rows, w->cols, w->row_norm, L, w->data);
+    TMAC_CUDA_TRY(cudaGetLastError());
+    return TMAC_OK;
+}
+
+int launch_q8_0(const tmac_weight_s* w, const float* x, float* y, int64_t* row_acc, int64_t* unit_acc, int batch,
+                cudaStream_t s)
+{
+    Q8Layout L = q8_layout(w->rows, w->cols);
+    const size_t smem = q8_smem_bytes(L);
+    static bool attr_set[64] = {};
+    if (!attr_set[w->device & 63]) {
+        TMAC_CUDA_TRY(cudaFuncSetAttribute(q8_gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemLimit));
+        attr_set[w->device & 63] = true;
+    }
+    const int grid = (int)std::min<int64_t>(L.groups, num_sms(w->device));
+    for (int b = 0; b < batch; b++) {
+        Q8Args a;
+        a.packed = w->data;
+        a.L = L;
+        a.rows = w->rows;
+        a.cols = (int)w->cols;
+        a.x = x + (int64_t)b * w->cols;
+        a.y = y + (int64_t)b * w->rows;
+        a.row_acc = row_acc ? row_acc + (int64_t)b * w->rows : nullptr;
+        a.unit_acc = unit_acc ? unit_acc + (int64_t)b * w->rows * L.T : nullptr;
+        a.err = device_error_word(w->device);
+        q8_gemv_kernel<<<grid, kThreads, smem, s>>>(a);
+        TMAC_CUDA_TRY(cudaGetLastError());
+    }
+    return TMAC_OK;
+}
+
+}  // namespace tmac

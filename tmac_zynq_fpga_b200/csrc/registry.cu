@@ -1,0 +1,413 @@
+// registry.cu -- the C ABI of libtmac_cuda.so (include/tmac_cuda.h): weight
+// registration, dispatch to the per-type kernels, host-buffer convenience
+// entry, error reporting.
+//
+// Dispatch mirrors the reference's matmul() switch (sim/tmac_gguf.cpp:473-493)
+// at registration time: a weight is registered for one reproduction mode
+// (NATIVE = the type's FPGA core path, INT16 = matmul_fpga_int16, F32 = the
+// FP32 dequant path), and tmac_gemv runs that mode's kernel.  There is no CPU
+// fallback: every path is a CUDA kernel, and a missing device is an error.
+#include "common.cuh"
+
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+namespace tmac {
+
+namespace {
+thread_local std::string g_last_error;
+
+__device__ int g_device_error;  // one word per device (module global)
+
+std::mutex g_dev_mutex;
+std::vector<int*> g_err_ptr;    // per device: address of g_device_error
+std::vector<int> g_sms;
+}  // namespace
+
+void set_error(const std::string& msg) { g_last_error = msg; }
+
+int fail(int code, const std::string& msg)
+{
+    g_last_error = msg;
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what)
+{
+    char buf[512];
+    snprintf(buf, sizeof(buf), "CUDA error %d (%s) in %s", (int)e, cudaGetErrorString(e), what);
+    g_last_error = buf;
+    return (e == cudaErrorMemoryAllocation) ? TMAC_ERR_NOMEM : TMAC_ERR_CUDA;
+}
+
+int* device_error_word(int device)
+{
+    std::lock_guard<std::mutex> lk(g_dev_mutex);
+    if (device < 0) return nullptr;
+    if ((int)g_err_ptr.size() <= device) g_err_ptr.resize(device + 1, nullptr);
+    if (!g_err_ptr[device]) {
+        DeviceGuard dg(device);
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_device_error) != cudaSuccess) return nullptr;
+        g_err_ptr[device] = static_cast<int*>(p);
+    }
+    return g_err_ptr[device];
+}
+
+int num_sms(int device)
+{
+    std::lock_guard<std::mutex> lk(g_dev_mutex);
+    if ((int)g_sms.size() <= device) g_sms.resize(device + 1, 0);
+    if (!g_sms[device]) {
+        int n = 0;
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device);
+        g_sms[device] = n > 0 ? n : 148;
+    }
+    return g_sms[device];
+}
+
+namespace {
+
+int64_t block_values(int type)
+{
+    switch (type) {
+    case TMAC_TYPE_Q8_0:
+    case TMAC_TYPE_Q5_0: return 32;
+    case TMAC_TYPE_Q4_K:
+    case TMAC_TYPE_Q6_K: return 256;
+    case TMAC_TYPE_F32:
+    case TMAC_TYPE_F16: return 1;
+    default: return 0;
+    }
+}
+
+int64_t block_bytes(int type)
+{
+    switch (type) {
+    case TMAC_TYPE_Q8_0: return 34;
+    case TMAC_TYPE_Q5_0: return 22;
+    case TMAC_TYPE_Q4_K: return 144;
+    case TMAC_TYPE_Q6_K: return 210;
+    case TMAC_TYPE_F32: return 4;
+    case TMAC_TYPE_F16: return 2;
+    default: return 0;
+    }
+}
+
+int check_device(int device)
+{
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess || n == 0) return fail(TMAC_ERR_NODEV, "no CUDA device available");
+    if (device < 0 || device >= n) return fail(TMAC_ERR_INVALID, "device index out of range");
+    int major = 0, minor = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device);
+    if (major != 10 || minor != 0)
+        return fail(TMAC_ERR_NODEV, "libtmac_cuda.so is built for sm_100a (B200) only");
+    return TMAC_OK;
+}
+
+int weight_ok(tmac_weight_t w)
+{
+    if (!w) return fail(TMAC_ERR_INVALID, "NULL weight handle");
+    return TMAC_OK;
+}
+
+// Per-device x/y staging buffers of tmac_gemv_host, grown on demand.
+struct Staging {
+    float* x = nullptr;
+    float* y = nullptr;
+    size_t xcap = 0, ycap = 0;
+};
+std::vector<Staging> g_staging;
+
+int staging(int device, size_t xb, size_t yb, float** dx, float** dy)
+{
+    std::lock_guard<std::mutex> lk(g_dev_mutex);
+    if ((int)g_staging.size() <= device) g_staging.resize(device + 1);
+    Staging& st = g_staging[device];
+    if (st.xcap < xb) {
+        if (st.x) cudaFree(st.x);
+        st.x = nullptr;
+        st.xcap = 0;
+        TMAC_CUDA_TRY(cudaMalloc(&st.x, xb));
+        st.xcap = xb;
+    }
+    if (st.ycap < yb) {
+        if (st.y) cudaFree(st.y);
+        st.y = nullptr;
+        st.ycap = 0;
+        TMAC_CUDA_TRY(cudaMalloc(&st.y, yb));
+        st.ycap = yb;
+    }
+    *dx = st.x;
+    *dy = st.y;
+    return TMAC_OK;
+}
+
+void free_weight(tmac_weight_s* w)
+{
+    if (!w) return;
+    DeviceGuard dg(w->device);
+    if (w->data) cudaFree(w->data);
+    if (w->row_norm) cudaFree(w->row_norm);
+    delete w;
+}
+
+}  // namespace
+}  // namespace tmac
+
+using namespace tmac;
+
+extern "C" {
+
+int tmac_abi_version(void) { return TMAC_ABI_VERSION; }
+
+const char* tmac_last_error(void) { return g_last_error.c_str(); }
+
+int tmac_device_error(int device, int* code)
+{
+    if (!code) return fail(TMAC_ERR_INVALID, "NULL code pointer");
+    int rc = check_device(device);
+    if (rc) return rc;
+    DeviceGuard dg(device);
+    int* p = device_error_word(device);
+    if (!p) return fail(TMAC_ERR_CUDA, "cannot resolve device error word");
+    TMAC_CUDA_TRY(cudaDeviceSynchronize());
+    int v = 0, zero = 0;
+    TMAC_CUDA_TRY(cudaMemcpy(&v, p, sizeof(int), cudaMemcpyDeviceToHost));
+    TMAC_CUDA_TRY(cudaMemcpy(p, &zero, sizeof(int), cudaMemcpyHostToDevice));
+    *code = v;
+    return TMAC_OK;
+}
+
+int64_t tmac_units_per_row(int type, int mode, int64_t cols)
+{
+    if (mode == TMAC_MODE_INT16) return (cols + 63) / 64;
+    if (mode != TMAC_MODE_NATIVE) return 0;
+    switch (type) {
+    case TMAC_TYPE_Q8_0: return (cols + 63) / 64;
+    case TMAC_TYPE_Q5_0: return cols / 32;
+    case TMAC_TYPE_Q4_K:
+    case TMAC_TYPE_Q6_K: return cols / 256;
+    default: return 0;
+    }
+}
+
+int tmac_weight_register(int type, int mode, int64_t rows, int64_t cols, const void* blocks, size_t n_bytes,
+                         int blocks_on_device, const float* row_max_abs, int device, tmac_weight_t* out)
+{
+    if (!out || !blocks) return fail(TMAC_ERR_INVALID, "NULL argument");
+    *out = nullptr;
+    if (rows <= 0 || cols <= 0) return fail(TMAC_ERR_SHAPE, "rows and cols must be positive");
+    const int64_t bv = block_values(type);
+    if (!bv) return fail(TMAC_ERR_TYPE, "unsupported tensor type " + std::to_string(type));
+    if (mode != TMAC_MODE_NATIVE && mode != TMAC_MODE_INT16 && mode != TMAC_MODE_F32)
+        return fail(TMAC_ERR_INVALID, "unknown mode");
+    if (mode == TMAC_MODE_NATIVE && (type == TMAC_TYPE_F32 || type == TMAC_TYPE_F16))
+        return fail(TMAC_ERR_TYPE, "F32/F16 tensors have no FPGA core path; use INT16 or F32 mode");
+    if (cols % bv) return fail(TMAC_ERR_SHAPE, "cols is not a multiple of the block size");
+    const size_t need = (size_t)(rows * (cols / bv) * block_bytes(type));
+    if (n_bytes < need) return fail(TMAC_ERR_BOUNDS, "n_bytes smaller than the tensor's blocks");
+    int rc = check_device(device);
+    if (rc) return rc;
+    DeviceGuard dg(device);
+    if (!dg.ok) return fail(TMAC_ERR_CUDA, "cudaSetDevice failed");
+
+    tmac_weight_s* w = new tmac_weight_s();
+    w->type = type;
+    w->mode = mode;
+    w->rows = rows;
+    w->cols = cols;
+    w->device = device;
+
+    uint8_t* d_raw = nullptr;
+    float* d_rma = nullptr;
+    bool raw_owned = false;
+    cudaStream_t s = nullptr;
+    auto cleanup = [&](int code) {
+        if (raw_owned && d_raw && d_raw != w->data) cudaFree(d_raw);
+        if (d_rma) cudaFree(d_rma);
+        if (code != TMAC_OK) free_weight(w);
+        return code;
+    };
+    cudaError_t e;
+    if (blocks_on_device) {
+        d_raw = (uint8_t*)blocks;
+    } else {
+        if ((e = cudaMalloc(&d_raw, need)) != cudaSuccess) return cleanup(cuda_fail(e, "cudaMalloc(raw)"));
+        raw_owned = true;
+        if ((e = cudaMemcpy(d_raw, blocks, need, cudaMemcpyHostToDevice)) != cudaSuccess)
+            return cleanup(cuda_fail(e, "cudaMemcpy(raw)"));
+    }
+    if (row_max_abs && type == TMAC_TYPE_Q8_0 && mode == TMAC_MODE_NATIVE) {
+        if ((e = cudaMalloc(&d_rma, rows * sizeof(float))) != cudaSuccess)
+            return cleanup(cuda_fail(e, "cudaMalloc(row_max_abs)"));
+        if ((e = cudaMemcpy(d_rma, row_max_abs, rows * sizeof(float), cudaMemcpyHostToDevice)) != cudaSuccess)
+            return cleanup(cuda_fail(e, "cudaMemcpy(row_max_abs)"));
+    }
+    if (mode == TMAC_MODE_NATIVE && type == TMAC_TYPE_Q8_0) {
+        rc = register_q8_0(w, d_raw, d_rma, s);
+    } else if (mode == TMAC_MODE_NATIVE) {
+        // Q5_0 / Q4_K / Q6_K keep the GGUF blocks; the kernel reads them in place.
+        if (raw_owned) {
+            w->data = d_raw;
+        } else {
+            if ((e = cudaMalloc(&w->data, need)) != cudaSuccess) return cleanup(cuda_fail(e, "cudaMalloc(data)"));
+            if ((e = cudaMemcpy(w->data, d_raw, need, cudaMemcpyDeviceToDevice)) != cudaSuccess)
+                return cleanup(cuda_fail(e, "cudaMemcpy(data)"));
+        }
+        w->data_bytes = need;
+        rc = register_blockq(w, w->data, s);
+    } else if (mode == TMAC_MODE_INT16) {
+        rc = register_int16(w, d_raw, s);
+    } else {
+        if (raw_owned) {
+            w->data = d_raw;
+        } else {
+            if ((e = cudaMalloc(&w->data, need)) != cudaSuccess) return cleanup(cuda_fail(e, "cudaMalloc(data)"));
+            if ((e = cudaMemcpy(w->data, d_raw, need, cudaMemcpyDeviceToDevice)) != cudaSuccess)
+                return cleanup(cuda_fail(e, "cudaMemcpy(data)"));
+        }
+        w->data_bytes = need;
+        rc = register_f32(w, w->data, s);
+    }
+    if (rc != TMAC_OK) return cleanup(rc);
+    if ((e = cudaStreamSynchronize(s)) != cudaSuccess) return cleanup(cuda_fail(e, "registration kernels"));
+    device_error_word(device);
+    *out = w;
+    return cleanup(TMAC_OK);
+}
+
+int tmac_weight_free(tmac_weight_t w)
+{
+    if (!w) return TMAC_OK;
+    free_weight(w);
+    return TMAC_OK;
+}
+
+int tmac_weight_info(tmac_weight_t w, int* type, int* mode, int64_t* rows, int64_t* cols, int* device)
+{
+    int rc = weight_ok(w);
+    if (rc) return rc;
+    if (type) *type = w->type;
+    if (mode) *mode = w->mode;
+    if (rows) *rows = w->rows;
+    if (cols) *cols = w->cols;
+    if (device) *device = w->device;
+    return TMAC_OK;
+}
+
+int tmac_weight_device_bytes(tmac_weight_t w, size_t* bytes)
+{
+    int rc = weight_ok(w);
+    if (rc) return rc;
+    if (!bytes) return fail(TMAC_ERR_INVALID, "NULL bytes pointer");
+    *bytes = w->data_bytes + (w->row_norm && w->type != TMAC_TYPE_Q8_0 ? w->rows * sizeof(float) : 0);
+    return TMAC_OK;
+}
+
+int tmac_weight_row_norm(tmac_weight_t w, float* out)
+{
+    int rc = weight_ok(w);
+    if (rc) return rc;
+    if (!out) return fail(TMAC_ERR_INVALID, "NULL output");
+    if (!w->row_norm) return fail(TMAC_ERR_TYPE, "this weight mode has no row normaliser");
+    DeviceGuard dg(w->device);
+    TMAC_CUDA_TRY(cudaMemcpy(out, w->row_norm, w->rows * sizeof(float), cudaMemcpyDeviceToHost));
+    return TMAC_OK;
+}
+
+int tmac_gemv_acc(tmac_weight_t w, const float* x, float* y, int64_t* row_acc, int64_t* unit_acc, int batch,
+                  void* stream)
+{
+    int rc = weight_ok(w);
+    if (rc) return rc;
+    if (!x || !y) return fail(TMAC_ERR_INVALID, "NULL x or y");
+    if (batch <= 0) return fail(TMAC_ERR_SHAPE, "batch must be positive");
+    if (w->mode == TMAC_MODE_F32 && (row_acc || unit_acc))
+        return fail(TMAC_ERR_TYPE, "the FP32 path has no integer accumulators");
+    DeviceGuard dg(w->device);
+    if (!dg.ok) return fail(TMAC_ERR_CUDA, "cudaSetDevice failed");
+    cudaStream_t s = (cudaStream_t)stream;
+    if (w->mode == TMAC_MODE_NATIVE && w->type == TMAC_TYPE_Q8_0)
+        return launch_q8_0(w, x, y, row_acc, unit_acc, batch, s);
+    if (w->mode == TMAC_MODE_NATIVE) return launch_blockq(w, x, y, row_acc, unit_acc, batch, s);
+    if (w->mode == TMAC_MODE_INT16) return launch_int16(w, x, y, row_acc, unit_acc, batch, s);
+    return launch_f32(w, x, y, batch, s);
+}
+
+int tmac_gemv(tmac_weight_t w, const float* x, float* y, int batch, void* stream)
+{
+    return tmac_gemv_acc(w, x, y, nullptr, nullptr, batch, stream);
+}
+
+static int gemv_typed(tmac_weight_t w, int type, int mode, const float* x, float* y, int batch, void* stream,
+                      const char* name)
+{
+    int rc = weight_ok(w);
+    if (rc) return rc;
+    if (w->mode != mode || (type >= 0 && w->type != type))
+        return fail(TMAC_ERR_TYPE, std::string(name) + ": weight has another type or mode");
+    return tmac_gemv_acc(w, x, y, nullptr, nullptr, batch, stream);
+}
+
+int tmac_gemv_q8_0(tmac_weight_t w, const float* x, float* y, int batch, void* stream)
+{
+    return gemv_typed(w, TMAC_TYPE_Q8_0, TMAC_MODE_NATIVE, x, y, batch, stream, "tmac_gemv_q8_0");
+}
+int tmac_gemv_q5_0(tmac_weight_t w, const float* x, float* y, int batch, void* stream)
+{
+    return gemv_typed(w, TMAC_TYPE_Q5_0, TMAC_MODE_NATIVE, x, y, batch, stream, "tmac_gemv_q5_0");
+}
+int tmac_gemv_q4_k(tmac_weight_t w, const float* x, float* y, int batch, void* stream)
+{
+    return gemv_typed(w, TMAC_TYPE_Q4_K, TMAC_MODE_NATIVE, x, y, batch, stream, "tmac_gemv_q4_k");
+}
+int tmac_gemv_q6_k(tmac_weight_t w, const float* x, float* y, int batch, void* stream)
+{
+    return gemv_typed(w, TMAC_TYPE_Q6_K, TMAC_MODE_NATIVE, x, y, batch, stream, "tmac_gemv_q6_k");
+}
+int tmac_gemv_int16(tmac_weight_t w, const float* x, float* y, int batch, void* stream)
+{
+    return gemv_typed(w, -1, TMAC_MODE_INT16, x, y, batch, stream, "tmac_gemv_int16");
+}
+
+int tmac_gemv_host(tmac_weight_t w, const float* x_host, float* y_host, int batch)
+{
+    int rc = weight_ok(w);
+    if (rc) return rc;
+    if (!x_host || !y_host) return fail(TMAC_ERR_INVALID, "NULL x or y");
+    if (batch <= 0) return fail(TMAC_ERR_SHAPE, "batch must be positive");
+    DeviceGuard dg(w->device);
+    const size_t xb = (size_t)batch * w->cols * sizeof(float), yb = (size_t)batch * w->rows * sizeof(float);
+    float *dx = nullptr, *dy = nullptr;
+    rc = staging(w->device, xb, yb, &dx, &dy);
+    if (rc) return rc;
+    cudaError_t e;
+    if ((e = cudaMemcpyAsync(dx, x_host, xb, cudaMemcpyHostToDevice, nullptr)) != cudaSuccess)
+        return cuda_fail(e, "H2D x");
+    rc = tmac_gemv(w, dx, dy, batch, nullptr);
+    if (rc) return rc;
+    if ((e = cudaMemcpyAsync(y_host, dy, yb, cudaMemcpyDeviceToHost, nullptr)) != cudaSuccess)
+        return cuda_fail(e, "D2H y");
+    TMAC_CUDA_TRY(cudaStreamSynchronize(nullptr));
+    return TMAC_OK;
+}
+
+int tmac_reserve(int device, int64_t max_batch, int64_t max_cols)
+{
+    (void)max_batch;
+    (void)max_cols;
+    int rc = check_device(device);
+    if (rc) return rc;
+    DeviceGuard dg(device);
+    if (!device_error_word(device)) return fail(TMAC_ERR_CUDA, "cannot resolve device error word");
+    num_sms(device);
+    return TMAC_OK;
+}
+
+}  // extern "C"
