@@ -28,13 +28,24 @@
 #include "common.cuh"
 
 #include <algorithm>
+#include <cstdlib>
 
 namespace tmac {
 namespace {
 
-constexpr int kConsumerWarps = 7;
-constexpr int kThreads = (kConsumerWarps + 1) * 32;
-constexpr int kMaxStages = 4;
+// Warp roles: kConsumerWarps compute tile sums (warp w owns tiles t = w mod 14,
+// so for cols <= 896 each warp owns one tile and keeps its activations in
+// registers), one warp streams row groups into shared memory with bulk copies,
+// and kFoldWarps warps fold the tile sums of each group into y in tile order.
+constexpr int kConsumerWarps = 14;
+constexpr int kProducerWarp = kConsumerWarps;
+constexpr int kFoldWarp0 = kConsumerWarps + 1;
+constexpr int kFoldWarps = 3;  // fold warp f takes groups i = f mod 3
+constexpr int kThreads = (kConsumerWarps + 1 + kFoldWarps) * 32;
+constexpr int kMaxStages = 6;
+// Tile-sum buffers: group i uses buffer i mod kAccBufs; kAccBufs is a multiple of
+// kFoldWarps so each buffer is folded by one warp only, in its own program order.
+constexpr int kAccBufs = 2 * kFoldWarps;
 constexpr size_t kSmemLimit = 220 * 1024;
 
 struct Q8Layout {
@@ -53,8 +64,8 @@ Q8Layout q8_layout(int64_t rows, int64_t cols)
     L.groups = (rows + 31) / 32;
     L.group_bytes = (int64_t)L.T * 2176 + 128;
     // Everything but the stages: barriers, tile sums, split activations, scratch.
-    const int64_t extra = 2 * kMaxStages * 8 + 2 * (int64_t)L.T * 32 * 8 + (int64_t)L.T * 16 * 4 * 2 +
-                          (int64_t)L.T * 2 * 4 + (int64_t)L.T * 64 * 2 + 16 * 4;
+    const int64_t extra = (2 * kMaxStages + 2 * kAccBufs) * 8 + kAccBufs * ((int64_t)L.T * 32 * 8 + 128) +
+                          (int64_t)L.T * 16 * 4 * 2 + (int64_t)L.T * 2 * 4 + (int64_t)L.T * 64 * 2 + 32 * 4;
     const int64_t fit = ((int64_t)kSmemLimit - extra) / L.group_bytes;
     L.stages = (int)std::min<int64_t>(kMaxStages, std::max<int64_t>(fit, 0));
     return L;
@@ -151,12 +162,13 @@ struct Q8Args {
     int64_t* row_acc;
     int64_t* unit_acc;
     int* err;
+    int probe;
 };
 
 // Exact sum over one 32-column block: 8 words of biased quants, the split
 // activations, the block's combined scale and activation sum.
 TMAC_DEV long long q8_block_dot(const uint32_t (&q)[8], const uint4& xh0, const uint4& xh1, const uint4& xl0,
-                                const uint4& xl1, uint32_t cs, int sx)
+                                const uint4& xl1, uint32_t cs, int sx, int probe = 0)
 {
     const uint32_t cl = cs & 255u, ch = cs >> 8;
     const uint32_t K2 = (128u * (256u - cl)) * 0x00010001u;
@@ -165,6 +177,7 @@ TMAC_DEV long long q8_block_dot(const uint32_t (&q)[8], const uint4& xh0, const 
     int qh = 0, ql = 0, eh = 0, el = 0;
 #pragma unroll
     for (int w = 0; w < 8; w++) {
+        if (probe == 3) { qh = dp4a_us(q[w], xh[w], qh); ql = dp4a_uu(q[w], xl[w], ql); continue; }
         const uint32_t a = __byte_perm(q[w], 0u, 0x4240);  // q'0 | q'2 << 16
         const uint32_t b = __byte_perm(q[w], 0u, 0x4341);  // q'1 | q'3 << 16
         const uint32_t ea = a * cl + K2;
@@ -180,38 +193,60 @@ TMAC_DEV long long q8_block_dot(const uint32_t (&q)[8], const uint4& xh0, const 
     return (long long)ch * (long long)qx + (long long)ex;
 }
 
+// Tile sums of tile t for the 32 rows of a staged group (lane = row).
+TMAC_DEV long long q8_tile_dot(const uint8_t* st, const Q8Layout& L, int t, int lane, const uint4 (&xh)[4],
+                               const uint4 (&xl)[4], int2 sx, int probe = 0)
+{
+    const uint4* qv = reinterpret_cast<const uint4*>(st);
+    uint4 c[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) c[j] = qv[(t * 4 + j) * 32 + lane];
+    const uint32_t csw = reinterpret_cast<const uint32_t*>(st + L.cs_off())[t * 32 + lane];
+    const uint32_t q0[8] = {c[0].x, c[0].y, c[0].z, c[0].w, c[1].x, c[1].y, c[1].z, c[1].w};
+    const uint32_t q1[8] = {c[2].x, c[2].y, c[2].z, c[2].w, c[3].x, c[3].y, c[3].z, c[3].w};
+    return q8_block_dot(q0, xh[0], xh[1], xl[0], xl[1], csw & 0xFFFFu, sx.x, probe) +
+           q8_block_dot(q1, xh[2], xh[3], xl[2], xl[3], csw >> 16, sx.y, probe);
+}
+
 __global__ void __launch_bounds__(kThreads, 1) q8_gemv_kernel(Q8Args a)
 {
     extern __shared__ __align__(128) uint8_t smem[];
     const Q8Layout L = a.L;
     const int T = L.T;
     uint8_t* stage_base = smem;
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.stages * L.group_bytes);
-    uint64_t* empty = full + L.stages;
-    long long* accs = reinterpret_cast<long long*>(empty + L.stages);           // [2][T][32]
-    uint32_t* xh_s = reinterpret_cast<uint32_t*>(accs + 2 * T * 32);            // [T*16]
-    uint32_t* xl_s = xh_s + T * 16;                                             // [T*16]
-    int* sx_s = reinterpret_cast<int*>(xl_s + T * 16);                          // [T*2]
-    int16_t* xq_s = reinterpret_cast<int16_t*>(sx_s + T * 2);                   // [T*64]
-    float* red = reinterpret_cast<float*>(xq_s + T * 64);                       // [8] + xs
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.stages * L.group_bytes);  // stage landed
+    uint64_t* empty = full + L.stages;                                             // stage consumed
+    uint64_t* acc_full = empty + L.stages;                                         // tile sums ready
+    uint64_t* acc_empty = acc_full + kAccBufs;                                     // tile sums folded
+    long long* accs = reinterpret_cast<long long*>(acc_empty + kAccBufs);           // [kAccBufs][T][32]
+    float* rs_buf = reinterpret_cast<float*>(accs + kAccBufs * T * 32);            // [kAccBufs][32]
+    uint32_t* xh_s = reinterpret_cast<uint32_t*>(rs_buf + kAccBufs * 32);          // [T*16]
+    uint32_t* xl_s = xh_s + T * 16;                                                // [T*16]
+    int* sx_s = reinterpret_cast<int*>(xl_s + T * 16);                             // [T*2]
+    int16_t* xq_s = reinterpret_cast<int16_t*>(sx_s + T * 2);                      // [T*64]
+    float* red = reinterpret_cast<float*>(xq_s + T * 64);                          // [16] + xs + abort
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(red + 20);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t g0 = (int64_t)blockIdx.x * L.groups / gridDim.x;
     const int64_t g1 = (int64_t)(blockIdx.x + 1) * L.groups / gridDim.x;
     const int ng = (int)(g1 - g0);
 
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(red + 12);
     if (threadIdx.x == 0) {
         for (int s = 0; s < L.stages; s++) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kConsumerWarps);
+        }
+        for (int b = 0; b < kAccBufs; b++) {
+            mbar_init(&acc_full[b], kConsumerWarps);
+            mbar_init(&acc_empty[b], 1);
         }
         *abort_flag = 0;
         fence_mbar_init();
     }
     __syncthreads();
 
-    if (warp == kConsumerWarps) {
+    if (warp == kProducerWarp) {
         // ---------------- producer: one lane streams this CTA's groups ----
         if (lane == 0) {
             int issued = 0;
@@ -234,17 +269,71 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemv_kernel(Q8Args a)
         return;
     }
 
+    if (warp >= kFoldWarp0) {
+        const int f = warp - kFoldWarp0;
+        // ---------------- fold: y = sum over tiles in order (tmac_gguf.cpp:1075-1076)
+        for (int i = f; i < ng; i += kFoldWarps) {
+            const int b = i % kAccBufs;
+            if (*abort_flag || !mbar_wait_bounded(&acc_full[b], (i / kAccBufs) & 1, a.err)) {
+                *abort_flag = 1;
+                break;
+            }
+            if (a.probe == 2) {
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&acc_empty[b]);
+                continue;
+            }
+            const float xs = red[16];
+            const long long* acc_buf = accs + b * T * 32;
+            const double rs = (double)rs_buf[b * 32 + lane];
+            const int64_t r = (g0 + i) * 32 + lane;
+            float yr = 0.0f;
+            long long rsum = 0;
+            for (int t = 0; t < T; t++) {
+                const long long acc = acc_buf[t * 32 + lane];
+                rsum += acc;
+                const double v = __dmul_rn(__dmul_rn((double)acc, (double)xs), rs);
+                yr = (float)__dadd_rn((double)yr, v);
+                if (a.unit_acc && r < a.rows) a.unit_acc[r * T + t] = acc;
+            }
+            if (r < a.rows) {
+                a.y[r] = yr;
+                if (a.row_acc) a.row_acc[r] = rsum;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[b]);
+        }
+        return;
+    }
+
     // ---------------- consumers: activation quantisation (overlaps the copies)
     const int nct = kConsumerWarps * 32;
+    // x is read from global memory once; xq_s first holds nothing, the values
+    // stay in registers between the max reduction and the quantisation.
+    constexpr int kXRegs = 4;  // covers T*64 <= kXRegs * 448 (cols <= 1792)
+    float xv[kXRegs];
     float mx = 0.0f;
-    for (int j = threadIdx.x; j < a.cols; j += nct) mx = fmaxf(mx, fabsf(a.x[j]));
+#pragma unroll
+    for (int k = 0; k < kXRegs; k++) {
+        const int j = threadIdx.x + k * nct;
+        xv[k] = (j < a.cols) ? a.x[j] : 0.0f;
+        mx = fmaxf(mx, fabsf(xv[k]));
+    }
+    for (int j = threadIdx.x + kXRegs * nct; j < a.cols; j += nct) mx = fmaxf(mx, fabsf(a.x[j]));
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     if (lane == 0) red[warp] = mx;
     named_bar_sync(1, nct);
     mx = 0.0f;
     for (int i = 0; i < kConsumerWarps; i++) mx = fmaxf(mx, red[i]);
     const float xs = x_scale_from_max(mx);
-    for (int j = threadIdx.x; j < T * 64; j += nct) xq_s[j] = (j < a.cols) ? quantize_one(a.x[j], xs) : 0;
+    if (threadIdx.x == 0) red[16] = xs;
+#pragma unroll
+    for (int k = 0; k < kXRegs; k++) {
+        const int j = threadIdx.x + k * nct;
+        if (j < T * 64) xq_s[j] = (j < a.cols) ? quantize_one(xv[k], xs) : 0;
+    }
+    for (int j = threadIdx.x + kXRegs * nct; j < T * 64; j += nct)
+        xq_s[j] = (j < a.cols) ? quantize_one(a.x[j], xs) : 0;
     named_bar_sync(1, nct);
     for (int j = threadIdx.x; j < T * 16; j += nct) {
         uint32_t h = 0, l = 0;
@@ -263,65 +352,58 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemv_kernel(Q8Args a)
     }
     named_bar_sync(1, nct);
 
+    // A warp that owns a single tile keeps its activations in registers.
+    const bool one_tile = (T <= kConsumerWarps);
+    uint4 xh[4], xl[4];
+    int2 sx = make_int2(0, 0);
+    if (one_tile && warp < T) {
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            xh[j] = reinterpret_cast<const uint4*>(xh_s + warp * 16)[j];
+            xl[j] = reinterpret_cast<const uint4*>(xl_s + warp * 16)[j];
+        }
+        sx = reinterpret_cast<const int2*>(sx_s)[warp];
+    }
+
     // ---------------- main loop over this CTA's 32-row groups -------------
-    bool ok = true;
     for (int i = 0; i < ng; i++) {
-        const int s = i % L.stages;
-        if (ok && *abort_flag) ok = false;
-        if (ok && !mbar_wait_bounded(&full[s], (i / L.stages) & 1, a.err)) {
-            ok = false;
+        const int s = i % L.stages, b = i % kAccBufs;
+        if (*abort_flag || !mbar_wait_bounded(&full[s], (i / L.stages) & 1, a.err) ||
+            (i >= kAccBufs && !mbar_wait_bounded(&acc_empty[b], ((i / kAccBufs) & 1) ^ 1, a.err))) {
             *abort_flag = 1;
+            break;
         }
         const uint8_t* st = stage_base + (int64_t)s * L.group_bytes;
-        long long* acc_buf = accs + (i & 1) * T * 32;
-        float rs = 1.0f;
-        if (ok) {
-            const uint4* qv = reinterpret_cast<const uint4*>(st);
-            const uint32_t* csv = reinterpret_cast<const uint32_t*>(st + L.cs_off());
-            rs = reinterpret_cast<const float*>(st + L.rs_off())[lane];
+        long long* acc_buf = accs + b * T * 32;
+        if (warp == 0) rs_buf[b * 32 + lane] = reinterpret_cast<const float*>(st + L.rs_off())[lane];
+        if (a.probe == 1 || a.probe == 2) {
+            acc_buf[warp * 32 + lane] = 0;
+        } else if (one_tile) {
+            if (warp < T) acc_buf[warp * 32 + lane] = q8_tile_dot(st, L, warp, lane, xh, xl, sx, a.probe);
+        } else {
             for (int t = warp; t < T; t += kConsumerWarps) {
-                uint4 c[4];
+                uint4 th[4], tl[4];
 #pragma unroll
-                for (int j = 0; j < 4; j++) c[j] = qv[(t * 4 + j) * 32 + lane];
-                const uint32_t csw = csv[t * 32 + lane];
-                const uint4* xh4 = reinterpret_cast<const uint4*>(xh_s + t * 16);
-                const uint4* xl4 = reinterpret_cast<const uint4*>(xl_s + t * 16);
-                const int2 sx = reinterpret_cast<const int2*>(sx_s)[t];
-                const uint32_t q0[8] = {c[0].x, c[0].y, c[0].z, c[0].w, c[1].x, c[1].y, c[1].z, c[1].w};
-                const uint32_t q1[8] = {c[2].x, c[2].y, c[2].z, c[2].w, c[3].x, c[3].y, c[3].z, c[3].w};
-                long long acc = q8_block_dot(q0, xh4[0], xh4[1], xl4[0], xl4[1], csw & 0xFFFFu, sx.x);
-                acc += q8_block_dot(q1, xh4[2], xh4[3], xl4[2], xl4[3], csw >> 16, sx.y);
-                acc_buf[t * 32 + lane] = acc;
+                for (int j = 0; j < 4; j++) {
+                    th[j] = reinterpret_cast<const uint4*>(xh_s + t * 16)[j];
+                    tl[j] = reinterpret_cast<const uint4*>(xl_s + t * 16)[j];
+                }
+                acc_buf[t * 32 + lane] = q8_tile_dot(st, L, t, lane, th, tl, reinterpret_cast<const int2*>(sx_s)[t]);
             }
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
-        named_bar_sync(1, nct);
-
-        // One warp folds the group's tile sums in tile order (tmac_gguf.cpp:1075-1076).
-        if (ok && warp == i % kConsumerWarps) {
-            const int64_t r = (g0 + i) * 32 + lane;
-            float yr = 0.0f;
-            long long rsum = 0;
-            for (int t = 0; t < T; t++) {
-                const long long acc = acc_buf[t * 32 + lane];
-                rsum += acc;
-                const double v = __dmul_rn(__dmul_rn((double)acc, (double)xs), (double)rs);
-                yr = (float)__dadd_rn((double)yr, v);
-                if (a.unit_acc && r < a.rows) a.unit_acc[r * T + t] = acc;
-            }
-            if (r < a.rows) {
-                a.y[r] = yr;
-                if (a.row_acc) a.row_acc[r] = rsum;
-            }
+        if (lane == 0) {
+            mbar_arrive(&empty[s]);
+            mbar_arrive(&acc_full[b]);
         }
     }
 }
 
 size_t q8_smem_bytes(const Q8Layout& L)
 {
-    return (size_t)L.stages * L.group_bytes + 2 * L.stages * sizeof(uint64_t) + 2 * (size_t)L.T * 32 * 8 +
-           (size_t)L.T * 16 * 4 * 2 + (size_t)L.T * 2 * 4 + (size_t)L.T * 64 * 2 + 16 * 4;  // red[8], abort flag
+    return (size_t)L.stages * L.group_bytes + (2 * L.stages + 2 * kAccBufs) * sizeof(uint64_t) +
+           kAccBufs * ((size_t)L.T * 32 * 8 + 128) + (size_t)L.T * 16 * 4 * 2 + (size_t)L.T * 2 * 4 +
+           (size_t)L.T * 64 * 2 + 32 * 4;  // red[16], xs, abort flag
 }
 
 }  // namespace
@@ -369,6 +451,7 @@ int launch_q8_0(const tmac_weight_s* w, const float* x, float* y, int64_t* row_a
         a.row_acc = row_acc ? row_acc + (int64_t)b * w->rows : nullptr;
         a.unit_acc = unit_acc ? unit_acc + (int64_t)b * w->rows * L.T : nullptr;
         a.err = device_error_word(w->device);
+        a.probe = getenv("TMAC_Q8_PROBE") ? atoi(getenv("TMAC_Q8_PROBE")) : 0;
         q8_gemv_kernel<<<grid, kThreads, smem, s>>>(a);
         TMAC_CUDA_TRY(cudaGetLastError());
     }
