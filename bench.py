@@ -241,6 +241,9 @@ def main():
 
     for i in range(args.warmup):
         step(i)
+    torch.cuda.synchronize()
+    if tm.device_error(local) != 0:
+        raise SystemExit("a kernel recorded a device-side error during warm-up")
     sampler = ClockSampler(local)
     sampler.start()
     time.sleep(0.3)

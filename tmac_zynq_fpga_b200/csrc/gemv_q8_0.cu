@@ -28,7 +28,6 @@
 #include "common.cuh"
 
 #include <algorithm>
-#include <cstdlib>
 
 namespace tmac {
 namespace {
@@ -47,6 +46,9 @@ constexpr int kMaxStages = 6;
 // kFoldWarps so each buffer is folded by one warp only, in its own program order.
 constexpr int kAccBufs = 2 * kFoldWarps;
 constexpr size_t kSmemLimit = 220 * 1024;
+// The small scratch at the end of shared memory holds one float per consumer
+// warp (max reduction) in [0,16), x_scale at [16] and the abort flag at [20].
+static_assert(kConsumerWarps <= 16, "max-reduction slots overlap x_scale / abort flag");
 
 struct Q8Layout {
     int T;               // 64-column tiles per row
@@ -162,13 +164,12 @@ struct Q8Args {
     int64_t* row_acc;
     int64_t* unit_acc;
     int* err;
-    int probe;
 };
 
 // Exact sum over one 32-column block: 8 words of biased quants, the split
 // activations, the block's combined scale and activation sum.
 TMAC_DEV long long q8_block_dot(const uint32_t (&q)[8], const uint4& xh0, const uint4& xh1, const uint4& xl0,
-                                const uint4& xl1, uint32_t cs, int sx, int probe = 0)
+                                const uint4& xl1, uint32_t cs, int sx)
 {
     const uint32_t cl = cs & 255u, ch = cs >> 8;
     const uint32_t K2 = (128u * (256u - cl)) * 0x00010001u;
@@ -177,7 +178,6 @@ TMAC_DEV long long q8_block_dot(const uint32_t (&q)[8], const uint4& xh0, const 
     int qh = 0, ql = 0, eh = 0, el = 0;
 #pragma unroll
     for (int w = 0; w < 8; w++) {
-        if (probe == 3) { qh = dp4a_us(q[w], xh[w], qh); ql = dp4a_uu(q[w], xl[w], ql); continue; }
         const uint32_t a = __byte_perm(q[w], 0u, 0x4240);  // q'0 | q'2 << 16
         const uint32_t b = __byte_perm(q[w], 0u, 0x4341);  // q'1 | q'3 << 16
         const uint32_t ea = a * cl + K2;
@@ -195,7 +195,7 @@ TMAC_DEV long long q8_block_dot(const uint32_t (&q)[8], const uint4& xh0, const 
 
 // Tile sums of tile t for the 32 rows of a staged group (lane = row).
 TMAC_DEV long long q8_tile_dot(const uint8_t* st, const Q8Layout& L, int t, int lane, const uint4 (&xh)[4],
-                               const uint4 (&xl)[4], int2 sx, int probe = 0)
+                               const uint4 (&xl)[4], int2 sx)
 {
     const uint4* qv = reinterpret_cast<const uint4*>(st);
     uint4 c[4];
@@ -204,8 +204,8 @@ TMAC_DEV long long q8_tile_dot(const uint8_t* st, const Q8Layout& L, int t, int 
     const uint32_t csw = reinterpret_cast<const uint32_t*>(st + L.cs_off())[t * 32 + lane];
     const uint32_t q0[8] = {c[0].x, c[0].y, c[0].z, c[0].w, c[1].x, c[1].y, c[1].z, c[1].w};
     const uint32_t q1[8] = {c[2].x, c[2].y, c[2].z, c[2].w, c[3].x, c[3].y, c[3].z, c[3].w};
-    return q8_block_dot(q0, xh[0], xh[1], xl[0], xl[1], csw & 0xFFFFu, sx.x, probe) +
-           q8_block_dot(q1, xh[2], xh[3], xl[2], xl[3], csw >> 16, sx.y, probe);
+    return q8_block_dot(q0, xh[0], xh[1], xl[0], xl[1], csw & 0xFFFFu, sx.x) +
+           q8_block_dot(q1, xh[2], xh[3], xl[2], xl[3], csw >> 16, sx.y);
 }
 
 __global__ void __launch_bounds__(kThreads, 1) q8_gemv_kernel(Q8Args a)
@@ -277,11 +277,6 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemv_kernel(Q8Args a)
             if (*abort_flag || !mbar_wait_bounded(&acc_full[b], (i / kAccBufs) & 1, a.err)) {
                 *abort_flag = 1;
                 break;
-            }
-            if (a.probe == 2) {
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&acc_empty[b]);
-                continue;
             }
             const float xs = red[16];
             const long long* acc_buf = accs + b * T * 32;
@@ -376,10 +371,8 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemv_kernel(Q8Args a)
         const uint8_t* st = stage_base + (int64_t)s * L.group_bytes;
         long long* acc_buf = accs + b * T * 32;
         if (warp == 0) rs_buf[b * 32 + lane] = reinterpret_cast<const float*>(st + L.rs_off())[lane];
-        if (a.probe == 1 || a.probe == 2) {
-            acc_buf[warp * 32 + lane] = 0;
-        } else if (one_tile) {
-            if (warp < T) acc_buf[warp * 32 + lane] = q8_tile_dot(st, L, warp, lane, xh, xl, sx, a.probe);
+        if (one_tile) {
+            if (warp < T) acc_buf[warp * 32 + lane] = q8_tile_dot(st, L, warp, lane, xh, xl, sx);
         } else {
             for (int t = warp; t < T; t += kConsumerWarps) {
                 uint4 th[4], tl[4];
@@ -451,7 +444,6 @@ int launch_q8_0(const tmac_weight_s* w, const float* x, float* y, int64_t* row_a
         a.row_acc = row_acc ? row_acc + (int64_t)b * w->rows : nullptr;
         a.unit_acc = unit_acc ? unit_acc + (int64_t)b * w->rows * L.T : nullptr;
         a.err = device_error_word(w->device);
-        a.probe = getenv("TMAC_Q8_PROBE") ? atoi(getenv("TMAC_Q8_PROBE")) : 0;
         q8_gemv_kernel<<<grid, kThreads, smem, s>>>(a);
         TMAC_CUDA_TRY(cudaGetLastError());
     }
