@@ -138,6 +138,66 @@ int tmac_gemv_host(tmac_weight_t w, const float* x_host, float* y_host, int batc
  * later calls allocate nothing (required before CUDA-graph capture). */
 int tmac_reserve(int device, int64_t max_batch, int64_t max_cols);
 
+/* ------------------------------------------------------------------------ */
+/* Phase-B descriptor chain (sim/fpga_sim.hpp:1254-1310, sim/tmac_gguf.cpp:513-880).
+ *
+ * A chain is a linked list of 32-byte descriptors inside a byte arena that
+ * stands for the FPGA's DDR: every address field is an absolute DDR offset,
+ * and the arena holds DDR bytes [arena_base, arena_base + arena_bytes).
+ * The descriptor layout is the reference's PhaseBDescriptor, byte for byte. */
+#define TMAC_DESC_TYPE_INT16 0
+#define TMAC_DESC_TYPE_Q5_0 6
+#define TMAC_DESC_TYPE_Q8_0 8
+#define TMAC_DESC_TYPE_Q4_K 12
+#define TMAC_DESC_TYPE_Q6_K 14
+#define TMAC_DESC_TYPE_CPU_OP 15
+#define TMAC_DESC_FLAG_INTERRUPT 0x01
+/* Tile sizes (blocks + scale section) of the reference's Phase-B packing. */
+#define TMAC_PHASEB_Q5_0_TILE_BYTES 4944 /* 8 rows x 896: 224 x 22 B + 8 x UQ16.8 */
+#define TMAC_PHASEB_Q6_K_TILE_BYTES 6848 /* 32 rows x 256: 32 x 210 B + 32 x UQ24.8 */
+#define TMAC_PHASEB_Q4_K_TILE_BYTES 8288 /* 56 rows x 256: 56 x 144 B + 56 x UQ24.8 */
+
+#pragma pack(push, 1)
+typedef struct tmac_phaseb_desc {
+    uint32_t next_desc_addr;  /* 0x00, 0 = end of chain */
+    uint32_t weight_addr;     /* 0x04 */
+    uint32_t act_addr;        /* 0x08, int16 activations */
+    uint32_t result_addr;     /* 0x0C, int64 per result row */
+    uint16_t num_tiles;       /* 0x10 */
+    uint16_t tile_bytes;      /* 0x12 */
+    uint8_t tensor_type;      /* 0x14, TMAC_DESC_TYPE_* */
+    uint8_t tile_res_rows;    /* 0x15 */
+    uint8_t flags;            /* 0x16 */
+    uint16_t act_total_bytes; /* 0x17 */
+    uint8_t num_col_groups;   /* 0x19 */
+    uint8_t reserved[6];      /* 0x1A */
+} tmac_phaseb_desc;
+#pragma pack(pop)
+
+typedef struct tmac_chain_stats {
+    int descriptors;      /* descriptors walked */
+    int unsupported;      /* descriptors of a type the reference runner skips (0 rows) */
+    int64_t result_rows;  /* int64 results written */
+} tmac_chain_stats;
+
+/*
+ * Replays a descriptor chain on the GPU: the replacement for phaseb_run_descriptor
+ * over the chain walked by phaseb_verify (tmac_gguf.cpp:761-831, :834-880).  For
+ * each descriptor the int64 accumulators are computed exactly as the reference
+ * runner does (Q5_0: row_inv recomputed from the tile's blocks; Q4_K / Q6_K:
+ * row_inv = UQ24.8 scale section / 256; CPU_OP: no rows; other types: skipped,
+ * 0 rows, as in the reference) and written at result_addr inside the arena.
+ *   arena_dev:   device copy of the DDR bytes [arena_base, arena_base + arena_bytes).
+ *   arena_host:  optional host mirror of the same bytes, used to walk the chain
+ *                without reading descriptors back from the device; NULL = read them.
+ *   head:        DDR offset of the first descriptor.
+ *   max_desc:    walk limit (a cycle in next_desc_addr is reported, not followed).
+ * Every offset and size is checked against the arena before any launch
+ * (TMAC_ERR_BOUNDS).  Asynchronous on `stream` once the walk is done.
+ */
+int tmac_chain_run(void* arena_dev, size_t arena_bytes, uint32_t arena_base, const void* arena_host,
+                   uint32_t head, int max_desc, tmac_chain_stats* stats, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -163,3 +163,66 @@ def ref_unit_sums(qtype, w, rows, cols, x, row_max_abs=None):
     if rc != 0:
         raise ValueError(f"reference harness rejected type={qtype} shape={rows}x{cols} rc={rc}")
     return out
+
+
+# ---- Phase-B descriptor chain ---------------------------------------------
+
+def phaseb_run(arena, base, desc_off, cap):
+    """Restated phaseb_run_descriptor: (rows, int64 accumulator[rows])."""
+    L = lib()
+    L.orc_phaseb_run.restype = _I64
+    L.orc_phaseb_run.argtypes = [_P, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_uint32, _P]
+    arena = np.ascontiguousarray(arena, dtype=np.uint8)
+    acc = np.zeros(max(cap, 1), np.int64)
+    rows = L.orc_phaseb_run(_ptr(arena), base, arena.nbytes, desc_off, _ptr(acc))
+    if rows < 0:
+        raise ValueError("descriptor outside the arena")
+    return rows, acc[:rows]
+
+
+def walk_chain(arena, base, head):
+    """Descriptor offsets of a chain (next_desc_addr at byte 0 of each)."""
+    offs, off = [], head
+    while off:
+        offs.append(off)
+        off = int(np.frombuffer(arena[off - base: off - base + 4].tobytes(), np.uint32)[0])
+    return offs
+
+
+def ref_build_chain(matmuls):
+    """Builds a chain with the reference's own drivers (--fpga-phaseb) for a list of
+    (type, raw blocks, rows, cols, x).  Returns (arena bytes, base, head, ys)."""
+    R = ref()
+    for n, res, args in (("ref_phaseb_begin", ctypes.c_int, []),
+                         ("ref_phaseb_matmul", ctypes.c_int, [ctypes.c_int, _P, _I64, _I64, ctypes.c_size_t, _P, _P]),
+                         ("ref_phaseb_info", ctypes.c_int, [_P, _P, _P, _P]),
+                         ("ref_phaseb_copy", ctypes.c_int, [_P, ctypes.c_uint32, ctypes.c_uint32]),
+                         ("ref_phaseb_run", ctypes.c_int, [ctypes.c_uint32, _P, _I64]),
+                         ("ref_phaseb_verify", ctypes.c_int, [])):
+        getattr(R, n).restype = res
+        getattr(R, n).argtypes = args
+    assert R.ref_phaseb_begin() == 0
+    ys = []
+    for qt, w, rows, cols, x in matmuls:
+        w = np.ascontiguousarray(w, dtype=np.uint8)
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        y = np.zeros(rows, np.float32)
+        R.ref_phaseb_matmul(qt, _ptr(w), rows, cols, w.nbytes, _ptr(x), _ptr(y))
+        ys.append(y)
+    head, base, end, ns = (ctypes.c_uint32(), ctypes.c_uint32(), ctypes.c_uint32(), ctypes.c_int())
+    R.ref_phaseb_info(ctypes.byref(head), ctypes.byref(base), ctypes.byref(end), ctypes.byref(ns))
+    arena = np.zeros(end.value - base.value, np.uint8)
+    assert R.ref_phaseb_copy(_ptr(arena), base.value, arena.nbytes) == 0
+    return arena, base.value, head.value, ys
+
+
+def ref_chain_results(arena, base, head, cap=1 << 16):
+    """The reference runner's accumulators for every descriptor of a chain that
+    ref_build_chain just built (phaseb_run_descriptor over the reference's DDR)."""
+    R = ref()
+    out = []
+    for off in walk_chain(arena, base, head):
+        acc = np.zeros(cap, np.int64)
+        n = R.ref_phaseb_run(off, _ptr(acc), cap)
+        out.append(acc[:n].copy())
+    return out

@@ -177,3 +177,74 @@ int ref_kquant_block_sums(int type, const uint8_t* w, int64_t rows, int64_t cols
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Phase-B descriptor chain, built and replayed by the reference itself
+// (tmac_gguf.cpp:513-880).  The chain lives in the reference's simulated DDR
+// (g_ddr) from 0x18000000 up; these entry points expose it byte for byte.
+extern "C" {
+
+int ref_phaseb_begin(void)
+{
+    if (!g_ddr) {
+        g_ddr = (uint8_t*)calloc(DDR_SIZE, 1);
+        if (!g_ddr) return -1;
+    }
+    phaseb_init();
+    return 0;
+}
+
+// One matmul through the reference's FPGA-model driver with --fpga-phaseb on:
+// the driver packs the tiles into g_ddr and appends a descriptor.
+int ref_phaseb_matmul(int type, const uint8_t* w, int64_t rows, int64_t cols, size_t nbytes,
+                      const float* x, float* y)
+{
+    Tensor t = make_tensor(type, rows, cols, w, nbytes);
+    set_switches(true, true, true, true, true);
+    g_fpga_phaseb = true;
+    matmul(&t, x, y, (int)rows, (int)cols);
+    set_switches(false, false, false, false, false);
+    return 0;
+}
+
+// head: first descriptor; base/end: the allocated arena [0x18000000, next_off).
+int ref_phaseb_info(uint32_t* head, uint32_t* base, uint32_t* end, int* nslots)
+{
+    *head = g_phaseb.head;
+    *base = 0x18000000u;
+    *end = g_phaseb.next_off;
+    *nslots = (int)g_phaseb.slots.size();
+    return 0;
+}
+
+int ref_phaseb_copy(uint8_t* out, uint32_t off, uint32_t n)
+{
+    if (!g_ddr || (uint64_t)off + n > DDR_SIZE) return -1;
+    memcpy(out, g_ddr + off, n);
+    return 0;
+}
+
+int ref_phaseb_write(const uint8_t* in, uint32_t off, uint32_t n)
+{
+    if (!g_ddr || (uint64_t)off + n > DDR_SIZE) return -1;
+    memcpy(g_ddr + off, in, n);
+    return 0;
+}
+
+// phaseb_run_descriptor on a zeroed accumulator; returns the rows it wrote.
+int ref_phaseb_run(uint32_t desc_off, int64_t* acc, int64_t cap)
+{
+    auto* d = (fpga_sim::PhaseBDescriptor*)(g_ddr + desc_off);
+    int64_t need = (d->tensor_type == fpga_sim::DESC_TYPE_Q5_0)
+                       ? (int64_t)d->num_tiles * d->tile_res_rows
+                       : (d->num_col_groups ? (int64_t)(d->num_tiles / d->num_col_groups) * d->tile_res_rows : 0);
+    if (need > cap) return -1;
+    memset(acc, 0, (size_t)cap * sizeof(int64_t));
+    return phaseb_run_descriptor(desc_off, acc);
+}
+
+// phaseb_verify: replays the chain, writes int64 results at each result_addr,
+// compares against the drivers' y (|err| <= 2); returns the error count.
+int ref_phaseb_verify(void) { return phaseb_verify(); }
+
+}  // extern "C"

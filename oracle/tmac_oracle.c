@@ -488,3 +488,80 @@ int orc_gemv(int type, int path, const uint8_t* w, int64_t rows, int64_t cols,
     }
     return -1;
 }
+
+/* ------------------------------------------------------------------------ */
+/* Phase-B chain replay: phaseb_run_descriptor (tmac_gguf.cpp:761-831) on an
+ * arena holding DDR bytes [base, base + bytes).  Writes the zero-initialised
+ * accumulator acc[] and returns the rows, 0 for CPU_OP / unsupported types,
+ * -1 for an offset outside the arena. */
+static int in_arena(uint64_t off, uint64_t n, uint64_t base, uint64_t bytes)
+{
+    return off >= base && off - base <= bytes && n <= bytes - (off - base);
+}
+
+int64_t orc_phaseb_run(const uint8_t* arena, uint32_t base, uint64_t bytes, uint32_t desc_off, int64_t* acc)
+{
+    if (!in_arena(desc_off, 32, base, bytes)) return -1;
+    const uint8_t* dsc = arena + (desc_off - base);
+    uint32_t wt = rd32(dsc + 4), act = rd32(dsc + 8);
+    int ntiles = rd16(dsc + 0x10), tb = rd16(dsc + 0x12), type = dsc[0x14], tr = dsc[0x15], cg = dsc[0x19];
+    if (type == ORC_Q5_0) {
+        int64_t rows = (int64_t)ntiles * tr;
+        if (!in_arena(wt, (uint64_t)ntiles * tb, base, bytes) || !in_arena(act, 896 * 2, base, bytes)) return -1;
+        const uint8_t* xa = arena + (act - base);
+        for (int64_t r = 0; r < rows; r++) acc[r] = 0;
+        for (int t = 0; t < ntiles; t++) {
+            const uint8_t* tile = arena + (wt - base) + (int64_t)t * tb;
+            float ri[8];
+            orc_row_inv_q5_0(tile, 8, 896, ri); /* phaseb_q5_0_row_inv, :740-759 */
+            for (int i = 0; i < 8; i++)
+                for (int b = 0; b < 28; b++) {
+                    const uint8_t* blk = tile + (i * 28 + b) * 22;
+                    float d = orc_f16_to_f32(rd16(blk));
+                    uint32_t qh = rd32(blk + 2);
+                    for (int wi = 0; wi < 32; wi++) {
+                        float norm = (d * (float)q5_0_quant(blk, qh, wi)) * ri[i];
+                        acc[(int64_t)t * tr + i] +=
+                            (int64_t)clamp_round_i16(norm) * (int16_t)rd16(xa + 2 * (b * 32 + wi));
+                    }
+                }
+        }
+        return rows;
+    }
+    if (type == ORC_Q4_K || type == ORC_Q6_K) {
+        int q4 = type == ORC_Q4_K, bb = q4 ? 144 : 210, blkb = q4 ? 56 * 144 : 32 * 210;
+        if (cg == 0) return -1;
+        int64_t rows = (int64_t)(ntiles / cg) * tr;
+        if (!in_arena(wt, (uint64_t)ntiles * tb, base, bytes) || !in_arena(act, (uint64_t)cg * 512, base, bytes))
+            return -1;
+        for (int64_t r = 0; r < rows; r++) acc[r] = 0;
+        for (int ti = 0; ti < ntiles; ti++) {
+            int c = ti % cg, rg = ti / cg;
+            const uint8_t* tile = arena + (wt - base) + (int64_t)ti * tb;
+            const uint8_t* xa = arena + (act - base) + c * 512;
+            for (int bi = 0; bi < tr; bi++) {
+                int out_row = rg * tr + bi;
+                float inv = (float)rd32(tile + blkb + bi * 4) / 256.0f; /* :790-795 */
+                const uint8_t* blk = tile + bi * bb;
+                int64_t s = 0;
+                for (int wi = 0; wi < 256; wi++) {
+                    float val;
+                    if (q4) {
+                        int sc, m;
+                        q4_k_scale_min(blk + 4, wi / 32, &sc, &m);
+                        float d = orc_f16_to_f32(rd16(blk)), dmin = orc_f16_to_f32(rd16(blk + 2));
+                        val = (d * (float)sc * (float)q4_k_quant(blk, wi) - dmin * (float)m) * inv;
+                    } else {
+                        int q, sc;
+                        q6_k_quant(blk, wi, &q, &sc);
+                        val = orc_f16_to_f32(rd16(blk + 208)) * (float)sc * (float)q * inv;
+                    }
+                    s += (int64_t)(int16_t)rd16(xa + 2 * wi) * (int64_t)clamp_round_i16(val);
+                }
+                if (out_row < 896) acc[out_row] += s;
+            }
+        }
+        return rows;
+    }
+    return 0;
+}

@@ -81,6 +81,11 @@ int orc_gemv(int type, int path, const uint8_t* w, int64_t rows, int64_t cols,
              const float* x, const float* row_max_abs,
              float* y, int64_t* row_acc, int64_t* unit_acc);
 
+/* Phase-B chain replay of one descriptor (phaseb_run_descriptor,
+ * tmac_gguf.cpp:761-831) over an arena holding DDR bytes [base, base+bytes).
+ * Returns the rows written to acc (0 for CPU_OP / unsupported types), or -1. */
+int64_t orc_phaseb_run(const uint8_t* arena, uint32_t base, uint64_t bytes, uint32_t desc_off, int64_t* acc);
+
 #ifdef __cplusplus
 }
 #endif

@@ -4,7 +4,8 @@ liuwantao3/tmac-zynq-fpga sim/tmac_gguf.cpp + sim/fpga_sim.hpp compiled
 unmodified into oracle/_ref/libtmac_ref.so (oracle/Makefile).  Run from the
 repository root after `make -C oracle`:
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py           # GEMV fixtures
+    python tests/golden/make_golden.py --chain   # Phase-B chain fixture
 
 Each fixture holds seeded synthetic GGUF blocks, the activations, and the
 reference's outputs: y for the FPGA-model path (matmul_fpga_*), the INT16
@@ -51,5 +52,27 @@ def main():
         print("wrote", name)
 
 
-if __name__ == "__main__":
+if __name__ == "__main__" and "--chain" not in sys.argv:
     main()
+
+
+def make_chain_fixture():
+    """A Phase-B chain built by the reference's own drivers with --fpga-phaseb
+    (Q5_0 128x896, Q4_K 112x512, Q6_K 64x512), its DDR arena image and the
+    reference runner's int64 accumulators per descriptor."""
+    ms = [(synth.Q5_0, synth.make_weights(synth.Q5_0, 128, 896, seed=61), 128, 896,
+           synth.make_activations(896, seed=61)[0]),
+          (synth.Q4_K, synth.make_weights(synth.Q4_K, 112, 512, seed=62), 112, 512,
+           synth.make_activations(512, seed=62)[0]),
+          (synth.Q6_K, synth.make_weights(synth.Q6_K, 64, 512, seed=63), 64, 512,
+           synth.make_activations(512, seed=63)[0])]
+    arena, base, head, ys = oracle.ref_build_chain(ms)
+    res = oracle.ref_chain_results(arena, base, head)
+    np.savez_compressed(os.path.join(HERE, "phaseb_chain.npz"), arena=arena, base=np.uint32(base),
+                        head=np.uint32(head), offsets=np.array(oracle.walk_chain(arena, base, head), np.uint32),
+                        results=np.concatenate(res), counts=np.array([len(r) for r in res], np.int64))
+    print("wrote phaseb_chain")
+
+
+if __name__ == "__main__" and "--chain" in sys.argv:
+    make_chain_fixture()

@@ -40,6 +40,11 @@ class TmacError(RuntimeError):
         self.code = code
 
 
+class ChainStats(ctypes.Structure):
+    """tmac_chain_stats"""
+    _fields_ = [("descriptors", ctypes.c_int), ("unsupported", ctypes.c_int), ("result_rows", ctypes.c_int64)]
+
+
 _lib = None
 _P = ctypes.c_void_p
 _I64 = ctypes.c_int64
@@ -78,6 +83,8 @@ def lib():
             "tmac_gemv_int16": (ctypes.c_int, [_P, _P, _P, ctypes.c_int, _P]),
             "tmac_gemv_host": (ctypes.c_int, [_P, _P, _P, ctypes.c_int]),
             "tmac_reserve": (ctypes.c_int, [ctypes.c_int, _I64, _I64]),
+            "tmac_chain_run": (ctypes.c_int, [_P, ctypes.c_size_t, ctypes.c_uint32, _P, ctypes.c_uint32,
+                                              ctypes.c_int, ctypes.POINTER(ChainStats), _P]),
         }
         for name, (res, args) in sig.items():
             f = getattr(L, name)
@@ -285,3 +292,13 @@ def matmul(A, x, y, rows, cols, sw: Switches | None = None):
             return matmul_fpga_q8(A, x, y, rows, cols)
         return matmul_fpga_int16(A, x, y, rows, cols)
     _run(A, x, y, rows, cols, MODE_F32)
+
+
+def chain_run(arena_dev, arena_bytes, base, head, arena_host=None, max_desc=1 << 20, stream=None):
+    """Replays a Phase-B descriptor chain held in a device arena (tmac_chain_run);
+    the int64 results land at each descriptor's result_addr inside the arena."""
+    st = ChainStats()
+    s = None if stream is None else (stream if isinstance(stream, int) else stream.cuda_stream)
+    check(lib().tmac_chain_run(_ptr(arena_dev), arena_bytes, base, _ptr(arena_host), head, max_desc,
+                               ctypes.byref(st), s))
+    return st

@@ -1,0 +1,238 @@
+// chain.cu -- Phase-B descriptor-chain runner (tmac_chain_run).
+//
+// Replaces phaseb_run_descriptor as driven by phaseb_verify
+// (sim/tmac_gguf.cpp:761-831, :834-880): walk the PhaseBDescriptor list
+// (sim/fpga_sim.hpp:1254-1279) held in a DDR-image arena and, per descriptor,
+// compute the int64 row accumulators of the packed tiles the way the
+// reference's core models do, then store them at result_addr.
+//   Q5_0 (type 6): 8x896 tiles of 224 GGUF blocks; row_inv is recomputed from
+//                  the tile's own blocks (phaseb_q5_0_row_inv, :740-759) and the
+//                  UQ16.8 scale section is ignored, as the reference does.
+//   Q4_K (12) / Q6_K (14): 56/32-row x 256-col tiles, tile index
+//                  ti = row_group * num_col_groups + col_group; row_inv =
+//                  (float)UQ24.8 / 256 from the tile's scale section.
+//   CPU_OP (15): no arithmetic, 0 rows.  Any other type: skipped, 0 rows.
+// The chain is walked on the host (descriptors are 32 bytes; the arena's host
+// mirror is used when the caller has one), every offset is bounds-checked, and
+// one kernel per arithmetic descriptor is enqueued in chain order.
+#include "common.cuh"
+#include "dequant.cuh"
+
+#include <cstring>
+#include <vector>
+
+namespace tmac {
+namespace {
+
+constexpr int kQ5Cols = 896, kQ5BlocksPerRow = 28, kQ5Rows = 8;
+constexpr int kQ4kBlkBytes = 56 * 144, kQ6kBlkBytes = 32 * 210;
+
+TMAC_DEV uint32_t ld_u32_bytes(const uint8_t* p)
+{
+    return (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);
+}
+TMAC_DEV int16_t ld_i16_bytes(const uint8_t* p) { return (int16_t)(uint16_t)(p[0] | (p[1] << 8)); }
+
+TMAC_DEV void st_i64_bytes(uint8_t* p, long long v)
+{
+    if (((uintptr_t)p & 7) == 0) {
+        *reinterpret_cast<long long*>(p) = v;
+    } else {
+        for (int i = 0; i < 8; i++) p[i] = (uint8_t)((unsigned long long)v >> (8 * i));
+    }
+}
+
+TMAC_DEV long long warp_sum_i64(long long v)
+{
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// One CTA per tile, one warp per row, one lane per 32-value block.
+__global__ void __launch_bounds__(256) chain_q5_0_kernel(const uint8_t* __restrict__ weight, const uint8_t* __restrict__ act,
+                                                         uint8_t* result, int tile_bytes)
+{
+    const int t = blockIdx.x, i = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint8_t* row = weight + (int64_t)t * tile_bytes + i * kQ5BlocksPerRow * 22;
+    const bool has = lane < kQ5BlocksPerRow;
+    float d = 0.0f;
+    uint32_t qh = 0;
+    const uint8_t* blk = row + (has ? lane : 0) * 22;
+    if (has) {
+        d = f16_bits_to_f32(ld_u16_unaligned(blk));
+        qh = ld_u32_bytes(blk + 2);
+    }
+    // row_inv from this tile's blocks (tmac_gguf.cpp:740-759)
+    float mx = 0.0f;
+    if (has)
+        for (int wi = 0; wi < 32; wi++) {
+            const int j = wi < 16 ? wi : wi - 16;
+            const int ql = wi < 16 ? (blk[6 + j] & 0xF) : (blk[6 + j] >> 4);
+            const int q = ((((qh >> wi) & 1) << 4) | ql) - 16;
+            mx = fmaxf(mx, fabsf(__fmul_rn(d, (float)q)));
+        }
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const float ri = __fdiv_rn(32767.0f, (mx < 1e-10f) ? 1.0f : mx);
+    // axi_vecmul_tile_q5_0_8x896_axilite (fpga_sim.hpp:1004-1052)
+    long long acc = 0;
+    if (has)
+        for (int wi = 0; wi < 32; wi++) {
+            const int j = wi < 16 ? wi : wi - 16;
+            const int ql = wi < 16 ? (blk[6 + j] & 0xF) : (blk[6 + j] >> 4);
+            const int q = ((((qh >> wi) & 1) << 4) | ql) - 16;
+            const int v = clamp_round_i16(__fmul_rn(__fmul_rn(d, (float)q), ri));
+            acc += (long long)v * (long long)ld_i16_bytes(act + 2 * (lane * 32 + wi));
+        }
+    acc = warp_sum_i64(acc);
+    if (lane == 0) st_i64_bytes(result + ((int64_t)t * kQ5Rows + i) * 8, acc);
+}
+
+// One CTA per row group, one warp per row, 8 values per lane per column group.
+template <int TYPE>
+__global__ void __launch_bounds__(256) chain_kquant_kernel(const uint8_t* __restrict__ weight,
+                                                           const uint8_t* __restrict__ act, uint8_t* result,
+                                                           int tile_bytes, int tr, int cg)
+{
+    constexpr int BB = (TYPE == TMAC_TYPE_Q4_K) ? 144 : 210;
+    constexpr int BLK = (TYPE == TMAC_TYPE_Q4_K) ? kQ4kBlkBytes : kQ6kBlkBytes;
+    const int rg = blockIdx.x, lane = threadIdx.x & 31;
+    for (int bi = threadIdx.x >> 5; bi < tr; bi += blockDim.x >> 5) {
+        const int out_row = rg * tr + bi;
+        long long acc = 0;
+        for (int c = 0; c < cg; c++) {
+            const uint8_t* tile = weight + ((int64_t)rg * cg + c) * tile_bytes;
+            const uint8_t* blk = tile + bi * BB;
+            // row_inv from the tile's UQ24.8 scale section (tmac_gguf.cpp:790-795)
+            const float ri = __fdiv_rn(__uint2float_rn(ld_u32_bytes(tile + BLK + bi * 4)), 256.0f);
+            const uint8_t* a = act + c * 256 * 2;
+            long long s = 0;
+            for (int k = 0; k < 8; k++) {
+                const int wi = lane * 8 + k;
+                float val;
+                if (TYPE == TMAC_TYPE_Q4_K) {
+                    // axilite_q4k_run (fpga_sim.hpp:730-788)
+                    const float d = f16_bits_to_f32(ld_u16_unaligned(blk));
+                    const float dmin = f16_bits_to_f32(ld_u16_unaligned(blk + 2));
+                    int sc, m;
+                    q4_k_scale_min(blk + 4, wi / 32, sc, m);
+                    if (sc > 63) sc = 63;
+                    if (m > 63) m = 63;
+                    const int sub = wi / 32, j = wi % 32;
+                    const uint8_t qb = blk[16 + (sub / 2) * 32 + j];
+                    const int q4 = (sub % 2 == 0) ? (qb & 0xF) : (qb >> 4);
+                    val = __fmul_rn(__fsub_rn(__fmul_rn(__fmul_rn(d, (float)sc), (float)q4), __fmul_rn(dmin, (float)m)),
+                                    ri);
+                } else {
+                    // axi_vecmul_tile_q6_k_axilite (fpga_sim.hpp:1058-1115)
+                    const float d = f16_bits_to_f32(ld_u16_unaligned(blk + 208));
+                    const int half = wi / 128, pos = wi % 128, l = pos % 32, sub = pos / 32;
+                    const uint8_t lb = blk[half * 64 + l + (sub % 2) * 32];
+                    const int ql = (sub < 2) ? (lb & 0xF) : (lb >> 4);
+                    const int qh = (blk[128 + half * 32 + l] >> (sub * 2)) & 0x3;
+                    const int q6 = ((qh << 4) | ql) - 32;
+                    const float scf = (float)(int8_t)blk[192 + half * 8 + (l / 16) + sub * 2];
+                    val = __fmul_rn(__fmul_rn(__fmul_rn(d, scf), (float)q6), ri);
+                }
+                s += (long long)ld_i16_bytes(a + 2 * wi) * (long long)clamp_round_i16(val);
+            }
+            acc += warp_sum_i64(s);
+        }
+        // the reference's accumulator only takes rows < 896 (fpga_sim.hpp:784, :1110)
+        if (lane == 0) st_i64_bytes(result + (int64_t)out_row * 8, out_row < 896 ? acc : 0);
+    }
+}
+
+struct Walked {
+    tmac_phaseb_desc d;
+    int64_t rows;
+};
+
+bool in_arena(uint64_t off, uint64_t n, uint64_t base, uint64_t bytes)
+{
+    return off >= base && off - base <= bytes && n <= bytes - (off - base);
+}
+
+}  // namespace
+}  // namespace tmac
+
+using namespace tmac;
+
+extern "C" int tmac_chain_run(void* arena_dev, size_t arena_bytes, uint32_t arena_base, const void* arena_host,
+                              uint32_t head, int max_desc, tmac_chain_stats* stats, void* stream)
+{
+    if (!arena_dev) return fail(TMAC_ERR_INVALID, "NULL arena");
+    if (max_desc <= 0) return fail(TMAC_ERR_INVALID, "max_desc must be positive");
+    cudaStream_t s = (cudaStream_t)stream;
+    uint8_t* dev = static_cast<uint8_t*>(arena_dev);
+    const uint8_t* host = static_cast<const uint8_t*>(arena_host);
+    std::vector<Walked> chain;
+    tmac_chain_stats st{};
+    // 1. walk and validate the whole chain before launching anything
+    for (uint32_t off = head; off != 0;) {
+        if ((int)chain.size() >= max_desc)
+            return fail(TMAC_ERR_BOUNDS, "descriptor chain longer than max_desc (cycle?)");
+        if (!in_arena(off, sizeof(tmac_phaseb_desc), arena_base, arena_bytes))
+            return fail(TMAC_ERR_BOUNDS, "descriptor offset outside the arena");
+        Walked w;
+        if (host) {
+            memcpy(&w.d, host + (off - arena_base), sizeof(w.d));
+        } else {
+            TMAC_CUDA_TRY(cudaMemcpy(&w.d, dev + (off - arena_base), sizeof(w.d), cudaMemcpyDeviceToHost));
+        }
+        const tmac_phaseb_desc& d = w.d;
+        const uint64_t tiles_end = (uint64_t)d.num_tiles * d.tile_bytes;
+        w.rows = 0;
+        switch (d.tensor_type) {
+        case TMAC_DESC_TYPE_Q5_0:
+            if (d.tile_res_rows != 8 || d.tile_bytes < 224 * 22)
+                return fail(TMAC_ERR_BOUNDS, "Q5_0 descriptor: tiles must be 8 rows x 896 columns");
+            w.rows = (int64_t)d.num_tiles * 8;
+            if (!in_arena(d.weight_addr, tiles_end, arena_base, arena_bytes) ||
+                !in_arena(d.act_addr, kQ5Cols * 2, arena_base, arena_bytes) ||
+                !in_arena(d.result_addr, (uint64_t)w.rows * 8, arena_base, arena_bytes))
+                return fail(TMAC_ERR_BOUNDS, "Q5_0 descriptor: weight/act/result outside the arena");
+            break;
+        case TMAC_DESC_TYPE_Q4_K:
+        case TMAC_DESC_TYPE_Q6_K: {
+            const bool q4 = d.tensor_type == TMAC_DESC_TYPE_Q4_K;
+            const int bb = q4 ? 144 : 210, blk = q4 ? kQ4kBlkBytes : kQ6kBlkBytes;
+            if (d.num_col_groups == 0 || d.num_tiles % d.num_col_groups)
+                return fail(TMAC_ERR_BOUNDS, "K-quant descriptor: num_tiles must be a multiple of num_col_groups");
+            if (d.tile_res_rows == 0 || d.tile_res_rows * bb > blk || d.tile_bytes < blk + d.tile_res_rows * 4)
+                return fail(TMAC_ERR_BOUNDS, "K-quant descriptor: tile_res_rows / tile_bytes inconsistent");
+            w.rows = (int64_t)(d.num_tiles / d.num_col_groups) * d.tile_res_rows;
+            if (!in_arena(d.weight_addr, tiles_end, arena_base, arena_bytes) ||
+                !in_arena(d.act_addr, (uint64_t)d.num_col_groups * 512, arena_base, arena_bytes) ||
+                !in_arena(d.result_addr, (uint64_t)w.rows * 8, arena_base, arena_bytes))
+                return fail(TMAC_ERR_BOUNDS, "K-quant descriptor: weight/act/result outside the arena");
+            break;
+        }
+        case TMAC_DESC_TYPE_CPU_OP: break;
+        default: st.unsupported++; break;
+        }
+        chain.push_back(w);
+        off = d.next_desc_addr;
+    }
+    // 2. enqueue one kernel per arithmetic descriptor, in chain order
+    for (const Walked& w : chain) {
+        const tmac_phaseb_desc& d = w.d;
+        st.descriptors++;
+        st.result_rows += w.rows;
+        if (w.rows == 0) continue;
+        const uint8_t* wt = dev + (d.weight_addr - arena_base);
+        const uint8_t* act = dev + (d.act_addr - arena_base);
+        uint8_t* res = dev + (d.result_addr - arena_base);
+        if (d.tensor_type == TMAC_DESC_TYPE_Q5_0) {
+            chain_q5_0_kernel<<<d.num_tiles, 256, 0, s>>>(wt, act, res, d.tile_bytes);
+        } else if (d.tensor_type == TMAC_DESC_TYPE_Q4_K) {
+            chain_kquant_kernel<TMAC_TYPE_Q4_K><<<d.num_tiles / d.num_col_groups, 256, 0, s>>>(
+                wt, act, res, d.tile_bytes, d.tile_res_rows, d.num_col_groups);
+        } else {
+            chain_kquant_kernel<TMAC_TYPE_Q6_K><<<d.num_tiles / d.num_col_groups, 256, 0, s>>>(
+                wt, act, res, d.tile_bytes, d.tile_res_rows, d.num_col_groups);
+        }
+        TMAC_CUDA_TRY(cudaGetLastError());
+    }
+    if (stats) *stats = st;
+    return TMAC_OK;
+}
