@@ -6,7 +6,9 @@ shards, one process per GPU).
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
 A step is one pass of the hot path over one activation vector: the GEMV over
-this rank's vocab shard (one kernel launch).  value = algorithmic bytes of all
+this rank's vocab shard with the shard's top-1 key fused into it (one kernel
+launch) and, on N > 1 GPUs, one int64 MAX all-reduce of the key (NCCL) so every
+rank holds the global greedy token.  value = algorithmic bytes of all
 ranks' shards (weights + x + y) / max-over-ranks device time, in GB/s.
 Weights are seeded synthetic GGUF blocks (no checkpoint available); each rank
 rotates over enough distinct weight copies that every step streams its shard
@@ -36,7 +38,7 @@ VOCAB, HIDDEN = 151936, 896
 Q8_BLOCK_BYTES = 34
 METRIC = json.load(open(os.path.join(ROOT, "BASELINE.json")))["metric"]
 UNIT = "GB/s"
-WORKLOAD = "Q8_0 tied-embedding logits GEMV 151936x896, batch 1 (BASELINE config 2)"
+WORKLOAD = "Q8_0 tied-embedding logits GEMV 151936x896 + argmax, batch 1 (BASELINE config 2)"
 L2_BYTES = 126 * 1024 * 1024
 
 
@@ -234,10 +236,15 @@ def main():
     torch.cuda.synchronize()
     x = torch.from_numpy(synth.make_activations(HIDDEN, seed=0)).cuda()
     y = torch.empty(rows, dtype=torch.float32, device="cuda")
+    key = torch.zeros(1, dtype=torch.int64, device="cuda")
     stream = torch.cuda.current_stream()
 
     def step(i):
-        weights[i % ncopies].gemv(x, y, stream=stream)
+        # logits of this rank's vocab shard + their top-1 key (one fused kernel),
+        # then the global greedy token: one int64 MAX all-reduce over NCCL.
+        weights[i % ncopies].gemv_top1(x, y, key, index_base=r0, stream=stream)
+        if world > 1:
+            dist.all_reduce(key, op=dist.ReduceOp.MAX)
 
     for i in range(args.warmup):
         step(i)
@@ -291,6 +298,11 @@ def main():
     clocks = sampler.stop()
     e2e_val = total_bytes / (float(e2e_ms.item()) * 1e-3) / 1e9
     assert tm.device_error(local) == 0
+    # the greedy token of the last step must be the global argmax of the logits
+    tok = tm.top1_decode(key.item())[1]
+    yl = y.cpu().numpy()
+    if world == 1:
+        assert tok == int(np.argmax(yl)), "fused top-1 disagrees with argmax of the logits"
 
     if rank == 0:
         pk, pk_kind = peaks()
@@ -304,6 +316,8 @@ def main():
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "int16/int64", "data": "synthetic",
             "config": {"workload": WORKLOAD, "rows": VOCAB, "cols": HIDDEN, "batch": 1,
+                       "step": "shard logits GEMV with fused top-1 key" + (" + NCCL int64 MAX all-reduce" if world > 1 else ""),
+                       "greedy_token": tok,
                        "parallelism": f"vocab-row shards x{world}", "shard_rows": rows,
                        "l2": f"inputs larger than L2: {ncopies} rotating weight copies of "
                              f"{per_copy / 1e6:.1f} MB per rank"},

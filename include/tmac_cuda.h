@@ -134,6 +134,23 @@ int tmac_gemv_int16(tmac_weight_t w, const float* x, float* y, int batch, void* 
  */
 int tmac_gemv_host(tmac_weight_t w, const float* x_host, float* y_host, int batch);
 
+/*
+ * Greedy top-1 over logits: the largest y and, among equal values, the lowest
+ * index, packed as a 63-bit key (order-preserving float bits << 31 |
+ * 0x7FFFFFFF - index) so that vocab shards on several GPUs merge with one
+ * int64 MAX all-reduce.  Stands in for sample_token / the top-10 print of the
+ * reference (tmac_gguf.cpp:1974-1990, :2164-2172) in greedy decoding.
+ *   tmac_top1:      max-merges the key of y[0..n) (indices + index_base) into
+ *                   *key (device); zero *key first for a fresh result.
+ *   tmac_gemv_top1: y = W.x and key[b] = top-1 of y[b] (key zeroed here).  For
+ *                   Q8_0 the top-1 is fused into the GEMV kernel's epilogue.
+ *   tmac_top1_decode: host-side unpacking of a key.
+ */
+int tmac_top1(const float* y, int64_t n, int64_t index_base, uint64_t* key, void* stream);
+int tmac_gemv_top1(tmac_weight_t w, const float* x, float* y, uint64_t* key, int64_t index_base, int batch,
+                   void* stream);
+int tmac_top1_decode(uint64_t key, float* value, int64_t* index);
+
 /* Allocate the per-device workspace for GEMVs up to batch x cols now, so that
  * later calls allocate nothing (required before CUDA-graph capture). */
 int tmac_reserve(int device, int64_t max_batch, int64_t max_cols);

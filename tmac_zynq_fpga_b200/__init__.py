@@ -83,6 +83,10 @@ def lib():
             "tmac_gemv_int16": (ctypes.c_int, [_P, _P, _P, ctypes.c_int, _P]),
             "tmac_gemv_host": (ctypes.c_int, [_P, _P, _P, ctypes.c_int]),
             "tmac_reserve": (ctypes.c_int, [ctypes.c_int, _I64, _I64]),
+            "tmac_top1": (ctypes.c_int, [_P, _I64, _I64, _P, _P]),
+            "tmac_gemv_top1": (ctypes.c_int, [_P, _P, _P, _P, _I64, ctypes.c_int, _P]),
+            "tmac_top1_decode": (ctypes.c_int, [ctypes.c_uint64, ctypes.POINTER(ctypes.c_float),
+                                                ctypes.POINTER(_I64)]),
             "tmac_chain_run": (ctypes.c_int, [_P, ctypes.c_size_t, ctypes.c_uint32, _P, ctypes.c_uint32,
                                               ctypes.c_int, ctypes.POINTER(ChainStats), _P]),
         }
@@ -168,6 +172,11 @@ class Weight:
         """Device GEMV on torch tensors / device pointers (asynchronous)."""
         s = None if stream is None else (stream if isinstance(stream, int) else stream.cuda_stream)
         check(lib().tmac_gemv_acc(self.handle, _ptr(x), _ptr(y), _ptr(row_acc), _ptr(unit_acc), batch, s))
+
+    def gemv_top1(self, x, y, key, index_base=0, batch=1, stream=None):
+        """y = W.x plus the packed top-1 key of y (device uint64/int64 key[batch])."""
+        s = None if stream is None else (stream if isinstance(stream, int) else stream.cuda_stream)
+        check(lib().tmac_gemv_top1(self.handle, _ptr(x), _ptr(y), _ptr(key), index_base, batch, s))
 
     def gemv_host(self, x, batch=None):
         """Host-buffer GEMV: numpy x[batch][cols] -> numpy y[batch][rows] (synchronous)."""
@@ -302,3 +311,10 @@ def chain_run(arena_dev, arena_bytes, base, head, arena_host=None, max_desc=1 <<
     check(lib().tmac_chain_run(_ptr(arena_dev), arena_bytes, base, _ptr(arena_host), head, max_desc,
                                ctypes.byref(st), s))
     return st
+
+
+def top1_decode(key):
+    """(value, index) of a packed top-1 key."""
+    v, i = ctypes.c_float(), _I64()
+    check(lib().tmac_top1_decode(ctypes.c_uint64(int(key) & 0xFFFFFFFFFFFFFFFF), ctypes.byref(v), ctypes.byref(i)))
+    return v.value, i.value

@@ -94,6 +94,18 @@ TMAC_DEV float block_max(float v, float* red, int nthreads)
     return m;
 }
 
+// Top-1 key of logit v at global index idx: the float's bits mapped to an
+// unsigned order (negatives inverted, positives with the sign bit set) in bits
+// 62..31, then 0x7FFFFFFF - idx, so the largest key is the largest logit and,
+// among equal logits, the lowest index.  The key is non-negative as an int64,
+// so an NCCL / torch int64 MAX all-reduce merges vocab shards.  0 = no key.
+TMAC_DEV unsigned long long top1_key(float v, int64_t idx)
+{
+    uint32_t u = __float_as_uint(v);
+    u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return ((unsigned long long)u << 31) | (0x7FFFFFFFull - (unsigned long long)(idx & 0x7FFFFFFF));
+}
+
 // x_scale of tmac_gguf.cpp:889-892 from max|x|.
 TMAC_DEV float x_scale_from_max(float mx) { return (mx < 1e-10f) ? 1.0f : __fdiv_rn(mx, 32767.0f); }
 // x_q of tmac_gguf.cpp:894-896.
@@ -180,7 +192,8 @@ namespace tmac {
 // Per-path launchers (one per .cu file).  All return TMAC_OK or an error.
 int register_q8_0(tmac_weight_s* w, const uint8_t* d_raw, const float* d_row_max_abs, cudaStream_t s);
 int launch_q8_0(const tmac_weight_s* w, const float* x, float* y, int64_t* row_acc, int64_t* unit_acc,
-                int batch, cudaStream_t s);
+                int batch, cudaStream_t s, unsigned long long* top1 = nullptr, int64_t index_base = 0);
+int launch_top1(const float* y, int64_t n, int64_t index_base, unsigned long long* key, cudaStream_t s);
 int register_blockq(tmac_weight_s* w, const uint8_t* d_raw, cudaStream_t s);
 int launch_blockq(const tmac_weight_s* w, const float* x, float* y, int64_t* row_acc, int64_t* unit_acc,
                   int batch, cudaStream_t s);

@@ -163,6 +163,8 @@ struct Q8Args {
     float* y;
     int64_t* row_acc;
     int64_t* unit_acc;
+    unsigned long long* top1;  // optional: max packed (value, index) key, see top1_key
+    int64_t index_base;        // global row index of row 0 (vocab shard offset)
     int* err;
 };
 
@@ -272,6 +274,7 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemv_kernel(Q8Args a)
     if (warp >= kFoldWarp0) {
         const int f = warp - kFoldWarp0;
         // ---------------- fold: y = sum over tiles in order (tmac_gguf.cpp:1075-1076)
+        unsigned long long best = 0;  // running top-1 key of this warp's rows
         for (int i = f; i < ng; i += kFoldWarps) {
             const int b = i % kAccBufs;
             if (*abort_flag || !mbar_wait_bounded(&acc_full[b], (i / kAccBufs) & 1, a.err)) {
@@ -294,9 +297,18 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemv_kernel(Q8Args a)
             if (r < a.rows) {
                 a.y[r] = yr;
                 if (a.row_acc) a.row_acc[r] = rsum;
+                const unsigned long long k = top1_key(yr, a.index_base + r);
+                best = k > best ? k : best;
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&acc_empty[b]);
+        }
+        if (a.top1) {
+            for (int o = 16; o > 0; o >>= 1) {
+                const unsigned long long k = __shfl_xor_sync(0xffffffffu, best, o);
+                best = k > best ? k : best;
+            }
+            if (lane == 0 && best) atomicMax(a.top1, best);
         }
         return;
     }
@@ -423,7 +435,7 @@ int register_q8_0(tmac_weight_s* w, const uint8_t* d_raw, const float* d_row_max
 }
 
 int launch_q8_0(const tmac_weight_s* w, const float* x, float* y, int64_t* row_acc, int64_t* unit_acc, int batch,
-                cudaStream_t s)
+                cudaStream_t s, unsigned long long* top1, int64_t index_base)
 {
     Q8Layout L = q8_layout(w->rows, w->cols);
     const size_t smem = q8_smem_bytes(L);
@@ -443,6 +455,8 @@ int launch_q8_0(const tmac_weight_s* w, const float* x, float* y, int64_t* row_a
         a.y = y + (int64_t)b * w->rows;
         a.row_acc = row_acc ? row_acc + (int64_t)b * w->rows : nullptr;
         a.unit_acc = unit_acc ? unit_acc + (int64_t)b * w->rows * L.T : nullptr;
+        a.top1 = top1 ? top1 + b : nullptr;
+        a.index_base = index_base;
         a.err = device_error_word(w->device);
         q8_gemv_kernel<<<grid, kThreads, smem, s>>>(a);
         TMAC_CUDA_TRY(cudaGetLastError());

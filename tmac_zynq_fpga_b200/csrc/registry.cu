@@ -398,6 +398,44 @@ int tmac_gemv_host(tmac_weight_t w, const float* x_host, float* y_host, int batc
     return TMAC_OK;
 }
 
+int tmac_top1(const float* y, int64_t n, int64_t index_base, uint64_t* key, void* stream)
+{
+    if (!y || !key) return fail(TMAC_ERR_INVALID, "NULL y or key");
+    if (n <= 0 || index_base < 0 || index_base + n > 0x7FFFFFFF) return fail(TMAC_ERR_SHAPE, "bad index range");
+    return launch_top1(y, n, index_base, reinterpret_cast<unsigned long long*>(key), (cudaStream_t)stream);
+}
+
+int tmac_gemv_top1(tmac_weight_t w, const float* x, float* y, uint64_t* key, int64_t index_base, int batch,
+                   void* stream)
+{
+    int rc = weight_ok(w);
+    if (rc) return rc;
+    if (!x || !y || !key) return fail(TMAC_ERR_INVALID, "NULL x, y or key");
+    if (batch <= 0) return fail(TMAC_ERR_SHAPE, "batch must be positive");
+    if (index_base < 0 || index_base + w->rows > 0x7FFFFFFF) return fail(TMAC_ERR_SHAPE, "bad index range");
+    DeviceGuard dg(w->device);
+    cudaStream_t s = (cudaStream_t)stream;
+    TMAC_CUDA_TRY(cudaMemsetAsync(key, 0, (size_t)batch * sizeof(uint64_t), s));
+    unsigned long long* k = reinterpret_cast<unsigned long long*>(key);
+    if (w->mode == TMAC_MODE_NATIVE && w->type == TMAC_TYPE_Q8_0)
+        return launch_q8_0(w, x, y, nullptr, nullptr, batch, s, k, index_base);
+    rc = tmac_gemv(w, x, y, batch, stream);
+    for (int b = 0; !rc && b < batch; b++) rc = launch_top1(y + (int64_t)b * w->rows, w->rows, index_base, k + b, s);
+    return rc;
+}
+
+int tmac_top1_decode(uint64_t key, float* value, int64_t* index)
+{
+    if (!key) return fail(TMAC_ERR_INVALID, "empty key");
+    uint32_t u = (uint32_t)(key >> 31);
+    u = (u & 0x80000000u) ? (u & 0x7FFFFFFFu) : ~u;
+    float v;
+    memcpy(&v, &u, sizeof(v));
+    if (value) *value = v;
+    if (index) *index = (int64_t)(0x7FFFFFFFu - (uint32_t)(key & 0x7FFFFFFFu));
+    return TMAC_OK;
+}
+
 int tmac_reserve(int device, int64_t max_batch, int64_t max_cols)
 {
     (void)max_batch;

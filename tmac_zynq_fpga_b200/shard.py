@@ -1,0 +1,45 @@
+"""Vocab-row sharding of the tied-embedding logits GEMV across GPUs.
+
+Each rank owns rows [r0, r1) of the 151936 x 896 Q8_0 matrix (contiguous,
+151936 / world rows), computes its logits shard and the top-1 key of the shard
+(tmac_gemv_top1, index_base = r0), and one int64 MAX all-reduce of that key
+gives every rank the global greedy token.  The key layout is top1_key in
+csrc/common.cuh: order-preserving float bits << 31 | (0x7FFFFFFF - index).
+"""
+from __future__ import annotations
+
+import numpy as np
+
+
+def shard_bounds(rows: int, world: int, rank: int):
+    """Contiguous row range of `rank` (sizes differ by at most one row)."""
+    return rank * rows // world, (rank + 1) * rows // world
+
+
+def pack_keys(y: np.ndarray, index_base: int = 0) -> np.ndarray:
+    """Host version of the device key, one per element of y (for checks)."""
+    u = np.ascontiguousarray(y, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    neg = (u & 0x80000000) != 0
+    ordered = np.where(neg, (~u) & 0xFFFFFFFF, u | 0x80000000)
+    idx = np.arange(y.size, dtype=np.uint64) + np.uint64(index_base)
+    return ((ordered << np.uint64(31)) | (np.uint64(0x7FFFFFFF) - idx)).astype(np.int64)
+
+
+def unpack_key(key: int):
+    """(value, index) of a key."""
+    key = int(key)
+    u = (key >> 31) & 0xFFFFFFFF
+    u = (u & 0x7FFFFFFF) if (u & 0x80000000) else (~u & 0xFFFFFFFF)
+    return float(np.array([u], np.uint32).view(np.float32)[0]), 0x7FFFFFFF - (key & 0x7FFFFFFF)
+
+
+def top1_index(y: np.ndarray) -> int:
+    """Lowest index among the largest values (the key's tie rule)."""
+    return int(np.argmax(y))  # numpy returns the first maximum
+
+
+def all_reduce_top1(key_tensor, group=None):
+    """Merges per-rank keys (int64 tensor) in place with a MAX all-reduce."""
+    import torch.distributed as dist
+    dist.all_reduce(key_tensor, op=dist.ReduceOp.MAX, group=group)
+    return key_tensor
