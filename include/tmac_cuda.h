@@ -215,6 +215,49 @@ typedef struct tmac_chain_stats {
 int tmac_chain_run(void* arena_dev, size_t arena_bytes, uint32_t arena_base, const void* arena_host,
                    uint32_t head, int max_desc, tmac_chain_stats* stats, void* stream);
 
+/* ------------------------------------------------------------------------ */
+/* Whole-model greedy decode (Qwen2-0.5B shape: 24 layers, hidden 896, 14/2
+ * heads of 64, SwiGLU 4864, vocab 151936, tied Q8_0 embedding), replacing the
+ * reference engine's process_prompt / generate loop (sim/tmac_gguf.cpp:1992-2047,
+ * forward_layer_with_cache :1559-1711, get_logits_q8 :1820-1845) with the top-k
+ * sampler replaced by greedy top-1 (lowest index on ties).
+ * switches: the reference's --fpga-* flags (tmac_gguf.cpp:2084-2091) as bits;
+ * a matrix whose type switch is off runs the INT16 path when TMAC_SW_FPGA is
+ * set, and everything runs the FP32 path when it is not (matmul(), :473-493). */
+#define TMAC_SW_FPGA 1  /* --fpga / --fpga-int16 (implied by every type switch) */
+#define TMAC_SW_Q8 2    /* --fpga-q8   */
+#define TMAC_SW_Q5_0 4  /* --fpga-q5-0 */
+#define TMAC_SW_Q4_K 8  /* --fpga-q4k  */
+#define TMAC_SW_Q6_K 16 /* --fpga-q6-k */
+#define TMAC_SW_ALL 31  /* all four type switches */
+
+typedef struct tmac_model_s* tmac_model_t;
+
+/* Empty model on `device` with a KV cache of max_seq positions. */
+int tmac_model_create(int device, int switches, int max_seq, tmac_model_t* out);
+/* Adds one tensor by its GGUF name (copied): the records load_tmac reads. */
+int tmac_model_add_tensor(tmac_model_t m, const char* name, int64_t rows, int64_t cols, int type, const void* data,
+                          size_t n_bytes);
+/* Reads every tensor of a `.tmac` file (load_tmac, tmac_gguf.cpp:1894-1947). */
+int tmac_model_load_tmac(tmac_model_t m, const char* path);
+/* Registers all matrices on the device and allocates the decode state. */
+int tmac_model_finalize(tmac_model_t m);
+/* Clears the KV cache (reset_cache, :1950-1956). */
+int tmac_model_reset(tmac_model_t m, void* stream);
+/* One token through all layers at `pos` (process_embedding + forward_all_layers).
+ * token < 0 takes the token from the model's device top-1 key (the last
+ * tmac_model_logits), so greedy steps chain without a host round trip. */
+int tmac_model_forward(tmac_model_t m, int token, int pos, void* stream);
+/* output_norm + logits GEMV of the current hidden state + greedy top-1 key. */
+int tmac_model_logits(tmac_model_t m, void* stream);
+/* Device addresses of the hidden state [896], logits [151936] and the key. */
+int tmac_model_buffers(tmac_model_t m, float** hidden, float** logits, uint64_t** key);
+/* Prompt + n_gen greedy steps; out_tokens[n_gen] (host); out_hidden optional
+ * host float[(n_gen + 1) * 896]: after the prompt and after each step. */
+int tmac_model_generate(tmac_model_t m, const int* prompt, int n_prompt, int n_gen, int* out_tokens,
+                        float* out_hidden, void* stream);
+int tmac_model_free(tmac_model_t m);
+
 #ifdef __cplusplus
 }
 #endif

@@ -248,3 +248,46 @@ int ref_phaseb_run(uint32_t desc_off, int64_t* acc, int64_t cap)
 int ref_phaseb_verify(void) { return phaseb_verify(); }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Whole-model greedy decode with the reference engine itself: load_tmac,
+// process_prompt, then per step get_logits_q8 / argmax / process_embedding /
+// forward_all_layers -- generate() (tmac_gguf.cpp:2025-2047) with the top-k
+// sampler replaced by a lowest-index argmax.
+// fpga = 1: --fpga-q8 --fpga-q5-0 --fpga-q4k --fpga-q6-k; 0: FP32 path.
+extern "C" int ref_decode(const char* path, const int* tokens, int n_prompt, int n_gen, int fpga,
+                          int* out_tokens, float* out_logit, float* out_hidden)
+{
+    if (!g_ddr) {
+        g_ddr = (uint8_t*)calloc(DDR_SIZE, 1);
+        if (!g_ddr) return -1;
+    }
+    if (g_tensors) {
+        free(g_tensors);
+        g_tensors = nullptr;
+    }
+    if (load_tmac(path) != 0) return -2;
+    set_switches(fpga != 0, fpga != 0, fpga != 0, fpga != 0, fpga != 0);
+    std::vector<float> hidden(HIDDEN_DIM), logits(VOCAB_SIZE);
+    std::vector<int> prompt(tokens, tokens + n_prompt);
+    if (process_prompt(hidden.data(), prompt, false) != 0) return -3;
+    if (out_hidden) memcpy(out_hidden, hidden.data(), HIDDEN_DIM * sizeof(float));
+    int produced = 0;
+    for (int gen = 0; gen < n_gen; gen++) {
+        int pos = n_prompt + gen;
+        if (pos >= MAX_SEQ_LEN) break;
+        if (g_fpga_q8) get_logits_q8(logits.data(), hidden.data());
+        else get_logits(logits.data(), hidden.data());
+        int best = 0;
+        for (int i = 1; i < VOCAB_SIZE; i++)
+            if (logits[i] > logits[best]) best = i;
+        out_tokens[gen] = best;
+        if (out_logit) out_logit[gen] = logits[best];
+        process_embedding(hidden.data(), best);
+        forward_all_layers(hidden.data(), pos);
+        if (out_hidden) memcpy(out_hidden + (size_t)(gen + 1) * HIDDEN_DIM, hidden.data(), HIDDEN_DIM * sizeof(float));
+        produced++;
+    }
+    set_switches(false, false, false, false, false);
+    return produced;
+}

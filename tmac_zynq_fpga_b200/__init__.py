@@ -318,3 +318,58 @@ def top1_decode(key):
     v, i = ctypes.c_float(), _I64()
     check(lib().tmac_top1_decode(ctypes.c_uint64(int(key) & 0xFFFFFFFFFFFFFFFF), ctypes.byref(v), ctypes.byref(i)))
     return v.value, i.value
+
+
+# ---------------------------------------------------------------------------
+# Whole-model greedy decode (tmac_model_*).
+
+SW_FPGA, SW_Q8, SW_Q5_0, SW_Q4_K, SW_Q6_K, SW_ALL = 1, 2, 4, 8, 16, 31
+
+
+def switches_from_argv(argv):
+    """The reference's --fpga-* flags as a TMAC_SW_* bit mask."""
+    sw = Switches().parse(argv)
+    bits = SW_FPGA if sw.use_fpga else 0
+    bits |= (SW_Q8 if sw.fpga_q8 else 0) | (SW_Q5_0 if sw.fpga_q5_0 else 0)
+    bits |= (SW_Q4_K if sw.fpga_q4k else 0) | (SW_Q6_K if sw.fpga_q6_k else 0)
+    return bits
+
+
+class Model:
+    """A device-resident Qwen2-0.5B-shaped model loaded from a `.tmac` file."""
+
+    def __init__(self, path, switches=SW_ALL, max_seq=512, device=0):
+        L = lib()
+        for n, args in (("tmac_model_create", [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.POINTER(_P)]),
+                        ("tmac_model_load_tmac", [_P, ctypes.c_char_p]), ("tmac_model_finalize", [_P]),
+                        ("tmac_model_reset", [_P, _P]), ("tmac_model_forward", [_P, ctypes.c_int, ctypes.c_int, _P]),
+                        ("tmac_model_logits", [_P, _P]), ("tmac_model_buffers", [_P, _P, _P, _P]),
+                        ("tmac_model_generate", [_P, _P, ctypes.c_int, ctypes.c_int, _P, _P, _P]),
+                        ("tmac_model_free", [_P])):
+            getattr(L, n).restype = ctypes.c_int
+            getattr(L, n).argtypes = args
+        h = _P()
+        check(L.tmac_model_create(device, switches, max_seq, ctypes.byref(h)))
+        self.handle = h.value
+        check(L.tmac_model_load_tmac(self.handle, path.encode()))
+        check(L.tmac_model_finalize(self.handle))
+
+    def generate(self, prompt, n_gen, want_hidden=False, stream=None):
+        prompt = np.ascontiguousarray(prompt, dtype=np.int32)
+        toks = np.zeros(n_gen, np.int32)
+        hid = np.zeros((n_gen + 1, 896), np.float32) if want_hidden else None
+        s = None if stream is None else (stream if isinstance(stream, int) else stream.cuda_stream)
+        check(lib().tmac_model_generate(self.handle, prompt.ctypes.data, len(prompt), n_gen, toks.ctypes.data,
+                                        None if hid is None else hid.ctypes.data, s))
+        return toks, hid
+
+    def free(self):
+        if getattr(self, "handle", None):
+            lib().tmac_model_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
