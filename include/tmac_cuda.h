@@ -151,6 +151,17 @@ int tmac_gemv_top1(tmac_weight_t w, const float* x, float* y, uint64_t* key, int
                    void* stream);
 int tmac_top1_decode(uint64_t key, float* value, int64_t* index);
 
+/*
+ * Activation quantisation done once (tmac_gguf.cpp:889-896): x_scale[b] =
+ * max|x[b]|/32767 (1 if below 1e-10), xq[b][j] = (int16)roundf(x[b][j]/x_scale[b]).
+ * tmac_gemv_xq then runs a NATIVE-mode GEMV on it; the result equals tmac_gemv
+ * on x bit for bit (every reference driver quantises its x the same way), so
+ * GEMVs sharing one activation vector (q/k/v, gate/up) quantise it once.
+ * cols must be a multiple of 8; device pointers; asynchronous.
+ */
+int tmac_quantize_x(const float* x, int64_t cols, int batch, int16_t* xq, float* xs, void* stream);
+int tmac_gemv_xq(tmac_weight_t w, const int16_t* xq, const float* xs, float* y, int batch, void* stream);
+
 /* Allocate the per-device workspace for GEMVs up to batch x cols now, so that
  * later calls allocate nothing (required before CUDA-graph capture). */
 int tmac_reserve(int device, int64_t max_batch, int64_t max_cols);

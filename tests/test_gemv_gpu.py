@@ -125,3 +125,29 @@ def test_drop_in_matmul_switch():
         tm.matmul(A, x, y, 64, 896, sw)
         o = oracle.gemv(tm.Q5_0, A.data, 64, 896, x, path=path)
         np.testing.assert_array_equal(y.view(np.int32), o.y.view(np.int32))
+
+
+@pytest.mark.parametrize("qtype,rows,cols,batch", [(tm.Q5_0, 4864, 896, 1), (tm.Q5_0, 128, 896, 3),
+                                                   (tm.Q8_0, 151936, 896, 1), (tm.Q8_0, 128, 896, 2),
+                                                   (tm.Q4_K, 896, 4864, 1), (tm.Q6_K, 896, 4864, 16)])
+def test_quantize_once_matches_gemv(qtype, rows, cols, batch):
+    """tmac_quantize_x + tmac_gemv_xq == tmac_gemv bit for bit (the reference
+    quantises x the same way in every driver, so sharing x_q changes nothing)."""
+    raw = synth.make_weights(qtype, rows, cols, seed=17)
+    x = synth.make_activations(cols, batch=batch, seed=17)
+    w = tm.Weight(qtype, rows, cols, raw)
+    xt = torch.from_numpy(x).cuda()
+    xq = torch.empty((batch, cols), dtype=torch.int16, device="cuda")
+    xs = torch.empty(batch, dtype=torch.float32, device="cuda")
+    y1 = torch.empty((batch, rows), dtype=torch.float32, device="cuda")
+    y2 = torch.empty_like(y1)
+    tm.check(tm.lib().tmac_quantize_x(xt.data_ptr(), cols, batch, xq.data_ptr(), xs.data_ptr(), None))
+    tm.check(tm.lib().tmac_gemv_xq(w.handle, xq.data_ptr(), xs.data_ptr(), y2.data_ptr(), batch, None))
+    w.gemv(xt, y1, batch=batch)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(y1.cpu().numpy().view(np.int32), y2.cpu().numpy().view(np.int32))
+    for b in range(batch):
+        xs_o, xq_o = oracle.quantize_x(x[b])
+        assert np.float32(xs[b].item()) == xs_o
+        np.testing.assert_array_equal(xq[b].cpu().numpy(), xq_o)
+    w.free()

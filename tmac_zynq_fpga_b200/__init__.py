@@ -87,6 +87,8 @@ def lib():
             "tmac_gemv_top1": (ctypes.c_int, [_P, _P, _P, _P, _I64, ctypes.c_int, _P]),
             "tmac_top1_decode": (ctypes.c_int, [ctypes.c_uint64, ctypes.POINTER(ctypes.c_float),
                                                 ctypes.POINTER(_I64)]),
+            "tmac_quantize_x": (ctypes.c_int, [_P, _I64, ctypes.c_int, _P, _P, _P]),
+            "tmac_gemv_xq": (ctypes.c_int, [_P, _P, _P, _P, ctypes.c_int, _P]),
             "tmac_chain_run": (ctypes.c_int, [_P, ctypes.c_size_t, ctypes.c_uint32, _P, ctypes.c_uint32,
                                               ctypes.c_int, ctypes.POINTER(ChainStats), _P]),
         }

@@ -192,11 +192,13 @@ namespace tmac {
 // Per-path launchers (one per .cu file).  All return TMAC_OK or an error.
 int register_q8_0(tmac_weight_s* w, const uint8_t* d_raw, const float* d_row_max_abs, cudaStream_t s);
 int launch_q8_0(const tmac_weight_s* w, const float* x, float* y, int64_t* row_acc, int64_t* unit_acc,
-                int batch, cudaStream_t s, unsigned long long* top1 = nullptr, int64_t index_base = 0);
+                int batch, cudaStream_t s, unsigned long long* top1 = nullptr, int64_t index_base = 0,
+                const int16_t* xq = nullptr, const float* xs = nullptr);
+int launch_quantize(const float* x, int64_t cols, int batch, int16_t* xq, float* xs, cudaStream_t s);
 int launch_top1(const float* y, int64_t n, int64_t index_base, unsigned long long* key, cudaStream_t s);
 int register_blockq(tmac_weight_s* w, const uint8_t* d_raw, cudaStream_t s);
-int launch_blockq(const tmac_weight_s* w, const float* x, float* y, int64_t* row_acc, int64_t* unit_acc,
-                  int batch, cudaStream_t s);
+int launch_blockq(const tmac_weight_s* w, const float* x, const int16_t* xq, const float* xs, float* y,
+                  int64_t* row_acc, int64_t* unit_acc, int batch, cudaStream_t s);
 int register_int16(tmac_weight_s* w, const uint8_t* d_raw, cudaStream_t s);
 int launch_int16(const tmac_weight_s* w, const float* x, float* y, int64_t* row_acc, int64_t* unit_acc,
                  int batch, cudaStream_t s);

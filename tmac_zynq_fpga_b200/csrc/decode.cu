@@ -56,19 +56,38 @@ __global__ void embed_q8_kernel(const uint8_t* __restrict__ emb, int token, cons
     }
 }
 
-// rms_norm (:447-454): one CTA; the sum of squares is sequential, as in the reference.
-__global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w, float* __restrict__ o,
-                               int n)
+// rms_norm (:447-454): one CTA; the sum of squares is sequential, as in the
+// reference (x staged in shared memory first).  With xq != nullptr the kernel
+// also quantises its output for the matmuls that read it (:889-896).
+__global__ void __launch_bounds__(256) rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                                      float* __restrict__ o, int16_t* __restrict__ xq,
+                                                      float* __restrict__ xs, int n)
 {
+    __shared__ float xsh[kInter];
+    __shared__ float red[8];
     __shared__ float scale;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) xsh[i] = x[i];
+    __syncthreads();
     if (threadIdx.x == 0) {
         float sum = 0.0f;
-        for (int i = 0; i < n; i++) sum = __fadd_rn(sum, __fmul_rn(x[i], x[i]));
+#pragma unroll 8
+        for (int i = 0; i < n; i++) sum = __fadd_rn(sum, __fmul_rn(xsh[i], xsh[i]));
         const float mean = __fdiv_rn(sum, (float)n);
         scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, 1e-6f)));
     }
     __syncthreads();
-    for (int i = threadIdx.x; i < n; i += blockDim.x) o[i] = __fmul_rn(__fmul_rn(x[i], w[i]), scale);
+    float mx = 0.0f;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const float v = __fmul_rn(__fmul_rn(xsh[i], w[i]), scale);
+        o[i] = v;
+        xsh[i] = v;
+        mx = fmaxf(mx, fabsf(v));
+    }
+    if (!xq) return;
+    mx = block_max(mx, red, blockDim.x);
+    const float s = x_scale_from_max(mx);
+    if (threadIdx.x == 0) *xs = s;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) xq[i] = quantize_one(xsh[i], s);
 }
 
 // q/k/v bias add (:1591-1614), RoPE on q and k (:1528-1554), KV-cache append (:1622-1623).
@@ -141,12 +160,24 @@ __global__ void add_kernel(float* __restrict__ h, const float* __restrict__ a, i
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) h[i] = __fadd_rn(h[i], a[i]);
 }
 
-__global__ void silu_mul_kernel(float* __restrict__ g, const float* __restrict__ u, int n)
+// silu(gate) * up (:459-461, :1697-1700), then the quantisation ffn_down's
+// matmul starts with: one CTA.
+__global__ void __launch_bounds__(1024) silu_mul_kernel(float* __restrict__ g, const float* __restrict__ u, int n,
+                                                        int16_t* __restrict__ xq, float* __restrict__ xs)
 {
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    __shared__ float red[32];
+    float mx = 0.0f;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
         const float x = g[i];
-        g[i] = __fmul_rn(__fdiv_rn(x, __fadd_rn(1.0f, expf_ref(-x))), u[i]);
+        const float v = __fmul_rn(__fdiv_rn(x, __fadd_rn(1.0f, expf_ref(-x))), u[i]);
+        g[i] = v;
+        mx = fmaxf(mx, fabsf(v));
     }
+    if (!xq) return;
+    mx = block_max(mx, red, blockDim.x);
+    const float s = x_scale_from_max(mx);
+    if (threadIdx.x == 0) *xs = s;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) xq[i] = quantize_one(g[i], s);
 }
 
 // ----------------------------------------------------------------- the model
@@ -172,6 +203,8 @@ struct tmac_model_s {
     float *kcache = nullptr, *vcache = nullptr, *rope_c = nullptr, *rope_s = nullptr;
     unsigned long long* key = nullptr;
     int* token_log = nullptr;
+    int16_t* xq = nullptr;  // quantised activations shared by several matmuls
+    float* xs = nullptr;
     std::vector<void*> allocs;
 };
 
@@ -203,10 +236,13 @@ std::string lname(int l, const char* suffix)
     return b;
 }
 
-int gemv(tmac_model_s* m, const std::string& name, const float* x, float* y, cudaStream_t s)
+// y = W.x; when the activation was already quantised (xq) and W runs a
+// NATIVE kernel, the kernel reads x_q instead of quantising x again.
+int gemv(tmac_model_s* m, const std::string& name, const float* x, float* y, cudaStream_t s, bool have_xq = false)
 {
     auto it = m->mats.find(name);
     if (it == m->mats.end()) return fail(TMAC_ERR_INVALID, "missing matrix " + name);
+    if (have_xq && it->second->mode == TMAC_MODE_NATIVE) return tmac_gemv_xq(it->second, m->xq, m->xs, y, 1, s);
     return tmac_gemv(it->second, x, y, 1, s);
 }
 
@@ -224,21 +260,21 @@ int layer(tmac_model_s* m, int l, int pos, cudaStream_t s)
     if (!an || !fn) return fail(TMAC_ERR_INVALID, "missing norm weights");
     float* kc = m->kcache + (int64_t)l * m->max_seq * kKvDim;
     float* vc = m->vcache + (int64_t)l * m->max_seq * kKvDim;
-    rmsnorm_kernel<<<1, 256, 0, s>>>(m->hidden, an, m->xn, kHidden);
-    if ((rc = gemv(m, lname(l, "attn_q.weight"), m->xn, m->q, s))) return rc;
-    if ((rc = gemv(m, lname(l, "attn_k.weight"), m->xn, m->k, s))) return rc;
-    if ((rc = gemv(m, lname(l, "attn_v.weight"), m->xn, m->v, s))) return rc;
+    rmsnorm_kernel<<<1, 256, 0, s>>>(m->hidden, an, m->xn, m->xq, m->xs, kHidden);
+    if ((rc = gemv(m, lname(l, "attn_q.weight"), m->xn, m->q, s, true))) return rc;
+    if ((rc = gemv(m, lname(l, "attn_k.weight"), m->xn, m->k, s, true))) return rc;
+    if ((rc = gemv(m, lname(l, "attn_v.weight"), m->xn, m->v, s, true))) return rc;
     qkv_rope_kernel<<<1, 512, 0, s>>>(m->q, m->k, m->v, vec_or_null(m, lname(l, "attn_q.bias")),
                                       vec_or_null(m, lname(l, "attn_k.bias")), vec_or_null(m, lname(l, "attn_v.bias")),
                                       m->rope_c, m->rope_s, pos, kc, vc);
     attention_kernel<<<kHeads, 256, (pos + 1) * sizeof(float), s>>>(m->q, kc, vc, pos, m->ctx);
     if ((rc = gemv(m, lname(l, "attn_output.weight"), m->ctx, m->attn, s))) return rc;
     add_kernel<<<4, 256, 0, s>>>(m->hidden, m->attn, kHidden);
-    rmsnorm_kernel<<<1, 256, 0, s>>>(m->hidden, fn, m->xn, kHidden);
-    if ((rc = gemv(m, lname(l, "ffn_gate.weight"), m->xn, m->gate, s))) return rc;
-    if ((rc = gemv(m, lname(l, "ffn_up.weight"), m->xn, m->up, s))) return rc;
-    silu_mul_kernel<<<19, 256, 0, s>>>(m->gate, m->up, kInter);
-    if ((rc = gemv(m, lname(l, "ffn_down.weight"), m->gate, m->ffn, s))) return rc;
+    rmsnorm_kernel<<<1, 256, 0, s>>>(m->hidden, fn, m->xn, m->xq, m->xs, kHidden);
+    if ((rc = gemv(m, lname(l, "ffn_gate.weight"), m->xn, m->gate, s, true))) return rc;
+    if ((rc = gemv(m, lname(l, "ffn_up.weight"), m->xn, m->up, s, true))) return rc;
+    silu_mul_kernel<<<1, 1024, 0, s>>>(m->gate, m->up, kInter, m->xq, m->xs);
+    if ((rc = gemv(m, lname(l, "ffn_down.weight"), m->gate, m->ffn, s, true))) return rc;
     add_kernel<<<4, 256, 0, s>>>(m->hidden, m->ffn, kHidden);
     TMAC_CUDA_TRY(cudaGetLastError());
     return TMAC_OK;
@@ -359,7 +395,8 @@ int tmac_model_finalize(tmac_model_t m)
         (rc = dev_alloc(m, &m->up, kInter)) || (rc = dev_alloc(m, &m->ffn, kHidden)) ||
         (rc = dev_alloc(m, &m->logits, kVocab)) || (rc = dev_alloc(m, &m->kcache, kv)) ||
         (rc = dev_alloc(m, &m->vcache, kv)) || (rc = dev_alloc(m, &m->key, 1)) ||
-        (rc = dev_alloc(m, &m->token_log, 1)))
+        (rc = dev_alloc(m, &m->token_log, 1)) || (rc = dev_alloc(m, &m->xq, kInter)) ||
+        (rc = dev_alloc(m, &m->xs, 1)))
         return rc;
     // RoPE tables with the reference's own float expression (apply_rope, :1528-1554)
     std::vector<float> c((size_t)m->max_seq * 32), sn((size_t)m->max_seq * 32);
@@ -414,7 +451,7 @@ int tmac_model_logits(tmac_model_t m, void* stream)
     const float* on = vec_or_null(m, "output_norm.weight");
     const float* x = m->hidden;
     if (on) {
-        rmsnorm_kernel<<<1, 256, 0, s>>>(m->hidden, on, m->xn, kHidden);
+        rmsnorm_kernel<<<1, 256, 0, s>>>(m->hidden, on, m->xn, nullptr, nullptr, kHidden);
         x = m->xn;
     }
     return tmac_gemv_top1(m->mats["token_embd.weight"], x, m->logits, (uint64_t*)m->key, 0, 1, stream);

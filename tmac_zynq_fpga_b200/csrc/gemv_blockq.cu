@@ -11,9 +11,9 @@
 //   v = clamp_round_i16(w_f32 * row_inv)      with w_f32 in the reference's order:
 //       Q5_0: d*q     Q4_K: (d*sc)*q4 - dmin*m     Q6_K: (d*sc)*q6
 // the int64 row sum is  acc = sum v * x_q  and  y = (float)((double)acc * x_scale / (double)row_inv).
-// The integer sum is order-free, so the work is split freely: one thread per
-// 32-value chunk (a Q5_0 block, a Q4_K sub-block, a Q6_K 32-value run), rows of
-// a CTA accumulated in shared memory with 64-bit atomics.
+// The integer sum is order-free, so the work is split freely: one warp per row,
+// each lane decoding one 32-value chunk (a Q5_0 block, a Q4_K sub-block, a Q6_K
+// 32-value run) per iteration, row sums by warp shuffle.
 #include "common.cuh"
 #include "dequant.cuh"
 
@@ -115,117 +115,153 @@ struct BlockqArgs {
     const uint8_t* raw;
     const float* row_inv;
     int64_t rows, cols;
-    const float* x;  // [nb][cols]
-    float* y;        // [nb][rows]
+    const float* x;        // [nb][cols] fp32 activations, or
+    const int16_t* xq_in;  // [nb][cols] already-quantised activations with
+    const float* xs_in;    // [nb] their x_scale (tmac_quantize_x)
+    float* y;              // [nb][rows]
     int64_t* row_acc;
     int64_t* unit_acc;
-    int nb;          // activation vectors handled by this launch
-    int rp;          // rows per CTA pass
+    int nb;                // activation vectors handled by this launch (<= NB)
 };
 
-template <int TYPE>
+TMAC_DEV long long warp_sum_ll(long long v)
+{
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// One warp per row (grid-stride), lane = one 32-value chunk per iteration; the
+// decoded chunk is reused for every activation vector of the launch.
+template <int TYPE, int NB>
 __global__ void __launch_bounds__(kThreads) blockq_gemv_kernel(BlockqArgs a)
 {
     extern __shared__ __align__(16) uint8_t smem[];
     const int64_t cols = a.cols, cpr = cols / 32;
     const int nb = a.nb;
     int16_t* xq = reinterpret_cast<int16_t*>(smem);                                    // [nb][cols]
-    float* xs = reinterpret_cast<float*>(smem + ((size_t)nb * cols * 2 + 15) / 16 * 16);  // [nb]
+    float* xs = reinterpret_cast<float*>(smem + ((size_t)nb * cols * 2 + 15) / 16 * 16);  // [NB]
     float* red = xs + 16;                                                              // [8]
-    unsigned long long* racc = reinterpret_cast<unsigned long long*>(red + 8);         // [rp][nb]
 
-    // activation quantisation, one vector at a time (tmac_gguf.cpp:889-896)
-    for (int b = 0; b < nb; b++) {
-        const float* xb = a.x + (int64_t)b * cols;
-        float mx = 0.0f;
-        for (int64_t j = threadIdx.x; j < cols; j += kThreads) mx = fmaxf(mx, fabsf(xb[j]));
-        mx = block_max(mx, red, kThreads);
-        const float s = x_scale_from_max(mx);
-        if (threadIdx.x == 0) xs[b] = s;
-        for (int64_t j = threadIdx.x; j < cols; j += kThreads) xq[b * cols + j] = quantize_one(xb[j], s);
+    if (a.xq_in) {
+        const uint4* src = reinterpret_cast<const uint4*>(a.xq_in);
+        uint4* dst = reinterpret_cast<uint4*>(xq);
+        for (int64_t j = threadIdx.x; j < (int64_t)nb * cols / 8; j += kThreads) dst[j] = src[j];
+        if (threadIdx.x < nb) xs[threadIdx.x] = a.xs_in[threadIdx.x];
+    } else {
+        // activation quantisation, one vector at a time (tmac_gguf.cpp:889-896)
+        for (int b = 0; b < nb; b++) {
+            const float* xb = a.x + (int64_t)b * cols;
+            float mx = 0.0f;
+            for (int64_t j = threadIdx.x; j < cols; j += kThreads) mx = fmaxf(mx, fabsf(xb[j]));
+            mx = block_max(mx, red, kThreads);
+            const float s = x_scale_from_max(mx);
+            if (threadIdx.x == 0) xs[b] = s;
+            for (int64_t j = threadIdx.x; j < cols; j += kThreads) xq[b * cols + j] = quantize_one(xb[j], s);
+        }
     }
     __syncthreads();
 
-    const int upr_div = (TYPE == TMAC_TYPE_Q5_0) ? 1 : 8;  // chunks per reported unit
-    const int64_t upr = cpr / upr_div;
-    for (int64_t r0 = (int64_t)blockIdx.x * a.rp; r0 < a.rows; r0 += (int64_t)gridDim.x * a.rp) {
-        const int nr = (int)std::min<int64_t>(a.rp, a.rows - r0);
-        for (int i = threadIdx.x; i < nr * nb; i += kThreads) racc[i] = 0ull;
-        __syncthreads();
-        for (int64_t c = threadIdx.x; c < (int64_t)nr * cpr; c += kThreads) {
-            const int rr = (int)(c / cpr);
-            const int64_t ch = c % cpr, r = r0 + rr;
+    const int lane = threadIdx.x & 31, nw = kThreads / 32;
+    const int64_t upr = (TYPE == TMAC_TYPE_Q5_0) ? cpr : cpr / 8;
+    for (int64_t r = (int64_t)blockIdx.x * nw + (threadIdx.x >> 5); r < a.rows; r += (int64_t)gridDim.x * nw) {
+        const float ri = __ldg(a.row_inv + r);
+        long long acc[NB];
+#pragma unroll
+        for (int b = 0; b < NB; b++) acc[b] = 0;
+        for (int64_t base = 0; base < cpr; base += 32) {
+            const int64_t ch = base + lane;
+            const bool live = ch < cpr;
             int v[32];
-            decode_chunk<TYPE>(a.raw, r, cpr, ch, __ldg(a.row_inv + r), v);
-            for (int b = 0; b < nb; b++) {
-                const uint4* xv = reinterpret_cast<const uint4*>(xq + b * cols + ch * 32);
-                long long acc = 0;
+            if (live) decode_chunk<TYPE>(a.raw, r, cpr, ch, ri, v);
 #pragma unroll
-                for (int q = 0; q < 4; q++) {
-                    const uint4 u = xv[q];
-                    const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+            for (int b = 0; b < NB; b++) {
+                if (b >= nb) break;
+                long long part = 0;
+                if (live) {
+                    const uint4* xv = reinterpret_cast<const uint4*>(xq + b * cols + ch * 32);
 #pragma unroll
-                    for (int k = 0; k < 4; k++) {
-                        const int x0 = (int)(int16_t)(w4[k] & 0xFFFF), x1 = (int)(int16_t)(w4[k] >> 16);
-                        acc += (long long)(v[q * 8 + 2 * k] * x0 + v[q * 8 + 2 * k + 1] * x1);
+                    for (int q = 0; q < 4; q++) {
+                        const uint4 u = xv[q];
+                        const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+                        for (int k = 0; k < 4; k++) {
+                            const int x0 = (int)(int16_t)(w4[k] & 0xFFFF), x1 = (int)(int16_t)(w4[k] >> 16);
+                            part += (long long)(v[q * 8 + 2 * k] * x0 + v[q * 8 + 2 * k + 1] * x1);
+                        }
                     }
                 }
-                atomicAdd(&racc[rr * nb + b], (unsigned long long)acc);
+                acc[b] += part;
                 if (a.unit_acc) {
-                    long long* u = (long long*)a.unit_acc + ((int64_t)b * a.rows + r) * upr + ch / upr_div;
-                    if (upr_div == 1) *u = acc;
-                    else atomicAdd(reinterpret_cast<unsigned long long*>(u), (unsigned long long)acc);
+                    long long* u = (long long*)a.unit_acc + ((int64_t)b * a.rows + r) * upr;
+                    if (TYPE == TMAC_TYPE_Q5_0) {
+                        if (live) u[ch] = part;
+                    } else {  // a 256-value block = 8 consecutive chunks = 8 consecutive lanes
+                        long long sb = part;
+                        for (int o = 1; o < 8; o <<= 1) sb += __shfl_xor_sync(0xffffffffu, sb, o);
+                        if (live && (lane & 7) == 0) u[ch / 8] = sb;
+                    }
                 }
             }
         }
-        __syncthreads();
-        for (int i = threadIdx.x; i < nr * nb; i += kThreads) {
-            const int rr = i / nb, b = i % nb;
-            const int64_t r = r0 + rr;
-            const long long acc = (long long)racc[i];
-            const double v = __ddiv_rn(__dmul_rn((double)acc, (double)xs[b]), (double)__ldg(a.row_inv + r));
-            a.y[(int64_t)b * a.rows + r] = (float)v;
-            if (a.row_acc) a.row_acc[(int64_t)b * a.rows + r] = acc;
+#pragma unroll
+        for (int b = 0; b < NB; b++) {
+            if (b >= nb) break;
+            const long long tot = warp_sum_ll(acc[b]);
+            if (lane == 0) {
+                const double v = __ddiv_rn(__dmul_rn((double)tot, (double)xs[b]), (double)ri);
+                a.y[(int64_t)b * a.rows + r] = (float)v;
+                if (a.row_acc) a.row_acc[(int64_t)b * a.rows + r] = tot;
+            }
         }
-        __syncthreads();
     }
 }
 
-template <int TYPE>
-int launch_type(const tmac_weight_s* w, const float* x, float* y, int64_t* row_acc, int64_t* unit_acc, int batch,
-                cudaStream_t s)
+template <int TYPE, int NB>
+int launch_nb(const tmac_weight_s* w, const BlockqArgs& a, cudaStream_t s)
 {
-    const int64_t cols = w->cols, cpr = cols / 32;
     const int64_t max_smem = 200 * 1024;
-    int bmax = (int)std::max<int64_t>(1, std::min<int64_t>(16, (max_smem - 4096) / (cols * 2)));
-    const int rp = (int)std::max<int64_t>(1, 512 / cpr);
     static bool attr[64] = {};
     if (!attr[w->device & 63]) {
-        TMAC_CUDA_TRY(cudaFuncSetAttribute(blockq_gemv_kernel<TYPE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        TMAC_CUDA_TRY(cudaFuncSetAttribute(blockq_gemv_kernel<TYPE, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            (int)max_smem));
         attr[w->device & 63] = true;
     }
+    const size_t smem = ((size_t)a.nb * a.cols * 2 + 15) / 16 * 16 + 24 * 4;
+    const int64_t warps = kThreads / 32;
+    const int grid = (int)std::min<int64_t>((a.rows + warps - 1) / warps, (int64_t)num_sms(w->device) * 8);
+    blockq_gemv_kernel<TYPE, NB><<<grid, kThreads, smem, s>>>(a);
+    TMAC_CUDA_TRY(cudaGetLastError());
+    return TMAC_OK;
+}
+
+template <int TYPE>
+int launch_type(const tmac_weight_s* w, const float* x, const int16_t* xq, const float* xs, float* y,
+                int64_t* row_acc, int64_t* unit_acc, int batch, cudaStream_t s)
+{
+    const int64_t cols = w->cols, cpr = cols / 32;
+    const int64_t max_smem = 200 * 1024;
+    const int bmax = (int)std::max<int64_t>(1, std::min<int64_t>(16, (max_smem - 4096) / (cols * 2)));
     const int64_t upr = (TYPE == TMAC_TYPE_Q5_0) ? cpr : cpr / 8;
-    if (unit_acc && TYPE != TMAC_TYPE_Q5_0)
-        TMAC_CUDA_TRY(cudaMemsetAsync(unit_acc, 0, (size_t)batch * w->rows * upr * sizeof(int64_t), s));
-    const int64_t passes = (w->rows + rp - 1) / rp;
-    const int grid = (int)std::min<int64_t>(passes, (int64_t)num_sms(w->device) * 4);
     for (int b0 = 0; b0 < batch; b0 += bmax) {
-        const int nb = std::min(bmax, batch - b0);
         BlockqArgs a;
         a.raw = w->data;
         a.row_inv = w->row_norm;
         a.rows = w->rows;
         a.cols = cols;
-        a.x = x + (int64_t)b0 * cols;
+        a.nb = std::min(bmax, batch - b0);
+        a.x = x ? x + (int64_t)b0 * cols : nullptr;
+        a.xq_in = xq ? xq + (int64_t)b0 * cols : nullptr;
+        a.xs_in = xs ? xs + b0 : nullptr;
         a.y = y + (int64_t)b0 * w->rows;
         a.row_acc = row_acc ? row_acc + (int64_t)b0 * w->rows : nullptr;
         a.unit_acc = unit_acc ? unit_acc + (int64_t)b0 * w->rows * upr : nullptr;
-        a.nb = nb;
-        a.rp = rp;
-        const size_t smem = ((size_t)nb * cols * 2 + 15) / 16 * 16 + 24 * 4 + (size_t)rp * nb * 8;
-        blockq_gemv_kernel<TYPE><<<grid, kThreads, smem, s>>>(a);
-        TMAC_CUDA_TRY(cudaGetLastError());
+        int rc;
+        if (a.nb == 1) rc = launch_nb<TYPE, 1>(w, a, s);
+        else if (a.nb <= 2) rc = launch_nb<TYPE, 2>(w, a, s);
+        else if (a.nb <= 4) rc = launch_nb<TYPE, 4>(w, a, s);
+        else if (a.nb <= 8) rc = launch_nb<TYPE, 8>(w, a, s);
+        else rc = launch_nb<TYPE, 16>(w, a, s);
+        if (rc) return rc;
     }
     return TMAC_OK;
 }
@@ -247,13 +283,13 @@ int register_blockq(tmac_weight_s* w, const uint8_t* d_raw, cudaStream_t s)
     return TMAC_OK;
 }
 
-int launch_blockq(const tmac_weight_s* w, const float* x, float* y, int64_t* row_acc, int64_t* unit_acc, int batch,
-                  cudaStream_t s)
+int launch_blockq(const tmac_weight_s* w, const float* x, const int16_t* xq, const float* xs, float* y,
+                  int64_t* row_acc, int64_t* unit_acc, int batch, cudaStream_t s)
 {
     switch (w->type) {
-    case TMAC_TYPE_Q5_0: return launch_type<TMAC_TYPE_Q5_0>(w, x, y, row_acc, unit_acc, batch, s);
-    case TMAC_TYPE_Q4_K: return launch_type<TMAC_TYPE_Q4_K>(w, x, y, row_acc, unit_acc, batch, s);
-    case TMAC_TYPE_Q6_K: return launch_type<TMAC_TYPE_Q6_K>(w, x, y, row_acc, unit_acc, batch, s);
+    case TMAC_TYPE_Q5_0: return launch_type<TMAC_TYPE_Q5_0>(w, x, xq, xs, y, row_acc, unit_acc, batch, s);
+    case TMAC_TYPE_Q4_K: return launch_type<TMAC_TYPE_Q4_K>(w, x, xq, xs, y, row_acc, unit_acc, batch, s);
+    case TMAC_TYPE_Q6_K: return launch_type<TMAC_TYPE_Q6_K>(w, x, xq, xs, y, row_acc, unit_acc, batch, s);
     default: return fail(TMAC_ERR_TYPE, "launch_blockq: unsupported type");
     }
 }

@@ -159,7 +159,9 @@ struct Q8Args {
     Q8Layout L;
     int64_t rows;
     int cols;
-    const float* x;
+    const float* x;          // fp32 activations, or
+    const int16_t* xq_in;    // already-quantised activations and
+    const float* xs_in;      // their x_scale (tmac_quantize_x)
     float* y;
     int64_t* row_acc;
     int64_t* unit_acc;
@@ -315,32 +317,39 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemv_kernel(Q8Args a)
 
     // ---------------- consumers: activation quantisation (overlaps the copies)
     const int nct = kConsumerWarps * 32;
-    // x is read from global memory once; xq_s first holds nothing, the values
-    // stay in registers between the max reduction and the quantisation.
-    constexpr int kXRegs = 4;  // covers T*64 <= kXRegs * 448 (cols <= 1792)
-    float xv[kXRegs];
-    float mx = 0.0f;
-#pragma unroll
-    for (int k = 0; k < kXRegs; k++) {
-        const int j = threadIdx.x + k * nct;
-        xv[k] = (j < a.cols) ? a.x[j] : 0.0f;
-        mx = fmaxf(mx, fabsf(xv[k]));
+    float xs;
+    if (a.xq_in) {
+        for (int j = threadIdx.x; j < T * 64; j += nct) xq_s[j] = (j < a.cols) ? a.xq_in[j] : (int16_t)0;
+        xs = *a.xs_in;
+        if (threadIdx.x == 0) red[16] = xs;
+    } else {
+        // x is read from global memory once; xq_s first holds nothing, the values
+        // stay in registers between the max reduction and the quantisation.
+        constexpr int kXRegs = 4;  // covers T*64 <= kXRegs * 448 (cols <= 1792)
+        float xv[kXRegs];
+        float mx = 0.0f;
+    #pragma unroll
+        for (int k = 0; k < kXRegs; k++) {
+            const int j = threadIdx.x + k * nct;
+            xv[k] = (j < a.cols) ? a.x[j] : 0.0f;
+            mx = fmaxf(mx, fabsf(xv[k]));
+        }
+        for (int j = threadIdx.x + kXRegs * nct; j < a.cols; j += nct) mx = fmaxf(mx, fabsf(a.x[j]));
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        if (lane == 0) red[warp] = mx;
+        named_bar_sync(1, nct);
+        mx = 0.0f;
+        for (int i = 0; i < kConsumerWarps; i++) mx = fmaxf(mx, red[i]);
+        xs = x_scale_from_max(mx);
+        if (threadIdx.x == 0) red[16] = xs;
+    #pragma unroll
+        for (int k = 0; k < kXRegs; k++) {
+            const int j = threadIdx.x + k * nct;
+            if (j < T * 64) xq_s[j] = (j < a.cols) ? quantize_one(xv[k], xs) : 0;
+        }
+        for (int j = threadIdx.x + kXRegs * nct; j < T * 64; j += nct)
+            xq_s[j] = (j < a.cols) ? quantize_one(a.x[j], xs) : 0;
     }
-    for (int j = threadIdx.x + kXRegs * nct; j < a.cols; j += nct) mx = fmaxf(mx, fabsf(a.x[j]));
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    if (lane == 0) red[warp] = mx;
-    named_bar_sync(1, nct);
-    mx = 0.0f;
-    for (int i = 0; i < kConsumerWarps; i++) mx = fmaxf(mx, red[i]);
-    const float xs = x_scale_from_max(mx);
-    if (threadIdx.x == 0) red[16] = xs;
-#pragma unroll
-    for (int k = 0; k < kXRegs; k++) {
-        const int j = threadIdx.x + k * nct;
-        if (j < T * 64) xq_s[j] = (j < a.cols) ? quantize_one(xv[k], xs) : 0;
-    }
-    for (int j = threadIdx.x + kXRegs * nct; j < T * 64; j += nct)
-        xq_s[j] = (j < a.cols) ? quantize_one(a.x[j], xs) : 0;
     named_bar_sync(1, nct);
     for (int j = threadIdx.x; j < T * 16; j += nct) {
         uint32_t h = 0, l = 0;
@@ -435,7 +444,7 @@ int register_q8_0(tmac_weight_s* w, const uint8_t* d_raw, const float* d_row_max
 }
 
 int launch_q8_0(const tmac_weight_s* w, const float* x, float* y, int64_t* row_acc, int64_t* unit_acc, int batch,
-                cudaStream_t s, unsigned long long* top1, int64_t index_base)
+                cudaStream_t s, unsigned long long* top1, int64_t index_base, const int16_t* xq, const float* xs)
 {
     Q8Layout L = q8_layout(w->rows, w->cols);
     const size_t smem = q8_smem_bytes(L);
@@ -451,7 +460,9 @@ int launch_q8_0(const tmac_weight_s* w, const float* x, float* y, int64_t* row_a
         a.L = L;
         a.rows = w->rows;
         a.cols = (int)w->cols;
-        a.x = x + (int64_t)b * w->cols;
+        a.x = x ? x + (int64_t)b * w->cols : nullptr;
+        a.xq_in = xq ? xq + (int64_t)b * w->cols : nullptr;
+        a.xs_in = xs ? xs + b : nullptr;
         a.y = y + (int64_t)b * w->rows;
         a.row_acc = row_acc ? row_acc + (int64_t)b * w->rows : nullptr;
         a.unit_acc = unit_acc ? unit_acc + (int64_t)b * w->rows * L.T : nullptr;

@@ -335,7 +335,7 @@ int tmac_gemv_acc(tmac_weight_t w, const float* x, float* y, int64_t* row_acc, i
     cudaStream_t s = (cudaStream_t)stream;
     if (w->mode == TMAC_MODE_NATIVE && w->type == TMAC_TYPE_Q8_0)
         return launch_q8_0(w, x, y, row_acc, unit_acc, batch, s);
-    if (w->mode == TMAC_MODE_NATIVE) return launch_blockq(w, x, y, row_acc, unit_acc, batch, s);
+    if (w->mode == TMAC_MODE_NATIVE) return launch_blockq(w, x, nullptr, nullptr, y, row_acc, unit_acc, batch, s);
     if (w->mode == TMAC_MODE_INT16) return launch_int16(w, x, y, row_acc, unit_acc, batch, s);
     return launch_f32(w, x, y, batch, s);
 }
