@@ -263,7 +263,9 @@ int tmac_model_forward(tmac_model_t m, int token, int pos, void* stream);
 int tmac_model_logits(tmac_model_t m, void* stream);
 /* Device addresses of the hidden state [896], logits [151936] and the key. */
 int tmac_model_buffers(tmac_model_t m, float** hidden, float** logits, uint64_t** key);
-/* Prompt + n_gen greedy steps; out_tokens[n_gen] (host); out_hidden optional
+/* Prompt + n_gen greedy steps on the model's own stream, each step replayed
+ * from a CUDA graph captured on first use (`stream` is not used; the call
+ * returns when done).  out_tokens[n_gen] (host); out_hidden optional
  * host float[(n_gen + 1) * 896]: after the prompt and after each step. */
 int tmac_model_generate(tmac_model_t m, const int* prompt, int n_prompt, int n_gen, int* out_tokens,
                         float* out_hidden, void* stream);

@@ -40,15 +40,27 @@ TMAC_DEV float logf_ref(float x) { return (float)log((double)x); }
 // Embedding row of a Q8_0 token_embd (read_embedding / dequant_q8_0, :225-234,
 // :413-427).  The token comes from a host int (token >= 0) or a device top-1 key.
 __global__ void embed_q8_kernel(const uint8_t* __restrict__ emb, int token, const unsigned long long* key,
-                                int* token_log, float* __restrict__ hidden)
+                                int* token_log, float* __restrict__ hidden, const int* pos_dev, int* tokens,
+                                int n_prompt)
 {
+    // token: a host id; or (pos_dev) the prompt token tokens[pos] while
+    // pos < n_prompt, else the greedy token of the device top-1 key.
     int tok = token;
-    if (key) {
+    int p = 0;
+    if (pos_dev) {
+        p = *pos_dev;
+        if (p < n_prompt) tok = tokens[p];
+        else tok = -1;
+    }
+    if (tok < 0 && key) {
         const unsigned long long k = *key;
         tok = (int)(0x7FFFFFFFu - (uint32_t)(k & 0x7FFFFFFFu));
     }
     if (tok < 0 || tok >= kVocab) tok = 0;
-    if (token_log && threadIdx.x == 0 && blockIdx.x == 0) *token_log = tok;
+    if (threadIdx.x == 0 && blockIdx.x == 0) {
+        if (token_log) *token_log = tok;
+        if (pos_dev) tokens[p] = tok;
+    }
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < kHidden; i += gridDim.x * blockDim.x) {
         const int64_t idx = (int64_t)tok * kHidden + i;
         const uint8_t* b = emb + (idx / 32) * 34;
@@ -56,29 +68,61 @@ __global__ void embed_q8_kernel(const uint8_t* __restrict__ emb, int token, cons
     }
 }
 
+// End of one token: log the hidden state at its position, advance the position.
+__global__ void step_done_kernel(const float* __restrict__ hidden, float* __restrict__ hidden_log, int* pos_dev)
+{
+    const int p = *pos_dev;
+    for (int i = threadIdx.x; i < kHidden; i += blockDim.x) hidden_log[(int64_t)p * kHidden + i] = hidden[i];
+    __syncthreads();
+    if (threadIdx.x == 0) *pos_dev = p + 1;
+}
+
 // rms_norm (:447-454): one CTA; the sum of squares is sequential, as in the
 // reference (x staged in shared memory first).  With xq != nullptr the kernel
 // also quantises its output for the matmuls that read it (:889-896).
-__global__ void __launch_bounds__(256) rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
-                                                      float* __restrict__ o, int16_t* __restrict__ xq,
-                                                      float* __restrict__ xs, int n)
+// With delta != nullptr the residual add comes first (x += delta, written back:
+// :1669 / :1710).  w == nullptr copies x unnormalised (get_logits_q8 without an
+// output_norm tensor, :1831-1838).
+__global__ void __launch_bounds__(256) rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ delta,
+                                                      const float* __restrict__ w, float* __restrict__ o,
+                                                      int16_t* __restrict__ xq, float* __restrict__ xs, int n)
 {
-    __shared__ float xsh[kInter];
+    __shared__ __align__(16) float xsh[kInter];
     __shared__ float red[8];
     __shared__ float scale;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) xsh[i] = x[i];
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        float v = x[i];
+        if (delta) {
+            v = __fadd_rn(v, delta[i]);
+            x[i] = v;
+        }
+        xsh[i] = v;
+    }
     __syncthreads();
-    if (threadIdx.x == 0) {
+    if (threadIdx.x == 0 && !w) scale = 1.0f;
+    if (threadIdx.x == 0 && w) {
         float sum = 0.0f;
-#pragma unroll 8
-        for (int i = 0; i < n; i++) sum = __fadd_rn(sum, __fmul_rn(xsh[i], xsh[i]));
+        const float4* x4 = reinterpret_cast<const float4*>(xsh);
+        int i = 0;
+        for (; i + 8 <= n; i += 8) {  // loads ahead of the (sequential) adds
+            const float4 a = x4[i / 4], b = x4[i / 4 + 1];
+            sum = __fadd_rn(sum, __fmul_rn(a.x, a.x));
+            sum = __fadd_rn(sum, __fmul_rn(a.y, a.y));
+            sum = __fadd_rn(sum, __fmul_rn(a.z, a.z));
+            sum = __fadd_rn(sum, __fmul_rn(a.w, a.w));
+            sum = __fadd_rn(sum, __fmul_rn(b.x, b.x));
+            sum = __fadd_rn(sum, __fmul_rn(b.y, b.y));
+            sum = __fadd_rn(sum, __fmul_rn(b.z, b.z));
+            sum = __fadd_rn(sum, __fmul_rn(b.w, b.w));
+        }
+        for (; i < n; i++) sum = __fadd_rn(sum, __fmul_rn(xsh[i], xsh[i]));
         const float mean = __fdiv_rn(sum, (float)n);
         scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, 1e-6f)));
     }
     __syncthreads();
     float mx = 0.0f;
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        const float v = __fmul_rn(__fmul_rn(xsh[i], w[i]), scale);
+        const float v = w ? __fmul_rn(__fmul_rn(xsh[i], w[i]), scale) : xsh[i];
         o[i] = v;
         xsh[i] = v;
         mx = fmaxf(mx, fabsf(v));
@@ -90,52 +134,47 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const float* __restrict__ 
     for (int i = threadIdx.x; i < n; i += blockDim.x) xq[i] = quantize_one(xsh[i], s);
 }
 
-// q/k/v bias add (:1591-1614), RoPE on q and k (:1528-1554), KV-cache append (:1622-1623).
-__global__ void qkv_rope_kernel(float* __restrict__ q, float* __restrict__ k, const float* __restrict__ v,
-                                const float* __restrict__ bq, const float* __restrict__ bk,
-                                const float* __restrict__ bv, const float* __restrict__ cs,
-                                const float* __restrict__ sn, int pos, float* __restrict__ kc,
-                                float* __restrict__ vc)
-{
-    const float* c = cs + (int64_t)pos * (kHeadDim / 2);
-    const float* s = sn + (int64_t)pos * (kHeadDim / 2);
-    for (int p = threadIdx.x; p < (kHidden + kKvDim) / 2; p += blockDim.x) {
-        const bool isq = p < kHidden / 2;
-        float* vec = isq ? q : k;
-        const float* b = isq ? bq : bk;
-        const int idx = 2 * (isq ? p : p - kHidden / 2);
-        const int d = idx % kHeadDim;
-        const float x0 = __fadd_rn(vec[idx], b ? b[idx] : 0.0f), x1 = __fadd_rn(vec[idx + 1], b ? b[idx + 1] : 0.0f);
-        const float cv = c[d / 2], sv = s[d / 2];
-        const float y0 = __fsub_rn(__fmul_rn(x0, cv), __fmul_rn(x1, sv));
-        const float y1 = __fadd_rn(__fmul_rn(x0, sv), __fmul_rn(x1, cv));
-        vec[idx] = y0;
-        vec[idx + 1] = y1;
-        if (!isq) {
-            kc[(int64_t)pos * kKvDim + idx] = y0;
-            kc[(int64_t)pos * kKvDim + idx + 1] = y1;
-        }
-    }
-    for (int i = threadIdx.x; i < kKvDim; i += blockDim.x)
-        vc[(int64_t)pos * kKvDim + i] = __fadd_rn(v[i], bv ? bv[i] : 0.0f);
-}
-
-// Attention of one query head over positions 0..pos (:1625-1660): one CTA per head.
-__global__ void __launch_bounds__(256) attention_kernel(const float* __restrict__ q, const float* __restrict__ kc,
-                                                        const float* __restrict__ vc, int pos,
-                                                        float* __restrict__ ctx)
+// One CTA per query head: q/k/v bias add (:1591-1614), RoPE on the head's q
+// and its KV head's k (:1528-1554), KV-cache append by the first query head of
+// each KV group (:1622-1623), then attention over positions 0..pos
+// (:1625-1660).  The current position's k/v come from shared memory, so the
+// append needs no ordering against the other heads.
+__global__ void __launch_bounds__(256) rope_attention_kernel(
+    const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
+    const float* __restrict__ bq, const float* __restrict__ bk, const float* __restrict__ bv,
+    const float* __restrict__ cs, const float* __restrict__ sn, int pos, const int* pos_dev, float* __restrict__ kc,
+    float* __restrict__ vc, float* __restrict__ ctx)
 {
     extern __shared__ float sc[];  // [pos + 1] scores, then weights
-    __shared__ float qs[kHeadDim];
+    __shared__ float qs[kHeadDim], ks[kHeadDim], vs[kHeadDim];
     __shared__ float log_sum;
-    const int h = blockIdx.x, kv = h / (kHeads / kKvHeads);
-    for (int d = threadIdx.x; d < kHeadDim; d += blockDim.x) qs[d] = q[h * kHeadDim + d];
+    if (pos_dev) pos = *pos_dev;
+    const int h = blockIdx.x, kvh = h / (kHeads / kKvHeads);
+    const float* c = cs + (int64_t)pos * (kHeadDim / 2);
+    const float* sv = sn + (int64_t)pos * (kHeadDim / 2);
+    if (threadIdx.x < kHeadDim) {  // thread j: pair j/2 of q (j even) or of k (j odd)
+        const int j = threadIdx.x, pr = j >> 1, d = 2 * pr;
+        const bool isk = j & 1;
+        const float* vec = isk ? k + kvh * kHeadDim : q + h * kHeadDim;
+        const float* b = isk ? (bk ? bk + kvh * kHeadDim : nullptr) : (bq ? bq + h * kHeadDim : nullptr);
+        const float x0 = __fadd_rn(vec[d], b ? b[d] : 0.0f), x1 = __fadd_rn(vec[d + 1], b ? b[d + 1] : 0.0f);
+        const float y0 = __fsub_rn(__fmul_rn(x0, c[pr]), __fmul_rn(x1, sv[pr]));
+        const float y1 = __fadd_rn(__fmul_rn(x0, sv[pr]), __fmul_rn(x1, c[pr]));
+        float* dst = isk ? ks : qs;
+        dst[d] = y0;
+        dst[d + 1] = y1;
+        vs[j] = __fadd_rn(v[kvh * kHeadDim + j], bv ? bv[kvh * kHeadDim + j] : 0.0f);
+    }
     __syncthreads();
+    if (h % (kHeads / kKvHeads) == 0 && threadIdx.x < kHeadDim) {
+        kc[(int64_t)pos * kKvDim + kvh * kHeadDim + threadIdx.x] = ks[threadIdx.x];
+        vc[(int64_t)pos * kKvDim + kvh * kHeadDim + threadIdx.x] = vs[threadIdx.x];
+    }
     for (int p = threadIdx.x; p <= pos; p += blockDim.x) {
-        const float* kp = kc + (int64_t)p * kKvDim + kv * kHeadDim;
-        float s = 0.0f;
-        for (int d = 0; d < kHeadDim; d++) s = __fadd_rn(s, __fmul_rn(qs[d], kp[d]));
-        sc[p] = __fdiv_rn(s, 8.0f);  // / sqrtf(64)
+        const float* kp = (p == pos) ? ks : kc + (int64_t)p * kKvDim + kvh * kHeadDim;
+        float sum = 0.0f;
+        for (int d = 0; d < kHeadDim; d++) sum = __fadd_rn(sum, __fmul_rn(qs[d], kp[d]));
+        sc[p] = __fdiv_rn(sum, 8.0f);  // / sqrtf(64)
     }
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -150,14 +189,12 @@ __global__ void __launch_bounds__(256) attention_kernel(const float* __restrict_
     __syncthreads();
     for (int d = threadIdx.x; d < kHeadDim; d += blockDim.x) {
         float a = 0.0f;
-        for (int p = 0; p <= pos; p++) a = __fadd_rn(a, __fmul_rn(sc[p], vc[(int64_t)p * kKvDim + kv * kHeadDim + d]));
+        for (int p = 0; p <= pos; p++) {
+            const float vv = (p == pos) ? vs[d] : vc[(int64_t)p * kKvDim + kvh * kHeadDim + d];
+            a = __fadd_rn(a, __fmul_rn(sc[p], vv));
+        }
         ctx[h * kHeadDim + d] = a;
     }
-}
-
-__global__ void add_kernel(float* __restrict__ h, const float* __restrict__ a, int n)
-{
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) h[i] = __fadd_rn(h[i], a[i]);
 }
 
 // silu(gate) * up (:459-461, :1697-1700), then the quantisation ffn_down's
@@ -205,6 +242,13 @@ struct tmac_model_s {
     int* token_log = nullptr;
     int16_t* xq = nullptr;  // quantised activations shared by several matmuls
     float* xs = nullptr;
+    // graph-driven generation: position, token and hidden-state logs on the device
+    int* pos_dev = nullptr;
+    int* tokens = nullptr;        // [max_seq]
+    float* hidden_log = nullptr;  // [max_seq][896]
+    cudaStream_t stream = nullptr;
+    cudaGraphExec_t g_prompt = nullptr, g_gen = nullptr;
+    int graph_n_prompt = -1;
     std::vector<void*> allocs;
 };
 
@@ -252,31 +296,53 @@ const float* vec_or_null(tmac_model_s* m, const std::string& name)
     return it == m->vecs.end() ? nullptr : it->second;
 }
 
-int layer(tmac_model_s* m, int l, int pos, cudaStream_t s)
+const float* next_norm(tmac_model_s* m, int l)
+{
+    return l + 1 < kLayers ? vec_or_null(m, lname(l + 1, "attn_norm.weight")) : vec_or_null(m, "output_norm.weight");
+}
+
+// One layer.  On entry xn / xq / xs hold attn_norm(hidden) of this layer; on
+// exit hidden has both residuals and xn / xq / xs hold the next layer's
+// attn_norm(hidden) (or output_norm(hidden) after the last layer).
+int layer(tmac_model_s* m, int l, int pos, cudaStream_t s, const int* pos_dev = nullptr)
 {
     int rc;
-    const float* an = vec_or_null(m, lname(l, "attn_norm.weight"));
     const float* fn = vec_or_null(m, lname(l, "ffn_norm.weight"));
-    if (!an || !fn) return fail(TMAC_ERR_INVALID, "missing norm weights");
+    if (!fn) return fail(TMAC_ERR_INVALID, "missing ffn_norm weights");
     float* kc = m->kcache + (int64_t)l * m->max_seq * kKvDim;
     float* vc = m->vcache + (int64_t)l * m->max_seq * kKvDim;
-    rmsnorm_kernel<<<1, 256, 0, s>>>(m->hidden, an, m->xn, m->xq, m->xs, kHidden);
-    if ((rc = gemv(m, lname(l, "attn_q.weight"), m->xn, m->q, s, true))) return rc;
-    if ((rc = gemv(m, lname(l, "attn_k.weight"), m->xn, m->k, s, true))) return rc;
-    if ((rc = gemv(m, lname(l, "attn_v.weight"), m->xn, m->v, s, true))) return rc;
-    qkv_rope_kernel<<<1, 512, 0, s>>>(m->q, m->k, m->v, vec_or_null(m, lname(l, "attn_q.bias")),
-                                      vec_or_null(m, lname(l, "attn_k.bias")), vec_or_null(m, lname(l, "attn_v.bias")),
-                                      m->rope_c, m->rope_s, pos, kc, vc);
-    attention_kernel<<<kHeads, 256, (pos + 1) * sizeof(float), s>>>(m->q, kc, vc, pos, m->ctx);
+    // q, k (and v when it has the same type) as one GEMV over concatenated rows
+    if (m->mats.count(lname(l, "attn_qkv"))) {
+        if ((rc = gemv(m, lname(l, "attn_qkv"), m->xn, m->q, s, true))) return rc;
+    } else {
+        if ((rc = gemv(m, lname(l, "attn_qk"), m->xn, m->q, s, true))) return rc;
+        if ((rc = gemv(m, lname(l, "attn_v.weight"), m->xn, m->v, s, true))) return rc;
+    }
+    const int nscore = pos_dev ? m->max_seq : pos + 1;
+    rope_attention_kernel<<<kHeads, 256, nscore * sizeof(float), s>>>(
+        m->q, m->k, m->v, vec_or_null(m, lname(l, "attn_q.bias")), vec_or_null(m, lname(l, "attn_k.bias")),
+        vec_or_null(m, lname(l, "attn_v.bias")), m->rope_c, m->rope_s, pos, pos_dev, kc, vc, m->ctx);
     if ((rc = gemv(m, lname(l, "attn_output.weight"), m->ctx, m->attn, s))) return rc;
-    add_kernel<<<4, 256, 0, s>>>(m->hidden, m->attn, kHidden);
-    rmsnorm_kernel<<<1, 256, 0, s>>>(m->hidden, fn, m->xn, m->xq, m->xs, kHidden);
-    if ((rc = gemv(m, lname(l, "ffn_gate.weight"), m->xn, m->gate, s, true))) return rc;
-    if ((rc = gemv(m, lname(l, "ffn_up.weight"), m->xn, m->up, s, true))) return rc;
+    rmsnorm_kernel<<<1, 256, 0, s>>>(m->hidden, m->attn, fn, m->xn, m->xq, m->xs, kHidden);
+    if ((rc = gemv(m, lname(l, "ffn_gate_up"), m->xn, m->gate, s, true))) return rc;
     silu_mul_kernel<<<1, 1024, 0, s>>>(m->gate, m->up, kInter, m->xq, m->xs);
     if ((rc = gemv(m, lname(l, "ffn_down.weight"), m->gate, m->ffn, s, true))) return rc;
-    add_kernel<<<4, 256, 0, s>>>(m->hidden, m->ffn, kHidden);
+    rmsnorm_kernel<<<1, 256, 0, s>>>(m->hidden, m->ffn, next_norm(m, l), m->xn, m->xq, m->xs, kHidden);
     TMAC_CUDA_TRY(cudaGetLastError());
+    return TMAC_OK;
+}
+
+// Embedding, then attn_norm of layer 0, then all layers.
+int forward_all(tmac_model_s* m, int token, const unsigned long long* key, int pos, cudaStream_t s,
+                const int* pos_dev, int n_prompt)
+{
+    int rc;
+    embed_q8_kernel<<<4, 256, 0, s>>>(m->emb_raw, token, key, m->token_log, m->hidden, pos_dev, m->tokens, n_prompt);
+    const float* an = vec_or_null(m, lname(0, "attn_norm.weight"));
+    if (!an) return fail(TMAC_ERR_INVALID, "missing attn_norm weights");
+    rmsnorm_kernel<<<1, 256, 0, s>>>(m->hidden, nullptr, an, m->xn, m->xq, m->xs, kHidden);
+    for (int l = 0; l < kLayers; l++)
+        if ((rc = layer(m, l, pos, s, pos_dev))) return rc;
     return TMAC_OK;
 }
 
@@ -361,6 +427,32 @@ int tmac_model_finalize(tmac_model_t m)
     if (emb == m->host.end() || emb->second.type != TMAC_TYPE_Q8_0 || emb->second.rows != kVocab ||
         emb->second.cols != kHidden)
         return fail(TMAC_ERR_SHAPE, "token_embd.weight must be Q8_0 151936 x 896");
+    // Matrices that read the same activation are registered as one weight over
+    // their concatenated rows (q|k|v, gate|up): every output row is computed
+    // independently, so the results are those of the separate matmuls.
+    auto concat = [&](const std::vector<std::string>& parts, const std::string& name) {
+        HostTensor t;
+        t.type = m->host[parts[0]].type;
+        t.cols = m->host[parts[0]].cols;
+        for (const auto& p : parts) {
+            HostTensor& h = m->host[p];
+            t.rows += h.rows;
+            t.data.insert(t.data.end(), h.data.begin(), h.data.end());
+            m->host.erase(p);
+        }
+        m->host[name] = std::move(t);
+    };
+    for (int l = 0; l < kLayers; l++) {
+        const std::string q = lname(l, "attn_q.weight"), k = lname(l, "attn_k.weight"), v = lname(l, "attn_v.weight");
+        const std::string g = lname(l, "ffn_gate.weight"), u = lname(l, "ffn_up.weight");
+        for (const auto& n : {q, k, v, g, u})
+            if (!m->host.count(n)) return fail(TMAC_ERR_INVALID, "missing tensor " + n);
+        if (m->host[q].type != m->host[k].type || m->host[g].type != m->host[u].type)
+            return fail(TMAC_ERR_TYPE, "attn_q/attn_k and ffn_gate/ffn_up must share a type");
+        if (m->host[v].type == m->host[q].type) concat({q, k, v}, lname(l, "attn_qkv"));
+        else concat({q, k}, lname(l, "attn_qk"));
+        concat({g, u}, lname(l, "ffn_gate_up"));
+    }
     for (auto& kv : m->host) {
         const std::string& name = kv.first;
         HostTensor& t = kv.second;
@@ -389,15 +481,19 @@ int tmac_model_finalize(tmac_model_t m)
     TMAC_CUDA_TRY(cudaMemcpy(m->emb_raw, emb->second.data.data(), emb->second.data.size(), cudaMemcpyHostToDevice));
     const size_t kv = (size_t)kLayers * m->max_seq * kKvDim;
     if ((rc = dev_alloc(m, &m->hidden, kHidden)) || (rc = dev_alloc(m, &m->xn, kHidden)) ||
-        (rc = dev_alloc(m, &m->q, kHidden)) || (rc = dev_alloc(m, &m->k, kKvDim)) ||
-        (rc = dev_alloc(m, &m->v, kKvDim)) || (rc = dev_alloc(m, &m->ctx, kHidden)) ||
-        (rc = dev_alloc(m, &m->attn, kHidden)) || (rc = dev_alloc(m, &m->gate, kInter)) ||
-        (rc = dev_alloc(m, &m->up, kInter)) || (rc = dev_alloc(m, &m->ffn, kHidden)) ||
+        (rc = dev_alloc(m, &m->q, kHidden + 2 * kKvDim)) || (rc = dev_alloc(m, &m->ctx, kHidden)) ||
+        (rc = dev_alloc(m, &m->attn, kHidden)) || (rc = dev_alloc(m, &m->gate, 2 * kInter)) ||
+        (rc = dev_alloc(m, &m->ffn, kHidden)) ||
         (rc = dev_alloc(m, &m->logits, kVocab)) || (rc = dev_alloc(m, &m->kcache, kv)) ||
         (rc = dev_alloc(m, &m->vcache, kv)) || (rc = dev_alloc(m, &m->key, 1)) ||
         (rc = dev_alloc(m, &m->token_log, 1)) || (rc = dev_alloc(m, &m->xq, kInter)) ||
-        (rc = dev_alloc(m, &m->xs, 1)))
+        (rc = dev_alloc(m, &m->xs, 1)) || (rc = dev_alloc(m, &m->pos_dev, 1)) ||
+        (rc = dev_alloc(m, &m->tokens, (size_t)m->max_seq)) ||
+        (rc = dev_alloc(m, &m->hidden_log, (size_t)m->max_seq * kHidden)))
         return rc;
+    m->k = m->q + kHidden;  // q | k | v and gate | up are contiguous: the concatenated GEMV outputs
+    m->v = m->k + kKvDim;
+    m->up = m->gate + kInter;
     // RoPE tables with the reference's own float expression (apply_rope, :1528-1554)
     std::vector<float> c((size_t)m->max_seq * 32), sn((size_t)m->max_seq * 32);
     for (int pos = 0; pos < m->max_seq; pos++)
@@ -436,9 +532,7 @@ int tmac_model_forward(tmac_model_t m, int token, int pos, void* stream)
     if (token >= kVocab) return fail(TMAC_ERR_SHAPE, "token id out of range");
     DeviceGuard dg(m->device);
     cudaStream_t s = (cudaStream_t)stream;
-    embed_q8_kernel<<<4, 256, 0, s>>>(m->emb_raw, token, token < 0 ? m->key : nullptr, m->token_log, m->hidden);
-    for (int l = 0; l < kLayers; l++)
-        if ((rc = layer(m, l, pos, s))) return rc;
+    if ((rc = forward_all(m, token, token < 0 ? m->key : nullptr, pos, s, nullptr, 0))) return rc;
     return TMAC_OK;
 }
 
@@ -447,14 +541,8 @@ int tmac_model_logits(tmac_model_t m, void* stream)
     int rc = model_ok(m);
     if (rc) return rc;
     DeviceGuard dg(m->device);
-    cudaStream_t s = (cudaStream_t)stream;
-    const float* on = vec_or_null(m, "output_norm.weight");
-    const float* x = m->hidden;
-    if (on) {
-        rmsnorm_kernel<<<1, 256, 0, s>>>(m->hidden, on, m->xn, nullptr, nullptr, kHidden);
-        x = m->xn;
-    }
-    return tmac_gemv_top1(m->mats["token_embd.weight"], x, m->logits, (uint64_t*)m->key, 0, 1, stream);
+    // xn already holds output_norm(hidden): the last layer's closing norm
+    return tmac_gemv_top1(m->mats["token_embd.weight"], m->xn, m->logits, (uint64_t*)m->key, 0, 1, stream);
 }
 
 int tmac_model_buffers(tmac_model_t m, float** hidden, float** logits, uint64_t** key)
@@ -470,29 +558,52 @@ int tmac_model_buffers(tmac_model_t m, float** hidden, float** logits, uint64_t*
 int tmac_model_generate(tmac_model_t m, const int* prompt, int n_prompt, int n_gen, int* out_tokens,
                         float* out_hidden, void* stream)
 {
+    (void)stream;  // generation runs on the model's own stream (graphs need a non-default stream)
     int rc = model_ok(m);
     if (rc) return rc;
     if (!prompt || n_prompt <= 0 || n_gen < 0 || !out_tokens) return fail(TMAC_ERR_INVALID, "bad arguments");
     if (n_prompt + n_gen > m->max_seq) return fail(TMAC_ERR_SHAPE, "prompt + generation exceed the KV cache");
-    DeviceGuard dg(m->device);
-    cudaStream_t s = (cudaStream_t)stream;
-    if ((rc = tmac_model_reset(m, stream))) return rc;
     for (int t = 0; t < n_prompt; t++)
-        if ((rc = tmac_model_forward(m, prompt[t], t, stream))) return rc;
-    if (out_hidden) {
-        TMAC_CUDA_TRY(cudaMemcpyAsync(out_hidden, m->hidden, kHidden * sizeof(float), cudaMemcpyDeviceToHost, s));
+        if (prompt[t] < 0 || prompt[t] >= kVocab) return fail(TMAC_ERR_SHAPE, "prompt token id out of range");
+    DeviceGuard dg(m->device);
+    if (!m->stream) TMAC_CUDA_TRY(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking));
+    cudaStream_t s = m->stream;
+    // One graph per step kind: a prompt step (embed + 24 layers) and a greedy
+    // step (output norm + logits + top-1, then embed + 24 layers).  Position
+    // and tokens live in device memory, so one capture serves every position.
+    if (m->graph_n_prompt != n_prompt) {
+        if (m->g_prompt) cudaGraphExecDestroy(m->g_prompt);
+        if (m->g_gen) cudaGraphExecDestroy(m->g_gen);
+        m->g_prompt = m->g_gen = nullptr;
+        for (int kind = 0; kind < 2; kind++) {
+            cudaGraph_t g = nullptr;
+            TMAC_CUDA_TRY(cudaStreamBeginCapture(s, cudaStreamCaptureModeRelaxed));
+            int crc = TMAC_OK;
+            if (kind == 1) crc = tmac_model_logits(m, s);
+            if (!crc) crc = forward_all(m, -1, m->key, 0, s, m->pos_dev, n_prompt);
+            if (!crc) step_done_kernel<<<1, 256, 0, s>>>(m->hidden, m->hidden_log, m->pos_dev);
+            cudaError_t e = cudaStreamEndCapture(s, &g);
+            if (crc) {
+                if (g) cudaGraphDestroy(g);
+                return crc;
+            }
+            if (e != cudaSuccess) return cuda_fail(e, "cudaStreamEndCapture");
+            e = cudaGraphInstantiate(kind ? &m->g_gen : &m->g_prompt, g, 0);
+            cudaGraphDestroy(g);
+            if (e != cudaSuccess) return cuda_fail(e, "cudaGraphInstantiate");
+        }
+        m->graph_n_prompt = n_prompt;
     }
-    for (int g = 0; g < n_gen; g++) {
-        // logits of the current hidden state, greedy token (device key), its
-        // embedding and the next forward pass: no host round trip per step.
-        if ((rc = tmac_model_logits(m, stream))) return rc;
-        if ((rc = tmac_model_forward(m, -1, n_prompt + g, stream))) return rc;
-        TMAC_CUDA_TRY(cudaMemcpyAsync(out_tokens + g, m->token_log, sizeof(int), cudaMemcpyDeviceToHost, s));
-        if (out_hidden)
-            TMAC_CUDA_TRY(cudaMemcpyAsync(out_hidden + (size_t)(g + 1) * kHidden, m->hidden, kHidden * sizeof(float),
-                                          cudaMemcpyDeviceToHost, s));
-    }
+    if ((rc = tmac_model_reset(m, s))) return rc;
+    TMAC_CUDA_TRY(cudaMemcpyAsync(m->tokens, prompt, n_prompt * sizeof(int), cudaMemcpyHostToDevice, s));
+    TMAC_CUDA_TRY(cudaMemsetAsync(m->pos_dev, 0, sizeof(int), s));
+    for (int t = 0; t < n_prompt; t++) TMAC_CUDA_TRY(cudaGraphLaunch(m->g_prompt, s));
+    for (int g = 0; g < n_gen; g++) TMAC_CUDA_TRY(cudaGraphLaunch(m->g_gen, s));
     TMAC_CUDA_TRY(cudaStreamSynchronize(s));
+    TMAC_CUDA_TRY(cudaMemcpy(out_tokens, m->tokens + n_prompt, n_gen * sizeof(int), cudaMemcpyDeviceToHost));
+    if (out_hidden)
+        TMAC_CUDA_TRY(cudaMemcpy(out_hidden, m->hidden_log + (size_t)(n_prompt - 1) * kHidden,
+                                 (size_t)(n_gen + 1) * kHidden * sizeof(float), cudaMemcpyDeviceToHost));
     return TMAC_OK;
 }
 
@@ -500,6 +611,9 @@ int tmac_model_free(tmac_model_t m)
 {
     if (!m) return TMAC_OK;
     DeviceGuard dg(m->device);
+    if (m->g_prompt) cudaGraphExecDestroy(m->g_prompt);
+    if (m->g_gen) cudaGraphExecDestroy(m->g_gen);
+    if (m->stream) cudaStreamDestroy(m->stream);
     for (auto& kv : m->mats) tmac_weight_free(kv.second);
     for (void* p : m->allocs) cudaFree(p);
     delete m;

@@ -130,47 +130,54 @@ TMAC_DEV long long warp_sum_ll(long long v)
     return v;
 }
 
-// One warp per row (grid-stride), lane = one 32-value chunk per iteration; the
-// decoded chunk is reused for every activation vector of the launch.
+// A CTA works on rows in groups of `rpc` rows, `wpr` warps per row; thread t of
+// a row decodes chunk t (then t + 32*wpr, ...) and reuses the decoded values for
+// every activation vector of the launch.  Row sums: warp shuffle, then the
+// row's warps combine through shared memory.
 template <int TYPE, int NB>
-__global__ void __launch_bounds__(kThreads) blockq_gemv_kernel(BlockqArgs a)
+__global__ void __launch_bounds__(kThreads) blockq_gemv_kernel(BlockqArgs a, int wpr, int rpc)
 {
     extern __shared__ __align__(16) uint8_t smem[];
     const int64_t cols = a.cols, cpr = cols / 32;
     const int nb = a.nb;
     int16_t* xq = reinterpret_cast<int16_t*>(smem);                                    // [nb][cols]
-    float* xs = reinterpret_cast<float*>(smem + ((size_t)nb * cols * 2 + 15) / 16 * 16);  // [NB]
+    float* xs = reinterpret_cast<float*>(smem + ((size_t)nb * cols * 2 + 15) / 16 * 16);  // [16]
     float* red = xs + 16;                                                              // [8]
+    long long* part_s = reinterpret_cast<long long*>(red + 8);                        // [8 warps][NB]
 
     if (a.xq_in) {
         const uint4* src = reinterpret_cast<const uint4*>(a.xq_in);
         uint4* dst = reinterpret_cast<uint4*>(xq);
-        for (int64_t j = threadIdx.x; j < (int64_t)nb * cols / 8; j += kThreads) dst[j] = src[j];
+        for (int64_t j = threadIdx.x; j < (int64_t)nb * cols / 8; j += blockDim.x) dst[j] = src[j];
         if (threadIdx.x < nb) xs[threadIdx.x] = a.xs_in[threadIdx.x];
     } else {
         // activation quantisation, one vector at a time (tmac_gguf.cpp:889-896)
         for (int b = 0; b < nb; b++) {
             const float* xb = a.x + (int64_t)b * cols;
             float mx = 0.0f;
-            for (int64_t j = threadIdx.x; j < cols; j += kThreads) mx = fmaxf(mx, fabsf(xb[j]));
-            mx = block_max(mx, red, kThreads);
+            for (int64_t j = threadIdx.x; j < cols; j += blockDim.x) mx = fmaxf(mx, fabsf(xb[j]));
+            mx = block_max(mx, red, blockDim.x);
             const float s = x_scale_from_max(mx);
             if (threadIdx.x == 0) xs[b] = s;
-            for (int64_t j = threadIdx.x; j < cols; j += kThreads) xq[b * cols + j] = quantize_one(xb[j], s);
+            for (int64_t j = threadIdx.x; j < cols; j += blockDim.x) xq[b * cols + j] = quantize_one(xb[j], s);
         }
     }
     __syncthreads();
 
-    const int lane = threadIdx.x & 31, nw = kThreads / 32;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int rw = warp % wpr, rr = warp / wpr;  // warp within the row, row within the group
+    const int tpr = wpr * 32;
     const int64_t upr = (TYPE == TMAC_TYPE_Q5_0) ? cpr : cpr / 8;
-    for (int64_t r = (int64_t)blockIdx.x * nw + (threadIdx.x >> 5); r < a.rows; r += (int64_t)gridDim.x * nw) {
-        const float ri = __ldg(a.row_inv + r);
+    for (int64_t r0 = (int64_t)blockIdx.x * rpc; r0 < a.rows; r0 += (int64_t)gridDim.x * rpc) {
+        const int64_t r = r0 + rr;
+        const bool row_live = r < a.rows;
+        const float ri = row_live ? __ldg(a.row_inv + r) : 1.0f;
         long long acc[NB];
 #pragma unroll
         for (int b = 0; b < NB; b++) acc[b] = 0;
-        for (int64_t base = 0; base < cpr; base += 32) {
-            const int64_t ch = base + lane;
-            const bool live = ch < cpr;
+        for (int64_t base = 0; base < cpr; base += tpr) {
+            const int64_t ch = base + rw * 32 + lane;
+            const bool live = row_live && ch < cpr;
             int v[32];
             if (live) decode_chunk<TYPE>(a.raw, r, cpr, ch, ri, v);
 #pragma unroll
@@ -206,13 +213,18 @@ __global__ void __launch_bounds__(kThreads) blockq_gemv_kernel(BlockqArgs a)
 #pragma unroll
         for (int b = 0; b < NB; b++) {
             if (b >= nb) break;
-            const long long tot = warp_sum_ll(acc[b]);
-            if (lane == 0) {
-                const double v = __ddiv_rn(__dmul_rn((double)tot, (double)xs[b]), (double)ri);
-                a.y[(int64_t)b * a.rows + r] = (float)v;
-                if (a.row_acc) a.row_acc[(int64_t)b * a.rows + r] = tot;
-            }
+            const long long t = warp_sum_ll(acc[b]);
+            if (lane == 0) part_s[warp * NB + b] = t;
         }
+        __syncthreads();
+        if (rw == 0 && lane < nb && row_live) {
+            long long tot = 0;
+            for (int w = 0; w < wpr; w++) tot += part_s[(rr * wpr + w) * NB + lane];
+            const double v = __ddiv_rn(__dmul_rn((double)tot, (double)xs[lane]), (double)ri);
+            a.y[(int64_t)lane * a.rows + r] = (float)v;
+            if (a.row_acc) a.row_acc[(int64_t)lane * a.rows + r] = tot;
+        }
+        __syncthreads();
     }
 }
 
@@ -226,10 +238,13 @@ int launch_nb(const tmac_weight_s* w, const BlockqArgs& a, cudaStream_t s)
                                            (int)max_smem));
         attr[w->device & 63] = true;
     }
-    const size_t smem = ((size_t)a.nb * a.cols * 2 + 15) / 16 * 16 + 24 * 4;
-    const int64_t warps = kThreads / 32;
-    const int grid = (int)std::min<int64_t>((a.rows + warps - 1) / warps, (int64_t)num_sms(w->device) * 8);
-    blockq_gemv_kernel<TYPE, NB><<<grid, kThreads, smem, s>>>(a);
+    // warps per row: enough lanes for every 32-value chunk of a row (at most 8)
+    const int64_t cpr = a.cols / 32;
+    const int wpr = (int)std::min<int64_t>(8, (cpr + 31) / 32);
+    const int rpc = 8 / wpr;
+    const size_t smem = ((size_t)a.nb * a.cols * 2 + 15) / 16 * 16 + 24 * 4 + 8 * NB * 8;
+    const int grid = (int)std::min<int64_t>((a.rows + rpc - 1) / rpc, (int64_t)num_sms(w->device) * 16);
+    blockq_gemv_kernel<TYPE, NB><<<grid, wpr * rpc * 32, smem, s>>>(a, wpr, rpc);
     TMAC_CUDA_TRY(cudaGetLastError());
     return TMAC_OK;
 }
