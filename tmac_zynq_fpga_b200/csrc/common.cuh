@@ -168,9 +168,42 @@ TMAC_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar
         "l"(src), "r"(bytes), "r"(smem_addr(bar))
         : "memory");
 }
+// Programmatic dependent launch.  pdl_wait: wait until the preceding grid in
+// the stream has completed and its writes are visible -- a no-op for a kernel
+// launched without the programmatic-serialisation attribute, so every kernel
+// calls it before its first read of data another kernel produced, and writes
+// nothing to global memory before it.  pdl_launch: let the next grid start
+// its own prologue now.
+TMAC_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+TMAC_DEV void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;"); }
+
 TMAC_DEV void named_bar_sync(int id, int nthreads)
 {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// Launches with programmatic stream serialisation while the calling thread has
+// PDL enabled (the decode engine enables it around its graph capture).
+extern thread_local bool g_pdl;
+struct PdlScope {
+    bool prev;
+    PdlScope() : prev(g_pdl) { g_pdl = true; }
+    ~PdlScope() { g_pdl = prev; }
+};
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = g_pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 
 }  // namespace tmac

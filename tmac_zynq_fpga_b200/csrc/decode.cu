@@ -43,6 +43,8 @@ __global__ void embed_q8_kernel(const uint8_t* __restrict__ emb, int token, cons
                                 int* token_log, float* __restrict__ hidden, const int* pos_dev, int* tokens,
                                 int n_prompt)
 {
+    pdl_launch();
+    pdl_wait();
     // token: a host id; or (pos_dev) the prompt token tokens[pos] while
     // pos < n_prompt, else the greedy token of the device top-1 key.
     int tok = token;
@@ -69,12 +71,18 @@ __global__ void embed_q8_kernel(const uint8_t* __restrict__ emb, int token, cons
 }
 
 // End of one token: log the hidden state at its position, advance the position.
-__global__ void step_done_kernel(const float* __restrict__ hidden, float* __restrict__ hidden_log, int* pos_dev)
+__global__ void step_done_kernel(const float* __restrict__ hidden, float* __restrict__ hidden_log, int* pos_dev,
+                                 unsigned long long* key)
 {
+    pdl_launch();
+    pdl_wait();
     const int p = *pos_dev;
     for (int i = threadIdx.x; i < kHidden; i += blockDim.x) hidden_log[(int64_t)p * kHidden + i] = hidden[i];
     __syncthreads();
-    if (threadIdx.x == 0) *pos_dev = p + 1;
+    if (threadIdx.x == 0) {
+        *pos_dev = p + 1;
+        *key = 0;  // ready for the next step's top-1 (atomic max)
+    }
 }
 
 // rms_norm (:447-454): one CTA; the sum of squares is sequential, as in the
@@ -87,6 +95,8 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(float* __restrict__ x, con
                                                       const float* __restrict__ w, float* __restrict__ o,
                                                       int16_t* __restrict__ xq, float* __restrict__ xs, int n)
 {
+    pdl_launch();
+    pdl_wait();
     __shared__ __align__(16) float xsh[kInter];
     __shared__ float red[8];
     __shared__ float scale;
@@ -145,6 +155,8 @@ __global__ void __launch_bounds__(256) rope_attention_kernel(
     const float* __restrict__ cs, const float* __restrict__ sn, int pos, const int* pos_dev, float* __restrict__ kc,
     float* __restrict__ vc, float* __restrict__ ctx)
 {
+    pdl_launch();
+    pdl_wait();
     extern __shared__ float sc[];  // [pos + 1] scores, then weights
     __shared__ float qs[kHeadDim], ks[kHeadDim], vs[kHeadDim];
     __shared__ float log_sum;
@@ -202,6 +214,8 @@ __global__ void __launch_bounds__(256) rope_attention_kernel(
 __global__ void __launch_bounds__(1024) silu_mul_kernel(float* __restrict__ g, const float* __restrict__ u, int n,
                                                         int16_t* __restrict__ xq, float* __restrict__ xs)
 {
+    pdl_launch();
+    pdl_wait();
     __shared__ float red[32];
     float mx = 0.0f;
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
@@ -319,15 +333,19 @@ int layer(tmac_model_s* m, int l, int pos, cudaStream_t s, const int* pos_dev = 
         if ((rc = gemv(m, lname(l, "attn_v.weight"), m->xn, m->v, s, true))) return rc;
     }
     const int nscore = pos_dev ? m->max_seq : pos + 1;
-    rope_attention_kernel<<<kHeads, 256, nscore * sizeof(float), s>>>(
-        m->q, m->k, m->v, vec_or_null(m, lname(l, "attn_q.bias")), vec_or_null(m, lname(l, "attn_k.bias")),
-        vec_or_null(m, lname(l, "attn_v.bias")), m->rope_c, m->rope_s, pos, pos_dev, kc, vc, m->ctx);
+    TMAC_CUDA_TRY(launch_k(rope_attention_kernel, dim3(kHeads), dim3(256), nscore * sizeof(float), s, (const float*)m->q,
+                           (const float*)m->k, (const float*)m->v, vec_or_null(m, lname(l, "attn_q.bias")),
+                           vec_or_null(m, lname(l, "attn_k.bias")), vec_or_null(m, lname(l, "attn_v.bias")),
+                           (const float*)m->rope_c, (const float*)m->rope_s, pos, pos_dev, kc, vc, m->ctx));
     if ((rc = gemv(m, lname(l, "attn_output.weight"), m->ctx, m->attn, s))) return rc;
-    rmsnorm_kernel<<<1, 256, 0, s>>>(m->hidden, m->attn, fn, m->xn, m->xq, m->xs, kHidden);
+    TMAC_CUDA_TRY(launch_k(rmsnorm_kernel, dim3(1), dim3(256), 0, s, m->hidden, (const float*)m->attn, fn, m->xn,
+                           m->xq, m->xs, kHidden));
     if ((rc = gemv(m, lname(l, "ffn_gate_up"), m->xn, m->gate, s, true))) return rc;
-    silu_mul_kernel<<<1, 1024, 0, s>>>(m->gate, m->up, kInter, m->xq, m->xs);
+    TMAC_CUDA_TRY(launch_k(silu_mul_kernel, dim3(1), dim3(1024), 0, s, m->gate, (const float*)m->up, kInter, m->xq,
+                           m->xs));
     if ((rc = gemv(m, lname(l, "ffn_down.weight"), m->gate, m->ffn, s, true))) return rc;
-    rmsnorm_kernel<<<1, 256, 0, s>>>(m->hidden, m->ffn, next_norm(m, l), m->xn, m->xq, m->xs, kHidden);
+    TMAC_CUDA_TRY(launch_k(rmsnorm_kernel, dim3(1), dim3(256), 0, s, m->hidden, (const float*)m->ffn, next_norm(m, l),
+                           m->xn, m->xq, m->xs, kHidden));
     TMAC_CUDA_TRY(cudaGetLastError());
     return TMAC_OK;
 }
@@ -337,13 +355,22 @@ int forward_all(tmac_model_s* m, int token, const unsigned long long* key, int p
                 const int* pos_dev, int n_prompt)
 {
     int rc;
-    embed_q8_kernel<<<4, 256, 0, s>>>(m->emb_raw, token, key, m->token_log, m->hidden, pos_dev, m->tokens, n_prompt);
+    TMAC_CUDA_TRY(launch_k(embed_q8_kernel, dim3(4), dim3(256), 0, s, (const uint8_t*)m->emb_raw, token, key,
+                           m->token_log, m->hidden, pos_dev, m->tokens, n_prompt));
     const float* an = vec_or_null(m, lname(0, "attn_norm.weight"));
     if (!an) return fail(TMAC_ERR_INVALID, "missing attn_norm weights");
-    rmsnorm_kernel<<<1, 256, 0, s>>>(m->hidden, nullptr, an, m->xn, m->xq, m->xs, kHidden);
+    TMAC_CUDA_TRY(launch_k(rmsnorm_kernel, dim3(1), dim3(256), 0, s, m->hidden, (const float*)nullptr, an, m->xn, m->xq,
+                           m->xs, kHidden));
     for (int l = 0; l < kLayers; l++)
         if ((rc = layer(m, l, pos, s, pos_dev))) return rc;
     return TMAC_OK;
+}
+
+// Logits of the current hidden state with the top-1 merged into m->key, which
+// the caller has zeroed (step_done_kernel does it inside generation graphs).
+int logits_into_key(tmac_model_s* m, cudaStream_t s)
+{
+    return launch_q8_0(m->mats["token_embd.weight"], m->xn, m->logits, nullptr, nullptr, 1, s, m->key, 0);
 }
 
 int model_ok(tmac_model_t m, bool need_final = true)
@@ -577,11 +604,20 @@ int tmac_model_generate(tmac_model_t m, const int* prompt, int n_prompt, int n_g
         m->g_prompt = m->g_gen = nullptr;
         for (int kind = 0; kind < 2; kind++) {
             cudaGraph_t g = nullptr;
+            PdlScope pdl;  // kernels of the step overlap their launch with the previous kernel
             TMAC_CUDA_TRY(cudaStreamBeginCapture(s, cudaStreamCaptureModeRelaxed));
             int crc = TMAC_OK;
-            if (kind == 1) crc = tmac_model_logits(m, s);
+            if (kind == 1) {
+                tmac_weight_s* lw = m->mats["token_embd.weight"];
+                if (lw->mode == TMAC_MODE_NATIVE) crc = logits_into_key(m, s);
+                else crc = tmac_model_logits(m, s);
+            }
             if (!crc) crc = forward_all(m, -1, m->key, 0, s, m->pos_dev, n_prompt);
-            if (!crc) step_done_kernel<<<1, 256, 0, s>>>(m->hidden, m->hidden_log, m->pos_dev);
+            if (!crc) {
+                cudaError_t le = launch_k(step_done_kernel, dim3(1), dim3(256), 0, s, (const float*)m->hidden,
+                                          m->hidden_log, m->pos_dev, m->key);
+                if (le != cudaSuccess) crc = cuda_fail(le, "step_done_kernel");
+            }
             cudaError_t e = cudaStreamEndCapture(s, &g);
             if (crc) {
                 if (g) cudaGraphDestroy(g);
@@ -595,6 +631,7 @@ int tmac_model_generate(tmac_model_t m, const int* prompt, int n_prompt, int n_g
         m->graph_n_prompt = n_prompt;
     }
     if ((rc = tmac_model_reset(m, s))) return rc;
+    TMAC_CUDA_TRY(cudaMemsetAsync(m->key, 0, sizeof(unsigned long long), s));
     TMAC_CUDA_TRY(cudaMemcpyAsync(m->tokens, prompt, n_prompt * sizeof(int), cudaMemcpyHostToDevice, s));
     TMAC_CUDA_TRY(cudaMemsetAsync(m->pos_dev, 0, sizeof(int), s));
     for (int t = 0; t < n_prompt; t++) TMAC_CUDA_TRY(cudaGraphLaunch(m->g_prompt, s));

@@ -44,26 +44,53 @@ __global__ void row_inv_kernel(const uint8_t* __restrict__ raw, int64_t rows, in
 }
 
 // --------------------------------------------------- chunk decode (32 values)
-// Decodes chunk `ch` of row `r` into v[32] (int16 values held in ints).
+// roundf(t) of the reference (round half away from zero) as an int16 in the
+// low 16 bits, exact for every finite |t| < 2^22 without a float->int
+// conversion instruction:
+//   floor(RD(|t| + 0.5)) == floor(|t| + 0.5)   (integers are representable, so
+//                                               rounding down never crosses one)
+//   RD(w + 2^23) = 2^23 + floor(w)             (the ulp there is 1)
+// then the sign of t is applied.  No clamp is needed: every |t| is at most
+// max|w| * (32767 / max|w|) rounded, i.e. below 32767.5.
+TMAC_DEV uint32_t round_i16(float t)
+{
+    const float w = __fadd_rd(fabsf(t), 0.5f);
+    const int va = __float_as_int(__fadd_rd(w, 8388608.0f)) - 0x4B000000;
+    const int m = __float_as_int(t) >> 31;
+    return (uint32_t)((va ^ m) - m);
+}
+
+// float(n) for 0 <= n < 2^23 minus a constant: exact, via the 2^23 exponent.
+TMAC_DEV float small_int_f(uint32_t n, float minus) { return __fsub_rn(__uint_as_float(0x4B000000u | n), minus); }
+
+TMAC_DEV uint32_t pack2(uint32_t lo, uint32_t hi) { return __byte_perm(lo, hi, 0x5410); }
+
+// Decodes chunk `ch` of row `r` into 16 words of int16 pairs (values 2i, 2i+1),
+// each value = roundf(w_f32 * row_inv) with w_f32 in the reference's fp32 order
+// (fpga_sim.hpp:1030-1037, :773-778, :1099-1104).
 template <int TYPE>
-TMAC_DEV void decode_chunk(const uint8_t* __restrict__ raw, int64_t r, int64_t cpr, int64_t ch, float ri, int (&v)[32])
+TMAC_DEV void decode_chunk(const uint8_t* __restrict__ raw, int64_t r, int64_t cpr, int64_t ch, float ri,
+                           uint32_t (&vw)[16])
 {
     if (TYPE == TMAC_TYPE_Q5_0) {
         const uint8_t* b = raw + (r * cpr + ch) * 22;  // 2-byte aligned
         const float d = f16_bits_to_f32(ldg16(b));
         const uint32_t qh = (uint32_t)ldg16(b + 2) | ((uint32_t)ldg16(b + 4) << 16);
-        uint8_t qs[16];
+        uint32_t qw[4];
 #pragma unroll
-        for (int i = 0; i < 8; i++) {
-            uint16_t h = ldg16(b + 6 + 2 * i);
-            qs[2 * i] = (uint8_t)h;
-            qs[2 * i + 1] = (uint8_t)(h >> 8);
-        }
+        for (int i = 0; i < 4; i++) qw[i] = (uint32_t)ldg16(b + 6 + 4 * i) | ((uint32_t)ldg16(b + 8 + 4 * i) << 16);
 #pragma unroll
-        for (int wi = 0; wi < 32; wi++) {
-            const int ql = wi < 16 ? (qs[wi] & 0xF) : (qs[wi - 16] >> 4);
-            const int q = ((((qh >> wi) & 1) << 4) | ql) - 16;
-            v[wi] = clamp_round_i16(__fmul_rn(__fmul_rn(d, (float)q), ri));
+        for (int wi = 0; wi < 32; wi += 2) {
+            uint32_t v2[2];
+#pragma unroll
+            for (int k = 0; k < 2; k++) {
+                const int e = wi + k, j = e & 15;
+                const uint32_t nib = (qw[j >> 2] >> (8 * (j & 3) + (e >= 16 ? 4 : 0))) & 0xFu;
+                const uint32_t raw5 = nib | (((qh >> e) & 1u) << 4);
+                const float q = small_int_f(raw5, 8388624.0f);  // raw5 - 16
+                v2[k] = round_i16(__fmul_rn(__fmul_rn(d, q), ri));
+            }
+            vw[wi / 2] = pack2(v2[0], v2[1]);
         }
     } else if (TYPE == TMAC_TYPE_Q4_K) {
         const int64_t sb = ch >> 3;
@@ -77,13 +104,20 @@ TMAC_DEV void decode_chunk(const uint8_t* __restrict__ raw, int64_t r, int64_t c
         q4_k_scale_min(hb + 4, sub, sc, m);
         const float A = __fmul_rn(d, (float)sc), B = __fmul_rn(dmin, (float)m);
         const uint4* qp = reinterpret_cast<const uint4*>(b + 16 + (sub >> 1) * 32);
-        uint4 q2[2] = {__ldg(qp), __ldg(qp + 1)};
-        const uint8_t* qs = reinterpret_cast<const uint8_t*>(q2);
+        const uint4 q0 = __ldg(qp), q1 = __ldg(qp + 1);
+        const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
         const int shift = (sub & 1) * 4;
 #pragma unroll
-        for (int j = 0; j < 32; j++) {
-            const int q4 = (qs[j] >> shift) & 0xF;
-            v[j] = clamp_round_i16(__fmul_rn(__fsub_rn(__fmul_rn(A, (float)q4), B), ri));
+        for (int j = 0; j < 32; j += 2) {
+            uint32_t v2[2];
+#pragma unroll
+            for (int k = 0; k < 2; k++) {
+                const int e = j + k;
+                const uint32_t q4 = (qw[e >> 2] >> (8 * (e & 3) + shift)) & 0xFu;
+                const float q = small_int_f(q4, 8388608.0f);
+                v2[k] = round_i16(__fmul_rn(__fsub_rn(__fmul_rn(A, q), B), ri));
+            }
+            vw[j / 2] = pack2(v2[0], v2[1]);
         }
     } else {  // Q6_K
         const int64_t sb = ch >> 3;
@@ -96,19 +130,43 @@ TMAC_DEV void decode_chunk(const uint8_t* __restrict__ raw, int64_t r, int64_t c
         const uint8_t* ql = b + half * 64 + (sub & 1) * 32;
         const uint8_t* qhp = b + 128 + half * 32;
         const int lshift = (sub < 2) ? 0 : 4, hshift = sub * 2;
+        uint32_t lw[8], hw[8];
 #pragma unroll
-        for (int i = 0; i < 16; i++) {
-            const uint16_t lw = ldg16(ql + 2 * i), hw = ldg16(qhp + 2 * i);
+        for (int i = 0; i < 8; i++) {
+            lw[i] = (uint32_t)ldg16(ql + 4 * i) | ((uint32_t)ldg16(ql + 4 * i + 2) << 16);
+            hw[i] = (uint32_t)ldg16(qhp + 4 * i) | ((uint32_t)ldg16(qhp + 4 * i + 2) << 16);
+        }
+#pragma unroll
+        for (int l = 0; l < 32; l += 2) {
+            uint32_t v2[2];
 #pragma unroll
             for (int k = 0; k < 2; k++) {
-                const int l = 2 * i + k;
-                const int lo = ((k ? (lw >> 8) : lw) >> lshift) & 0xF;
-                const int hi = ((k ? (hw >> 8) : hw) >> hshift) & 0x3;
-                const int q6 = ((hi << 4) | lo) - 32;
-                v[l] = clamp_round_i16(__fmul_rn(__fmul_rn(l < 16 ? A0 : A1, (float)q6), ri));
+                const int e = l + k, bs = 8 * (e & 3);
+                const uint32_t lo = (lw[e >> 2] >> (bs + lshift)) & 0xFu;
+                const uint32_t hi = (hw[e >> 2] >> (bs + hshift)) & 0x3u;
+                const float q = small_int_f((hi << 4) | lo, 8388640.0f);  // q6 = raw6 - 32
+                v2[k] = round_i16(__fmul_rn(__fmul_rn(e < 16 ? A0 : A1, q), ri));
             }
+            vw[l / 2] = pack2(v2[0], v2[1]);
         }
     }
+}
+
+// Exact sum of 32 int16 weights (16 packed words) times the chunk's activations
+// given as signed high bytes xh and unsigned low bytes xl (x_q = 256*xh + xl):
+// dp2a products fit int32 for a chunk (|sum| < 2^28).
+TMAC_DEV long long chunk_dot(const uint32_t (&vw)[16], const uint32_t* xh, const uint32_t* xl)
+{
+    int sh = 0, sl = 0;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const uint32_t h = xh[i], l = xl[i];
+        asm("dp2a.lo.s32.s32 %0, %1, %2, %0;" : "+r"(sh) : "r"(vw[2 * i]), "r"(h));
+        asm("dp2a.hi.s32.s32 %0, %1, %2, %0;" : "+r"(sh) : "r"(vw[2 * i + 1]), "r"(h));
+        asm("dp2a.lo.s32.u32 %0, %1, %2, %0;" : "+r"(sl) : "r"(vw[2 * i]), "r"(l));
+        asm("dp2a.hi.s32.u32 %0, %1, %2, %0;" : "+r"(sl) : "r"(vw[2 * i + 1]), "r"(l));
+    }
+    return (long long)sh * 256 + (long long)sl;
 }
 
 struct BlockqArgs {
@@ -140,15 +198,38 @@ __global__ void __launch_bounds__(kThreads) blockq_gemv_kernel(BlockqArgs a, int
     extern __shared__ __align__(16) uint8_t smem[];
     const int64_t cols = a.cols, cpr = cols / 32;
     const int nb = a.nb;
-    int16_t* xq = reinterpret_cast<int16_t*>(smem);                                    // [nb][cols]
+    // activations as byte planes: x_q = 256 * xh (signed) + xl (unsigned)
+    uint8_t* xh = smem;                                                                // [nb][cols]
+    uint8_t* xl = smem + (size_t)nb * cols;                                            // [nb][cols]
     float* xs = reinterpret_cast<float*>(smem + ((size_t)nb * cols * 2 + 15) / 16 * 16);  // [16]
     float* red = xs + 16;                                                              // [8]
     long long* part_s = reinterpret_cast<long long*>(red + 8);                        // [8 warps][NB]
+    pdl_launch();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int rw = warp % wpr, rr = warp / wpr;  // warp within the row, row within the group
+    const int tpr = wpr * 32;
+    // The weights do not depend on the preceding kernel: fetch and decode this
+    // thread's first chunk before waiting for the activations.
+    uint32_t v0[16];
+    bool have_v0 = false;
+    {
+        const int64_t r = (int64_t)blockIdx.x * rpc + rr, ch = rw * 32 + lane;
+        if (r < a.rows && ch < cpr) {
+            decode_chunk<TYPE>(a.raw, r, cpr, ch, __ldg(a.row_inv + r), v0);
+            have_v0 = true;
+        }
+    }
+    pdl_wait();  // activations come from the preceding kernel
 
     if (a.xq_in) {
-        const uint4* src = reinterpret_cast<const uint4*>(a.xq_in);
-        uint4* dst = reinterpret_cast<uint4*>(xq);
-        for (int64_t j = threadIdx.x; j < (int64_t)nb * cols / 8; j += blockDim.x) dst[j] = src[j];
+        const uint2* src = reinterpret_cast<const uint2*>(a.xq_in);
+        uint32_t* h4 = reinterpret_cast<uint32_t*>(xh);
+        uint32_t* l4 = reinterpret_cast<uint32_t*>(xl);
+        for (int64_t j = threadIdx.x; j < (int64_t)nb * cols / 4; j += blockDim.x) {
+            const uint2 w = src[j];  // four int16
+            h4[j] = __byte_perm(w.x, w.y, 0x7531);
+            l4[j] = __byte_perm(w.x, w.y, 0x6420);
+        }
         if (threadIdx.x < nb) xs[threadIdx.x] = a.xs_in[threadIdx.x];
     } else {
         // activation quantisation, one vector at a time (tmac_gguf.cpp:889-896)
@@ -159,14 +240,15 @@ __global__ void __launch_bounds__(kThreads) blockq_gemv_kernel(BlockqArgs a, int
             mx = block_max(mx, red, blockDim.x);
             const float s = x_scale_from_max(mx);
             if (threadIdx.x == 0) xs[b] = s;
-            for (int64_t j = threadIdx.x; j < cols; j += blockDim.x) xq[b * cols + j] = quantize_one(xb[j], s);
+            for (int64_t j = threadIdx.x; j < cols; j += blockDim.x) {
+                const int16_t q = quantize_one(xb[j], s);
+                xh[b * cols + j] = (uint8_t)((uint16_t)q >> 8);
+                xl[b * cols + j] = (uint8_t)(q & 0xFF);
+            }
         }
     }
     __syncthreads();
 
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int rw = warp % wpr, rr = warp / wpr;  // warp within the row, row within the group
-    const int tpr = wpr * 32;
     const int64_t upr = (TYPE == TMAC_TYPE_Q5_0) ? cpr : cpr / 8;
     for (int64_t r0 = (int64_t)blockIdx.x * rpc; r0 < a.rows; r0 += (int64_t)gridDim.x * rpc) {
         const int64_t r = r0 + rr;
@@ -178,24 +260,21 @@ __global__ void __launch_bounds__(kThreads) blockq_gemv_kernel(BlockqArgs a, int
         for (int64_t base = 0; base < cpr; base += tpr) {
             const int64_t ch = base + rw * 32 + lane;
             const bool live = row_live && ch < cpr;
-            int v[32];
-            if (live) decode_chunk<TYPE>(a.raw, r, cpr, ch, ri, v);
+            uint32_t v[16];
+            if (r0 == (int64_t)blockIdx.x * rpc && base == 0 && have_v0) {
+#pragma unroll
+                for (int i = 0; i < 16; i++) v[i] = v0[i];
+            } else if (live) {
+                decode_chunk<TYPE>(a.raw, r, cpr, ch, ri, v);
+            }
 #pragma unroll
             for (int b = 0; b < NB; b++) {
                 if (b >= nb) break;
                 long long part = 0;
                 if (live) {
-                    const uint4* xv = reinterpret_cast<const uint4*>(xq + b * cols + ch * 32);
-#pragma unroll
-                    for (int q = 0; q < 4; q++) {
-                        const uint4 u = xv[q];
-                        const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-                        for (int k = 0; k < 4; k++) {
-                            const int x0 = (int)(int16_t)(w4[k] & 0xFFFF), x1 = (int)(int16_t)(w4[k] >> 16);
-                            part += (long long)(v[q * 8 + 2 * k] * x0 + v[q * 8 + 2 * k + 1] * x1);
-                        }
-                    }
+                    const uint32_t* h4 = reinterpret_cast<const uint32_t*>(xh + b * cols + ch * 32);
+                    const uint32_t* l4 = reinterpret_cast<const uint32_t*>(xl + b * cols + ch * 32);
+                    part = chunk_dot(v, h4, l4);
                 }
                 acc[b] += part;
                 if (a.unit_acc) {
@@ -244,7 +323,7 @@ int launch_nb(const tmac_weight_s* w, const BlockqArgs& a, cudaStream_t s)
     const int rpc = 8 / wpr;
     const size_t smem = ((size_t)a.nb * a.cols * 2 + 15) / 16 * 16 + 24 * 4 + 8 * NB * 8;
     const int grid = (int)std::min<int64_t>((a.rows + rpc - 1) / rpc, (int64_t)num_sms(w->device) * 16);
-    blockq_gemv_kernel<TYPE, NB><<<grid, wpr * rpc * 32, smem, s>>>(a, wpr, rpc);
+    TMAC_CUDA_TRY(launch_k(blockq_gemv_kernel<TYPE, NB>, dim3(grid), dim3(wpr * rpc * 32), smem, s, a, wpr, rpc));
     TMAC_CUDA_TRY(cudaGetLastError());
     return TMAC_OK;
 }

@@ -232,6 +232,7 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemv_kernel(Q8Args a)
     volatile int* abort_flag = reinterpret_cast<volatile int*>(red + 20);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    pdl_launch();
     const int64_t g0 = (int64_t)blockIdx.x * L.groups / gridDim.x;
     const int64_t g1 = (int64_t)(blockIdx.x + 1) * L.groups / gridDim.x;
     const int ng = (int)(g1 - g0);
@@ -317,6 +318,7 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemv_kernel(Q8Args a)
 
     // ---------------- consumers: activation quantisation (overlaps the copies)
     const int nct = kConsumerWarps * 32;
+    pdl_wait();  // x comes from the preceding kernel; the weights stream already
     float xs;
     if (a.xq_in) {
         for (int j = threadIdx.x; j < T * 64; j += nct) xq_s[j] = (j < a.cols) ? a.xq_in[j] : (int16_t)0;
@@ -469,7 +471,7 @@ int launch_q8_0(const tmac_weight_s* w, const float* x, float* y, int64_t* row_a
         a.top1 = top1 ? top1 + b : nullptr;
         a.index_base = index_base;
         a.err = device_error_word(w->device);
-        q8_gemv_kernel<<<grid, kThreads, smem, s>>>(a);
+        TMAC_CUDA_TRY(launch_k(q8_gemv_kernel, dim3(grid), dim3(kThreads), smem, s, a));
         TMAC_CUDA_TRY(cudaGetLastError());
     }
     return TMAC_OK;

@@ -26,6 +26,8 @@ std::vector<int*> g_err_ptr;    // per device: address of g_device_error
 std::vector<int> g_sms;
 }  // namespace
 
+thread_local bool g_pdl = false;
+
 void set_error(const std::string& msg) { g_last_error = msg; }
 
 int fail(int code, const std::string& msg)
