@@ -163,7 +163,11 @@ int tmac_quantize_x(const float* x, int64_t cols, int batch, int16_t* xq, float*
 int tmac_gemv_xq(tmac_weight_t w, const int16_t* xq, const float* xs, float* y, int batch, void* stream);
 
 /* Allocate the per-device workspace for GEMVs up to batch x cols now, so that
- * later calls allocate nothing (required before CUDA-graph capture). */
+ * later calls allocate nothing (required before CUDA-graph capture).
+ * tmac_gemv on a NATIVE Q5_0 / Q4_K / Q6_K weight quantises x once into this
+ * workspace (x_q int16 [batch][cols], x_scale [batch]) and grows it with
+ * cudaMalloc when a call needs more; calls on one device share it, so they
+ * must be ordered on one stream. */
 int tmac_reserve(int device, int64_t max_batch, int64_t max_cols);
 
 /* ------------------------------------------------------------------------ */

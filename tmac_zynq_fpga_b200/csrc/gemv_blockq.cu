@@ -322,7 +322,10 @@ int launch_nb(const tmac_weight_s* w, const BlockqArgs& a, cudaStream_t s)
     const int wpr = (int)std::min<int64_t>(8, (cpr + 31) / 32);
     const int rpc = 8 / wpr;
     const size_t smem = ((size_t)a.nb * a.cols * 2 + 15) / 16 * 16 + 24 * 4 + 8 * NB * 8;
-    const int grid = (int)std::min<int64_t>((a.rows + rpc - 1) / rpc, (int64_t)num_sms(w->device) * 16);
+    // few enough CTAs that the per-CTA activation quantisation (when x is fp32)
+    // stays small next to the rows each CTA works through
+    const int64_t cap = (int64_t)num_sms(w->device) * (a.xq_in ? 16 : 2);
+    const int grid = (int)std::min<int64_t>((a.rows + rpc - 1) / rpc, cap);
     TMAC_CUDA_TRY(launch_k(blockq_gemv_kernel<TYPE, NB>, dim3(grid), dim3(wpr * rpc * 32), smem, s, a, wpr, rpc));
     TMAC_CUDA_TRY(cudaGetLastError());
     return TMAC_OK;

@@ -12,6 +12,8 @@ __global__ void __launch_bounds__(1024) quantize_kernel(const float* __restrict_
                                                         int16_t* __restrict__ xq, float* __restrict__ xs)
 {
     __shared__ float red[32];
+    pdl_launch();
+    pdl_wait();
     const float* xb = x + (int64_t)blockIdx.x * cols;
     float mx = 0.0f;
     for (int64_t j = threadIdx.x; j < cols; j += blockDim.x) mx = fmaxf(mx, fabsf(xb[j]));
@@ -25,7 +27,7 @@ __global__ void __launch_bounds__(1024) quantize_kernel(const float* __restrict_
 
 int launch_quantize(const float* x, int64_t cols, int batch, int16_t* xq, float* xs, cudaStream_t s)
 {
-    quantize_kernel<<<batch, 1024, 0, s>>>(x, cols, xq, xs);
+    TMAC_CUDA_TRY(launch_k(quantize_kernel, dim3(batch), dim3(1024), 0, s, x, cols, xq, xs));
     TMAC_CUDA_TRY(cudaGetLastError());
     return TMAC_OK;
 }

@@ -150,6 +150,39 @@ int staging(int device, size_t xb, size_t yb, float** dx, float** dy)
     return TMAC_OK;
 }
 
+// Per-device activation workspace of the two-kernel block-quant GEMV path:
+// x_q (int16) and x_scale for up to `xq_cap` values / `xs_cap` vectors.
+struct Workspace {
+    int16_t* xq = nullptr;
+    float* xs = nullptr;
+    size_t xq_cap = 0, xs_cap = 0;
+};
+std::vector<Workspace> g_ws;
+
+int workspace(int device, size_t nxq, size_t nxs, int16_t** xq, float** xs)
+{
+    std::lock_guard<std::mutex> lk(g_dev_mutex);
+    if ((int)g_ws.size() <= device) g_ws.resize(device + 1);
+    Workspace& w = g_ws[device];
+    if (w.xq_cap < nxq) {
+        if (w.xq) cudaFree(w.xq);
+        w.xq = nullptr;
+        w.xq_cap = 0;
+        TMAC_CUDA_TRY(cudaMalloc(&w.xq, nxq * sizeof(int16_t)));
+        w.xq_cap = nxq;
+    }
+    if (w.xs_cap < nxs) {
+        if (w.xs) cudaFree(w.xs);
+        w.xs = nullptr;
+        w.xs_cap = 0;
+        TMAC_CUDA_TRY(cudaMalloc(&w.xs, nxs * sizeof(float)));
+        w.xs_cap = nxs;
+    }
+    *xq = w.xq;
+    *xs = w.xs;
+    return TMAC_OK;
+}
+
 void free_weight(tmac_weight_s* w)
 {
     if (!w) return;
@@ -337,7 +370,17 @@ int tmac_gemv_acc(tmac_weight_t w, const float* x, float* y, int64_t* row_acc, i
     cudaStream_t s = (cudaStream_t)stream;
     if (w->mode == TMAC_MODE_NATIVE && w->type == TMAC_TYPE_Q8_0)
         return launch_q8_0(w, x, y, row_acc, unit_acc, batch, s);
-    if (w->mode == TMAC_MODE_NATIVE) return launch_blockq(w, x, nullptr, nullptr, y, row_acc, unit_acc, batch, s);
+    if (w->mode == TMAC_MODE_NATIVE) {
+        // Quantise x once (one CTA per vector) into the device workspace, then
+        // every GEMV CTA reads x_q instead of re-quantising all columns.
+        if (w->cols % 8) return launch_blockq(w, x, nullptr, nullptr, y, row_acc, unit_acc, batch, s);
+        int16_t* xq = nullptr;
+        float* xs = nullptr;
+        int rc2 = workspace(w->device, (size_t)batch * w->cols, (size_t)batch, &xq, &xs);
+        if (rc2) return rc2;
+        if ((rc2 = launch_quantize(x, w->cols, batch, xq, xs, s))) return rc2;
+        return launch_blockq(w, nullptr, xq, xs, y, row_acc, unit_acc, batch, s);
+    }
     if (w->mode == TMAC_MODE_INT16) return launch_int16(w, x, y, row_acc, unit_acc, batch, s);
     return launch_f32(w, x, y, batch, s);
 }
@@ -440,11 +483,14 @@ int tmac_top1_decode(uint64_t key, float* value, int64_t* index)
 
 int tmac_reserve(int device, int64_t max_batch, int64_t max_cols)
 {
-    (void)max_batch;
-    (void)max_cols;
     int rc = check_device(device);
     if (rc) return rc;
+    if (max_batch < 0 || max_cols < 0) return fail(TMAC_ERR_SHAPE, "negative size");
     DeviceGuard dg(device);
+    int16_t* xq;
+    float* xs;
+    if (max_batch > 0 && max_cols > 0 && (rc = workspace(device, (size_t)(max_batch * max_cols), (size_t)max_batch, &xq, &xs)))
+        return rc;
     if (!device_error_word(device)) return fail(TMAC_ERR_CUDA, "cannot resolve device error word");
     num_sms(device);
     return TMAC_OK;
