@@ -170,6 +170,21 @@ int tmac_gemv_xq(tmac_weight_t w, const int16_t* xq, const float* xs, float* y, 
  * must be ordered on one stream. */
 int tmac_reserve(int device, int64_t max_batch, int64_t max_cols);
 
+/* NATIVE Q5_0 / Q4_K / Q6_K GEMV that allocates nothing.  No counterpart in
+ * the reference (its drivers are host code with no device memory to manage);
+ * it is for callers that may not allocate device memory, e.g. code running
+ * inside a caller-owned memory pool or a real-time loop that forbids
+ * cudaMalloc.  x is quantised into a fixed module-scope scratch of
+ * TMAC_STATIC_MAX_VALUES int16 values and TMAC_STATIC_MAX_BATCH scales per
+ * device; batch x cols above that fails with TMAC_ERR_SHAPE (use tmac_gemv).
+ * Results equal tmac_gemv bit for bit.  The scratch address is resolved on a
+ * device's first call, so make that first call before any stream capture.
+ * All calls on one device share the scratch: calls that overlap (different
+ * streams or threads without ordering) race and give wrong results. */
+#define TMAC_STATIC_MAX_VALUES 131072 /* 256 KiB of int16 x_q */
+#define TMAC_STATIC_MAX_BATCH 64
+int tmac_gemv_static(tmac_weight_t w, const float* x, float* y, int batch, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Phase-B descriptor chain (sim/fpga_sim.hpp:1254-1310, sim/tmac_gguf.cpp:513-880).
  *

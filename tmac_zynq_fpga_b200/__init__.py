@@ -82,6 +82,7 @@ def lib():
             "tmac_gemv_q6_k": (ctypes.c_int, [_P, _P, _P, ctypes.c_int, _P]),
             "tmac_gemv_int16": (ctypes.c_int, [_P, _P, _P, ctypes.c_int, _P]),
             "tmac_gemv_host": (ctypes.c_int, [_P, _P, _P, ctypes.c_int]),
+            "tmac_gemv_static": (ctypes.c_int, [_P, _P, _P, ctypes.c_int, _P]),
             "tmac_reserve": (ctypes.c_int, [ctypes.c_int, _I64, _I64]),
             "tmac_top1": (ctypes.c_int, [_P, _I64, _I64, _P, _P]),
             "tmac_gemv_top1": (ctypes.c_int, [_P, _P, _P, _P, _I64, ctypes.c_int, _P]),

@@ -183,6 +183,39 @@ int workspace(int device, size_t nxq, size_t nxs, int16_t** xq, float** xs)
     return TMAC_OK;
 }
 
+// Fixed scratch of tmac_gemv_static: x_q and x_scale in module memory, so that
+// entry point never allocates.  Its address is resolved once per device (with
+// that device current) and cached.  Every element the GEMV reads is written by
+// the quantise kernel first, so nothing here has to start at zero.
+constexpr int64_t kStaticXq = TMAC_STATIC_MAX_VALUES;
+constexpr int kStaticXs = TMAC_STATIC_MAX_BATCH;
+__device__ __align__(256) int16_t g_static_xq[kStaticXq];
+__device__ __align__(256) float g_static_xs[kStaticXs];
+std::vector<int16_t*> g_static_xq_ptr;
+std::vector<float*> g_static_xs_ptr;
+
+int static_scratch(int device, int16_t** xq, float** xs)
+{
+    std::lock_guard<std::mutex> lk(g_dev_mutex);
+    if ((int)g_static_xq_ptr.size() <= device) {
+        g_static_xq_ptr.resize(device + 1, nullptr);
+        g_static_xs_ptr.resize(device + 1, nullptr);
+    }
+    if (!g_static_xq_ptr[device]) {
+        void* a = nullptr;
+        void* b = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&a, g_static_xq);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_static_xq)");
+        e = cudaGetSymbolAddress(&b, g_static_xs);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_static_xs)");
+        g_static_xq_ptr[device] = static_cast<int16_t*>(a);
+        g_static_xs_ptr[device] = static_cast<float*>(b);
+    }
+    *xq = g_static_xq_ptr[device];
+    *xs = g_static_xs_ptr[device];
+    return TMAC_OK;
+}
+
 void free_weight(tmac_weight_s* w)
 {
     if (!w) return;
@@ -388,6 +421,30 @@ int tmac_gemv_acc(tmac_weight_t w, const float* x, float* y, int64_t* row_acc, i
 int tmac_gemv(tmac_weight_t w, const float* x, float* y, int batch, void* stream)
 {
     return tmac_gemv_acc(w, x, y, nullptr, nullptr, batch, stream);
+}
+
+int tmac_gemv_static(tmac_weight_t w, const float* x, float* y, int batch, void* stream)
+{
+    int rc = weight_ok(w);
+    if (rc) return rc;
+    if (!x || !y) return fail(TMAC_ERR_INVALID, "NULL x or y");
+    if (batch <= 0) return fail(TMAC_ERR_SHAPE, "batch must be positive");
+    if (w->mode != TMAC_MODE_NATIVE || w->type == TMAC_TYPE_Q8_0)
+        return fail(TMAC_ERR_TYPE, "tmac_gemv_static: only NATIVE Q5_0 / Q4_K / Q6_K weights use scratch");
+    if (w->cols % 8) return fail(TMAC_ERR_SHAPE, "tmac_gemv_static: cols must be a multiple of 8");
+    if (batch > kStaticXs || (int64_t)batch * w->cols > kStaticXq)
+        return fail(TMAC_ERR_SHAPE, "tmac_gemv_static: batch x cols = " + std::to_string((int64_t)batch * w->cols) +
+                                        " (batch " + std::to_string(batch) + ") exceeds the fixed scratch of " +
+                                        std::to_string(kStaticXq) + " values / " + std::to_string(kStaticXs) +
+                                        " vectors; use tmac_gemv");
+    DeviceGuard dg(w->device);
+    if (!dg.ok) return fail(TMAC_ERR_CUDA, "cudaSetDevice failed");
+    int16_t* xq = nullptr;
+    float* xs = nullptr;
+    if ((rc = static_scratch(w->device, &xq, &xs))) return rc;
+    cudaStream_t s = (cudaStream_t)stream;
+    if ((rc = launch_quantize(x, w->cols, batch, xq, xs, s))) return rc;
+    return launch_blockq(w, nullptr, xq, xs, y, nullptr, nullptr, batch, s);
 }
 
 static int gemv_typed(tmac_weight_t w, int type, int mode, const float* x, float* y, int batch, void* stream,
