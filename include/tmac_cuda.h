@@ -164,10 +164,10 @@ int tmac_gemv_xq(tmac_weight_t w, const int16_t* xq, const float* xs, float* y, 
 
 /* Allocate the per-device workspace for GEMVs up to batch x cols now, so that
  * later calls allocate nothing (required before CUDA-graph capture).
- * tmac_gemv on a NATIVE Q5_0 / Q4_K / Q6_K weight quantises x once into this
- * workspace (x_q int16 [batch][cols], x_scale [batch]) and grows it with
- * cudaMalloc when a call needs more; calls on one device share it, so they
- * must be ordered on one stream. */
+ * tmac_gemv on a NATIVE Q5_0 / Q4_K / Q6_K weight with batch > 2 quantises x
+ * once into this workspace (x_q as byte planes, x_scale [batch]) and grows it
+ * with cudaMalloc when a call needs more; calls on one device share it, so they
+ * must be ordered on one stream.  Batch 1-2 quantises inside the GEMV. */
 int tmac_reserve(int device, int64_t max_batch, int64_t max_cols);
 
 /* NATIVE Q5_0 / Q4_K / Q6_K GEMV that allocates nothing.  No counterpart in

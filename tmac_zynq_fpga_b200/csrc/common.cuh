@@ -125,6 +125,11 @@ TMAC_DEV void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes)
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
                  : "memory");
 }
+// Adds to the transaction count of the current phase without arriving.
+TMAC_DEV void mbar_expect_tx(uint64_t* bar, uint32_t bytes)
+{
+    asm volatile("mbarrier.expect_tx.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes) : "memory");
+}
 TMAC_DEV void mbar_arrive(uint64_t* bar)
 {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
@@ -219,6 +224,9 @@ struct tmac_weight_s {
     int64_t groups = 0;          // row groups (interleaved layouts)
     int64_t group_bytes = 0;     // bytes per row group
     int tiles = 0;               // 64-column tiles per row (Q8_0 / INT16)
+    int* exc_ptr = nullptr;      // NATIVE Q5_0/K-quants: per-row exception offsets [rows + 1]
+    void* exc = nullptr;         // int4 (row, col, v - v', 0) entries
+    int64_t n_exc = 0;
 };
 
 namespace tmac {
@@ -227,11 +235,14 @@ int register_q8_0(tmac_weight_s* w, const uint8_t* d_raw, const float* d_row_max
 int launch_q8_0(const tmac_weight_s* w, const float* x, float* y, int64_t* row_acc, int64_t* unit_acc,
                 int batch, cudaStream_t s, unsigned long long* top1 = nullptr, int64_t index_base = 0,
                 const int16_t* xq = nullptr, const float* xs = nullptr);
-int launch_quantize(const float* x, int64_t cols, int batch, int16_t* xq, float* xs, cudaStream_t s);
+int launch_quantize(const float* x, int64_t cols, int batch, int16_t* xq, float* xs, cudaStream_t s,
+                    uint8_t* xp = nullptr);
 int launch_top1(const float* y, int64_t n, int64_t index_base, unsigned long long* key, cudaStream_t s);
 int register_blockq(tmac_weight_s* w, const uint8_t* d_raw, cudaStream_t s);
-int launch_blockq(const tmac_weight_s* w, const float* x, const int16_t* xq, const float* xs, float* y,
-                  int64_t* row_acc, int64_t* unit_acc, int batch, cudaStream_t s);
+// Activations: fp32 x, or int16 xq, or byte planes xp ([batch][2][cols]: high
+// bytes, low bytes) with their x_scale xs.
+int launch_blockq(const tmac_weight_s* w, const float* x, const int16_t* xq, const uint8_t* xp, const float* xs,
+                  float* y, int64_t* row_acc, int64_t* unit_acc, int batch, cudaStream_t s);
 int register_int16(tmac_weight_s* w, const uint8_t* d_raw, cudaStream_t s);
 int launch_int16(const tmac_weight_s* w, const float* x, float* y, int64_t* row_acc, int64_t* unit_acc,
                  int batch, cudaStream_t s);

@@ -85,6 +85,17 @@ __global__ void step_done_kernel(const float* __restrict__ hidden, float* __rest
     }
 }
 
+// x_q value i of an n-vector as int16 (Q8_0 kernels) and as byte planes
+// (block-quant kernels).
+TMAC_DEV void store_xq(int16_t* xq, uint8_t* xp, int n, int i, int16_t q)
+{
+    xq[i] = q;
+    if (xp) {
+        xp[i] = (uint8_t)((uint16_t)q >> 8);
+        xp[n + i] = (uint8_t)(q & 0xFF);
+    }
+}
+
 // rms_norm (:447-454): one CTA; the sum of squares is sequential, as in the
 // reference (x staged in shared memory first).  With xq != nullptr the kernel
 // also quantises its output for the matmuls that read it (:889-896).
@@ -93,7 +104,8 @@ __global__ void step_done_kernel(const float* __restrict__ hidden, float* __rest
 // output_norm tensor, :1831-1838).
 __global__ void __launch_bounds__(256) rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ delta,
                                                       const float* __restrict__ w, float* __restrict__ o,
-                                                      int16_t* __restrict__ xq, float* __restrict__ xs, int n)
+                                                      int16_t* __restrict__ xq, uint8_t* __restrict__ xp,
+                                                      float* __restrict__ xs, int n)
 {
     pdl_launch();
     pdl_wait();
@@ -141,7 +153,7 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(float* __restrict__ x, con
     mx = block_max(mx, red, blockDim.x);
     const float s = x_scale_from_max(mx);
     if (threadIdx.x == 0) *xs = s;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) xq[i] = quantize_one(xsh[i], s);
+    for (int i = threadIdx.x; i < n; i += blockDim.x) store_xq(xq, xp, n, i, quantize_one(xsh[i], s));
 }
 
 // One CTA per query head: q/k/v bias add (:1591-1614), RoPE on the head's q
@@ -212,7 +224,8 @@ __global__ void __launch_bounds__(256) rope_attention_kernel(
 // silu(gate) * up (:459-461, :1697-1700), then the quantisation ffn_down's
 // matmul starts with: one CTA.
 __global__ void __launch_bounds__(1024) silu_mul_kernel(float* __restrict__ g, const float* __restrict__ u, int n,
-                                                        int16_t* __restrict__ xq, float* __restrict__ xs)
+                                                        int16_t* __restrict__ xq, uint8_t* __restrict__ xp,
+                                                        float* __restrict__ xs)
 {
     pdl_launch();
     pdl_wait();
@@ -228,7 +241,7 @@ __global__ void __launch_bounds__(1024) silu_mul_kernel(float* __restrict__ g, c
     mx = block_max(mx, red, blockDim.x);
     const float s = x_scale_from_max(mx);
     if (threadIdx.x == 0) *xs = s;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) xq[i] = quantize_one(g[i], s);
+    for (int i = threadIdx.x; i < n; i += blockDim.x) store_xq(xq, xp, n, i, quantize_one(g[i], s));
 }
 
 // ----------------------------------------------------------------- the model
@@ -255,6 +268,7 @@ struct tmac_model_s {
     unsigned long long* key = nullptr;
     int* token_log = nullptr;
     int16_t* xq = nullptr;  // quantised activations shared by several matmuls
+    uint8_t* xp = nullptr;  // the same x_q as byte planes (block-quant GEMVs)
     float* xs = nullptr;
     // graph-driven generation: position, token and hidden-state logs on the device
     int* pos_dev = nullptr;
@@ -300,7 +314,12 @@ int gemv(tmac_model_s* m, const std::string& name, const float* x, float* y, cud
 {
     auto it = m->mats.find(name);
     if (it == m->mats.end()) return fail(TMAC_ERR_INVALID, "missing matrix " + name);
-    if (have_xq && it->second->mode == TMAC_MODE_NATIVE) return tmac_gemv_xq(it->second, m->xq, m->xs, y, 1, s);
+    const tmac_weight_s* w = it->second;
+    if (have_xq && w->mode == TMAC_MODE_NATIVE) {
+        if (w->type == TMAC_TYPE_Q8_0)
+            return launch_q8_0(w, nullptr, y, nullptr, nullptr, 1, s, nullptr, 0, m->xq, m->xs);
+        return launch_blockq(w, nullptr, nullptr, m->xp, m->xs, y, nullptr, nullptr, 1, s);
+    }
     return tmac_gemv(it->second, x, y, 1, s);
 }
 
@@ -339,13 +358,13 @@ int layer(tmac_model_s* m, int l, int pos, cudaStream_t s, const int* pos_dev = 
                            (const float*)m->rope_c, (const float*)m->rope_s, pos, pos_dev, kc, vc, m->ctx));
     if ((rc = gemv(m, lname(l, "attn_output.weight"), m->ctx, m->attn, s))) return rc;
     TMAC_CUDA_TRY(launch_k(rmsnorm_kernel, dim3(1), dim3(256), 0, s, m->hidden, (const float*)m->attn, fn, m->xn,
-                           m->xq, m->xs, kHidden));
+                           m->xq, m->xp, m->xs, kHidden));
     if ((rc = gemv(m, lname(l, "ffn_gate_up"), m->xn, m->gate, s, true))) return rc;
     TMAC_CUDA_TRY(launch_k(silu_mul_kernel, dim3(1), dim3(1024), 0, s, m->gate, (const float*)m->up, kInter, m->xq,
-                           m->xs));
+                           m->xp, m->xs));
     if ((rc = gemv(m, lname(l, "ffn_down.weight"), m->gate, m->ffn, s, true))) return rc;
     TMAC_CUDA_TRY(launch_k(rmsnorm_kernel, dim3(1), dim3(256), 0, s, m->hidden, (const float*)m->ffn, next_norm(m, l),
-                           m->xn, m->xq, m->xs, kHidden));
+                           m->xn, m->xq, m->xp, m->xs, kHidden));
     TMAC_CUDA_TRY(cudaGetLastError());
     return TMAC_OK;
 }
@@ -360,7 +379,7 @@ int forward_all(tmac_model_s* m, int token, const unsigned long long* key, int p
     const float* an = vec_or_null(m, lname(0, "attn_norm.weight"));
     if (!an) return fail(TMAC_ERR_INVALID, "missing attn_norm weights");
     TMAC_CUDA_TRY(launch_k(rmsnorm_kernel, dim3(1), dim3(256), 0, s, m->hidden, (const float*)nullptr, an, m->xn, m->xq,
-                           m->xs, kHidden));
+                           m->xp, m->xs, kHidden));
     for (int l = 0; l < kLayers; l++)
         if ((rc = layer(m, l, pos, s, pos_dev))) return rc;
     return TMAC_OK;
@@ -514,6 +533,7 @@ int tmac_model_finalize(tmac_model_t m)
         (rc = dev_alloc(m, &m->logits, kVocab)) || (rc = dev_alloc(m, &m->kcache, kv)) ||
         (rc = dev_alloc(m, &m->vcache, kv)) || (rc = dev_alloc(m, &m->key, 1)) ||
         (rc = dev_alloc(m, &m->token_log, 1)) || (rc = dev_alloc(m, &m->xq, kInter)) ||
+        (rc = dev_alloc(m, &m->xp, 2 * kInter)) ||
         (rc = dev_alloc(m, &m->xs, 1)) || (rc = dev_alloc(m, &m->pos_dev, 1)) ||
         (rc = dev_alloc(m, &m->tokens, (size_t)m->max_seq)) ||
         (rc = dev_alloc(m, &m->hidden_log, (size_t)m->max_seq * kHidden)))

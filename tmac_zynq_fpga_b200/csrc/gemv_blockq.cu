@@ -8,23 +8,43 @@
 //
 // Per row r: row_inv[r] = 32767 / max|w| (weight-only, computed once at
 // registration), every weight becomes
-//   v = clamp_round_i16(w_f32 * row_inv)      with w_f32 in the reference's order:
+//   v = roundf(w_f32 * row_inv)      with w_f32 in the reference's fp32 order:
 //       Q5_0: d*q     Q4_K: (d*sc)*q4 - dmin*m     Q6_K: (d*sc)*q6
 // the int64 row sum is  acc = sum v * x_q  and  y = (float)((double)acc * x_scale / (double)row_inv).
-// The integer sum is order-free, so the work is split freely: one warp per row,
-// each lane decoding one 32-value chunk (a Q5_0 block, a Q4_K sub-block, a Q6_K
-// 32-value run) per iteration, row sums by warp shuffle.
+//
+// Fast decode + exception list.  The GEMV computes every weight with packed
+// fp32x2 arithmetic as v' (two values per instruction):
+//   Q5_0, Q6_K: v' = RNE(q * c), c = RN(scale * row_inv) per 16/32 values
+//   Q4_K:       v' = RNE((RN(q*A - B)) * row_inv)       (the first product is exact)
+// v' equals v except where the value sits within an ulp of a half-integer (the
+// reference rounds half away from zero; its product is rounded once more).  At
+// registration every (row, col) with v != v' is found by running both decodes
+// on the device layout, and stored per row as (col, v - v'); the GEMV adds
+// sum (v - v') * x_q[col] for the row, so the int64 row sum is the reference's
+// exactly.  Measured: well under one exception per 1000 weights.
+//
+// Device layout (row groups of 8 rows, every section 16-byte aligned, so that a
+// CTA's share of groups is one contiguous bulk copy into shared memory):
+//   Q5_0 group:  qs[8*cpr][16] | qh[8*cpr] u32 | d[8*cpr] f16   block k = j*8 + r
+//   Q4_K group:  the 144-byte GGUF blocks, k = r*nsb + sb
+//   Q6_K group:  ql[8*nsb][128] | qh[8*nsb][64] | sc[8*nsb][16] | d[8*nsb] f16, k = r*nsb + sb
+// Same bytes per weight as GGUF (22 / 144 / 210 per block); rows padded to 8.
+//
+// Kernel: each CTA bulk-copies its groups into shared memory BEFORE waiting on
+// the preceding kernel (programmatic dependent launch), so in a chain of GEMVs
+// the weight stream of one overlaps the tail of the one before.  Then it
+// stages x_q as two byte planes (x_q = 256*xh + xl) and decodes from shared
+// memory: Q5_0 with 4 lanes per row (8 rows = one group per warp), K-quants
+// one warp per row (lane = 4 super-block phases x 8 sub-blocks).
 #include "common.cuh"
 #include "dequant.cuh"
 
 #include <algorithm>
+#include <vector>
 
 namespace tmac {
 namespace {
 
-constexpr int kThreads = 256;
-
-TMAC_DEV uint16_t ldg16(const uint8_t* p) { return __ldg(reinterpret_cast<const uint16_t*>(p)); }
 
 // ------------------------------------------------------------ row_inv pass --
 template <int TYPE>
@@ -43,315 +63,700 @@ __global__ void row_inv_kernel(const uint8_t* __restrict__ raw, int64_t rows, in
     if (lane == 0) ri[r] = __fdiv_rn(32767.0f, (mx < 1e-10f) ? 1.0f : mx);
 }
 
-// --------------------------------------------------- chunk decode (32 values)
-// roundf(t) of the reference (round half away from zero) as an int16 in the
-// low 16 bits, exact for every finite |t| < 2^22 without a float->int
-// conversion instruction:
-//   floor(RD(|t| + 0.5)) == floor(|t| + 0.5)   (integers are representable, so
-//                                               rounding down never crosses one)
+// ------------------------------------------------------------------ layout --
+template <int TYPE>
+struct Geo;
+template <>
+struct Geo<TMAC_TYPE_Q5_0> {
+    static constexpr int kBlockBytes = 22, kBlockVals = 32;
+    __host__ __device__ static int64_t group_bytes(int64_t nblk) { return 176 * nblk; }
+};
+template <>
+struct Geo<TMAC_TYPE_Q4_K> {
+    static constexpr int kBlockBytes = 144, kBlockVals = 256;
+    __host__ __device__ static int64_t group_bytes(int64_t nblk) { return 1152 * nblk; }
+};
+template <>
+struct Geo<TMAC_TYPE_Q6_K> {
+    static constexpr int kBlockBytes = 210, kBlockVals = 256;
+    __host__ __device__ static int64_t group_bytes(int64_t nblk) { return 1680 * nblk; }
+};
+
+// One thread per GGUF block: copies it into the grouped layout.
+template <int TYPE>
+__global__ void relayout_kernel(const uint8_t* __restrict__ raw, int64_t rows, int64_t nblk, uint8_t* __restrict__ out)
+{
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= rows * nblk) return;
+    const int64_t row = i / nblk, j = i % nblk, g = row >> 3;
+    const int r = (int)(row & 7);
+    const uint8_t* b = raw + i * Geo<TYPE>::kBlockBytes;
+    uint8_t* G = out + g * Geo<TYPE>::group_bytes(nblk);
+    if (TYPE == TMAC_TYPE_Q5_0) {
+        const int64_t k = j * 8 + r;
+        for (int t = 0; t < 16; t++) G[16 * k + t] = b[6 + t];
+        for (int t = 0; t < 4; t++) G[128 * nblk + 4 * k + t] = b[2 + t];
+        for (int t = 0; t < 2; t++) G[160 * nblk + 2 * k + t] = b[t];
+    } else if (TYPE == TMAC_TYPE_Q4_K) {
+        const int64_t k = r * nblk + j;
+        for (int t = 0; t < 144; t++) G[144 * k + t] = b[t];
+    } else {
+        const int64_t k = r * nblk + j;
+        for (int t = 0; t < 128; t++) G[128 * k + t] = b[t];
+        for (int t = 0; t < 64; t++) G[1024 * nblk + 64 * k + t] = b[128 + t];
+        for (int t = 0; t < 16; t++) G[1536 * nblk + 16 * k + t] = b[192 + t];
+        for (int t = 0; t < 2; t++) G[1664 * nblk + 2 * k + t] = b[208 + t];
+    }
+}
+
+// ------------------------------------------------------- chunk field loads --
+// A chunk is 32 consecutive values of a row.  Its raw codes go into R[8]:
+// byte k of R[i] is the unsigned code of value 4i+k (Q5_0: q+16, Q4_K: q,
+// Q6_K: q+32), together with the chunk's fp32 scale factors.
+struct Chunk {
+    uint32_t R[8];
+    float s0, s1;  // Q5_0: d, d   Q4_K: A = d*sc, B = dmin*m   Q6_K: A0, A1 (values 0-15, 16-31)
+};
+
+// Byte loads of a row group, through generic pointers (registration kernels,
+// global memory) or 32-bit shared-memory addresses (the GEMV).
+struct GlobalBytes {
+    const uint8_t* p;
+    TMAC_DEV uint4 ld128(uint32_t off) const { return *reinterpret_cast<const uint4*>(p + off); }
+    TMAC_DEV uint32_t ld32(uint32_t off) const { return *reinterpret_cast<const uint32_t*>(p + off); }
+    TMAC_DEV uint32_t ld16(uint32_t off) const { return *reinterpret_cast<const uint16_t*>(p + off); }
+};
+struct SharedBytes {
+    uint32_t a;
+    TMAC_DEV uint4 ld128(uint32_t off) const
+    {
+        uint4 v;
+        asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                     : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                     : "r"(a + off));
+        return v;
+    }
+    TMAC_DEV uint32_t ld32(uint32_t off) const
+    {
+        uint32_t v;
+        asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a + off));
+        return v;
+    }
+    TMAC_DEV uint32_t ld16(uint32_t off) const
+    {
+        uint16_t v;
+        asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a + off));
+        return v;
+    }
+};
+
+// Q5_0 block k of group G (cpr blocks per row).
+template <class M>
+TMAC_DEV void load_q5_0(const M& G, uint32_t cpr, uint32_t k, Chunk& c)
+{
+    const uint4 qs = G.ld128(16 * k);
+    const uint32_t qh = G.ld32(128 * cpr + 4 * k);
+    c.s0 = c.s1 = f16_bits_to_f32((uint16_t)G.ld16(160 * cpr + 2 * k));
+    const uint32_t w[4] = {qs.x, qs.y, qs.z, qs.w};
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        // bit e of qh is the fifth bit of value e: spread 4 bits to bit 4 of 4 bytes
+        const uint32_t lo = ((qh >> (4 * i)) & 0xFu) * 0x02040810u;
+        const uint32_t hi = ((qh >> (16 + 4 * i)) & 0xFu) * 0x02040810u;
+        c.R[i] = (lo & 0x10101010u) | (w[i] & 0x0F0F0F0Fu);
+        c.R[4 + i] = (hi & 0x10101010u) | ((w[i] >> 4) & 0x0F0F0F0Fu);
+    }
+}
+
+// Q4_K sub-block `sub` (0..7) of the 144-byte block at offset b.
+template <class M>
+TMAC_DEV void load_q4_k(const M& G, uint32_t b, int sub, Chunk& c)
+{
+    const uint4 hdr = G.ld128(b);
+    const uint8_t* hb = reinterpret_cast<const uint8_t*>(&hdr);
+    const float d = f16_bits_to_f32((uint16_t)(hdr.x & 0xFFFF));
+    const float dmin = f16_bits_to_f32((uint16_t)(hdr.x >> 16));
+    int sc, m;
+    q4_k_scale_min(hb + 4, sub, sc, m);
+    c.s0 = __fmul_rn(d, (float)sc);
+    c.s1 = __fmul_rn(dmin, (float)m);
+    const uint32_t qo = b + 16 + (sub >> 1) * 32;
+    const uint4 q0 = G.ld128(qo), q1 = G.ld128(qo + 16);
+    const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+    const int shift = (sub & 1) * 4;
+#pragma unroll
+    for (int i = 0; i < 8; i++) c.R[i] = (qw[i] >> shift) & 0x0F0F0F0Fu;
+}
+
+// Q6_K sub-block `sub` (0..7) of block k of group G (nsb blocks per row).
+template <class M>
+TMAC_DEV void load_q6_k(const M& G, uint32_t nsb, uint32_t k, int sub, Chunk& c)
+{
+    const int half = sub >> 2, s4 = sub & 3;
+    const uint32_t lo = 128 * k + half * 64 + (s4 & 1) * 32, ho = 1024 * nsb + 64 * k + half * 32;
+    const uint32_t scw = G.ld16(1536 * nsb + 16 * k + half * 8 + s4 * 2);
+    const float d = f16_bits_to_f32((uint16_t)G.ld16(1664 * nsb + 2 * k));
+    c.s0 = __fmul_rn(d, (float)(int8_t)(scw & 0xFF));
+    c.s1 = __fmul_rn(d, (float)(int8_t)(scw >> 8));
+    const uint4 l0 = G.ld128(lo), l1 = G.ld128(lo + 16), h0 = G.ld128(ho), h1 = G.ld128(ho + 16);
+    const uint32_t lw[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
+    const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+    const int lshift = (s4 < 2) ? 0 : 4, hshift = 2 * s4;
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+        c.R[i] = ((lw[i] >> lshift) & 0x0F0F0F0Fu) | (((hw[i] >> hshift) << 4) & 0x30303030u);
+}
+
+template <int TYPE>
+__host__ __device__ constexpr int code_bias()
+{
+    return TYPE == TMAC_TYPE_Q5_0 ? 16 : (TYPE == TMAC_TYPE_Q6_K ? 32 : 0);
+}
+
+// ------------------------------------------------------------ exact decode --
+// roundf(t) of the reference (round half away from zero), exact for every
+// finite |t| < 2^22 without a float->int conversion:
+//   floor(RD(|t| + 0.5)) == floor(|t| + 0.5)   (integers are representable)
 //   RD(w + 2^23) = 2^23 + floor(w)             (the ulp there is 1)
-// then the sign of t is applied.  No clamp is needed: every |t| is at most
-// max|w| * (32767 / max|w|) rounded, i.e. below 32767.5.
-TMAC_DEV uint32_t round_i16(float t)
+// then the sign of t.  |t| never exceeds 32767.5: max|w| * (32767/max|w|) rounds
+// to within an ulp of 32767.
+TMAC_DEV int round_ref(float t)
 {
     const float w = __fadd_rd(fabsf(t), 0.5f);
     const int va = __float_as_int(__fadd_rd(w, 8388608.0f)) - 0x4B000000;
-    const int m = __float_as_int(t) >> 31;
-    return (uint32_t)((va ^ m) - m);
+    return (t < 0.0f) ? -va : va;
 }
 
-// float(n) for 0 <= n < 2^23 minus a constant: exact, via the 2^23 exponent.
-TMAC_DEV float small_int_f(uint32_t n, float minus) { return __fsub_rn(__uint_as_float(0x4B000000u | n), minus); }
-
-TMAC_DEV uint32_t pack2(uint32_t lo, uint32_t hi) { return __byte_perm(lo, hi, 0x5410); }
-
-// Decodes chunk `ch` of row `r` into 16 words of int16 pairs (values 2i, 2i+1),
-// each value = roundf(w_f32 * row_inv) with w_f32 in the reference's fp32 order
-// (fpga_sim.hpp:1030-1037, :773-778, :1099-1104).
+// Value e (0..31) of the chunk with the reference's fp32 expression.
 template <int TYPE>
-TMAC_DEV void decode_chunk(const uint8_t* __restrict__ raw, int64_t r, int64_t cpr, int64_t ch, float ri,
-                           uint32_t (&vw)[16])
+TMAC_DEV int exact_value(const Chunk& c, int e, float ri)
 {
-    if (TYPE == TMAC_TYPE_Q5_0) {
-        const uint8_t* b = raw + (r * cpr + ch) * 22;  // 2-byte aligned
-        const float d = f16_bits_to_f32(ldg16(b));
-        const uint32_t qh = (uint32_t)ldg16(b + 2) | ((uint32_t)ldg16(b + 4) << 16);
-        uint32_t qw[4];
+    const int code = (int)((c.R[e >> 2] >> (8 * (e & 3))) & 0xFFu);
+    const float q = (float)(code - code_bias<TYPE>());
+    float w;
+    if (TYPE == TMAC_TYPE_Q5_0) w = __fmul_rn(c.s0, q);                           // fpga_sim.hpp:1030-1037
+    else if (TYPE == TMAC_TYPE_Q4_K) w = __fsub_rn(__fmul_rn(c.s0, q), c.s1);     // :773-778
+    else w = __fmul_rn(e < 16 ? c.s0 : c.s1, q);                                  // :1099-1104
+    return round_ref(__fmul_rn(w, ri));
+}
+
+// ------------------------------------------------------------- fast decode --
+TMAC_DEV uint64_t pk2(float lo, float hi)
+{
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+TMAC_DEV uint64_t pk2u(uint32_t lo, uint32_t hi)
+{
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
+    return r;
+}
+TMAC_DEV uint64_t add2(uint64_t a, uint64_t b)
+{
+    uint64_t r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+TMAC_DEV uint64_t fma2(uint64_t a, uint64_t b, uint64_t c)
+{
+    uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+// The low 16 bits of both halves of a pair of floats in [2^23, 2^24), as one
+// word of two int16 (the integers RNE(.) - 1.5*2^23 in two's complement).
+TMAC_DEV uint32_t lo16x2(uint64_t v)
+{
+    uint32_t lo, hi;
+    asm("mov.b64 {%0, %1}, %2;" : "=r"(lo), "=r"(hi) : "l"(v));
+    return __byte_perm(lo, hi, 0x5410);
+}
+
+constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23: x + kMagic = kMagic + RNE(x) for |x| < 2^22
+
+// Fast values v' of the chunk as 16 words of int16 pairs (values 2i, 2i+1).
+template <int TYPE>
+TMAC_DEV void fast_values(const Chunk& c, float ri, uint32_t (&vw)[16])
+{
+    const uint64_t off = pk2(-(8388608.0f + code_bias<TYPE>()), -(8388608.0f + code_bias<TYPE>()));
+    const uint64_t mag = pk2(kMagic, kMagic);
+    uint64_t m0, m1, a1;
+    if (TYPE == TMAC_TYPE_Q4_K) {
+        m0 = pk2(c.s0, c.s0);
+        a1 = pk2(-c.s1, -c.s1);
+        m1 = pk2(ri, ri);
+    } else {
+        const float c0 = __fmul_rn(c.s0, ri), c1 = __fmul_rn(c.s1, ri);
+        m0 = pk2(c0, c0);
+        m1 = pk2(c1, c1);
+        a1 = 0;
+    }
 #pragma unroll
-        for (int i = 0; i < 4; i++) qw[i] = (uint32_t)ldg16(b + 6 + 4 * i) | ((uint32_t)ldg16(b + 8 + 4 * i) << 16);
-#pragma unroll
-        for (int wi = 0; wi < 32; wi += 2) {
-            uint32_t v2[2];
-#pragma unroll
-            for (int k = 0; k < 2; k++) {
-                const int e = wi + k, j = e & 15;
-                const uint32_t nib = (qw[j >> 2] >> (8 * (j & 3) + (e >= 16 ? 4 : 0))) & 0xFu;
-                const uint32_t raw5 = nib | (((qh >> e) & 1u) << 4);
-                const float q = small_int_f(raw5, 8388624.0f);  // raw5 - 16
-                v2[k] = round_i16(__fmul_rn(__fmul_rn(d, q), ri));
-            }
-            vw[wi / 2] = pack2(v2[0], v2[1]);
+    for (int i = 0; i < 8; i++) {
+        const uint32_t R = c.R[i];
+        // float(2^23 + code) for the four codes, then q = code - bias exactly
+        const uint64_t q01 = add2(pk2u(__byte_perm(R, 0x4B000000u, 0x7540), __byte_perm(R, 0x4B000000u, 0x7541)), off);
+        const uint64_t q23 = add2(pk2u(__byte_perm(R, 0x4B000000u, 0x7542), __byte_perm(R, 0x4B000000u, 0x7543)), off);
+        uint64_t u01, u23;
+        if (TYPE == TMAC_TYPE_Q4_K) {
+            u01 = fma2(fma2(q01, m0, a1), m1, mag);
+            u23 = fma2(fma2(q23, m0, a1), m1, mag);
+        } else {
+            const uint64_t cc = (i < 4) ? m0 : m1;
+            u01 = fma2(q01, cc, mag);
+            u23 = fma2(q23, cc, mag);
         }
-    } else if (TYPE == TMAC_TYPE_Q4_K) {
-        const int64_t sb = ch >> 3;
-        const int sub = (int)(ch & 7);
-        const uint8_t* b = raw + (r * (cpr >> 3) + sb) * 144;  // 16-byte aligned
-        const uint4 hdr = __ldg(reinterpret_cast<const uint4*>(b));
-        const uint8_t* hb = reinterpret_cast<const uint8_t*>(&hdr);
-        const float d = f16_bits_to_f32((uint16_t)(hb[0] | (hb[1] << 8)));
-        const float dmin = f16_bits_to_f32((uint16_t)(hb[2] | (hb[3] << 8)));
-        int sc, m;
-        q4_k_scale_min(hb + 4, sub, sc, m);
-        const float A = __fmul_rn(d, (float)sc), B = __fmul_rn(dmin, (float)m);
-        const uint4* qp = reinterpret_cast<const uint4*>(b + 16 + (sub >> 1) * 32);
-        const uint4 q0 = __ldg(qp), q1 = __ldg(qp + 1);
-        const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-        const int shift = (sub & 1) * 4;
-#pragma unroll
-        for (int j = 0; j < 32; j += 2) {
-            uint32_t v2[2];
-#pragma unroll
-            for (int k = 0; k < 2; k++) {
-                const int e = j + k;
-                const uint32_t q4 = (qw[e >> 2] >> (8 * (e & 3) + shift)) & 0xFu;
-                const float q = small_int_f(q4, 8388608.0f);
-                v2[k] = round_i16(__fmul_rn(__fsub_rn(__fmul_rn(A, q), B), ri));
-            }
-            vw[j / 2] = pack2(v2[0], v2[1]);
-        }
-    } else {  // Q6_K
-        const int64_t sb = ch >> 3;
-        const int within = (int)(ch & 7), half = within >> 2, sub = within & 3;
-        const uint8_t* b = raw + (r * (cpr >> 3) + sb) * 210;  // 2-byte aligned
-        const float d = f16_bits_to_f32(ldg16(b + 208));
-        const uint16_t scw = ldg16(b + 192 + half * 8 + sub * 2);
-        const float A0 = __fmul_rn(d, (float)(int8_t)(scw & 0xFF));
-        const float A1 = __fmul_rn(d, (float)(int8_t)(scw >> 8));
-        const uint8_t* ql = b + half * 64 + (sub & 1) * 32;
-        const uint8_t* qhp = b + 128 + half * 32;
-        const int lshift = (sub < 2) ? 0 : 4, hshift = sub * 2;
-        uint32_t lw[8], hw[8];
-#pragma unroll
-        for (int i = 0; i < 8; i++) {
-            lw[i] = (uint32_t)ldg16(ql + 4 * i) | ((uint32_t)ldg16(ql + 4 * i + 2) << 16);
-            hw[i] = (uint32_t)ldg16(qhp + 4 * i) | ((uint32_t)ldg16(qhp + 4 * i + 2) << 16);
-        }
-#pragma unroll
-        for (int l = 0; l < 32; l += 2) {
-            uint32_t v2[2];
-#pragma unroll
-            for (int k = 0; k < 2; k++) {
-                const int e = l + k, bs = 8 * (e & 3);
-                const uint32_t lo = (lw[e >> 2] >> (bs + lshift)) & 0xFu;
-                const uint32_t hi = (hw[e >> 2] >> (bs + hshift)) & 0x3u;
-                const float q = small_int_f((hi << 4) | lo, 8388640.0f);  // q6 = raw6 - 32
-                v2[k] = round_i16(__fmul_rn(__fmul_rn(e < 16 ? A0 : A1, q), ri));
-            }
-            vw[l / 2] = pack2(v2[0], v2[1]);
-        }
+        vw[2 * i] = lo16x2(u01);
+        vw[2 * i + 1] = lo16x2(u23);
     }
 }
 
 // Exact sum of 32 int16 weights (16 packed words) times the chunk's activations
 // given as signed high bytes xh and unsigned low bytes xl (x_q = 256*xh + xl):
 // dp2a products fit int32 for a chunk (|sum| < 2^28).
-TMAC_DEV long long chunk_dot(const uint32_t (&vw)[16], const uint32_t* xh, const uint32_t* xl)
+TMAC_DEV long long chunk_dot(const uint32_t (&vw)[16], const uint8_t* xh, const uint8_t* xl)
 {
     int sh = 0, sl = 0;
 #pragma unroll
-    for (int i = 0; i < 8; i++) {
-        const uint32_t h = xh[i], l = xl[i];
-        asm("dp2a.lo.s32.s32 %0, %1, %2, %0;" : "+r"(sh) : "r"(vw[2 * i]), "r"(h));
-        asm("dp2a.hi.s32.s32 %0, %1, %2, %0;" : "+r"(sh) : "r"(vw[2 * i + 1]), "r"(h));
-        asm("dp2a.lo.s32.u32 %0, %1, %2, %0;" : "+r"(sl) : "r"(vw[2 * i]), "r"(l));
-        asm("dp2a.hi.s32.u32 %0, %1, %2, %0;" : "+r"(sl) : "r"(vw[2 * i + 1]), "r"(l));
+    for (int q = 0; q < 2; q++) {
+        const uint4 H = reinterpret_cast<const uint4*>(xh)[q];
+        const uint4 L = reinterpret_cast<const uint4*>(xl)[q];
+        const uint32_t h[4] = {H.x, H.y, H.z, H.w}, l[4] = {L.x, L.y, L.z, L.w};
+#pragma unroll
+        for (int t = 0; t < 4; t++) {
+            const int i = 4 * q + t;
+            asm("dp2a.lo.s32.s32 %0, %1, %2, %0;" : "+r"(sh) : "r"(vw[2 * i]), "r"(h[t]));
+            asm("dp2a.hi.s32.s32 %0, %1, %2, %0;" : "+r"(sh) : "r"(vw[2 * i + 1]), "r"(h[t]));
+            asm("dp2a.lo.s32.u32 %0, %1, %2, %0;" : "+r"(sl) : "r"(vw[2 * i]), "r"(l[t]));
+            asm("dp2a.hi.s32.u32 %0, %1, %2, %0;" : "+r"(sl) : "r"(vw[2 * i + 1]), "r"(l[t]));
+        }
     }
     return (long long)sh * 256 + (long long)sl;
 }
 
-struct BlockqArgs {
-    const uint8_t* raw;
-    const float* row_inv;
-    int64_t rows, cols;
-    const float* x;        // [nb][cols] fp32 activations, or
-    const int16_t* xq_in;  // [nb][cols] already-quantised activations with
-    const float* xs_in;    // [nb] their x_scale (tmac_quantize_x)
-    float* y;              // [nb][rows]
-    int64_t* row_acc;
-    int64_t* unit_acc;
-    int nb;                // activation vectors handled by this launch (<= NB)
-};
-
-TMAC_DEV long long warp_sum_ll(long long v)
+// Loads chunk `ch` (0..cpr-1) of row r (0..7) of a group.
+template <int TYPE, class M>
+TMAC_DEV void load_chunk(const M& G, int r, uint32_t nblk, uint32_t ch, Chunk& c)
 {
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    return v;
+    if (TYPE == TMAC_TYPE_Q5_0) load_q5_0(G, nblk, ch * 8 + r, c);
+    else if (TYPE == TMAC_TYPE_Q4_K) load_q4_k(G, 144 * (r * nblk + (ch >> 3)), (int)(ch & 7), c);
+    else load_q6_k(G, nblk, r * nblk + (ch >> 3), (int)(ch & 7), c);
 }
 
-// A CTA works on rows in groups of `rpc` rows, `wpr` warps per row; thread t of
-// a row decodes chunk t (then t + 32*wpr, ...) and reuses the decoded values for
-// every activation vector of the launch.  Row sums: warp shuffle, then the
-// row's warps combine through shared memory.
-template <int TYPE, int NB>
-__global__ void __launch_bounds__(kThreads) blockq_gemv_kernel(BlockqArgs a, int wpr, int rpc)
+// ------------------------------------------------------ exception finding --
+// Warp per row.  mode 0: count the values with v != v' into cnt[row];
+// mode 1: write (row, col, v - v', 0) at cursor[row]++.
+template <int TYPE>
+__global__ void exceptions_kernel(const uint8_t* __restrict__ data, const float* __restrict__ row_inv, int64_t rows,
+                                  int64_t cols, int* __restrict__ cnt, int* __restrict__ cursor, int4* __restrict__ exc)
 {
-    extern __shared__ __align__(16) uint8_t smem[];
-    const int64_t cols = a.cols, cpr = cols / 32;
-    const int nb = a.nb;
-    // activations as byte planes: x_q = 256 * xh (signed) + xl (unsigned)
-    uint8_t* xh = smem;                                                                // [nb][cols]
-    uint8_t* xl = smem + (size_t)nb * cols;                                            // [nb][cols]
-    float* xs = reinterpret_cast<float*>(smem + ((size_t)nb * cols * 2 + 15) / 16 * 16);  // [16]
-    float* red = xs + 16;                                                              // [8]
-    long long* part_s = reinterpret_cast<long long*>(red + 8);                        // [8 warps][NB]
-    pdl_launch();
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int rw = warp % wpr, rr = warp / wpr;  // warp within the row, row within the group
-    const int tpr = wpr * 32;
-    // The weights do not depend on the preceding kernel: fetch and decode this
-    // thread's first chunk before waiting for the activations.
-    uint32_t v0[16];
-    bool have_v0 = false;
-    {
-        const int64_t r = (int64_t)blockIdx.x * rpc + rr, ch = rw * 32 + lane;
-        if (r < a.rows && ch < cpr) {
-            decode_chunk<TYPE>(a.raw, r, cpr, ch, __ldg(a.row_inv + r), v0);
-            have_v0 = true;
+    const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const int64_t nblk = cols / Geo<TYPE>::kBlockVals, cpr = cols / 32;
+    const GlobalBytes G{data + (row >> 3) * Geo<TYPE>::group_bytes(nblk)};
+    const float ri = row_inv[row];
+    int n = 0;
+    for (int64_t ch = lane; ch < cpr; ch += 32) {
+        Chunk c;
+        load_chunk<TYPE>(G, (int)(row & 7), (uint32_t)nblk, (uint32_t)ch, c);
+        uint32_t vw[16];
+        fast_values<TYPE>(c, ri, vw);
+        for (int e = 0; e < 32; e++) {
+            const int vf = (int)(int16_t)((vw[e >> 1] >> (16 * (e & 1))) & 0xFFFFu);
+            const int ve = exact_value<TYPE>(c, e, ri);
+            if (ve != vf) {
+                if (cursor) {
+                    const int at = atomicAdd(cursor + row, 1);
+                    exc[at] = make_int4((int)row, (int)(ch * 32 + e), ve - vf, 0);
+                }
+                n++;
+            }
         }
     }
-    pdl_wait();  // activations come from the preceding kernel
+    for (int o = 16; o > 0; o >>= 1) n += __shfl_xor_sync(0xffffffffu, n, o);
+    if (lane == 0 && cnt) cnt[row] = n;
+}
 
-    if (a.xq_in) {
-        const uint2* src = reinterpret_cast<const uint2*>(a.xq_in);
-        uint32_t* h4 = reinterpret_cast<uint32_t*>(xh);
-        uint32_t* l4 = reinterpret_cast<uint32_t*>(xl);
-        for (int64_t j = threadIdx.x; j < (int64_t)nb * cols / 4; j += blockDim.x) {
-            const uint2 w = src[j];  // four int16
-            h4[j] = __byte_perm(w.x, w.y, 0x7531);
-            l4[j] = __byte_perm(w.x, w.y, 0x6420);
+// ------------------------------------------------------------------ GEMV --
+struct BqArgs {
+    const uint8_t* data;     // grouped layout
+    const float* row_inv;
+    int64_t rows, cols, groups, group_bytes;
+    int gpc;                 // groups per CTA
+    const float* x;          // [nb][cols] fp32 activations, or
+    const int16_t* xq_in;    // [nb][cols] quantised activations, or
+    const uint8_t* xp_in;    // [nb][2][cols] the same as byte planes (high, low)
+    const float* xs_in;      // [nb] x_scale of xq_in / xp_in
+    float* y;                // [nb][rows]
+    int64_t* row_acc;
+    int64_t* unit_acc;
+    const int* exc_ptr;      // [rows + 1]
+    const int4* exc;         // (row, col, v - v', 0), grouped by row
+    int* err;
+    int nb;
+};
+
+#ifdef TMAC_TRACE
+// Diagnostic build only (-DTMAC_TRACE): per-CTA clock64 stamps of the kernel's
+// phases and per-warp main-loop start/end, read back with tmac_trace_read_blockq*.
+__device__ unsigned long long g_bq_trace[1024][12];
+__device__ unsigned long long g_bq_wtrace[1024][16][2];  // per warp: main-loop start, end
+#define BQ_STAMP(i)                                                                   \
+    do {                                                                              \
+        if (threadIdx.x == 0 && blockIdx.x < 1024) g_bq_trace[blockIdx.x][i] = clock64(); \
+    } while (0)
+#else
+#define BQ_STAMP(i) \
+    do {            \
+    } while (0)
+#endif
+
+constexpr int kExcCap = 512;  // exception entries staged in shared memory per pass
+
+// Shared memory of one CTA (offsets from the dynamic base; all 16-byte aligned).
+struct BqSmem {
+    int64_t w, x, acc, ri, ep, exc, xs, red, misc, bar, total;
+    __host__ __device__ BqSmem(int64_t gpc, int64_t group_bytes, int64_t nb, int64_t cols)
+    {
+        const int64_t rows = gpc * 8;
+        w = 0;
+        x = w + gpc * group_bytes;                   // [nb][2][cols] planes
+        acc = x + 2 * nb * cols;                     // uint32 [2][rows][nb]: low, high words
+        ri = acc + rows * nb * 8;                    // float [rows]
+        ep = ri + (rows * 4 + 15) / 16 * 16;         // int [rows + 4]: exception offsets
+        exc = ep + (rows + 4) * 4;                   // int4 [kExcCap]
+        xs = exc + kExcCap * 16;                     // float [16]
+        red = xs + 64;                               // float [32]
+        misc = red + 128;                            // int [4]
+        bar = misc + 16;                             // 2 mbarriers
+        total = bar + 16;
+    }
+};
+
+// int64 accumulation in shared memory as two 32-bit words with native 32-bit
+// atomics: the carry out of the low word is added to the high word.
+TMAC_DEV void acc_add(uint32_t* lo, uint32_t* hi, long long v)
+{
+    const uint32_t l = (uint32_t)(unsigned long long)v;
+    const uint32_t old = atomicAdd(lo, l);
+    const uint32_t carry = (old + l < old) ? 1u : 0u;
+    atomicAdd(hi, (uint32_t)((unsigned long long)v >> 32) + carry);
+}
+
+TMAC_DEV long long xq_at(const uint8_t* xpl, int64_t cols, int b, int64_t col)
+{
+    const uint8_t* p = xpl + (int64_t)b * 2 * cols;
+    return (long long)(int8_t)p[col] * 256 + (long long)p[cols + col];
+}
+
+template <int TYPE, int NB>
+__global__ void __launch_bounds__(512) blockq_gemv_kernel(BqArgs a)
+{
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int64_t cols = a.cols, cpr = cols / 32, nblk = cols / Geo<TYPE>::kBlockVals;
+    const int nb = a.nb;
+    const BqSmem L(a.gpc, a.group_bytes, nb, cols);
+    const int64_t g0 = (int64_t)blockIdx.x * a.gpc;
+    const int ng = (int)min((int64_t)a.gpc, a.groups - g0);
+    const int rows_cta = ng * 8;
+    const int64_t row0 = g0 * 8;
+    uint8_t* wsm = smem + L.w;
+    uint8_t* xpl = smem + L.x;
+    uint32_t* acc_lo = reinterpret_cast<uint32_t*>(smem + L.acc);   // [rows_cta * nb]
+    uint32_t* acc_hi = acc_lo + (int64_t)a.gpc * 8 * nb;
+    int* ep_s = reinterpret_cast<int*>(smem + L.ep);
+    float* ri_s = reinterpret_cast<float*>(smem + L.ri);
+    int4* exc_s = reinterpret_cast<int4*>(smem + L.exc);
+    int* misc_s = reinterpret_cast<int*>(smem + L.misc);
+    float* xs_s = reinterpret_cast<float*>(smem + L.xs);
+    float* red = reinterpret_cast<float*>(smem + L.red);
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L.bar);  // [0] weights, [1] activations
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+
+    BQ_STAMP(0);
+    // ---- prologue: everything here depends on the weights only.  One thread
+    // stages the CTA's weights, row_inv and exception entries with bulk copies
+    // completing on bar[0].
+    if (threadIdx.x == 0) {
+        mbar_init(&bar[0], 1);
+        mbar_init(&bar[1], 1);
+        fence_mbar_init();
+        const uint32_t wbytes = (uint32_t)(ng * a.group_bytes), rbytes = (uint32_t)(rows_cta * 4);
+        const uint32_t ebytes = (uint32_t)((rows_cta + 4) * 4);
+        mbar_expect_tx(&bar[0], wbytes + rbytes + ebytes);
+        const uint8_t* src = a.data + g0 * a.group_bytes;
+        for (uint32_t off = 0; off < wbytes; off += 32768u)
+            bulk_g2s(wsm + off, src + off, min(32768u, wbytes - off), &bar[0]);
+        bulk_g2s(ri_s, a.row_inv + row0, rbytes, &bar[0]);  // row_inv and exc_ptr are padded
+        bulk_g2s(ep_s, a.exc_ptr + row0, ebytes, &bar[0]);  // to whole groups (+4)
+        const int e0 = __ldg(a.exc_ptr + row0), e1 = __ldg(a.exc_ptr + min(row0 + rows_cta, a.rows));
+        misc_s[0] = e0;
+        misc_s[1] = e1;
+        const uint32_t n = (uint32_t)min(e1 - e0, kExcCap);
+        mbar_arrive_expect_tx(&bar[0], n * 16);
+        if (n) bulk_g2s(exc_s, a.exc + e0, n * 16, &bar[0]);
+    }
+    pdl_launch();
+    for (int t = threadIdx.x; t < rows_cta * nb; t += blockDim.x) acc_lo[t] = acc_hi[t] = 0;
+
+    BQ_STAMP(1);
+    // ---- activations come from the preceding kernel
+    pdl_wait();
+    if (a.xp_in) {
+        if (threadIdx.x == 0) {
+            const uint32_t bytes = (uint32_t)(2 * nb * cols);
+            mbar_arrive_expect_tx(&bar[1], bytes);
+            for (uint32_t off = 0; off < bytes; off += 32768u)
+                bulk_g2s(xpl + off, a.xp_in + off, min(32768u, bytes - off), &bar[1]);
         }
-        if (threadIdx.x < nb) xs[threadIdx.x] = a.xs_in[threadIdx.x];
+        if (threadIdx.x < nb) xs_s[threadIdx.x] = a.xs_in[threadIdx.x];
+    } else if (a.xq_in) {
+        // int16 input: split into the byte planes while staging (4 loads in flight)
+        const uint4* src = reinterpret_cast<const uint4*>(a.xq_in);
+        const int64_t n8 = (int64_t)nb * cols / 8;
+        for (int64_t j0 = threadIdx.x; j0 < n8; j0 += 4 * (int64_t)blockDim.x) {
+            uint4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int64_t j = j0 + u * (int64_t)blockDim.x;
+                if (j < n8) v[u] = src[j];
+            }
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int64_t j = j0 + u * (int64_t)blockDim.x;
+                if (j >= n8) break;
+                const int64_t e = j * 8, b = e / cols, c = e % cols;
+                uint8_t* p = xpl + b * 2 * cols + c;
+                *reinterpret_cast<uint2*>(p) =
+                    make_uint2(__byte_perm(v[u].x, v[u].y, 0x7531), __byte_perm(v[u].z, v[u].w, 0x7531));
+                *reinterpret_cast<uint2*>(p + cols) =
+                    make_uint2(__byte_perm(v[u].x, v[u].y, 0x6420), __byte_perm(v[u].z, v[u].w, 0x6420));
+            }
+        }
+        if (threadIdx.x < nb) xs_s[threadIdx.x] = a.xs_in[threadIdx.x];
     } else {
-        // activation quantisation, one vector at a time (tmac_gguf.cpp:889-896)
+        // activation quantisation, one vector at a time (tmac_gguf.cpp:889-896);
+        // x stays in registers between the max and the quantisation
+        constexpr int kXr = 12;
         for (int b = 0; b < nb; b++) {
             const float* xb = a.x + (int64_t)b * cols;
+            float xv[kXr];
             float mx = 0.0f;
-            for (int64_t j = threadIdx.x; j < cols; j += blockDim.x) mx = fmaxf(mx, fabsf(xb[j]));
+#pragma unroll
+            for (int k = 0; k < kXr; k++) {
+                const int64_t j = threadIdx.x + (int64_t)k * blockDim.x;
+                xv[k] = (j < cols) ? xb[j] : 0.0f;
+                mx = fmaxf(mx, fabsf(xv[k]));
+            }
+            for (int64_t j = threadIdx.x + (int64_t)kXr * blockDim.x; j < cols; j += blockDim.x)
+                mx = fmaxf(mx, fabsf(xb[j]));
             mx = block_max(mx, red, blockDim.x);
             const float s = x_scale_from_max(mx);
-            if (threadIdx.x == 0) xs[b] = s;
-            for (int64_t j = threadIdx.x; j < cols; j += blockDim.x) {
+            if (threadIdx.x == 0) xs_s[b] = s;
+            uint8_t* p = xpl + (int64_t)b * 2 * cols;
+#pragma unroll
+            for (int k = 0; k < kXr; k++) {
+                const int64_t j = threadIdx.x + (int64_t)k * blockDim.x;
+                if (j < cols) {
+                    const int16_t q = quantize_one(xv[k], s);
+                    p[j] = (uint8_t)((uint16_t)q >> 8);
+                    p[cols + j] = (uint8_t)(q & 0xFF);
+                }
+            }
+            for (int64_t j = threadIdx.x + (int64_t)kXr * blockDim.x; j < cols; j += blockDim.x) {
                 const int16_t q = quantize_one(xb[j], s);
-                xh[b * cols + j] = (uint8_t)((uint16_t)q >> 8);
-                xl[b * cols + j] = (uint8_t)(q & 0xFF);
+                p[j] = (uint8_t)((uint16_t)q >> 8);
+                p[cols + j] = (uint8_t)(q & 0xFF);
             }
         }
     }
     __syncthreads();
+    BQ_STAMP(2);
+    if (!mbar_wait_bounded(&bar[0], 0, a.err)) return;
+    BQ_STAMP(3);
+    if (a.xp_in && !mbar_wait_bounded(&bar[1], 0, a.err)) return;
+    BQ_STAMP(4);
 
-    const int64_t upr = (TYPE == TMAC_TYPE_Q5_0) ? cpr : cpr / 8;
-    for (int64_t r0 = (int64_t)blockIdx.x * rpc; r0 < a.rows; r0 += (int64_t)gridDim.x * rpc) {
-        const int64_t r = r0 + rr;
-        const bool row_live = r < a.rows;
-        const float ri = row_live ? __ldg(a.row_inv + r) : 1.0f;
-        long long acc[NB];
+    // ---- main loop.  Work items are (slot, step): Q5_0 slot = a group of 8
+    // rows (lane = row r + 8 * l, chunk j = 4*step + l: 4 lanes per row), K-quant
+    // slot = one row (lane = 8 * phase + sub-block, super-block = 4*step +
+    // phase).  Each warp takes a contiguous run of items and adds its row sums
+    // into acc_s when the slot changes.
+    const bool q5 = (TYPE == TMAC_TYPE_Q5_0);
+    const int64_t upr = q5 ? cpr : nblk;
+    const int slots = q5 ? ng : rows_cta;
+    const int steps = (int)(q5 ? (cpr + 3) / 4 : (nblk + 3) / 4);
+    const int items = slots * steps;
+    const int it0 = (int)((int64_t)items * warp / nwarps), it1 = (int)((int64_t)items * (warp + 1) / nwarps);
+    const int r_lane = q5 ? (lane & 7) : 0;
+    const int l_lane = q5 ? (lane >> 3) : lane;
+    long long acc[NB];
 #pragma unroll
-        for (int b = 0; b < NB; b++) acc[b] = 0;
-        for (int64_t base = 0; base < cpr; base += tpr) {
-            const int64_t ch = base + rw * 32 + lane;
-            const bool live = row_live && ch < cpr;
-            uint32_t v[16];
-            if (r0 == (int64_t)blockIdx.x * rpc && base == 0 && have_v0) {
-#pragma unroll
-                for (int i = 0; i < 16; i++) v[i] = v0[i];
-            } else if (live) {
-                decode_chunk<TYPE>(a.raw, r, cpr, ch, ri, v);
-            }
-#pragma unroll
-            for (int b = 0; b < NB; b++) {
-                if (b >= nb) break;
-                long long part = 0;
-                if (live) {
-                    const uint32_t* h4 = reinterpret_cast<const uint32_t*>(xh + b * cols + ch * 32);
-                    const uint32_t* l4 = reinterpret_cast<const uint32_t*>(xl + b * cols + ch * 32);
-                    part = chunk_dot(v, h4, l4);
-                }
-                acc[b] += part;
-                if (a.unit_acc) {
-                    long long* u = (long long*)a.unit_acc + ((int64_t)b * a.rows + r) * upr;
-                    if (TYPE == TMAC_TYPE_Q5_0) {
-                        if (live) u[ch] = part;
-                    } else {  // a 256-value block = 8 consecutive chunks = 8 consecutive lanes
-                        long long sb = part;
-                        for (int o = 1; o < 8; o <<= 1) sb += __shfl_xor_sync(0xffffffffu, sb, o);
-                        if (live && (lane & 7) == 0) u[ch / 8] = sb;
-                    }
-                }
-            }
+    for (int b = 0; b < NB; b++) acc[b] = 0;
+#ifdef TMAC_TRACE
+    if (lane == 0 && blockIdx.x < 1024) g_bq_wtrace[blockIdx.x][warp][0] = clock64();
+#endif
+    const uint32_t wsm_a = smem_addr(wsm);
+    int slot = it0 / steps, s = it0 % steps;
+    for (int it = it0; it < it1; it++) {
+        const int rr = q5 ? slot * 8 + r_lane : slot;  // row within the CTA
+        const SharedBytes G{wsm_a + (uint32_t)(rr >> 3) * (uint32_t)a.group_bytes};
+        const int r = rr & 7;
+        const float ri = ri_s[rr];
+        const uint32_t ch = q5 ? (uint32_t)(4 * s + l_lane) : (uint32_t)(4 * s + (lane >> 3)) * 8 + (lane & 7);
+        const bool cl = ch < cpr;
+        uint32_t vw[16];
+        if (cl) {
+            Chunk c;
+            load_chunk<TYPE>(G, r, (uint32_t)nblk, ch, c);
+            fast_values<TYPE>(c, ri, vw);
         }
 #pragma unroll
         for (int b = 0; b < NB; b++) {
             if (b >= nb) break;
-            const long long t = warp_sum_ll(acc[b]);
-            if (lane == 0) part_s[warp * NB + b] = t;
+            long long part = 0;
+            if (cl) {
+                const uint8_t* p = xpl + (int64_t)b * 2 * cols + ch * 32;
+                part = chunk_dot(vw, p, p + cols);
+            }
+            acc[b] += part;
+            if (a.unit_acc) {
+                const int64_t row = row0 + rr;
+                long long* u = (long long*)a.unit_acc + ((int64_t)b * a.rows + row) * upr;
+                if (q5) {
+                    if (cl && row < a.rows) u[ch] = part;
+                } else {  // a 256-value block = 8 chunks held by 8 consecutive lanes
+                    long long sb = part;
+                    for (int o = 1; o < 8; o <<= 1) sb += __shfl_xor_sync(0xffffffffu, sb, o);
+                    if (cl && (lane & 7) == 0 && row < a.rows) u[ch / 8] = sb;
+                }
+            }
         }
-        __syncthreads();
-        if (rw == 0 && lane < nb && row_live) {
-            long long tot = 0;
-            for (int w = 0; w < wpr; w++) tot += part_s[(rr * wpr + w) * NB + lane];
-            const double v = __ddiv_rn(__dmul_rn((double)tot, (double)xs[lane]), (double)ri);
-            a.y[(int64_t)lane * a.rows + r] = (float)v;
-            if (a.row_acc) a.row_acc[(int64_t)lane * a.rows + r] = tot;
+        // flush the row sums when this warp's next item is in another slot
+        if (++s == steps || it + 1 == it1) {
+#pragma unroll
+            for (int b = 0; b < NB; b++) {
+                if (b >= nb) break;
+                long long v = acc[b];
+                for (int o = q5 ? 8 : 1; o < 32; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                if (l_lane == 0) acc_add(&acc_lo[rr * nb + b], &acc_hi[rr * nb + b], v);
+                acc[b] = 0;
+            }
+            if (s == steps) {
+                s = 0;
+                slot++;
+            }
         }
-        __syncthreads();
     }
+#ifdef TMAC_TRACE
+    if (lane == 0 && blockIdx.x < 1024) g_bq_wtrace[blockIdx.x][warp][1] = clock64();
+#endif
+    __syncthreads();
+    BQ_STAMP(5);
+
+    // ---- exceptions: acc += (v - v') * x_q[col], one thread per (entry, vector)
+    const int e0 = ep_s[0], e1 = ep_s[rows_cta];
+    for (int base = e0; base < e1; base += kExcCap) {
+        const int n = min(e1 - base, kExcCap);
+        if (base != e0) {  // more entries than the prologue staged
+            __syncthreads();
+            for (int t = threadIdx.x; t < n; t += blockDim.x) exc_s[t] = __ldg(a.exc + base + t);
+            __syncthreads();
+        }
+        for (int t = threadIdx.x; t < n * nb; t += blockDim.x) {
+            const int4 ex = exc_s[t / nb];
+            const int b = t % nb, rr = ex.x - (int)row0;
+            const long long d = (long long)ex.z * xq_at(xpl, cols, b, ex.y);
+            acc_add(&acc_lo[rr * nb + b], &acc_hi[rr * nb + b], d);
+            if (a.unit_acc) {
+                long long* u = (long long*)a.unit_acc + ((int64_t)b * a.rows + ex.x) * upr;
+                atomicAdd(reinterpret_cast<unsigned long long*>(&u[q5 ? ex.y / 32 : ex.y / 256]), (unsigned long long)d);
+            }
+        }
+    }
+    __syncthreads();
+    BQ_STAMP(6);
+    // ---- rows: y = (float)((double)acc * x_scale / (double)row_inv)
+    for (int t = threadIdx.x; t < rows_cta * nb; t += blockDim.x) {
+        const int rr = t / nb, b = t % nb;
+        const int64_t row = row0 + rr;
+        if (row >= a.rows) continue;
+        const long long tot = (long long)(((unsigned long long)acc_hi[rr * nb + b] << 32) | acc_lo[rr * nb + b]);
+        const double v = __ddiv_rn(__dmul_rn((double)tot, (double)xs_s[b]), (double)ri_s[rr]);
+        a.y[(int64_t)b * a.rows + row] = (float)v;
+        if (a.row_acc) a.row_acc[(int64_t)b * a.rows + row] = tot;
+    }
+#ifdef TMAC_TRACE
+    __syncthreads();
+    if (threadIdx.x == 0 && blockIdx.x < 1024) {
+        uint32_t smid;
+        asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+        g_bq_trace[blockIdx.x][7] = clock64();
+        g_bq_trace[blockIdx.x][8] = smid;
+    }
+#endif
 }
 
+constexpr int64_t kMaxSmem = 220 * 1024;
+
 template <int TYPE, int NB>
-int launch_nb(const tmac_weight_s* w, const BlockqArgs& a, cudaStream_t s)
+int launch_nb(const tmac_weight_s* w, BqArgs a, cudaStream_t s)
 {
-    const int64_t max_smem = 200 * 1024;
     static bool attr[64] = {};
     if (!attr[w->device & 63]) {
         TMAC_CUDA_TRY(cudaFuncSetAttribute(blockq_gemv_kernel<TYPE, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           (int)max_smem));
+                                           (int)kMaxSmem));
         attr[w->device & 63] = true;
     }
-    // warps per row: enough lanes for every 32-value chunk of a row (at most 8)
-    const int64_t cpr = a.cols / 32;
-    const int wpr = (int)std::min<int64_t>(8, (cpr + 31) / 32);
-    const int rpc = 8 / wpr;
-    const size_t smem = ((size_t)a.nb * a.cols * 2 + 15) / 16 * 16 + 24 * 4 + 8 * NB * 8;
-    // few enough CTAs that the per-CTA activation quantisation (when x is fp32)
-    // stays small next to the rows each CTA works through
-    const int64_t cap = (int64_t)num_sms(w->device) * (a.xq_in ? 16 : 2);
-    const int grid = (int)std::min<int64_t>((a.rows + rpc - 1) / rpc, cap);
-    TMAC_CUDA_TRY(launch_k(blockq_gemv_kernel<TYPE, NB>, dim3(grid), dim3(wpr * rpc * 32), smem, s, a, wpr, rpc));
+    // one wave: every SM gets ceil(groups / SMs) groups, fewer if shared memory
+    // cannot hold them next to the activations
+    const int64_t sms = num_sms(w->device);
+    int64_t gpc = std::max<int64_t>(1, (a.groups + sms - 1) / sms);
+    while (gpc > 1 && BqSmem(gpc, a.group_bytes, a.nb, a.cols).total > kMaxSmem) gpc--;
+    a.gpc = (int)gpc;
+    const int grid = (int)((a.groups + gpc - 1) / gpc);
+    const int64_t slots = (TYPE == TMAC_TYPE_Q5_0) ? gpc : gpc * 8;
+    const int64_t steps = (TYPE == TMAC_TYPE_Q5_0) ? (a.cols / 32 + 3) / 4 : (a.cols / 256 + 3) / 4;
+    const int warps = (int)std::max<int64_t>(1, std::min<int64_t>(16, slots * steps));
+    TMAC_CUDA_TRY(launch_k(blockq_gemv_kernel<TYPE, NB>, dim3(grid), dim3(warps * 32),
+                           (size_t)BqSmem(gpc, a.group_bytes, a.nb, a.cols).total, s, a));
     TMAC_CUDA_TRY(cudaGetLastError());
     return TMAC_OK;
 }
 
 template <int TYPE>
-int launch_type(const tmac_weight_s* w, const float* x, const int16_t* xq, const float* xs, float* y,
-                int64_t* row_acc, int64_t* unit_acc, int batch, cudaStream_t s)
+int launch_type(const tmac_weight_s* w, const float* x, const int16_t* xq, const uint8_t* xp, const float* xs,
+                float* y, int64_t* row_acc, int64_t* unit_acc, int batch, cudaStream_t s)
 {
     const int64_t cols = w->cols, cpr = cols / 32;
-    const int64_t max_smem = 200 * 1024;
-    const int bmax = (int)std::max<int64_t>(1, std::min<int64_t>(16, (max_smem - 4096) / (cols * 2)));
-    const int64_t upr = (TYPE == TMAC_TYPE_Q5_0) ? cpr : cpr / 8;
+    // activation planes take 2*cols bytes per vector next to one group of weights
+    const int64_t fixed = BqSmem(1, w->group_bytes, 0, cols).total + 16 * 8 * 8;
+    const int bmax = (int)std::max<int64_t>(1, std::min<int64_t>(16, (kMaxSmem - fixed) / (cols * 2)));
+    const int64_t upr = (TYPE == TMAC_TYPE_Q5_0) ? cpr : cols / 256;
+    int* err = device_error_word(w->device);
     for (int b0 = 0; b0 < batch; b0 += bmax) {
-        BlockqArgs a;
-        a.raw = w->data;
+        BqArgs a;
+        a.data = w->data;
         a.row_inv = w->row_norm;
         a.rows = w->rows;
         a.cols = cols;
+        a.groups = w->groups;
+        a.group_bytes = w->group_bytes;
+        a.gpc = 1;
         a.nb = std::min(bmax, batch - b0);
         a.x = x ? x + (int64_t)b0 * cols : nullptr;
         a.xq_in = xq ? xq + (int64_t)b0 * cols : nullptr;
+        a.xp_in = xp ? xp + (int64_t)b0 * 2 * cols : nullptr;
         a.xs_in = xs ? xs + b0 : nullptr;
         a.y = y + (int64_t)b0 * w->rows;
         a.row_acc = row_acc ? row_acc + (int64_t)b0 * w->rows : nullptr;
         a.unit_acc = unit_acc ? unit_acc + (int64_t)b0 * w->rows * upr : nullptr;
+        a.exc_ptr = w->exc_ptr;
+        a.exc = reinterpret_cast<const int4*>(w->exc);
+        a.err = err;
         int rc;
         if (a.nb == 1) rc = launch_nb<TYPE, 1>(w, a, s);
         else if (a.nb <= 2) rc = launch_nb<TYPE, 2>(w, a, s);
@@ -363,30 +768,89 @@ int launch_type(const tmac_weight_s* w, const float* x, const int16_t* xq, const
     return TMAC_OK;
 }
 
-}  // namespace
-
-int register_blockq(tmac_weight_s* w, const uint8_t* d_raw, cudaStream_t s)
+template <int TYPE>
+int register_type(tmac_weight_s* w, const uint8_t* d_raw, cudaStream_t s)
 {
-    TMAC_CUDA_TRY(cudaMalloc(&w->row_norm, (size_t)w->rows * sizeof(float)));
+    const int64_t rows = w->rows, nblk = w->cols / Geo<TYPE>::kBlockVals;
+    // row_inv padded to whole row groups (zeros), so a CTA copies its slice in one piece
+    TMAC_CUDA_TRY(cudaMalloc(&w->row_norm, (size_t)(rows + 7) / 8 * 8 * sizeof(float)));
+    TMAC_CUDA_TRY(cudaMemsetAsync(w->row_norm, 0, (size_t)(rows + 7) / 8 * 8 * sizeof(float), s));
     const int wpb = 8;
-    const unsigned grid = (unsigned)((w->rows + wpb - 1) / wpb);
-    switch (w->type) {
-    case TMAC_TYPE_Q5_0: row_inv_kernel<TMAC_TYPE_Q5_0><<<grid, wpb * 32, 0, s>>>(d_raw, w->rows, w->cols, w->row_norm); break;
-    case TMAC_TYPE_Q4_K: row_inv_kernel<TMAC_TYPE_Q4_K><<<grid, wpb * 32, 0, s>>>(d_raw, w->rows, w->cols, w->row_norm); break;
-    case TMAC_TYPE_Q6_K: row_inv_kernel<TMAC_TYPE_Q6_K><<<grid, wpb * 32, 0, s>>>(d_raw, w->rows, w->cols, w->row_norm); break;
-    default: return fail(TMAC_ERR_TYPE, "register_blockq: unsupported type");
-    }
+    const unsigned rgrid = (unsigned)((rows + wpb - 1) / wpb);
+    row_inv_kernel<TYPE><<<rgrid, wpb * 32, 0, s>>>(d_raw, rows, w->cols, w->row_norm);
     TMAC_CUDA_TRY(cudaGetLastError());
+
+    w->groups = (rows + 7) / 8;
+    w->group_bytes = Geo<TYPE>::group_bytes(nblk);
+    w->data_bytes = (size_t)(w->groups * w->group_bytes);
+    TMAC_CUDA_TRY(cudaMalloc(&w->data, w->data_bytes));
+    TMAC_CUDA_TRY(cudaMemsetAsync(w->data, 0, w->data_bytes, s));
+    const int64_t nblocks = rows * nblk;
+    relayout_kernel<TYPE><<<(unsigned)((nblocks + 255) / 256), 256, 0, s>>>(d_raw, rows, nblk, w->data);
+    TMAC_CUDA_TRY(cudaGetLastError());
+
+    // exception lists: count, prefix-sum on the host, fill
+    int* d_cnt = nullptr;
+    // exc_ptr padded to whole row groups + 4 (a CTA copies rows_cta + 4 offsets)
+    const int64_t nptr = w->groups * 8 + 4;
+    TMAC_CUDA_TRY(cudaMalloc(&w->exc_ptr, (size_t)nptr * sizeof(int)));
+    TMAC_CUDA_TRY(cudaMalloc(&d_cnt, (size_t)rows * sizeof(int)));
+    exceptions_kernel<TYPE><<<rgrid, wpb * 32, 0, s>>>(w->data, w->row_norm, rows, w->cols, d_cnt, nullptr, nullptr);
+    cudaError_t e = cudaGetLastError();
+    std::vector<int> cnt(rows), ptr(nptr, 0);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(cnt.data(), d_cnt, rows * sizeof(int), cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) {
+        cudaFree(d_cnt);
+        return cuda_fail(e, "exception count");
+    }
+    for (int64_t r = 0; r < rows; r++) ptr[r + 1] = ptr[r] + cnt[r];
+    for (int64_t r = rows + 1; r < nptr; r++) ptr[r] = ptr[rows];
+    w->n_exc = ptr[rows];
+    e = cudaMemcpy(w->exc_ptr, ptr.data(), nptr * sizeof(int), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMalloc(&w->exc, std::max<int64_t>(1, w->n_exc) * sizeof(int4));
+    if (e == cudaSuccess) e = cudaMemcpy(d_cnt, ptr.data(), rows * sizeof(int), cudaMemcpyHostToDevice);  // cursors
+    if (e == cudaSuccess && w->n_exc > 0) {
+        exceptions_kernel<TYPE><<<rgrid, wpb * 32, 0, s>>>(w->data, w->row_norm, rows, w->cols, nullptr, d_cnt,
+                                                           reinterpret_cast<int4*>(w->exc));
+        e = cudaGetLastError();
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    }
+    cudaFree(d_cnt);
+    if (e != cudaSuccess) return cuda_fail(e, "exception fill");
     return TMAC_OK;
 }
 
-int launch_blockq(const tmac_weight_s* w, const float* x, const int16_t* xq, const float* xs, float* y,
-                  int64_t* row_acc, int64_t* unit_acc, int batch, cudaStream_t s)
+}  // namespace
+
+#ifdef TMAC_TRACE
+extern "C" int tmac_trace_read_blockq(unsigned long long* out)
+{
+    return (int)cudaMemcpyFromSymbol(out, g_bq_trace, sizeof(g_bq_trace));
+}
+extern "C" int tmac_trace_read_blockq_warps(unsigned long long* out)
+{
+    return (int)cudaMemcpyFromSymbol(out, g_bq_wtrace, sizeof(g_bq_wtrace));
+}
+#endif
+
+int register_blockq(tmac_weight_s* w, const uint8_t* d_raw, cudaStream_t s)
 {
     switch (w->type) {
-    case TMAC_TYPE_Q5_0: return launch_type<TMAC_TYPE_Q5_0>(w, x, xq, xs, y, row_acc, unit_acc, batch, s);
-    case TMAC_TYPE_Q4_K: return launch_type<TMAC_TYPE_Q4_K>(w, x, xq, xs, y, row_acc, unit_acc, batch, s);
-    case TMAC_TYPE_Q6_K: return launch_type<TMAC_TYPE_Q6_K>(w, x, xq, xs, y, row_acc, unit_acc, batch, s);
+    case TMAC_TYPE_Q5_0: return register_type<TMAC_TYPE_Q5_0>(w, d_raw, s);
+    case TMAC_TYPE_Q4_K: return register_type<TMAC_TYPE_Q4_K>(w, d_raw, s);
+    case TMAC_TYPE_Q6_K: return register_type<TMAC_TYPE_Q6_K>(w, d_raw, s);
+    default: return fail(TMAC_ERR_TYPE, "register_blockq: unsupported type");
+    }
+}
+
+int launch_blockq(const tmac_weight_s* w, const float* x, const int16_t* xq, const uint8_t* xp, const float* xs,
+                  float* y, int64_t* row_acc, int64_t* unit_acc, int batch, cudaStream_t s)
+{
+    switch (w->type) {
+    case TMAC_TYPE_Q5_0: return launch_type<TMAC_TYPE_Q5_0>(w, x, xq, xp, xs, y, row_acc, unit_acc, batch, s);
+    case TMAC_TYPE_Q4_K: return launch_type<TMAC_TYPE_Q4_K>(w, x, xq, xp, xs, y, row_acc, unit_acc, batch, s);
+    case TMAC_TYPE_Q6_K: return launch_type<TMAC_TYPE_Q6_K>(w, x, xq, xp, xs, y, row_acc, unit_acc, batch, s);
     default: return fail(TMAC_ERR_TYPE, "launch_blockq: unsupported type");
     }
 }

@@ -8,8 +8,12 @@
 namespace tmac {
 namespace {
 
+// xq: int16 [batch][cols]; xp: the same values as byte planes [batch][2][cols]
+// (high bytes, then low bytes), the form the block-quant GEMVs stage with one
+// bulk copy.  Either may be null.
 __global__ void __launch_bounds__(1024) quantize_kernel(const float* __restrict__ x, int64_t cols,
-                                                        int16_t* __restrict__ xq, float* __restrict__ xs)
+                                                        int16_t* __restrict__ xq, uint8_t* __restrict__ xp,
+                                                        float* __restrict__ xs)
 {
     __shared__ float red[32];
     pdl_launch();
@@ -20,14 +24,22 @@ __global__ void __launch_bounds__(1024) quantize_kernel(const float* __restrict_
     mx = block_max(mx, red, blockDim.x);
     const float s = x_scale_from_max(mx);
     if (threadIdx.x == 0) xs[blockIdx.x] = s;
-    for (int64_t j = threadIdx.x; j < cols; j += blockDim.x) xq[(int64_t)blockIdx.x * cols + j] = quantize_one(xb[j], s);
+    uint8_t* p = xp ? xp + (int64_t)blockIdx.x * 2 * cols : nullptr;
+    for (int64_t j = threadIdx.x; j < cols; j += blockDim.x) {
+        const int16_t q = quantize_one(xb[j], s);
+        if (xq) xq[(int64_t)blockIdx.x * cols + j] = q;
+        if (p) {
+            p[j] = (uint8_t)((uint16_t)q >> 8);
+            p[cols + j] = (uint8_t)(q & 0xFF);
+        }
+    }
 }
 
 }  // namespace
 
-int launch_quantize(const float* x, int64_t cols, int batch, int16_t* xq, float* xs, cudaStream_t s)
+int launch_quantize(const float* x, int64_t cols, int batch, int16_t* xq, float* xs, cudaStream_t s, uint8_t* xp)
 {
-    TMAC_CUDA_TRY(launch_k(quantize_kernel, dim3(batch), dim3(1024), 0, s, x, cols, xq, xs));
+    TMAC_CUDA_TRY(launch_k(quantize_kernel, dim3(batch), dim3(1024), 0, s, x, cols, xq, xp, xs));
     TMAC_CUDA_TRY(cudaGetLastError());
     return TMAC_OK;
 }
@@ -52,5 +64,5 @@ extern "C" int tmac_gemv_xq(tmac_weight_t w, const int16_t* xq, const float* xs,
     DeviceGuard dg(w->device);
     cudaStream_t s = (cudaStream_t)stream;
     if (w->type == TMAC_TYPE_Q8_0) return launch_q8_0(w, nullptr, y, nullptr, nullptr, batch, s, nullptr, 0, xq, xs);
-    return launch_blockq(w, nullptr, xq, xs, y, nullptr, nullptr, batch, s);
+    return launch_blockq(w, nullptr, xq, nullptr, xs, y, nullptr, nullptr, batch, s);
 }

@@ -151,7 +151,8 @@ int staging(int device, size_t xb, size_t yb, float** dx, float** dy)
 }
 
 // Per-device activation workspace of the two-kernel block-quant GEMV path:
-// x_q (int16) and x_scale for up to `xq_cap` values / `xs_cap` vectors.
+// x_q (2 bytes per value, stored as byte planes) and x_scale for up to
+// `xq_cap` values / `xs_cap` vectors.
 struct Workspace {
     int16_t* xq = nullptr;
     float* xs = nullptr;
@@ -222,6 +223,8 @@ void free_weight(tmac_weight_s* w)
     DeviceGuard dg(w->device);
     if (w->data) cudaFree(w->data);
     if (w->row_norm) cudaFree(w->row_norm);
+    if (w->exc_ptr) cudaFree(w->exc_ptr);
+    if (w->exc) cudaFree(w->exc);
     delete w;
 }
 
@@ -320,16 +323,8 @@ int tmac_weight_register(int type, int mode, int64_t rows, int64_t cols, const v
     if (mode == TMAC_MODE_NATIVE && type == TMAC_TYPE_Q8_0) {
         rc = register_q8_0(w, d_raw, d_rma, s);
     } else if (mode == TMAC_MODE_NATIVE) {
-        // Q5_0 / Q4_K / Q6_K keep the GGUF blocks; the kernel reads them in place.
-        if (raw_owned) {
-            w->data = d_raw;
-        } else {
-            if ((e = cudaMalloc(&w->data, need)) != cudaSuccess) return cleanup(cuda_fail(e, "cudaMalloc(data)"));
-            if ((e = cudaMemcpy(w->data, d_raw, need, cudaMemcpyDeviceToDevice)) != cudaSuccess)
-                return cleanup(cuda_fail(e, "cudaMemcpy(data)"));
-        }
-        w->data_bytes = need;
-        rc = register_blockq(w, w->data, s);
+        // Q5_0 / Q4_K / Q6_K: re-laid out in row groups (gemv_blockq.cu)
+        rc = register_blockq(w, d_raw, s);
     } else if (mode == TMAC_MODE_INT16) {
         rc = register_int16(w, d_raw, s);
     } else {
@@ -374,7 +369,8 @@ int tmac_weight_device_bytes(tmac_weight_t w, size_t* bytes)
     int rc = weight_ok(w);
     if (rc) return rc;
     if (!bytes) return fail(TMAC_ERR_INVALID, "NULL bytes pointer");
-    *bytes = w->data_bytes + (w->row_norm && w->type != TMAC_TYPE_Q8_0 ? w->rows * sizeof(float) : 0);
+    *bytes = w->data_bytes + (w->row_norm && w->type != TMAC_TYPE_Q8_0 ? w->rows * sizeof(float) : 0) +
+             (w->exc_ptr ? (size_t)(w->groups * 8 + 4) * sizeof(int) + w->n_exc * 16 : 0);
     return TMAC_OK;
 }
 
@@ -404,15 +400,16 @@ int tmac_gemv_acc(tmac_weight_t w, const float* x, float* y, int64_t* row_acc, i
     if (w->mode == TMAC_MODE_NATIVE && w->type == TMAC_TYPE_Q8_0)
         return launch_q8_0(w, x, y, row_acc, unit_acc, batch, s);
     if (w->mode == TMAC_MODE_NATIVE) {
-        // Quantise x once (one CTA per vector) into the device workspace, then
-        // every GEMV CTA reads x_q instead of re-quantising all columns.
-        if (w->cols % 8) return launch_blockq(w, x, nullptr, nullptr, y, row_acc, unit_acc, batch, s);
+        // one or two vectors: every CTA quantises x itself (one launch); more:
+        // quantise once into the device workspace, then the GEMV
+        if (batch <= 2) return launch_blockq(w, x, nullptr, nullptr, nullptr, y, row_acc, unit_acc, batch, s);
         int16_t* xq = nullptr;
         float* xs = nullptr;
         int rc2 = workspace(w->device, (size_t)batch * w->cols, (size_t)batch, &xq, &xs);
         if (rc2) return rc2;
-        if ((rc2 = launch_quantize(x, w->cols, batch, xq, xs, s))) return rc2;
-        return launch_blockq(w, nullptr, xq, xs, y, row_acc, unit_acc, batch, s);
+        uint8_t* xp = reinterpret_cast<uint8_t*>(xq);
+        if ((rc2 = launch_quantize(x, w->cols, batch, nullptr, xs, s, xp))) return rc2;
+        return launch_blockq(w, nullptr, nullptr, xp, xs, y, row_acc, unit_acc, batch, s);
     }
     if (w->mode == TMAC_MODE_INT16) return launch_int16(w, x, y, row_acc, unit_acc, batch, s);
     return launch_f32(w, x, y, batch, s);
@@ -443,8 +440,9 @@ int tmac_gemv_static(tmac_weight_t w, const float* x, float* y, int batch, void*
     float* xs = nullptr;
     if ((rc = static_scratch(w->device, &xq, &xs))) return rc;
     cudaStream_t s = (cudaStream_t)stream;
-    if ((rc = launch_quantize(x, w->cols, batch, xq, xs, s))) return rc;
-    return launch_blockq(w, nullptr, xq, xs, y, nullptr, nullptr, batch, s);
+    uint8_t* xp = reinterpret_cast<uint8_t*>(xq);  // the scratch holds x_q as byte planes
+    if ((rc = launch_quantize(x, w->cols, batch, nullptr, xs, s, xp))) return rc;
+    return launch_blockq(w, nullptr, nullptr, xp, xs, y, nullptr, nullptr, batch, s);
 }
 
 static int gemv_typed(tmac_weight_t w, int type, int mode, const float* x, float* y, int batch, void* stream,
