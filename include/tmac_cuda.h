@@ -170,6 +170,17 @@ int tmac_gemv_xq(tmac_weight_t w, const int16_t* xq, const float* xs, float* y, 
  * must be ordered on one stream.  Batch 1-2 quantises inside the GEMV. */
 int tmac_reserve(int device, int64_t max_batch, int64_t max_cols);
 
+/* Batched matmul on the tensor cores (prefill: m activation rows at once; the
+ * reference runs matmul_fpga_q5_0 / _q4_k / _q6_k once per token,
+ * sim/tmac_gguf.cpp:1992-2023).  y[m][rows] equals tmac_gemv with batch m bit
+ * for bit: every row is quantised like one GEMV call, the products are the
+ * reference's exact int16 weights times x_q (tcgen05 int8 MMAs on byte planes),
+ * row_acc (optional, int64 [m][rows]) the integer row sums.  NATIVE Q5_0 /
+ * Q4_K / Q6_K weights; cols a multiple of 16, at most 32768.  The first call on
+ * a weight decodes its int16 planes (2 bytes per weight, kept with the weight).
+ * Device pointers; asynchronous on `stream`. */
+int tmac_gemm(tmac_weight_t w, const float* x, float* y, int64_t* row_acc, int m, void* stream);
+
 /* NATIVE Q5_0 / Q4_K / Q6_K GEMV that allocates nothing.  No counterpart in
  * the reference (its drivers are host code with no device memory to manage);
  * it is for callers that may not allocate device memory, e.g. code running

@@ -83,6 +83,7 @@ def lib():
             "tmac_gemv_int16": (ctypes.c_int, [_P, _P, _P, ctypes.c_int, _P]),
             "tmac_gemv_host": (ctypes.c_int, [_P, _P, _P, ctypes.c_int]),
             "tmac_gemv_static": (ctypes.c_int, [_P, _P, _P, ctypes.c_int, _P]),
+            "tmac_gemm": (ctypes.c_int, [_P, _P, _P, _P, ctypes.c_int, _P]),
             "tmac_reserve": (ctypes.c_int, [ctypes.c_int, _I64, _I64]),
             "tmac_top1": (ctypes.c_int, [_P, _I64, _I64, _P, _P]),
             "tmac_gemv_top1": (ctypes.c_int, [_P, _P, _P, _P, _I64, ctypes.c_int, _P]),
@@ -175,6 +176,11 @@ class Weight:
         """Device GEMV on torch tensors / device pointers (asynchronous)."""
         s = None if stream is None else (stream if isinstance(stream, int) else stream.cuda_stream)
         check(lib().tmac_gemv_acc(self.handle, _ptr(x), _ptr(y), _ptr(row_acc), _ptr(unit_acc), batch, s))
+
+    def gemm(self, x, y, m, row_acc=None, stream=None):
+        """Tensor-core batched matmul: y[m][rows] for m fp32 activation rows (device)."""
+        s = None if stream is None else (stream if isinstance(stream, int) else stream.cuda_stream)
+        check(lib().tmac_gemm(self.handle, _ptr(x), _ptr(y), _ptr(row_acc), m, s))
 
     def gemv_top1(self, x, y, key, index_base=0, batch=1, stream=None):
         """y = W.x plus the packed top-1 key of y (device uint64/int64 key[batch])."""

@@ -227,6 +227,8 @@ struct tmac_weight_s {
     int* exc_ptr = nullptr;      // NATIVE Q5_0/K-quants: per-row exception offsets [rows + 1]
     void* exc = nullptr;         // int4 (row, col, v - v', 0) entries
     int64_t n_exc = 0;
+    void* gwh = nullptr;         // tensor-core GEMM: exact int16 weights as byte planes
+    void* gwl = nullptr;         // (high, low), decoded on first tmac_gemm
 };
 
 namespace tmac {
@@ -243,6 +245,12 @@ int register_blockq(tmac_weight_s* w, const uint8_t* d_raw, cudaStream_t s);
 // bytes, low bytes) with their x_scale xs.
 int launch_blockq(const tmac_weight_s* w, const float* x, const int16_t* xq, const uint8_t* xp, const float* xs,
                   float* y, int64_t* row_acc, int64_t* unit_acc, int batch, cudaStream_t s);
+// The reference's exact int16 weights of a NATIVE Q5_0 / Q4_K / Q6_K weight as
+// byte planes wh (signed high) / wl (low), [rows][cols] row-major.
+int blockq_planes(const tmac_weight_s* w, int8_t* wh, uint8_t* wl, cudaStream_t s);
+// Tensor-core GEMM (gemm_tc.cu): Y[m][rows] = the GEMV of each of m fp32 rows.
+int gemm_prepare(tmac_weight_s* w, cudaStream_t s);
+int launch_gemm(tmac_weight_s* w, const float* x, float* y, int64_t* acc_out, int M, cudaStream_t s);
 int register_int16(tmac_weight_s* w, const uint8_t* d_raw, cudaStream_t s);
 int launch_int16(const tmac_weight_s* w, const float* x, float* y, int64_t* row_acc, int64_t* unit_acc,
                  int batch, cudaStream_t s);

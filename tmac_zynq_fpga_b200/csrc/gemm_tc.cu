@@ -1,0 +1,370 @@
+// gemm_tc.cu -- the batched form of the NATIVE Q5_0 / Q4_K / Q6_K matmul on
+// the 5th-generation tensor cores: Y[M][N] = the GEMV of every one of M
+// activation rows, bit for bit (prefill; the reference has no batched path and
+// runs matmul_fpga_* once per token, sim/tmac_gguf.cpp:1992-2023).
+//
+// Exact int16 x int16 with 8-bit MMAs.  Each weight is the reference's int16
+// v (decoded once, gemv_blockq.cu planes_kernel) and each activation the int16
+// x_q of its row (tmac_gguf.cpp:889-896); both are split into a signed high
+// byte and an unsigned low byte, v = 256*vh + vl, x = 256*xh + xl, and
+//   sum v*x = 65536 * sum vh*xh + 256 * (sum vh*xl + sum vl*xh) + sum vl*xl
+// with four tcgen05.mma kind::i8 products accumulating in three int32 TMEM
+// accumulators (each stays below 2^31 for K <= 32768).  The epilogue forms the
+// int64 row sum and y = (float)((double)acc * x_scale / (double)row_inv)
+// exactly as the GEMV does.
+//
+// Tile 128 (rows of X) x 128 (weight rows) x 128 (K bytes); operands staged by
+// TMA (128-byte swizzle, out-of-range rows and columns read as zero) through a
+// 3-stage mbarrier ring.  Warp 0 issues the copies, warp 1 owns TMEM and issues
+// the MMAs, warps 2-5 read the accumulators (each warp its 32 TMEM lanes).
+#include "common.cuh"
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <mutex>
+#include <vector>
+
+namespace tmac {
+namespace {
+
+constexpr int BM = 128, BN = 128, BK = 128, STAGES = 3;
+constexpr uint32_t kTile = BM * BK;            // bytes of one operand tile (BM == BN)
+constexpr uint32_t kStageBytes = 4 * kTile;    // xh, xl, wh, wl
+constexpr int kThreads = 192;
+constexpr uint32_t kTmemCols = 512;            // hh [0,128) | mid [128,256) | ll [256,384)
+constexpr size_t kSmem = STAGES * kStageBytes + 1024 + 256;
+
+struct GemmArgs {
+    const float* xs;       // [M] x_scale of each activation row
+    const float* row_inv;  // [N]
+    float* y;              // [M][N]
+    int64_t* acc_out;      // optional [M][N] int64 row sums
+    int M, N, K;
+    int* err;
+};
+
+// ------------------------------------------------------------ PTX helpers --
+TMAC_DEV void tma_load_2d(void* dst, const CUtensorMap* tm, int x, int y, uint64_t* bar)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(smem_addr(bar))
+        : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row atoms of
+// 128 bytes (stride 1024 bytes), sm_100 descriptor version 1.
+TMAC_DEV uint64_t desc_sw128(uint32_t saddr)
+{
+    uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)1 << 16;              // leading byte offset (16 B; unused when swizzled)
+    d |= (uint64_t)(1024 >> 4) << 32;    // stride byte offset
+    d |= (uint64_t)1 << 46;              // version
+    d |= (uint64_t)2 << 61;              // SWIZZLE_128B
+    return d;
+}
+
+// Instruction descriptor for kind::i8: s32 accumulate, A/B signed (1) or
+// unsigned (0), both K-major, M = 128, N = 128.
+__host__ __device__ constexpr uint32_t idesc_i8(uint32_t a_signed, uint32_t b_signed)
+{
+    return (2u << 4) | (a_signed << 7) | (b_signed << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
+TMAC_DEV void mma_i8(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate)
+{
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
+}
+
+TMAC_DEV void mma_commit(uint64_t* bar)
+{
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+                 : "memory");
+}
+TMAC_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+TMAC_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+TMAC_DEV void tmem_ld16(uint32_t taddr, uint32_t (&r)[16])
+{
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+TMAC_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// ----------------------------------------------------------------- kernel --
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_i8x4_kernel(const __grid_constant__ CUtensorMap tm_xh, const __grid_constant__ CUtensorMap tm_xl,
+                     const __grid_constant__ CUtensorMap tm_wh, const __grid_constant__ CUtensorMap tm_wl, GemmArgs a)
+{
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * kStageBytes);
+    uint64_t* empty = full + STAGES;
+    uint64_t* done = empty + STAGES;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    volatile int* abort_s = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
+    const int KB = (a.K + BK - 1) / BK;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < STAGES; i++) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 1);
+        }
+        mbar_init(done, 1);
+        *abort_s = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
+                     "r"(kTmemCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            for (int kb = 0; kb < KB; kb++) {
+                const int s = kb % STAGES;
+                if (kb >= STAGES && !mbar_wait_bounded(&empty[s], ((kb / STAGES) - 1) & 1, a.err)) {
+                    *abort_s = 1;
+                    break;
+                }
+                if (*abort_s) break;
+                uint8_t* st = smem + s * kStageBytes;
+                mbar_arrive_expect_tx(&full[s], kStageBytes);
+                tma_load_2d(st, &tm_xh, kb * BK, m0, &full[s]);
+                tma_load_2d(st + kTile, &tm_xl, kb * BK, m0, &full[s]);
+                tma_load_2d(st + 2 * kTile, &tm_wh, kb * BK, n0, &full[s]);
+                tma_load_2d(st + 3 * kTile, &tm_wl, kb * BK, n0, &full[s]);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t kHH = idesc_i8(1, 1), kHL = idesc_i8(1, 0), kLH = idesc_i8(0, 1), kLL = idesc_i8(0, 0);
+            for (int kb = 0; kb < KB; kb++) {
+                const int s = kb % STAGES;
+                if (*abort_s || !mbar_wait_bounded(&full[s], (kb / STAGES) & 1, a.err)) {
+                    *abort_s = 1;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t st = smem_addr(smem + s * kStageBytes);
+#pragma unroll
+                for (int kk = 0; kk < BK / 32; kk++) {  // 32 bytes of K per MMA
+                    const uint64_t xh = desc_sw128(st + kk * 32), xl = desc_sw128(st + kTile + kk * 32);
+                    const uint64_t wh = desc_sw128(st + 2 * kTile + kk * 32), wl = desc_sw128(st + 3 * kTile + kk * 32);
+                    const uint32_t acc = (kb | kk) != 0;
+                    mma_i8(tmem, xh, wh, kHH, acc);
+                    mma_i8(tmem + 128, xh, wl, kHL, acc);
+                    mma_i8(tmem + 128, xl, wh, kLH, 1u);
+                    mma_i8(tmem + 256, xl, wl, kLL, acc);
+                }
+                mma_commit(&empty[s]);  // the stage is free once these MMAs have read it
+            }
+            mma_commit(done);  // completes when every MMA issued above has
+        }
+    } else {
+        // epilogue: warp w reads TMEM lanes 32*(w%4) .. +31, one activation row per thread
+        const bool ok = mbar_wait_bounded(done, 0, a.err);
+        tc_fence_after();
+        const int q = warp & 3, row = q * 32 + lane, m = m0 + row;
+        const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16);
+        const double xsd = (m < a.M) ? (double)a.xs[m] : 0.0;
+        for (int c = 0; c < BN; c += 16) {
+            uint32_t hh[16], md[16], ll[16];
+            tmem_ld16(taddr + c, hh);
+            tmem_ld16(taddr + 128 + c, md);
+            tmem_ld16(taddr + 256 + c, ll);
+            tmem_wait_ld();
+            if (!ok || *abort_s || m >= a.M) continue;
+#pragma unroll
+            for (int j = 0; j < 16; j++) {
+                const int n = n0 + c + j;
+                if (n >= a.N) break;
+                const long long acc = (long long)(int32_t)hh[j] * 65536 + (long long)(int32_t)md[j] * 256 +
+                                      (long long)(int32_t)ll[j];
+                const double v = __ddiv_rn(__dmul_rn((double)acc, xsd), (double)a.row_inv[n]);
+                a.y[(int64_t)m * a.N + n] = (float)v;
+                if (a.acc_out) a.acc_out[(int64_t)m * a.N + n] = acc;
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        if (*abort_s && lane == 0) mbar_wait_bounded(done, 0, nullptr);  // MMAs issued before an abort
+        __syncwarp();
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+    }
+}
+
+// Activation rows -> x_scale and byte planes (one CTA per row, tmac_gguf.cpp:889-896).
+__global__ void __launch_bounds__(256) quantize_rows_kernel(const float* __restrict__ x, int64_t K,
+                                                            int8_t* __restrict__ xh, uint8_t* __restrict__ xl,
+                                                            float* __restrict__ xs)
+{
+    __shared__ float red[8];
+    pdl_launch();
+    pdl_wait();
+    const float* xr = x + (int64_t)blockIdx.x * K;
+    float mx = 0.0f;
+    for (int64_t j = threadIdx.x; j < K; j += blockDim.x) mx = fmaxf(mx, fabsf(xr[j]));
+    mx = block_max(mx, red, blockDim.x);
+    const float s = x_scale_from_max(mx);
+    if (threadIdx.x == 0) xs[blockIdx.x] = s;
+    for (int64_t j = threadIdx.x; j < K; j += blockDim.x) {
+        const int16_t q = quantize_one(xr[j], s);
+        xh[(int64_t)blockIdx.x * K + j] = (int8_t)(q >> 8);
+        xl[(int64_t)blockIdx.x * K + j] = (uint8_t)(q & 0xFF);
+    }
+}
+
+// ------------------------------------------------------------------ host --
+// cuTensorMapEncodeTiled through the runtime's driver entry point, so the
+// library has no link-time dependency on libcuda.
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
+{
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+int encode_plane_map(CUtensorMap* tm, const void* base, int64_t rows, int64_t K)
+{
+    const auto encode = encode_fn();
+    if (!encode) return fail(TMAC_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)K};
+    const cuuint32_t box[2] = {BK, 128};
+    const cuuint32_t es[2] = {1, 1};
+    const CUresult r = encode(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims,
+                                              strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(TMAC_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+    return TMAC_OK;
+}
+
+struct GemmWorkspace {
+    int8_t* xh = nullptr;
+    uint8_t* xl = nullptr;
+    float* xs = nullptr;
+    size_t cap = 0, rows_cap = 0;
+};
+std::mutex g_gemm_mutex;
+std::vector<GemmWorkspace> g_gemm_ws;
+
+int gemm_workspace(int device, int64_t M, int64_t K, GemmWorkspace** out)
+{
+    std::lock_guard<std::mutex> lk(g_gemm_mutex);
+    if ((int)g_gemm_ws.size() <= device) g_gemm_ws.resize(device + 1);
+    GemmWorkspace& w = g_gemm_ws[device];
+    const size_t need = (size_t)(M * K);
+    if (w.cap < need) {
+        if (w.xh) cudaFree(w.xh);
+        if (w.xl) cudaFree(w.xl);
+        w.xh = nullptr;
+        w.xl = nullptr;
+        w.cap = 0;
+        TMAC_CUDA_TRY(cudaMalloc(&w.xh, need));
+        TMAC_CUDA_TRY(cudaMalloc(&w.xl, need));
+        w.cap = need;
+    }
+    if (w.rows_cap < (size_t)M) {
+        if (w.xs) cudaFree(w.xs);
+        w.xs = nullptr;
+        w.rows_cap = 0;
+        TMAC_CUDA_TRY(cudaMalloc(&w.xs, (size_t)M * sizeof(float)));
+        w.rows_cap = (size_t)M;
+    }
+    *out = &w;
+    return TMAC_OK;
+}
+
+}  // namespace
+
+// Exact int16 planes of the weight, decoded on first use.
+int gemm_prepare(tmac_weight_s* w, cudaStream_t s)
+{
+    if (w->gwh) return TMAC_OK;
+    const size_t n = (size_t)(w->rows * w->cols);
+    TMAC_CUDA_TRY(cudaMalloc(&w->gwh, n));
+    TMAC_CUDA_TRY(cudaMalloc(&w->gwl, n));
+    int rc = blockq_planes(w, reinterpret_cast<int8_t*>(w->gwh), reinterpret_cast<uint8_t*>(w->gwl), s);
+    if (rc) return rc;
+    return TMAC_OK;
+}
+
+int launch_gemm(tmac_weight_s* w, const float* x, float* y, int64_t* acc_out, int M, cudaStream_t s)
+{
+    int rc = gemm_prepare(w, s);
+    if (rc) return rc;
+    GemmWorkspace* ws = nullptr;
+    if ((rc = gemm_workspace(w->device, M, w->cols, &ws))) return rc;
+    TMAC_CUDA_TRY(launch_k(quantize_rows_kernel, dim3(M), dim3(256), 0, s, x, w->cols, ws->xh, ws->xl, ws->xs));
+    TMAC_CUDA_TRY(cudaGetLastError());
+    alignas(64) CUtensorMap tm[4];
+    if ((rc = encode_plane_map(&tm[0], ws->xh, M, w->cols)) || (rc = encode_plane_map(&tm[1], ws->xl, M, w->cols)) ||
+        (rc = encode_plane_map(&tm[2], w->gwh, w->rows, w->cols)) ||
+        (rc = encode_plane_map(&tm[3], w->gwl, w->rows, w->cols)))
+        return rc;
+    static bool attr[64] = {};
+    if (!attr[w->device & 63]) {
+        TMAC_CUDA_TRY(cudaFuncSetAttribute(gemm_i8x4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem));
+        attr[w->device & 63] = true;
+    }
+    GemmArgs a;
+    a.xs = ws->xs;
+    a.row_inv = w->row_norm;
+    a.y = y;
+    a.acc_out = acc_out;
+    a.M = M;
+    a.N = (int)w->rows;
+    a.K = (int)w->cols;
+    a.err = device_error_word(w->device);
+    const dim3 grid((unsigned)((w->rows + BN - 1) / BN), (unsigned)((M + BM - 1) / BM));
+    TMAC_CUDA_TRY(launch_k(gemm_i8x4_kernel, grid, dim3(kThreads), kSmem, s, tm[0], tm[1], tm[2], tm[3], a));
+    TMAC_CUDA_TRY(cudaGetLastError());
+    return TMAC_OK;
+}
+
+}  // namespace tmac
+
+using namespace tmac;
+
+extern "C" int tmac_gemm(tmac_weight_t w, const float* x, float* y, int64_t* row_acc, int m, void* stream)
+{
+    if (!w) return fail(TMAC_ERR_INVALID, "NULL weight handle");
+    if (!x || !y) return fail(TMAC_ERR_INVALID, "NULL x or y");
+    if (m <= 0) return fail(TMAC_ERR_SHAPE, "m must be positive");
+    if (w->mode != TMAC_MODE_NATIVE || w->type == TMAC_TYPE_Q8_0)
+        return fail(TMAC_ERR_TYPE, "tmac_gemm: NATIVE Q5_0 / Q4_K / Q6_K weights only");
+    if (w->cols % 16 || w->cols > 32768) return fail(TMAC_ERR_SHAPE, "tmac_gemm: cols must be a multiple of 16, <= 32768");
+    DeviceGuard dg(w->device);
+    if (!dg.ok) return fail(TMAC_ERR_CUDA, "cudaSetDevice failed");
+    return launch_gemm(w, x, y, row_acc, m, (cudaStream_t)stream);
+}

@@ -380,6 +380,45 @@ __global__ void exceptions_kernel(const uint8_t* __restrict__ data, const float*
     if (lane == 0 && cnt) cnt[row] = n;
 }
 
+// ------------------------------------------------------ exact int16 planes --
+// The reference's int16 weights v (exact decode) as byte planes for the tensor-
+// core GEMM: wh[row][col] = v >> 8 (signed), wl[row][col] = v & 0xFF.  One warp
+// per row, lane per chunk; rows at or beyond `rows` are left as they are.
+template <int TYPE>
+__global__ void planes_kernel(const uint8_t* __restrict__ data, const float* __restrict__ row_inv, int64_t rows,
+                              int64_t cols, int8_t* __restrict__ wh, uint8_t* __restrict__ wl)
+{
+    const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const int64_t nblk = cols / Geo<TYPE>::kBlockVals, cpr = cols / 32;
+    const GlobalBytes G{data + (row >> 3) * Geo<TYPE>::group_bytes(nblk)};
+    const float ri = row_inv[row];
+    for (int64_t ch = lane; ch < cpr; ch += 32) {
+        Chunk c;
+        load_chunk<TYPE>(G, (int)(row & 7), (uint32_t)nblk, (uint32_t)ch, c);
+        uint32_t hw[8], lw[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            uint32_t h = 0, l = 0;
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const int v = exact_value<TYPE>(c, 4 * i + k, ri);
+                h |= (uint32_t)((v >> 8) & 0xFF) << (8 * k);
+                l |= (uint32_t)(v & 0xFF) << (8 * k);
+            }
+            hw[i] = h;
+            lw[i] = l;
+        }
+        uint4* ph = reinterpret_cast<uint4*>(wh + row * cols + ch * 32);
+        uint4* pl = reinterpret_cast<uint4*>(wl + row * cols + ch * 32);
+        ph[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        ph[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
+        pl[0] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        pl[1] = make_uint4(lw[4], lw[5], lw[6], lw[7]);
+    }
+}
+
 // ------------------------------------------------------------------ GEMV --
 struct BqArgs {
     const uint8_t* data;     // grouped layout
@@ -842,6 +881,19 @@ int register_blockq(tmac_weight_s* w, const uint8_t* d_raw, cudaStream_t s)
     case TMAC_TYPE_Q6_K: return register_type<TMAC_TYPE_Q6_K>(w, d_raw, s);
     default: return fail(TMAC_ERR_TYPE, "register_blockq: unsupported type");
     }
+}
+
+int blockq_planes(const tmac_weight_s* w, int8_t* wh, uint8_t* wl, cudaStream_t s)
+{
+    const unsigned grid = (unsigned)((w->rows + 7) / 8);
+    switch (w->type) {
+    case TMAC_TYPE_Q5_0: planes_kernel<TMAC_TYPE_Q5_0><<<grid, 256, 0, s>>>(w->data, w->row_norm, w->rows, w->cols, wh, wl); break;
+    case TMAC_TYPE_Q4_K: planes_kernel<TMAC_TYPE_Q4_K><<<grid, 256, 0, s>>>(w->data, w->row_norm, w->rows, w->cols, wh, wl); break;
+    case TMAC_TYPE_Q6_K: planes_kernel<TMAC_TYPE_Q6_K><<<grid, 256, 0, s>>>(w->data, w->row_norm, w->rows, w->cols, wh, wl); break;
+    default: return fail(TMAC_ERR_TYPE, "blockq_planes: unsupported type");
+    }
+    TMAC_CUDA_TRY(cudaGetLastError());
+    return TMAC_OK;
 }
 
 int launch_blockq(const tmac_weight_s* w, const float* x, const int16_t* xq, const uint8_t* xp, const float* xs,

@@ -225,6 +225,8 @@ void free_weight(tmac_weight_s* w)
     if (w->row_norm) cudaFree(w->row_norm);
     if (w->exc_ptr) cudaFree(w->exc_ptr);
     if (w->exc) cudaFree(w->exc);
+    if (w->gwh) cudaFree(w->gwh);
+    if (w->gwl) cudaFree(w->gwl);
     delete w;
 }
 
