@@ -299,6 +299,18 @@ int tmac_model_buffers(tmac_model_t m, float** hidden, float** logits, uint64_t*
  * host float[(n_gen + 1) * 896]: after the prompt and after each step. */
 int tmac_model_generate(tmac_model_t m, const int* prompt, int n_prompt, int n_gen, int* out_tokens,
                         float* out_hidden, void* stream);
+/* Batched prefill (no reference counterpart: the reference feeds a prompt one
+ * token at a time, process_prompt, sim/tmac_gguf.cpp:1992-2023).  n_seq
+ * independent sequences of len tokens (host ids, [n_seq][len]) run through all
+ * layers at once with every projection on the tensor cores (tmac_gemm).  Each
+ * position's final hidden state equals what the decode engine computes after
+ * feeding that sequence's tokens up to it, bit for bit.  next_tokens (host
+ * [n_seq], optional) gets each sequence's greedy next token; hidden_out (host
+ * [n_seq][len][896], optional) every position's hidden state before
+ * output_norm.  Needs every matrix on its FPGA-core path (TMAC_SW_ALL) and
+ * len <= max_seq.  Synchronous. */
+int tmac_model_prefill(tmac_model_t m, const int* tokens, int n_seq, int len, int* next_tokens, float* hidden_out,
+                       void* stream);
 int tmac_model_free(tmac_model_t m);
 
 #ifdef __cplusplus

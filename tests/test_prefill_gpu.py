@@ -1,0 +1,49 @@
+"""Batched prefill (tmac_model_prefill) against the decode engine and the reference.
+
+Prefill runs n_seq sequences through all layers at once on the tensor cores;
+every per-token operation is the decode engine's, so each position's hidden
+state must equal the decode engine's after feeding the same tokens up to that
+position, bit for bit.  The decode engine itself matches the reference's
+greedy tokens (test_decode_gpu.py), so the first generated token after the
+fixture prompt must also be the reference's.
+"""
+import os
+
+import numpy as np
+import pytest
+
+import tmac_zynq_fpga_b200 as tm
+from tmac_zynq_fpga_b200 import model
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+FIX = os.path.join(HERE, "golden", "decode_greedy_seed0.npz")
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def mdl():
+    m = tm.Model(model.default_model_path(0), switches=tm.SW_ALL, max_seq=512)
+    yield m
+    m.free()
+
+
+def test_prefill_matches_decode_every_position(mdl):
+    g = np.load(FIX)
+    prompt = g["prompt"].astype(np.int32)
+    other = model.prompt_tokens(len(prompt), seed=5)
+    nxt, hid = mdl.prefill(np.stack([prompt, other]), want_hidden=True)
+    for p in range(len(prompt)):
+        _, h = mdl.generate(prompt[:p + 1], 0, want_hidden=True)
+        np.testing.assert_array_equal(hid[0, p], h[0], err_msg=f"position {p}")
+    toks, _ = mdl.generate(other, 1)
+    assert nxt[1] == toks[0]
+    assert nxt[0] == g["tokens"][0]  # the reference's first greedy token
+
+
+def test_prefill_sequences_are_independent(mdl):
+    a = model.prompt_tokens(24, seed=11)
+    b = model.prompt_tokens(24, seed=12)
+    n2, h2 = mdl.prefill(np.stack([a, b]), want_hidden=True)
+    n1, h1 = mdl.prefill(b[None, :], want_hidden=True)
+    assert n2[1] == n1[0]
+    np.testing.assert_array_equal(h2[1], h1[0])

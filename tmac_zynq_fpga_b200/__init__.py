@@ -352,6 +352,7 @@ class Model:
         for n, args in (("tmac_model_create", [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.POINTER(_P)]),
                         ("tmac_model_load_tmac", [_P, ctypes.c_char_p]), ("tmac_model_finalize", [_P]),
                         ("tmac_model_reset", [_P, _P]), ("tmac_model_forward", [_P, ctypes.c_int, ctypes.c_int, _P]),
+                        ("tmac_model_prefill", [_P, _P, ctypes.c_int, ctypes.c_int, _P, _P, _P]),
                         ("tmac_model_logits", [_P, _P]), ("tmac_model_buffers", [_P, _P, _P, _P]),
                         ("tmac_model_generate", [_P, _P, ctypes.c_int, ctypes.c_int, _P, _P, _P]),
                         ("tmac_model_free", [_P])):
@@ -371,6 +372,18 @@ class Model:
         check(lib().tmac_model_generate(self.handle, prompt.ctypes.data, len(prompt), n_gen, toks.ctypes.data,
                                         None if hid is None else hid.ctypes.data, s))
         return toks, hid
+
+    def prefill(self, tokens, want_hidden=False, stream=None):
+        """Batched prefill of tokens [n_seq][len]: (next greedy token per sequence,
+        hidden states [n_seq][len][896] or None)."""
+        tokens = np.ascontiguousarray(np.atleast_2d(tokens), dtype=np.int32)
+        n_seq, ln = tokens.shape
+        nxt = np.zeros(n_seq, np.int32)
+        hid = np.zeros((n_seq, ln, 896), np.float32) if want_hidden else None
+        s = None if stream is None else (stream if isinstance(stream, int) else stream.cuda_stream)
+        check(lib().tmac_model_prefill(self.handle, tokens.ctypes.data, n_seq, ln, nxt.ctypes.data,
+                                       None if hid is None else hid.ctypes.data, s))
+        return nxt, hid
 
     def free(self):
         if getattr(self, "handle", None):

@@ -251,6 +251,32 @@ int blockq_planes(const tmac_weight_s* w, int8_t* wh, uint8_t* wl, cudaStream_t 
 // Tensor-core GEMM (gemm_tc.cu): Y[m][rows] = the GEMV of each of m fp32 rows.
 int gemm_prepare(tmac_weight_s* w, cudaStream_t s);
 int launch_gemm(tmac_weight_s* w, const float* x, float* y, int64_t* acc_out, int M, cudaStream_t s);
+// Activation rows -> x_scale and byte planes (x_q = 256*xh + xl).
+int quantize_rows(const float* x, int64_t K, int M, int8_t* xh, uint8_t* xl, float* xs, cudaStream_t s);
+// One GEMM over byte planes: columns [k_off, k_off + K) of X [M][x_stride] and
+// W [N][w_stride]; mode 0: y[m][n] = acc * xs[m] / row_param[n] (block-quant
+// row_inv); mode 1: y[m][n] = (float)(y[m][n] + acc * xs[m] * row_param[n]) (one
+// 64-column tile of the Q8_0 fold, row_param = row_scale).
+struct GemmOperands {
+    const uint8_t *xh = nullptr, *xl = nullptr;
+    int64_t x_stride = 0;
+    const float* xs = nullptr;
+    int M = 0;
+    const uint8_t *wh = nullptr, *wl = nullptr;
+    int64_t w_stride = 0;
+    int N = 0;
+    int64_t K = 0, k_off = 0;
+    const float* row_param = nullptr;
+    int mode = 0;
+    float* y = nullptr;
+    int64_t y_stride = 0;
+    int64_t* acc_out = nullptr;
+    int device = 0;
+};
+int gemm_planes(const GemmOperands& op, cudaStream_t s);
+// Q8_0 weight (NATIVE layout) -> its int16 deq = (q * cs) >> 8 as byte planes
+// [rows][cols] (gemv_q8_0.cu).
+int q8_planes(const tmac_weight_s* w, int8_t* wh, uint8_t* wl, cudaStream_t s);
 int register_int16(tmac_weight_s* w, const uint8_t* d_raw, cudaStream_t s);
 int launch_int16(const tmac_weight_s* w, const float* x, float* y, int64_t* row_acc, int64_t* unit_acc,
                  int batch, cudaStream_t s);

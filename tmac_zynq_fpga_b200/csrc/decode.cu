@@ -15,7 +15,7 @@
 // expf/logf are evaluated as (float)exp((double)x) like glibc; any remaining
 // last-ulp difference is why decode parity is stated as identical greedy tokens
 // plus a hidden-state tolerance.
-#include "common.cuh"
+#include "model.cuh"
 
 #include <cmath>
 #include <cstdio>
@@ -27,14 +27,6 @@
 namespace tmac {
 namespace {
 
-constexpr int kHidden = 896, kInter = 4864, kVocab = 151936, kLayers = 24;
-constexpr int kHeads = 14, kKvHeads = 2, kHeadDim = 64, kKvDim = kKvHeads * kHeadDim;
-
-// glibc's expf / logf evaluate in double precision and round once, which makes
-// them correctly rounded in nearly all cases; doing the same here reproduces
-// the reference's values far more often than the single-precision intrinsics.
-TMAC_DEV float expf_ref(float x) { return (float)exp((double)x); }
-TMAC_DEV float logf_ref(float x) { return (float)log((double)x); }
 
 // ------------------------------------------------------------------ kernels
 // Embedding row of a Q8_0 token_embd (read_embedding / dequant_q8_0, :225-234,
@@ -244,41 +236,8 @@ __global__ void __launch_bounds__(1024) silu_mul_kernel(float* __restrict__ g, c
     for (int i = threadIdx.x; i < n; i += blockDim.x) store_xq(xq, xp, n, i, quantize_one(g[i], s));
 }
 
-// ----------------------------------------------------------------- the model
-struct HostTensor {
-    int64_t rows = 0, cols = 0;
-    int type = 0;
-    std::vector<uint8_t> data;
-};
-
 }  // namespace
 }  // namespace tmac
-
-struct tmac_model_s {
-    int device = 0, switches = 0, max_seq = 0;
-    std::map<std::string, tmac::HostTensor> host;  // until finalize
-    bool final = false;
-    // device state
-    std::map<std::string, tmac_weight_t> mats;
-    std::map<std::string, float*> vecs;
-    uint8_t* emb_raw = nullptr;
-    float *hidden = nullptr, *xn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *ctx = nullptr,
-          *attn = nullptr, *gate = nullptr, *up = nullptr, *ffn = nullptr, *logits = nullptr;
-    float *kcache = nullptr, *vcache = nullptr, *rope_c = nullptr, *rope_s = nullptr;
-    unsigned long long* key = nullptr;
-    int* token_log = nullptr;
-    int16_t* xq = nullptr;  // quantised activations shared by several matmuls
-    uint8_t* xp = nullptr;  // the same x_q as byte planes (block-quant GEMVs)
-    float* xs = nullptr;
-    // graph-driven generation: position, token and hidden-state logs on the device
-    int* pos_dev = nullptr;
-    int* tokens = nullptr;        // [max_seq]
-    float* hidden_log = nullptr;  // [max_seq][896]
-    cudaStream_t stream = nullptr;
-    cudaGraphExec_t g_prompt = nullptr, g_gen = nullptr;
-    int graph_n_prompt = -1;
-    std::vector<void*> allocs;
-};
 
 namespace tmac {
 namespace {
@@ -293,20 +252,7 @@ int mode_for(int switches, int type)
     return TMAC_MODE_INT16;
 }
 
-template <typename T>
-int dev_alloc(tmac_model_s* m, T** p, size_t n)
-{
-    TMAC_CUDA_TRY(cudaMalloc((void**)p, n * sizeof(T)));
-    m->allocs.push_back(*p);
-    return TMAC_OK;
-}
 
-std::string lname(int l, const char* suffix)
-{
-    char b[128];
-    snprintf(b, sizeof(b), "blk.%d.%s", l, suffix);
-    return b;
-}
 
 // y = W.x; when the activation was already quantised (xq) and W runs a
 // NATIVE kernel, the kernel reads x_q instead of quantising x again.
@@ -323,11 +269,6 @@ int gemv(tmac_model_s* m, const std::string& name, const float* x, float* y, cud
     return tmac_gemv(it->second, x, y, 1, s);
 }
 
-const float* vec_or_null(tmac_model_s* m, const std::string& name)
-{
-    auto it = m->vecs.find(name);
-    return it == m->vecs.end() ? nullptr : it->second;
-}
 
 const float* next_norm(tmac_model_s* m, int l)
 {
@@ -671,6 +612,7 @@ int tmac_model_free(tmac_model_t m)
     if (m->g_prompt) cudaGraphExecDestroy(m->g_prompt);
     if (m->g_gen) cudaGraphExecDestroy(m->g_gen);
     if (m->stream) cudaStreamDestroy(m->stream);
+    prefill_free(m);
     for (auto& kv : m->mats) tmac_weight_free(kv.second);
     for (void* p : m->allocs) cudaFree(p);
     delete m;

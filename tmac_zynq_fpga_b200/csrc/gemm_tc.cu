@@ -37,11 +37,13 @@ constexpr uint32_t kTmemCols = 512;            // hh [0,128) | mid [128,256) | l
 constexpr size_t kSmem = STAGES * kStageBytes + 1024 + 256;
 
 struct GemmArgs {
-    const float* xs;       // [M] x_scale of each activation row
-    const float* row_inv;  // [N]
-    float* y;              // [M][N]
-    int64_t* acc_out;      // optional [M][N] int64 row sums
+    const float* xs;         // [M] x_scale of each activation row
+    const float* row_param;  // [N] row_inv (mode 0) or row_scale (mode 1)
+    float* y;                // [M][y_stride]
+    int64_t* acc_out;        // optional [M][N] int64 sums
+    int64_t y_stride;
     int M, N, K;
+    int mode;                // 0: y = acc*xs/row_inv   1: y = (float)(y + acc*xs*row_scale)
     int* err;
 };
 
@@ -199,8 +201,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (n >= a.N) break;
                 const long long acc = (long long)(int32_t)hh[j] * 65536 + (long long)(int32_t)md[j] * 256 +
                                       (long long)(int32_t)ll[j];
-                const double v = __ddiv_rn(__dmul_rn((double)acc, xsd), (double)a.row_inv[n]);
-                a.y[(int64_t)m * a.N + n] = (float)v;
+                float* yp = a.y + (int64_t)m * a.y_stride + n;
+                if (a.mode == 0) {
+                    *yp = (float)__ddiv_rn(__dmul_rn((double)acc, xsd), (double)a.row_param[n]);
+                } else {  // one 64-column tile of the Q8_0 fold (gemv_q8_0.cu)
+                    const double v = __dmul_rn(__dmul_rn((double)acc, xsd), (double)a.row_param[n]);
+                    *yp = (float)__dadd_rn((double)*yp, v);
+                }
                 if (a.acc_out) a.acc_out[(int64_t)m * a.N + n] = acc;
             }
         }
@@ -219,6 +226,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 __global__ void __launch_bounds__(256) quantize_rows_kernel(const float* __restrict__ x, int64_t K,
                                                             int8_t* __restrict__ xh, uint8_t* __restrict__ xl,
                                                             float* __restrict__ xs)
+
 {
     __shared__ float red[8];
     pdl_launch();
@@ -253,12 +261,12 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
     return fn;
 }
 
-int encode_plane_map(CUtensorMap* tm, const void* base, int64_t rows, int64_t K)
+int encode_plane_map(CUtensorMap* tm, const void* base, int64_t rows, int64_t K, int64_t stride)
 {
     const auto encode = encode_fn();
     if (!encode) return fail(TMAC_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
     const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
-    const cuuint64_t strides[1] = {(cuuint64_t)K};
+    const cuuint64_t strides[1] = {(cuuint64_t)stride};
     const cuuint32_t box[2] = {BK, 128};
     const cuuint32_t es[2] = {1, 1};
     const CUresult r = encode(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims,
@@ -319,37 +327,70 @@ int gemm_prepare(tmac_weight_s* w, cudaStream_t s)
     return TMAC_OK;
 }
 
+int quantize_rows(const float* x, int64_t K, int M, int8_t* xh, uint8_t* xl, float* xs, cudaStream_t s)
+{
+    TMAC_CUDA_TRY(launch_k(quantize_rows_kernel, dim3(M), dim3(256), 0, s, x, K, xh, xl, xs));
+    TMAC_CUDA_TRY(cudaGetLastError());
+    return TMAC_OK;
+}
+
+int gemm_planes(const GemmOperands& op, cudaStream_t s)
+{
+    alignas(64) CUtensorMap tm[4];
+    int rc;
+    if ((rc = encode_plane_map(&tm[0], op.xh + op.k_off, op.M, op.K, op.x_stride)) ||
+        (rc = encode_plane_map(&tm[1], op.xl + op.k_off, op.M, op.K, op.x_stride)) ||
+        (rc = encode_plane_map(&tm[2], op.wh + op.k_off, op.N, op.K, op.w_stride)) ||
+        (rc = encode_plane_map(&tm[3], op.wl + op.k_off, op.N, op.K, op.w_stride)))
+        return rc;
+    static bool attr[64] = {};
+    if (!attr[op.device & 63]) {
+        TMAC_CUDA_TRY(cudaFuncSetAttribute(gemm_i8x4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem));
+        attr[op.device & 63] = true;
+    }
+    GemmArgs a;
+    a.xs = op.xs;
+    a.row_param = op.row_param;
+    a.y = op.y;
+    a.acc_out = op.acc_out;
+    a.y_stride = op.y_stride;
+    a.M = op.M;
+    a.N = op.N;
+    a.K = (int)op.K;
+    a.mode = op.mode;
+    a.err = device_error_word(op.device);
+    const dim3 grid((unsigned)((op.N + BN - 1) / BN), (unsigned)((op.M + BM - 1) / BM));
+    TMAC_CUDA_TRY(launch_k(gemm_i8x4_kernel, grid, dim3(kThreads), kSmem, s, tm[0], tm[1], tm[2], tm[3], a));
+    TMAC_CUDA_TRY(cudaGetLastError());
+    return TMAC_OK;
+}
+
 int launch_gemm(tmac_weight_s* w, const float* x, float* y, int64_t* acc_out, int M, cudaStream_t s)
 {
     int rc = gemm_prepare(w, s);
     if (rc) return rc;
     GemmWorkspace* ws = nullptr;
     if ((rc = gemm_workspace(w->device, M, w->cols, &ws))) return rc;
-    TMAC_CUDA_TRY(launch_k(quantize_rows_kernel, dim3(M), dim3(256), 0, s, x, w->cols, ws->xh, ws->xl, ws->xs));
-    TMAC_CUDA_TRY(cudaGetLastError());
-    alignas(64) CUtensorMap tm[4];
-    if ((rc = encode_plane_map(&tm[0], ws->xh, M, w->cols)) || (rc = encode_plane_map(&tm[1], ws->xl, M, w->cols)) ||
-        (rc = encode_plane_map(&tm[2], w->gwh, w->rows, w->cols)) ||
-        (rc = encode_plane_map(&tm[3], w->gwl, w->rows, w->cols)))
-        return rc;
-    static bool attr[64] = {};
-    if (!attr[w->device & 63]) {
-        TMAC_CUDA_TRY(cudaFuncSetAttribute(gemm_i8x4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem));
-        attr[w->device & 63] = true;
-    }
-    GemmArgs a;
-    a.xs = ws->xs;
-    a.row_inv = w->row_norm;
-    a.y = y;
-    a.acc_out = acc_out;
-    a.M = M;
-    a.N = (int)w->rows;
-    a.K = (int)w->cols;
-    a.err = device_error_word(w->device);
-    const dim3 grid((unsigned)((w->rows + BN - 1) / BN), (unsigned)((M + BM - 1) / BM));
-    TMAC_CUDA_TRY(launch_k(gemm_i8x4_kernel, grid, dim3(kThreads), kSmem, s, tm[0], tm[1], tm[2], tm[3], a));
-    TMAC_CUDA_TRY(cudaGetLastError());
-    return TMAC_OK;
+    if ((rc = quantize_rows(x, w->cols, M, ws->xh, ws->xl, ws->xs, s))) return rc;
+    GemmOperands op;
+    op.xh = reinterpret_cast<const uint8_t*>(ws->xh);
+    op.xl = ws->xl;
+    op.x_stride = w->cols;
+    op.xs = ws->xs;
+    op.M = M;
+    op.wh = reinterpret_cast<const uint8_t*>(w->gwh);
+    op.wl = reinterpret_cast<const uint8_t*>(w->gwl);
+    op.w_stride = w->cols;
+    op.N = (int)w->rows;
+    op.K = w->cols;
+    op.k_off = 0;
+    op.row_param = w->row_norm;
+    op.mode = 0;
+    op.y = y;
+    op.y_stride = w->rows;
+    op.acc_out = acc_out;
+    op.device = w->device;
+    return gemm_planes(op, s);
 }
 
 }  // namespace tmac

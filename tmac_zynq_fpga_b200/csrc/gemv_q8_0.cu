@@ -153,6 +153,31 @@ __global__ void q8_pack_kernel(const uint8_t* __restrict__ raw, int64_t rows, in
     }
 }
 
+// deq = (q * cs) >> 8 of every weight (the int16 the reference multiplies,
+// fpga_sim.hpp:322-349) as byte planes for the tensor-core GEMM; one thread
+// per (row, 16-column chunk) of the packed layout.
+__global__ void q8_planes_kernel(const uint8_t* __restrict__ packed, Q8Layout L, int64_t rows, int64_t cols,
+                                 int8_t* __restrict__ wh, uint8_t* __restrict__ wl)
+{
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // (row, chunk of 16 columns)
+    const int64_t chunks = cols / 16;
+    if (i >= rows * chunks) return;
+    const int64_t r = i / chunks, c0 = (i % chunks) * 16;
+    const int64_t g = r / 32;
+    const int l = (int)(r % 32), t = (int)(c0 / 64), j = (int)((c0 % 64) / 16);
+    const uint8_t* rec = packed + g * L.group_bytes;
+    const uint4 qv = reinterpret_cast<const uint4*>(rec)[((int64_t)t * 4 + j) * 32 + l];
+    const uint32_t cs2 = reinterpret_cast<const uint32_t*>(rec + L.cs_off())[t * 32 + l];
+    const int cs = (int)((cs2 >> (16 * (j >> 1))) & 0xFFFFu);
+    const uint8_t* qb = reinterpret_cast<const uint8_t*>(&qv);
+    for (int b = 0; b < 16; b++) {
+        const int q = (int)(int8_t)(qb[b] ^ 0x80);
+        const int deq = (q * cs) >> 8;
+        wh[r * cols + c0 + b] = (int8_t)(deq >> 8);
+        wl[r * cols + c0 + b] = (uint8_t)(deq & 0xFF);
+    }
+}
+
 // -------------------------------------------------------------- the GEMV --
 struct Q8Args {
     const uint8_t* packed;
@@ -441,6 +466,16 @@ int register_q8_0(tmac_weight_s* w, const uint8_t* d_raw, const float* d_row_max
     TMAC_CUDA_TRY(cudaGetLastError());
     dim3 grid(L.T, (unsigned)L.groups);
     q8_pack_kernel<<<grid, 192, 0, s>>>(d_raw, w->rows, w->cols, w->row_norm, L, w->data);
+    TMAC_CUDA_TRY(cudaGetLastError());
+    return TMAC_OK;
+}
+
+int q8_planes(const tmac_weight_s* w, int8_t* wh, uint8_t* wl, cudaStream_t s)
+{
+    if (w->cols % 16) return fail(TMAC_ERR_SHAPE, "q8_planes: cols must be a multiple of 16");
+    const Q8Layout L = q8_layout(w->rows, w->cols);
+    const int64_t n = w->rows * (w->cols / 16);
+    q8_planes_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(w->data, L, w->rows, w->cols, wh, wl);
     TMAC_CUDA_TRY(cudaGetLastError());
     return TMAC_OK;
 }

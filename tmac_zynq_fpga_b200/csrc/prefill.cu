@@ -1,0 +1,464 @@
+// prefill.cu -- batched prefill of the Qwen2-0.5B-shaped model: n_seq
+// independent sequences of len tokens go through all 24 layers at once, every
+// projection as one tensor-core GEMM over all n_seq*len rows (gemm_tc.cu).
+//
+// The reference has no batched path: process_prompt (sim/tmac_gguf.cpp:1992-2023)
+// feeds the prompt one token at a time through forward_layer_with_cache
+// (:1559-1711).  Every per-token operation here is the decode engine's
+// (decode.cu), in the same fp32 operation order:
+//   embedding  dequant_q8_0 row                      (:225-234, :413-427)
+//   rms_norm   sequential sum of squares             (:447-454)
+//   matmuls    x_q per row, exact int16 weights      (a3-a5 / a2, as the GEMVs)
+//   rope       adjacent pairs, host cos/sin tables   (:1528-1554)
+//   attention  causal over the sequence's positions  (:1625-1660)
+//   silu       x / (1 + expf(-x)) * up               (:459-461)
+// so position t of a sequence gets the hidden state the decode engine computes
+// after feeding tokens 0..t, bit for bit.  After the last layer the last
+// position of each sequence goes through output_norm and the tied Q8_0 logits;
+// its top-1 is the first generated token.
+#include "model.cuh"
+
+#include <cstring>
+
+namespace tmac {
+
+struct PrefillState {
+    int64_t cap = 0;  // tokens the buffers hold
+    float *hidden = nullptr, *qkv = nullptr, *qr = nullptr, *kr = nullptr, *vr = nullptr, *ctx = nullptr,
+          *attn = nullptr, *gu = nullptr, *ffn = nullptr, *xlast = nullptr, *logits = nullptr;
+    int8_t* xh = nullptr;  // byte planes of the current matmul input [cap][kInter]
+    uint8_t* xl = nullptr;
+    float* xs = nullptr;
+    int* tokens = nullptr;
+    unsigned long long* keys = nullptr;
+    int64_t cap_seq = 0;
+    std::map<std::string, std::pair<int8_t*, uint8_t*>> q8planes;  // Q8_0 matrices (attn_v)
+    std::vector<void*> allocs;
+};
+
+namespace {
+
+constexpr int kQkv = kHidden + 2 * kKvDim;  // 1152
+
+// ------------------------------------------------------------------ kernels
+__global__ void pf_embed_kernel(const uint8_t* __restrict__ emb, const int* __restrict__ tokens,
+                                float* __restrict__ hidden)
+{
+    const int64_t t = blockIdx.x;
+    int tok = tokens[t];
+    if (tok < 0 || tok >= kVocab) tok = 0;
+    for (int i = threadIdx.x; i < kHidden; i += blockDim.x) {
+        const int64_t idx = (int64_t)tok * kHidden + i;
+        const uint8_t* b = emb + (idx / 32) * 34;
+        hidden[t * kHidden + i] = __fmul_rn((float)(int8_t)b[2 + idx % 32], f16_bits_to_f32(ld_u16_unaligned(b)));
+    }
+}
+
+// One warp per token: x += delta (written back), rms_norm with weights w, then
+// x_q of the normalised row as byte planes.  Rows whose position is the last
+// of a sequence also store the normalised fp32 row in xlast[seq] (logits).
+__global__ void __launch_bounds__(256) pf_rmsnorm_kernel(float* __restrict__ hidden, const float* __restrict__ delta,
+                                                         const float* __restrict__ w, int64_t M,
+                                                         int8_t* __restrict__ xh, uint8_t* __restrict__ xl,
+                                                         float* __restrict__ xs, float* __restrict__ xlast, int len)
+{
+    __shared__ __align__(16) float buf[8][kHidden];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t t = (int64_t)blockIdx.x * 8 + warp;
+    if (t >= M) return;
+    float* x = hidden + t * kHidden;
+    float* v = buf[warp];
+    for (int i = lane; i < kHidden; i += 32) {
+        float a = x[i];
+        if (delta) {
+            a = __fadd_rn(a, delta[t * kHidden + i]);
+            x[i] = a;
+        }
+        v[i] = a;
+    }
+    __syncwarp();
+    float scale = 1.0f;
+    if (w) {
+        if (lane == 0) {
+            float sum = 0.0f;
+            const float4* v4 = reinterpret_cast<const float4*>(v);
+            for (int i = 0; i < kHidden / 4; i += 8) {  // loads ahead of the sequential adds
+                float4 f[8];
+#pragma unroll
+                for (int u = 0; u < 8; u++) f[u] = v4[i + u];
+#pragma unroll
+                for (int u = 0; u < 8; u++) {
+                    sum = __fadd_rn(sum, __fmul_rn(f[u].x, f[u].x));
+                    sum = __fadd_rn(sum, __fmul_rn(f[u].y, f[u].y));
+                    sum = __fadd_rn(sum, __fmul_rn(f[u].z, f[u].z));
+                    sum = __fadd_rn(sum, __fmul_rn(f[u].w, f[u].w));
+                }
+            }
+            const float mean = __fdiv_rn(sum, (float)kHidden);
+            scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, 1e-6f)));
+        }
+        scale = __shfl_sync(0xffffffffu, scale, 0);
+    }
+    const bool last = xlast && (t % len) == len - 1;
+    float mx = 0.0f;
+    for (int i = lane; i < kHidden; i += 32) {
+        const float o = w ? __fmul_rn(__fmul_rn(v[i], w[i]), scale) : v[i];
+        v[i] = o;
+        mx = fmaxf(mx, fabsf(o));
+        if (last) xlast[(t / len) * kHidden + i] = o;
+    }
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (!xh) return;
+    const float s = x_scale_from_max(mx);
+    if (lane == 0) xs[t] = s;
+    for (int i = lane; i < kHidden; i += 32) {
+        const int16_t q = quantize_one(v[i], s);
+        xh[t * kHidden + i] = (int8_t)(q >> 8);
+        xl[t * kHidden + i] = (uint8_t)(q & 0xFF);
+    }
+}
+
+// q/k bias + RoPE, v bias (the decode kernel's prologue), one CTA per token.
+__global__ void __launch_bounds__(kHidden / 2 + kKvDim / 2) pf_rope_kernel(
+    const float* __restrict__ qkv, const float* __restrict__ bq, const float* __restrict__ bk,
+    const float* __restrict__ bv, const float* __restrict__ cs, const float* __restrict__ sn, int len,
+    float* __restrict__ qr, float* __restrict__ kr, float* __restrict__ vr)
+{
+    const int64_t t = blockIdx.x;
+    const int pos = (int)(t % len);
+    const float* c = cs + (int64_t)pos * (kHeadDim / 2);
+    const float* sv = sn + (int64_t)pos * (kHeadDim / 2);
+    const float* row = qkv + t * kQkv;
+    const int j = threadIdx.x;  // pair j: q pairs 0..447, then k pairs 448..511
+    const bool isk = j >= kHidden / 2;
+    const int jj = isk ? j - kHidden / 2 : j;
+    const int d = 2 * jj, pr = (d % kHeadDim) / 2;
+    const float* vec = isk ? row + kHidden : row;
+    const float* b = isk ? bk : bq;
+    const float x0 = __fadd_rn(vec[d], b ? b[d] : 0.0f), x1 = __fadd_rn(vec[d + 1], b ? b[d + 1] : 0.0f);
+    const float y0 = __fsub_rn(__fmul_rn(x0, c[pr]), __fmul_rn(x1, sv[pr]));
+    const float y1 = __fadd_rn(__fmul_rn(x0, sv[pr]), __fmul_rn(x1, c[pr]));
+    float* dst = isk ? kr + t * kKvDim : qr + t * kHidden;
+    dst[d] = y0;
+    dst[d + 1] = y1;
+    if (j < kKvDim) vr[t * kKvDim + j] = __fadd_rn(row[kHidden + kKvDim + j], bv ? bv[j] : 0.0f);
+}
+
+// Causal attention, one warp per (token, query head): scores over positions
+// 0..pos of the token's sequence in d order, /8, log-sum-exp softmax with the
+// sums in position order, context in position order (decode.cu's
+// rope_attention_kernel, per token).
+constexpr int kAttnWarps = 4;
+__global__ void __launch_bounds__(kAttnWarps * 32) pf_attention_kernel(const float* __restrict__ qr,
+                                                                       const float* __restrict__ kr,
+                                                                       const float* __restrict__ vr, int64_t M,
+                                                                       int len, float* __restrict__ ctx)
+{
+    extern __shared__ float sm[];  // per warp: q[64], scores[len]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t item = (int64_t)blockIdx.x * kAttnWarps + warp;
+    if (item >= M * kHeads) return;
+    const int64_t t = item / kHeads;
+    const int h = (int)(item % kHeads), kvh = h / (kHeads / kKvHeads);
+    const int pos = (int)(t % len);
+    const int64_t t0 = t - pos;  // first token of the sequence
+    float* qs = sm + (int64_t)warp * (kHeadDim + len);
+    float* sc = qs + kHeadDim;
+    qs[lane] = qr[t * kHidden + h * kHeadDim + lane];
+    qs[lane + 32] = qr[t * kHidden + h * kHeadDim + lane + 32];
+    __syncwarp();
+    for (int p = lane; p <= pos; p += 32) {
+        const float4* kp = reinterpret_cast<const float4*>(kr + (t0 + p) * kKvDim + kvh * kHeadDim);
+        float sum = 0.0f;
+#pragma unroll
+        for (int d4 = 0; d4 < kHeadDim / 4; d4++) {
+            const float4 k4 = kp[d4];
+            sum = __fadd_rn(sum, __fmul_rn(qs[4 * d4], k4.x));
+            sum = __fadd_rn(sum, __fmul_rn(qs[4 * d4 + 1], k4.y));
+            sum = __fadd_rn(sum, __fmul_rn(qs[4 * d4 + 2], k4.z));
+            sum = __fadd_rn(sum, __fmul_rn(qs[4 * d4 + 3], k4.w));
+        }
+        sc[p] = __fdiv_rn(sum, 8.0f);
+    }
+    __syncwarp();
+    float mx = -INFINITY;
+    for (int p = lane; p <= pos; p += 32) mx = fmaxf(mx, sc[p]);
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    // exp terms in parallel, their sum in position order
+    for (int p = lane; p <= pos; p += 32) sc[p] = expf_ref(__fsub_rn(sc[p], mx));
+    __syncwarp();
+    float es = 0.0f;
+    if (lane == 0)
+        for (int p = 0; p <= pos; p++) es = __fadd_rn(es, sc[p]);
+    es = __shfl_sync(0xffffffffu, es, 0);
+    const float log_sum = __fadd_rn(logf_ref(es), mx);
+    __syncwarp();
+    // weights need the raw scores again: recompute them (same expression)
+    for (int p = lane; p <= pos; p += 32) {
+        const float4* kp = reinterpret_cast<const float4*>(kr + (t0 + p) * kKvDim + kvh * kHeadDim);
+        float sum = 0.0f;
+#pragma unroll
+        for (int d4 = 0; d4 < kHeadDim / 4; d4++) {
+            const float4 k4 = kp[d4];
+            sum = __fadd_rn(sum, __fmul_rn(qs[4 * d4], k4.x));
+            sum = __fadd_rn(sum, __fmul_rn(qs[4 * d4 + 1], k4.y));
+            sum = __fadd_rn(sum, __fmul_rn(qs[4 * d4 + 2], k4.z));
+            sum = __fadd_rn(sum, __fmul_rn(qs[4 * d4 + 3], k4.w));
+        }
+        sc[p] = expf_ref(__fsub_rn(__fdiv_rn(sum, 8.0f), log_sum));
+    }
+    __syncwarp();
+    const float* vb = vr + t0 * kKvDim + kvh * kHeadDim;
+    float a0 = 0.0f, a1 = 0.0f;
+    for (int p = 0; p <= pos; p++) {
+        const float wgt = sc[p];
+        a0 = __fadd_rn(a0, __fmul_rn(wgt, vb[(int64_t)p * kKvDim + lane]));
+        a1 = __fadd_rn(a1, __fmul_rn(wgt, vb[(int64_t)p * kKvDim + lane + 32]));
+    }
+    ctx[t * kHidden + h * kHeadDim + lane] = a0;
+    ctx[t * kHidden + h * kHeadDim + lane + 32] = a1;
+}
+
+// silu(gate) * up per token (one warp), then x_q of the row as byte planes.
+__global__ void __launch_bounds__(256) pf_silu_kernel(float* __restrict__ gu, int64_t M, int8_t* __restrict__ xh,
+                                                      uint8_t* __restrict__ xl, float* __restrict__ xs)
+{
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t t = (int64_t)blockIdx.x * 8 + warp;
+    if (t >= M) return;
+    float* g = gu + t * 2 * kInter;
+    const float* u = g + kInter;
+    float mx = 0.0f;
+    for (int i = lane; i < kInter; i += 32) {
+        const float x = g[i];
+        const float v = __fmul_rn(__fdiv_rn(x, __fadd_rn(1.0f, expf_ref(-x))), u[i]);
+        g[i] = v;
+        mx = fmaxf(mx, fabsf(v));
+    }
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const float s = x_scale_from_max(mx);
+    if (lane == 0) xs[t] = s;
+    __syncwarp();
+    for (int i = lane; i < kInter; i += 32) {
+        const int16_t q = quantize_one(g[i], s);
+        xh[t * kInter + i] = (int8_t)(q >> 8);
+        xl[t * kInter + i] = (uint8_t)(q & 0xFF);
+    }
+}
+
+// --------------------------------------------------------------------- host
+template <typename T>
+int ps_alloc(PrefillState* p, T** ptr, size_t n)
+{
+    TMAC_CUDA_TRY(cudaMalloc((void**)ptr, n * sizeof(T)));
+    p->allocs.push_back(*ptr);
+    return TMAC_OK;
+}
+
+int ensure_state(tmac_model_s* m, int64_t M, int n_seq)
+{
+    if (!m->prefill) m->prefill = new PrefillState();
+    PrefillState* p = m->prefill;
+    if (p->cap >= M && p->cap_seq >= n_seq) return TMAC_OK;
+    for (void* a : p->allocs) cudaFree(a);
+    p->allocs.clear();
+    p->cap = 0;
+    p->cap_seq = 0;
+    int rc;
+    if ((rc = ps_alloc(p, &p->hidden, (size_t)M * kHidden)) || (rc = ps_alloc(p, &p->qkv, (size_t)M * kQkv)) ||
+        (rc = ps_alloc(p, &p->qr, (size_t)M * kHidden)) || (rc = ps_alloc(p, &p->kr, (size_t)M * kKvDim)) ||
+        (rc = ps_alloc(p, &p->vr, (size_t)M * kKvDim)) || (rc = ps_alloc(p, &p->ctx, (size_t)M * kHidden)) ||
+        (rc = ps_alloc(p, &p->attn, (size_t)M * kHidden)) || (rc = ps_alloc(p, &p->gu, (size_t)M * 2 * kInter)) ||
+        (rc = ps_alloc(p, &p->ffn, (size_t)M * kHidden)) || (rc = ps_alloc(p, &p->xh, (size_t)M * kInter)) ||
+        (rc = ps_alloc(p, &p->xl, (size_t)M * kInter)) || (rc = ps_alloc(p, &p->xs, (size_t)M)) ||
+        (rc = ps_alloc(p, &p->tokens, (size_t)M)) || (rc = ps_alloc(p, &p->xlast, (size_t)n_seq * kHidden)) ||
+        (rc = ps_alloc(p, &p->logits, (size_t)n_seq * kVocab)) || (rc = ps_alloc(p, &p->keys, (size_t)n_seq)))
+        return rc;
+    p->cap = M;
+    p->cap_seq = n_seq;
+    return TMAC_OK;
+}
+
+// GEMM of the current planes (K columns) with a NATIVE block-quant weight into
+// y[M][y_stride] (columns [0, rows)).
+int pf_gemm(tmac_model_s* m, tmac_weight_s* w, int64_t M, int64_t K, float* y, int64_t y_stride, cudaStream_t s)
+{
+    if (w->cols != K) return fail(TMAC_ERR_SHAPE, "prefill: matrix width does not match its input");
+    int rc = gemm_prepare(w, s);
+    if (rc) return rc;
+    PrefillState* p = m->prefill;
+    GemmOperands op;
+    op.xh = reinterpret_cast<const uint8_t*>(p->xh);
+    op.xl = p->xl;
+    op.x_stride = K;
+    op.xs = p->xs;
+    op.M = (int)M;
+    op.wh = reinterpret_cast<const uint8_t*>(w->gwh);
+    op.wl = reinterpret_cast<const uint8_t*>(w->gwl);
+    op.w_stride = K;
+    op.N = (int)w->rows;
+    op.K = K;
+    op.row_param = w->row_norm;
+    op.mode = 0;
+    op.y = y;
+    op.y_stride = y_stride;
+    op.device = m->device;
+    return gemm_planes(op, s);
+}
+
+// Q8_0 matrix (attn_v of the Q8 layers): 64-column tiles folded in order into
+// y as the Q8 GEMV does, one GEMM launch per tile.
+int pf_gemm_q8(tmac_model_s* m, const std::string& name, tmac_weight_s* w, int64_t M, float* y, int64_t y_stride,
+               cudaStream_t s)
+{
+    PrefillState* p = m->prefill;
+    auto it = p->q8planes.find(name);
+    if (it == p->q8planes.end()) {
+        int8_t* wh = nullptr;
+        uint8_t* wl = nullptr;
+        int rc;
+        if ((rc = ps_alloc(p, &wh, (size_t)(w->rows * w->cols))) || (rc = ps_alloc(p, &wl, (size_t)(w->rows * w->cols))))
+            return rc;
+        if ((rc = q8_planes(w, wh, wl, s))) return rc;
+        it = p->q8planes.emplace(name, std::make_pair(wh, wl)).first;
+    }
+    // the fold starts from 0.0f: y = (float)(0.0 + tile 0), then the other tiles
+    for (int64_t r = 0; r < M; r += 65535) {
+        const int64_t rows = std::min<int64_t>(65535, M - r);
+        TMAC_CUDA_TRY(cudaMemset2DAsync(y + r * y_stride, y_stride * sizeof(float), 0, w->rows * sizeof(float), rows, s));
+    }
+    for (int64_t k0 = 0; k0 < w->cols; k0 += 64) {
+        GemmOperands op;
+        op.xh = reinterpret_cast<const uint8_t*>(p->xh);
+        op.xl = p->xl;
+        op.x_stride = w->cols;
+        op.xs = p->xs;
+        op.M = (int)M;
+        op.wh = reinterpret_cast<const uint8_t*>(it->second.first);
+        op.wl = it->second.second;
+        op.w_stride = w->cols;
+        op.N = (int)w->rows;
+        op.K = std::min<int64_t>(64, w->cols - k0);
+        op.k_off = k0;
+        op.row_param = w->row_norm;
+        op.mode = 1;
+        op.y = y;
+        op.y_stride = y_stride;
+        op.device = m->device;
+        int rc = gemm_planes(op, s);
+        if (rc) return rc;
+    }
+    return TMAC_OK;
+}
+
+tmac_weight_s* mat(tmac_model_s* m, const std::string& name)
+{
+    auto it = m->mats.find(name);
+    return it == m->mats.end() ? nullptr : it->second;
+}
+
+int prefill_run(tmac_model_s* m, int64_t M, int n_seq, int len, cudaStream_t s)
+{
+    PrefillState* p = m->prefill;
+    int rc;
+    pf_embed_kernel<<<(unsigned)M, 128, 0, s>>>(m->emb_raw, p->tokens, p->hidden);
+    TMAC_CUDA_TRY(cudaGetLastError());
+    const unsigned nblk8 = (unsigned)((M + 7) / 8);
+    const size_t attn_smem = (size_t)kAttnWarps * (kHeadDim + len) * sizeof(float);
+    static bool attr_done = false;
+    if (!attr_done) {
+        TMAC_CUDA_TRY(cudaFuncSetAttribute(pf_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024));
+        attr_done = true;
+    }
+    for (int l = 0; l < kLayers; l++) {
+        const float* an = vec_or_null(m, lname(l, "attn_norm.weight"));
+        const float* fn = vec_or_null(m, lname(l, "ffn_norm.weight"));
+        if (!an || !fn) return fail(TMAC_ERR_INVALID, "missing norm weights");
+        pf_rmsnorm_kernel<<<nblk8, 256, 0, s>>>(p->hidden, l == 0 ? nullptr : p->ffn, an, M, p->xh, p->xl, p->xs,
+                                               nullptr, len);
+        TMAC_CUDA_TRY(cudaGetLastError());
+        if (tmac_weight_s* w = mat(m, lname(l, "attn_qkv"))) {
+            if ((rc = pf_gemm(m, w, M, kHidden, p->qkv, kQkv, s))) return rc;
+        } else {
+            tmac_weight_s* qk = mat(m, lname(l, "attn_qk"));
+            tmac_weight_s* v = mat(m, lname(l, "attn_v.weight"));
+            if (!qk || !v) return fail(TMAC_ERR_INVALID, "missing attention matrices");
+            if ((rc = pf_gemm(m, qk, M, kHidden, p->qkv, kQkv, s))) return rc;
+            if (v->type == TMAC_TYPE_Q8_0) {
+                if ((rc = pf_gemm_q8(m, lname(l, "attn_v.weight"), v, M, p->qkv + kHidden + kKvDim, kQkv, s)))
+                    return rc;
+            } else if ((rc = pf_gemm(m, v, M, kHidden, p->qkv + kHidden + kKvDim, kQkv, s))) {
+                return rc;
+            }
+        }
+        pf_rope_kernel<<<(unsigned)M, kHidden / 2 + kKvDim / 2, 0, s>>>(
+            p->qkv, vec_or_null(m, lname(l, "attn_q.bias")), vec_or_null(m, lname(l, "attn_k.bias")),
+            vec_or_null(m, lname(l, "attn_v.bias")), m->rope_c, m->rope_s, len, p->qr, p->kr, p->vr);
+        TMAC_CUDA_TRY(cudaGetLastError());
+        pf_attention_kernel<<<(unsigned)((M * kHeads + kAttnWarps - 1) / kAttnWarps), kAttnWarps * 32, attn_smem, s>>>(
+            p->qr, p->kr, p->vr, M, len, p->ctx);
+        TMAC_CUDA_TRY(cudaGetLastError());
+        if ((rc = quantize_rows(p->ctx, kHidden, (int)M, p->xh, p->xl, p->xs, s))) return rc;
+        tmac_weight_s* wo = mat(m, lname(l, "attn_output.weight"));
+        if (!wo || (rc = pf_gemm(m, wo, M, kHidden, p->attn, kHidden, s))) return wo ? rc : fail(TMAC_ERR_INVALID, "missing attn_output");
+        pf_rmsnorm_kernel<<<nblk8, 256, 0, s>>>(p->hidden, p->attn, fn, M, p->xh, p->xl, p->xs, nullptr, len);
+        TMAC_CUDA_TRY(cudaGetLastError());
+        tmac_weight_s* gu = mat(m, lname(l, "ffn_gate_up"));
+        if (!gu || (rc = pf_gemm(m, gu, M, kHidden, p->gu, 2 * kInter, s))) return gu ? rc : fail(TMAC_ERR_INVALID, "missing ffn_gate_up");
+        pf_silu_kernel<<<nblk8, 256, 0, s>>>(p->gu, M, p->xh, p->xl, p->xs);
+        TMAC_CUDA_TRY(cudaGetLastError());
+        tmac_weight_s* wd = mat(m, lname(l, "ffn_down.weight"));
+        if (!wd || (rc = pf_gemm(m, wd, M, kInter, p->ffn, kHidden, s))) return wd ? rc : fail(TMAC_ERR_INVALID, "missing ffn_down");
+    }
+    // last residual, output_norm of every sequence's last position, logits + top-1
+    pf_rmsnorm_kernel<<<nblk8, 256, 0, s>>>(p->hidden, p->ffn, vec_or_null(m, "output_norm.weight"), M, nullptr,
+                                           nullptr, nullptr, p->xlast, len);
+    TMAC_CUDA_TRY(cudaGetLastError());
+    TMAC_CUDA_TRY(cudaMemsetAsync(p->keys, 0, n_seq * sizeof(unsigned long long), s));
+    return launch_q8_0(m->mats["token_embd.weight"], p->xlast, p->logits, nullptr, nullptr, n_seq, s, p->keys, 0);
+}
+
+}  // namespace
+
+void prefill_free(tmac_model_s* m)
+{
+    if (!m->prefill) return;
+    for (void* a : m->prefill->allocs) cudaFree(a);
+    delete m->prefill;
+    m->prefill = nullptr;
+}
+
+}  // namespace tmac
+
+using namespace tmac;
+
+extern "C" int tmac_model_prefill(tmac_model_t m, const int* tokens, int n_seq, int len, int* next_tokens,
+                                  float* hidden_out, void* stream)
+{
+    if (!m || !tokens) return fail(TMAC_ERR_INVALID, "NULL model or tokens");
+    if (!m->final) return fail(TMAC_ERR_INVALID, "model not finalized");
+    if (n_seq <= 0 || len <= 0 || len > m->max_seq) return fail(TMAC_ERR_SHAPE, "need 0 < len <= max_seq, n_seq > 0");
+    for (const auto& kv : m->mats)
+        if (kv.second->mode != TMAC_MODE_NATIVE)
+            return fail(TMAC_ERR_TYPE, "prefill needs every matrix on its FPGA-core path (all --fpga-* switches)");
+    DeviceGuard dg(m->device);
+    if (!dg.ok) return fail(TMAC_ERR_CUDA, "cudaSetDevice failed");
+    const int64_t M = (int64_t)n_seq * len;
+    int rc = ensure_state(m, M, n_seq);
+    if (rc) return rc;
+    cudaStream_t s = (cudaStream_t)stream;
+    PrefillState* p = m->prefill;
+    TMAC_CUDA_TRY(cudaMemcpyAsync(p->tokens, tokens, M * sizeof(int), cudaMemcpyHostToDevice, s));
+    if ((rc = prefill_run(m, M, n_seq, len, s))) return rc;
+    if (next_tokens) {
+        std::vector<unsigned long long> keys(n_seq);
+        TMAC_CUDA_TRY(cudaMemcpyAsync(keys.data(), p->keys, n_seq * sizeof(unsigned long long), cudaMemcpyDeviceToHost, s));
+        TMAC_CUDA_TRY(cudaStreamSynchronize(s));
+        for (int i = 0; i < n_seq; i++) next_tokens[i] = (int)(0x7FFFFFFFu - (uint32_t)(keys[i] & 0x7FFFFFFFu));
+    }
+    if (hidden_out) {
+        TMAC_CUDA_TRY(cudaMemcpyAsync(hidden_out, p->hidden, M * kHidden * sizeof(float), cudaMemcpyDeviceToHost, s));
+    }
+    TMAC_CUDA_TRY(cudaStreamSynchronize(s));
+    return TMAC_OK;
+}
