@@ -31,7 +31,8 @@ struct PrefillState {
     float* xs = nullptr;
     int* tokens = nullptr;
     unsigned long long* keys = nullptr;
-    int64_t cap_seq = 0;
+    float* scores = nullptr;  // [n_seq*heads*len][len]
+    int64_t cap_seq = 0, cap_scores = 0;
     std::map<std::string, std::pair<int8_t*, uint8_t*>> q8planes;  // Q8_0 matrices (attn_v)
     std::vector<void*> allocs;
 };
@@ -144,79 +145,131 @@ __global__ void __launch_bounds__(kHidden / 2 + kKvDim / 2) pf_rope_kernel(
     if (j < kKvDim) vr[t * kKvDim + j] = __fadd_rn(row[kHidden + kKvDim + j], bv ? bv[j] : 0.0f);
 }
 
-// Causal attention, one warp per (token, query head): scores over positions
-// 0..pos of the token's sequence in d order, /8, log-sum-exp softmax with the
-// sums in position order, context in position order (decode.cu's
-// rope_attention_kernel, per token).
-constexpr int kAttnWarps = 4;
-__global__ void __launch_bounds__(kAttnWarps * 32) pf_attention_kernel(const float* __restrict__ qr,
-                                                                       const float* __restrict__ kr,
-                                                                       const float* __restrict__ vr, int64_t M,
-                                                                       int len, float* __restrict__ ctx)
+// Causal attention in two passes, with K and V tiles in shared memory shared by
+// the 7 query heads of a KV head and a block of queries.  Every value is the
+// decode engine's (rope_attention_kernel) for that token: scores in d order /8,
+// max, exp terms summed in position order, log-sum-exp weights, context
+// accumulated in position order.
+constexpr int kQBlk = 32;                       // queries per CTA
+constexpr int kPTile = 64;                      // positions per K/V tile
+constexpr int kGroup = kHeads / kKvHeads;       // 7 query heads per KV head
+constexpr int kPairs = kGroup * kQBlk;          // (head, query) pairs per CTA
+constexpr size_t kScoresSmem = (size_t)(kPairs + kPTile) * (kHeadDim + 1) * sizeof(float);
+
+// S[(seq*kHeads + h)*len + t][p] = (q_t . k_p) / 8 for p <= t.
+__global__ void __launch_bounds__(256) pf_scores_kernel(const float* __restrict__ qr, const float* __restrict__ kr,
+                                                        int len, float* __restrict__ S)
 {
-    extern __shared__ float sm[];  // per warp: q[64], scores[len]
+    extern __shared__ float ssm[];
+    float(*qs)[kHeadDim + 1] = reinterpret_cast<float(*)[kHeadDim + 1]>(ssm);                 // [kPairs]
+    float(*ks)[kHeadDim + 1] = reinterpret_cast<float(*)[kHeadDim + 1]>(ssm + kPairs * (kHeadDim + 1));  // [kPTile]
+    const int seq = blockIdx.x, kvh = blockIdx.y, t0 = blockIdx.z * kQBlk;
+    const int nq = min(kQBlk, len - t0);
+    const int64_t base = (int64_t)seq * len;
+    for (int i = threadIdx.x; i < kPairs * kHeadDim; i += blockDim.x) {
+        const int pr = i / kHeadDim, d = i % kHeadDim, hh = pr / kQBlk, tq = pr % kQBlk;
+        qs[pr][d] = (tq < nq) ? qr[(base + t0 + tq) * kHidden + (kvh * kGroup + hh) * kHeadDim + d] : 0.0f;
+    }
+    const int tlast = t0 + nq - 1;
+    const int j = threadIdx.x & 15, sub = threadIdx.x >> 4;  // 16 threads per pair, 16 pairs per pass
+    for (int p0 = 0; p0 <= tlast; p0 += kPTile) {
+        __syncthreads();
+        for (int i = threadIdx.x; i < kPTile * kHeadDim; i += blockDim.x) {
+            const int pp = i / kHeadDim, d = i % kHeadDim;
+            ks[pp][d] = (p0 + pp < len) ? kr[(base + p0 + pp) * kKvDim + kvh * kHeadDim + d] : 0.0f;
+        }
+        __syncthreads();
+        for (int pr = sub; pr < kPairs; pr += 16) {
+            const int hh = pr / kQBlk, tq = pr % kQBlk, t = t0 + tq;
+            if (tq >= nq || p0 > t) continue;
+            float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll 8
+            for (int d = 0; d < kHeadDim; d++) {
+                const float q = qs[pr][d];
+#pragma unroll
+                for (int u = 0; u < 4; u++) acc[u] = __fadd_rn(acc[u], __fmul_rn(q, ks[j + 16 * u][d]));
+            }
+            float* row = S + ((int64_t)(seq * kHeads + kvh * kGroup + hh) * len + t) * len;
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int p = p0 + j + 16 * u;
+                if (p <= t) row[p] = __fdiv_rn(acc[u], 8.0f);
+            }
+        }
+    }
+}
+
+// Softmax and context: one CTA per (sequence, KV head, query block), 8 warps,
+// each warp owning kPairs / 8 (head, query) pairs.
+constexpr int kCtxWarps = 8, kPairsPerWarp = kPairs / kCtxWarps;
+__global__ void __launch_bounds__(kCtxWarps * 32) pf_softmax_ctx_kernel(const float* __restrict__ S,
+                                                                        const float* __restrict__ vr, int len,
+                                                                        float* __restrict__ ctx)
+{
+    extern __shared__ float dsm[];  // ex[kCtxWarps][len]
+    __shared__ float vs[kPTile][kHeadDim];
+    __shared__ float lsum[kPairs];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t item = (int64_t)blockIdx.x * kAttnWarps + warp;
-    if (item >= M * kHeads) return;
-    const int64_t t = item / kHeads;
-    const int h = (int)(item % kHeads), kvh = h / (kHeads / kKvHeads);
-    const int pos = (int)(t % len);
-    const int64_t t0 = t - pos;  // first token of the sequence
-    float* qs = sm + (int64_t)warp * (kHeadDim + len);
-    float* sc = qs + kHeadDim;
-    qs[lane] = qr[t * kHidden + h * kHeadDim + lane];
-    qs[lane + 32] = qr[t * kHidden + h * kHeadDim + lane + 32];
-    __syncwarp();
-    for (int p = lane; p <= pos; p += 32) {
-        const float4* kp = reinterpret_cast<const float4*>(kr + (t0 + p) * kKvDim + kvh * kHeadDim);
-        float sum = 0.0f;
-#pragma unroll
-        for (int d4 = 0; d4 < kHeadDim / 4; d4++) {
-            const float4 k4 = kp[d4];
-            sum = __fadd_rn(sum, __fmul_rn(qs[4 * d4], k4.x));
-            sum = __fadd_rn(sum, __fmul_rn(qs[4 * d4 + 1], k4.y));
-            sum = __fadd_rn(sum, __fmul_rn(qs[4 * d4 + 2], k4.z));
-            sum = __fadd_rn(sum, __fmul_rn(qs[4 * d4 + 3], k4.w));
+    const int seq = blockIdx.x, kvh = blockIdx.y, t0 = blockIdx.z * kQBlk;
+    const int nq = min(kQBlk, len - t0);
+    const int64_t base = (int64_t)seq * len;
+    float* ex = dsm + (int64_t)warp * len;
+    // pass 1: max, exp terms, their sum in position order, log-sum
+    for (int k = 0; k < kPairsPerWarp; k++) {
+        const int pr = warp * kPairsPerWarp + k, hh = pr / kQBlk, tq = pr % kQBlk, t = t0 + tq;
+        if (tq >= nq) continue;
+        const float* row = S + ((int64_t)(seq * kHeads + kvh * kGroup + hh) * len + t) * len;
+        float mx = -INFINITY;
+        for (int p = lane; p <= t; p += 32) mx = fmaxf(mx, row[p]);
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        for (int p = lane; p <= t; p += 32) ex[p] = expf_ref(__fsub_rn(row[p], mx));
+        __syncwarp();
+        if (lane == 0) {
+            float es = 0.0f;
+            for (int p = 0; p <= t; p++) es = __fadd_rn(es, ex[p]);
+            lsum[pr] = __fadd_rn(logf_ref(es), mx);
         }
-        sc[p] = __fdiv_rn(sum, 8.0f);
+        __syncwarp();
     }
-    __syncwarp();
-    float mx = -INFINITY;
-    for (int p = lane; p <= pos; p += 32) mx = fmaxf(mx, sc[p]);
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    // exp terms in parallel, their sum in position order
-    for (int p = lane; p <= pos; p += 32) sc[p] = expf_ref(__fsub_rn(sc[p], mx));
-    __syncwarp();
-    float es = 0.0f;
-    if (lane == 0)
-        for (int p = 0; p <= pos; p++) es = __fadd_rn(es, sc[p]);
-    es = __shfl_sync(0xffffffffu, es, 0);
-    const float log_sum = __fadd_rn(logf_ref(es), mx);
-    __syncwarp();
-    // weights need the raw scores again: recompute them (same expression)
-    for (int p = lane; p <= pos; p += 32) {
-        const float4* kp = reinterpret_cast<const float4*>(kr + (t0 + p) * kKvDim + kvh * kHeadDim);
-        float sum = 0.0f;
+    // pass 2: context, positions in order across V tiles
+    float a0[kPairsPerWarp], a1[kPairsPerWarp];
 #pragma unroll
-        for (int d4 = 0; d4 < kHeadDim / 4; d4++) {
-            const float4 k4 = kp[d4];
-            sum = __fadd_rn(sum, __fmul_rn(qs[4 * d4], k4.x));
-            sum = __fadd_rn(sum, __fmul_rn(qs[4 * d4 + 1], k4.y));
-            sum = __fadd_rn(sum, __fmul_rn(qs[4 * d4 + 2], k4.z));
-            sum = __fadd_rn(sum, __fmul_rn(qs[4 * d4 + 3], k4.w));
+    for (int k = 0; k < kPairsPerWarp; k++) a0[k] = a1[k] = 0.0f;
+    const int tlast = t0 + nq - 1;
+    for (int p0 = 0; p0 <= tlast; p0 += kPTile) {
+        __syncthreads();
+        for (int i = threadIdx.x; i < kPTile * kHeadDim; i += blockDim.x) {
+            const int pp = i / kHeadDim, d = i % kHeadDim;
+            vs[pp][d] = (p0 + pp < len) ? vr[(base + p0 + pp) * kKvDim + kvh * kHeadDim + d] : 0.0f;
         }
-        sc[p] = expf_ref(__fsub_rn(__fdiv_rn(sum, 8.0f), log_sum));
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < kPairsPerWarp; k++) {
+            const int pr = warp * kPairsPerWarp + k, hh = pr / kQBlk, tq = pr % kQBlk, t = t0 + tq;
+            if (tq >= nq || p0 > t) continue;
+            const float* row = S + ((int64_t)(seq * kHeads + kvh * kGroup + hh) * len + t) * len + p0;
+            const float ls = lsum[pr];
+            const int np = min(kPTile, t - p0 + 1);
+            const float w0 = (lane < np) ? expf_ref(__fsub_rn(row[lane], ls)) : 0.0f;
+            const float w1 = (lane + 32 < np) ? expf_ref(__fsub_rn(row[lane + 32], ls)) : 0.0f;
+            float x0 = a0[k], x1 = a1[k];
+            for (int pp = 0; pp < np; pp++) {
+                const float w = __shfl_sync(0xffffffffu, pp < 32 ? w0 : w1, pp & 31);
+                x0 = __fadd_rn(x0, __fmul_rn(w, vs[pp][lane]));
+                x1 = __fadd_rn(x1, __fmul_rn(w, vs[pp][lane + 32]));
+            }
+            a0[k] = x0;
+            a1[k] = x1;
+        }
     }
-    __syncwarp();
-    const float* vb = vr + t0 * kKvDim + kvh * kHeadDim;
-    float a0 = 0.0f, a1 = 0.0f;
-    for (int p = 0; p <= pos; p++) {
-        const float wgt = sc[p];
-        a0 = __fadd_rn(a0, __fmul_rn(wgt, vb[(int64_t)p * kKvDim + lane]));
-        a1 = __fadd_rn(a1, __fmul_rn(wgt, vb[(int64_t)p * kKvDim + lane + 32]));
+#pragma unroll
+    for (int k = 0; k < kPairsPerWarp; k++) {
+        const int pr = warp * kPairsPerWarp + k, hh = pr / kQBlk, tq = pr % kQBlk;
+        if (tq >= nq) continue;
+        float* c = ctx + (base + t0 + tq) * kHidden + (kvh * kGroup + hh) * kHeadDim;
+        c[lane] = a0[k];
+        c[lane + 32] = a1[k];
     }
-    ctx[t * kHidden + h * kHeadDim + lane] = a0;
-    ctx[t * kHidden + h * kHeadDim + lane + 32] = a1;
 }
 
 // silu(gate) * up per token (one warp), then x_q of the row as byte planes.
@@ -255,11 +308,12 @@ int ps_alloc(PrefillState* p, T** ptr, size_t n)
     return TMAC_OK;
 }
 
-int ensure_state(tmac_model_s* m, int64_t M, int n_seq)
+int ensure_state(tmac_model_s* m, int64_t M, int n_seq, int len)
 {
     if (!m->prefill) m->prefill = new PrefillState();
     PrefillState* p = m->prefill;
-    if (p->cap >= M && p->cap_seq >= n_seq) return TMAC_OK;
+    const int64_t nsc = M * kHeads * len;
+    if (p->cap >= M && p->cap_seq >= n_seq && p->cap_scores >= nsc) return TMAC_OK;
     for (void* a : p->allocs) cudaFree(a);
     p->allocs.clear();
     p->cap = 0;
@@ -272,10 +326,12 @@ int ensure_state(tmac_model_s* m, int64_t M, int n_seq)
         (rc = ps_alloc(p, &p->ffn, (size_t)M * kHidden)) || (rc = ps_alloc(p, &p->xh, (size_t)M * kInter)) ||
         (rc = ps_alloc(p, &p->xl, (size_t)M * kInter)) || (rc = ps_alloc(p, &p->xs, (size_t)M)) ||
         (rc = ps_alloc(p, &p->tokens, (size_t)M)) || (rc = ps_alloc(p, &p->xlast, (size_t)n_seq * kHidden)) ||
-        (rc = ps_alloc(p, &p->logits, (size_t)n_seq * kVocab)) || (rc = ps_alloc(p, &p->keys, (size_t)n_seq)))
+        (rc = ps_alloc(p, &p->logits, (size_t)n_seq * kVocab)) || (rc = ps_alloc(p, &p->keys, (size_t)n_seq)) ||
+        (rc = ps_alloc(p, &p->scores, (size_t)nsc)))
         return rc;
     p->cap = M;
     p->cap_seq = n_seq;
+    p->cap_scores = nsc;
     return TMAC_OK;
 }
 
@@ -364,12 +420,15 @@ int prefill_run(tmac_model_s* m, int64_t M, int n_seq, int len, cudaStream_t s)
     pf_embed_kernel<<<(unsigned)M, 128, 0, s>>>(m->emb_raw, p->tokens, p->hidden);
     TMAC_CUDA_TRY(cudaGetLastError());
     const unsigned nblk8 = (unsigned)((M + 7) / 8);
-    const size_t attn_smem = (size_t)kAttnWarps * (kHeadDim + len) * sizeof(float);
+    const size_t ctx_smem = (size_t)kCtxWarps * len * sizeof(float);
     static bool attr_done = false;
     if (!attr_done) {
-        TMAC_CUDA_TRY(cudaFuncSetAttribute(pf_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024));
+        TMAC_CUDA_TRY(cudaFuncSetAttribute(pf_softmax_ctx_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024));
+        TMAC_CUDA_TRY(cudaFuncSetAttribute(pf_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kScoresSmem));
         attr_done = true;
     }
+    if (ctx_smem > 160 * 1024) return fail(TMAC_ERR_SHAPE, "prefill: sequence too long for the attention kernel");
+    const dim3 agrid((unsigned)n_seq, kKvHeads, (unsigned)((len + kQBlk - 1) / kQBlk));
     for (int l = 0; l < kLayers; l++) {
         const float* an = vec_or_null(m, lname(l, "attn_norm.weight"));
         const float* fn = vec_or_null(m, lname(l, "ffn_norm.weight"));
@@ -395,8 +454,9 @@ int prefill_run(tmac_model_s* m, int64_t M, int n_seq, int len, cudaStream_t s)
             p->qkv, vec_or_null(m, lname(l, "attn_q.bias")), vec_or_null(m, lname(l, "attn_k.bias")),
             vec_or_null(m, lname(l, "attn_v.bias")), m->rope_c, m->rope_s, len, p->qr, p->kr, p->vr);
         TMAC_CUDA_TRY(cudaGetLastError());
-        pf_attention_kernel<<<(unsigned)((M * kHeads + kAttnWarps - 1) / kAttnWarps), kAttnWarps * 32, attn_smem, s>>>(
-            p->qr, p->kr, p->vr, M, len, p->ctx);
+        pf_scores_kernel<<<agrid, 256, kScoresSmem, s>>>(p->qr, p->kr, len, p->scores);
+        TMAC_CUDA_TRY(cudaGetLastError());
+        pf_softmax_ctx_kernel<<<agrid, kCtxWarps * 32, ctx_smem, s>>>(p->scores, p->vr, len, p->ctx);
         TMAC_CUDA_TRY(cudaGetLastError());
         if ((rc = quantize_rows(p->ctx, kHidden, (int)M, p->xh, p->xl, p->xs, s))) return rc;
         tmac_weight_s* wo = mat(m, lname(l, "attn_output.weight"));
@@ -444,7 +504,7 @@ extern "C" int tmac_model_prefill(tmac_model_t m, const int* tokens, int n_seq, 
     DeviceGuard dg(m->device);
     if (!dg.ok) return fail(TMAC_ERR_CUDA, "cudaSetDevice failed");
     const int64_t M = (int64_t)n_seq * len;
-    int rc = ensure_state(m, M, n_seq);
+    int rc = ensure_state(m, M, n_seq, len);
     if (rc) return rc;
     cudaStream_t s = (cudaStream_t)stream;
     PrefillState* p = m->prefill;
