@@ -47,3 +47,14 @@ def test_prefill_sequences_are_independent(mdl):
     n1, h1 = mdl.prefill(b[None, :], want_hidden=True)
     assert n2[1] == n1[0]
     np.testing.assert_array_equal(h2[1], h1[0])
+
+
+def test_prefill_growing_batches_keep_weight_planes(mdl):
+    """A larger batch re-makes the activation buffers; the cached weight planes
+    (the Q8_0 attn_v layers) must survive it."""
+    a = model.prompt_tokens(16, seed=21)
+    n_small, h_small = mdl.prefill(a[None, :], want_hidden=True)
+    batch = np.stack([model.prompt_tokens(16, seed=22 + i) for i in range(5)] + [a])
+    n_big, h_big = mdl.prefill(batch, want_hidden=True)
+    assert n_big[-1] == n_small[0]
+    np.testing.assert_array_equal(h_big[-1], h_small[0])

@@ -13,10 +13,11 @@
 // int64 row sum and y = (float)((double)acc * x_scale / (double)row_inv)
 // exactly as the GEMV does.
 //
-// Tile 128 (rows of X) x 128 (weight rows) x 128 (K bytes); operands staged by
-// TMA (128-byte swizzle, out-of-range rows and columns read as zero) through a
-// 3-stage mbarrier ring.  Warp 0 issues the copies, warp 1 owns TMEM and issues
-// the MMAs, warps 2-5 read the accumulators (each warp its 32 TMEM lanes).
+// Persistent kernel, one CTA per SM, tiles of 128 (rows of X) x 80 (weight
+// rows) x 128 (K bytes); operands staged by TMA (128-byte swizzle, out-of-range
+// rows and columns read as zero) through a 4-stage mbarrier ring.  Warp 0
+// issues the copies, warp 1 owns TMEM and issues the MMAs into one of two
+// accumulator sets, eight epilogue warps drain the other set.
 #include "common.cuh"
 
 #include <cuda.h>
@@ -29,11 +30,15 @@
 namespace tmac {
 namespace {
 
-constexpr int BM = 128, BN = 128, BK = 128, STAGES = 3;
-constexpr uint32_t kTile = BM * BK;            // bytes of one operand tile (BM == BN)
-constexpr uint32_t kStageBytes = 4 * kTile;    // xh, xl, wh, wl
-constexpr int kThreads = 192;
-constexpr uint32_t kTmemCols = 512;            // hh [0,128) | mid [128,256) | ll [256,384)
+// Tile 128 (activation rows) x 80 (weight rows) x 128 (K bytes).  Three int32
+// accumulators of 80 columns per tile, two tiles in flight: 480 TMEM columns.
+constexpr int BM = 128, BN = 80, BK = 128, STAGES = 4;
+constexpr uint32_t kTileX = BM * BK, kTileW = BN * BK;     // bytes of one plane tile
+constexpr uint32_t kStageBytes = 2 * kTileX + 2 * kTileW;  // xh, xl, wh, wl
+constexpr int kEpiWarps = 8;                               // 2 per TMEM lane quarter, 40 columns each
+constexpr int kThreads = (2 + kEpiWarps) * 32;
+constexpr uint32_t kTmemCols = 512;                        // buffer b: hh | mid | ll at b*256 + {0, 80, 160}
+constexpr int kEpiCols = BN / 2;
 constexpr size_t kSmem = STAGES * kStageBytes + 1024 + 256;
 
 struct GemmArgs {
@@ -43,6 +48,7 @@ struct GemmArgs {
     int64_t* acc_out;        // optional [M][N] int64 sums
     int64_t y_stride;
     int M, N, K;
+    int tiles_m, tiles_n;
     int mode;                // 0: y = acc*xs/row_inv   1: y = (float)(y + acc*xs*row_scale)
     int* err;
 };
@@ -70,7 +76,7 @@ TMAC_DEV uint64_t desc_sw128(uint32_t saddr)
 }
 
 // Instruction descriptor for kind::i8: s32 accumulate, A/B signed (1) or
-// unsigned (0), both K-major, M = 128, N = 128.
+// unsigned (0), both K-major, M = BM, N = BN.
 __host__ __device__ constexpr uint32_t idesc_i8(uint32_t a_signed, uint32_t b_signed)
 {
     return (2u << 4) | (a_signed << 7) | (b_signed << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
@@ -92,18 +98,20 @@ TMAC_DEV void mma_commit(uint64_t* bar)
 TMAC_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 TMAC_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-TMAC_DEV void tmem_ld16(uint32_t taddr, uint32_t (&r)[16])
+TMAC_DEV void tmem_ld8(uint32_t taddr, uint32_t* r)
 {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-        "%15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr));
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr));
 }
 TMAC_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // ----------------------------------------------------------------- kernel --
+// Persistent: CTA c takes tiles c, c + grid, ...; tile i -> (m tile i % tiles_m,
+// n tile i / tiles_m), so consecutive tiles share a weight tile.  Warp 0
+// streams operands through the STAGES ring, warp 1 issues the MMAs into the
+// accumulator buffer of the tile's parity, warps 2.. drain a finished buffer
+// into registers, release it, then form y while the next tile accumulates.
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_i8x4_kernel(const __grid_constant__ CUtensorMap tm_xh, const __grid_constant__ CUtensorMap tm_xl,
                      const __grid_constant__ CUtensorMap tm_wh, const __grid_constant__ CUtensorMap tm_wl, GemmArgs a)
@@ -112,20 +120,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * kStageBytes);
     uint64_t* empty = full + STAGES;
-    uint64_t* done = empty + STAGES;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    uint64_t* tfull = empty + STAGES;   // [2] accumulator buffer ready
+    uint64_t* tempty = tfull + 2;       // [2] accumulator buffer drained
+    uint64_t* drain = tempty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
     volatile int* abort_s = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
     const int KB = (a.K + BK - 1) / BK;
+    const int ntiles = a.tiles_m * a.tiles_n;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < STAGES; i++) {
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], 1);
         }
-        mbar_init(done, 1);
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&tfull[i], 1);
+            mbar_init(&tempty[i], kEpiWarps);
+        }
+        mbar_init(drain, 1);
         *abort_s = 0;
         fence_mbar_init();
     }
@@ -141,72 +155,106 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (warp == 0) {
         if (lane == 0) {
-            for (int kb = 0; kb < KB; kb++) {
-                const int s = kb % STAGES;
-                if (kb >= STAGES && !mbar_wait_bounded(&empty[s], ((kb / STAGES) - 1) & 1, a.err)) {
-                    *abort_s = 1;
-                    break;
+            int64_t g = 0;  // k-blocks issued so far
+            for (int tile = blockIdx.x; tile < ntiles && !*abort_s; tile += gridDim.x) {
+                const int m0 = (tile % a.tiles_m) * BM, n0 = (tile / a.tiles_m) * BN;
+                for (int kb = 0; kb < KB; kb++, g++) {
+                    const int s = (int)(g % STAGES);
+                    if (g >= STAGES && !mbar_wait_bounded(&empty[s], (int)((g / STAGES - 1) & 1), a.err)) {
+                        *abort_s = 1;
+                        break;
+                    }
+                    uint8_t* st = smem + s * kStageBytes;
+                    mbar_arrive_expect_tx(&full[s], kStageBytes);
+                    tma_load_2d(st, &tm_xh, kb * BK, m0, &full[s]);
+                    tma_load_2d(st + kTileX, &tm_xl, kb * BK, m0, &full[s]);
+                    tma_load_2d(st + 2 * kTileX, &tm_wh, kb * BK, n0, &full[s]);
+                    tma_load_2d(st + 2 * kTileX + kTileW, &tm_wl, kb * BK, n0, &full[s]);
                 }
-                if (*abort_s) break;
-                uint8_t* st = smem + s * kStageBytes;
-                mbar_arrive_expect_tx(&full[s], kStageBytes);
-                tma_load_2d(st, &tm_xh, kb * BK, m0, &full[s]);
-                tma_load_2d(st + kTile, &tm_xl, kb * BK, m0, &full[s]);
-                tma_load_2d(st + 2 * kTile, &tm_wh, kb * BK, n0, &full[s]);
-                tma_load_2d(st + 3 * kTile, &tm_wl, kb * BK, n0, &full[s]);
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
             constexpr uint32_t kHH = idesc_i8(1, 1), kHL = idesc_i8(1, 0), kLH = idesc_i8(0, 1), kLL = idesc_i8(0, 0);
-            for (int kb = 0; kb < KB; kb++) {
-                const int s = kb % STAGES;
-                if (*abort_s || !mbar_wait_bounded(&full[s], (kb / STAGES) & 1, a.err)) {
+            int64_t g = 0;
+            int li = 0;
+            for (int tile = blockIdx.x; tile < ntiles && !*abort_s; tile += gridDim.x, li++) {
+                const int b = li & 1, use = li >> 1;
+                if (use >= 1 && !mbar_wait_bounded(&tempty[b], (use - 1) & 1, a.err)) {
                     *abort_s = 1;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t st = smem_addr(smem + s * kStageBytes);
+                const uint32_t acc0 = tmem + (uint32_t)b * 256;
+                for (int kb = 0; kb < KB; kb++, g++) {
+                    const int s = (int)(g % STAGES);
+                    if (*abort_s || !mbar_wait_bounded(&full[s], (int)((g / STAGES) & 1), a.err)) {
+                        *abort_s = 1;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t st = smem_addr(smem + s * kStageBytes);
 #pragma unroll
-                for (int kk = 0; kk < BK / 32; kk++) {  // 32 bytes of K per MMA
-                    const uint64_t xh = desc_sw128(st + kk * 32), xl = desc_sw128(st + kTile + kk * 32);
-                    const uint64_t wh = desc_sw128(st + 2 * kTile + kk * 32), wl = desc_sw128(st + 3 * kTile + kk * 32);
-                    const uint32_t acc = (kb | kk) != 0;
-                    mma_i8(tmem, xh, wh, kHH, acc);
-                    mma_i8(tmem + 128, xh, wl, kHL, acc);
-                    mma_i8(tmem + 128, xl, wh, kLH, 1u);
-                    mma_i8(tmem + 256, xl, wl, kLL, acc);
+                    for (int kk = 0; kk < BK / 32; kk++) {  // 32 bytes of K per MMA
+                        const uint64_t xh = desc_sw128(st + kk * 32), xl = desc_sw128(st + kTileX + kk * 32);
+                        const uint64_t wh = desc_sw128(st + 2 * kTileX + kk * 32);
+                        const uint64_t wl = desc_sw128(st + 2 * kTileX + kTileW + kk * 32);
+                        const uint32_t acc = (kb | kk) != 0;
+                        mma_i8(acc0, xh, wh, kHH, acc);
+                        mma_i8(acc0 + BN, xh, wl, kHL, acc);
+                        mma_i8(acc0 + BN, xl, wh, kLH, 1u);
+                        mma_i8(acc0 + 2 * BN, xl, wl, kLL, acc);
+                    }
+                    mma_commit(&empty[s]);  // the stage is free once these MMAs have read it
                 }
-                mma_commit(&empty[s]);  // the stage is free once these MMAs have read it
+                if (*abort_s) break;
+                mma_commit(&tfull[b]);
             }
-            mma_commit(done);  // completes when every MMA issued above has
+            mma_commit(drain);  // completes when every MMA issued above has
+            mbar_wait_bounded(drain, 0, a.err);
         }
     } else {
-        // epilogue: warp w reads TMEM lanes 32*(w%4) .. +31, one activation row per thread
-        const bool ok = mbar_wait_bounded(done, 0, a.err);
-        tc_fence_after();
-        const int q = warp & 3, row = q * 32 + lane, m = m0 + row;
-        const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16);
-        const double xsd = (m < a.M) ? (double)a.xs[m] : 0.0;
-        for (int c = 0; c < BN; c += 16) {
-            uint32_t hh[16], md[16], ll[16];
-            tmem_ld16(taddr + c, hh);
-            tmem_ld16(taddr + 128 + c, md);
-            tmem_ld16(taddr + 256 + c, ll);
-            tmem_wait_ld();
-            if (!ok || *abort_s || m >= a.M) continue;
+        // epilogue warp: TMEM lanes 32*(warp%4) .. +31 (one activation row per
+        // thread), columns [half*40, half*40 + 40) of the tile
+        const int q = warp & 3, half = (warp - 2) >> 2;
+        const int c0 = half * kEpiCols;
+        int li = 0;
+        for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, li++) {
+            const int m0 = (tile % a.tiles_m) * BM, n0 = (tile / a.tiles_m) * BN;
+            const int m = m0 + q * 32 + lane;
+            const int b = li & 1, use = li >> 1;
+            const double xsd = (m < a.M) ? (double)a.xs[m] : 0.0;
+            const bool ok = !*abort_s && mbar_wait_bounded(&tfull[b], use & 1, a.err);
+            if (!ok) {
+                *abort_s = 1;
+                break;
+            }
+            tc_fence_after();
+            const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)b * 256 + c0;
+            uint32_t hh[kEpiCols], md[kEpiCols], ll[kEpiCols];
 #pragma unroll
-            for (int j = 0; j < 16; j++) {
-                const int n = n0 + c + j;
-                if (n >= a.N) break;
+            for (int c = 0; c < kEpiCols; c += 8) {
+                tmem_ld8(taddr + c, hh + c);
+                tmem_ld8(taddr + BN + c, md + c);
+                tmem_ld8(taddr + 2 * BN + c, ll + c);
+            }
+            tmem_wait_ld();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[b]);  // the buffer can take tile li + 2
+            if (m >= a.M) continue;
+            float* yrow = a.y + (int64_t)m * a.y_stride + n0 + c0;
+#pragma unroll
+            for (int j = 0; j < kEpiCols; j++) {
+                const int n = n0 + c0 + j;
+                if (n >= a.N) continue;
                 const long long acc = (long long)(int32_t)hh[j] * 65536 + (long long)(int32_t)md[j] * 256 +
                                       (long long)(int32_t)ll[j];
-                float* yp = a.y + (int64_t)m * a.y_stride + n;
                 if (a.mode == 0) {
-                    *yp = (float)__ddiv_rn(__dmul_rn((double)acc, xsd), (double)a.row_param[n]);
+                    yrow[j] = (float)__ddiv_rn(__dmul_rn((double)acc, xsd), (double)__ldg(a.row_param + n));
                 } else {  // one 64-column tile of the Q8_0 fold (gemv_q8_0.cu)
-                    const double v = __dmul_rn(__dmul_rn((double)acc, xsd), (double)a.row_param[n]);
-                    *yp = (float)__dadd_rn((double)*yp, v);
+                    const double v = __dmul_rn(__dmul_rn((double)acc, xsd), (double)__ldg(a.row_param + n));
+                    yrow[j] = (float)__dadd_rn((double)yrow[j], v);
                 }
                 if (a.acc_out) a.acc_out[(int64_t)m * a.N + n] = acc;
             }
@@ -215,8 +263,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
-        if (*abort_s && lane == 0) mbar_wait_bounded(done, 0, nullptr);  // MMAs issued before an abort
-        __syncwarp();
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
     }
@@ -261,13 +307,13 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
     return fn;
 }
 
-int encode_plane_map(CUtensorMap* tm, const void* base, int64_t rows, int64_t K, int64_t stride)
+int encode_plane_map(CUtensorMap* tm, const void* base, int64_t rows, int64_t K, int64_t stride, uint32_t box_rows)
 {
     const auto encode = encode_fn();
     if (!encode) return fail(TMAC_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
     const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
     const cuuint64_t strides[1] = {(cuuint64_t)stride};
-    const cuuint32_t box[2] = {BK, 128};
+    const cuuint32_t box[2] = {BK, box_rows};
     const cuuint32_t es[2] = {1, 1};
     const CUresult r = encode(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims,
                                               strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -338,10 +384,10 @@ int gemm_planes(const GemmOperands& op, cudaStream_t s)
 {
     alignas(64) CUtensorMap tm[4];
     int rc;
-    if ((rc = encode_plane_map(&tm[0], op.xh + op.k_off, op.M, op.K, op.x_stride)) ||
-        (rc = encode_plane_map(&tm[1], op.xl + op.k_off, op.M, op.K, op.x_stride)) ||
-        (rc = encode_plane_map(&tm[2], op.wh + op.k_off, op.N, op.K, op.w_stride)) ||
-        (rc = encode_plane_map(&tm[3], op.wl + op.k_off, op.N, op.K, op.w_stride)))
+    if ((rc = encode_plane_map(&tm[0], op.xh + op.k_off, op.M, op.K, op.x_stride, BM)) ||
+        (rc = encode_plane_map(&tm[1], op.xl + op.k_off, op.M, op.K, op.x_stride, BM)) ||
+        (rc = encode_plane_map(&tm[2], op.wh + op.k_off, op.N, op.K, op.w_stride, BN)) ||
+        (rc = encode_plane_map(&tm[3], op.wl + op.k_off, op.N, op.K, op.w_stride, BN)))
         return rc;
     static bool attr[64] = {};
     if (!attr[op.device & 63]) {
@@ -358,8 +404,10 @@ int gemm_planes(const GemmOperands& op, cudaStream_t s)
     a.N = op.N;
     a.K = (int)op.K;
     a.mode = op.mode;
+    a.tiles_m = (op.M + BM - 1) / BM;
+    a.tiles_n = (op.N + BN - 1) / BN;
     a.err = device_error_word(op.device);
-    const dim3 grid((unsigned)((op.N + BN - 1) / BN), (unsigned)((op.M + BM - 1) / BM));
+    const dim3 grid((unsigned)std::min<int64_t>((int64_t)a.tiles_m * a.tiles_n, num_sms(op.device)));
     TMAC_CUDA_TRY(launch_k(gemm_i8x4_kernel, grid, dim3(kThreads), kSmem, s, tm[0], tm[1], tm[2], tm[3], a));
     TMAC_CUDA_TRY(cudaGetLastError());
     return TMAC_OK;

@@ -34,7 +34,8 @@ struct PrefillState {
     float* scores = nullptr;  // [n_seq*heads*len][len]
     int64_t cap_seq = 0, cap_scores = 0;
     std::map<std::string, std::pair<int8_t*, uint8_t*>> q8planes;  // Q8_0 matrices (attn_v)
-    std::vector<void*> allocs;
+    std::vector<void*> allocs;        // activation buffers (re-made when a larger batch comes)
+    std::vector<void*> plane_allocs;  // weight planes (kept for the model's lifetime)
 };
 
 namespace {
@@ -373,8 +374,10 @@ int pf_gemm_q8(tmac_model_s* m, const std::string& name, tmac_weight_s* w, int64
         int8_t* wh = nullptr;
         uint8_t* wl = nullptr;
         int rc;
-        if ((rc = ps_alloc(p, &wh, (size_t)(w->rows * w->cols))) || (rc = ps_alloc(p, &wl, (size_t)(w->rows * w->cols))))
-            return rc;
+        TMAC_CUDA_TRY(cudaMalloc(&wh, (size_t)(w->rows * w->cols)));
+        p->plane_allocs.push_back(wh);
+        TMAC_CUDA_TRY(cudaMalloc(&wl, (size_t)(w->rows * w->cols)));
+        p->plane_allocs.push_back(wl);
         if ((rc = q8_planes(w, wh, wl, s))) return rc;
         it = p->q8planes.emplace(name, std::make_pair(wh, wl)).first;
     }
@@ -484,6 +487,7 @@ void prefill_free(tmac_model_s* m)
 {
     if (!m->prefill) return;
     for (void* a : m->prefill->allocs) cudaFree(a);
+    for (void* a : m->prefill->plane_allocs) cudaFree(a);
     delete m->prefill;
     m->prefill = nullptr;
 }
