@@ -229,6 +229,7 @@ struct tmac_weight_s {
     int64_t n_exc = 0;
     void* gwh = nullptr;         // tensor-core GEMM: exact int16 weights as byte planes
     void* gwl = nullptr;         // (high, low), decoded on first tmac_gemm
+    void* grinv = nullptr;       // double [rows]: RN(1 / row_inv) for the GEMM epilogue
 };
 
 namespace tmac {
@@ -267,6 +268,7 @@ struct GemmOperands {
     int N = 0;
     int64_t K = 0, k_off = 0;
     const float* row_param = nullptr;
+    const double* row_rinv = nullptr;  // mode 0: RN(1 / row_param) in double
     int mode = 0;
     float* y = nullptr;
     int64_t y_stride = 0;

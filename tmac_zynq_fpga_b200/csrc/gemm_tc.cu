@@ -44,6 +44,7 @@ constexpr size_t kSmem = STAGES * kStageBytes + 1024 + 256;
 struct GemmArgs {
     const float* xs;         // [M] x_scale of each activation row
     const float* row_param;  // [N] row_inv (mode 0) or row_scale (mode 1)
+    const double* row_rinv;  // [N] RN(1 / row_inv) in double (mode 0)
     float* y;                // [M][y_stride]
     int64_t* acc_out;        // optional [M][N] int64 sums
     int64_t y_stride;
@@ -106,9 +107,26 @@ TMAC_DEV void tmem_ld8(uint32_t taddr, uint32_t* r)
 }
 TMAC_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// (float)(p / ri) with p / ri rounded to double first, as the GEMV computes it
+// (__ddiv_rn then the float conversion).  p * RN(1/ri) is within 2 double ulps
+// of the double quotient; unless its 29 bits below float precision lie within
+// 16 units of the float rounding midpoint (or the value is outside the normal
+// float range) both round to the same float, else the exact division decides.
+TMAC_DEV float quotient_f32(double p, double rinv, float ri)
+{
+    const double q = __dmul_rn(p, rinv);
+    const long long bits = __double_as_longlong(q);
+    const int exp = (int)((bits >> 52) & 0x7FF);
+    const int low = (int)(bits & 0x1FFFFFFF);
+    const bool near_mid = abs(low - 0x10000000) <= 16;
+    if (near_mid || exp < 1023 - 120 || exp > 1023 + 120) return (float)__ddiv_rn(p, (double)ri);
+    return (float)q;
+}
+
 // ----------------------------------------------------------------- kernel --
-// Persistent: CTA c takes tiles c, c + grid, ...; tile i -> (m tile i % tiles_m,
-// n tile i / tiles_m), so consecutive tiles share a weight tile.  Warp 0
+// Persistent: CTA c takes tiles c, c + grid, ...; tile i -> (m tile i / tiles_n,
+// n tile i % tiles_n), so the tiles in flight share few activation tiles, which
+// stay in L2 while every weight tile passes them.  Warp 0
 // streams operands through the STAGES ring, warp 1 issues the MMAs into the
 // accumulator buffer of the tile's parity, warps 2.. drain a finished buffer
 // into registers, release it, then form y while the next tile accumulates.
@@ -157,7 +175,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             int64_t g = 0;  // k-blocks issued so far
             for (int tile = blockIdx.x; tile < ntiles && !*abort_s; tile += gridDim.x) {
-                const int m0 = (tile % a.tiles_m) * BM, n0 = (tile / a.tiles_m) * BN;
+                const int m0 = (tile / a.tiles_n) * BM, n0 = (tile % a.tiles_n) * BN;
                 for (int kb = 0; kb < KB; kb++, g++) {
                     const int s = (int)(g % STAGES);
                     if (g >= STAGES && !mbar_wait_bounded(&empty[s], (int)((g / STAGES - 1) & 1), a.err)) {
@@ -220,7 +238,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int c0 = half * kEpiCols;
         int li = 0;
         for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, li++) {
-            const int m0 = (tile % a.tiles_m) * BM, n0 = (tile / a.tiles_m) * BN;
+            const int m0 = (tile / a.tiles_n) * BM, n0 = (tile % a.tiles_n) * BN;
             const int m = m0 + q * 32 + lane;
             const int b = li & 1, use = li >> 1;
             const double xsd = (m < a.M) ? (double)a.xs[m] : 0.0;
@@ -231,33 +249,53 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             tc_fence_after();
             const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)b * 256 + c0;
-            uint32_t hh[kEpiCols], md[kEpiCols], ll[kEpiCols];
-#pragma unroll
+            float* yrow = a.y + (int64_t)m * a.y_stride + n0 + c0;
+            const bool row_ok = m < a.M;
+            // 8 columns at a time: three TMEM loads, then the 8 outputs
+#pragma unroll 1
             for (int c = 0; c < kEpiCols; c += 8) {
-                tmem_ld8(taddr + c, hh + c);
-                tmem_ld8(taddr + BN + c, md + c);
-                tmem_ld8(taddr + 2 * BN + c, ll + c);
+                uint32_t hh[8], md[8], ll[8];
+                tmem_ld8(taddr + c, hh);
+                tmem_ld8(taddr + BN + c, md);
+                tmem_ld8(taddr + 2 * BN + c, ll);
+                double rinv[8];
+                float rp[8];
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    const int n = min(n0 + c0 + c + j, a.N - 1);
+                    rp[j] = __ldg(a.row_param + n);
+                    rinv[j] = (a.mode == 0) ? __ldg(a.row_rinv + n) : 0.0;
+                }
+                tmem_wait_ld();
+                if (!row_ok) continue;
+                const bool full8 = n0 + c0 + c + 8 <= a.N && ((reinterpret_cast<uintptr_t>(yrow + c) & 15) == 0);
+                float out[8];
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    const long long acc = (long long)(int32_t)hh[j] * 65536 + (long long)(int32_t)md[j] * 256 +
+                                          (long long)(int32_t)ll[j];
+                    const double p = __dmul_rn((double)acc, xsd);
+                    if (a.mode == 0) {
+                        out[j] = quotient_f32(p, rinv[j], rp[j]);
+                    } else {  // one 64-column tile of the Q8_0 fold (gemv_q8_0.cu)
+                        const double v = __dmul_rn(p, (double)rp[j]);
+                        const bool in = n0 + c0 + c + j < a.N;
+                        out[j] = (float)__dadd_rn((double)(in ? yrow[c + j] : 0.0f), v);
+                    }
+                    if (a.acc_out && n0 + c0 + c + j < a.N) a.acc_out[(int64_t)m * a.N + n0 + c0 + c + j] = acc;
+                }
+                if (full8) {
+                    *reinterpret_cast<float4*>(yrow + c) = make_float4(out[0], out[1], out[2], out[3]);
+                    *reinterpret_cast<float4*>(yrow + c + 4) = make_float4(out[4], out[5], out[6], out[7]);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 8; j++)
+                        if (n0 + c0 + c + j < a.N) yrow[c + j] = out[j];
+                }
             }
-            tmem_wait_ld();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty[b]);  // the buffer can take tile li + 2
-            if (m >= a.M) continue;
-            float* yrow = a.y + (int64_t)m * a.y_stride + n0 + c0;
-#pragma unroll
-            for (int j = 0; j < kEpiCols; j++) {
-                const int n = n0 + c0 + j;
-                if (n >= a.N) continue;
-                const long long acc = (long long)(int32_t)hh[j] * 65536 + (long long)(int32_t)md[j] * 256 +
-                                      (long long)(int32_t)ll[j];
-                if (a.mode == 0) {
-                    yrow[j] = (float)__ddiv_rn(__dmul_rn((double)acc, xsd), (double)__ldg(a.row_param + n));
-                } else {  // one 64-column tile of the Q8_0 fold (gemv_q8_0.cu)
-                    const double v = __dmul_rn(__dmul_rn((double)acc, xsd), (double)__ldg(a.row_param + n));
-                    yrow[j] = (float)__dadd_rn((double)yrow[j], v);
-                }
-                if (a.acc_out) a.acc_out[(int64_t)m * a.N + n] = acc;
-            }
         }
     }
     tc_fence_before();
@@ -266,6 +304,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
     }
+}
+
+__global__ void rinv_kernel(const float* __restrict__ ri, int64_t n, double* __restrict__ out)
+{
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) out[i] = __ddiv_rn(1.0, (double)ri[i]);
 }
 
 // Activation rows -> x_scale and byte planes (one CTA per row, tmac_gguf.cpp:889-896).
@@ -370,6 +414,9 @@ int gemm_prepare(tmac_weight_s* w, cudaStream_t s)
     TMAC_CUDA_TRY(cudaMalloc(&w->gwl, n));
     int rc = blockq_planes(w, reinterpret_cast<int8_t*>(w->gwh), reinterpret_cast<uint8_t*>(w->gwl), s);
     if (rc) return rc;
+    TMAC_CUDA_TRY(cudaMalloc(&w->grinv, (size_t)w->rows * sizeof(double)));
+    rinv_kernel<<<(unsigned)((w->rows + 255) / 256), 256, 0, s>>>(w->row_norm, w->rows, reinterpret_cast<double*>(w->grinv));
+    TMAC_CUDA_TRY(cudaGetLastError());
     return TMAC_OK;
 }
 
@@ -397,6 +444,7 @@ int gemm_planes(const GemmOperands& op, cudaStream_t s)
     GemmArgs a;
     a.xs = op.xs;
     a.row_param = op.row_param;
+    a.row_rinv = op.row_rinv;
     a.y = op.y;
     a.acc_out = op.acc_out;
     a.y_stride = op.y_stride;
@@ -433,6 +481,7 @@ int launch_gemm(tmac_weight_s* w, const float* x, float* y, int64_t* acc_out, in
     op.K = w->cols;
     op.k_off = 0;
     op.row_param = w->row_norm;
+    op.row_rinv = reinterpret_cast<const double*>(w->grinv);
     op.mode = 0;
     op.y = y;
     op.y_stride = w->rows;

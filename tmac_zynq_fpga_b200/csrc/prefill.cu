@@ -356,6 +356,7 @@ int pf_gemm(tmac_model_s* m, tmac_weight_s* w, int64_t M, int64_t K, float* y, i
     op.N = (int)w->rows;
     op.K = K;
     op.row_param = w->row_norm;
+    op.row_rinv = reinterpret_cast<const double*>(w->grinv);
     op.mode = 0;
     op.y = y;
     op.y_stride = y_stride;

@@ -227,6 +227,7 @@ void free_weight(tmac_weight_s* w)
     if (w->exc) cudaFree(w->exc);
     if (w->gwh) cudaFree(w->gwh);
     if (w->gwl) cudaFree(w->gwl);
+    if (w->grinv) cudaFree(w->grinv);
     delete w;
 }
 
