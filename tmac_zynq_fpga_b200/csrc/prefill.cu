@@ -200,76 +200,84 @@ __global__ void __launch_bounds__(256) pf_scores_kernel(const float* __restrict_
     }
 }
 
-// Softmax and context: one CTA per (sequence, KV head, query block), 8 warps,
-// each warp owning kPairs / 8 (head, query) pairs.
-constexpr int kCtxWarps = 8, kPairsPerWarp = kPairs / kCtxWarps;
-__global__ void __launch_bounds__(kCtxWarps * 32) pf_softmax_ctx_kernel(const float* __restrict__ S,
-                                                                        const float* __restrict__ vr, int len,
-                                                                        float* __restrict__ ctx)
+// Softmax and context: one CTA per (sequence, KV head, query block), 256
+// threads.  Pass 1: one thread per (head, query) pair: max, then the exp terms
+// summed in position order, log-sum.  Pass 2, per 64-position tile: every weight
+// exp(s - log_sum) into shared memory, then each thread accumulates 7 pairs x 8
+// dims in position order, with separately rounded multiply and add (the packed
+// fp32x2 forms are contracted into fused multiply-adds by the assembler, which
+// changes the result in about 1 case in 150, so they are not used here).
+constexpr int kCtxThreads = 256;
+constexpr int kWStride = kPairs + 1;  // weights tile [kPTile][kWStride]
+constexpr size_t kCtxSmem = (size_t)(kPTile * kHeadDim + kPTile * kWStride + kPairs) * sizeof(float);
+__global__ void __launch_bounds__(kCtxThreads) pf_softmax_ctx_kernel(const float* __restrict__ S,
+                                                                     const float* __restrict__ vr, int len,
+                                                                     float* __restrict__ ctx)
 {
-    extern __shared__ float dsm[];  // ex[kCtxWarps][len]
-    __shared__ float vs[kPTile][kHeadDim];
-    __shared__ float lsum[kPairs];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    extern __shared__ __align__(16) float csm[];
+    float* vs = csm;                                 // [kPTile][kHeadDim]
+    float* wt = vs + kPTile * kHeadDim;              // [kPTile][kWStride]
+    float* lsum = wt + kPTile * kWStride;            // [kPairs]
     const int seq = blockIdx.x, kvh = blockIdx.y, t0 = blockIdx.z * kQBlk;
     const int nq = min(kQBlk, len - t0);
     const int64_t base = (int64_t)seq * len;
-    float* ex = dsm + (int64_t)warp * len;
-    // pass 1: max, exp terms, their sum in position order, log-sum
-    for (int k = 0; k < kPairsPerWarp; k++) {
-        const int pr = warp * kPairsPerWarp + k, hh = pr / kQBlk, tq = pr % kQBlk, t = t0 + tq;
-        if (tq >= nq) continue;
-        const float* row = S + ((int64_t)(seq * kHeads + kvh * kGroup + hh) * len + t) * len;
-        float mx = -INFINITY;
-        for (int p = lane; p <= t; p += 32) mx = fmaxf(mx, row[p]);
-        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        for (int p = lane; p <= t; p += 32) ex[p] = expf_ref(__fsub_rn(row[p], mx));
-        __syncwarp();
-        if (lane == 0) {
-            float es = 0.0f;
-            for (int p = 0; p <= t; p++) es = __fadd_rn(es, ex[p]);
-            lsum[pr] = __fadd_rn(logf_ref(es), mx);
-        }
-        __syncwarp();
+    auto srow = [&](int pr) {
+        return S + ((int64_t)(seq * kHeads + kvh * kGroup + pr / kQBlk) * len + t0 + pr % kQBlk) * len;
+    };
+    // pass 1
+    if (threadIdx.x < kPairs && threadIdx.x % kQBlk < nq) {
+        const int pr = threadIdx.x, t = t0 + pr % kQBlk;
+        const float* row = srow(pr);
+        float mx = row[0];
+        for (int p = 1; p <= t; p++) mx = fmaxf(mx, row[p]);
+        float es = 0.0f;
+        for (int p = 0; p <= t; p++) es = __fadd_rn(es, expf_ref(__fsub_rn(row[p], mx)));
+        lsum[pr] = __fadd_rn(logf_ref(es), mx);
     }
-    // pass 2: context, positions in order across V tiles
-    float a0[kPairsPerWarp], a1[kPairsPerWarp];
+    // pass 2
+    const int pg = threadIdx.x >> 3, db = threadIdx.x & 7;  // pairs 7*pg .. +6, dims 8*db .. +7
+    float acc[7][8];
 #pragma unroll
-    for (int k = 0; k < kPairsPerWarp; k++) a0[k] = a1[k] = 0.0f;
+    for (int i = 0; i < 7; i++)
+#pragma unroll
+        for (int k = 0; k < 8; k++) acc[i][k] = 0.0f;
     const int tlast = t0 + nq - 1;
     for (int p0 = 0; p0 <= tlast; p0 += kPTile) {
         __syncthreads();
-        for (int i = threadIdx.x; i < kPTile * kHeadDim; i += blockDim.x) {
-            const int pp = i / kHeadDim, d = i % kHeadDim;
-            vs[pp][d] = (p0 + pp < len) ? vr[(base + p0 + pp) * kKvDim + kvh * kHeadDim + d] : 0.0f;
+        for (int i = threadIdx.x; i < kPTile * kHeadDim / 4; i += kCtxThreads) {
+            const int pp = i / (kHeadDim / 4), d4 = i % (kHeadDim / 4);
+            float4 v4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (p0 + pp < len) v4 = *reinterpret_cast<const float4*>(vr + (base + p0 + pp) * kKvDim + kvh * kHeadDim + 4 * d4);
+            *reinterpret_cast<float4*>(vs + pp * kHeadDim + 4 * d4) = v4;
+        }
+        for (int e = threadIdx.x; e < kPairs * kPTile; e += kCtxThreads) {
+            const int pr = e / kPTile, pp = e % kPTile, t = t0 + pr % kQBlk, p = p0 + pp;
+            float w = 0.0f;
+            if (pr % kQBlk < nq && p <= t) w = expf_ref(__fsub_rn(srow(pr)[p], lsum[pr]));
+            wt[pp * kWStride + pr] = w;
         }
         __syncthreads();
+        const int np = min(kPTile, tlast - p0 + 1);
+        for (int pp = 0; pp < np; pp++) {
+            const float4 va = *reinterpret_cast<const float4*>(vs + pp * kHeadDim + 8 * db);
+            const float4 vb = *reinterpret_cast<const float4*>(vs + pp * kHeadDim + 8 * db + 4);
+            const float v[8] = {va.x, va.y, va.z, va.w, vb.x, vb.y, vb.z, vb.w};
+            const float* wrow = wt + pp * kWStride + 7 * pg;
 #pragma unroll
-        for (int k = 0; k < kPairsPerWarp; k++) {
-            const int pr = warp * kPairsPerWarp + k, hh = pr / kQBlk, tq = pr % kQBlk, t = t0 + tq;
-            if (tq >= nq || p0 > t) continue;
-            const float* row = S + ((int64_t)(seq * kHeads + kvh * kGroup + hh) * len + t) * len + p0;
-            const float ls = lsum[pr];
-            const int np = min(kPTile, t - p0 + 1);
-            const float w0 = (lane < np) ? expf_ref(__fsub_rn(row[lane], ls)) : 0.0f;
-            const float w1 = (lane + 32 < np) ? expf_ref(__fsub_rn(row[lane + 32], ls)) : 0.0f;
-            float x0 = a0[k], x1 = a1[k];
-            for (int pp = 0; pp < np; pp++) {
-                const float w = __shfl_sync(0xffffffffu, pp < 32 ? w0 : w1, pp & 31);
-                x0 = __fadd_rn(x0, __fmul_rn(w, vs[pp][lane]));
-                x1 = __fadd_rn(x1, __fmul_rn(w, vs[pp][lane + 32]));
+            for (int i = 0; i < 7; i++) {
+                const float w = wrow[i];
+#pragma unroll
+                for (int k = 0; k < 8; k++) acc[i][k] = __fadd_rn(acc[i][k], __fmul_rn(w, v[k]));
             }
-            a0[k] = x0;
-            a1[k] = x1;
         }
     }
 #pragma unroll
-    for (int k = 0; k < kPairsPerWarp; k++) {
-        const int pr = warp * kPairsPerWarp + k, hh = pr / kQBlk, tq = pr % kQBlk;
+    for (int i = 0; i < 7; i++) {
+        const int pr = 7 * pg + i, tq = pr % kQBlk;
         if (tq >= nq) continue;
-        float* c = ctx + (base + t0 + tq) * kHidden + (kvh * kGroup + hh) * kHeadDim;
-        c[lane] = a0[k];
-        c[lane + 32] = a1[k];
+        float* c = ctx + (base + t0 + tq) * kHidden + (kvh * kGroup + pr / kQBlk) * kHeadDim + 8 * db;
+        *reinterpret_cast<float4*>(c) = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+        *reinterpret_cast<float4*>(c + 4) = make_float4(acc[i][4], acc[i][5], acc[i][6], acc[i][7]);
     }
 }
 
@@ -424,14 +432,13 @@ int prefill_run(tmac_model_s* m, int64_t M, int n_seq, int len, cudaStream_t s)
     pf_embed_kernel<<<(unsigned)M, 128, 0, s>>>(m->emb_raw, p->tokens, p->hidden);
     TMAC_CUDA_TRY(cudaGetLastError());
     const unsigned nblk8 = (unsigned)((M + 7) / 8);
-    const size_t ctx_smem = (size_t)kCtxWarps * len * sizeof(float);
+    const size_t ctx_smem = kCtxSmem;
     static bool attr_done = false;
     if (!attr_done) {
-        TMAC_CUDA_TRY(cudaFuncSetAttribute(pf_softmax_ctx_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024));
+        TMAC_CUDA_TRY(cudaFuncSetAttribute(pf_softmax_ctx_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kCtxSmem));
         TMAC_CUDA_TRY(cudaFuncSetAttribute(pf_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kScoresSmem));
         attr_done = true;
     }
-    if (ctx_smem > 160 * 1024) return fail(TMAC_ERR_SHAPE, "prefill: sequence too long for the attention kernel");
     const dim3 agrid((unsigned)n_seq, kKvHeads, (unsigned)((len + kQBlk - 1) / kQBlk));
     for (int l = 0; l < kLayers; l++) {
         const float* an = vec_or_null(m, lname(l, "attn_norm.weight"));
@@ -460,7 +467,7 @@ int prefill_run(tmac_model_s* m, int64_t M, int n_seq, int len, cudaStream_t s)
         TMAC_CUDA_TRY(cudaGetLastError());
         pf_scores_kernel<<<agrid, 256, kScoresSmem, s>>>(p->qr, p->kr, len, p->scores);
         TMAC_CUDA_TRY(cudaGetLastError());
-        pf_softmax_ctx_kernel<<<agrid, kCtxWarps * 32, ctx_smem, s>>>(p->scores, p->vr, len, p->ctx);
+        pf_softmax_ctx_kernel<<<agrid, kCtxThreads, ctx_smem, s>>>(p->scores, p->vr, len, p->ctx);
         TMAC_CUDA_TRY(cudaGetLastError());
         if ((rc = quantize_rows(p->ctx, kHidden, (int)M, p->xh, p->xl, p->xs, s))) return rc;
         tmac_weight_s* wo = mat(m, lname(l, "attn_output.weight"));
