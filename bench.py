@@ -196,6 +196,43 @@ def cpu_baseline_single():
                       f"(reference's own code; its fpga_sim MatmulAccel FSM thread runs beside the caller)"}
 
 
+def model_extras():
+    """BASELINE configs 4 and 5 through the public model API on this GPU:
+    greedy decode (8-token prompt + 64 steps, tokens checked against the
+    reference's, committed fixture) and batched prefill of 64 x 512 tokens.
+    Wall-clock per call (host buffers in and out), after a warm-up call."""
+    import tmac_zynq_fpga_b200 as tm
+    from tmac_zynq_fpga_b200 import model
+    g = np.load(os.path.join(ROOT, "tests", "golden", "decode_greedy_seed0.npz"))
+    m = tm.Model(model.default_model_path(int(g["model_seed"])), switches=tm.SW_ALL, max_seq=512)
+    prompt, ref = g["prompt"].astype(np.int32), g["tokens"]
+    n = len(ref)
+    toks, _ = m.generate(prompt, n)
+    reps = 5
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        toks, _ = m.generate(prompt, n)
+    dt = (time.perf_counter() - t0) / reps
+    decode = {"tok_s": n / dt, "ms_per_call": 1000 * dt, "prompt_tokens": len(prompt), "generated": n,
+              "ms_per_forward": 1000 * dt / (len(prompt) + n),
+              "tokens_match_reference": bool(np.array_equal(toks, ref)),
+              "config": "BASELINE config 4: 24 layers, mixed Q5_0/Q8_0/Q4_K/Q6_K, greedy, CUDA graphs",
+              "api": "tmac_model_generate"}
+    rng = np.random.default_rng(0)
+    ptoks = rng.integers(0, VOCAB, size=(64, 512)).astype(np.int32)
+    nxt, _ = m.prefill(ptoks)
+    t0 = time.perf_counter()
+    for _ in range(3):
+        nxt2, _ = m.prefill(ptoks)
+    dt = (time.perf_counter() - t0) / 3
+    prefill = {"tok_s": ptoks.size / dt, "ms_per_call": 1000 * dt, "n_seq": 64, "len": 512,
+               "deterministic": bool(np.array_equal(nxt, nxt2)),
+               "config": "BASELINE config 5: 64 x 512 tokens, exact int16 x int16 on tcgen05 int8 MMAs",
+               "api": "tmac_model_prefill"}
+    m.free()
+    return decode, prefill
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -203,6 +240,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-model", action="store_true", help="skip the decode / prefill measurements")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -311,6 +349,9 @@ def main():
         if traffic is not None and world > 1:
             traffic = traffic * rows / VOCAB
         cpu = None if (args.no_cpu_baseline or world > 1) else cpu_baseline_single()
+        decode = prefill = None
+        if world == 1 and not args.no_model:
+            decode, prefill = model_extras()
         out = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
@@ -329,6 +370,8 @@ def main():
                     "d2h_bytes_per_step": rows * 4, "api": "tmac_gemv_host", "steps": e2e_steps},
             "gpu_launches": args.steps,
             "clocks": clocks,
+            "decode": decode,
+            "prefill": prefill,
         }
         print(json.dumps(out))
     for w in weights:
