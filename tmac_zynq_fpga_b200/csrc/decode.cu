@@ -100,10 +100,17 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(float* __restrict__ x, con
                                                       float* __restrict__ xs, int n)
 {
     pdl_launch();
-    pdl_wait();
     __shared__ __align__(16) float xsh[kInter];
     __shared__ float red[8];
     __shared__ float scale;
+    // the norm weights do not depend on the preceding kernel
+    float wv[4];
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        const int i = threadIdx.x + k * blockDim.x;
+        wv[k] = (w && i < n) ? w[i] : 1.0f;
+    }
+    pdl_wait();
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
         float v = x[i];
         if (delta) {
@@ -118,24 +125,34 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(float* __restrict__ x, con
         float sum = 0.0f;
         const float4* x4 = reinterpret_cast<const float4*>(xsh);
         int i = 0;
-        for (; i + 8 <= n; i += 8) {  // loads ahead of the (sequential) adds
-            const float4 a = x4[i / 4], b = x4[i / 4 + 1];
-            sum = __fadd_rn(sum, __fmul_rn(a.x, a.x));
-            sum = __fadd_rn(sum, __fmul_rn(a.y, a.y));
-            sum = __fadd_rn(sum, __fmul_rn(a.z, a.z));
-            sum = __fadd_rn(sum, __fmul_rn(a.w, a.w));
-            sum = __fadd_rn(sum, __fmul_rn(b.x, b.x));
-            sum = __fadd_rn(sum, __fmul_rn(b.y, b.y));
-            sum = __fadd_rn(sum, __fmul_rn(b.z, b.z));
-            sum = __fadd_rn(sum, __fmul_rn(b.w, b.w));
+        for (; i + 32 <= n; i += 32) {  // 32 values loaded ahead of the sequential adds
+            float4 f[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++) f[u] = x4[i / 4 + u];
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                sum = __fadd_rn(sum, __fmul_rn(f[u].x, f[u].x));
+                sum = __fadd_rn(sum, __fmul_rn(f[u].y, f[u].y));
+                sum = __fadd_rn(sum, __fmul_rn(f[u].z, f[u].z));
+                sum = __fadd_rn(sum, __fmul_rn(f[u].w, f[u].w));
+            }
         }
         for (; i < n; i++) sum = __fadd_rn(sum, __fmul_rn(xsh[i], xsh[i]));
-        const float mean = __fdiv_rn(sum, (float)n);
+    const float mean = __fdiv_rn(sum, (float)n);
         scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, 1e-6f)));
     }
     __syncthreads();
     float mx = 0.0f;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        const int i = threadIdx.x + k * blockDim.x;
+        if (i >= n) break;
+        const float v = w ? __fmul_rn(__fmul_rn(xsh[i], wv[k]), scale) : xsh[i];
+        o[i] = v;
+        xsh[i] = v;
+        mx = fmaxf(mx, fabsf(v));
+    }
+    for (int i = threadIdx.x + 4 * blockDim.x; i < n; i += blockDim.x) {
         const float v = w ? __fmul_rn(__fmul_rn(xsh[i], w[i]), scale) : xsh[i];
         o[i] = v;
         xsh[i] = v;
@@ -148,6 +165,8 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(float* __restrict__ x, con
     for (int i = threadIdx.x; i < n; i += blockDim.x) store_xq(xq, xp, n, i, quantize_one(xsh[i], s));
 }
 
+constexpr int kAttnChunk = 128;  // K/V rows staged in shared memory at a time
+
 // One CTA per query head: q/k/v bias add (:1591-1614), RoPE on the head's q
 // and its KV head's k (:1528-1554), KV-cache append by the first query head of
 // each KV group (:1622-1623), then attention over positions 0..pos
@@ -157,14 +176,16 @@ __global__ void __launch_bounds__(256) rope_attention_kernel(
     const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
     const float* __restrict__ bq, const float* __restrict__ bk, const float* __restrict__ bv,
     const float* __restrict__ cs, const float* __restrict__ sn, int pos, const int* pos_dev, float* __restrict__ kc,
-    float* __restrict__ vc, float* __restrict__ ctx)
+    float* __restrict__ vc, float* __restrict__ ctx, int nscore)
 {
     pdl_launch();
     pdl_wait();
-    extern __shared__ float sc[];  // [pos + 1] scores, then weights
+    extern __shared__ float sc[];  // [nsc] scores, then weights; [nsc] exp terms; K/V staging
+    __shared__ float red_s[8];
     __shared__ float qs[kHeadDim], ks[kHeadDim], vs[kHeadDim];
     __shared__ float log_sum;
     if (pos_dev) pos = *pos_dev;
+    const int nsc = nscore;
     const int h = blockIdx.x, kvh = h / (kHeads / kKvHeads);
     const float* c = cs + (int64_t)pos * (kHeadDim / 2);
     const float* sv = sn + (int64_t)pos * (kHeadDim / 2);
@@ -186,31 +207,58 @@ __global__ void __launch_bounds__(256) rope_attention_kernel(
         kc[(int64_t)pos * kKvDim + kvh * kHeadDim + threadIdx.x] = ks[threadIdx.x];
         vc[(int64_t)pos * kKvDim + kvh * kHeadDim + threadIdx.x] = vs[threadIdx.x];
     }
-    for (int p = threadIdx.x; p <= pos; p += blockDim.x) {
-        const float* kp = (p == pos) ? ks : kc + (int64_t)p * kKvDim + kvh * kHeadDim;
-        float sum = 0.0f;
-        for (int d = 0; d < kHeadDim; d++) sum = __fadd_rn(sum, __fmul_rn(qs[d], kp[d]));
-        sc[p] = __fdiv_rn(sum, 8.0f);  // / sqrtf(64)
+    // scores: K rows of this KV head staged in shared memory, 128 positions at a
+    // time (rows padded to 65 floats), one position per thread, d in order
+    float* kv = sc + 2 * nsc;  // [kAttnChunk][kHeadDim + 1]
+    for (int c0 = 0; c0 <= pos; c0 += kAttnChunk) {
+        const int rows = min(kAttnChunk, pos + 1 - c0);
+        __syncthreads();
+        for (int i = threadIdx.x; i < rows * kHeadDim; i += blockDim.x) {
+            const int r = i / kHeadDim, d = i % kHeadDim, p = c0 + r;
+            kv[r * (kHeadDim + 1) + d] = (p == pos) ? ks[d] : kc[(int64_t)p * kKvDim + kvh * kHeadDim + d];
+        }
+        __syncthreads();
+        for (int r = threadIdx.x; r < rows; r += blockDim.x) {
+            const float* kp = kv + r * (kHeadDim + 1);
+            float sum = 0.0f;
+            for (int d = 0; d < kHeadDim; d++) sum = __fadd_rn(sum, __fmul_rn(qs[d], kp[d]));
+            sc[c0 + r] = __fdiv_rn(sum, 8.0f);  // / sqrtf(64)
+        }
     }
     __syncthreads();
+    // max (order-free), the exp terms in parallel, their sum in position order
+    float mx = -INFINITY;
+    for (int p = threadIdx.x; p <= pos; p += blockDim.x) mx = fmaxf(mx, sc[p]);
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((threadIdx.x & 31) == 0) red_s[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    mx = red_s[0];
+    for (int i = 1; i < (int)(blockDim.x >> 5); i++) mx = fmaxf(mx, red_s[i]);
+    float* ex = sc + pos + 1;
+    for (int p = threadIdx.x; p <= pos; p += blockDim.x) ex[p] = expf_ref(__fsub_rn(sc[p], mx));
+    __syncthreads();
     if (threadIdx.x == 0) {
-        float mx = sc[0];
-        for (int p = 1; p <= pos; p++) mx = sc[p] > mx ? sc[p] : mx;
         float es = 0.0f;
-        for (int p = 0; p <= pos; p++) es = __fadd_rn(es, expf_ref(__fsub_rn(sc[p], mx)));
+        for (int p = 0; p <= pos; p++) es = __fadd_rn(es, ex[p]);
         log_sum = __fadd_rn(logf_ref(es), mx);
     }
     __syncthreads();
     for (int p = threadIdx.x; p <= pos; p += blockDim.x) sc[p] = expf_ref(__fsub_rn(sc[p], log_sum));
     __syncthreads();
-    for (int d = threadIdx.x; d < kHeadDim; d += blockDim.x) {
-        float a = 0.0f;
-        for (int p = 0; p <= pos; p++) {
-            const float vv = (p == pos) ? vs[d] : vc[(int64_t)p * kKvDim + kvh * kHeadDim + d];
-            a = __fadd_rn(a, __fmul_rn(sc[p], vv));
+    // context: V rows staged the same way, positions in order
+    float a = 0.0f;
+    for (int c0 = 0; c0 <= pos; c0 += kAttnChunk) {
+        const int rows = min(kAttnChunk, pos + 1 - c0);
+        __syncthreads();
+        for (int i = threadIdx.x; i < rows * kHeadDim; i += blockDim.x) {
+            const int r = i / kHeadDim, d = i % kHeadDim, p = c0 + r;
+            kv[r * (kHeadDim + 1) + d] = (p == pos) ? vs[d] : vc[(int64_t)p * kKvDim + kvh * kHeadDim + d];
         }
-        ctx[h * kHeadDim + d] = a;
+        __syncthreads();
+        if (threadIdx.x < kHeadDim)
+            for (int r = 0; r < rows; r++) a = __fadd_rn(a, __fmul_rn(sc[c0 + r], kv[r * (kHeadDim + 1) + threadIdx.x]));
     }
+    if (threadIdx.x < kHeadDim) ctx[h * kHeadDim + threadIdx.x] = a;
 }
 
 // silu(gate) * up (:459-461, :1697-1700), then the quantisation ffn_down's
@@ -293,10 +341,11 @@ int layer(tmac_model_s* m, int l, int pos, cudaStream_t s, const int* pos_dev = 
         if ((rc = gemv(m, lname(l, "attn_v.weight"), m->xn, m->v, s, true))) return rc;
     }
     const int nscore = pos_dev ? m->max_seq : pos + 1;
-    TMAC_CUDA_TRY(launch_k(rope_attention_kernel, dim3(kHeads), dim3(256), nscore * sizeof(float), s, (const float*)m->q,
+    TMAC_CUDA_TRY(launch_k(rope_attention_kernel, dim3(kHeads), dim3(256),
+                           (2 * nscore + kAttnChunk * (kHeadDim + 1)) * sizeof(float), s, (const float*)m->q,
                            (const float*)m->k, (const float*)m->v, vec_or_null(m, lname(l, "attn_q.bias")),
                            vec_or_null(m, lname(l, "attn_k.bias")), vec_or_null(m, lname(l, "attn_v.bias")),
-                           (const float*)m->rope_c, (const float*)m->rope_s, pos, pos_dev, kc, vc, m->ctx));
+                           (const float*)m->rope_c, (const float*)m->rope_s, pos, pos_dev, kc, vc, m->ctx, nscore));
     if ((rc = gemv(m, lname(l, "attn_output.weight"), m->ctx, m->attn, s))) return rc;
     TMAC_CUDA_TRY(launch_k(rmsnorm_kernel, dim3(1), dim3(256), 0, s, m->hidden, (const float*)m->attn, fn, m->xn,
                            m->xq, m->xp, m->xs, kHidden));
