@@ -196,38 +196,58 @@ def cpu_baseline_single():
                       f"(reference's own code; its fpga_sim MatmulAccel FSM thread runs beside the caller)"}
 
 
-def model_extras():
-    """BASELINE configs 4 and 5 through the public model API on this GPU:
-    greedy decode (8-token prompt + 64 steps, tokens checked against the
-    reference's, committed fixture) and batched prefill of 64 x 512 tokens.
-    Wall-clock per call (host buffers in and out), after a warm-up call."""
+def model_extras(world=1, rank=0):
+    """BASELINE configs 4 and 5 through the public model API: greedy decode
+    (8-token prompt + 64 steps, tokens checked against the reference's committed
+    fixture; one GPU only: decode does not shard) and batched prefill of 64 x 512
+    tokens, sharded by sequence over the ranks (no collective on the data path;
+    time = max over ranks).  Wall clock per call (host buffers in and out), after
+    a warm-up call."""
+    import torch
+    import torch.distributed as dist
     import tmac_zynq_fpga_b200 as tm
-    from tmac_zynq_fpga_b200 import model
+    from tmac_zynq_fpga_b200 import model, shard
     g = np.load(os.path.join(ROOT, "tests", "golden", "decode_greedy_seed0.npz"))
-    m = tm.Model(model.default_model_path(int(g["model_seed"])), switches=tm.SW_ALL, max_seq=512)
-    prompt, ref = g["prompt"].astype(np.int32), g["tokens"]
-    n = len(ref)
-    toks, _ = m.generate(prompt, n)
-    reps = 5
-    t0 = time.perf_counter()
-    for _ in range(reps):
+    m = tm.Model(model.default_model_path(int(g["model_seed"])), switches=tm.SW_ALL, max_seq=512,
+                 device=torch.cuda.current_device())
+    decode = None
+    if world == 1:
+        prompt, ref = g["prompt"].astype(np.int32), g["tokens"]
+        n = len(ref)
         toks, _ = m.generate(prompt, n)
-    dt = (time.perf_counter() - t0) / reps
-    decode = {"tok_s": n / dt, "ms_per_call": 1000 * dt, "prompt_tokens": len(prompt), "generated": n,
-              "ms_per_forward": 1000 * dt / (len(prompt) + n),
-              "tokens_match_reference": bool(np.array_equal(toks, ref)),
-              "config": "BASELINE config 4: 24 layers, mixed Q5_0/Q8_0/Q4_K/Q6_K, greedy, CUDA graphs",
-              "api": "tmac_model_generate"}
+        reps = 5
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            toks, _ = m.generate(prompt, n)
+        dt = (time.perf_counter() - t0) / reps
+        decode = {"tok_s": n / dt, "ms_per_call": 1000 * dt, "prompt_tokens": len(prompt), "generated": n,
+                  "ms_per_forward": 1000 * dt / (len(prompt) + n),
+                  "tokens_match_reference": bool(np.array_equal(toks, ref)),
+                  "config": "BASELINE config 4: 24 layers, mixed Q5_0/Q8_0/Q4_K/Q6_K, greedy, CUDA graphs",
+                  "api": "tmac_model_generate"}
     rng = np.random.default_rng(0)
     ptoks = rng.integers(0, VOCAB, size=(64, 512)).astype(np.int32)
-    nxt, _ = m.prefill(ptoks)
+    s0, s1 = shard.sequence_shard(len(ptoks), world, rank)
+    mine = ptoks[s0:s1]
+    nxt, _ = m.prefill(mine)
+    reps = 3
+    if world > 1:
+        dist.barrier()
     t0 = time.perf_counter()
-    for _ in range(3):
-        nxt2, _ = m.prefill(ptoks)
-    dt = (time.perf_counter() - t0) / 3
-    prefill = {"tok_s": ptoks.size / dt, "ms_per_call": 1000 * dt, "n_seq": 64, "len": 512,
-               "deterministic": bool(np.array_equal(nxt, nxt2)),
-               "config": "BASELINE config 5: 64 x 512 tokens, exact int16 x int16 on tcgen05 int8 MMAs",
+    for _ in range(reps):
+        nxt2, _ = m.prefill(mine)
+    dt = torch.tensor([(time.perf_counter() - t0) / reps], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(dt, op=dist.ReduceOp.MAX)
+        allnxt = shard.gather_next_tokens(nxt2, len(ptoks))
+    else:
+        allnxt = nxt2
+    dt = float(dt.item())
+    prefill = {"tok_s": ptoks.size / dt, "ms_per_call": 1000 * dt, "n_seq": len(ptoks), "len": ptoks.shape[1],
+               "n_gpus": world, "seq_per_gpu": s1 - s0, "scaling": "strong (fixed 64 x 512 batch)",
+               "deterministic": bool(np.array_equal(nxt, nxt2)), "next_tokens_gathered": int(len(allnxt)),
+               "config": "BASELINE config 5: 64 x 512 tokens, sequence shards, exact int16 x int16 on "
+                         "tcgen05 int8 MMAs",
                "api": "tmac_model_prefill"}
     m.free()
     return decode, prefill
@@ -342,6 +362,10 @@ def main():
     if world == 1:
         assert tok == int(np.argmax(yl)), "fused top-1 disagrees with argmax of the logits"
 
+    decode = prefill = None
+    if not args.no_model:
+        decode, prefill = model_extras(world, rank)
+
     if rank == 0:
         pk, pk_kind = peaks()
         achieved = alg_bytes(rows) / (kernel_us * 1e-6) / 1e9
@@ -349,9 +373,6 @@ def main():
         if traffic is not None and world > 1:
             traffic = traffic * rows / VOCAB
         cpu = None if (args.no_cpu_baseline or world > 1) else cpu_baseline_single()
-        decode = prefill = None
-        if world == 1 and not args.no_model:
-            decode, prefill = model_extras()
         out = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,

@@ -74,3 +74,24 @@ def test_shard_bounds_cover_vocab():
         b = [shard.shard_bounds(151936, world, r) for r in range(world)]
         assert b[0][0] == 0 and b[-1][1] == 151936
         assert all(b[i][1] == b[i + 1][0] for i in range(world - 1))
+
+
+def _prefill_rank(rank, world, port, n_seq, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    toks = np.random.default_rng(3).integers(0, 151936, size=(n_seq, 16))
+    s0, s1 = shard.sequence_shard(n_seq, world, rank)
+    # stand-in for each rank's prefill: a deterministic function of the sequence
+    local = (toks[s0:s1].sum(axis=1) * 7919 % 151936).astype(np.int32)
+    out[rank] = shard.gather_next_tokens(local, n_seq).tolist()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("n_seq", [64, 7])
+def test_two_rank_sequence_sharded_prefill_gathers_in_batch_order(n_seq):
+    world = 2
+    out = mp.Manager().dict()
+    mp.spawn(_prefill_rank, args=(world, _free_port(), n_seq, out), nprocs=world, join=True)
+    toks = np.random.default_rng(3).integers(0, 151936, size=(n_seq, 16))
+    expect = (toks.sum(axis=1) * 7919 % 151936).astype(np.int32).tolist()
+    assert out[0] == expect and out[1] == expect

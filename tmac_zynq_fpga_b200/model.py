@@ -97,8 +97,9 @@ def default_model_path(seed: int = 0) -> str:
     os.makedirs(d, exist_ok=True)
     p = os.path.join(d, f"qwen2_0_5b_synth_seed{seed}.tmac")
     if not os.path.exists(p):
-        write_tmac(p + ".tmp", seed=seed)
-        os.replace(p + ".tmp", p)
+        tmp = f"{p}.tmp{os.getpid()}"  # one writer per process; the rename is atomic
+        write_tmac(tmp, seed=seed)
+        os.replace(tmp, p)
     return p
 
 

@@ -43,3 +43,32 @@ def all_reduce_top1(key_tensor, group=None):
     import torch.distributed as dist
     dist.all_reduce(key_tensor, op=dist.ReduceOp.MAX, group=group)
     return key_tensor
+
+
+# ------------------------------------------------------------------ prefill
+# The multi-sequence prefill batch shards by sequence: rank r prefills sequences
+# [s0, s1) of the batch with tmac_model_prefill on its own GPU.  Sequences are
+# independent, so there is no collective on the data path; the per-sequence
+# next tokens are gathered once at the end.
+
+def sequence_shard(n_seq: int, world: int, rank: int):
+    """Contiguous sequence range of `rank` (sizes differ by at most one)."""
+    return shard_bounds(n_seq, world, rank)
+
+
+def gather_next_tokens(local, n_seq: int, group=None):
+    """All ranks' next tokens (int32 [s1 - s0] each) in batch order, on every rank."""
+    import torch
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    dev = "cuda" if dist.get_backend(group) == "nccl" else "cpu"
+    most = -(-n_seq // world)
+    buf = torch.full((most,), -1, dtype=torch.int64, device=dev)
+    buf[: len(local)] = torch.as_tensor(np.asarray(local, dtype=np.int64), device=dev)
+    parts = [torch.empty_like(buf) for _ in range(world)]
+    dist.all_gather(parts, buf, group=group)
+    out = []
+    for r in range(world):
+        s0, s1 = sequence_shard(n_seq, world, r)
+        out.append(parts[r][: s1 - s0].cpu().numpy())
+    return np.concatenate(out).astype(np.int32)
