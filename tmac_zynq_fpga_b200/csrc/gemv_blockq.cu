@@ -492,7 +492,7 @@ TMAC_DEV long long xq_at(const uint8_t* xpl, int64_t cols, int b, int64_t col)
 }
 
 template <int TYPE, int NB>
-__global__ void __launch_bounds__(512) blockq_gemv_kernel(BqArgs a)
+__global__ void __launch_bounds__(NB == 1 ? 1024 : 512) blockq_gemv_kernel(BqArgs a)
 {
     extern __shared__ __align__(128) uint8_t smem[];
     const int64_t cols = a.cols, cpr = cols / 32, nblk = cols / Geo<TYPE>::kBlockVals;
@@ -759,7 +759,8 @@ int launch_nb(const tmac_weight_s* w, BqArgs a, cudaStream_t s)
     const int grid = (int)((a.groups + gpc - 1) / gpc);
     const int64_t slots = (TYPE == TMAC_TYPE_Q5_0) ? gpc : gpc * 8;
     const int64_t steps = (TYPE == TMAC_TYPE_Q5_0) ? (a.cols / 32 + 3) / 4 : (a.cols / 256 + 3) / 4;
-    const int warps = (int)std::max<int64_t>(1, std::min<int64_t>(16, slots * steps));
+    // batch 1 fits 64 registers a thread: up to 32 warps hide the decode's latency
+    const int warps = (int)std::max<int64_t>(1, std::min<int64_t>(NB == 1 ? 32 : 16, slots * steps));
     TMAC_CUDA_TRY(launch_k(blockq_gemv_kernel<TYPE, NB>, dim3(grid), dim3(warps * 32),
                            (size_t)BqSmem(gpc, a.group_bytes, a.nb, a.cols).total, s, a));
     TMAC_CUDA_TRY(cudaGetLastError());
