@@ -111,6 +111,8 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(float* __restrict__ x, con
         wv[k] = (w && i < n) ? w[i] : 1.0f;
     }
     pdl_wait();
+    // the squares in parallel (into xsh[n..2n), n <= kInter / 2), their sum in order
+    float* sq = xsh + ((n + 3) & ~3);
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
         float v = x[i];
         if (delta) {
@@ -118,12 +120,13 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(float* __restrict__ x, con
             x[i] = v;
         }
         xsh[i] = v;
+        sq[i] = __fmul_rn(v, v);
     }
     __syncthreads();
     if (threadIdx.x == 0 && !w) scale = 1.0f;
     if (threadIdx.x == 0 && w) {
         float sum = 0.0f;
-        const float4* x4 = reinterpret_cast<const float4*>(xsh);
+        const float4* x4 = reinterpret_cast<const float4*>(sq);
         int i = 0;
         for (; i + 32 <= n; i += 32) {  // 32 values loaded ahead of the sequential adds
             float4 f[8];
@@ -131,14 +134,14 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(float* __restrict__ x, con
             for (int u = 0; u < 8; u++) f[u] = x4[i / 4 + u];
 #pragma unroll
             for (int u = 0; u < 8; u++) {
-                sum = __fadd_rn(sum, __fmul_rn(f[u].x, f[u].x));
-                sum = __fadd_rn(sum, __fmul_rn(f[u].y, f[u].y));
-                sum = __fadd_rn(sum, __fmul_rn(f[u].z, f[u].z));
-                sum = __fadd_rn(sum, __fmul_rn(f[u].w, f[u].w));
+                sum = __fadd_rn(sum, f[u].x);
+                sum = __fadd_rn(sum, f[u].y);
+                sum = __fadd_rn(sum, f[u].z);
+                sum = __fadd_rn(sum, f[u].w);
             }
         }
-        for (; i < n; i++) sum = __fadd_rn(sum, __fmul_rn(xsh[i], xsh[i]));
-    const float mean = __fdiv_rn(sum, (float)n);
+        for (; i < n; i++) sum = __fadd_rn(sum, sq[i]);
+        const float mean = __fdiv_rn(sum, (float)n);
         scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, 1e-6f)));
     }
     __syncthreads();
