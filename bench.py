@@ -261,6 +261,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-model", action="store_true", help="skip the decode / prefill measurements")
+    ap.add_argument("--collective", choices=["peer", "nccl"], default="peer",
+                    help="top-1 merge across ranks: NVLink peer-memory exchange kernel or NCCL all-reduce")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -297,12 +299,35 @@ def main():
     key = torch.zeros(1, dtype=torch.int64, device="cuda")
     stream = torch.cuda.current_stream()
 
+    # top-1 merge across ranks: the peer-memory exchange kernel (checked against
+    # the NCCL all-reduce of the same key first), else the NCCL all-reduce
+    merge, merge_kind = None, "none"
+    if world > 1:
+        merge_kind = "nccl int64 MAX all-reduce"
+        if args.collective == "peer":
+            from tmac_zynq_fpga_b200 import shard
+            try:
+                xchg = shard.PeerTop1(local)
+                weights[0].gemv_top1(x, y, key, index_base=r0, stream=stream)
+                ref = key.clone()
+                dist.all_reduce(ref, op=dist.ReduceOp.MAX)
+                xchg(key, stream)
+                torch.cuda.synchronize()
+                if not torch.equal(ref, key) or tm.device_error(local) != 0:
+                    raise RuntimeError("peer exchange disagrees with the NCCL all-reduce")
+                merge, merge_kind = xchg, "NVLink peer-memory exchange kernel (tmac_xchg_top1)"
+            except Exception as e:  # keep NCCL
+                merge_kind = f"nccl int64 MAX all-reduce (peer exchange unavailable: {e})"
+
     def step(i):
         # logits of this rank's vocab shard + their top-1 key (one fused kernel),
-        # then the global greedy token: one int64 MAX all-reduce over NCCL.
+        # then the global greedy token on every rank
         weights[i % ncopies].gemv_top1(x, y, key, index_base=r0, stream=stream)
         if world > 1:
-            dist.all_reduce(key, op=dist.ReduceOp.MAX)
+            if merge is not None:
+                merge(key, stream)
+            else:
+                dist.all_reduce(key, op=dist.ReduceOp.MAX)
 
     for i in range(args.warmup):
         step(i)
@@ -378,7 +403,7 @@ def main():
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "int16/int64", "data": "synthetic",
             "config": {"workload": WORKLOAD, "rows": VOCAB, "cols": HIDDEN, "batch": 1,
-                       "step": "shard logits GEMV with fused top-1 key" + (" + NCCL int64 MAX all-reduce" if world > 1 else ""),
+                       "step": "shard logits GEMV with fused top-1 key" + (f" + {merge_kind}" if world > 1 else ""),
                        "greedy_token": tok,
                        "parallelism": f"vocab-row shards x{world}", "shard_rows": rows,
                        "l2": f"inputs larger than L2: {ncopies} rotating weight copies of "
@@ -389,7 +414,7 @@ def main():
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_val, "unit": UNIT, "h2d_bytes_per_step": HIDDEN * 4,
                     "d2h_bytes_per_step": rows * 4, "api": "tmac_gemv_host", "steps": e2e_steps},
-            "gpu_launches": args.steps,
+            "gpu_launches": args.steps * (2 if merge is not None else 1),
             "clocks": clocks,
             "decode": decode,
             "prefill": prefill,
@@ -397,6 +422,8 @@ def main():
         print(json.dumps(out))
     for w in weights:
         w.free()
+    if merge is not None:
+        merge.free()
     if world > 1:
         dist.destroy_process_group()
 

@@ -197,6 +197,25 @@ int tmac_gemm(tmac_weight_t w, const float* x, float* y, int64_t* row_acc, int m
 int tmac_gemv_static(tmac_weight_t w, const float* x, float* y, int batch, void* stream);
 
 /* ------------------------------------------------------------------------ */
+/* Top-1 merge of vocab-sharded logits over NVLink peer memory (multi-GPU
+ * greedy step; the reference samples from the whole logits vector on one
+ * host, sim/tmac_gguf.cpp:1974-1990).  One exchange object per rank (one
+ * process per GPU): create it, pass every rank's IPC handle to every rank
+ * (e.g. an all-gather on the host), open, then per step tmac_xchg_top1 turns
+ * this rank's shard key (device uint64, from tmac_gemv_top1) into the global
+ * maximum key on every rank.  The kernel stores the key into every rank's
+ * buffer and waits for all ranks' keys of the same step (bounded: after ~2 s it
+ * records TMAC_ERR_TIMEOUT, read with tmac_device_error, and leaves the key).
+ * All ranks must call tmac_xchg_top1 the same number of times. */
+typedef struct tmac_xchg_s* tmac_xchg_t;
+#define TMAC_XCHG_HANDLE_BYTES 64
+int tmac_xchg_create(int device, int world, int rank, tmac_xchg_t* out);
+int tmac_xchg_ipc_handle(tmac_xchg_t x, void* handle);           /* TMAC_XCHG_HANDLE_BYTES bytes */
+int tmac_xchg_open(tmac_xchg_t x, const void* handles);          /* world x TMAC_XCHG_HANDLE_BYTES */
+int tmac_xchg_top1(tmac_xchg_t x, uint64_t* key, void* stream);
+int tmac_xchg_free(tmac_xchg_t x);
+
+/* ------------------------------------------------------------------------ */
 /* Phase-B descriptor chain (sim/fpga_sim.hpp:1254-1310, sim/tmac_gguf.cpp:513-880).
  *
  * A chain is a linked list of 32-byte descriptors inside a byte arena that

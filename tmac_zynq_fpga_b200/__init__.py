@@ -84,6 +84,11 @@ def lib():
             "tmac_gemv_host": (ctypes.c_int, [_P, _P, _P, ctypes.c_int]),
             "tmac_gemv_static": (ctypes.c_int, [_P, _P, _P, ctypes.c_int, _P]),
             "tmac_gemm": (ctypes.c_int, [_P, _P, _P, _P, ctypes.c_int, _P]),
+            "tmac_xchg_create": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.POINTER(_P)]),
+            "tmac_xchg_ipc_handle": (ctypes.c_int, [_P, _P]),
+            "tmac_xchg_open": (ctypes.c_int, [_P, ctypes.c_char_p]),
+            "tmac_xchg_top1": (ctypes.c_int, [_P, _P, _P]),
+            "tmac_xchg_free": (ctypes.c_int, [_P]),
             "tmac_reserve": (ctypes.c_int, [ctypes.c_int, _I64, _I64]),
             "tmac_top1": (ctypes.c_int, [_P, _I64, _I64, _P, _P]),
             "tmac_gemv_top1": (ctypes.c_int, [_P, _P, _P, _P, _I64, ctypes.c_int, _P]),

@@ -1,0 +1,164 @@
+// xchg.cu -- the logits top-1 merge across GPUs over NVLink peer memory.
+//
+// Each rank's logits GEMV leaves the packed top-1 key of its vocab shard on its
+// device (tmac_gemv_top1).  The global greedy token is the maximum key over the
+// ranks (the reference's sample_token with top-1, sim/tmac_gguf.cpp:1974-1990,
+// over the whole vocabulary).  Instead of a library all-reduce, one small kernel
+// per step stores the key into a slot of every rank's exchange buffer (plain
+// stores to peer memory through CUDA IPC mappings), then waits for every
+// rank's slot of this step in its own buffer and takes the maximum.
+//
+// Buffer of each rank: keys[2][world] then tags[2][world] (uint64).  Step s uses
+// half s & 1: the key is stored, then the tag s with release semantics at system
+// scope; the reader acquires the tag before reading the key.  A rank can be at
+// most one step ahead of another (it cannot finish step s + 1 before every rank
+// has published s + 1, which each does only after reading step s), so the other
+// half is never overwritten while it is still being read.  Every wait is
+// bounded (~2 s): on expiry the kernel records TMAC_ERR_TIMEOUT and returns.
+#include "xchg.cuh"
+
+#include <cstring>
+
+namespace tmac {
+
+XchgDev xchg_dev(const tmac_xchg_s* x)
+{
+    XchgDev d;
+    d.peers = x->peer_dev;
+    d.own = x->buf;
+    d.step = x->step;
+    d.partial = x->partial;
+    d.counter = x->counter;
+    d.world = x->world;
+    d.rank = x->rank;
+    return d;
+}
+
+namespace {
+
+constexpr int kMaxRanks = 64;
+
+// One warp per 32 ranks; thread r publishes to rank r and reads rank r's slot.
+__global__ void xchg_top1_kernel(unsigned long long* key, XchgDev x, int* err)
+{
+    __shared__ unsigned long long best[kMaxRanks / 32];
+    __shared__ int failed;
+    pdl_launch();
+    pdl_wait();  // the key comes from the preceding kernel
+    const int t = threadIdx.x;
+    const uint64_t step = *x.step + 1;
+    if (t == 0) failed = 0;
+    __syncthreads();
+    if (t < x.world) xchg_publish(x, t, step, *key);
+    unsigned long long mine = 0;
+    if (t < x.world && !xchg_read(x, t, step, &mine)) {
+        failed = 1;
+        if (err) atomicExch(err, (int)TMAC_ERR_TIMEOUT);
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long v = __shfl_xor_sync(0xffffffffu, mine, o);
+        mine = v > mine ? v : mine;
+    }
+    if ((t & 31) == 0) best[t >> 5] = mine;
+    __syncthreads();
+    if (t == 0) {
+        unsigned long long m = 0;
+        for (int w = 0; w < (int)(blockDim.x >> 5); w++) m = best[w] > m ? best[w] : m;
+        if (!failed) *key = m;
+        *x.step = step;
+    }
+}
+
+}  // namespace
+}  // namespace tmac
+
+using namespace tmac;
+
+extern "C" {
+
+int tmac_xchg_create(int device, int world, int rank, tmac_xchg_t* out)
+{
+    if (!out) return fail(TMAC_ERR_INVALID, "NULL output");
+    *out = nullptr;
+    if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world) return fail(TMAC_ERR_SHAPE, "bad world / rank");
+    DeviceGuard dg(device);
+    if (!dg.ok) return fail(TMAC_ERR_CUDA, "cudaSetDevice failed");
+    tmac_xchg_s* x = new tmac_xchg_s();
+    x->device = device;
+    x->world = world;
+    x->rank = rank;
+    const size_t bytes = (size_t)4 * world * sizeof(uint64_t);
+    cudaError_t e = cudaMalloc(&x->buf, bytes);
+    if (e == cudaSuccess) e = cudaMemset(x->buf, 0, bytes);
+    if (e == cudaSuccess) e = cudaMalloc(&x->step, sizeof(uint64_t));
+    if (e == cudaSuccess) e = cudaMemset(x->step, 0, sizeof(uint64_t));
+    if (e == cudaSuccess) e = cudaMalloc(&x->peer_dev, world * sizeof(uint64_t*));
+    if (e == cudaSuccess) e = cudaMalloc(&x->partial, sizeof(unsigned long long) + sizeof(unsigned));
+    if (e == cudaSuccess) e = cudaMemset(x->partial, 0, sizeof(unsigned long long) + sizeof(unsigned));
+    if (e == cudaSuccess) x->counter = reinterpret_cast<unsigned*>(x->partial + 1);
+    if (e != cudaSuccess) {
+        if (x->buf) cudaFree(x->buf);
+        if (x->step) cudaFree(x->step);
+        delete x;
+        return cuda_fail(e, "tmac_xchg_create");
+    }
+    x->peer.assign(world, nullptr);
+    x->peer[rank] = x->buf;
+    *out = x;
+    return TMAC_OK;
+}
+
+int tmac_xchg_ipc_handle(tmac_xchg_t x, void* handle)
+{
+    if (!x || !handle) return fail(TMAC_ERR_INVALID, "NULL argument");
+    DeviceGuard dg(x->device);
+    cudaIpcMemHandle_t h;
+    TMAC_CUDA_TRY(cudaIpcGetMemHandle(&h, x->buf));
+    memcpy(handle, &h, sizeof(h));
+    return TMAC_OK;
+}
+
+int tmac_xchg_open(tmac_xchg_t x, const void* handles)
+{
+    if (!x || !handles) return fail(TMAC_ERR_INVALID, "NULL argument");
+    DeviceGuard dg(x->device);
+    for (int r = 0; r < x->world; r++) {
+        if (r == x->rank) continue;
+        cudaIpcMemHandle_t h;
+        memcpy(&h, (const uint8_t*)handles + (size_t)r * TMAC_XCHG_HANDLE_BYTES, sizeof(h));
+        void* p = nullptr;
+        TMAC_CUDA_TRY(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+        x->peer[r] = static_cast<uint64_t*>(p);
+    }
+    TMAC_CUDA_TRY(cudaMemcpy(x->peer_dev, x->peer.data(), x->world * sizeof(uint64_t*), cudaMemcpyHostToDevice));
+    return TMAC_OK;
+}
+
+int tmac_xchg_top1(tmac_xchg_t x, uint64_t* key, void* stream)
+{
+    if (!x || !key) return fail(TMAC_ERR_INVALID, "NULL argument");
+    for (int r = 0; r < x->world; r++)
+        if (!x->peer[r]) return fail(TMAC_ERR_INVALID, "tmac_xchg_open has not mapped every rank");
+    DeviceGuard dg(x->device);
+    const int threads = (x->world + 31) / 32 * 32;
+    TMAC_CUDA_TRY(launch_k(xchg_top1_kernel, dim3(1), dim3(threads), 0, (cudaStream_t)stream,
+                           reinterpret_cast<unsigned long long*>(key), xchg_dev(x), device_error_word(x->device)));
+    TMAC_CUDA_TRY(cudaGetLastError());
+    return TMAC_OK;
+}
+
+int tmac_xchg_free(tmac_xchg_t x)
+{
+    if (!x) return TMAC_OK;
+    DeviceGuard dg(x->device);
+    for (int r = 0; r < x->world; r++)
+        if (r != x->rank && x->peer[r]) cudaIpcCloseMemHandle(x->peer[r]);
+    cudaFree(x->peer_dev);
+    cudaFree(x->partial);
+    cudaFree(x->step);
+    cudaFree(x->buf);
+    delete x;
+    return TMAC_OK;
+}
+
+}  // extern "C"

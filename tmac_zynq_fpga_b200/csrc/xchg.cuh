@@ -1,0 +1,94 @@
+// xchg.cuh -- the peer-memory top-1 exchange shared by xchg.cu (a kernel of its
+// own) and the Q8_0 logits GEMV (fused into its last CTA, gemv_q8_0.cu).
+//
+// Buffer of each rank: keys[2][world] then tags[2][world] (uint64).  Step s uses
+// half s & 1: the key is stored into every rank's buffer, then the tag s with
+// release semantics at system scope; the reader acquires each rank's tag in its
+// own buffer before reading the key.  A rank can be at most one step ahead of
+// another (it cannot finish step s + 1 before every rank has published s + 1,
+// which each does only after reading step s), so the other half is never
+// overwritten while it is still being read.  Waits are bounded (~2 s).
+#pragma once
+
+#include "common.cuh"
+
+#include <vector>
+
+struct tmac_xchg_s {
+    int device = 0, world = 0, rank = 0;
+    uint64_t* buf = nullptr;           // this rank's keys[2][world] | tags[2][world]
+    uint64_t* step = nullptr;          // device step counter of this rank
+    unsigned long long* partial = nullptr;  // fused GEMV: running key of this rank's shard
+    unsigned* counter = nullptr;            // fused GEMV: CTAs finished
+    std::vector<uint64_t*> peer;       // every rank's buffer as mapped here (own = buf)
+    uint64_t** peer_dev = nullptr;     // the same table on the device
+};
+
+namespace tmac {
+
+struct XchgDev {
+    uint64_t** peers = nullptr;  // nullptr: no exchange
+    uint64_t* own = nullptr;
+    uint64_t* step = nullptr;
+    unsigned long long* partial = nullptr;
+    unsigned* counter = nullptr;
+    int world = 0, rank = 0;
+};
+
+TMAC_DEV void st_release_sys(uint64_t* p, uint64_t v)
+{
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+TMAC_DEV uint64_t ld_acquire_sys(const uint64_t* p)
+{
+    uint64_t v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Publishes `k` for this step to rank t (thread t < world).
+TMAC_DEV void xchg_publish(const XchgDev& x, int t, uint64_t step, unsigned long long k)
+{
+    const int half = (int)(step & 1);
+    uint64_t* dst = x.peers[t];
+    dst[half * x.world + x.rank] = k;
+    st_release_sys(dst + 2 * x.world + half * x.world + x.rank, step);
+}
+
+// Rank t's key of this step from the own buffer; false after ~2 s.
+TMAC_DEV bool xchg_read(const XchgDev& x, int t, uint64_t step, unsigned long long* k)
+{
+    const int half = (int)(step & 1);
+    const uint64_t* tag = x.own + 2 * x.world + half * x.world + t;
+    if (ld_acquire_sys(tag) != step) {
+        const uint64_t t0 = global_timer_ns();
+        for (uint32_t it = 1;; it++) {
+            if (ld_acquire_sys(tag) == step) break;
+            if ((it & 255u) == 0 && global_timer_ns() - t0 > 2000000000ull) return false;
+        }
+    }
+    *k = x.own[half * x.world + t];
+    return true;
+}
+
+// One thread: publish to every rank, then the maximum of every rank's key
+// (*out unchanged and TMAC_ERR_TIMEOUT recorded if a rank does not arrive).
+TMAC_DEV void xchg_top1_thread(const XchgDev& x, unsigned long long k, unsigned long long* out, int* err)
+{
+    const uint64_t step = *x.step + 1;
+    for (int t = 0; t < x.world; t++) xchg_publish(x, t, step, k);
+    unsigned long long m = 0;
+    bool ok = true;
+    for (int t = 0; t < x.world && ok; t++) {
+        unsigned long long v = 0;
+        ok = xchg_read(x, t, step, &v);
+        m = v > m ? v : m;
+    }
+    if (ok) *out = m;
+    else if (err) atomicExch(err, (int)TMAC_ERR_TIMEOUT);
+    *x.step = step;
+}
+
+XchgDev xchg_dev(const tmac_xchg_s* x);  // xchg.cu
+
+}  // namespace tmac

@@ -72,3 +72,38 @@ def gather_next_tokens(local, n_seq: int, group=None):
         s0, s1 = sequence_shard(n_seq, world, r)
         out.append(parts[r][: s1 - s0].cpu().numpy())
     return np.concatenate(out).astype(np.int32)
+
+
+# ------------------------------------------------ peer-memory top-1 exchange
+class PeerTop1:
+    """Global top-1 key over NVLink peer memory (tmac_xchg_*): every rank
+    stores its shard key into every rank's exchange buffer and takes the
+    maximum of this step's keys, in one small kernel per step.  Setup shares
+    the CUDA IPC handles of the buffers over the process group."""
+
+    def __init__(self, device: int, group=None):
+        import ctypes
+        import torch.distributed as dist
+        from . import lib, check, _P
+        self._lib = lib()
+        world, rank = dist.get_world_size(group), dist.get_rank(group)
+        self.handle = _P()
+        check(self._lib.tmac_xchg_create(device, world, rank, ctypes.byref(self.handle)))
+        buf = (ctypes.c_uint8 * 64)()
+        check(self._lib.tmac_xchg_ipc_handle(self.handle, buf))
+        handles = [None] * world
+        dist.all_gather_object(handles, bytes(buf), group=group)
+        joined = b"".join(handles)
+        check(self._lib.tmac_xchg_open(self.handle, joined))
+        dist.barrier(group=group)
+
+    def __call__(self, key_tensor, stream=None):
+        from . import check
+        s = None if stream is None else (stream if isinstance(stream, int) else stream.cuda_stream)
+        check(self._lib.tmac_xchg_top1(self.handle, key_tensor.data_ptr(), s))
+        return key_tensor
+
+    def free(self):
+        if getattr(self, "handle", None):
+            self._lib.tmac_xchg_free(self.handle)
+            self.handle = None
