@@ -261,8 +261,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-model", action="store_true", help="skip the decode / prefill measurements")
-    ap.add_argument("--collective", choices=["peer", "nccl"], default="peer",
-                    help="top-1 merge across ranks: NVLink peer-memory exchange kernel or NCCL all-reduce")
+    ap.add_argument("--collective", choices=["fused", "peer", "nccl"], default="fused",
+                    help="top-1 merge across ranks: inside the logits GEMV over NVLink peer memory, "
+                         "a separate peer-memory exchange kernel, or an NCCL all-reduce")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -299,30 +300,42 @@ def main():
     key = torch.zeros(1, dtype=torch.int64, device="cuda")
     stream = torch.cuda.current_stream()
 
-    # top-1 merge across ranks: the peer-memory exchange kernel (checked against
-    # the NCCL all-reduce of the same key first), else the NCCL all-reduce
-    merge, merge_kind = None, "none"
+    # top-1 merge across ranks over NVLink peer memory (fused into the logits
+    # GEMV, or a kernel of its own), checked first against the NCCL all-reduce
+    # of the shard keys; NCCL all-reduce if that check fails
+    merge, merge_kind, fused = None, "none", False
     if world > 1:
         merge_kind = "nccl int64 MAX all-reduce"
-        if args.collective == "peer":
+        if args.collective in ("fused", "peer"):
             from tmac_zynq_fpga_b200 import shard
             try:
                 xchg = shard.PeerTop1(local)
                 weights[0].gemv_top1(x, y, key, index_base=r0, stream=stream)
                 ref = key.clone()
                 dist.all_reduce(ref, op=dist.ReduceOp.MAX)
-                xchg(key, stream)
+                if args.collective == "fused":
+                    xchg.gemv_top1(weights[0], x, y, key, r0, stream)
+                else:
+                    xchg(key, stream)
                 torch.cuda.synchronize()
                 if not torch.equal(ref, key) or tm.device_error(local) != 0:
                     raise RuntimeError("peer exchange disagrees with the NCCL all-reduce")
-                merge, merge_kind = xchg, "NVLink peer-memory exchange kernel (tmac_xchg_top1)"
+                merge = xchg
+                fused = args.collective == "fused"
+                merge_kind = ("top-1 exchange over NVLink peer memory inside the GEMV's last CTA "
+                              "(tmac_xchg_gemv_top1)" if fused else
+                              "NVLink peer-memory exchange kernel (tmac_xchg_top1)")
             except Exception as e:  # keep NCCL
                 merge_kind = f"nccl int64 MAX all-reduce (peer exchange unavailable: {e})"
 
     def step(i):
-        # logits of this rank's vocab shard + their top-1 key (one fused kernel),
-        # then the global greedy token on every rank
-        weights[i % ncopies].gemv_top1(x, y, key, index_base=r0, stream=stream)
+        # logits of this rank's vocab shard + their top-1 key, then the global
+        # greedy token on every rank
+        w = weights[i % ncopies]
+        if fused:
+            merge.gemv_top1(w, x, y, key, r0, stream)
+            return
+        w.gemv_top1(x, y, key, index_base=r0, stream=stream)
         if world > 1:
             if merge is not None:
                 merge(key, stream)
@@ -414,7 +427,7 @@ def main():
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_val, "unit": UNIT, "h2d_bytes_per_step": HIDDEN * 4,
                     "d2h_bytes_per_step": rows * 4, "api": "tmac_gemv_host", "steps": e2e_steps},
-            "gpu_launches": args.steps * (2 if merge is not None else 1),
+            "gpu_launches": args.steps * (2 if (merge is not None and not fused) else 1),
             "clocks": clocks,
             "decode": decode,
             "prefill": prefill,

@@ -71,6 +71,13 @@ const char* tmac_last_error(void);
 /* Reads and clears the device-side error word of `device` (synchronises that
  * device).  *code receives 0 or the TMAC_ERR_* a kernel recorded. */
 int tmac_device_error(int device, int* code);
+/* Programmatic dependent launch for the kernels this host thread launches
+ * from now on (default off; returns the previous setting).  When on, a
+ * kernel may start while the preceding kernel on the stream finishes: it
+ * sets up and streams its weights, and waits for the predecessor before it
+ * reads activations or writes outputs, so results are unchanged.  Consecutive
+ * GEMVs then overlap one launch's ramp-up with the other's tail. */
+int tmac_set_pdl(int on);
 
 /*
  * Register one weight tensor: W[rows][cols] as raw GGUF blocks (the bytes a
@@ -213,6 +220,16 @@ int tmac_xchg_create(int device, int world, int rank, tmac_xchg_t* out);
 int tmac_xchg_ipc_handle(tmac_xchg_t x, void* handle);           /* TMAC_XCHG_HANDLE_BYTES bytes */
 int tmac_xchg_open(tmac_xchg_t x, const void* handles);          /* world x TMAC_XCHG_HANDLE_BYTES */
 int tmac_xchg_top1(tmac_xchg_t x, uint64_t* key, void* stream);
+/* The logits step of one rank in one launch: y = W.in (batch 1) over this
+ * rank's vocab shard (rows index_base ..), and *key = the maximum top-1 key
+ * over every rank's shard.  For a Q8_0 weight the exchange runs inside the
+ * GEMV (its last CTA publishes the shard key to every rank and waits for
+ * theirs), so no key reset or second launch is needed; other weights take
+ * tmac_gemv_top1 followed by tmac_xchg_top1.  Shares the step count with
+ * tmac_xchg_top1, so the two may be mixed as long as every rank makes the
+ * same sequence of calls. */
+int tmac_xchg_gemv_top1(tmac_xchg_t x, tmac_weight_t w, const float* in, float* y, uint64_t* key,
+                        int64_t index_base, void* stream);
 int tmac_xchg_free(tmac_xchg_t x);
 
 /* ------------------------------------------------------------------------ */

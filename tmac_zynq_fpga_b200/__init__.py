@@ -88,6 +88,8 @@ def lib():
             "tmac_xchg_ipc_handle": (ctypes.c_int, [_P, _P]),
             "tmac_xchg_open": (ctypes.c_int, [_P, ctypes.c_char_p]),
             "tmac_xchg_top1": (ctypes.c_int, [_P, _P, _P]),
+            "tmac_set_pdl": (ctypes.c_int, [ctypes.c_int]),
+            "tmac_xchg_gemv_top1": (ctypes.c_int, [_P, _P, _P, _P, _P, ctypes.c_int64, _P]),
             "tmac_xchg_free": (ctypes.c_int, [_P]),
             "tmac_reserve": (ctypes.c_int, [ctypes.c_int, _I64, _I64]),
             "tmac_top1": (ctypes.c_int, [_P, _I64, _I64, _P, _P]),

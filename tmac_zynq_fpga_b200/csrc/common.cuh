@@ -107,6 +107,16 @@ TMAC_DEV unsigned long long top1_key(float v, int64_t idx)
 }
 
 // x_scale of tmac_gguf.cpp:889-892 from max|x|.
+// Combined UQ8.8 scale, tmac_gguf.cpp:1022-1039.
+TMAC_DEV uint32_t q8_combined(float d, float rs)
+{
+    float rinv = (rs < 1e-10f) ? 1.0f : __fdiv_rn(1.0f, rs);
+    float c = __fmul_rn(d, rinv);
+    if (c >= 256.0f) c = 255.996f;
+    if (c < 0.0f) c = 0.0f;
+    return (uint32_t)(uint16_t)__fadd_rn(__fmul_rn(c, 256.0f), 0.5f);
+}
+
 TMAC_DEV float x_scale_from_max(float mx) { return (mx < 1e-10f) ? 1.0f : __fdiv_rn(mx, 32767.0f); }
 // x_q of tmac_gguf.cpp:894-896.
 TMAC_DEV int16_t quantize_one(float x, float xs) { return (int16_t)(int)roundf(__fdiv_rn(x, xs)); }
@@ -158,6 +168,31 @@ TMAC_DEV bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* err)
     for (uint32_t it = 1;; it++) {
         if (mbar_try_wait(bar, parity)) return true;
         if ((it & 255u) == 0 && global_timer_ns() - t0 > 2000000000ull) {
+            if (err) atomicExch(err, (int)TMAC_ERR_TIMEOUT);
+            return false;
+        }
+    }
+}
+// As mbar_wait_bounded, but every poll may suspend the thread until the
+// phase completes or ~hint_ns pass, so a warp that waits long issues few
+// instructions (the issue slots stay with the warps doing the work).
+TMAC_DEV bool mbar_try_wait_hint(uint64_t* bar, uint32_t parity, uint32_t hint_ns)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+TMAC_DEV bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, int* err)
+{
+    if (mbar_try_wait(bar, parity)) return true;
+    uint64_t t0 = global_timer_ns();
+    for (uint32_t it = 1;; it++) {
+        if (mbar_try_wait_hint(bar, parity, 20000u)) return true;
+        if ((it & 15u) == 0 && global_timer_ns() - t0 > 2000000000ull) {
             if (err) atomicExch(err, (int)TMAC_ERR_TIMEOUT);
             return false;
         }
@@ -230,14 +265,25 @@ struct tmac_weight_s {
     void* gwh = nullptr;         // tensor-core GEMM: exact int16 weights as byte planes
     void* gwl = nullptr;         // (high, low), decoded on first tmac_gemm
     void* grinv = nullptr;       // double [rows]: RN(1 / row_inv) for the GEMM epilogue
+    // Q8_0 wide layout (tall matrices, gemv_q8_wide.cu): row-major planes of
+    // biased quants [rows_pad][cols] and combined scales [rows_pad][nbp] (u16,
+    // at data + cs_off), row_norm padded to rows_pad; tmap = the quant plane's
+    // tensor map (a CUtensorMap).
+    int q8_wide = 0;
+    int nbp = 0;
+    int64_t rows_pad = 0, cs_off = 0;
+    alignas(64) unsigned char tmap[128] = {};
 };
 
 namespace tmac {
 // Per-path launchers (one per .cu file).  All return TMAC_OK or an error.
 int register_q8_0(tmac_weight_s* w, const uint8_t* d_raw, const float* d_row_max_abs, cudaStream_t s);
+struct XchgDev;  // xchg.cuh
+// With xg, top1 is the global key: the last CTA merges this rank's shard key
+// with every rank's over peer memory (batch 1 only, top1 not zeroed first).
 int launch_q8_0(const tmac_weight_s* w, const float* x, float* y, int64_t* row_acc, int64_t* unit_acc,
                 int batch, cudaStream_t s, unsigned long long* top1 = nullptr, int64_t index_base = 0,
-                const int16_t* xq = nullptr, const float* xs = nullptr);
+                const int16_t* xq = nullptr, const float* xs = nullptr, const XchgDev* xg = nullptr);
 int launch_quantize(const float* x, int64_t cols, int batch, int16_t* xq, float* xs, cudaStream_t s,
                     uint8_t* xp = nullptr);
 int launch_top1(const float* y, int64_t n, int64_t index_base, unsigned long long* key, cudaStream_t s);
@@ -279,6 +325,14 @@ int gemm_planes(const GemmOperands& op, cudaStream_t s);
 // Q8_0 weight (NATIVE layout) -> its int16 deq = (q * cs) >> 8 as byte planes
 // [rows][cols] (gemv_q8_0.cu).
 int q8_planes(const tmac_weight_s* w, int8_t* wh, uint8_t* wl, cudaStream_t s);
+// Q8_0 wide layout (gemv_q8_wide.cu): chosen by register_q8_0 for tall matrices.
+bool q8_wide_eligible(int64_t rows, int64_t cols);
+// row_norm (rows_pad floats, the first rows holding row_scale) is set by the caller.
+int register_q8_wide(tmac_weight_s* w, const uint8_t* d_raw, cudaStream_t s);
+int launch_q8_wide(const tmac_weight_s* w, const float* x, float* y, int64_t* row_acc, int64_t* unit_acc, int batch,
+                   cudaStream_t s, unsigned long long* top1, int64_t index_base, const int16_t* xq, const float* xs,
+                   const XchgDev* xg);
+int q8_wide_planes(const tmac_weight_s* w, int8_t* wh, uint8_t* wl, cudaStream_t s);
 int register_int16(tmac_weight_s* w, const uint8_t* d_raw, cudaStream_t s);
 int launch_int16(const tmac_weight_s* w, const float* x, float* y, int64_t* row_acc, int64_t* unit_acc,
                  int batch, cudaStream_t s);

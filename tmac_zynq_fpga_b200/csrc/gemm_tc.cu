@@ -18,10 +18,7 @@
 // rows and columns read as zero) through a 4-stage mbarrier ring.  Warp 0
 // issues the copies, warp 1 owns TMEM and issues the MMAs into one of two
 // accumulator sets, eight epilogue warps drain the other set.
-#include "common.cuh"
-
-#include <cuda.h>
-#include <cudaTypedefs.h>
+#include "tcgen05.cuh"
 
 #include <algorithm>
 #include <mutex>
@@ -54,58 +51,12 @@ struct GemmArgs {
     int* err;
 };
 
-// ------------------------------------------------------------ PTX helpers --
-TMAC_DEV void tma_load_2d(void* dst, const CUtensorMap* tm, int x, int y, uint64_t* bar)
-{
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-            smem_addr(dst)),
-        "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(smem_addr(bar))
-        : "memory");
-}
-
-// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row atoms of
-// 128 bytes (stride 1024 bytes), sm_100 descriptor version 1.
-TMAC_DEV uint64_t desc_sw128(uint32_t saddr)
-{
-    uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
-    d |= (uint64_t)1 << 16;              // leading byte offset (16 B; unused when swizzled)
-    d |= (uint64_t)(1024 >> 4) << 32;    // stride byte offset
-    d |= (uint64_t)1 << 46;              // version
-    d |= (uint64_t)2 << 61;              // SWIZZLE_128B
-    return d;
-}
-
 // Instruction descriptor for kind::i8: s32 accumulate, A/B signed (1) or
 // unsigned (0), both K-major, M = BM, N = BN.
 __host__ __device__ constexpr uint32_t idesc_i8(uint32_t a_signed, uint32_t b_signed)
 {
     return (2u << 4) | (a_signed << 7) | (b_signed << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
 }
-
-TMAC_DEV void mma_i8(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate)
-{
-    asm volatile(
-        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-        " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(d_tmem),
-        "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
-}
-
-TMAC_DEV void mma_commit(uint64_t* bar)
-{
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
-                 : "memory");
-}
-TMAC_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-TMAC_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-TMAC_DEV void tmem_ld8(uint32_t taddr, uint32_t* r)
-{
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
-                 : "r"(taddr));
-}
-TMAC_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // (float)(p / ri) with p / ri rounded to double first, as the GEMV computes it
 // (__ddiv_rn then the float conversion).  p * RN(1/ri) is within 2 double ulps
@@ -170,6 +121,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    pdl_wait();  // under programmatic launch only the set-up above overlaps the preceding kernel
 
     if (warp == 0) {
         if (lane == 0) {
@@ -335,22 +287,6 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const float* __restr
 }
 
 // ------------------------------------------------------------------ host --
-// cuTensorMapEncodeTiled through the runtime's driver entry point, so the
-// library has no link-time dependency on libcuda.
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
-{
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-    });
-    return fn;
-}
-
 int encode_plane_map(CUtensorMap* tm, const void* base, int64_t rows, int64_t K, int64_t stride, uint32_t box_rows)
 {
     const auto encode = encode_fn();

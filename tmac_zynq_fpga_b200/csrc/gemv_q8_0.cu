@@ -25,7 +25,7 @@
 // and every dot product is a dp4a against the split activation
 // x_q = 256*xh + xl (xh signed byte, xl unsigned byte):
 //   sum deq*x = ch*(sum q'*x - 128*Sx) + (sum eb*x - 128*Sx),  Sx = sum of x_q over the block.
-#include "common.cuh"
+#include "xchg.cuh"
 
 #include <algorithm>
 
@@ -95,16 +95,6 @@ __global__ void q8_row_scale_kernel(const uint8_t* __restrict__ raw, int64_t row
         for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     }
     if (lane == 0) row_scale[r] = (mx < 1e-10f) ? 1.0f : __fdiv_rn(mx, 32767.0f);
-}
-
-// Combined UQ8.8 scale, tmac_gguf.cpp:1022-1039.
-TMAC_DEV uint32_t q8_combined(float d, float rs)
-{
-    float rinv = (rs < 1e-10f) ? 1.0f : __fdiv_rn(1.0f, rs);
-    float c = __fmul_rn(d, rinv);
-    if (c >= 256.0f) c = 255.996f;
-    if (c < 0.0f) c = 0.0f;
-    return (uint32_t)(uint16_t)__fadd_rn(__fmul_rn(c, 256.0f), 0.5f);
 }
 
 // One CTA per (group, tile): 128 threads write the 16-byte quant chunks,
@@ -192,6 +182,7 @@ struct Q8Args {
     int64_t* unit_acc;
     unsigned long long* top1;  // optional: max packed (value, index) key, see top1_key
     int64_t index_base;        // global row index of row 0 (vocab shard offset)
+    XchgDev xg;                // peers != nullptr: merge top1 across ranks (fused exchange)
     int* err;
 };
 
@@ -282,7 +273,7 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemv_kernel(Q8Args a)
             int issued = 0;
             for (int i = 0; i < ng; i++) {
                 const int s = i % L.stages;
-                if (i >= L.stages && !mbar_wait_bounded(&empty[s], ((i / L.stages) & 1) ^ 1, a.err)) {
+                if (i >= L.stages && !mbar_wait_sleep(&empty[s], ((i / L.stages) & 1) ^ 1, a.err)) {
                     *abort_flag = 1;
                     break;
                 }
@@ -305,7 +296,7 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemv_kernel(Q8Args a)
         unsigned long long best = 0;  // running top-1 key of this warp's rows
         for (int i = f; i < ng; i += kFoldWarps) {
             const int b = i % kAccBufs;
-            if (*abort_flag || !mbar_wait_bounded(&acc_full[b], (i / kAccBufs) & 1, a.err)) {
+            if (*abort_flag || !mbar_wait_sleep(&acc_full[b], (i / kAccBufs) & 1, a.err)) {
                 *abort_flag = 1;
                 break;
             }
@@ -336,7 +327,7 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemv_kernel(Q8Args a)
                 const unsigned long long k = __shfl_xor_sync(0xffffffffu, best, o);
                 best = k > best ? k : best;
             }
-            if (lane == 0 && best) atomicMax(a.top1, best);
+            top1_cta_finish(a.xg, a.top1, best, f == 0, 2, kFoldWarps * 32, a.err);
         }
         return;
     }
@@ -411,7 +402,7 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemv_kernel(Q8Args a)
     // ---------------- main loop over this CTA's 32-row groups -------------
     for (int i = 0; i < ng; i++) {
         const int s = i % L.stages, b = i % kAccBufs;
-        if (*abort_flag || !mbar_wait_bounded(&full[s], (i / L.stages) & 1, a.err) ||
+        if (*abort_flag || !mbar_wait_sleep(&full[s], (i / L.stages) & 1, a.err) ||
             (i >= kAccBufs && !mbar_wait_bounded(&acc_empty[b], ((i / kAccBufs) & 1) ^ 1, a.err))) {
             *abort_flag = 1;
             break;
@@ -452,6 +443,15 @@ size_t q8_smem_bytes(const Q8Layout& L)
 int register_q8_0(tmac_weight_s* w, const uint8_t* d_raw, const float* d_row_max_abs, cudaStream_t s)
 {
     if (w->cols % 32) return fail(TMAC_ERR_SHAPE, "Q8_0 needs cols % 32 == 0");
+    const int wpb = 8;
+    if (q8_wide_eligible(w->rows, w->cols)) {
+        const int64_t rows_pad = (w->rows + 127) / 128 * 128;
+        TMAC_CUDA_TRY(cudaMalloc(&w->row_norm, (size_t)rows_pad * sizeof(float)));
+        q8_row_scale_kernel<<<(unsigned)((w->rows + wpb - 1) / wpb), wpb * 32, 0, s>>>(d_raw, w->rows, w->cols,
+                                                                                       d_row_max_abs, w->row_norm);
+        TMAC_CUDA_TRY(cudaGetLastError());
+        return register_q8_wide(w, d_raw, s);
+    }
     Q8Layout L = q8_layout(w->rows, w->cols);
     w->tiles = L.T;
     w->groups = L.groups;
@@ -460,7 +460,6 @@ int register_q8_0(tmac_weight_s* w, const uint8_t* d_raw, const float* d_row_max
     if (L.stages < 2) return fail(TMAC_ERR_SHAPE, "Q8_0: cols too large for a two-stage row-group pipeline");
     TMAC_CUDA_TRY(cudaMalloc(&w->row_norm, (size_t)w->rows * sizeof(float)));
     TMAC_CUDA_TRY(cudaMalloc(&w->data, w->data_bytes));
-    const int wpb = 8;
     q8_row_scale_kernel<<<(unsigned)((w->rows + wpb - 1) / wpb), wpb * 32, 0, s>>>(d_raw, w->rows, w->cols,
                                                                                    d_row_max_abs, w->row_norm);
     TMAC_CUDA_TRY(cudaGetLastError());
@@ -472,6 +471,7 @@ int register_q8_0(tmac_weight_s* w, const uint8_t* d_raw, const float* d_row_max
 
 int q8_planes(const tmac_weight_s* w, int8_t* wh, uint8_t* wl, cudaStream_t s)
 {
+    if (w->q8_wide) return q8_wide_planes(w, wh, wl, s);
     if (w->cols % 16) return fail(TMAC_ERR_SHAPE, "q8_planes: cols must be a multiple of 16");
     const Q8Layout L = q8_layout(w->rows, w->cols);
     const int64_t n = w->rows * (w->cols / 16);
@@ -481,8 +481,11 @@ int q8_planes(const tmac_weight_s* w, int8_t* wh, uint8_t* wl, cudaStream_t s)
 }
 
 int launch_q8_0(const tmac_weight_s* w, const float* x, float* y, int64_t* row_acc, int64_t* unit_acc, int batch,
-                cudaStream_t s, unsigned long long* top1, int64_t index_base, const int16_t* xq, const float* xs)
+                cudaStream_t s, unsigned long long* top1, int64_t index_base, const int16_t* xq, const float* xs,
+                const XchgDev* xg)
 {
+    if (w->q8_wide) return launch_q8_wide(w, x, y, row_acc, unit_acc, batch, s, top1, index_base, xq, xs, xg);
+    if (xg && (batch != 1 || !top1)) return fail(TMAC_ERR_SHAPE, "the fused exchange takes batch 1 and a key");
     Q8Layout L = q8_layout(w->rows, w->cols);
     const size_t smem = q8_smem_bytes(L);
     static bool attr_set[64] = {};
@@ -505,6 +508,7 @@ int launch_q8_0(const tmac_weight_s* w, const float* x, float* y, int64_t* row_a
         a.unit_acc = unit_acc ? unit_acc + (int64_t)b * w->rows * L.T : nullptr;
         a.top1 = top1 ? top1 + b : nullptr;
         a.index_base = index_base;
+        if (xg) a.xg = *xg;
         a.err = device_error_word(w->device);
         TMAC_CUDA_TRY(launch_k(q8_gemv_kernel, dim3(grid), dim3(kThreads), smem, s, a));
         TMAC_CUDA_TRY(cudaGetLastError());

@@ -242,6 +242,13 @@ int tmac_abi_version(void) { return TMAC_ABI_VERSION; }
 
 const char* tmac_last_error(void) { return g_last_error.c_str(); }
 
+int tmac_set_pdl(int on)
+{
+    const int prev = g_pdl ? 1 : 0;
+    g_pdl = on != 0;
+    return prev;
+}
+
 int tmac_device_error(int device, int* code)
 {
     if (!code) return fail(TMAC_ERR_INVALID, "NULL code pointer");

@@ -99,6 +99,8 @@ int tmac_xchg_create(int device, int world, int rank, tmac_xchg_t* out)
     if (e != cudaSuccess) {
         if (x->buf) cudaFree(x->buf);
         if (x->step) cudaFree(x->step);
+        if (x->peer_dev) cudaFree(x->peer_dev);
+        if (x->partial) cudaFree(x->partial);
         delete x;
         return cuda_fail(e, "tmac_xchg_create");
     }
@@ -145,6 +147,24 @@ int tmac_xchg_top1(tmac_xchg_t x, uint64_t* key, void* stream)
                            reinterpret_cast<unsigned long long*>(key), xchg_dev(x), device_error_word(x->device)));
     TMAC_CUDA_TRY(cudaGetLastError());
     return TMAC_OK;
+}
+
+int tmac_xchg_gemv_top1(tmac_xchg_t x, tmac_weight_t w, const float* in, float* y, uint64_t* key,
+                        int64_t index_base, void* stream)
+{
+    if (!x || !w || !in || !y || !key) return fail(TMAC_ERR_INVALID, "NULL argument");
+    for (int r = 0; r < x->world; r++)
+        if (!x->peer[r]) return fail(TMAC_ERR_INVALID, "tmac_xchg_open has not mapped every rank");
+    if (w->device != x->device) return fail(TMAC_ERR_INVALID, "weight and exchange on different devices");
+    if (!(w->mode == TMAC_MODE_NATIVE && w->type == TMAC_TYPE_Q8_0)) {
+        const int rc = tmac_gemv_top1(w, in, y, key, index_base, 1, stream);
+        return rc ? rc : tmac_xchg_top1(x, key, stream);
+    }
+    if (index_base < 0 || index_base + w->rows > 0x7FFFFFFF) return fail(TMAC_ERR_SHAPE, "bad index range");
+    DeviceGuard dg(x->device);
+    const XchgDev d = xchg_dev(x);
+    return launch_q8_0(w, in, y, nullptr, nullptr, 1, (cudaStream_t)stream,
+                       reinterpret_cast<unsigned long long*>(key), index_base, nullptr, nullptr, &d);
 }
 
 int tmac_xchg_free(tmac_xchg_t x)

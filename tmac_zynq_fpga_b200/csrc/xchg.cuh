@@ -89,6 +89,36 @@ TMAC_DEV void xchg_top1_thread(const XchgDev& x, unsigned long long k, unsigned 
     *x.step = step;
 }
 
+// End of a GEMV CTA that tracks the top-1 key of its rows: every warp of the
+// `bar_threads` (named barrier `bar_id`) calls it with its warp-reduced key.
+// Without an exchange the keys max-merge into *top1.  With one they merge into
+// the shard's running key; the last CTA to finish takes it (resetting it and
+// the CTA count for the next call) and merges it with every rank's over peer
+// memory into *top1.
+TMAC_DEV void top1_cta_finish(const XchgDev& xg, unsigned long long* top1, unsigned long long best, bool leader_warp,
+                              int bar_id, int bar_threads, int* err)
+{
+    const int lane = threadIdx.x & 31;
+    if (!xg.peers) {
+        if (lane == 0 && best) atomicMax(top1, best);
+        return;
+    }
+    if (lane == 0) {
+        if (best) atomicMax(xg.partial, best);
+        __threadfence();
+    }
+    asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(bar_threads) : "memory");
+    if (leader_warp && lane == 0) {
+        const unsigned done = atomicAdd(xg.counter, 1u);
+        if (done == gridDim.x - 1) {
+            __threadfence();
+            const unsigned long long k = atomicExch(xg.partial, 0ull);
+            atomicExch(xg.counter, 0u);
+            xchg_top1_thread(xg, k, top1, err);
+        }
+    }
+}
+
 XchgDev xchg_dev(const tmac_xchg_s* x);  // xchg.cu
 
 }  // namespace tmac

@@ -78,7 +78,8 @@ def gather_next_tokens(local, n_seq: int, group=None):
 class PeerTop1:
     """Global top-1 key over NVLink peer memory (tmac_xchg_*): every rank
     stores its shard key into every rank's exchange buffer and takes the
-    maximum of this step's keys, in one small kernel per step.  Setup shares
+    maximum of this step's keys, in one small kernel per step, or inside the
+    logits GEMV itself (gemv_top1).  Setup shares
     the CUDA IPC handles of the buffers over the process group."""
 
     def __init__(self, device: int, group=None):
@@ -101,6 +102,16 @@ class PeerTop1:
         from . import check
         s = None if stream is None else (stream if isinstance(stream, int) else stream.cuda_stream)
         check(self._lib.tmac_xchg_top1(self.handle, key_tensor.data_ptr(), s))
+        return key_tensor
+
+    def gemv_top1(self, weight, x, y, key_tensor, index_base: int, stream=None):
+        """Logits of this rank's vocab shard (batch 1) and the global top-1 key
+        in one launch (tmac_xchg_gemv_top1: the exchange runs in the Q8_0
+        GEMV's last CTA)."""
+        from . import check
+        s = None if stream is None else (stream if isinstance(stream, int) else stream.cuda_stream)
+        check(self._lib.tmac_xchg_gemv_top1(self.handle, weight.handle, x.data_ptr(), y.data_ptr(),
+                                            key_tensor.data_ptr(), int(index_base), s))
         return key_tensor
 
     def free(self):
