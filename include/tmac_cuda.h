@@ -137,7 +137,9 @@ int tmac_gemv_int16(tmac_weight_t w, const float* x, float* y, int batch, void* 
  * Host-buffer GEMV: copies x[batch][cols] host->device, runs tmac_gemv on the
  * weight's device and copies y[batch][rows] back; synchronous.  This is the
  * drop-in for the reference's `void matmul_fpga_X(const Tensor*, const float*
- * x, float* y, int rows, int cols)` calls on host arrays.
+ * x, float* y, int rows, int cols)` calls on host arrays.  For a NATIVE Q8_0
+ * weight and a page-locked y (cudaHostAlloc / cudaHostRegister) the kernel
+ * stores y straight into host memory, overlapping the transfer with the GEMV.
  */
 int tmac_gemv_host(tmac_weight_t w, const float* x_host, float* y_host, int batch);
 

@@ -500,9 +500,22 @@ int tmac_gemv_host(tmac_weight_t w, const float* x_host, float* y_host, int batc
     cudaError_t e;
     if ((e = cudaMemcpyAsync(dx, x_host, xb, cudaMemcpyHostToDevice, nullptr)) != cudaSuccess)
         return cuda_fail(e, "H2D x");
-    rc = tmac_gemv(w, dx, dy, batch, nullptr);
+    // A page-locked y that this device can address is written by the Q8_0
+    // kernel itself (one plain store per row), so the transfer to the host
+    // overlaps the GEMV instead of following it.  Other paths, and pageable y,
+    // go through the device staging buffer.
+    float* y_dev = nullptr;
+    if (w->type == TMAC_TYPE_Q8_0 && w->mode == TMAC_MODE_NATIVE) {
+        cudaPointerAttributes pa;
+        if (cudaPointerGetAttributes(&pa, y_host) == cudaSuccess && pa.type == cudaMemoryTypeHost &&
+            pa.devicePointer)
+            y_dev = static_cast<float*>(pa.devicePointer);
+        else
+            cudaGetLastError();  // clear the lookup's error state
+    }
+    rc = tmac_gemv(w, dx, y_dev ? y_dev : dy, batch, nullptr);
     if (rc) return rc;
-    if ((e = cudaMemcpyAsync(y_host, dy, yb, cudaMemcpyDeviceToHost, nullptr)) != cudaSuccess)
+    if (!y_dev && (e = cudaMemcpyAsync(y_host, dy, yb, cudaMemcpyDeviceToHost, nullptr)) != cudaSuccess)
         return cuda_fail(e, "D2H y");
     TMAC_CUDA_TRY(cudaStreamSynchronize(nullptr));
     return TMAC_OK;
