@@ -261,6 +261,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-model", action="store_true", help="skip the decode / prefill measurements")
+    ap.add_argument("--no-pdl", action="store_true",
+                    help="launch each step's kernel after the previous one ends (no programmatic dependent launch)")
     ap.add_argument("--collective", choices=["fused", "peer", "nccl"], default="fused",
                     help="top-1 merge across ranks: inside the logits GEMV over NVLink peer memory, "
                          "a separate peer-memory exchange kernel, or an NCCL all-reduce")
@@ -342,6 +344,9 @@ def main():
             else:
                 dist.all_reduce(key, op=dist.ReduceOp.MAX)
 
+    # consecutive steps' kernels: the next one's prologue and weight copies may
+    # start while the previous one finishes (tmac_set_pdl; results unchanged)
+    prev_pdl = tm.lib().tmac_set_pdl(0 if args.no_pdl else 1)
     for i in range(args.warmup):
         step(i)
     torch.cuda.synchronize()
@@ -370,6 +375,7 @@ def main():
     total_bytes = alg_bytes(VOCAB) + (world - 1) * HIDDEN * 4  # every rank reads x
     value = total_bytes / (ms_per_step * 1e-3) / 1e9
     kernel_us = ms / args.steps * 1e3  # one launch per step on this rank
+    tm.lib().tmac_set_pdl(prev_pdl)
 
     # e2e: the public host-buffer entry (tmac_gemv_host): H2D x, GEMV, D2H y per step.
     xh = torch.from_numpy(synth.make_activations(HIDDEN, seed=0)).pin_memory()
@@ -419,6 +425,8 @@ def main():
                        "step": "shard logits GEMV with fused top-1 key" + (f" + {merge_kind}" if world > 1 else ""),
                        "greedy_token": tok,
                        "parallelism": f"vocab-row shards x{world}", "shard_rows": rows,
+                       "launch": "back-to-back, no programmatic dependent launch" if args.no_pdl else
+                                 "programmatic dependent launch between steps (tmac_set_pdl)",
                        "l2": f"inputs larger than L2: {ncopies} rotating weight copies of "
                              f"{per_copy / 1e6:.1f} MB per rank"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk, "unit": "GB/s",

@@ -151,8 +151,12 @@ int tmac_gemv_host(tmac_weight_t w, const float* x_host, float* y_host, int batc
  * reference (tmac_gguf.cpp:1974-1990, :2164-2172) in greedy decoding.
  *   tmac_top1:      max-merges the key of y[0..n) (indices + index_base) into
  *                   *key (device); zero *key first for a fresh result.
- *   tmac_gemv_top1: y = W.x and key[b] = top-1 of y[b] (key zeroed here).  For
- *                   Q8_0 the top-1 is fused into the GEMV kernel's epilogue.
+ *   tmac_gemv_top1: y = W.x and key[b] = top-1 of y[b] (the key's old value
+ *                   does not matter).  For Q8_0 the top-1 is fused into the
+ *                   GEMV kernel: its CTAs merge into a running key kept with
+ *                   the weight and the last CTA writes key[b], so the call is
+ *                   one launch per batch row; top-1 calls on one weight must
+ *                   not run concurrently.
  *   tmac_top1_decode: host-side unpacking of a key.
  */
 int tmac_top1(const float* y, int64_t n, int64_t index_base, uint64_t* key, void* stream);

@@ -269,6 +269,9 @@ struct tmac_weight_s {
     // biased quants [rows_pad][cols] and combined scales [rows_pad][nbp] (u16,
     // at data + cs_off), row_norm padded to rows_pad; tmap = the quant plane's
     // tensor map (a CUtensorMap).
+    // Q8_0: running top-1 key (u64) and CTA count (u32) of the call in flight,
+    // so a top-1 call needs no key reset (calls on one weight are serial).
+    void* top1_scratch = nullptr;
     int q8_wide = 0;
     int nbp = 0;
     int64_t rows_pad = 0, cs_off = 0;

@@ -400,18 +400,39 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemv_kernel(Q8Args a)
     }
 
     // ---------------- main loop over this CTA's 32-row groups -------------
-    for (int i = 0; i < ng; i++) {
-        const int s = i % L.stages, b = i % kAccBufs;
-        if (*abort_flag || !mbar_wait_sleep(&full[s], (i / L.stages) & 1, a.err) ||
-            (i >= kAccBufs && !mbar_wait_bounded(&acc_empty[b], ((i / kAccBufs) & 1) ^ 1, a.err))) {
+    // Two groups per iteration: their tile sums are independent, which doubles
+    // the work in flight per warp and halves the per-group loop and barrier cost.
+    for (int i = 0; i < ng; i += 2) {
+        const bool two = i + 1 < ng;
+        const int s0 = i % L.stages, b0 = i % kAccBufs;
+        const int s1 = (i + 1) % L.stages, b1 = (i + 1) % kAccBufs;
+        if (*abort_flag || !mbar_wait_sleep(&full[s0], (i / L.stages) & 1, a.err) ||
+            (i >= kAccBufs && !mbar_wait_bounded(&acc_empty[b0], ((i / kAccBufs) & 1) ^ 1, a.err)) ||
+            (two && (!mbar_wait_sleep(&full[s1], ((i + 1) / L.stages) & 1, a.err) ||
+                     (i + 1 >= kAccBufs &&
+                      !mbar_wait_bounded(&acc_empty[b1], (((i + 1) / kAccBufs) & 1) ^ 1, a.err))))) {
             *abort_flag = 1;
             break;
         }
-        const uint8_t* st = stage_base + (int64_t)s * L.group_bytes;
-        long long* acc_buf = accs + b * T * 32;
-        if (warp == 0) rs_buf[b * 32 + lane] = reinterpret_cast<const float*>(st + L.rs_off())[lane];
+        const uint8_t* st0 = stage_base + (int64_t)s0 * L.group_bytes;
+        const uint8_t* st1 = stage_base + (int64_t)s1 * L.group_bytes;
+        long long* acc0 = accs + b0 * T * 32;
+        long long* acc1 = accs + b1 * T * 32;
+        if (warp == 0) {
+            rs_buf[b0 * 32 + lane] = reinterpret_cast<const float*>(st0 + L.rs_off())[lane];
+            if (two) rs_buf[b1 * 32 + lane] = reinterpret_cast<const float*>(st1 + L.rs_off())[lane];
+        }
         if (one_tile) {
-            if (warp < T) acc_buf[warp * 32 + lane] = q8_tile_dot(st, L, warp, lane, xh, xl, sx);
+            if (warp < T) {
+                if (two) {
+                    const long long v0 = q8_tile_dot(st0, L, warp, lane, xh, xl, sx);
+                    const long long v1 = q8_tile_dot(st1, L, warp, lane, xh, xl, sx);
+                    acc0[warp * 32 + lane] = v0;
+                    acc1[warp * 32 + lane] = v1;
+                } else {
+                    acc0[warp * 32 + lane] = q8_tile_dot(st0, L, warp, lane, xh, xl, sx);
+                }
+            }
         } else {
             for (int t = warp; t < T; t += kConsumerWarps) {
                 uint4 th[4], tl[4];
@@ -420,13 +441,19 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemv_kernel(Q8Args a)
                     th[j] = reinterpret_cast<const uint4*>(xh_s + t * 16)[j];
                     tl[j] = reinterpret_cast<const uint4*>(xl_s + t * 16)[j];
                 }
-                acc_buf[t * 32 + lane] = q8_tile_dot(st, L, t, lane, th, tl, reinterpret_cast<const int2*>(sx_s)[t]);
+                const int2 sxt = reinterpret_cast<const int2*>(sx_s)[t];
+                acc0[t * 32 + lane] = q8_tile_dot(st0, L, t, lane, th, tl, sxt);
+                if (two) acc1[t * 32 + lane] = q8_tile_dot(st1, L, t, lane, th, tl, sxt);
             }
         }
         __syncwarp();
         if (lane == 0) {
-            mbar_arrive(&empty[s]);
-            mbar_arrive(&acc_full[b]);
+            mbar_arrive(&empty[s0]);
+            mbar_arrive(&acc_full[b0]);
+            if (two) {
+                mbar_arrive(&empty[s1]);
+                mbar_arrive(&acc_full[b1]);
+            }
         }
     }
 }
@@ -450,6 +477,8 @@ int register_q8_0(tmac_weight_s* w, const uint8_t* d_raw, const float* d_row_max
         q8_row_scale_kernel<<<(unsigned)((w->rows + wpb - 1) / wpb), wpb * 32, 0, s>>>(d_raw, w->rows, w->cols,
                                                                                        d_row_max_abs, w->row_norm);
         TMAC_CUDA_TRY(cudaGetLastError());
+        TMAC_CUDA_TRY(cudaMalloc(&w->top1_scratch, 16));
+        TMAC_CUDA_TRY(cudaMemsetAsync(w->top1_scratch, 0, 16, s));
         return register_q8_wide(w, d_raw, s);
     }
     Q8Layout L = q8_layout(w->rows, w->cols);
@@ -460,6 +489,8 @@ int register_q8_0(tmac_weight_s* w, const uint8_t* d_raw, const float* d_row_max
     if (L.stages < 2) return fail(TMAC_ERR_SHAPE, "Q8_0: cols too large for a two-stage row-group pipeline");
     TMAC_CUDA_TRY(cudaMalloc(&w->row_norm, (size_t)w->rows * sizeof(float)));
     TMAC_CUDA_TRY(cudaMalloc(&w->data, w->data_bytes));
+    TMAC_CUDA_TRY(cudaMalloc(&w->top1_scratch, 16));
+    TMAC_CUDA_TRY(cudaMemsetAsync(w->top1_scratch, 0, 16, s));
     q8_row_scale_kernel<<<(unsigned)((w->rows + wpb - 1) / wpb), wpb * 32, 0, s>>>(d_raw, w->rows, w->cols,
                                                                                    d_row_max_abs, w->row_norm);
     TMAC_CUDA_TRY(cudaGetLastError());
@@ -508,7 +539,12 @@ int launch_q8_0(const tmac_weight_s* w, const float* x, float* y, int64_t* row_a
         a.unit_acc = unit_acc ? unit_acc + (int64_t)b * w->rows * L.T : nullptr;
         a.top1 = top1 ? top1 + b : nullptr;
         a.index_base = index_base;
-        if (xg) a.xg = *xg;
+        if (xg) {
+            a.xg = *xg;
+        } else if (top1) {
+            a.xg.partial = static_cast<unsigned long long*>(w->top1_scratch);
+            a.xg.counter = reinterpret_cast<unsigned*>(a.xg.partial + 1);
+        }
         a.err = device_error_word(w->device);
         TMAC_CUDA_TRY(launch_k(q8_gemv_kernel, dim3(grid), dim3(kThreads), smem, s, a));
         TMAC_CUDA_TRY(cudaGetLastError());

@@ -601,7 +601,12 @@ int launch_q8_wide(const tmac_weight_s* w, const float* x, float* y, int64_t* ro
         a.unit_acc = unit_acc ? unit_acc + (int64_t)b * w->rows * w->tiles : nullptr;
         a.top1 = top1 ? top1 + b : nullptr;
         a.index_base = index_base;
-        if (xg) a.xg = *xg;
+        if (xg) {
+            a.xg = *xg;
+        } else if (top1) {
+            a.xg.partial = static_cast<unsigned long long*>(w->top1_scratch);
+            a.xg.counter = reinterpret_cast<unsigned*>(a.xg.partial + 1);
+        }
         a.rows = w->rows;
         a.cols = (int)w->cols;
         a.nbp = w->nbp;

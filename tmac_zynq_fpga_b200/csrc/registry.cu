@@ -228,6 +228,7 @@ void free_weight(tmac_weight_s* w)
     if (w->gwh) cudaFree(w->gwh);
     if (w->gwl) cudaFree(w->gwl);
     if (w->grinv) cudaFree(w->grinv);
+    if (w->top1_scratch) cudaFree(w->top1_scratch);
     delete w;
 }
 
@@ -538,10 +539,10 @@ int tmac_gemv_top1(tmac_weight_t w, const float* x, float* y, uint64_t* key, int
     if (index_base < 0 || index_base + w->rows > 0x7FFFFFFF) return fail(TMAC_ERR_SHAPE, "bad index range");
     DeviceGuard dg(w->device);
     cudaStream_t s = (cudaStream_t)stream;
-    TMAC_CUDA_TRY(cudaMemsetAsync(key, 0, (size_t)batch * sizeof(uint64_t), s));
     unsigned long long* k = reinterpret_cast<unsigned long long*>(key);
-    if (w->mode == TMAC_MODE_NATIVE && w->type == TMAC_TYPE_Q8_0)
+    if (w->mode == TMAC_MODE_NATIVE && w->type == TMAC_TYPE_Q8_0)  // the kernel writes the key: no reset
         return launch_q8_0(w, x, y, nullptr, nullptr, batch, s, k, index_base);
+    TMAC_CUDA_TRY(cudaMemsetAsync(key, 0, (size_t)batch * sizeof(uint64_t), s));
     rc = tmac_gemv(w, x, y, batch, stream);
     for (int b = 0; !rc && b < batch; b++) rc = launch_top1(y + (int64_t)b * w->rows, w->rows, index_base, k + b, s);
     return rc;

@@ -91,15 +91,16 @@ TMAC_DEV void xchg_top1_thread(const XchgDev& x, unsigned long long k, unsigned 
 
 // End of a GEMV CTA that tracks the top-1 key of its rows: every warp of the
 // `bar_threads` (named barrier `bar_id`) calls it with its warp-reduced key.
-// Without an exchange the keys max-merge into *top1.  With one they merge into
-// the shard's running key; the last CTA to finish takes it (resetting it and
-// the CTA count for the next call) and merges it with every rank's over peer
-// memory into *top1.
+// Without a running key (xg.partial == nullptr) the keys max-merge into *top1,
+// which the caller zeroed.  With one, the CTAs max-merge into it and the last
+// CTA to finish (atomic count) takes it, resetting it and the count for the
+// next call, and writes it to *top1 -- after merging it with every rank's key
+// over peer memory when xg.peers is set.
 TMAC_DEV void top1_cta_finish(const XchgDev& xg, unsigned long long* top1, unsigned long long best, bool leader_warp,
                               int bar_id, int bar_threads, int* err)
 {
     const int lane = threadIdx.x & 31;
-    if (!xg.peers) {
+    if (!xg.partial) {
         if (lane == 0 && best) atomicMax(top1, best);
         return;
     }
@@ -114,7 +115,10 @@ TMAC_DEV void top1_cta_finish(const XchgDev& xg, unsigned long long* top1, unsig
             __threadfence();
             const unsigned long long k = atomicExch(xg.partial, 0ull);
             atomicExch(xg.counter, 0u);
-            xchg_top1_thread(xg, k, top1, err);
+            if (xg.peers)
+                xchg_top1_thread(xg, k, top1, err);
+            else
+                *top1 = k;
         }
     }
 }
