@@ -231,6 +231,7 @@ TMAC_DEV long long q8_tile_dot(const uint8_t* st, const Q8Layout& L, int t, int 
 __global__ void __launch_bounds__(kThreads, 1) q8_gemv_kernel(Q8Args a)
 {
     extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ unsigned long long top1_slots[kFoldWarps];
     const Q8Layout L = a.L;
     const int T = L.T;
     uint8_t* stage_base = smem;
@@ -249,9 +250,10 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemv_kernel(Q8Args a)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     pdl_launch();
-    const int64_t g0 = (int64_t)blockIdx.x * L.groups / gridDim.x;
-    const int64_t g1 = (int64_t)(blockIdx.x + 1) * L.groups / gridDim.x;
-    const int ng = (int)(g1 - g0);
+    // CTA c takes groups c, c + grid, c + 2 grid, ...: at any time the SMs
+    // stream one contiguous window of the weights.
+    const int ng = (int)((L.groups - blockIdx.x + gridDim.x - 1) / gridDim.x);
+    auto group_of = [&](int i) -> int64_t { return (int64_t)blockIdx.x + (int64_t)i * gridDim.x; };
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < L.stages; s++) {
@@ -278,7 +280,7 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemv_kernel(Q8Args a)
                     break;
                 }
                 mbar_arrive_expect_tx(&full[s], (uint32_t)L.group_bytes);
-                bulk_g2s(stage_base + (int64_t)s * L.group_bytes, a.packed + (g0 + i) * L.group_bytes,
+                bulk_g2s(stage_base + (int64_t)s * L.group_bytes, a.packed + group_of(i) * L.group_bytes,
                          (uint32_t)L.group_bytes, &full[s]);
                 issued = i + 1;
             }
@@ -303,7 +305,7 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemv_kernel(Q8Args a)
             const float xs = red[16];
             const long long* acc_buf = accs + b * T * 32;
             const double rs = (double)rs_buf[b * 32 + lane];
-            const int64_t r = (g0 + i) * 32 + lane;
+            const int64_t r = group_of(i) * 32 + lane;
             float yr = 0.0f;
             long long rsum = 0;
             for (int t = 0; t < T; t++) {
@@ -327,7 +329,7 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemv_kernel(Q8Args a)
                 const unsigned long long k = __shfl_xor_sync(0xffffffffu, best, o);
                 best = k > best ? k : best;
             }
-            top1_cta_finish(a.xg, a.top1, best, f == 0, 2, kFoldWarps * 32, a.err);
+            top1_cta_finish(a.xg, a.top1, best, top1_slots, f, f == 0, 2, kFoldWarps * 32, a.err);
         }
         return;
     }

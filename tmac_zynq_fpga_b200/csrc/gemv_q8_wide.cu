@@ -214,6 +214,7 @@ TMAC_DEV int x_part(int v, int p) { return p == 0 ? (v & 127) : p == 1 ? ((v >> 
 __global__ void __launch_bounds__(kThreads, 1) q8_wide_kernel(const __grid_constant__ CUtensorMap tm_q, WideArgs a)
 {
     extern __shared__ uint8_t smem_raw[];
+    __shared__ unsigned long long top1_slots[kEpiWarps];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     const uint32_t sbase = smem_addr(smem);
     uint16_t* cs_s = reinterpret_cast<uint16_t*>(smem + kOffCs);
@@ -509,7 +510,8 @@ __global__ void __launch_bounds__(kThreads, 1) q8_wide_kernel(const __grid_const
                     const unsigned long long k = __shfl_xor_sync(0xffffffffu, best, o);
                     best = k > best ? k : best;
                 }
-                top1_cta_finish(a.xg, a.top1, best, warp == kWarpEpi0, 2, kEpiWarps * 32, a.err);
+                top1_cta_finish(a.xg, a.top1, best, top1_slots, warp - kWarpEpi0, warp == kWarpEpi0, 2, kEpiWarps * 32,
+                                a.err);
             }
         }
     }

@@ -90,36 +90,39 @@ TMAC_DEV void xchg_top1_thread(const XchgDev& x, unsigned long long k, unsigned 
 }
 
 // End of a GEMV CTA that tracks the top-1 key of its rows: every warp of the
-// `bar_threads` (named barrier `bar_id`) calls it with its warp-reduced key.
-// Without a running key (xg.partial == nullptr) the keys max-merge into *top1,
-// which the caller zeroed.  With one, the CTAs max-merge into it and the last
-// CTA to finish (atomic count) takes it, resetting it and the count for the
-// next call, and writes it to *top1 -- after merging it with every rank's key
-// over peer memory when xg.peers is set.
-TMAC_DEV void top1_cta_finish(const XchgDev& xg, unsigned long long* top1, unsigned long long best, bool leader_warp,
-                              int bar_id, int bar_threads, int* err)
+// `bar_threads` (named barrier `bar_id`) calls it with its warp-reduced key;
+// `slots` is shared memory for one key per calling warp, `slot` this warp's.
+// The CTA's maximum is merged with one atomic.  Without a running key
+// (xg.partial == nullptr) it max-merges into *top1, which the caller zeroed.
+// With one, it max-merges into the running key and the last CTA to finish
+// (atomic count) takes that, resetting it and the count for the next call,
+// and writes it to *top1 -- after merging it with every rank's key over peer
+// memory when xg.peers is set.
+TMAC_DEV void top1_cta_finish(const XchgDev& xg, unsigned long long* top1, unsigned long long best,
+                              unsigned long long* slots, int slot, bool leader_warp, int bar_id, int bar_threads,
+                              int* err)
 {
     const int lane = threadIdx.x & 31;
+    if (lane == 0) slots[slot] = best;
+    asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(bar_threads) : "memory");
+    if (!(leader_warp && lane == 0)) return;
+    unsigned long long m = 0;
+    for (int w = 0; w < bar_threads / 32; w++) m = slots[w] > m ? slots[w] : m;
     if (!xg.partial) {
-        if (lane == 0 && best) atomicMax(top1, best);
+        if (m) atomicMax(top1, m);
         return;
     }
-    if (lane == 0) {
-        if (best) atomicMax(xg.partial, best);
+    if (m) atomicMax(xg.partial, m);
+    __threadfence();
+    const unsigned done = atomicAdd(xg.counter, 1u);
+    if (done == gridDim.x - 1) {
         __threadfence();
-    }
-    asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(bar_threads) : "memory");
-    if (leader_warp && lane == 0) {
-        const unsigned done = atomicAdd(xg.counter, 1u);
-        if (done == gridDim.x - 1) {
-            __threadfence();
-            const unsigned long long k = atomicExch(xg.partial, 0ull);
-            atomicExch(xg.counter, 0u);
-            if (xg.peers)
-                xchg_top1_thread(xg, k, top1, err);
-            else
-                *top1 = k;
-        }
+        const unsigned long long k = atomicExch(xg.partial, 0ull);
+        atomicExch(xg.counter, 0u);
+        if (xg.peers)
+            xchg_top1_thread(xg, k, top1, err);
+        else
+            *top1 = k;
     }
 }
 
