@@ -470,8 +470,8 @@ struct BqSmem {
         xs = exc + kExcCap * 16;                     // float [16]
         red = xs + 64;                               // float [32]
         misc = red + 128;                            // int [4]
-        bar = misc + 16;                             // 2 mbarriers
-        total = bar + 16;
+        bar = misc + 16;                             // 3 mbarriers
+        total = bar + 24;
     }
 };
 
@@ -512,31 +512,36 @@ __global__ void __launch_bounds__(NB == 1 ? 1024 : 512) blockq_gemv_kernel(BqArg
     int* misc_s = reinterpret_cast<int*>(smem + L.misc);
     float* xs_s = reinterpret_cast<float*>(smem + L.xs);
     float* red = reinterpret_cast<float*>(smem + L.red);
-    uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L.bar);  // [0] weights, [1] activations
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L.bar);  // [0] weights, [1] activations, [2] exceptions
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
 
     BQ_STAMP(0);
-    // ---- prologue: everything here depends on the weights only.  One thread
-    // stages the CTA's weights, row_inv and exception entries with bulk copies
-    // completing on bar[0].
+    // ---- prologue: everything here depends on the weights only.  Thread 0
+    // stages the CTA's weights, row_inv and exception offsets with bulk copies
+    // completing on bar[0]; thread 32 (thread 0 in a one-warp CTA) looks up
+    // the CTA's exception range and stages those entries on bar[2], so its
+    // global loads do not hold up the weight copies.
+    const unsigned exc_thread = blockDim.x > 32 ? 32u : 0u;
     if (threadIdx.x == 0) {
         mbar_init(&bar[0], 1);
         mbar_init(&bar[1], 1);
         fence_mbar_init();
         const uint32_t wbytes = (uint32_t)(ng * a.group_bytes), rbytes = (uint32_t)(rows_cta * 4);
         const uint32_t ebytes = (uint32_t)((rows_cta + 4) * 4);
-        mbar_expect_tx(&bar[0], wbytes + rbytes + ebytes);
+        mbar_arrive_expect_tx(&bar[0], wbytes + rbytes + ebytes);
         const uint8_t* src = a.data + g0 * a.group_bytes;
         for (uint32_t off = 0; off < wbytes; off += 32768u)
             bulk_g2s(wsm + off, src + off, min(32768u, wbytes - off), &bar[0]);
         bulk_g2s(ri_s, a.row_inv + row0, rbytes, &bar[0]);  // row_inv and exc_ptr are padded
         bulk_g2s(ep_s, a.exc_ptr + row0, ebytes, &bar[0]);  // to whole groups (+4)
+    }
+    if (threadIdx.x == exc_thread) {
+        mbar_init(&bar[2], 1);
+        fence_mbar_init();
         const int e0 = __ldg(a.exc_ptr + row0), e1 = __ldg(a.exc_ptr + min(row0 + rows_cta, a.rows));
-        misc_s[0] = e0;
-        misc_s[1] = e1;
         const uint32_t n = (uint32_t)min(e1 - e0, kExcCap);
-        mbar_arrive_expect_tx(&bar[0], n * 16);
-        if (n) bulk_g2s(exc_s, a.exc + e0, n * 16, &bar[0]);
+        mbar_arrive_expect_tx(&bar[2], n * 16);
+        if (n) bulk_g2s(exc_s, a.exc + e0, n * 16, &bar[2]);
     }
     pdl_launch();
     for (int t = threadIdx.x; t < rows_cta * nb; t += blockDim.x) acc_lo[t] = acc_hi[t] = 0;
@@ -693,10 +698,14 @@ __global__ void __launch_bounds__(NB == 1 ? 1024 : 512) blockq_gemv_kernel(BqArg
 #ifdef TMAC_TRACE
     if (lane == 0 && blockIdx.x < 1024) g_bq_wtrace[blockIdx.x][warp][1] = clock64();
 #endif
-    __syncthreads();
     BQ_STAMP(5);
 
-    // ---- exceptions: acc += (v - v') * x_q[col], one thread per (entry, vector)
+    // ---- exceptions: acc += (v - v') * x_q[col], one thread per (entry,
+    // vector).  The adds are atomic like the main loop's, so a warp starts on
+    // them as soon as its own main-loop items are done -- unless per-unit sums
+    // are wanted: the main loop stores those, so it must finish first.
+    if (a.unit_acc) __syncthreads();
+    if (!mbar_wait_bounded(&bar[2], 0, a.err)) return;
     const int e0 = ep_s[0], e1 = ep_s[rows_cta];
     for (int base = e0; base < e1; base += kExcCap) {
         const int n = min(e1 - base, kExcCap);
