@@ -282,29 +282,55 @@ __global__ void __launch_bounds__(kCtxThreads) pf_softmax_ctx_kernel(const float
 }
 
 // silu(gate) * up per token (one warp), then x_q of the row as byte planes.
-__global__ void __launch_bounds__(256) pf_silu_kernel(float* __restrict__ gu, int64_t M, int8_t* __restrict__ xh,
-                                                      uint8_t* __restrict__ xl, float* __restrict__ xs)
+// silu(gate) * up for one token per CTA, kept in registers: its absolute
+// maximum, x_scale and the byte planes of its x_q are all the down
+// projection needs, so h itself is not written back.  kSiluThreads threads x
+// kSiluVec float4 = kInter values.
+constexpr int kSiluThreads = 304, kSiluVec = 4;
+static_assert(kSiluThreads * kSiluVec * 4 == kInter, "silu tiling");
+__global__ void __launch_bounds__(kSiluThreads) pf_silu_kernel(const float* __restrict__ gu, int8_t* __restrict__ xh,
+                                                              uint8_t* __restrict__ xl, float* __restrict__ xs)
 {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t t = (int64_t)blockIdx.x * 8 + warp;
-    if (t >= M) return;
-    float* g = gu + t * 2 * kInter;
-    const float* u = g + kInter;
+    __shared__ float red[(kSiluThreads + 31) / 32];
+    const int64_t t = blockIdx.x;
+    const float4* g4 = reinterpret_cast<const float4*>(gu + t * 2 * kInter);
+    const float4* u4 = reinterpret_cast<const float4*>(gu + t * 2 * kInter + kInter);
+    float v[kSiluVec][4];
     float mx = 0.0f;
-    for (int i = lane; i < kInter; i += 32) {
-        const float x = g[i];
-        const float v = __fmul_rn(__fdiv_rn(x, __fadd_rn(1.0f, expf_ref(-x))), u[i]);
-        g[i] = v;
-        mx = fmaxf(mx, fabsf(v));
+#pragma unroll
+    for (int k = 0; k < kSiluVec; k++) {
+        const int i = threadIdx.x + k * kSiluThreads;
+        const float4 g = g4[i], u = u4[i];
+        const float gv[4] = {g.x, g.y, g.z, g.w}, uv[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            v[k][e] = __fmul_rn(__fdiv_rn(gv[e], __fadd_rn(1.0f, expf_ref(-gv[e]))), uv[e]);
+            mx = fmaxf(mx, fabsf(v[k][e]));
+        }
     }
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) red[warp] = mx;
+    __syncthreads();
+    mx = 0.0f;
+#pragma unroll
+    for (int w = 0; w < (kSiluThreads + 31) / 32; w++) mx = fmaxf(mx, red[w]);
     const float s = x_scale_from_max(mx);
-    if (lane == 0) xs[t] = s;
-    __syncwarp();
-    for (int i = lane; i < kInter; i += 32) {
-        const int16_t q = quantize_one(g[i], s);
-        xh[t * kInter + i] = (int8_t)(q >> 8);
-        xl[t * kInter + i] = (uint8_t)(q & 0xFF);
+    if (threadIdx.x == 0) xs[t] = s;
+    uint32_t* h4 = reinterpret_cast<uint32_t*>(xh + t * kInter);
+    uint32_t* l4 = reinterpret_cast<uint32_t*>(xl + t * kInter);
+#pragma unroll
+    for (int k = 0; k < kSiluVec; k++) {
+        uint32_t hw = 0, lw = 0;
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            const int16_t q = quantize_one(v[k][e], s);
+            hw |= (uint32_t)((uint16_t)q >> 8) << (8 * e);
+            lw |= (uint32_t)(q & 0xFF) << (8 * e);
+        }
+        const int i = threadIdx.x + k * kSiluThreads;
+        h4[i] = hw;
+        l4[i] = lw;
     }
 }
 
@@ -476,7 +502,7 @@ int prefill_run(tmac_model_s* m, int64_t M, int n_seq, int len, cudaStream_t s)
         TMAC_CUDA_TRY(cudaGetLastError());
         tmac_weight_s* gu = mat(m, lname(l, "ffn_gate_up"));
         if (!gu || (rc = pf_gemm(m, gu, M, kHidden, p->gu, 2 * kInter, s))) return gu ? rc : fail(TMAC_ERR_INVALID, "missing ffn_gate_up");
-        pf_silu_kernel<<<nblk8, 256, 0, s>>>(p->gu, M, p->xh, p->xl, p->xs);
+        pf_silu_kernel<<<(unsigned)M, kSiluThreads, 0, s>>>(p->gu, p->xh, p->xl, p->xs);
         TMAC_CUDA_TRY(cudaGetLastError());
         tmac_weight_s* wd = mat(m, lname(l, "ffn_down.weight"));
         if (!wd || (rc = pf_gemm(m, wd, M, kInter, p->ffn, kHidden, s))) return wd ? rc : fail(TMAC_ERR_INVALID, "missing ffn_down");
