@@ -58,3 +58,15 @@ def test_prefill_growing_batches_keep_weight_planes(mdl):
     n_big, h_big = mdl.prefill(batch, want_hidden=True)
     assert n_big[-1] == n_small[0]
     np.testing.assert_array_equal(h_big[-1], h_small[0])
+
+
+def test_prefill_long_odd_length_matches_decode(mdl):
+    """131 tokens: two K/V tiles of 128 positions, a last query block of 3 and
+    score rows padded to a multiple of 4."""
+    a = model.prompt_tokens(131, seed=31)
+    nxt, hid = mdl.prefill(a[None, :], want_hidden=True)
+    for p in (0, 63, 64, 127, 128, 130):
+        _, h = mdl.generate(a[:p + 1], 0, want_hidden=True)
+        np.testing.assert_array_equal(hid[0, p], h[0], err_msg=f"position {p}")
+    toks, _ = mdl.generate(a, 1)
+    assert nxt[0] == toks[0]

@@ -31,8 +31,7 @@ struct PrefillState {
     float* xs = nullptr;
     int* tokens = nullptr;
     unsigned long long* keys = nullptr;
-    float* scores = nullptr;  // [n_seq*heads*len][len]
-    int64_t cap_seq = 0, cap_scores = 0;
+    int64_t cap_seq = 0;
     std::map<std::string, std::pair<int8_t*, uint8_t*>> q8planes;  // Q8_0 matrices (attn_v)
     std::vector<void*> allocs;        // activation buffers (re-made when a larger batch comes)
     std::vector<void*> plane_allocs;  // weight planes (kept for the model's lifetime)
@@ -146,142 +145,159 @@ __global__ void __launch_bounds__(kHidden / 2 + kKvDim / 2) pf_rope_kernel(
     if (j < kKvDim) vr[t * kKvDim + j] = __fadd_rn(row[kHidden + kKvDim + j], bv ? bv[j] : 0.0f);
 }
 
-// Causal attention in two passes, with K and V tiles in shared memory shared by
-// the 7 query heads of a KV head and a block of queries.  Every value is the
-// decode engine's (rope_attention_kernel) for that token: scores in d order /8,
-// max, exp terms summed in position order, log-sum-exp weights, context
-// accumulated in position order.
-constexpr int kQBlk = 32;                       // queries per CTA
-constexpr int kPTile = 64;                      // positions per K/V tile
-constexpr int kGroup = kHeads / kKvHeads;       // 7 query heads per KV head
-constexpr int kPairs = kGroup * kQBlk;          // (head, query) pairs per CTA
-constexpr size_t kScoresSmem = (size_t)(kPairs + kPTile) * (kHeadDim + 1) * sizeof(float);
+constexpr int kGroup = kHeads / kKvHeads;  // 7 query heads per KV head
 
-// S[(seq*kHeads + h)*len + t][p] = (q_t . k_p) / 8 for p <= t.
-__global__ void __launch_bounds__(256) pf_scores_kernel(const float* __restrict__ qr, const float* __restrict__ kr,
-                                                        int len, float* __restrict__ S)
+// Causal attention in one pass over shared memory: one CTA per (sequence, KV
+// head, QB queries), the 7 query heads of the KV head together.  The scores
+// of its 7*QB (head, query) pairs stay in shared memory (S), so they never go
+// through HBM; every value is the decode engine's (rope_attention_kernel) for
+// that token: scores in d order /8, max, exp terms summed in position order
+// (one thread per pair over the terms computed by all threads), log-sum-exp
+// weights, context accumulated in position order.
+constexpr int kAThreads = 512;
+constexpr int kAPTile = 128;                    // K/V positions staged at a time
+constexpr int kARow = kHeadDim + 4;             // staged K/V and q rows: 16-byte aligned, banks spread
+// S and E rows are len rounded up to 4 floats, so every region stays 16-byte aligned.
+template <int QB>
+constexpr size_t attn_smem(int len)
 {
-    extern __shared__ float ssm[];
-    float(*qs)[kHeadDim + 1] = reinterpret_cast<float(*)[kHeadDim + 1]>(ssm);                 // [kPairs]
-    float(*ks)[kHeadDim + 1] = reinterpret_cast<float(*)[kHeadDim + 1]>(ssm + kPairs * (kHeadDim + 1));  // [kPTile]
-    const int seq = blockIdx.x, kvh = blockIdx.y, t0 = blockIdx.z * kQBlk;
-    const int nq = min(kQBlk, len - t0);
-    const int64_t base = (int64_t)seq * len;
-    for (int i = threadIdx.x; i < kPairs * kHeadDim; i += blockDim.x) {
-        const int pr = i / kHeadDim, d = i % kHeadDim, hh = pr / kQBlk, tq = pr % kQBlk;
-        qs[pr][d] = (tq < nq) ? qr[(base + t0 + tq) * kHidden + (kvh * kGroup + hh) * kHeadDim + d] : 0.0f;
-    }
-    const int tlast = t0 + nq - 1;
-    const int j = threadIdx.x & 15, sub = threadIdx.x >> 4;  // 16 threads per pair, 16 pairs per pass
-    for (int p0 = 0; p0 <= tlast; p0 += kPTile) {
-        __syncthreads();
-        for (int i = threadIdx.x; i < kPTile * kHeadDim; i += blockDim.x) {
-            const int pp = i / kHeadDim, d = i % kHeadDim;
-            ks[pp][d] = (p0 + pp < len) ? kr[(base + p0 + pp) * kKvDim + kvh * kHeadDim + d] : 0.0f;
-        }
-        __syncthreads();
-        for (int pr = sub; pr < kPairs; pr += 16) {
-            const int hh = pr / kQBlk, tq = pr % kQBlk, t = t0 + tq;
-            if (tq >= nq || p0 > t) continue;
-            float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll 8
-            for (int d = 0; d < kHeadDim; d++) {
-                const float q = qs[pr][d];
-#pragma unroll
-                for (int u = 0; u < 4; u++) acc[u] = __fadd_rn(acc[u], __fmul_rn(q, ks[j + 16 * u][d]));
-            }
-            float* row = S + ((int64_t)(seq * kHeads + kvh * kGroup + hh) * len + t) * len;
-#pragma unroll
-            for (int u = 0; u < 4; u++) {
-                const int p = p0 + j + 16 * u;
-                if (p <= t) row[p] = __fdiv_rn(acc[u], 8.0f);
-            }
-        }
-    }
+    return (size_t)(2 * kGroup * QB * ((len + 3) & ~3) + kAPTile * kARow + kGroup * QB * kARow + 2 * kGroup * QB) *
+           sizeof(float);
 }
 
-// Softmax and context: one CTA per (sequence, KV head, query block), 256
-// threads.  Pass 1: one thread per (head, query) pair: max, then the exp terms
-// summed in position order, log-sum.  Pass 2, per 64-position tile: every weight
-// exp(s - log_sum) into shared memory, then each thread accumulates 7 pairs x 8
-// dims in position order, with separately rounded multiply and add (the packed
-// fp32x2 forms are contracted into fused multiply-adds by the assembler, which
-// changes the result in about 1 case in 150, so they are not used here).
-constexpr int kCtxThreads = 256;
-constexpr int kWStride = kPairs + 1;  // weights tile [kPTile][kWStride]
-constexpr size_t kCtxSmem = (size_t)(kPTile * kHeadDim + kPTile * kWStride + kPairs) * sizeof(float);
-__global__ void __launch_bounds__(kCtxThreads) pf_softmax_ctx_kernel(const float* __restrict__ S,
-                                                                     const float* __restrict__ vr, int len,
-                                                                     float* __restrict__ ctx)
+template <int QB>
+__global__ void __launch_bounds__(kAThreads) pf_attention_kernel(const float* __restrict__ qr,
+                                                                 const float* __restrict__ kr,
+                                                                 const float* __restrict__ vr, int len,
+                                                                 float* __restrict__ ctx)
 {
-    extern __shared__ __align__(16) float csm[];
-    float* vs = csm;                                 // [kPTile][kHeadDim]
-    float* wt = vs + kPTile * kHeadDim;              // [kPTile][kWStride]
-    float* lsum = wt + kPTile * kWStride;            // [kPairs]
-    const int seq = blockIdx.x, kvh = blockIdx.y, t0 = blockIdx.z * kQBlk;
-    const int nq = min(kQBlk, len - t0);
-    const int64_t base = (int64_t)seq * len;
-    auto srow = [&](int pr) {
-        return S + ((int64_t)(seq * kHeads + kvh * kGroup + pr / kQBlk) * len + t0 + pr % kQBlk) * len;
-    };
-    // pass 1
-    if (threadIdx.x < kPairs && threadIdx.x % kQBlk < nq) {
-        const int pr = threadIdx.x, t = t0 + pr % kQBlk;
-        const float* row = srow(pr);
-        float mx = row[0];
-        for (int p = 1; p <= t; p++) mx = fmaxf(mx, row[p]);
-        float es = 0.0f;
-        for (int p = 0; p <= t; p++) es = __fadd_rn(es, expf_ref(__fsub_rn(row[p], mx)));
-        lsum[pr] = __fadd_rn(logf_ref(es), mx);
-    }
-    // pass 2
-    const int pg = threadIdx.x >> 3, db = threadIdx.x & 7;  // pairs 7*pg .. +6, dims 8*db .. +7
-    float acc[7][8];
-#pragma unroll
-    for (int i = 0; i < 7; i++)
-#pragma unroll
-        for (int k = 0; k < 8; k++) acc[i][k] = 0.0f;
+    constexpr int NP = kGroup * QB;  // pair pr = head * QB + query
+    extern __shared__ __align__(16) float asm_[];
+    const int ls4 = (len + 3) & ~3;        // row stride of S and E
+    float* S = asm_;                       // [NP][ls4] scores
+    float* E = S + NP * ls4;               // [NP][ls4] exp terms, then weights
+    float* kv = E + NP * ls4;              // [kAPTile][kARow] K, later V
+    float* qs = kv + kAPTile * kARow;      // [NP][kARow]
+    float* mxs = qs + NP * kARow;          // [NP]
+    float* lss = mxs + NP;                 // [NP]
+    const int seq = blockIdx.x, kvh = blockIdx.y;
+    const int nqb = (len + QB - 1) / QB;
+    const int t0 = (nqb - 1 - (int)blockIdx.z) * QB;  // longest rows first
+    const int nq = min(QB, len - t0);
     const int tlast = t0 + nq - 1;
-    for (int p0 = 0; p0 <= tlast; p0 += kPTile) {
+    const int64_t base = (int64_t)seq * len;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+
+    for (int i = tid; i < NP * (kHeadDim / 4); i += kAThreads) {
+        const int pr = i / (kHeadDim / 4), d4 = i % (kHeadDim / 4), hh = pr / QB, tq = pr % QB;
+        float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (tq < nq)
+            v = *reinterpret_cast<const float4*>(qr + (base + t0 + tq) * kHidden + (kvh * kGroup + hh) * kHeadDim + 4 * d4);
+        *reinterpret_cast<float4*>(qs + pr * kARow + 4 * d4) = v;
+    }
+    // ---- scores: thread (query, position) of the tile, the 7 heads at once
+    for (int p0 = 0; p0 <= tlast; p0 += kAPTile) {
         __syncthreads();
-        for (int i = threadIdx.x; i < kPTile * kHeadDim / 4; i += kCtxThreads) {
+        for (int i = tid; i < kAPTile * (kHeadDim / 4); i += kAThreads) {
             const int pp = i / (kHeadDim / 4), d4 = i % (kHeadDim / 4);
-            float4 v4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            if (p0 + pp < len) v4 = *reinterpret_cast<const float4*>(vr + (base + p0 + pp) * kKvDim + kvh * kHeadDim + 4 * d4);
-            *reinterpret_cast<float4*>(vs + pp * kHeadDim + 4 * d4) = v4;
-        }
-        for (int e = threadIdx.x; e < kPairs * kPTile; e += kCtxThreads) {
-            const int pr = e / kPTile, pp = e % kPTile, t = t0 + pr % kQBlk, p = p0 + pp;
-            float w = 0.0f;
-            if (pr % kQBlk < nq && p <= t) w = expf_ref(__fsub_rn(srow(pr)[p], lsum[pr]));
-            wt[pp * kWStride + pr] = w;
+            float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (p0 + pp <= tlast)
+                v = *reinterpret_cast<const float4*>(kr + (base + p0 + pp) * kKvDim + kvh * kHeadDim + 4 * d4);
+            *reinterpret_cast<float4*>(kv + pp * kARow + 4 * d4) = v;
         }
         __syncthreads();
-        const int np = min(kPTile, tlast - p0 + 1);
-        for (int pp = 0; pp < np; pp++) {
-            const float4 va = *reinterpret_cast<const float4*>(vs + pp * kHeadDim + 8 * db);
-            const float4 vb = *reinterpret_cast<const float4*>(vs + pp * kHeadDim + 8 * db + 4);
-            const float v[8] = {va.x, va.y, va.z, va.w, vb.x, vb.y, vb.z, vb.w};
-            const float* wrow = wt + pp * kWStride + 7 * pg;
+        for (int i = tid; i < QB * kAPTile; i += kAThreads) {
+            const int tq = i / kAPTile, pp = i % kAPTile, p = p0 + pp;
+            if (tq >= nq || p > t0 + tq) continue;
+            float acc[kGroup];
 #pragma unroll
-            for (int i = 0; i < 7; i++) {
-                const float w = wrow[i];
+            for (int hh = 0; hh < kGroup; hh++) acc[hh] = 0.0f;
+#pragma unroll 4
+            for (int d4 = 0; d4 < kHeadDim / 4; d4++) {
+                const float4 k4 = *reinterpret_cast<const float4*>(kv + pp * kARow + 4 * d4);
 #pragma unroll
-                for (int k = 0; k < 8; k++) acc[i][k] = __fadd_rn(acc[i][k], __fmul_rn(w, v[k]));
+                for (int hh = 0; hh < kGroup; hh++) {
+                    const float4 q4 = *reinterpret_cast<const float4*>(qs + (hh * QB + tq) * kARow + 4 * d4);
+                    acc[hh] = __fadd_rn(acc[hh], __fmul_rn(q4.x, k4.x));
+                    acc[hh] = __fadd_rn(acc[hh], __fmul_rn(q4.y, k4.y));
+                    acc[hh] = __fadd_rn(acc[hh], __fmul_rn(q4.z, k4.z));
+                    acc[hh] = __fadd_rn(acc[hh], __fmul_rn(q4.w, k4.w));
+                }
             }
+#pragma unroll
+            for (int hh = 0; hh < kGroup; hh++) S[(hh * QB + tq) * ls4 + p] = __fdiv_rn(acc[hh], 8.0f);
         }
     }
-#pragma unroll
-    for (int i = 0; i < 7; i++) {
-        const int pr = 7 * pg + i, tq = pr % kQBlk;
+    __syncthreads();
+    // ---- per pair: max (any order), then the exp terms (one warp per pair)
+    for (int pr = warp; pr < NP; pr += kAThreads / 32) {
+        const int tq = pr % QB, t = t0 + tq;
         if (tq >= nq) continue;
-        float* c = ctx + (base + t0 + tq) * kHidden + (kvh * kGroup + pr / kQBlk) * kHeadDim + 8 * db;
-        *reinterpret_cast<float4*>(c) = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
-        *reinterpret_cast<float4*>(c + 4) = make_float4(acc[i][4], acc[i][5], acc[i][6], acc[i][7]);
+        const float* row = S + pr * ls4;
+        float mx = -INFINITY;
+        for (int p = lane; p <= t; p += 32) mx = fmaxf(mx, row[p]);
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        for (int p = lane; p <= t; p += 32) E[pr * ls4 + p] = expf_ref(__fsub_rn(row[p], mx));
+        if (lane == 0) mxs[pr] = mx;
+    }
+    __syncthreads();
+    // ---- the sums in position order, one thread per pair
+    if (tid < NP && tid % QB < nq) {
+        const int pr = tid, t = t0 + pr % QB;
+        const float* e = E + pr * ls4;
+        float es = 0.0f;
+        int p = 0;
+        for (; p + 3 <= t; p += 4) {  // rows are 16-byte aligned
+            const float4 v = *reinterpret_cast<const float4*>(e + p);
+            es = __fadd_rn(es, v.x);
+            es = __fadd_rn(es, v.y);
+            es = __fadd_rn(es, v.z);
+            es = __fadd_rn(es, v.w);
+        }
+        for (; p <= t; p++) es = __fadd_rn(es, e[p]);
+        lss[pr] = __fadd_rn(logf_ref(es), mxs[pr]);
+    }
+    __syncthreads();
+    // ---- weights exp(s - log_sum) over the terms
+    for (int pr = warp; pr < NP; pr += kAThreads / 32) {
+        const int tq = pr % QB, t = t0 + tq;
+        if (tq >= nq) continue;
+        const float ls = lss[pr];
+        for (int p = lane; p <= t; p += 32) E[pr * ls4 + p] = expf_ref(__fsub_rn(S[pr * ls4 + p], ls));
+    }
+    // ---- context: thread (query, dim, head half), positions in order
+    const int hq = tid / (QB * kHeadDim);               // 0: heads 0..3, 1: heads 4..6
+    const int tq = (tid / kHeadDim) % QB, d = tid % kHeadDim;
+    const bool active = tid < 2 * QB * kHeadDim && tq < nq;
+    const int h0 = hq ? 4 : 0, nh = hq ? kGroup - 4 : 4;
+    const int t = t0 + tq;
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    for (int p0 = 0; p0 <= tlast; p0 += kAPTile) {
+        __syncthreads();
+        for (int i = tid; i < kAPTile * (kHeadDim / 4); i += kAThreads) {
+            const int pp = i / (kHeadDim / 4), d4 = i % (kHeadDim / 4);
+            float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (p0 + pp <= tlast)
+                v = *reinterpret_cast<const float4*>(vr + (base + p0 + pp) * kKvDim + kvh * kHeadDim + 4 * d4);
+            *reinterpret_cast<float4*>(kv + pp * kARow + 4 * d4) = v;
+        }
+        __syncthreads();
+        if (!active) continue;
+        const int np = min(kAPTile, t - p0 + 1);
+        for (int pp = 0; pp < np; pp++) {
+            const float v = kv[pp * kARow + d];
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+                if (j < nh) acc[j] = __fadd_rn(acc[j], __fmul_rn(E[((h0 + j) * QB + tq) * ls4 + p0 + pp], v));
+        }
+    }
+    if (active) {
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+            if (j < nh) ctx[(base + t) * kHidden + (kvh * kGroup + h0 + j) * kHeadDim + d] = acc[j];
     }
 }
 
-// silu(gate) * up per token (one warp), then x_q of the row as byte planes.
 // silu(gate) * up for one token per CTA, kept in registers: its absolute
 // maximum, x_scale and the byte planes of its x_q are all the down
 // projection needs, so h itself is not written back.  kSiluThreads threads x
@@ -347,8 +363,7 @@ int ensure_state(tmac_model_s* m, int64_t M, int n_seq, int len)
 {
     if (!m->prefill) m->prefill = new PrefillState();
     PrefillState* p = m->prefill;
-    const int64_t nsc = M * kHeads * len;
-    if (p->cap >= M && p->cap_seq >= n_seq && p->cap_scores >= nsc) return TMAC_OK;
+    if (p->cap >= M && p->cap_seq >= n_seq) return TMAC_OK;
     for (void* a : p->allocs) cudaFree(a);
     p->allocs.clear();
     p->cap = 0;
@@ -361,12 +376,10 @@ int ensure_state(tmac_model_s* m, int64_t M, int n_seq, int len)
         (rc = ps_alloc(p, &p->ffn, (size_t)M * kHidden)) || (rc = ps_alloc(p, &p->xh, (size_t)M * kInter)) ||
         (rc = ps_alloc(p, &p->xl, (size_t)M * kInter)) || (rc = ps_alloc(p, &p->xs, (size_t)M)) ||
         (rc = ps_alloc(p, &p->tokens, (size_t)M)) || (rc = ps_alloc(p, &p->xlast, (size_t)n_seq * kHidden)) ||
-        (rc = ps_alloc(p, &p->logits, (size_t)n_seq * kVocab)) || (rc = ps_alloc(p, &p->keys, (size_t)n_seq)) ||
-        (rc = ps_alloc(p, &p->scores, (size_t)nsc)))
+        (rc = ps_alloc(p, &p->logits, (size_t)n_seq * kVocab)) || (rc = ps_alloc(p, &p->keys, (size_t)n_seq)))
         return rc;
     p->cap = M;
     p->cap_seq = n_seq;
-    p->cap_scores = nsc;
     return TMAC_OK;
 }
 
@@ -458,14 +471,21 @@ int prefill_run(tmac_model_s* m, int64_t M, int n_seq, int len, cudaStream_t s)
     pf_embed_kernel<<<(unsigned)M, 128, 0, s>>>(m->emb_raw, p->tokens, p->hidden);
     TMAC_CUDA_TRY(cudaGetLastError());
     const unsigned nblk8 = (unsigned)((M + 7) / 8);
-    const size_t ctx_smem = kCtxSmem;
-    static bool attr_done = false;
-    if (!attr_done) {
-        TMAC_CUDA_TRY(cudaFuncSetAttribute(pf_softmax_ctx_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kCtxSmem));
-        TMAC_CUDA_TRY(cudaFuncSetAttribute(pf_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kScoresSmem));
-        attr_done = true;
+    // attention: 4 queries per CTA while their scores fit in shared memory
+    constexpr size_t kMaxAttnSmem = 227 * 1024;
+    const int qb = attn_smem<4>(len) <= kMaxAttnSmem ? 4 : attn_smem<2>(len) <= kMaxAttnSmem ? 2 : 1;
+    const size_t asmem = qb == 4 ? attn_smem<4>(len) : qb == 2 ? attn_smem<2>(len) : attn_smem<1>(len);
+    if (asmem > kMaxAttnSmem) return fail(TMAC_ERR_SHAPE, "prefill: sequence too long for the attention kernel");
+    {
+        static bool attr_done[3] = {};
+        const int k = qb == 4 ? 0 : qb == 2 ? 1 : 2;
+        if (!attr_done[k]) {
+            auto fn = qb == 4 ? pf_attention_kernel<4> : qb == 2 ? pf_attention_kernel<2> : pf_attention_kernel<1>;
+            TMAC_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxAttnSmem));
+            attr_done[k] = true;
+        }
     }
-    const dim3 agrid((unsigned)n_seq, kKvHeads, (unsigned)((len + kQBlk - 1) / kQBlk));
+    const dim3 agrid((unsigned)n_seq, kKvHeads, (unsigned)((len + qb - 1) / qb));
     for (int l = 0; l < kLayers; l++) {
         const float* an = vec_or_null(m, lname(l, "attn_norm.weight"));
         const float* fn = vec_or_null(m, lname(l, "ffn_norm.weight"));
@@ -491,9 +511,12 @@ int prefill_run(tmac_model_s* m, int64_t M, int n_seq, int len, cudaStream_t s)
             p->qkv, vec_or_null(m, lname(l, "attn_q.bias")), vec_or_null(m, lname(l, "attn_k.bias")),
             vec_or_null(m, lname(l, "attn_v.bias")), m->rope_c, m->rope_s, len, p->qr, p->kr, p->vr);
         TMAC_CUDA_TRY(cudaGetLastError());
-        pf_scores_kernel<<<agrid, 256, kScoresSmem, s>>>(p->qr, p->kr, len, p->scores);
-        TMAC_CUDA_TRY(cudaGetLastError());
-        pf_softmax_ctx_kernel<<<agrid, kCtxThreads, ctx_smem, s>>>(p->scores, p->vr, len, p->ctx);
+        if (qb == 4)
+            pf_attention_kernel<4><<<agrid, kAThreads, asmem, s>>>(p->qr, p->kr, p->vr, len, p->ctx);
+        else if (qb == 2)
+            pf_attention_kernel<2><<<agrid, kAThreads, asmem, s>>>(p->qr, p->kr, p->vr, len, p->ctx);
+        else
+            pf_attention_kernel<1><<<agrid, kAThreads, asmem, s>>>(p->qr, p->kr, p->vr, len, p->ctx);
         TMAC_CUDA_TRY(cudaGetLastError());
         if ((rc = quantize_rows(p->ctx, kHidden, (int)M, p->xh, p->xl, p->xs, s))) return rc;
         tmac_weight_s* wo = mat(m, lname(l, "attn_output.weight"));
