@@ -41,7 +41,7 @@ constexpr int kProducerWarp = kConsumerWarps;
 constexpr int kFoldWarp0 = kConsumerWarps + 1;
 constexpr int kFoldWarps = 3;  // fold warp f takes groups i = f mod 3
 constexpr int kThreads = (kConsumerWarps + 1 + kFoldWarps) * 32;
-constexpr int kMaxStages = 6;
+constexpr int kMaxStages = 4;
 // Tile-sum buffers: group i uses buffer i mod kAccBufs; kAccBufs is a multiple of
 // kFoldWarps so each buffer is folded by one warp only, in its own program order.
 constexpr int kAccBufs = 2 * kFoldWarps;
