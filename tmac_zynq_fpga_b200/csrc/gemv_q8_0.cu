@@ -381,10 +381,11 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemv_kernel(Q8Args a)
         xh_s[j] = h;
         xl_s[j] = l;
     }
-    for (int j = threadIdx.x; j < T * 2; j += nct) {
-        int sum = 0;
-        for (int k = 0; k < 32; k++) sum += xq_s[j * 32 + k];
-        sx_s[j] = sum;
+    // block sums of x_q: one warp per 32-column block, a shuffle reduction
+    for (int j = warp; j < T * 2; j += kConsumerWarps) {
+        int sum = xq_s[j * 32 + lane];
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        if (lane == 0) sx_s[j] = sum;
     }
     named_bar_sync(1, nct);
 
