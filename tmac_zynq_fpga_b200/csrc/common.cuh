@@ -293,8 +293,11 @@ int launch_top1(const float* y, int64_t n, int64_t index_base, unsigned long lon
 int register_blockq(tmac_weight_s* w, const uint8_t* d_raw, cudaStream_t s);
 // Activations: fp32 x, or int16 xq, or byte planes xp ([batch][2][cols]: high
 // bytes, low bytes) with their x_scale xs.
+// xmax_parts: with fp32 x at batch 1, max |x| is the maximum of these n_parts
+// values (left by the producer kernel), so the CTAs skip that reduction.
 int launch_blockq(const tmac_weight_s* w, const float* x, const int16_t* xq, const uint8_t* xp, const float* xs,
-                  float* y, int64_t* row_acc, int64_t* unit_acc, int batch, cudaStream_t s);
+                  float* y, int64_t* row_acc, int64_t* unit_acc, int batch, cudaStream_t s,
+                  const float* xmax_parts = nullptr, int n_parts = 0);
 // The reference's exact int16 weights of a NATIVE Q5_0 / Q4_K / Q6_K weight as
 // byte planes wh (signed high) / wl (low), [rows][cols] row-major.
 int blockq_planes(const tmac_weight_s* w, int8_t* wh, uint8_t* wl, cudaStream_t s);

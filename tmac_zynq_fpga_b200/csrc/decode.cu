@@ -287,6 +287,30 @@ __global__ void __launch_bounds__(1024) silu_mul_kernel(float* __restrict__ g, c
     for (int i = threadIdx.x; i < n; i += blockDim.x) store_xq(xq, xp, n, i, quantize_one(g[i], s));
 }
 
+// silu(gate) * up over kSiluCtas CTAs, one value per thread, written back in
+// place; each CTA leaves the maximum |h| of its slice, and ffn_down's GEMV
+// quantises h itself from the maximum of those (no single-CTA reduction).
+static_assert(kSiluCtas * 256 == kInter, "one value per thread");
+__global__ void __launch_bounds__(256) silu_part_kernel(float* __restrict__ g, const float* __restrict__ u,
+                                                        float* __restrict__ part_max)
+{
+    pdl_launch();
+    pdl_wait();
+    __shared__ float red[8];
+    const int i = blockIdx.x * 256 + threadIdx.x;
+    const float x = g[i];
+    const float v = __fmul_rn(__fdiv_rn(x, __fadd_rn(1.0f, expf_ref(-x))), u[i]);
+    g[i] = v;
+    float mx = fabsf(v);
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < 8; w++) mx = fmaxf(mx, red[w]);
+        part_max[blockIdx.x] = fmaxf(mx, red[0]);
+    }
+}
+
 }  // namespace
 }  // namespace tmac
 
@@ -353,9 +377,20 @@ int layer(tmac_model_s* m, int l, int pos, cudaStream_t s, const int* pos_dev = 
     TMAC_CUDA_TRY(launch_k(rmsnorm_kernel, dim3(1), dim3(256), 0, s, m->hidden, (const float*)m->attn, fn, m->xn,
                            m->xq, m->xp, m->xs, kHidden));
     if ((rc = gemv(m, lname(l, "ffn_gate_up"), m->xn, m->gate, s, true))) return rc;
-    TMAC_CUDA_TRY(launch_k(silu_mul_kernel, dim3(1), dim3(1024), 0, s, m->gate, (const float*)m->up, kInter, m->xq,
-                           m->xp, m->xs));
-    if ((rc = gemv(m, lname(l, "ffn_down.weight"), m->gate, m->ffn, s, true))) return rc;
+    const auto wdi = m->mats.find(lname(l, "ffn_down.weight"));
+    const tmac_weight_s* wd = wdi == m->mats.end() ? nullptr : wdi->second;
+    if (wd && wd->mode == TMAC_MODE_NATIVE && wd->type != TMAC_TYPE_Q8_0) {
+        // h over several CTAs; the block-quant GEMV quantises it from their maxima
+        TMAC_CUDA_TRY(launch_k(silu_part_kernel, dim3(kSiluCtas), dim3(256), 0, s, m->gate, (const float*)m->up,
+                               m->silu_max));
+        if ((rc = launch_blockq(wd, m->gate, nullptr, nullptr, nullptr, m->ffn, nullptr, nullptr, 1, s, m->silu_max,
+                                kSiluCtas)))
+            return rc;
+    } else {
+        TMAC_CUDA_TRY(launch_k(silu_mul_kernel, dim3(1), dim3(1024), 0, s, m->gate, (const float*)m->up, kInter,
+                               m->xq, m->xp, m->xs));
+        if ((rc = gemv(m, lname(l, "ffn_down.weight"), m->gate, m->ffn, s, true))) return rc;
+    }
     TMAC_CUDA_TRY(launch_k(rmsnorm_kernel, dim3(1), dim3(256), 0, s, m->hidden, (const float*)m->ffn, next_norm(m, l),
                            m->xn, m->xq, m->xp, m->xs, kHidden));
     TMAC_CUDA_TRY(cudaGetLastError());
@@ -528,6 +563,7 @@ int tmac_model_finalize(tmac_model_t m)
         (rc = dev_alloc(m, &m->token_log, 1)) || (rc = dev_alloc(m, &m->xq, kInter)) ||
         (rc = dev_alloc(m, &m->xp, 2 * kInter)) ||
         (rc = dev_alloc(m, &m->xs, 1)) || (rc = dev_alloc(m, &m->pos_dev, 1)) ||
+        (rc = dev_alloc(m, &m->silu_max, kSiluCtas)) ||
         (rc = dev_alloc(m, &m->tokens, (size_t)m->max_seq)) ||
         (rc = dev_alloc(m, &m->hidden_log, (size_t)m->max_seq * kHidden)))
         return rc;

@@ -429,6 +429,8 @@ struct BqArgs {
     const int16_t* xq_in;    // [nb][cols] quantised activations, or
     const uint8_t* xp_in;    // [nb][2][cols] the same as byte planes (high, low)
     const float* xs_in;      // [nb] x_scale of xq_in / xp_in
+    const float* xmax_parts; // optional (nb 1, fp32 x): max |x| is the maximum of these
+    int n_parts;
     float* y;                // [nb][rows]
     int64_t* row_acc;
     int64_t* unit_acc;
@@ -595,9 +597,14 @@ __global__ void __launch_bounds__(NB == 1 ? 1024 : 512) blockq_gemv_kernel(BqArg
                 xv[k] = (j < cols) ? xb[j] : 0.0f;
                 mx = fmaxf(mx, fabsf(xv[k]));
             }
-            for (int64_t j = threadIdx.x + (int64_t)kXr * blockDim.x; j < cols; j += blockDim.x)
-                mx = fmaxf(mx, fabsf(xb[j]));
-            mx = block_max(mx, red, blockDim.x);
+            if (a.xmax_parts) {  // the producer left per-CTA maxima: no reduction here
+                mx = 0.0f;
+                for (int i = 0; i < a.n_parts; i++) mx = fmaxf(mx, __ldg(a.xmax_parts + i));
+            } else {
+                for (int64_t j = threadIdx.x + (int64_t)kXr * blockDim.x; j < cols; j += blockDim.x)
+                    mx = fmaxf(mx, fabsf(xb[j]));
+                mx = block_max(mx, red, blockDim.x);
+            }
             const float s = x_scale_from_max(mx);
             if (threadIdx.x == 0) xs_s[b] = s;
             uint8_t* p = xpl + (int64_t)b * 2 * cols;
@@ -778,8 +785,10 @@ int launch_nb(const tmac_weight_s* w, BqArgs a, cudaStream_t s)
 
 template <int TYPE>
 int launch_type(const tmac_weight_s* w, const float* x, const int16_t* xq, const uint8_t* xp, const float* xs,
-                float* y, int64_t* row_acc, int64_t* unit_acc, int batch, cudaStream_t s)
+                float* y, int64_t* row_acc, int64_t* unit_acc, int batch, cudaStream_t s, const float* xmax_parts,
+                int n_parts)
 {
+    if (xmax_parts && (batch != 1 || !x)) return fail(TMAC_ERR_SHAPE, "per-CTA maxima need batch 1 and fp32 x");
     const int64_t cols = w->cols, cpr = cols / 32;
     // activation planes take 2*cols bytes per vector next to one group of weights
     const int64_t fixed = BqSmem(1, w->group_bytes, 0, cols).total + 16 * 8 * 8;
@@ -800,6 +809,8 @@ int launch_type(const tmac_weight_s* w, const float* x, const int16_t* xq, const
         a.xq_in = xq ? xq + (int64_t)b0 * cols : nullptr;
         a.xp_in = xp ? xp + (int64_t)b0 * 2 * cols : nullptr;
         a.xs_in = xs ? xs + b0 : nullptr;
+        a.xmax_parts = xmax_parts;
+        a.n_parts = n_parts;
         a.y = y + (int64_t)b0 * w->rows;
         a.row_acc = row_acc ? row_acc + (int64_t)b0 * w->rows : nullptr;
         a.unit_acc = unit_acc ? unit_acc + (int64_t)b0 * w->rows * upr : nullptr;
@@ -907,12 +918,16 @@ int blockq_planes(const tmac_weight_s* w, int8_t* wh, uint8_t* wl, cudaStream_t 
 }
 
 int launch_blockq(const tmac_weight_s* w, const float* x, const int16_t* xq, const uint8_t* xp, const float* xs,
-                  float* y, int64_t* row_acc, int64_t* unit_acc, int batch, cudaStream_t s)
+                  float* y, int64_t* row_acc, int64_t* unit_acc, int batch, cudaStream_t s, const float* xmax_parts,
+                  int n_parts)
 {
     switch (w->type) {
-    case TMAC_TYPE_Q5_0: return launch_type<TMAC_TYPE_Q5_0>(w, x, xq, xp, xs, y, row_acc, unit_acc, batch, s);
-    case TMAC_TYPE_Q4_K: return launch_type<TMAC_TYPE_Q4_K>(w, x, xq, xp, xs, y, row_acc, unit_acc, batch, s);
-    case TMAC_TYPE_Q6_K: return launch_type<TMAC_TYPE_Q6_K>(w, x, xq, xp, xs, y, row_acc, unit_acc, batch, s);
+    case TMAC_TYPE_Q5_0:
+        return launch_type<TMAC_TYPE_Q5_0>(w, x, xq, xp, xs, y, row_acc, unit_acc, batch, s, xmax_parts, n_parts);
+    case TMAC_TYPE_Q4_K:
+        return launch_type<TMAC_TYPE_Q4_K>(w, x, xq, xp, xs, y, row_acc, unit_acc, batch, s, xmax_parts, n_parts);
+    case TMAC_TYPE_Q6_K:
+        return launch_type<TMAC_TYPE_Q6_K>(w, x, xq, xp, xs, y, row_acc, unit_acc, batch, s, xmax_parts, n_parts);
     default: return fail(TMAC_ERR_TYPE, "launch_blockq: unsupported type");
     }
 }

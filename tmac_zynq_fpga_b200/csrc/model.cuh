@@ -13,6 +13,7 @@
 namespace tmac {
 
 constexpr int kHidden = 896, kInter = 4864, kVocab = 151936, kLayers = 24;
+constexpr int kSiluCtas = 19;  // x 256 threads = kInter
 constexpr int kHeads = 14, kKvHeads = 2, kHeadDim = 64, kKvDim = kKvHeads * kHeadDim;
 
 // glibc's expf / logf evaluate in double precision and round once, which makes
@@ -47,6 +48,7 @@ struct tmac_model_s {
     int16_t* xq = nullptr;  // quantised activations shared by several matmuls
     uint8_t* xp = nullptr;  // the same x_q as byte planes (block-quant GEMVs)
     float* xs = nullptr;
+    float* silu_max = nullptr;  // [kSiluCtas] per-CTA max |h| of silu(gate) * up
     // graph-driven generation: position, token and hidden-state logs on the device
     int* pos_dev = nullptr;
     int* tokens = nullptr;        // [max_seq]
