@@ -58,3 +58,25 @@ def test_registration_rejects_bad_arguments_without_gpu():
     assert L.tmac_weight_register(tm.Q5_0, 0, 4, 32, buf, 64, 0, None, 0, ctypes.byref(h)) == -4
     assert L.tmac_weight_register(tm.F32, 0, 4, 4, buf, 64, 0, None, 0, ctypes.byref(h)) == -2
     assert b"n_bytes" in L.tmac_last_error() or L.tmac_last_error()
+
+
+def test_peer_exchange_rejects_bad_arguments_without_gpu():
+    L = tm.lib()
+    key = ctypes.c_uint64(0)
+    out = ctypes.c_void_p()
+    # argument checks come before any device access
+    assert L.tmac_xchg_create(0, 0, 0, ctypes.byref(out)) != 0        # world < 1
+    assert L.tmac_xchg_create(0, 2, 2, ctypes.byref(out)) != 0        # rank >= world
+    assert L.tmac_xchg_create(0, 2, 0, None) != 0
+    assert L.tmac_xchg_top1(None, ctypes.byref(key), None) != 0
+    assert L.tmac_xchg_gemv_top1(None, None, None, None, None, 0, None) != 0
+    assert L.tmac_xchg_ipc_handle(None, None) != 0
+    assert L.tmac_xchg_open(None, None) != 0
+    assert L.tmac_xchg_free(None) == 0
+
+
+def test_pdl_switch_returns_previous_setting():
+    L = tm.lib()
+    prev = L.tmac_set_pdl(1)
+    assert L.tmac_set_pdl(0) == 1
+    assert L.tmac_set_pdl(prev) == 0
