@@ -459,7 +459,7 @@ constexpr int kExcCap = 512;  // exception entries staged in shared memory per p
 
 // Shared memory of one CTA (offsets from the dynamic base; all 16-byte aligned).
 struct BqSmem {
-    int64_t w, x, acc, ri, ep, exc, xs, red, misc, bar, total;
+    int64_t w, x, acc, ri, ep, exc, xs, red, bar, total;
     __host__ __device__ BqSmem(int64_t gpc, int64_t group_bytes, int64_t nb, int64_t cols)
     {
         const int64_t rows = gpc * 8;
@@ -471,8 +471,7 @@ struct BqSmem {
         exc = ep + (rows + 4) * 4;                   // int4 [kExcCap]
         xs = exc + kExcCap * 16;                     // float [16]
         red = xs + 64;                               // float [32]
-        misc = red + 128;                            // int [4]
-        bar = misc + 16;                             // 3 mbarriers
+        bar = red + 128;                             // 3 mbarriers
         total = bar + 24;
     }
 };
@@ -511,7 +510,6 @@ __global__ void __launch_bounds__(NB == 1 ? 1024 : 512) blockq_gemv_kernel(BqArg
     int* ep_s = reinterpret_cast<int*>(smem + L.ep);
     float* ri_s = reinterpret_cast<float*>(smem + L.ri);
     int4* exc_s = reinterpret_cast<int4*>(smem + L.exc);
-    int* misc_s = reinterpret_cast<int*>(smem + L.misc);
     float* xs_s = reinterpret_cast<float*>(smem + L.xs);
     float* red = reinterpret_cast<float*>(smem + L.red);
     uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L.bar);  // [0] weights, [1] activations, [2] exceptions

@@ -359,7 +359,7 @@ int ps_alloc(PrefillState* p, T** ptr, size_t n)
     return TMAC_OK;
 }
 
-int ensure_state(tmac_model_s* m, int64_t M, int n_seq, int len)
+int ensure_state(tmac_model_s* m, int64_t M, int n_seq)
 {
     if (!m->prefill) m->prefill = new PrefillState();
     PrefillState* p = m->prefill;
@@ -565,7 +565,7 @@ extern "C" int tmac_model_prefill(tmac_model_t m, const int* tokens, int n_seq, 
     DeviceGuard dg(m->device);
     if (!dg.ok) return fail(TMAC_ERR_CUDA, "cudaSetDevice failed");
     const int64_t M = (int64_t)n_seq * len;
-    int rc = ensure_state(m, M, n_seq, len);
+    int rc = ensure_state(m, M, n_seq);
     if (rc) return rc;
     cudaStream_t s = (cudaStream_t)stream;
     PrefillState* p = m->prefill;
