@@ -298,6 +298,25 @@ typedef struct tmac_chain_stats {
 int tmac_chain_run(void* arena_dev, size_t arena_bytes, uint32_t arena_base, const void* arena_host,
                    uint32_t head, int max_desc, tmac_chain_stats* stats, void* stream);
 
+/*
+ * Phase-B dump for the Verilog testbench: the files the reference's
+ * --dump-phaseb writes (phaseb_dump_files, tmac_gguf.cpp:597-708), with the
+ * expected rows computed on the GPU (tmac_chain_run, one descriptor at a time).
+ *   bin_path: DDR bytes [bin_base, desc_base + 32 * ndesc) of the arena with the
+ *             chain's descriptors copied in chain order to desc_base and every
+ *             next_desc_addr but the last set to 0xFFFFFFFF (the reference uses
+ *             bin_base = 0x18000000 and desc_base = its allocator's next free
+ *             offset rounded up to 32).
+ *   hdr_path: uint32 magic 0x50484244 ("PHBD"), ndesc, desc_base, total rows;
+ *             per descriptor uint32 {result_addr, rows, act_total_bytes,
+ *             previous descriptor's result_addr, offset of its rows}; then the
+ *             int64 rows of every descriptor in chain order.
+ * arena_host holds DDR [arena_base, arena_base + arena_bytes) and must reach past
+ * the copied descriptors; it is not modified.  Synchronous; uses `device`.
+ */
+int tmac_phaseb_dump(const void* arena_host, size_t arena_bytes, uint32_t arena_base, uint32_t head,
+                     uint32_t desc_base, uint32_t bin_base, const char* bin_path, const char* hdr_path, int device);
+
 /* ------------------------------------------------------------------------ */
 /* Whole-model greedy decode (Qwen2-0.5B shape: 24 layers, hidden 896, 14/2
  * heads of 64, SwiGLU 4864, vocab 151936, tied Q8_0 embedding), replacing the

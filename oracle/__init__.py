@@ -226,3 +226,39 @@ def ref_chain_results(arena, base, head, cap=1 << 16):
         n = R.ref_phaseb_run(off, _ptr(acc), cap)
         out.append(acc[:n].copy())
     return out
+
+
+def phaseb_dump_bytes(arena, base, head, desc_base, bin_base, cap=1 << 16):
+    """Restated phaseb_dump_files (sim/tmac_gguf.cpp:597-708): the bytes of the
+    testbench's DDR image (.bin) and header (.hdr).  The chain's descriptors are
+    copied in chain order to desc_base, every next_desc_addr but the last set to
+    0xFFFFFFFF; the image is DDR [bin_base, desc_base + 32 * ndesc).  The header
+    is magic "PHBD", ndesc, desc_base, total rows, then per descriptor
+    (result_addr, rows, act_total_bytes, previous result_addr, offset of its rows)
+    as uint32 and every descriptor's int64 rows from phaseb_run.  `arena` covers
+    [base, base + len) and must reach past the copied descriptors."""
+    arena = np.ascontiguousarray(arena, dtype=np.uint8)
+    offs = walk_chain(arena, base, head)
+    n = len(offs)
+    img = arena.copy()
+    for i, off in enumerate(offs):
+        d = arena[off - base: off - base + 32].copy()
+        d[0:4] = np.frombuffer(np.uint32(0xFFFFFFFF if i < n - 1 else 0).tobytes(), np.uint8)
+        img[desc_base - base + 32 * i: desc_base - base + 32 * (i + 1)] = d
+    end = desc_base + 32 * n
+    bin_bytes = img[bin_base - base: end - base].tobytes()
+    rows, accs, table = [], [], []
+    prev, pos = 0, 0
+    for off in offs:
+        r, acc = phaseb_run(arena, base, off, cap)
+        d = arena[off - base: off - base + 32]
+        result_addr = int(np.frombuffer(d[12:16].tobytes(), np.uint32)[0])
+        act_bytes = int(d[0x17]) | (int(d[0x18]) << 8)
+        table.append((result_addr, r, act_bytes, prev, pos))
+        accs.append(acc)
+        pos += r
+        prev = result_addr
+    hdr = np.array([0x50484244, n, desc_base, pos], np.uint32).tobytes()
+    hdr += np.array(table, np.uint32).reshape(-1).tobytes() if table else b""
+    hdr += b"".join(a.astype(np.int64).tobytes() for a in accs)
+    return bin_bytes, hdr

@@ -139,3 +139,53 @@ def test_gpu_chain_full_model_shapes():
         res = int.from_bytes(arena[off - base + 12: off - base + 16].tobytes(), "little")
         got = np.frombuffer(out[res - base: res - base + 8 * len(ref)].tobytes(), np.int64)
         np.testing.assert_array_equal(got, ref)
+
+
+# ---- Phase-B dump (phaseb_dump_files, tmac_gguf.cpp:597-708) ---------------
+
+def _dump_case():
+    arena, base, head, offs, results, counts = load_fixture()
+    desc_base = base + ((arena.nbytes + 31) & ~31)       # the reference: next free offset rounded to 32
+    room = np.concatenate([arena, np.zeros(desc_base - base - arena.nbytes + 32 * len(offs), np.uint8)])
+    return room, base, head, offs, results, counts, desc_base
+
+
+def test_oracle_dump_layout_and_rows():
+    room, base, head, offs, results, counts, desc_base = _dump_case()
+    b, h = oracle.phaseb_dump_bytes(room, base, head, desc_base, base)
+    hdr = np.frombuffer(h[:16], np.uint32)
+    assert list(hdr) == [0x50484244, len(offs), desc_base, int(sum(counts))]
+    table = np.frombuffer(h[16:16 + 20 * len(offs)], np.uint32).reshape(-1, 5)
+    assert list(table[:, 1]) == list(counts) and list(table[:, 4]) == [0, 128, 240]
+    assert table[0, 3] == 0 and list(table[1:, 3]) == list(table[:-1, 0])
+    np.testing.assert_array_equal(np.frombuffer(h[16 + 20 * len(offs):], np.int64), results)
+    assert len(b) == desc_base + 32 * len(offs) - base
+    nxt = [int(np.frombuffer(b[desc_base - base + 32 * i: desc_base - base + 32 * i + 4], np.uint32)[0])
+           for i in range(len(offs))]
+    assert nxt == [0xFFFFFFFF] * (len(offs) - 1) + [0]
+    for i, off in enumerate(offs):  # every other descriptor byte copied unchanged
+        assert b[desc_base - base + 32 * i + 4: desc_base - base + 32 * (i + 1)] == \
+            room[off - base + 4: off - base + 32].tobytes()
+
+
+def test_dump_rejects_bad_arguments_without_gpu():
+    room, base, head, offs, *_ , desc_base = _dump_case()
+    L = tm.lib()
+    buf = np.ascontiguousarray(room)
+    assert L.tmac_phaseb_dump(None, 0, base, head, desc_base, base, b"a", b"b", 0) == -1
+    # misaligned or too-late desc_base, bin_base past desc_base: refused before any device access
+    assert L.tmac_phaseb_dump(buf.ctypes.data, buf.nbytes, base, head, desc_base + 4, base, b"a", b"b", 0) == -4
+    assert L.tmac_phaseb_dump(buf.ctypes.data, buf.nbytes, base, head, desc_base + 64, base, b"a", b"b", 0) == -4
+    assert L.tmac_phaseb_dump(buf.ctypes.data, buf.nbytes, base, head, desc_base, desc_base + 32, b"a", b"b", 0) == -4
+
+
+@pytest.mark.gpu
+def test_gpu_dump_files_equal_the_oracle():
+    room, base, head, offs, results, counts, desc_base = _dump_case()
+    out = os.path.join(HERE, ".phaseb_out")
+    os.makedirs(out, exist_ok=True)
+    bp, hp = os.path.join(out, "tb_phaseb.bin"), os.path.join(out, "tb_phaseb.hdr")
+    tm.phaseb_dump(room, base, head, desc_base, base, bp, hp)
+    b, h = oracle.phaseb_dump_bytes(room, base, head, desc_base, base)
+    assert open(bp, "rb").read() == b
+    assert open(hp, "rb").read() == h

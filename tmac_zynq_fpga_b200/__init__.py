@@ -89,6 +89,8 @@ def lib():
             "tmac_xchg_open": (ctypes.c_int, [_P, ctypes.c_char_p]),
             "tmac_xchg_top1": (ctypes.c_int, [_P, _P, _P]),
             "tmac_set_pdl": (ctypes.c_int, [ctypes.c_int]),
+            "tmac_phaseb_dump": (ctypes.c_int, [_P, ctypes.c_size_t, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32,
+                                                ctypes.c_uint32, ctypes.c_char_p, ctypes.c_char_p, ctypes.c_int]),
             "tmac_xchg_gemv_top1": (ctypes.c_int, [_P, _P, _P, _P, _P, ctypes.c_int64, _P]),
             "tmac_xchg_free": (ctypes.c_int, [_P]),
             "tmac_reserve": (ctypes.c_int, [ctypes.c_int, _I64, _I64]),
@@ -327,6 +329,14 @@ def chain_run(arena_dev, arena_bytes, base, head, arena_host=None, max_desc=1 <<
     check(lib().tmac_chain_run(_ptr(arena_dev), arena_bytes, base, _ptr(arena_host), head, max_desc,
                                ctypes.byref(st), s))
     return st
+
+
+def phaseb_dump(arena_host, base, head, desc_base, bin_base, bin_path, hdr_path, device=0):
+    """Writes the reference's --dump-phaseb testbench files for a chain held in the
+    host DDR image `arena_host` (tmac_phaseb_dump; expected rows from the GPU)."""
+    arena_host = np.ascontiguousarray(arena_host, dtype=np.uint8)
+    check(lib().tmac_phaseb_dump(_ptr(arena_host), arena_host.nbytes, base, head, desc_base, bin_base,
+                                 os.fsencode(bin_path), os.fsencode(hdr_path), device))
 
 
 def top1_decode(key):

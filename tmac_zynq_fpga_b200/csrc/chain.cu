@@ -236,3 +236,100 @@ extern "C" int tmac_chain_run(void* arena_dev, size_t arena_bytes, uint32_t aren
     if (stats) *stats = st;
     return TMAC_OK;
 }
+
+// Phase-B dump for the Verilog testbench (phaseb_dump_files, tmac_gguf.cpp:597-708):
+// the expected rows of every descriptor come from the GPU runner above, one
+// descriptor at a time (its next_desc_addr cleared in a scratch copy of the arena),
+// exactly as the reference runs phaseb_run_descriptor per descriptor.
+extern "C" int tmac_phaseb_dump(const void* arena_host, size_t arena_bytes, uint32_t arena_base, uint32_t head,
+                                uint32_t desc_base, uint32_t bin_base, const char* bin_path, const char* hdr_path,
+                                int device)
+{
+    if (!arena_host || !bin_path || !hdr_path) return fail(TMAC_ERR_INVALID, "NULL arena or path");
+    const uint8_t* src = static_cast<const uint8_t*>(arena_host);
+    // 1. the chain, walked and bounds-checked on the host
+    std::vector<uint32_t> offs;
+    for (uint32_t off = head; off != 0;) {
+        if (offs.size() >= (1u << 20)) return fail(TMAC_ERR_BOUNDS, "descriptor chain too long (cycle?)");
+        if (!in_arena(off, sizeof(tmac_phaseb_desc), arena_base, arena_bytes))
+            return fail(TMAC_ERR_BOUNDS, "descriptor offset outside the arena");
+        offs.push_back(off);
+        tmac_phaseb_desc d;
+        memcpy(&d, src + (off - arena_base), sizeof(d));
+        off = d.next_desc_addr;
+    }
+    const uint64_t ndesc = offs.size();
+    const uint64_t desc_end = (uint64_t)desc_base + ndesc * sizeof(tmac_phaseb_desc);
+    if ((desc_base & 31u) || !in_arena(desc_base, ndesc * sizeof(tmac_phaseb_desc), arena_base, arena_bytes))
+        return fail(TMAC_ERR_BOUNDS, "desc_base must be 32-byte aligned with room for the descriptors in the arena");
+    if (bin_base < arena_base || bin_base > desc_base) return fail(TMAC_ERR_BOUNDS, "bin_base outside [arena, desc_base]");
+    // 2. expected rows on the GPU
+    DeviceGuard dg(device);
+    if (!dg.ok) return fail(TMAC_ERR_CUDA, "cudaSetDevice failed");
+    std::vector<uint8_t> mirror(src, src + arena_bytes);
+    uint8_t* dev = nullptr;
+    TMAC_CUDA_TRY(cudaMalloc(&dev, arena_bytes));
+    struct Freer {
+        uint8_t* p;
+        ~Freer() { cudaFree(p); }
+    } freer{dev};
+    TMAC_CUDA_TRY(cudaMemcpy(dev, src, arena_bytes, cudaMemcpyHostToDevice));
+    struct Info {
+        uint32_t result_addr, rows, act_bytes;
+        std::vector<int64_t> acc;
+    };
+    std::vector<Info> info(ndesc);
+    for (uint64_t i = 0; i < ndesc; i++) {
+        const uint32_t off = offs[i];
+        tmac_phaseb_desc d;
+        memcpy(&d, src + (off - arena_base), sizeof(d));
+        tmac_phaseb_desc alone = d;
+        alone.next_desc_addr = 0;
+        memcpy(mirror.data() + (off - arena_base), &alone, sizeof(alone));
+        TMAC_CUDA_TRY(cudaMemcpy(dev + (off - arena_base), &alone, sizeof(alone), cudaMemcpyHostToDevice));
+        tmac_chain_stats st{};
+        const int rc = tmac_chain_run(dev, arena_bytes, arena_base, mirror.data(), off, 1, &st, nullptr);
+        if (rc) return rc;
+        Info& in = info[i];
+        in.result_addr = d.result_addr;
+        in.rows = (uint32_t)st.result_rows;
+        in.act_bytes = d.act_total_bytes;
+        in.acc.resize(in.rows);
+        if (in.rows)
+            TMAC_CUDA_TRY(cudaMemcpy(in.acc.data(), dev + (d.result_addr - arena_base), (size_t)in.rows * 8,
+                                     cudaMemcpyDeviceToHost));
+        memcpy(mirror.data() + (off - arena_base), &d, sizeof(d));
+        TMAC_CUDA_TRY(cudaMemcpy(dev + (off - arena_base), &d, sizeof(d), cudaMemcpyHostToDevice));
+    }
+    // 3. the DDR image with the descriptors placed contiguously at desc_base
+    std::vector<uint8_t> img(src, src + arena_bytes);
+    for (uint64_t i = 0; i < ndesc; i++) {
+        tmac_phaseb_desc d;
+        memcpy(&d, src + (offs[i] - arena_base), sizeof(d));
+        d.next_desc_addr = (i + 1 < ndesc) ? 0xFFFFFFFFu : 0u;
+        memcpy(img.data() + (desc_base - arena_base) + i * sizeof(d), &d, sizeof(d));
+    }
+    FILE* fb = fopen(bin_path, "wb");
+    if (!fb) return fail(TMAC_ERR_INVALID, std::string("cannot write ") + bin_path);
+    const size_t nb = (size_t)(desc_end - bin_base);
+    const bool okb = fwrite(img.data() + (bin_base - arena_base), 1, nb, fb) == nb;
+    fclose(fb);
+    if (!okb) return fail(TMAC_ERR_INVALID, std::string("short write to ") + bin_path);
+    // 4. the header
+    std::vector<uint32_t> h = {0x50484244u, (uint32_t)ndesc, desc_base, 0u};
+    uint32_t pos = 0, prev = 0;
+    for (const Info& in : info) {
+        h.insert(h.end(), {in.result_addr, in.rows, in.act_bytes, prev, pos});
+        pos += in.rows;
+        prev = in.result_addr;
+    }
+    h[3] = pos;
+    FILE* fh = fopen(hdr_path, "wb");
+    if (!fh) return fail(TMAC_ERR_INVALID, std::string("cannot write ") + hdr_path);
+    bool okh = fwrite(h.data(), 4, h.size(), fh) == h.size();
+    for (const Info& in : info)
+        if (in.rows) okh = okh && fwrite(in.acc.data(), 8, in.rows, fh) == in.rows;
+    fclose(fh);
+    if (!okh) return fail(TMAC_ERR_INVALID, std::string("short write to ") + hdr_path);
+    return TMAC_OK;
+}
