@@ -90,6 +90,9 @@ int tmac_set_pdl(int on);
  *   row_max_abs:   optional host float[rows] for Q8_0 NATIVE
  *                  (the `*_row_max_abs` tensor, sim/matmul_q8.cpp:22-35).
  * The handle owns its device memory until tmac_weight_free.
+ * Environment: TMAC_Q8_WIDE=1 at registration puts a NATIVE Q8_0 matrix with
+ * rows >= 16384 and 128 <= cols <= 896 in the tensor-core layout (identical
+ * results; slower than the default CUDA-core kernel on B200 at batch 1).
  */
 int tmac_weight_register(int type, int mode, int64_t rows, int64_t cols,
                          const void* blocks, size_t n_bytes, int blocks_on_device,
