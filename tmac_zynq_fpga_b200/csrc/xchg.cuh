@@ -113,10 +113,11 @@ TMAC_DEV void top1_cta_finish(const XchgDev& xg, unsigned long long* top1, unsig
         return;
     }
     if (m) atomicMax(xg.partial, m);
-    __threadfence();
-    const unsigned done = atomicAdd(xg.counter, 1u);
+    // acquire-release count: each CTA's max is ordered before its increment,
+    // and the CTA that sees the last increment sees every max
+    unsigned done;
+    asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(done) : "l"(xg.counter) : "memory");
     if (done == gridDim.x - 1) {
-        __threadfence();
         const unsigned long long k = atomicExch(xg.partial, 0ull);
         atomicExch(xg.counter, 0u);
         if (xg.peers)
