@@ -14,6 +14,10 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "liboracle.so")
 REF_PATH = os.path.join(HERE, "_ref", "libtmac_ref.so")
+# The reference engine with its matmul_fpga_* drivers bound to libtmac_cuda.so
+# (tmac_zynq_fpga_b200/host/matmul_fpga_binding.cpp): not a checker, the
+# drop-in under test.  Loading it touches no GPU; its drivers need one.
+REF_SHIM_PATH = os.path.join(HERE, "_ref", "libtmac_ref_shim.so")
 
 PATH_NATIVE, PATH_INT16, PATH_F32 = 0, 1, 2
 
@@ -60,6 +64,14 @@ def lib():
 
 def ref_available():
     return os.path.exists(REF_PATH)
+
+
+def ref_shim():
+    """The reference engine re-pointed at libtmac_cuda.so (see REF_SHIM_PATH)."""
+    R = ctypes.CDLL(REF_SHIM_PATH)
+    R.ref_decode.restype = ctypes.c_int
+    R.ref_decode.argtypes = [ctypes.c_char_p, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P, _P, _P]
+    return R
 
 
 def ref():

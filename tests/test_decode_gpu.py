@@ -12,6 +12,7 @@ import os
 import numpy as np
 import pytest
 
+import oracle
 import tmac_zynq_fpga_b200 as tm
 from tmac_zynq_fpga_b200 import model
 
@@ -43,3 +44,27 @@ def test_hidden_states_within_tolerance(decoded):
     ref = g["hidden"]
     err = np.abs(hid - ref).max(axis=1) / np.abs(ref).max(axis=1)
     assert err.max() < HIDDEN_RTOL, f"max relative hidden error {err.max():.3g} (per step {np.round(err, 6)})"
+
+
+@pytest.mark.skipif(not os.path.exists(oracle.REF_SHIM_PATH), reason="oracle/_ref/libtmac_ref_shim.so not built")
+def test_reference_engine_on_the_binding_is_bit_identical():
+    """The drop-in itself: the reference's own decode loop (load_tmac,
+    process_prompt, get_logits_q8, forward_all_layers; tmac_gguf.cpp) with its
+    five matmul_fpga_* drivers replaced by tmac_zynq_fpga_b200/host/
+    matmul_fpga_binding.cpp.  Every matmul is bit-exact, the rest is the
+    reference's own CPU code, so tokens, logits and every hidden state equal the
+    fixture the unmodified reference produced -- exactly, not within a
+    tolerance."""
+    g = np.load(FIX)
+    R = oracle.ref_shim()
+    prompt = g["prompt"].astype(np.int32)
+    n_gen = len(g["tokens"])
+    toks = np.zeros(n_gen, np.int32)
+    logit = np.zeros(n_gen, np.float32)
+    hidden = np.zeros((n_gen + 1, model.HIDDEN), np.float32)
+    n = R.ref_decode(model.default_model_path(0).encode(), prompt.ctypes.data, len(prompt), n_gen, 1,
+                     toks.ctypes.data, logit.ctypes.data, hidden.ctypes.data)
+    assert n == n_gen
+    np.testing.assert_array_equal(toks, g["tokens"])
+    np.testing.assert_array_equal(logit.view(np.int32), g["logit"].view(np.int32))
+    np.testing.assert_array_equal(hidden.view(np.int32), g["hidden"].view(np.int32))
