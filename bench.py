@@ -1,5 +1,5 @@
 #!/usr/bin/env python3
-"""Benchmark of the Q8_0 tied-embedding logits GEMV:
+"""Benchmark of the Q8_0 tied-embedding logits GEMV (151936 x 896, batch 1):
 151936 x 896 Q8_0 weights, batch 1, fp32 logits, on 1..8 B200s (vocab-row
 shards, one process per GPU).
 
@@ -197,7 +197,7 @@ def cpu_baseline_single():
 
 
 def model_extras(world=1, rank=0):
-    """BASELINE configs 4 and 5 through the public model API: greedy decode
+    """Full decode and batched prefill through the public model API: greedy decode
     (8-token prompt + 64 steps, tokens checked against the reference's committed
     fixture; one GPU only: decode does not shard) and batched prefill of 64 x 512
     tokens, sharded by sequence over the ranks (no collective on the data path;

@@ -1,4 +1,4 @@
-"""Full greedy decode against the reference engine itself.
+"""Full greedy decode of the mixed-quant 24-layer model against the reference engine itself.
 
 The fixture tests/golden/decode_greedy_seed0.npz comes from the reference's
 own process_prompt / get_logits_q8 / forward_all_layers (oracle/_ref, see

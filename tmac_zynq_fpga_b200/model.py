@@ -6,7 +6,7 @@ sim/tmac_gguf.cpp:1894-1947): b"TMAC", u64 n_tensors, then per tensor
 u64 name_len, name bytes, u64 rows, u64 cols, u32 GGUF type, u64 n_bytes, data.
 rows = GGUF ne[1] (output dim), cols = ne[0] (input dim).
 
-Quantisation mix: layers {0,1,3,6,7,8,9,10,13,16,19,21} use
+Quantisation mix of the benchmark model: layers {0,1,3,6,7,8,9,10,13,16,19,21} use
 Q8_0 attn_v and Q6_K ffn_down, the other 12 layers Q5_0 attn_v and Q4_K
 ffn_down; attn_q/k/output and ffn_gate/up are Q5_0; token_embd is Q8_0 (tied
 with the output); norms are F32 ~ 1 + N(0, 0.02); q/k/v biases F32 ~ N(0, 0.02).
