@@ -253,6 +253,64 @@ def model_extras(world=1, rank=0):
     return decode, prefill
 
 
+def gemv_shapes():
+    """The other GEMV configurations (configs 1 and 3): device time per GEMV in a
+    CUDA graph of back-to-back launches with programmatic dependent launch,
+    over rotating weight copies larger than L2 (so every launch streams its
+    weights from HBM), fp32 x in / fp32 y out.  At these sizes (0.5-3.6 MB of
+    weights) a launch's fixed latency, not HBM bandwidth, bounds the time."""
+    import torch
+    import tmac_zynq_fpga_b200 as tm
+    from tmac_zynq_fpga_b200 import synth
+    pk, _ = peaks()
+    out = []
+    cases = [("config 1: Q5_0 attn_q", synth.Q5_0, 896, 896, 1),
+             ("config 3: Q4_K ffn_down", synth.Q4_K, 896, 4864, 1),
+             ("config 3: Q6_K ffn_down", synth.Q6_K, 896, 4864, 1),
+             ("config 3: Q4_K ffn_down", synth.Q4_K, 896, 4864, 16),
+             ("config 3: Q6_K ffn_down", synth.Q6_K, 896, 4864, 16),
+             ("ffn_gate|up: Q5_0", synth.Q5_0, 9728, 896, 1)]
+    L = tm.lib()
+    for name, qt, rows, cols, batch in cases:
+        raw = synth.make_weights(qt, rows, cols, seed=1)
+        w0 = tm.Weight(qt, rows, cols, raw)
+        ncopy = max(2, int(2 * L2_BYTES // w0.device_bytes()) + 1)
+        ws = [w0] + [tm.Weight(qt, rows, cols, raw) for _ in range(ncopy - 1)]
+        x = torch.from_numpy(synth.make_activations(cols, batch=batch, seed=1)).cuda()
+        y = torch.empty((batch, rows), device="cuda")
+        L.tmac_reserve(0, batch, cols)
+        st = torch.cuda.Stream()
+        with torch.cuda.stream(st):
+            for w in ws:
+                w.gemv(x, y, batch=batch, stream=st)
+        torch.cuda.synchronize()
+        prev = L.tmac_set_pdl(1)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=st):
+            for w in ws:
+                w.gemv(x, y, batch=batch, stream=st)
+        L.tmac_set_pdl(prev)
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 10
+        e0.record(st)
+        for _ in range(reps):
+            g.replay()
+        e1.record(st)
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) / (reps * len(ws)) * 1e3
+        blk = {synth.Q5_0: 22 / 32, synth.Q4_K: 144 / 256, synth.Q6_K: 210 / 256}[qt]
+        alg = rows * cols * blk + batch * (rows + cols) * 4
+        out.append({"case": name, "rows": rows, "cols": cols, "batch": batch, "us_per_gemv": us,
+                    "gbs": alg / us / 1e3, "frac_of_hbm": alg / us / 1e3 / pk})
+        for w in ws:
+            w.free()
+    assert tm.device_error(0) == 0
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -409,6 +467,7 @@ def main():
     decode = prefill = None
     if not args.no_model:
         decode, prefill = model_extras(world, rank)
+    shapes = gemv_shapes() if (world == 1 and not args.no_model) else None
 
     if rank == 0:
         pk, pk_kind = peaks()
@@ -438,6 +497,7 @@ def main():
             "gpu_launches": args.steps * (2 if (merge is not None and not fused) else 1),
             "clocks": clocks,
             "decode": decode,
+            "gemv_shapes": shapes,
             "prefill": prefill,
         }
         print(json.dumps(out))
