@@ -295,10 +295,11 @@ def gemv_shapes():
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         reps = 10
-        e0.record(st)
+        cur = torch.cuda.current_stream()  # replay() runs on the current stream
+        e0.record(cur)
         for _ in range(reps):
             g.replay()
-        e1.record(st)
+        e1.record(cur)
         torch.cuda.synchronize()
         us = e0.elapsed_time(e1) / (reps * len(ws)) * 1e3
         blk = {synth.Q5_0: 22 / 32, synth.Q4_K: 144 / 256, synth.Q6_K: 210 / 256}[qt]
