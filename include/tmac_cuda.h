@@ -302,6 +302,54 @@ int tmac_chain_run(void* arena_dev, size_t arena_bytes, uint32_t arena_base, con
                    uint32_t head, int max_desc, tmac_chain_stats* stats, void* stream);
 
 /*
+ * Hardware-format descriptor chain: the 32-byte descriptor the FPGA's HP FSM
+ * walks (vivado_integration/sw/tmac_baremetal.h:100-113, API.md "Descriptor
+ * Format"), a different layout from tmac_phaseb_desc above.
+ *   type 1 (Q5_0):  num_tiles (0 counts as 1) tiles of TMAC_HW_Q5_0_TILE_BYTES
+ *                   at weight_addr + i * 2696, each 4 rows x 896 columns as 56
+ *                   48-byte two-core blocks (bytes 0-21 core 0's GGUF block,
+ *                   22-43 core 1's, 44-47 zero; blocks 0-27 hold rows 0 / 2 of
+ *                   the tile, 28-55 rows 1 / 3) and four UQ8.8 norms at 2688.
+ *                   Activations: 896 int16 at act_addr (act_total_bytes >= 1792),
+ *                   read once for every tile.  Results: int64 per row,
+ *                   consecutive from result_addr (32 bytes per tile).
+ *   type 15 (CPU_OP): the FSM's passthrough mode -- act_total_bytes bytes copied
+ *                   from act_addr to result_addr (the interrupt mode, where the
+ *                   host runs an operation, is the caller's own code).
+ *   type 0 (Q8_0):  skipped and counted as unsupported: no CPU model of its
+ *                   fixed-point tile exists in the reference.
+ * Numerics of a Q5_0 tile: the reference's HP-FSM core model
+ * axi_vecmul_tile_q5_0_4x896_axilite (sim/fpga_sim.hpp:1194-1249) with float
+ * row norms recomputed from the tile's blocks (32767 / max|d*q|, as
+ * q5_preprocess_tile computes them, tmac_baremetal.cpp:497-516); the UQ8.8 norm
+ * section overflows for typical rows and is not read.  The int64 row sums are
+ * those of matmul_fpga_q5_0 on the same rows.
+ * Arena, walk limit, bounds checks, stats and stream as tmac_chain_run. */
+#define TMAC_HW_DESC_Q8_0 0
+#define TMAC_HW_DESC_Q5_0 1
+#define TMAC_HW_DESC_CPU_OP 15
+#define TMAC_HW_Q5_0_TILE_BYTES 2696 /* 56 x 48 B blocks + 4 x UQ8.8 norms */
+
+#pragma pack(push, 1)
+typedef struct tmac_hw_desc {
+    uint32_t next_addr;          /* 0x00, 0 = end of chain */
+    uint32_t weight_addr;        /* 0x04 */
+    uint32_t act_addr;           /* 0x08 */
+    uint32_t result_addr;        /* 0x0C */
+    uint16_t tensor_type;        /* 0x10, TMAC_HW_DESC_* */
+    uint16_t reserved0;          /* 0x12 */
+    uint8_t num_groups;          /* 0x14, Q8_0 column groups in bits 3..0 */
+    uint8_t reserved1;           /* 0x15 */
+    uint16_t num_tiles;          /* 0x16 */
+    uint8_t act_total_bytes[3];  /* 0x18, 24-bit little-endian */
+    uint8_t reserved3[5];        /* 0x1B */
+} tmac_hw_desc;
+#pragma pack(pop)
+
+int tmac_chain_run_hw(void* arena_dev, size_t arena_bytes, uint32_t arena_base, const void* arena_host,
+                      uint32_t head, int max_desc, tmac_chain_stats* stats, void* stream);
+
+/*
  * Phase-B dump for the Verilog testbench: the files the reference's
  * --dump-phaseb writes (phaseb_dump_files, tmac_gguf.cpp:597-708), with the
  * expected rows computed on the GPU (tmac_chain_run, one descriptor at a time).

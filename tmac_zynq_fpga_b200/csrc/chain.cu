@@ -15,9 +15,15 @@
 // The chain is walked on the host (descriptors are 32 bytes; the arena's host
 // mirror is used when the caller has one), every offset is bounds-checked, and
 // one kernel per arithmetic descriptor is enqueued in chain order.
+//
+// tmac_chain_run_hw walks the FPGA's own HP-FSM descriptor format instead
+// (tmac_hw_desc, vivado_integration/sw/tmac_baremetal.h:100-113): Q5_0 type 1
+// as 4-row tiles of 48-byte two-core blocks (axi_vecmul_tile_q5_0_4x896_axilite,
+// fpga_sim.hpp:1194-1249), CPU_OP 15 as the FSM's act -> result passthrough.
 #include "common.cuh"
 #include "dequant.cuh"
 
+#include <algorithm>
 #include <cstring>
 #include <vector>
 
@@ -85,6 +91,61 @@ __global__ void __launch_bounds__(256) chain_q5_0_kernel(const uint8_t* __restri
         }
     acc = warp_sum_i64(acc);
     if (lane == 0) st_i64_bytes(result + ((int64_t)t * kQ5Rows + i) * 8, acc);
+}
+
+// Hardware-format Q5_0 tile (tmac_hw_desc type 1): one CTA per 4-row tile,
+// warp i = row i, lane j = the row's 32-column block j.  Row i's block j is the
+// core (i >> 1) half of 48-byte block (i & 1) * 28 + j (vivado_integration/API.md,
+// "Q5_0 (tensor_type=1)"); the arithmetic is axi_vecmul_tile_q5_0_4x896_axilite
+// (fpga_sim.hpp:1194-1249) with the row norm recomputed from the row's blocks.
+__global__ void __launch_bounds__(128) chain_q5_0_hw_kernel(const uint8_t* __restrict__ weight,
+                                                            const uint8_t* __restrict__ act, uint8_t* result)
+{
+    const int t = blockIdx.x, i = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const bool has = lane < kQ5BlocksPerRow;
+    const uint8_t* blk = weight + (int64_t)t * TMAC_HW_Q5_0_TILE_BYTES +
+                         ((i & 1) * kQ5BlocksPerRow + (has ? lane : 0)) * 48 + (i >> 1) * 22;
+    float d = 0.0f;
+    uint32_t qh = 0;
+    uint8_t qs[16];
+    if (has) {
+        d = f16_bits_to_f32(ld_u16_unaligned(blk));
+        qh = ld_u32_bytes(blk + 2);
+#pragma unroll
+        for (int k = 0; k < 16; k++) qs[k] = blk[6 + k];
+    }
+    // the row norm of q5_preprocess_tile (tmac_baremetal.cpp:497-516): 32767 / max|d*q|
+    float mx = 0.0f;
+    if (has) {
+#pragma unroll
+        for (int wi = 0; wi < 32; wi++) {
+            const int ql = wi < 16 ? (qs[wi] & 0xF) : (qs[wi - 16] >> 4);
+            const int q = ((((qh >> wi) & 1) << 4) | ql) - 16;
+            mx = fmaxf(mx, fabsf(__fmul_rn(d, (float)q)));
+        }
+    }
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const float rn = (mx < 1e-10f) ? 1.0f : __fdiv_rn(32767.0f, mx);
+    long long acc = 0;
+    if (has) {
+        const uint8_t* a = act + 2 * (lane * 32);
+#pragma unroll
+        for (int wi = 0; wi < 32; wi++) {
+            const int ql = wi < 16 ? (qs[wi] & 0xF) : (qs[wi - 16] >> 4);
+            const int q = ((((qh >> wi) & 1) << 4) | ql) - 16;
+            // d * (float)q5 * row_norm, left to right, then clamp and roundf
+            const int v = clamp_round_i16(__fmul_rn(__fmul_rn(d, (float)q), rn));
+            acc += (long long)v * (long long)ld_i16_bytes(a + 2 * wi);
+        }
+    }
+    acc = warp_sum_i64(acc);
+    if (lane == 0) st_i64_bytes(result + ((int64_t)t * 4 + i) * 8, acc);
+}
+
+// Passthrough of a hardware CPU_OP descriptor: act bytes copied to result.
+__global__ void chain_copy_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, uint32_t n)
+{
+    for (uint32_t k = blockIdx.x * blockDim.x + threadIdx.x; k < n; k += gridDim.x * blockDim.x) dst[k] = src[k];
 }
 
 // One CTA per row group, one warp per row, 8 values per lane per column group.
@@ -331,5 +392,79 @@ extern "C" int tmac_phaseb_dump(const void* arena_host, size_t arena_bytes, uint
         if (in.rows) okh = okh && fwrite(in.acc.data(), 8, in.rows, fh) == in.rows;
     fclose(fh);
     if (!okh) return fail(TMAC_ERR_INVALID, std::string("short write to ") + hdr_path);
+    return TMAC_OK;
+}
+
+// Hardware-format chain (tmac_hw_desc, vivado_integration/sw/tmac_baremetal.h:100-113).
+extern "C" int tmac_chain_run_hw(void* arena_dev, size_t arena_bytes, uint32_t arena_base, const void* arena_host,
+                                 uint32_t head, int max_desc, tmac_chain_stats* stats, void* stream)
+{
+    if (!arena_dev) return fail(TMAC_ERR_INVALID, "NULL arena");
+    if (max_desc <= 0) return fail(TMAC_ERR_INVALID, "max_desc must be positive");
+    cudaStream_t s = (cudaStream_t)stream;
+    uint8_t* dev = static_cast<uint8_t*>(arena_dev);
+    const uint8_t* host = static_cast<const uint8_t*>(arena_host);
+    struct HwWalked {
+        tmac_hw_desc d;
+        int tiles;
+        uint32_t act_bytes;
+        int64_t rows;
+    };
+    std::vector<HwWalked> chain;
+    tmac_chain_stats st{};
+    for (uint32_t off = head; off != 0;) {
+        if ((int)chain.size() >= max_desc)
+            return fail(TMAC_ERR_BOUNDS, "descriptor chain longer than max_desc (cycle?)");
+        if (!in_arena(off, sizeof(tmac_hw_desc), arena_base, arena_bytes))
+            return fail(TMAC_ERR_BOUNDS, "descriptor offset outside the arena");
+        HwWalked w;
+        if (host) {
+            memcpy(&w.d, host + (off - arena_base), sizeof(w.d));
+        } else {
+            TMAC_CUDA_TRY(cudaMemcpy(&w.d, dev + (off - arena_base), sizeof(w.d), cudaMemcpyDeviceToHost));
+        }
+        const tmac_hw_desc& d = w.d;
+        w.tiles = d.num_tiles ? d.num_tiles : 1;  // 0 -> 1 (API.md: backward compatible)
+        w.act_bytes = (uint32_t)d.act_total_bytes[0] | ((uint32_t)d.act_total_bytes[1] << 8) |
+                      ((uint32_t)d.act_total_bytes[2] << 16);
+        w.rows = 0;
+        if (d.tensor_type == TMAC_HW_DESC_Q5_0) {
+            if (w.act_bytes < kQ5Cols * 2)
+                return fail(TMAC_ERR_BOUNDS, "HW Q5_0 descriptor: act_total_bytes below 896 int16 values");
+            w.rows = (int64_t)w.tiles * 4;
+            if (!in_arena(d.weight_addr, (uint64_t)w.tiles * TMAC_HW_Q5_0_TILE_BYTES, arena_base, arena_bytes) ||
+                !in_arena(d.act_addr, kQ5Cols * 2, arena_base, arena_bytes) ||
+                !in_arena(d.result_addr, (uint64_t)w.rows * 8, arena_base, arena_bytes))
+                return fail(TMAC_ERR_BOUNDS, "HW Q5_0 descriptor: weight/act/result outside the arena");
+        } else if (d.tensor_type == TMAC_HW_DESC_CPU_OP) {
+            if (!in_arena(d.act_addr, w.act_bytes, arena_base, arena_bytes) ||
+                !in_arena(d.result_addr, w.act_bytes, arena_base, arena_bytes))
+                return fail(TMAC_ERR_BOUNDS, "HW CPU_OP descriptor: act/result outside the arena");
+            const uint64_t a0 = d.act_addr, r0 = d.result_addr;
+            if (w.act_bytes && a0 < r0 + w.act_bytes && r0 < a0 + w.act_bytes && a0 != r0)
+                return fail(TMAC_ERR_BOUNDS, "HW CPU_OP descriptor: act and result ranges overlap");
+        } else {
+            st.unsupported++;
+        }
+        chain.push_back(w);
+        off = d.next_addr;
+    }
+    for (const HwWalked& w : chain) {
+        const tmac_hw_desc& d = w.d;
+        st.descriptors++;
+        st.result_rows += w.rows;
+        if (d.tensor_type == TMAC_HW_DESC_Q5_0) {
+            chain_q5_0_hw_kernel<<<w.tiles, 128, 0, s>>>(dev + (d.weight_addr - arena_base),
+                                                         dev + (d.act_addr - arena_base),
+                                                         dev + (d.result_addr - arena_base));
+            TMAC_CUDA_TRY(cudaGetLastError());
+        } else if (d.tensor_type == TMAC_HW_DESC_CPU_OP && w.act_bytes && d.act_addr != d.result_addr) {
+            const unsigned grid = std::min(148u, (w.act_bytes + 255u) / 256u);
+            chain_copy_kernel<<<grid, 256, 0, s>>>(dev + (d.act_addr - arena_base), dev + (d.result_addr - arena_base),
+                                                   w.act_bytes);
+            TMAC_CUDA_TRY(cudaGetLastError());
+        }
+    }
+    if (stats) *stats = st;
     return TMAC_OK;
 }
