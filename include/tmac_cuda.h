@@ -15,7 +15,14 @@
  * Threading: a weight handle belongs to the device it was registered on; calls
  * on it must use a stream of that device.  The library keeps one workspace per
  * device; calls from several host threads on one device must be serialised by
- * the caller (as the reference's single-threaded engine does).
+ * the caller (as the reference's single-threaded engine does).  The exception
+ * is tmac_gemv_host, which holds a per-device lock for its whole call.
+ *
+ * Device state: addresses of the library's module variables (the device error
+ * word, the tmac_gemv_static scratch) are looked up once per device and kept,
+ * as are weights and workspaces.  None of it survives cudaDeviceReset or the
+ * destruction of a device's primary context: free every handle first and do
+ * not call the library on that device afterwards in the same process.
  */
 #ifndef TMAC_CUDA_H
 #define TMAC_CUDA_H
@@ -78,6 +85,13 @@ int tmac_device_error(int device, int* code);
  * reads activations or writes outputs, so results are unchanged.  Consecutive
  * GEMVs then overlap one launch's ramp-up with the other's tail. */
 int tmac_set_pdl(int on);
+/* Limit of every bounded device wait (bulk-copy barriers, the peer exchange) on
+ * `device`, in ns; default 2 s.  After the limit a kernel records
+ * TMAC_ERR_TIMEOUT (tmac_device_error), waits -- within the limit again -- for
+ * the copies it has in flight, and returns without its results.  The
+ * counterpart of MatmulAccel::wait_done's timeout (sim/fpga_sim.hpp:232-241) and
+ * the hardware chain watchdog.  Synchronous; not during stream capture. */
+int tmac_set_wait_limit_ns(int device, uint64_t ns);
 
 /*
  * Register one weight tensor: W[rows][cols] as raw GGUF blocks (the bytes a
@@ -90,9 +104,6 @@ int tmac_set_pdl(int on);
  *   row_max_abs:   optional host float[rows] for Q8_0 NATIVE
  *                  (the `*_row_max_abs` tensor, sim/matmul_q8.cpp:22-35).
  * The handle owns its device memory until tmac_weight_free.
- * Environment: TMAC_Q8_WIDE=1 at registration puts a NATIVE Q8_0 matrix with
- * rows >= 16384 and 128 <= cols <= 896 in the tensor-core layout (identical
- * results; slower than the default CUDA-core kernel on B200 at batch 1).
  */
 int tmac_weight_register(int type, int mode, int64_t rows, int64_t cols,
                          const void* blocks, size_t n_bytes, int blocks_on_device,
@@ -220,8 +231,12 @@ int tmac_gemv_static(tmac_weight_t w, const float* x, float* y, int batch, void*
  * (e.g. an all-gather on the host), open, then per step tmac_xchg_top1 turns
  * this rank's shard key (device uint64, from tmac_gemv_top1) into the global
  * maximum key on every rank.  The kernel stores the key into every rank's
- * buffer and waits for all ranks' keys of the same step (bounded: after ~2 s it
- * records TMAC_ERR_TIMEOUT, read with tmac_device_error, and leaves the key).
+ * buffer and waits for all ranks' keys of the same step (bounded by
+ * tmac_set_wait_limit_ns: after the limit it records TMAC_ERR_TIMEOUT, read
+ * with tmac_device_error, and leaves the key; the ranks' step counts then
+ * differ, so free and re-create the exchange on every rank before going on).
+ * Ranks in one process (threads) open each other's handles too: the buffer is
+ * then reached by its device address instead of an IPC mapping.
  * All ranks must call tmac_xchg_top1 the same number of times. */
 typedef struct tmac_xchg_s* tmac_xchg_t;
 #define TMAC_XCHG_HANDLE_BYTES 64

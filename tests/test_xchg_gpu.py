@@ -62,6 +62,60 @@ def test_fused_exchange_one_rank_matches_gemv_top1(qtype, rows, cols):
         L.tmac_xchg_free(h)
 
 
+@pytest.mark.parametrize("fused", [True, False])
+def test_exchange_wait_runs_out_when_a_rank_never_publishes(fused):
+    """Rank 1 of a two-rank exchange is a second buffer in this process that no
+    kernel ever writes (a flag nothing sets).  With a 50 ms wait limit, rank 0's
+    wait gives up: the call returns, tmac_device_error reports TMAC_ERR_TIMEOUT,
+    the caller's key is left as it was, and the device still runs a normal GEMV
+    correctly afterwards (the counterpart of MatmulAccel::wait_done's timeout,
+    sim/fpga_sim.hpp:232-241)."""
+    torch = pytest.importorskip("torch")
+    import time
+    L = tm.lib()
+    L.tmac_set_wait_limit_ns.argtypes = [ctypes.c_int, ctypes.c_uint64]
+    rows, cols = 2048, 896
+    w = tm.Weight(synth.Q8_0, rows, cols, synth.make_weights(synth.Q8_0, rows, cols, seed=33))
+    h0, h1 = ctypes.c_void_p(), ctypes.c_void_p()
+    tm.check(L.tmac_xchg_create(0, 2, 0, ctypes.byref(h0)))
+    tm.check(L.tmac_xchg_create(0, 2, 1, ctypes.byref(h1)))
+    try:
+        handles = (ctypes.c_uint8 * 128)()
+        tm.check(L.tmac_xchg_ipc_handle(h0, ctypes.byref(handles, 0)))
+        tm.check(L.tmac_xchg_ipc_handle(h1, ctypes.byref(handles, 64)))
+        tm.check(L.tmac_xchg_open(h0, bytes(handles)))
+        assert tm.device_error(0) == 0
+        tm.check(L.tmac_set_wait_limit_ns(0, 50_000_000))
+        x = torch.from_numpy(synth.make_activations(cols, seed=34)).cuda()
+        y = torch.empty(rows, device="cuda")
+        sentinel = 0x1234567
+        key = torch.full((1,), sentinel, dtype=torch.int64, device="cuda")
+        t0 = time.time()
+        if fused:
+            tm.check(L.tmac_xchg_gemv_top1(h0, w.handle, x.data_ptr(), y.data_ptr(), key.data_ptr(), 0, None))
+        else:
+            w.gemv_top1(x, y, key)
+            key.fill_(sentinel)
+            tm.check(L.tmac_xchg_top1(h0, key.data_ptr(), None))
+        torch.cuda.synchronize()
+        assert time.time() - t0 < 10.0
+        assert tm.device_error(0) == -7          # TMAC_ERR_TIMEOUT
+        assert key.item() == sentinel            # the key is left as it was
+        assert tm.device_error(0) == 0           # read-and-clear
+    finally:
+        L.tmac_set_wait_limit_ns(0, 2_000_000_000)
+        L.tmac_xchg_free(h0)
+        L.tmac_xchg_free(h1)
+    # the context is still usable: a plain GEMV + top-1 is right
+    y2 = torch.empty(rows, device="cuda")
+    k2 = torch.zeros(1, dtype=torch.int64, device="cuda")
+    w.gemv_top1(x, y2, k2)
+    torch.cuda.synchronize()
+    assert tm.device_error(0) == 0
+    assert tm.top1_decode(k2.item())[1] == int(np.argmax(y2.cpu().numpy()))
+    w.free()
+
+
 def test_fused_exchange_rejects_bad_arguments():
     torch = pytest.importorskip("torch")
     L = tm.lib()

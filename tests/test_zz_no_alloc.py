@@ -22,8 +22,11 @@ def _static(w, x, y, batch, stream=None):
                                      batch, stream)
 
 
+# The last case fills the scratch exactly (batch 64 x 2048 columns = the value
+# limit, and the batch limit), through four 16-vector launches.
 @pytest.mark.parametrize("qtype,rows,cols,batch", [(synth.Q5_0, 4864, 896, 1), (synth.Q5_0, 896, 896, 16),
-                                                   (synth.Q4_K, 896, 4864, 1), (synth.Q6_K, 896, 4864, 4)])
+                                                   (synth.Q4_K, 896, 4864, 1), (synth.Q6_K, 896, 4864, 4),
+                                                   (synth.Q5_0, 896, 2048, 64)])
 def test_static_matches_gemv_two_calls(qtype, rows, cols, batch):
     torch = pytest.importorskip("torch")
     w = tm.Weight(qtype, rows, cols, synth.make_weights(qtype, rows, cols, seed=91))

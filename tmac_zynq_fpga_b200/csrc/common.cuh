@@ -160,14 +160,32 @@ TMAC_DEV uint64_t global_timer_ns()
     asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
     return t;
 }
-// Bounded wait: gives up after ~2 s, records TMAC_ERR_TIMEOUT and returns false.
+}  // namespace tmac
+
+// Limit of every bounded device wait, in ns (tmac_set_wait_limit_ns).  Without
+// relocatable device code each translation unit has its own copy, so every
+// unit that includes this header registers a setter for its copy.
+static __device__ unsigned long long g_tmac_wait_limit_ns = 2000000000ull;
+static cudaError_t tmac_set_wait_limit_this_unit(unsigned long long ns)
+{
+    return cudaMemcpyToSymbol(g_tmac_wait_limit_ns, &ns, sizeof(ns));
+}
+namespace tmac {
+int register_wait_limit_setter(cudaError_t (*set)(unsigned long long));  // registry.cu
+}
+static const int g_tmac_wait_limit_reg = tmac::register_wait_limit_setter(&tmac_set_wait_limit_this_unit);
+
+namespace tmac {
+TMAC_DEV unsigned long long wait_limit_ns() { return *(volatile const unsigned long long*)&g_tmac_wait_limit_ns; }
+// Bounded wait: gives up after the wait limit (2 s unless set), records
+// TMAC_ERR_TIMEOUT and returns false.
 TMAC_DEV bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* err)
 {
     if (mbar_try_wait(bar, parity)) return true;
     uint64_t t0 = global_timer_ns();
     for (uint32_t it = 1;; it++) {
         if (mbar_try_wait(bar, parity)) return true;
-        if ((it & 255u) == 0 && global_timer_ns() - t0 > 2000000000ull) {
+        if ((it & 255u) == 0 && global_timer_ns() - t0 > wait_limit_ns()) {
             if (err) atomicExch(err, (int)TMAC_ERR_TIMEOUT);
             return false;
         }
@@ -192,7 +210,7 @@ TMAC_DEV bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, int* err)
     uint64_t t0 = global_timer_ns();
     for (uint32_t it = 1;; it++) {
         if (mbar_try_wait_hint(bar, parity, 20000u)) return true;
-        if ((it & 15u) == 0 && global_timer_ns() - t0 > 2000000000ull) {
+        if ((it & 15u) == 0 && global_timer_ns() - t0 > wait_limit_ns()) {
             if (err) atomicExch(err, (int)TMAC_ERR_TIMEOUT);
             return false;
         }
@@ -265,17 +283,9 @@ struct tmac_weight_s {
     void* gwh = nullptr;         // tensor-core GEMM: exact int16 weights as byte planes
     void* gwl = nullptr;         // (high, low), decoded on first tmac_gemm
     void* grinv = nullptr;       // double [rows]: RN(1 / row_inv) for the GEMM epilogue
-    // Q8_0 wide layout (tall matrices, gemv_q8_wide.cu): row-major planes of
-    // biased quants [rows_pad][cols] and combined scales [rows_pad][nbp] (u16,
-    // at data + cs_off), row_norm padded to rows_pad; tmap = the quant plane's
-    // tensor map (a CUtensorMap).
     // Q8_0: running top-1 key (u64) and CTA count (u32) of the call in flight,
     // so a top-1 call needs no key reset (calls on one weight are serial).
     void* top1_scratch = nullptr;
-    int q8_wide = 0;
-    int nbp = 0;
-    int64_t rows_pad = 0, cs_off = 0;
-    alignas(64) unsigned char tmap[128] = {};
 };
 
 namespace tmac {
@@ -331,14 +341,6 @@ int gemm_planes(const GemmOperands& op, cudaStream_t s);
 // Q8_0 weight (NATIVE layout) -> its int16 deq = (q * cs) >> 8 as byte planes
 // [rows][cols] (gemv_q8_0.cu).
 int q8_planes(const tmac_weight_s* w, int8_t* wh, uint8_t* wl, cudaStream_t s);
-// Q8_0 wide layout (gemv_q8_wide.cu): chosen by register_q8_0 for tall matrices.
-bool q8_wide_eligible(int64_t rows, int64_t cols);
-// row_norm (rows_pad floats, the first rows holding row_scale) is set by the caller.
-int register_q8_wide(tmac_weight_s* w, const uint8_t* d_raw, cudaStream_t s);
-int launch_q8_wide(const tmac_weight_s* w, const float* x, float* y, int64_t* row_acc, int64_t* unit_acc, int batch,
-                   cudaStream_t s, unsigned long long* top1, int64_t index_base, const int16_t* xq, const float* xs,
-                   const XchgDev* xg);
-int q8_wide_planes(const tmac_weight_s* w, int8_t* wh, uint8_t* wl, cudaStream_t s);
 int register_int16(tmac_weight_s* w, const uint8_t* d_raw, cudaStream_t s);
 int launch_int16(const tmac_weight_s* w, const float* x, float* y, int64_t* row_acc, int64_t* unit_acc,
                  int batch, cudaStream_t s);

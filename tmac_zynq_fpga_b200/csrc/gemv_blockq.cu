@@ -624,9 +624,19 @@ __global__ void __launch_bounds__(NB == 1 ? 1024 : 512) blockq_gemv_kernel(BqArg
     }
     __syncthreads();
     BQ_STAMP(2);
-    if (!mbar_wait_bounded(&bar[0], 0, a.err)) return;
+    // A wait that gives up records TMAC_ERR_TIMEOUT; before the CTA exits, the
+    // threads that issued bulk copies wait (bounded again) for those copies, so
+    // no copy lands in shared memory after the CTA is gone.
+    auto drain_and_exit = [&]() {
+        if (threadIdx.x == 0) {
+            mbar_wait_bounded(&bar[0], 0, nullptr);
+            if (a.xp_in) mbar_wait_bounded(&bar[1], 0, nullptr);
+        }
+        if (threadIdx.x == exc_thread) mbar_wait_bounded(&bar[2], 0, nullptr);
+    };
+    if (!mbar_wait_bounded(&bar[0], 0, a.err)) return drain_and_exit();
     BQ_STAMP(3);
-    if (a.xp_in && !mbar_wait_bounded(&bar[1], 0, a.err)) return;
+    if (a.xp_in && !mbar_wait_bounded(&bar[1], 0, a.err)) return drain_and_exit();
     BQ_STAMP(4);
 
     // ---- main loop.  Work items are (slot, step): Q5_0 slot = a group of 8
@@ -710,7 +720,7 @@ __global__ void __launch_bounds__(NB == 1 ? 1024 : 512) blockq_gemv_kernel(BqArg
     // them as soon as its own main-loop items are done -- unless per-unit sums
     // are wanted: the main loop stores those, so it must finish first.
     if (a.unit_acc) __syncthreads();
-    if (!mbar_wait_bounded(&bar[2], 0, a.err)) return;
+    if (!mbar_wait_bounded(&bar[2], 0, a.err)) return drain_and_exit();
     const int e0 = ep_s[0], e1 = ep_s[rows_cta];
     for (int base = e0; base < e1; base += kExcCap) {
         const int n = min(e1 - base, kExcCap);

@@ -474,16 +474,6 @@ int register_q8_0(tmac_weight_s* w, const uint8_t* d_raw, const float* d_row_max
 {
     if (w->cols % 32) return fail(TMAC_ERR_SHAPE, "Q8_0 needs cols % 32 == 0");
     const int wpb = 8;
-    if (q8_wide_eligible(w->rows, w->cols)) {
-        const int64_t rows_pad = (w->rows + 127) / 128 * 128;
-        TMAC_CUDA_TRY(cudaMalloc(&w->row_norm, (size_t)rows_pad * sizeof(float)));
-        q8_row_scale_kernel<<<(unsigned)((w->rows + wpb - 1) / wpb), wpb * 32, 0, s>>>(d_raw, w->rows, w->cols,
-                                                                                       d_row_max_abs, w->row_norm);
-        TMAC_CUDA_TRY(cudaGetLastError());
-        TMAC_CUDA_TRY(cudaMalloc(&w->top1_scratch, 16));
-        TMAC_CUDA_TRY(cudaMemsetAsync(w->top1_scratch, 0, 16, s));
-        return register_q8_wide(w, d_raw, s);
-    }
     Q8Layout L = q8_layout(w->rows, w->cols);
     w->tiles = L.T;
     w->groups = L.groups;
@@ -505,7 +495,6 @@ int register_q8_0(tmac_weight_s* w, const uint8_t* d_raw, const float* d_row_max
 
 int q8_planes(const tmac_weight_s* w, int8_t* wh, uint8_t* wl, cudaStream_t s)
 {
-    if (w->q8_wide) return q8_wide_planes(w, wh, wl, s);
     if (w->cols % 16) return fail(TMAC_ERR_SHAPE, "q8_planes: cols must be a multiple of 16");
     const Q8Layout L = q8_layout(w->rows, w->cols);
     const int64_t n = w->rows * (w->cols / 16);
@@ -518,7 +507,6 @@ int launch_q8_0(const tmac_weight_s* w, const float* x, float* y, int64_t* row_a
                 cudaStream_t s, unsigned long long* top1, int64_t index_base, const int16_t* xq, const float* xs,
                 const XchgDev* xg)
 {
-    if (w->q8_wide) return launch_q8_wide(w, x, y, row_acc, unit_acc, batch, s, top1, index_base, xq, xs, xg);
     if (xg && (batch != 1 || !top1)) return fail(TMAC_ERR_SHAPE, "the fused exchange takes batch 1 and a key");
     Q8Layout L = q8_layout(w->rows, w->cols);
     const size_t smem = q8_smem_bytes(L);

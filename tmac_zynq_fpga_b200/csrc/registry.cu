@@ -22,6 +22,7 @@ thread_local std::string g_last_error;
 __device__ int g_device_error;  // one word per device (module global)
 
 std::mutex g_dev_mutex;
+std::vector<cudaError_t (*)(unsigned long long)>& wait_limit_setters();
 std::vector<int*> g_err_ptr;    // per device: address of g_device_error
 std::vector<int> g_sms;
 }  // namespace
@@ -217,6 +218,12 @@ int static_scratch(int device, int16_t** xq, float** xs)
     return TMAC_OK;
 }
 
+std::vector<cudaError_t (*)(unsigned long long)>& wait_limit_setters()
+{
+    static std::vector<cudaError_t (*)(unsigned long long)> v;
+    return v;
+}
+
 void free_weight(tmac_weight_s* w)
 {
     if (!w) return;
@@ -233,6 +240,15 @@ void free_weight(tmac_weight_s* w)
 }
 
 }  // namespace
+
+int register_wait_limit_setter(cudaError_t (*set)(unsigned long long))
+{
+    static std::mutex mu;
+    std::lock_guard<std::mutex> lk(mu);
+    wait_limit_setters().push_back(set);
+    return (int)wait_limit_setters().size();
+}
+
 }  // namespace tmac
 
 using namespace tmac;
@@ -242,6 +258,17 @@ extern "C" {
 int tmac_abi_version(void) { return TMAC_ABI_VERSION; }
 
 const char* tmac_last_error(void) { return g_last_error.c_str(); }
+
+int tmac_set_wait_limit_ns(int device, uint64_t ns)
+{
+    int rc = check_device(device);
+    if (rc) return rc;
+    if (ns == 0) return fail(TMAC_ERR_INVALID, "the wait limit must be positive");
+    DeviceGuard dg(device);
+    if (!dg.ok) return fail(TMAC_ERR_CUDA, "cudaSetDevice failed");
+    for (auto set : wait_limit_setters()) TMAC_CUDA_TRY(set((unsigned long long)ns));
+    return TMAC_OK;
+}
 
 int tmac_set_pdl(int on)
 {
@@ -494,6 +521,10 @@ int tmac_gemv_host(tmac_weight_t w, const float* x_host, float* y_host, int batc
     if (!x_host || !y_host) return fail(TMAC_ERR_INVALID, "NULL x or y");
     if (batch <= 0) return fail(TMAC_ERR_SHAPE, "batch must be positive");
     DeviceGuard dg(w->device);
+    // The device's staging buffers belong to one call at a time, from the
+    // lookup (which may grow them) to the final synchronisation.
+    static std::mutex host_mu[64];
+    std::lock_guard<std::mutex> hold(host_mu[w->device & 63]);
     const size_t xb = (size_t)batch * w->cols * sizeof(float), yb = (size_t)batch * w->rows * sizeof(float);
     float *dx = nullptr, *dy = nullptr;
     rc = staging(w->device, xb, yb, &dx, &dy);

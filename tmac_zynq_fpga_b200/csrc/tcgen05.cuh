@@ -1,5 +1,5 @@
 // tcgen05.cuh -- the 5th-generation tensor-core and TMA building blocks shared
-// by the Q8_0 logits GEMV (gemv_q8_wide.cu) and the batched GEMM (gemm_tc.cu):
+// by the batched GEMM (gemm_tc.cu) and the int8 tensor peak probe:
 // tensor-map loads, shared-memory matrix descriptors (K-major, 128-byte
 // swizzle), kind::i8 MMAs with TMEM accumulators, commits and TMEM loads.
 #pragma once

@@ -14,10 +14,16 @@
 // most one step ahead of another (it cannot finish step s + 1 before every rank
 // has published s + 1, which each does only after reading step s), so the other
 // half is never overwritten while it is still being read.  Every wait is
-// bounded (~2 s): on expiry the kernel records TMAC_ERR_TIMEOUT and returns.
+// bounded (tmac_set_wait_limit_ns, 2 s by default): on expiry the kernel records
+// TMAC_ERR_TIMEOUT, leaves the key as it was and returns.  The step counters of
+// the ranks then no longer agree, so an exchange that timed out is freed and
+// created again on every rank before the next step.
 #include "xchg.cuh"
 
 #include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
 
 namespace tmac {
 
@@ -37,6 +43,21 @@ XchgDev xchg_dev(const tmac_xchg_s* x)
 namespace {
 
 constexpr int kMaxRanks = 64;
+
+// Exchange buffers created in this process, by their IPC handle: a rank whose
+// peer lives in the same process (ranks driven by threads of one process)
+// reaches that buffer through its device address -- CUDA cannot open an IPC
+// handle in the process that exported it.
+struct LocalBuf {
+    int device;
+    uint64_t* buf;
+};
+std::mutex g_local_mu;
+std::map<std::string, LocalBuf>& local_bufs()
+{
+    static std::map<std::string, LocalBuf> m;
+    return m;
+}
 
 // One warp per 32 ranks; thread r publishes to rank r and reads rank r's slot.
 __global__ void xchg_top1_kernel(unsigned long long* key, XchgDev x, int* err)
@@ -105,6 +126,7 @@ int tmac_xchg_create(int device, int world, int rank, tmac_xchg_t* out)
         return cuda_fail(e, "tmac_xchg_create");
     }
     x->peer.assign(world, nullptr);
+    x->ipc_mapped.assign(world, 0);
     x->peer[rank] = x->buf;
     *out = x;
     return TMAC_OK;
@@ -117,6 +139,8 @@ int tmac_xchg_ipc_handle(tmac_xchg_t x, void* handle)
     cudaIpcMemHandle_t h;
     TMAC_CUDA_TRY(cudaIpcGetMemHandle(&h, x->buf));
     memcpy(handle, &h, sizeof(h));
+    std::lock_guard<std::mutex> lk(g_local_mu);
+    local_bufs()[std::string((const char*)&h, sizeof(h))] = LocalBuf{x->device, x->buf};
     return TMAC_OK;
 }
 
@@ -128,9 +152,26 @@ int tmac_xchg_open(tmac_xchg_t x, const void* handles)
         if (r == x->rank) continue;
         cudaIpcMemHandle_t h;
         memcpy(&h, (const uint8_t*)handles + (size_t)r * TMAC_XCHG_HANDLE_BYTES, sizeof(h));
+        LocalBuf local{-1, nullptr};
+        {
+            std::lock_guard<std::mutex> lk(g_local_mu);
+            auto it = local_bufs().find(std::string((const char*)&h, sizeof(h)));
+            if (it != local_bufs().end()) local = it->second;
+        }
+        if (local.buf) {  // same process: the device address, with peer access across devices
+            if (local.device != x->device) {
+                const cudaError_t e = cudaDeviceEnablePeerAccess(local.device, 0);
+                if (e != cudaSuccess && e != cudaErrorPeerAccessAlreadyEnabled) return cuda_fail(e, "peer access");
+                cudaGetLastError();
+            }
+            x->peer[r] = local.buf;
+            x->ipc_mapped[r] = 0;
+            continue;
+        }
         void* p = nullptr;
         TMAC_CUDA_TRY(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
         x->peer[r] = static_cast<uint64_t*>(p);
+        x->ipc_mapped[r] = 1;
     }
     TMAC_CUDA_TRY(cudaMemcpy(x->peer_dev, x->peer.data(), x->world * sizeof(uint64_t*), cudaMemcpyHostToDevice));
     return TMAC_OK;
@@ -172,7 +213,12 @@ int tmac_xchg_free(tmac_xchg_t x)
     if (!x) return TMAC_OK;
     DeviceGuard dg(x->device);
     for (int r = 0; r < x->world; r++)
-        if (r != x->rank && x->peer[r]) cudaIpcCloseMemHandle(x->peer[r]);
+        if (r != x->rank && x->peer[r] && x->ipc_mapped[r]) cudaIpcCloseMemHandle(x->peer[r]);
+    {
+        std::lock_guard<std::mutex> lk(g_local_mu);
+        for (auto it = local_bufs().begin(); it != local_bufs().end();)
+            it = (it->second.buf == x->buf) ? local_bufs().erase(it) : std::next(it);
+    }
     cudaFree(x->peer_dev);
     cudaFree(x->partial);
     cudaFree(x->step);

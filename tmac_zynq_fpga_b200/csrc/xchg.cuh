@@ -21,6 +21,7 @@ struct tmac_xchg_s {
     unsigned long long* partial = nullptr;  // fused GEMV: running key of this rank's shard
     unsigned* counter = nullptr;            // fused GEMV: CTAs finished
     std::vector<uint64_t*> peer;       // every rank's buffer as mapped here (own = buf)
+    std::vector<char> ipc_mapped;      // peer[r] came from cudaIpcOpenMemHandle
     uint64_t** peer_dev = nullptr;     // the same table on the device
 };
 
@@ -55,7 +56,7 @@ TMAC_DEV void xchg_publish(const XchgDev& x, int t, uint64_t step, unsigned long
     st_release_sys(dst + 2 * x.world + half * x.world + x.rank, step);
 }
 
-// Rank t's key of this step from the own buffer; false after ~2 s.
+// Rank t's key of this step from the own buffer; false after the wait limit.
 TMAC_DEV bool xchg_read(const XchgDev& x, int t, uint64_t step, unsigned long long* k)
 {
     const int half = (int)(step & 1);
@@ -64,7 +65,7 @@ TMAC_DEV bool xchg_read(const XchgDev& x, int t, uint64_t step, unsigned long lo
         const uint64_t t0 = global_timer_ns();
         for (uint32_t it = 1;; it++) {
             if (ld_acquire_sys(tag) == step) break;
-            if ((it & 255u) == 0 && global_timer_ns() - t0 > 2000000000ull) return false;
+            if ((it & 255u) == 0 && global_timer_ns() - t0 > wait_limit_ns()) return false;
         }
     }
     *k = x.own[half * x.world + t];

@@ -15,8 +15,9 @@
 #include <cstdint>
 #include <cstdio>
 #include <cstdlib>
+#include <map>
 #include <mutex>
-#include <unordered_map>
+#include <utility>
 
 struct Tensor {
     char name[128];
@@ -29,7 +30,9 @@ struct Tensor {
 namespace {
 
 std::mutex g_mu;
-std::unordered_map<const void*, tmac_weight_t> g_cache[3];  // by TMAC_MODE_*
+// Registered weights by (tensor, row_max_abs table), one map per TMAC_MODE_*:
+// a Q8_0 tensor called with another row_max_abs table gets its own registration.
+std::map<std::pair<const void*, const void*>, tmac_weight_t> g_cache[3];
 
 [[noreturn]] void die(const char* what)
 {
@@ -37,16 +40,24 @@ std::unordered_map<const void*, tmac_weight_t> g_cache[3];  // by TMAC_MODE_*
     abort();
 }
 
-tmac_weight_t weight_for(const Tensor* A, int mode, const float* row_max_abs = nullptr)
+tmac_weight_t weight_for(const Tensor* A, int rows, int cols, int mode, const float* row_max_abs = nullptr)
 {
+    // y holds A->rows values in every reference call site; a partial call
+    // would make tmac_gemv_host write past the caller's y
+    if ((uint64_t)rows != A->rows || (uint64_t)cols != A->cols) {
+        fprintf(stderr, "[TMAC] %s: rows x cols %d x %d differ from the tensor's %llu x %llu\n", A->name, rows, cols,
+                (unsigned long long)A->rows, (unsigned long long)A->cols);
+        abort();
+    }
     std::lock_guard<std::mutex> lk(g_mu);
-    auto it = g_cache[mode].find(A);
+    const auto key = std::make_pair((const void*)A, (const void*)row_max_abs);
+    auto it = g_cache[mode].find(key);
     if (it != g_cache[mode].end()) return it->second;
     tmac_weight_t w = nullptr;
     if (tmac_weight_register((int)A->type, mode, (int64_t)A->rows, (int64_t)A->cols, A->data, (size_t)A->n_bytes,
                              /*blocks_on_device=*/0, row_max_abs, /*device=*/0, &w) != TMAC_OK)
         die(A->name);
-    return g_cache[mode][A] = w;
+    return g_cache[mode][key] = w;
 }
 
 void run(tmac_weight_t w, const float* x, float* y)
@@ -56,23 +67,23 @@ void run(tmac_weight_t w, const float* x, float* y)
 
 }  // namespace
 
-void matmul_fpga_int16(const Tensor* A, const float* x, float* y, int, int)
+void matmul_fpga_int16(const Tensor* A, const float* x, float* y, int rows, int cols)
 {
-    run(weight_for(A, TMAC_MODE_INT16), x, y);
+    run(weight_for(A, rows, cols, TMAC_MODE_INT16), x, y);
 }
-void matmul_fpga_q8(const Tensor* A, const float* x, float* y, int, int, const float* row_max_abs)
+void matmul_fpga_q8(const Tensor* A, const float* x, float* y, int rows, int cols, const float* row_max_abs)
 {
-    run(weight_for(A, TMAC_MODE_NATIVE, row_max_abs), x, y);
+    run(weight_for(A, rows, cols, TMAC_MODE_NATIVE, row_max_abs), x, y);
 }
-void matmul_fpga_q4_k(const Tensor* A, const float* x, float* y, int, int)
+void matmul_fpga_q4_k(const Tensor* A, const float* x, float* y, int rows, int cols)
 {
-    run(weight_for(A, TMAC_MODE_NATIVE), x, y);
+    run(weight_for(A, rows, cols, TMAC_MODE_NATIVE), x, y);
 }
-void matmul_fpga_q5_0(const Tensor* A, const float* x, float* y, int, int)
+void matmul_fpga_q5_0(const Tensor* A, const float* x, float* y, int rows, int cols)
 {
-    run(weight_for(A, TMAC_MODE_NATIVE), x, y);
+    run(weight_for(A, rows, cols, TMAC_MODE_NATIVE), x, y);
 }
-void matmul_fpga_q6_k(const Tensor* A, const float* x, float* y, int, int)
+void matmul_fpga_q6_k(const Tensor* A, const float* x, float* y, int rows, int cols)
 {
-    run(weight_for(A, TMAC_MODE_NATIVE), x, y);
+    run(weight_for(A, rows, cols, TMAC_MODE_NATIVE), x, y);
 }
