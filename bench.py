@@ -38,13 +38,74 @@ VOCAB, HIDDEN = 151936, 896
 Q8_BLOCK_BYTES = 34
 METRIC = json.load(open(os.path.join(ROOT, "BASELINE.json")))["metric"]
 UNIT = "GB/s"
-WORKLOAD = "Q8_0 tied-embedding logits GEMV 151936x896 + argmax, batch 1 (BASELINE config 2)"
+WORKLOAD = "Q8_0 tied-embedding logits GEMV 151936x896 + argmax, batch 1"
 L2_BYTES = 126 * 1024 * 1024
 
 
 def alg_bytes(rows, cols=HIDDEN):
     """Algorithmic bytes of one GEMV: GGUF weight blocks + fp32 x + fp32 y."""
     return rows * (cols // 32) * Q8_BLOCK_BYTES + cols * 4 + rows * 4
+
+
+LAYER_BYTES = 246930432    # GGUF weight bytes of the 24 layers (12 Q8_0/Q6_K + 12 Q5_0/Q4_K mixes)
+LOGITS_BYTES = 144643072   # the tied Q8_0 token_embd, 151936 x 896
+MACS_PER_TOKEN = 357826560  # int16 multiply-accumulates of the 24 layers' projections per token
+
+
+def decode_bytes(n_prompt, n_gen):
+    """Algorithmic HBM bytes of one generate call: every forward streams the
+    layer weights, every greedy step the logits weights, and attention at
+    position p reads 24 layers x (k, v) x 128 floats x (p + 1)."""
+    fwd = n_prompt + n_gen
+    return fwd * LAYER_BYTES + n_gen * LOGITS_BYTES + 24576 * fwd * (fwd + 1) // 2
+
+
+_I8_PEAK = None
+
+
+def probe_i8_peak():
+    """Dense int8 tensor rate of this GPU in TOPS (tmac_probe_mma_i8), best of 3."""
+    global _I8_PEAK
+    if _I8_PEAK is None:
+        import ctypes
+        import tmac_zynq_fpga_b200 as tm
+        L = tm.lib()
+        L.tmac_probe_mma_i8.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_double)]
+        best = 0.0
+        for _ in range(3):
+            v = ctypes.c_double(0.0)
+            tm.check(L.tmac_probe_mma_i8(0, 20000, ctypes.byref(v)))
+            best = max(best, v.value)
+        _I8_PEAK = best
+    return _I8_PEAK
+
+
+def gemm_roofline(i8_peak):
+    """The prefill's largest GEMM alone: gate|up (9728 x 896 Q5_0) on 32768
+    activation rows through tmac_gemm, CUDA events over 5 launches."""
+    import torch
+    import tmac_zynq_fpga_b200 as tm
+    from tmac_zynq_fpga_b200 import synth
+    rows, cols, m = 9728, 896, 32768
+    w = tm.Weight(synth.Q5_0, rows, cols, synth.make_weights(synth.Q5_0, rows, cols, seed=5))
+    x = torch.randn((m, cols), device="cuda")
+    y = torch.empty((m, rows), device="cuda")
+    for _ in range(2):
+        w.gemm(x, y, m)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 5
+    cur = torch.cuda.current_stream()
+    e0.record(cur)
+    for _ in range(reps):
+        w.gemm(x, y, m)
+    e1.record(cur)
+    torch.cuda.synchronize()
+    dt = e0.elapsed_time(e1) / reps * 1e-3
+    w.free()
+    ops = 8.0 * rows * cols * m
+    return {"case": "gate|up 9728x896 Q5_0, M=32768 (tmac_gemm: row quantisation + gemm_i8x4_kernel)",
+            "ms": dt * 1e3, "achieved": ops / dt / 1e12, "frac": ops / dt / 1e12 / i8_peak}
 
 
 def peaks():
@@ -125,7 +186,9 @@ class ClockSampler:
 
 # ------------------------------------------------------------------ reference
 def _ref_worker(args):
-    rows0, rows1, reps = args
+    rows0, rows1, reps, cpus = args
+    if cpus:
+        os.sched_setaffinity(0, cpus)  # the caller thread and its MatmulAccel thread
     import oracle
     from tmac_zynq_fpga_b200 import synth
     rows = rows1 - rows0
@@ -138,14 +201,16 @@ def _ref_worker(args):
     return time.perf_counter() - t
 
 
-def reference_throughput(rows_per_proc, procs, reps=1):
+def reference_throughput(rows_per_proc, procs, reps=1, pin=None):
     """The reference's matmul_fpga_q8 on `procs` host processes, each over its own
-    `rows_per_proc`-row slice of the logits matrix; returns (GB/s, seconds)."""
+    `rows_per_proc`-row slice of the logits matrix; returns (GB/s, seconds).
+    pin: per-process CPU sets (None: unpinned)."""
     import multiprocessing as mp
     ctx = mp.get_context("fork")
     with ctx.Pool(procs) as pool:
         t0 = time.perf_counter()
-        times = pool.map(_ref_worker, [(i * rows_per_proc, (i + 1) * rows_per_proc, reps) for i in range(procs)])
+        times = pool.map(_ref_worker, [(i * rows_per_proc, (i + 1) * rows_per_proc, reps,
+                                        None if pin is None else pin[i]) for i in range(procs)])
         wall = time.perf_counter() - t0
     elapsed = max(times)
     return procs * reps * alg_bytes(rows_per_proc) / elapsed / 1e9, elapsed, wall
@@ -160,40 +225,87 @@ def run_reference(args):
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libtmac_ref.so was not built "
                           "(reference sources absent when building)"}))
         return
-    cores = len(os.sched_getaffinity(0))
-    procs = max(1, cores)
+    cpus = sorted(os.sched_getaffinity(0))
+    cores = len(cpus)
+    # each process runs two busy threads (the caller and fpga_sim's MatmulAccel
+    # FSM thread, sim/fpga_sim.hpp:195-205): one process per two cores, pinned
+    procs = max(1, cores // 2)
+    pin = [set(cpus[2 * i:2 * i + 2]) for i in range(procs)]
     rows_per_proc = 4096  # ~50 ms of reference work per process per step
     vals = []
-    for _ in range(args.warmup):
-        reference_throughput(rows_per_proc, procs)
+    for _ in range(min(args.warmup, 3)):
+        reference_throughput(rows_per_proc, procs, pin=pin)
+    steps = min(args.steps, 50)
     t0 = time.perf_counter()
-    for _ in range(args.steps):
-        vals.append(reference_throughput(rows_per_proc, procs)[0])
+    for _ in range(steps):
+        vals.append(reference_throughput(rows_per_proc, procs, pin=pin)[0])
     total = time.perf_counter() - t0
     v = statistics.median(vals)
-    sample = (f"{procs} processes x {rows_per_proc} rows of the 151936x896 Q8_0 logits matrix per step "
-              f"(matmul_fpga_q8, each process = caller thread + fpga_sim MatmulAccel thread)")
+    sample = (f"{procs} processes (2 cores each: caller + fpga_sim MatmulAccel thread) x {rows_per_proc} rows "
+              f"of the 151936x896 Q8_0 logits matrix per step, median of {steps} steps (matmul_fpga_q8)")
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * total / max(args.steps, 1),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int16/int64",
         "data": "synthetic", "config": {"workload": WORKLOAD, "parallelism": f"{procs} host processes"},
-        "cpu_baseline": {"value": v, "unit": UNIT, "cores": procs, "kind": "reference", "sample": sample},
+        "cpu_baseline": {"value": v, "unit": UNIT, "cores": 2 * procs, "kind": "reference", "sample": sample},
         "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "decode": reference_decode_sample(),
     }))
+
+
+def reference_decode_sample():
+    """The reference engine's own decode (process_prompt + greedy steps of
+    sim/tmac_gguf.cpp, all four --fpga-* switches, oracle/_ref) on the same
+    seed-0 synthetic model: a 1-token prompt and 2 greedy steps, i.e. 3 forwards
+    and 2 logits GEMVs, on one process pinned to two cores.  Sampled: the full
+    8 + 64 run takes minutes of host time."""
+    import ctypes
+    import multiprocessing as mp
+    ctx = mp.get_context("fork")
+    with ctx.Pool(1) as pool:
+        return pool.apply(_ref_decode_worker)
+
+
+def _ref_decode_worker():
+    import ctypes
+    import oracle
+    from tmac_zynq_fpga_b200 import model
+    cpus = sorted(os.sched_getaffinity(0))[:2]
+    os.sched_setaffinity(0, set(cpus))
+    path = model.default_model_path(0)
+    R = oracle.ref()
+    R.ref_decode.restype = ctypes.c_int
+    R.ref_decode.argtypes = [ctypes.c_char_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                             ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+    prompt = model.prompt_tokens(8, seed=0)[:1].copy()
+    n_gen = 2
+    toks = np.zeros(n_gen, np.int32)
+    t0 = time.perf_counter()
+    n = R.ref_decode(path.encode(), prompt.ctypes.data, len(prompt), n_gen, 1, toks.ctypes.data, None, None)
+    dt = time.perf_counter() - t0
+    fwd = len(prompt) + n_gen
+    return {"tok_s": n_gen / dt, "ms_per_forward": 1000 * dt / fwd, "seconds": dt, "prompt_tokens": len(prompt),
+            "generated": int(n), "cores": len(cpus), "sampled": True,
+            "config": "reference engine (tmac_gguf.cpp process_prompt + greedy steps, all --fpga-* switches) "
+                      "on the seed-0 synthetic Qwen2-0.5B-shaped model; includes load_tmac of the model file"}
 
 
 # ------------------------------------------------------------------- ours
 def cpu_baseline_single():
-    """The reference (oracle/_ref) on one host process, bounded ~10 s sample."""
+    """The reference (oracle/_ref) on one host process pinned to two cores (its
+    caller thread and fpga_sim's MatmulAccel thread): the median of 5 runs, each
+    4 calls of matmul_fpga_q8 over a quarter of the logits matrix (~10 s)."""
     import oracle
     if not oracle.ref_available():
         return None
     rows = 37984  # a quarter of the vocabulary: ~0.45 s per call
-    gbs, el, _ = reference_throughput(rows, 1, reps=16)
-    return {"value": gbs, "unit": UNIT, "cores": 1, "kind": "reference",
-            "sample": f"16 x matmul_fpga_q8 over a {rows}x896 slice of the logits matrix, 1 process "
-                      f"(reference's own code; its fpga_sim MatmulAccel FSM thread runs beside the caller)"}
+    pin = [set(sorted(os.sched_getaffinity(0))[:2])]
+    runs = [reference_throughput(rows, 1, reps=4, pin=pin)[0] for _ in range(5)]
+    return {"value": statistics.median(runs), "unit": UNIT, "cores": 2, "kind": "reference",
+            "sample": f"median of 5 runs of 4 x matmul_fpga_q8 over a {rows}x896 slice of the logits matrix, "
+                      f"1 process pinned to 2 cores (caller + fpga_sim MatmulAccel FSM thread); "
+                      f"runs {', '.join(f'{r:.4f}' for r in runs)} GB/s"}
 
 
 def model_extras(world=1, rank=0):
@@ -220,10 +332,19 @@ def model_extras(world=1, rank=0):
         for _ in range(reps):
             toks, _ = m.generate(prompt, n)
         dt = (time.perf_counter() - t0) / reps
+        fwd = len(prompt) + n
+        dbytes = decode_bytes(len(prompt), n)
+        pk, pk_kind = peaks()
         decode = {"tok_s": n / dt, "ms_per_call": 1000 * dt, "prompt_tokens": len(prompt), "generated": n,
-                  "ms_per_forward": 1000 * dt / (len(prompt) + n),
+                  "ms_per_forward": 1000 * dt / fwd,
+                  "roofline": {"bound": "hbm", "achieved": dbytes / dt / 1e9, "peak": pk, "unit": "GB/s",
+                               "frac": dbytes / dt / 1e9 / pk, "peak_kind": f"{pk_kind} hbm_gbs (copy)",
+                               "bytes_per_call": dbytes,
+                               "bytes": f"{fwd} forwards x {LAYER_BYTES} B of layer weights + {n} x "
+                                        f"{LOGITS_BYTES} B of logits weights + KV reads 24576 B x (pos + 1)"},
                   "tokens_match_reference": bool(np.array_equal(toks, ref)),
-                  "config": "BASELINE config 4: 24 layers, mixed Q5_0/Q8_0/Q4_K/Q6_K, greedy, CUDA graphs",
+                  "config": "Qwen2-0.5B-shaped decode: 24 layers, mixed Q5_0/Q8_0/Q4_K/Q6_K, 512-slot KV, "
+                            "greedy, CUDA graphs",
                   "api": "tmac_model_generate"}
     rng = np.random.default_rng(0)
     ptoks = rng.integers(0, VOCAB, size=(64, 512)).astype(np.int32)
@@ -243,11 +364,21 @@ def model_extras(world=1, rank=0):
     else:
         allnxt = nxt2
     dt = float(dt.item())
+    i8_ops = 8 * MACS_PER_TOKEN * ptoks.size  # Mode E: 4 int8 MMAs of 2 ops per int16 multiply-accumulate
+    i8_peak = probe_i8_peak() if rank == 0 else None
     prefill = {"tok_s": ptoks.size / dt, "ms_per_call": 1000 * dt, "n_seq": len(ptoks), "len": ptoks.shape[1],
+               "roofline": None if not i8_peak else {
+                   "bound": "tensor", "achieved": i8_ops / dt / 1e12, "peak": i8_peak, "unit": "TOPS (int8)",
+                   "frac": i8_ops / dt / 1e12 / (i8_peak * world),
+                   "peak_kind": "measured on this GPU: tcgen05.mma kind::i8 M128 N256 back to back "
+                                "(tmac_probe_mma_i8)",
+                   "ops": f"8 x {MACS_PER_TOKEN} int8 ops per token (4 MMAs per int16 MAC) over all projections; "
+                          "the whole call (attention, norms, logits included) is timed",
+                   "gemm_only": gemm_roofline(i8_peak)},
                "n_gpus": world, "seq_per_gpu": s1 - s0, "scaling": "strong (fixed 64 x 512 batch)",
                "deterministic": bool(np.array_equal(nxt, nxt2)), "next_tokens_gathered": int(len(allnxt)),
-               "config": "BASELINE config 5: 64 x 512 tokens, sequence shards, exact int16 x int16 on "
-                         "tcgen05 int8 MMAs",
+               "config": "batched prefill of the same model: 64 x 512 tokens, sequence shards, exact "
+                         "int16 x int16 on tcgen05 int8 MMAs",
                "api": "tmac_model_prefill"}
     m.free()
     return decode, prefill
@@ -264,12 +395,13 @@ def gemv_shapes():
     from tmac_zynq_fpga_b200 import synth
     pk, _ = peaks()
     out = []
-    cases = [("config 1: Q5_0 attn_q", synth.Q5_0, 896, 896, 1),
-             ("config 3: Q4_K ffn_down", synth.Q4_K, 896, 4864, 1),
-             ("config 3: Q6_K ffn_down", synth.Q6_K, 896, 4864, 1),
-             ("config 3: Q4_K ffn_down", synth.Q4_K, 896, 4864, 16),
-             ("config 3: Q6_K ffn_down", synth.Q6_K, 896, 4864, 16),
-             ("ffn_gate|up: Q5_0", synth.Q5_0, 9728, 896, 1)]
+    cases = [("attn_q Q5_0", synth.Q5_0, 896, 896, 1),
+             ("ffn_down Q4_K", synth.Q4_K, 896, 4864, 1),
+             ("ffn_down Q6_K", synth.Q6_K, 896, 4864, 1),
+             ("ffn_down Q4_K", synth.Q4_K, 896, 4864, 16),
+             ("ffn_down Q6_K", synth.Q6_K, 896, 4864, 16),
+             ("ffn_gate Q5_0", synth.Q5_0, 4864, 896, 1),
+             ("ffn_gate|up Q5_0", synth.Q5_0, 9728, 896, 1)]
     L = tm.lib()
     for name, qt, rows, cols, batch in cases:
         raw = synth.make_weights(qt, rows, cols, seed=1)
@@ -308,8 +440,54 @@ def gemv_shapes():
                     "gbs": alg / us / 1e3, "frac_of_hbm": alg / us / 1e3 / pk})
         for w in ws:
             w.free()
+    out.append(hw_chain_shape(pk))
     assert tm.device_error(0) == 0
     return out
+
+
+def hw_chain_shape(pk):
+    """attn_q 896x896 Q5_0 through the FPGA's own descriptor format: one chain of
+    D hardware descriptors (type 1, num_tiles = 224 4-row tiles each), every one
+    over its own copy of the matrix so that the chain streams more than twice
+    L2 from HBM; one tmac_chain_run_hw call per chain, CUDA events around it.
+    Per descriptor: int16 x (from the arena) in, 896 int64 rows out."""
+    import torch
+    from tmac_zynq_fpga_b200 import hwchain, synth
+    rows = cols = 896
+    w = synth.make_weights(synth.Q5_0, rows, cols, seed=1)
+    xq = np.clip(np.round(synth.make_activations(cols, seed=1)[0] * 8000), -32768, 32767).astype(np.int16)
+    tiles = hwchain.pack_q5_0_tiles(w, rows).reshape(-1)
+    D = int(2 * L2_BYTES // tiles.nbytes) + 1
+    base = 0x10000000
+    act = base + 32 * D
+    wt0 = (act + 2 * cols + 255) // 256 * 256
+    stride = (tiles.nbytes + 255) // 256 * 256
+    res0 = wt0 + D * stride
+    arena = np.zeros(res0 - base + D * rows * 8, np.uint8)
+    for i in range(D):
+        nxt = base + 32 * (i + 1) if i + 1 < D else 0
+        arena[32 * i:32 * i + 32] = np.frombuffer(
+            hwchain.desc_bytes(nxt, wt0 + i * stride, act, res0 + i * rows * 8, hwchain.Q5_0, 0, rows // 4,
+                               2 * cols), np.uint8)
+        arena[wt0 - base + i * stride:wt0 - base + i * stride + tiles.nbytes] = tiles
+    arena[act - base:act - base + 2 * cols] = xq.view(np.uint8)
+    dev = torch.from_numpy(arena).cuda()
+    for _ in range(2):
+        hwchain.chain_run_hw(dev, arena.nbytes, base, base, arena_host=arena)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 5
+    cur = torch.cuda.current_stream()
+    e0.record(cur)
+    for _ in range(reps):
+        hwchain.chain_run_hw(dev, arena.nbytes, base, base, arena_host=arena, stream=cur)
+    e1.record(cur)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) / (reps * D) * 1e3
+    alg = rows * cols * 22 // 32 + cols * 2 + rows * 8
+    return {"case": "attn_q Q5_0 as one hardware descriptor (num_tiles=224) per matrix, tmac_chain_run_hw",
+            "rows": rows, "cols": cols, "batch": 1, "descriptors_per_chain": D, "us_per_gemv": us,
+            "gbs": alg / us / 1e3, "frac_of_hbm": alg / us / 1e3 / pk}
 
 
 def main():

@@ -208,6 +208,13 @@ int tmac_reserve(int device, int64_t max_batch, int64_t max_cols);
  * Device pointers; asynchronous on `stream`. */
 int tmac_gemm(tmac_weight_t w, const float* x, float* y, int64_t* row_acc, int m, void* stream);
 
+/* Measurement aid (no reference counterpart): dense int8 tensor-core rate of
+ * `device` in TOPS (2 ops per multiply-accumulate), from `iters` x 4
+ * back-to-back tcgen05.mma kind::i8 (M 128, N 256, K 32) per SM with operands
+ * resident in shared memory; one launch timed with CUDA events.  The roofline
+ * denominator of tmac_gemm / tmac_model_prefill.  Synchronous. */
+int tmac_probe_mma_i8(int device, int iters, double* tops);
+
 /* NATIVE Q5_0 / Q4_K / Q6_K GEMV that allocates nothing.  No counterpart in
  * the reference (its drivers are host code with no device memory to manage);
  * it is for callers that may not allocate device memory, e.g. code running
