@@ -15,7 +15,7 @@
 // expf/logf are evaluated as (float)exp((double)x) like glibc; any remaining
 // last-ulp difference is why decode parity is stated as identical greedy tokens
 // plus a hidden-state tolerance.
-#include "model.cuh"
+#include "decode_ops.cuh"
 
 #include <cmath>
 #include <cstdio>
@@ -123,27 +123,7 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(float* __restrict__ x, con
         sq[i] = __fmul_rn(v, v);
     }
     __syncthreads();
-    if (threadIdx.x == 0 && !w) scale = 1.0f;
-    if (threadIdx.x == 0 && w) {
-        float sum = 0.0f;
-        const float4* x4 = reinterpret_cast<const float4*>(sq);
-        int i = 0;
-        for (; i + 32 <= n; i += 32) {  // 32 values loaded ahead of the sequential adds
-            float4 f[8];
-#pragma unroll
-            for (int u = 0; u < 8; u++) f[u] = x4[i / 4 + u];
-#pragma unroll
-            for (int u = 0; u < 8; u++) {
-                sum = __fadd_rn(sum, f[u].x);
-                sum = __fadd_rn(sum, f[u].y);
-                sum = __fadd_rn(sum, f[u].z);
-                sum = __fadd_rn(sum, f[u].w);
-            }
-        }
-        for (; i < n; i++) sum = __fadd_rn(sum, sq[i]);
-        const float mean = __fdiv_rn(sum, (float)n);
-        scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, 1e-6f)));
-    }
+    if (threadIdx.x == 0) scale = w ? rms_scale(sq, n) : 1.0f;
     __syncthreads();
     float mx = 0.0f;
 #pragma unroll
@@ -168,13 +148,7 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(float* __restrict__ x, con
     for (int i = threadIdx.x; i < n; i += blockDim.x) store_xq(xq, xp, n, i, quantize_one(xsh[i], s));
 }
 
-constexpr int kAttnChunk = 128;  // K/V rows staged in shared memory at a time
-
-// One CTA per query head: q/k/v bias add (:1591-1614), RoPE on the head's q
-// and its KV head's k (:1528-1554), KV-cache append by the first query head of
-// each KV group (:1622-1623), then attention over positions 0..pos
-// (:1625-1660).  The current position's k/v come from shared memory, so the
-// append needs no ordering against the other heads.
+// One CTA of 256 threads per query head (rope_attention_head, decode_ops.cuh).
 __global__ void __launch_bounds__(256) rope_attention_kernel(
     const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
     const float* __restrict__ bq, const float* __restrict__ bk, const float* __restrict__ bv,
@@ -184,84 +158,9 @@ __global__ void __launch_bounds__(256) rope_attention_kernel(
     pdl_launch();
     pdl_wait();
     extern __shared__ float sc[];  // [nsc] scores, then weights; [nsc] exp terms; K/V staging
-    __shared__ float red_s[8];
-    __shared__ float qs[kHeadDim], ks[kHeadDim], vs[kHeadDim];
-    __shared__ float log_sum;
+    __shared__ AttnShared sh;
     if (pos_dev) pos = *pos_dev;
-    const int nsc = nscore;
-    const int h = blockIdx.x, kvh = h / (kHeads / kKvHeads);
-    const float* c = cs + (int64_t)pos * (kHeadDim / 2);
-    const float* sv = sn + (int64_t)pos * (kHeadDim / 2);
-    if (threadIdx.x < kHeadDim) {  // thread j: pair j/2 of q (j even) or of k (j odd)
-        const int j = threadIdx.x, pr = j >> 1, d = 2 * pr;
-        const bool isk = j & 1;
-        const float* vec = isk ? k + kvh * kHeadDim : q + h * kHeadDim;
-        const float* b = isk ? (bk ? bk + kvh * kHeadDim : nullptr) : (bq ? bq + h * kHeadDim : nullptr);
-        const float x0 = __fadd_rn(vec[d], b ? b[d] : 0.0f), x1 = __fadd_rn(vec[d + 1], b ? b[d + 1] : 0.0f);
-        const float y0 = __fsub_rn(__fmul_rn(x0, c[pr]), __fmul_rn(x1, sv[pr]));
-        const float y1 = __fadd_rn(__fmul_rn(x0, sv[pr]), __fmul_rn(x1, c[pr]));
-        float* dst = isk ? ks : qs;
-        dst[d] = y0;
-        dst[d + 1] = y1;
-        vs[j] = __fadd_rn(v[kvh * kHeadDim + j], bv ? bv[kvh * kHeadDim + j] : 0.0f);
-    }
-    __syncthreads();
-    if (h % (kHeads / kKvHeads) == 0 && threadIdx.x < kHeadDim) {
-        kc[(int64_t)pos * kKvDim + kvh * kHeadDim + threadIdx.x] = ks[threadIdx.x];
-        vc[(int64_t)pos * kKvDim + kvh * kHeadDim + threadIdx.x] = vs[threadIdx.x];
-    }
-    // scores: K rows of this KV head staged in shared memory, 128 positions at a
-    // time (rows padded to 65 floats), one position per thread, d in order
-    float* kv = sc + 2 * nsc;  // [kAttnChunk][kHeadDim + 1]
-    for (int c0 = 0; c0 <= pos; c0 += kAttnChunk) {
-        const int rows = min(kAttnChunk, pos + 1 - c0);
-        __syncthreads();
-        for (int i = threadIdx.x; i < rows * kHeadDim; i += blockDim.x) {
-            const int r = i / kHeadDim, d = i % kHeadDim, p = c0 + r;
-            kv[r * (kHeadDim + 1) + d] = (p == pos) ? ks[d] : kc[(int64_t)p * kKvDim + kvh * kHeadDim + d];
-        }
-        __syncthreads();
-        for (int r = threadIdx.x; r < rows; r += blockDim.x) {
-            const float* kp = kv + r * (kHeadDim + 1);
-            float sum = 0.0f;
-            for (int d = 0; d < kHeadDim; d++) sum = __fadd_rn(sum, __fmul_rn(qs[d], kp[d]));
-            sc[c0 + r] = __fdiv_rn(sum, 8.0f);  // / sqrtf(64)
-        }
-    }
-    __syncthreads();
-    // max (order-free), the exp terms in parallel, their sum in position order
-    float mx = -INFINITY;
-    for (int p = threadIdx.x; p <= pos; p += blockDim.x) mx = fmaxf(mx, sc[p]);
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    if ((threadIdx.x & 31) == 0) red_s[threadIdx.x >> 5] = mx;
-    __syncthreads();
-    mx = red_s[0];
-    for (int i = 1; i < (int)(blockDim.x >> 5); i++) mx = fmaxf(mx, red_s[i]);
-    float* ex = sc + pos + 1;
-    for (int p = threadIdx.x; p <= pos; p += blockDim.x) ex[p] = expf_ref(__fsub_rn(sc[p], mx));
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        float es = 0.0f;
-        for (int p = 0; p <= pos; p++) es = __fadd_rn(es, ex[p]);
-        log_sum = __fadd_rn(logf_ref(es), mx);
-    }
-    __syncthreads();
-    for (int p = threadIdx.x; p <= pos; p += blockDim.x) sc[p] = expf_ref(__fsub_rn(sc[p], log_sum));
-    __syncthreads();
-    // context: V rows staged the same way, positions in order
-    float a = 0.0f;
-    for (int c0 = 0; c0 <= pos; c0 += kAttnChunk) {
-        const int rows = min(kAttnChunk, pos + 1 - c0);
-        __syncthreads();
-        for (int i = threadIdx.x; i < rows * kHeadDim; i += blockDim.x) {
-            const int r = i / kHeadDim, d = i % kHeadDim, p = c0 + r;
-            kv[r * (kHeadDim + 1) + d] = (p == pos) ? vs[d] : vc[(int64_t)p * kKvDim + kvh * kHeadDim + d];
-        }
-        __syncthreads();
-        if (threadIdx.x < kHeadDim)
-            for (int r = 0; r < rows; r++) a = __fadd_rn(a, __fmul_rn(sc[c0 + r], kv[r * (kHeadDim + 1) + threadIdx.x]));
-    }
-    if (threadIdx.x < kHeadDim) ctx[h * kHeadDim + threadIdx.x] = a;
+    rope_attention_head(blockIdx.x, q, k, v, bq, bk, bv, cs, sn, pos, kc, vc, ctx, nscore, sc, sh, 1);
 }
 
 // silu(gate) * up (:459-461, :1697-1700), then the quantisation ffn_down's
@@ -276,7 +175,7 @@ __global__ void __launch_bounds__(1024) silu_mul_kernel(float* __restrict__ g, c
     float mx = 0.0f;
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
         const float x = g[i];
-        const float v = __fmul_rn(__fdiv_rn(x, __fadd_rn(1.0f, expf_ref(-x))), u[i]);
+        const float v = silu_mul(x, u[i]);
         g[i] = v;
         mx = fmaxf(mx, fabsf(v));
     }
@@ -299,7 +198,7 @@ __global__ void __launch_bounds__(256) silu_part_kernel(float* __restrict__ g, c
     __shared__ float red[8];
     const int i = blockIdx.x * 256 + threadIdx.x;
     const float x = g[i];
-    const float v = __fmul_rn(__fdiv_rn(x, __fadd_rn(1.0f, expf_ref(-x))), u[i]);
+    const float v = silu_mul(x, u[i]);
     g[i] = v;
     float mx = fabsf(v);
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
@@ -369,7 +268,7 @@ int layer(tmac_model_s* m, int l, int pos, cudaStream_t s, const int* pos_dev = 
     }
     const int nscore = pos_dev ? m->max_seq : pos + 1;
     TMAC_CUDA_TRY(launch_k(rope_attention_kernel, dim3(kHeads), dim3(256),
-                           (2 * nscore + kAttnChunk * (kHeadDim + 1)) * sizeof(float), s, (const float*)m->q,
+                           attn_scratch_bytes(nscore), s, (const float*)m->q,
                            (const float*)m->k, (const float*)m->v, vec_or_null(m, lname(l, "attn_q.bias")),
                            vec_or_null(m, lname(l, "attn_k.bias")), vec_or_null(m, lname(l, "attn_v.bias")),
                            (const float*)m->rope_c, (const float*)m->rope_s, pos, pos_dev, kc, vc, m->ctx, nscore));

@@ -1,0 +1,147 @@
+// decode_ops.cuh -- the decode step's context operations as device functions,
+// shared by the per-kernel decode engine (decode.cu) and the persistent decode
+// kernel (decode_mega.cu) so that both compute every value identically.
+// Reference: forward_layer_with_cache (sim/tmac_gguf.cpp:1559-1711), rms_norm
+// (:447-454), apply_rope (:1528-1554), attention (:1625-1660), silu (:459-461).
+#pragma once
+
+#include "model.cuh"
+
+namespace tmac {
+
+// rms_norm's scale (:447-454): 1 / sqrtf(sum / n + 1e-6) with the sum of the
+// squares sq[0..n) taken in order (sq 16-byte aligned; one thread).
+TMAC_DEV float rms_scale(const float* sq, int n)
+{
+    float sum = 0.0f;
+    const float4* x4 = reinterpret_cast<const float4*>(sq);
+    int i = 0;
+    for (; i + 32 <= n; i += 32) {  // 32 values loaded ahead of the sequential adds
+        float4 f[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) f[u] = x4[i / 4 + u];
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            sum = __fadd_rn(sum, f[u].x);
+            sum = __fadd_rn(sum, f[u].y);
+            sum = __fadd_rn(sum, f[u].z);
+            sum = __fadd_rn(sum, f[u].w);
+        }
+    }
+    for (; i < n; i++) sum = __fadd_rn(sum, sq[i]);
+    const float mean = __fdiv_rn(sum, (float)n);
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, 1e-6f)));
+}
+
+// silu(g) * u (:459-461, :1697-1700).
+TMAC_DEV float silu_mul(float g, float u) { return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf_ref(-g))), u); }
+
+constexpr int kAttnChunk = 128;   // K/V rows staged in shared memory at a time
+constexpr int kAttnThreads = 256; // threads of one head's attention
+
+struct AttnShared {
+    float red[kAttnThreads / 32];
+    float q[kHeadDim], k[kHeadDim], v[kHeadDim];
+    float log_sum;
+};
+
+// Bytes of the dynamic scratch `sc` that rope_attention_head needs for nscore
+// score slots.
+__host__ __device__ constexpr size_t attn_scratch_bytes(int nscore)
+{
+    return (2 * (size_t)nscore + kAttnChunk * (kHeadDim + 1)) * sizeof(float);
+}
+
+// Query head h, run by threads 0..255 of a CTA (they synchronise on named
+// barrier `bar`): q/k/v bias add (:1591-1614), RoPE on the head's q and its KV
+// head's k (:1528-1554), KV-cache append by the first query head of each KV
+// group (:1622-1623), then attention over positions 0..pos (:1625-1660):
+// scores q.k in d order / sqrtf(64), max, exp terms, their sum in position
+// order, log-sum-exp weights, context accumulated in position order.  The
+// current position's k/v come from shared memory, so the append needs no
+// ordering against the other heads.  `sc` holds attn_scratch_bytes(nscore).
+TMAC_DEV void rope_attention_head(int h, const float* __restrict__ q, const float* __restrict__ k,
+                                  const float* __restrict__ v, const float* __restrict__ bq,
+                                  const float* __restrict__ bk, const float* __restrict__ bv,
+                                  const float* __restrict__ cs, const float* __restrict__ sn, int pos,
+                                  float* __restrict__ kc, float* __restrict__ vc, float* __restrict__ ctx, int nscore,
+                                  float* sc, AttnShared& sh, int bar)
+{
+    const int tid = threadIdx.x;
+    const int nsc = nscore;
+    const int kvh = h / (kHeads / kKvHeads);
+    const float* c = cs + (int64_t)pos * (kHeadDim / 2);
+    const float* sv = sn + (int64_t)pos * (kHeadDim / 2);
+    if (tid < kHeadDim) {  // thread j: pair j/2 of q (j even) or of k (j odd)
+        const int j = tid, pr = j >> 1, d = 2 * pr;
+        const bool isk = j & 1;
+        const float* vec = isk ? k + kvh * kHeadDim : q + h * kHeadDim;
+        const float* b = isk ? (bk ? bk + kvh * kHeadDim : nullptr) : (bq ? bq + h * kHeadDim : nullptr);
+        const float x0 = __fadd_rn(vec[d], b ? b[d] : 0.0f), x1 = __fadd_rn(vec[d + 1], b ? b[d + 1] : 0.0f);
+        const float y0 = __fsub_rn(__fmul_rn(x0, c[pr]), __fmul_rn(x1, sv[pr]));
+        const float y1 = __fadd_rn(__fmul_rn(x0, sv[pr]), __fmul_rn(x1, c[pr]));
+        float* dst = isk ? sh.k : sh.q;
+        dst[d] = y0;
+        dst[d + 1] = y1;
+        sh.v[j] = __fadd_rn(v[kvh * kHeadDim + j], bv ? bv[kvh * kHeadDim + j] : 0.0f);
+    }
+    named_bar_sync(bar, kAttnThreads);
+    if (h % (kHeads / kKvHeads) == 0 && tid < kHeadDim) {
+        kc[(int64_t)pos * kKvDim + kvh * kHeadDim + tid] = sh.k[tid];
+        vc[(int64_t)pos * kKvDim + kvh * kHeadDim + tid] = sh.v[tid];
+    }
+    // scores: K rows of this KV head staged in shared memory, 128 positions at a
+    // time (rows padded to 65 floats), one position per thread, d in order
+    float* kv = sc + 2 * nsc;  // [kAttnChunk][kHeadDim + 1]
+    for (int c0 = 0; c0 <= pos; c0 += kAttnChunk) {
+        const int rows = min(kAttnChunk, pos + 1 - c0);
+        named_bar_sync(bar, kAttnThreads);
+        for (int i = tid; i < rows * kHeadDim; i += kAttnThreads) {
+            const int r = i / kHeadDim, d = i % kHeadDim, p = c0 + r;
+            kv[r * (kHeadDim + 1) + d] = (p == pos) ? sh.k[d] : kc[(int64_t)p * kKvDim + kvh * kHeadDim + d];
+        }
+        named_bar_sync(bar, kAttnThreads);
+        for (int r = tid; r < rows; r += kAttnThreads) {
+            const float* kp = kv + r * (kHeadDim + 1);
+            float sum = 0.0f;
+            for (int d = 0; d < kHeadDim; d++) sum = __fadd_rn(sum, __fmul_rn(sh.q[d], kp[d]));
+            sc[c0 + r] = __fdiv_rn(sum, 8.0f);  // / sqrtf(64)
+        }
+    }
+    named_bar_sync(bar, kAttnThreads);
+    // max (order-free), the exp terms in parallel, their sum in position order
+    float mx = -INFINITY;
+    for (int p = tid; p <= pos; p += kAttnThreads) mx = fmaxf(mx, sc[p]);
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((tid & 31) == 0) sh.red[tid >> 5] = mx;
+    named_bar_sync(bar, kAttnThreads);
+    mx = sh.red[0];
+    for (int i = 1; i < kAttnThreads / 32; i++) mx = fmaxf(mx, sh.red[i]);
+    float* ex = sc + pos + 1;
+    for (int p = tid; p <= pos; p += kAttnThreads) ex[p] = expf_ref(__fsub_rn(sc[p], mx));
+    named_bar_sync(bar, kAttnThreads);
+    if (tid == 0) {
+        float es = 0.0f;
+        for (int p = 0; p <= pos; p++) es = __fadd_rn(es, ex[p]);
+        sh.log_sum = __fadd_rn(logf_ref(es), mx);
+    }
+    named_bar_sync(bar, kAttnThreads);
+    for (int p = tid; p <= pos; p += kAttnThreads) sc[p] = expf_ref(__fsub_rn(sc[p], sh.log_sum));
+    named_bar_sync(bar, kAttnThreads);
+    // context: V rows staged the same way, positions in order
+    float a = 0.0f;
+    for (int c0 = 0; c0 <= pos; c0 += kAttnChunk) {
+        const int rows = min(kAttnChunk, pos + 1 - c0);
+        named_bar_sync(bar, kAttnThreads);
+        for (int i = tid; i < rows * kHeadDim; i += kAttnThreads) {
+            const int r = i / kHeadDim, d = i % kHeadDim, p = c0 + r;
+            kv[r * (kHeadDim + 1) + d] = (p == pos) ? sh.v[d] : vc[(int64_t)p * kKvDim + kvh * kHeadDim + d];
+        }
+        named_bar_sync(bar, kAttnThreads);
+        if (tid < kHeadDim)
+            for (int r = 0; r < rows; r++) a = __fadd_rn(a, __fmul_rn(sc[c0 + r], kv[r * (kHeadDim + 1) + tid]));
+    }
+    if (tid < kHeadDim) ctx[h * kHeadDim + tid] = a;
+}
+
+}  // namespace tmac
