@@ -433,6 +433,12 @@ int tmac_model_buffers(tmac_model_t m, float** hidden, float** logits, uint64_t*
  * host float[(n_gen + 1) * 896]: after the prompt and after each step. */
 int tmac_model_generate(tmac_model_t m, const int* prompt, int n_prompt, int n_gen, int* out_tokens,
                         float* out_hidden, void* stream);
+/* Which engine tmac_model_generate ran: 1 = the persistent kernel (one
+ * cooperative launch per token, every matrix on its FPGA-core path), 0 = the
+ * per-kernel engine (CUDA graphs; other switch settings, or TMAC_DECODE=graph in
+ * the environment), -1 = not decided yet (no generate call so far).  Both give
+ * identical results. */
+int tmac_model_decode_engine(tmac_model_t m);
 /* Batched prefill (no reference counterpart: the reference feeds a prompt one
  * token at a time, process_prompt, sim/tmac_gguf.cpp:1992-2023).  n_seq
  * independent sequences of len tokens (host ids, [n_seq][len]) run through all

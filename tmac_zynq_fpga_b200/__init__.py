@@ -372,7 +372,7 @@ class Model:
                         ("tmac_model_prefill", [_P, _P, ctypes.c_int, ctypes.c_int, _P, _P, _P]),
                         ("tmac_model_logits", [_P, _P]), ("tmac_model_buffers", [_P, _P, _P, _P]),
                         ("tmac_model_generate", [_P, _P, ctypes.c_int, ctypes.c_int, _P, _P, _P]),
-                        ("tmac_model_free", [_P])):
+                        ("tmac_model_decode_engine", [_P]), ("tmac_model_free", [_P])):
             getattr(L, n).restype = ctypes.c_int
             getattr(L, n).argtypes = args
         h = _P()
@@ -389,6 +389,11 @@ class Model:
         check(lib().tmac_model_generate(self.handle, prompt.ctypes.data, len(prompt), n_gen, toks.ctypes.data,
                                         None if hid is None else hid.ctypes.data, s))
         return toks, hid
+
+    def decode_engine(self):
+        """1: the last generate ran the persistent decode kernel; 0: the per-kernel
+        engine; -1: no generate yet."""
+        return lib().tmac_model_decode_engine(self.handle)
 
     def prefill(self, tokens, want_hidden=False, stream=None):
         """Batched prefill of tokens [n_seq][len]: (next greedy token per sequence,

@@ -18,6 +18,7 @@
 #include "decode_ops.cuh"
 
 #include <cmath>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <map>
@@ -543,6 +544,35 @@ int tmac_model_generate(tmac_model_t m, const int* prompt, int n_prompt, int n_g
     DeviceGuard dg(m->device);
     if (!m->stream) TMAC_CUDA_TRY(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking));
     cudaStream_t s = m->stream;
+    // The persistent kernel (decode_mega.cu) runs a whole token in one launch
+    // when every matrix is on its FPGA-core path; TMAC_DECODE=graph selects the
+    // per-kernel engine below (identical results).
+    const char* engine = getenv("TMAC_DECODE");
+    const bool want_mega = !(engine && strcmp(engine, "graph") == 0);
+    if (want_mega && m->mega_state == 0) {
+        if ((rc = mega_prepare(m, &m->mega))) return rc;
+        m->mega_state = m->mega ? 1 : -1;
+    }
+    if (want_mega && m->mega) {
+        if ((rc = tmac_model_reset(m, s))) return rc;
+        TMAC_CUDA_TRY(cudaMemsetAsync(m->key, 0, sizeof(unsigned long long), s));
+        TMAC_CUDA_TRY(cudaMemcpyAsync(m->tokens, prompt, n_prompt * sizeof(int), cudaMemcpyHostToDevice, s));
+        TMAC_CUDA_TRY(cudaMemsetAsync(m->pos_dev, 0, sizeof(int), s));
+        for (int t = 0; t < n_prompt; t++)
+            if ((rc = mega_launch(m->mega, n_prompt, s))) return rc;
+        for (int g = 0; g < n_gen; g++) {
+            if ((rc = logits_into_key(m, s))) return rc;  // xn = output_norm(hidden), left by the kernel
+            if ((rc = mega_launch(m->mega, n_prompt, s))) return rc;
+        }
+        TMAC_CUDA_TRY(cudaStreamSynchronize(s));
+        TMAC_CUDA_TRY(cudaMemcpy(out_tokens, m->tokens + n_prompt, n_gen * sizeof(int), cudaMemcpyDeviceToHost));
+        if (out_hidden)
+            TMAC_CUDA_TRY(cudaMemcpy(out_hidden, m->hidden_log + (size_t)(n_prompt - 1) * kHidden,
+                                     (size_t)(n_gen + 1) * kHidden * sizeof(float), cudaMemcpyDeviceToHost));
+        m->last_engine = 1;
+        return TMAC_OK;
+    }
+    m->last_engine = 0;
     // One graph per step kind: a prompt step (embed + 24 layers) and a greedy
     // step (output norm + logits + top-1, then embed + 24 layers).  Position
     // and tokens live in device memory, so one capture serves every position.
@@ -592,6 +622,12 @@ int tmac_model_generate(tmac_model_t m, const int* prompt, int n_prompt, int n_g
     return TMAC_OK;
 }
 
+int tmac_model_decode_engine(tmac_model_t m)
+{
+    if (!m) return -1;
+    return m->last_engine;
+}
+
 int tmac_model_free(tmac_model_t m)
 {
     if (!m) return TMAC_OK;
@@ -600,6 +636,7 @@ int tmac_model_free(tmac_model_t m)
     if (m->g_gen) cudaGraphExecDestroy(m->g_gen);
     if (m->stream) cudaStreamDestroy(m->stream);
     prefill_free(m);
+    mega_free(m->mega);
     for (auto& kv : m->mats) tmac_weight_free(kv.second);
     for (void* p : m->allocs) cudaFree(p);
     delete m;

@@ -1,0 +1,827 @@
+// decode_mega.cu -- one token of the greedy decode (embedding + the 24 layers of
+// forward_layer_with_cache, sim/tmac_gguf.cpp:1559-1711) as ONE persistent
+// kernel: one CTA per SM, launched cooperatively, every CTA resident for the
+// whole token.
+//
+// Why: the per-kernel engine (decode.cu) runs ~200 small kernels per token, and
+// each small GEMV pays a fixed ramp (first weight bytes, activation staging,
+// finalise) that dwarfs its 0.1-3 MB of HBM traffic.  Here the weight stream
+// does not wait for the activations: each CTA owns a fixed share of every
+// projection's 8-row groups and bulk-copies its share of layer l + 1 into
+// shared memory while layer l computes, so a projection phase only decodes
+// from shared memory.  Phases hand activations over through global memory and
+// per-(layer, phase) arrival counters (release / acquire at GPU scope).
+//
+// Phases of layer l (weights of phases A, C, D, E are the four shared-memory
+// slots of this CTA):
+//   A  attn_norm (every CTA with work recomputes it: in-order sum of squares,
+//      as rms_norm :447-454) -> x_q; q|k|v rows of this CTA (Q5_0 groups, or
+//      one 32-row Q8_0 attn_v group in the Q8_0 layers)
+//   B  CTA head_cta0 + h, h < 14: bias + RoPE + KV append + attention of query
+//      head h (rope_attention_head)
+//   C  ctx -> x_q; attn_output rows; hidden[r] += y[r]
+//   D  ffn_norm -> x_q; gate rows and the matching up rows; h = silu(g) * u,
+//      per-CTA max |h|
+//   E  x_q of h from the maximum of those maxima; ffn_down rows; hidden[r] += y[r]
+// then, after layer 23, CTA 0 logs the hidden state, writes output_norm(hidden)
+// for the logits GEMV, advances the position and clears the top-1 key.
+//
+// Every value is computed with the same device functions and the same
+// operation order as the per-kernel engine, so both engines give identical
+// hidden states, bit for bit (tests/test_decode_gpu.py checks it).
+//
+// Waits: every spin on an arrival counter and every bulk-copy barrier wait is
+// bounded (tmac_set_wait_limit_ns); on expiry the kernel records
+// TMAC_ERR_TIMEOUT, raises an abort flag that the other CTAs' waits see, waits
+// (bounded) for its own copies in flight and returns.
+#include "blockq_dev.cuh"
+#include "decode_ops.cuh"
+#include "q8_dev.cuh"
+
+#include <algorithm>
+#include <cstdlib>
+#include <cstring>
+#include <vector>
+
+namespace tmac {
+namespace {
+
+constexpr int kMegaThreads = 768;
+constexpr int kMegaWarps = kMegaThreads / 32;
+constexpr int kSlots = 4;  // weight slots: q|k|v, attn_output, gate|up, ffn_down
+constexpr int kMaxSeg = 6;
+constexpr int kPhases = 5;  // arrival counters per layer
+enum : uint32_t { PH_QKV = 0, PH_ATTN = 1, PH_O = 2, PH_GU = 3, PH_DOWN = 4 };
+enum : uint32_t { SK_NONE = 0, SK_Q5 = 1, SK_Q8 = 2, SK_Q4K = 3, SK_Q6K = 4 };
+constexpr size_t kMaxSmemBytes = 227 * 1024;
+
+struct MegaSeg {
+    const void* src;
+    uint32_t dst, bytes;
+};
+// What one CTA does with one weight slot in one layer: the bulk copies that fill
+// the slot (weights, then row_inv, then exception entries) and the rows they
+// hold -- up to two ranges of whole 8-row groups (gate and up), or one 32-row
+// Q8_0 group.
+struct MegaSlot {
+    MegaSeg seg[kMaxSeg];
+    uint32_t total, nseg, kind, rows;  // expect-tx bytes, copies, SK_*, local rows
+    uint32_t ri_off, exc_off, exc_n, ngate;  // ngate: local rows of range 0
+    int32_t row0[2];   // first weight row of each range
+    int32_t out0[2];   // output index of each range's first row
+};
+static_assert(sizeof(MegaSlot) % 16 == 0, "slots are bulk-copied");
+
+struct MegaLayer {
+    const float *attn_norm, *ffn_norm, *bq, *bk, *bv;
+    float *kc, *vc;
+    uint32_t expect[kPhases];  // CTAs that signal each phase
+    uint32_t pad;
+};
+
+struct MegaArgs {
+    const MegaLayer* layers;
+    const MegaSlot* slots;  // [grid][kLayers][kSlots]
+    uint32_t slot_off[kSlots];
+    uint32_t plan_off, x_off, norm_off, att_off, acc_off, misc_off, max_rows;
+    const uint8_t* emb;  // token_embd GGUF Q8_0 blocks
+    unsigned long long* key;
+    int* token_log;
+    int* tokens;
+    int* pos_dev;
+    int n_prompt;
+    float *hidden, *qkv, *ctx, *hbuf, *xn, *hidden_log;
+    const float *rope_c, *rope_s, *out_norm;
+    unsigned* counters;  // [kLayers][kPhases], then the abort flag, then partmax[grid]; zeroed per launch
+    int* abort_flag;
+    float* partmax;
+    int* err;
+    int max_seq;
+    int head_cta0;
+};
+
+struct MegaMisc {
+    uint64_t bar[kSlots];
+    uint64_t plan_bar;
+    uint32_t armed[kSlots], waited[kSlots];
+    float red[32];
+    float xs, scale;
+    int abort, token, pos;
+    int sx[32];
+    AttnShared attn;
+};
+
+// --------------------------------------------------------------- sync bits --
+TMAC_DEV uint32_t ld_acquire_gpu(const unsigned* p)
+{
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+TMAC_DEV void red_release_gpu(unsigned* p)
+{
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(p) : "memory");
+}
+
+// Thread 0: wait until *cnt >= target (bounded; false on timeout or abort).
+TMAC_DEV bool grid_wait(const unsigned* cnt, unsigned target, int* abort_g, int* err)
+{
+    if (ld_acquire_gpu(cnt) >= target) return true;
+    const uint64_t t0 = global_timer_ns();
+    for (uint32_t it = 1;; it++) {
+        if (ld_acquire_gpu(cnt) >= target) return true;
+        if ((it & 31u) == 0) {
+            if (*(volatile int*)abort_g) return false;
+            if (global_timer_ns() - t0 > wait_limit_ns()) {
+                if (err) atomicExch(err, (int)TMAC_ERR_TIMEOUT);
+                atomicExch(abort_g, 1);
+                return false;
+            }
+        }
+    }
+}
+
+// Thread 0: the copies of one slot for one layer.
+TMAC_DEV void issue_slot(const MegaSlot& sp, uint8_t* base, MegaMisc& ms, int slot)
+{
+    if (sp.kind == SK_NONE || sp.total == 0) return;
+    mbar_arrive_expect_tx(&ms.bar[slot], sp.total);
+    for (uint32_t s = 0; s < sp.nseg; s++) {
+        const uint8_t* src = static_cast<const uint8_t*>(sp.seg[s].src);
+        for (uint32_t off = 0; off < sp.seg[s].bytes; off += 32768u)
+            bulk_g2s(base + sp.seg[s].dst + off, src + off, min(32768u, sp.seg[s].bytes - off), &ms.bar[slot]);
+    }
+    ms.armed[slot]++;
+}
+
+// ---------------------------------------------------------------- compute --
+// Block-quant rows of a slot: the main loop, exceptions and finalise of
+// blockq_gemv_kernel (gemv_blockq.cu) at batch 1 over the slot's groups.
+// yv[rr] = (float)((double)acc * x_scale / (double)row_inv).
+template <int TYPE>
+TMAC_DEV void mega_blockq(const uint8_t* wsm, const MegaSlot& sp, int cols, const uint8_t* xpl, float xs,
+                          uint32_t* acc_lo, uint32_t* acc_hi, float* yv)
+{
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int64_t cpr = cols / 32, nblk = cols / Geo<TYPE>::kBlockVals;
+    const int64_t group_bytes = Geo<TYPE>::group_bytes(nblk);
+    const int rows_cta = (int)sp.rows, ng = rows_cta / 8;
+    const float* ri_s = reinterpret_cast<const float*>(wsm + sp.ri_off);
+    const int4* exc_s = reinterpret_cast<const int4*>(wsm + sp.exc_off);
+    for (int t = tid; t < rows_cta; t += kMegaThreads) acc_lo[t] = acc_hi[t] = 0;
+    __syncthreads();
+    const bool q5 = (TYPE == TMAC_TYPE_Q5_0);
+    const int slots = q5 ? ng : rows_cta;
+    const int steps = (int)(q5 ? (cpr + 3) / 4 : (nblk + 3) / 4);
+    const int items = slots * steps;
+    const int it0 = (int)((int64_t)items * warp / kMegaWarps), it1 = (int)((int64_t)items * (warp + 1) / kMegaWarps);
+    const int r_lane = q5 ? (lane & 7) : 0;
+    const int l_lane = q5 ? (lane >> 3) : lane;
+    const uint32_t wsm_a = smem_addr(wsm);
+    long long acc = 0;
+    int slot = items ? it0 / steps : 0, s = items ? it0 % steps : 0;
+    for (int it = it0; it < it1; it++) {
+        const int rr = q5 ? slot * 8 + r_lane : slot;
+        const SharedBytes G{wsm_a + (uint32_t)(rr >> 3) * (uint32_t)group_bytes};
+        const int r = rr & 7;
+        const float ri = ri_s[rr];
+        const uint32_t ch = q5 ? (uint32_t)(4 * s + l_lane) : (uint32_t)(4 * s + (lane >> 3)) * 8 + (lane & 7);
+        if (ch < cpr) {
+            Chunk c;
+            uint32_t vw[16];
+            load_chunk<TYPE>(G, r, (uint32_t)nblk, ch, c);
+            fast_values<TYPE>(c, ri, vw);
+            acc += chunk_dot(vw, xpl + ch * 32, xpl + cols + ch * 32);
+        }
+        if (++s == steps || it + 1 == it1) {
+            long long v = acc;
+            for (int o = q5 ? 8 : 1; o < 32; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            if (l_lane == 0) acc_add(&acc_lo[rr], &acc_hi[rr], v);
+            acc = 0;
+            if (s == steps) {
+                s = 0;
+                slot++;
+            }
+        }
+    }
+    // exceptions: (v - v') * x_q[col] for the entries of this slot's rows
+    const int n1 = (int)sp.ngate;
+    for (int t = tid; t < (int)sp.exc_n; t += kMegaThreads) {
+        const int4 ex = exc_s[t];
+        const int rr = (ex.x >= sp.row0[0] && ex.x < sp.row0[0] + n1) ? ex.x - sp.row0[0] : ex.x - sp.row0[1] + n1;
+        acc_add(&acc_lo[rr], &acc_hi[rr], (long long)ex.z * xq_at(xpl, cols, 0, ex.y));
+    }
+    __syncthreads();
+    for (int t = tid; t < rows_cta; t += kMegaThreads) {
+        const long long tot = (long long)(((unsigned long long)acc_hi[t] << 32) | acc_lo[t]);
+        yv[t] = (float)__ddiv_rn(__dmul_rn((double)tot, (double)xs), (double)ri_s[t]);
+    }
+    __syncthreads();
+}
+
+// One 32-row Q8_0 record (gemv_q8_0.cu layout): tile t on warp t (lane = row),
+// then the fold over tiles in order, y = (float)(y + acc * x_scale * row_scale)
+// (tmac_gguf.cpp:1075-1076).  sx: the x_q sums of every 32-column block.
+TMAC_DEV void mega_q8(const uint8_t* rec, int cols, const uint8_t* xpl, const int* sx, float xs, long long* tsum,
+                      float* yv)
+{
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    Q8Layout L;
+    L.T = cols / 64;
+    L.stages = 0;
+    L.groups = 1;
+    L.group_bytes = (int64_t)L.T * 2176 + 128;
+    for (int t = warp; t < L.T; t += kMegaWarps) {
+        uint4 xh[4], xl[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            xh[j] = reinterpret_cast<const uint4*>(xpl + t * 64)[j];
+            xl[j] = reinterpret_cast<const uint4*>(xpl + cols + t * 64)[j];
+        }
+        tsum[t * 32 + lane] = q8_tile_dot(rec, L, t, lane, xh, xl, make_int2(sx[2 * t], sx[2 * t + 1]));
+    }
+    __syncthreads();
+    if (warp == 0) {
+        const double rs = (double)reinterpret_cast<const float*>(rec + L.rs_off())[lane];
+        float yr = 0.0f;
+        for (int t = 0; t < L.T; t++) {
+            const double v = __dmul_rn(__dmul_rn((double)tsum[t * 32 + lane], (double)xs), rs);
+            yr = (float)__dadd_rn((double)yr, v);
+        }
+        yv[lane] = yr;
+    }
+    __syncthreads();
+}
+
+// rms_norm of xv[0..n) with weights w (the order of rmsnorm_kernel, decode.cu),
+// then x_q of the result as byte planes xpl[0..n) (high) / xpl[n..2n) (low) and
+// x_scale in ms.xs.  All threads.
+TMAC_DEV void mega_norm_quantize(float* xv, float* sq, const float* __restrict__ w, int n, uint8_t* xpl,
+                                 MegaMisc& ms)
+{
+    const int tid = threadIdx.x;
+    for (int i = tid; i < n; i += kMegaThreads) sq[i] = __fmul_rn(xv[i], xv[i]);
+    __syncthreads();
+    if (tid == 0) ms.scale = rms_scale(sq, n);
+    __syncthreads();
+    const float scale = ms.scale;
+    float mx = 0.0f;
+    for (int i = tid; i < n; i += kMegaThreads) {
+        const float v = __fmul_rn(__fmul_rn(xv[i], __ldg(w + i)), scale);
+        xv[i] = v;
+        mx = fmaxf(mx, fabsf(v));
+    }
+    mx = block_max(mx, ms.red, kMegaThreads);
+    const float s = x_scale_from_max(mx);
+    if (tid == 0) ms.xs = s;
+    for (int i = tid; i < n; i += kMegaThreads) {
+        const int16_t q = quantize_one(xv[i], s);
+        xpl[i] = (uint8_t)((uint16_t)q >> 8);
+        xpl[n + i] = (uint8_t)(q & 0xFF);
+    }
+    __syncthreads();
+}
+
+// x_q of v[0..n) with x_scale from max_abs (tmac_gguf.cpp:889-896).
+TMAC_DEV void mega_quantize(const float* v, int n, float max_abs, uint8_t* xpl, MegaMisc& ms)
+{
+    const float s = x_scale_from_max(max_abs);
+    if (threadIdx.x == 0) ms.xs = s;
+    for (int i = threadIdx.x; i < n; i += kMegaThreads) {
+        const int16_t q = quantize_one(__ldcg(v + i), s);
+        xpl[i] = (uint8_t)((uint16_t)q >> 8);
+        xpl[n + i] = (uint8_t)(q & 0xFF);
+    }
+    __syncthreads();
+}
+
+// x_q sums of every 32-column block (the Q8_0 dot products' correction term).
+TMAC_DEV void mega_block_sums(const uint8_t* xpl, int n, int* sx)
+{
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int j = warp; j < n / 32; j += kMegaWarps) {
+        int v = (int)(int8_t)xpl[j * 32 + lane] * 256 + (int)xpl[n + j * 32 + lane];
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (lane == 0) sx[j] = v;
+    }
+    __syncthreads();
+}
+
+__global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaArgs a)
+{
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int tid = threadIdx.x, cta = blockIdx.x;
+    MegaSlot* plans = reinterpret_cast<MegaSlot*>(smem + a.plan_off);  // [kLayers][kSlots]
+    uint8_t* xpl = smem + a.x_off;
+    float* xv = reinterpret_cast<float*>(smem + a.norm_off);
+    float* sq = xv + kHidden;
+    float* att = reinterpret_cast<float*>(smem + a.att_off);
+    uint32_t* acc_lo = reinterpret_cast<uint32_t*>(smem + a.acc_off);
+    uint32_t* acc_hi = acc_lo + a.max_rows;
+    float* yv = reinterpret_cast<float*>(acc_hi + a.max_rows);
+    long long* tsum = reinterpret_cast<long long*>(smem + a.acc_off + (((size_t)a.max_rows * 12 + 15) & ~(size_t)15));
+    MegaMisc& ms = *reinterpret_cast<MegaMisc*>(smem + a.misc_off);
+    uint8_t* slot_base[kSlots];
+    for (int s = 0; s < kSlots; s++) slot_base[s] = smem + a.slot_off[s];
+
+    // ---- set-up: this CTA's copy plans, then layer 0's weights for every slot
+    if (tid == 0) {
+        for (int s = 0; s < kSlots; s++) {
+            mbar_init(&ms.bar[s], 1);
+            ms.armed[s] = ms.waited[s] = 0;
+        }
+        mbar_init(&ms.plan_bar, 1);
+        ms.abort = 0;
+        fence_mbar_init();
+        const uint32_t pb = (uint32_t)(kLayers * kSlots * sizeof(MegaSlot));
+        mbar_arrive_expect_tx(&ms.plan_bar, pb);
+        const uint8_t* src = reinterpret_cast<const uint8_t*>(a.slots + (size_t)cta * kLayers * kSlots);
+        for (uint32_t off = 0; off < pb; off += 32768u)
+            bulk_g2s(reinterpret_cast<uint8_t*>(plans) + off, src + off, min(32768u, pb - off), &ms.plan_bar);
+        if (!mbar_wait_bounded(&ms.plan_bar, 0, a.err)) {
+            ms.abort = 1;
+            atomicExch(a.abort_flag, 1);
+        } else {
+            for (int s = 0; s < kSlots; s++) issue_slot(plans[s], slot_base[s], ms, s);
+        }
+        // token of this position: the prompt, else the greedy key of the last logits
+        const int p = *a.pos_dev;
+        int tok = p < a.n_prompt ? a.tokens[p] : -1;
+        if (tok < 0 && a.key) {
+            const unsigned long long k = *a.key;
+            tok = (int)(0x7FFFFFFFu - (uint32_t)(k & 0x7FFFFFFFu));
+        }
+        if (tok < 0 || tok >= kVocab) tok = 0;
+        ms.pos = p;
+        ms.token = tok;
+        if (cta == 0) {
+            *a.token_log = tok;
+            a.tokens[p] = tok;
+        }
+    }
+    __syncthreads();
+    const int pos = ms.pos;
+    unsigned* cnt = a.counters;
+
+    // A wait that failed anywhere ends the token: drain this CTA's copies, return.
+    auto drain = [&]() {
+        if (tid == 0)
+            for (int s = 0; s < kSlots; s++)
+                for (; ms.waited[s] < ms.armed[s]; ms.waited[s]++) mbar_wait_bounded(&ms.bar[s], ms.waited[s] & 1, nullptr);
+    };
+    // All threads: wait for this layer's copies of `slot`.
+    auto wait_slot = [&](int slot) -> bool {
+        const uint32_t par = ms.waited[slot] & 1;
+        const bool ok = mbar_wait_sleep(&ms.bar[slot], par, a.err);
+        if (!ok) ms.abort = 1;
+        __syncthreads();
+        if (tid == 0 && !ms.abort) ms.waited[slot]++;
+        const bool go = !ms.abort;
+        __syncthreads();
+        if (!go && tid == 0) atomicExch(a.abort_flag, 1);
+        return go;
+    };
+    // Thread 0 waits for a phase's arrivals; everyone learns the outcome.
+    auto wait_phase = [&](int l, int ph, unsigned target) -> bool {
+        if (tid == 0 && !grid_wait(&cnt[l * kPhases + ph], target, a.abort_flag, a.err)) ms.abort = 1;
+        __syncthreads();
+        return !ms.abort;
+    };
+    // End of a phase with a slot: arrive, then refill the slot for layer l + 1.
+    auto finish = [&](int l, int ph, int slot) {
+        __syncthreads();
+        if (tid == 0) {
+            red_release_gpu(&cnt[l * kPhases + ph]);
+            if (slot >= 0 && l + 1 < kLayers) issue_slot(plans[(l + 1) * kSlots + slot], slot_base[slot], ms, slot);
+        }
+    };
+
+    if (ms.abort) {
+        drain();
+        return;
+    }
+
+    for (int l = 0; l < kLayers; l++) {
+        const MegaLayer& L = a.layers[l];
+        // ------------------------------------------------ A: q|k|v rows
+        const MegaSlot& pa = plans[l * kSlots + 0];
+        if (pa.kind != SK_NONE) {
+            if (l == 0) {  // embedding row of the token (read_embedding / dequant_q8_0, :225-234)
+                const int tok = ms.token;
+                for (int i = tid; i < kHidden; i += kMegaThreads) {
+                    const int64_t idx = (int64_t)tok * kHidden + i;
+                    const uint8_t* b = a.emb + (idx / 32) * 34;
+                    const float v = __fmul_rn((float)(int8_t)b[2 + idx % 32], f16_bits_to_f32(ld_u16_unaligned(b)));
+                    xv[i] = v;
+                    if (cta == 0) a.hidden[i] = v;
+                }
+            } else {
+                if (!wait_phase(l - 1, PH_DOWN, __ldg(&a.layers[l - 1].expect[PH_DOWN]))) break;
+                for (int i = tid; i < kHidden; i += kMegaThreads) xv[i] = __ldcg(a.hidden + i);
+            }
+            __syncthreads();
+            mega_norm_quantize(xv, sq, L.attn_norm, kHidden, xpl, ms);
+            if (pa.kind == SK_Q8) mega_block_sums(xpl, kHidden, ms.sx);
+            if (!wait_slot(0)) break;
+            if (pa.kind == SK_Q8) mega_q8(slot_base[0], kHidden, xpl, ms.sx, ms.xs, tsum, yv);
+            else mega_blockq<TMAC_TYPE_Q5_0>(slot_base[0], pa, kHidden, xpl, ms.xs, acc_lo, acc_hi, yv);
+            for (int t = tid; t < (int)pa.rows; t += kMegaThreads) a.qkv[pa.out0[0] + t] = yv[t];
+            finish(l, PH_QKV, 0);
+        }
+        // ------------------------------------------------ B: attention of one head
+        const int h = cta - a.head_cta0;
+        if (h >= 0 && h < kHeads) {
+            if (!wait_phase(l, PH_QKV, __ldg(&L.expect[PH_QKV]))) break;
+            if (tid < kAttnThreads)
+                rope_attention_head(h, a.qkv, a.qkv + kHidden, a.qkv + kHidden + kKvDim, L.bq, L.bk, L.bv, a.rope_c,
+                                    a.rope_s, pos, L.kc, L.vc, a.ctx, a.max_seq, att, ms.attn, 1);
+            finish(l, PH_ATTN, -1);
+        }
+        // ------------------------------------------------ C: attn_output + residual
+        const MegaSlot& pc = plans[l * kSlots + 1];
+        if (pc.kind != SK_NONE) {
+            if (!wait_phase(l, PH_ATTN, kHeads)) break;
+            float mx = 0.0f;
+            for (int i = tid; i < kHidden; i += kMegaThreads) mx = fmaxf(mx, fabsf(__ldcg(a.ctx + i)));
+            mx = block_max(mx, ms.red, kMegaThreads);
+            mega_quantize(a.ctx, kHidden, mx, xpl, ms);
+            if (!wait_slot(1)) break;
+            mega_blockq<TMAC_TYPE_Q5_0>(slot_base[1], pc, kHidden, xpl, ms.xs, acc_lo, acc_hi, yv);
+            for (int t = tid; t < (int)pc.rows; t += kMegaThreads) {
+                float* hp = a.hidden + pc.out0[0] + t;
+                *hp = __fadd_rn(__ldcg(hp), yv[t]);
+            }
+            finish(l, PH_O, 1);
+        }
+        // ------------------------------------------------ D: gate|up + silu
+        const MegaSlot& pd = plans[l * kSlots + 2];
+        if (pd.kind != SK_NONE) {
+            if (!wait_phase(l, PH_O, __ldg(&L.expect[PH_O]))) break;
+            for (int i = tid; i < kHidden; i += kMegaThreads) xv[i] = __ldcg(a.hidden + i);
+            __syncthreads();
+            mega_norm_quantize(xv, sq, L.ffn_norm, kHidden, xpl, ms);
+            if (!wait_slot(2)) break;
+            mega_blockq<TMAC_TYPE_Q5_0>(slot_base[2], pd, kHidden, xpl, ms.xs, acc_lo, acc_hi, yv);
+            const int n = (int)pd.ngate;
+            float mx = 0.0f;
+            for (int t = tid; t < n; t += kMegaThreads) {
+                const float v = silu_mul(yv[t], yv[n + t]);
+                a.hbuf[pd.out0[0] + t] = v;
+                mx = fmaxf(mx, fabsf(v));
+            }
+            mx = block_max(mx, ms.red, kMegaThreads);
+            if (tid == 0) a.partmax[cta] = mx;
+            finish(l, PH_GU, 2);
+        }
+        // ------------------------------------------------ E: ffn_down + residual
+        const MegaSlot& pe = plans[l * kSlots + 3];
+        if (pe.kind != SK_NONE) {
+            if (!wait_phase(l, PH_GU, __ldg(&L.expect[PH_GU]))) break;
+            float mx = 0.0f;
+            for (int i = tid; i < (int)gridDim.x; i += kMegaThreads) mx = fmaxf(mx, __ldcg(a.partmax + i));
+            mx = block_max(mx, ms.red, kMegaThreads);
+            mega_quantize(a.hbuf, kInter, mx, xpl, ms);
+            if (!wait_slot(3)) break;
+            if (pe.kind == SK_Q6K)
+                mega_blockq<TMAC_TYPE_Q6_K>(slot_base[3], pe, kInter, xpl, ms.xs, acc_lo, acc_hi, yv);
+            else
+                mega_blockq<TMAC_TYPE_Q4_K>(slot_base[3], pe, kInter, xpl, ms.xs, acc_lo, acc_hi, yv);
+            for (int t = tid; t < (int)pe.rows; t += kMegaThreads) {
+                float* hp = a.hidden + pe.out0[0] + t;
+                *hp = __fadd_rn(__ldcg(hp), yv[t]);
+            }
+            finish(l, PH_DOWN, 3);
+        }
+    }
+    if (ms.abort) {
+        drain();
+        return;
+    }
+    // ---- end of the token (CTA 0): hidden log, output_norm for the logits GEMV,
+    // next position, key cleared for the next step's top-1
+    if (cta == 0) {
+        if (!wait_phase(kLayers - 1, PH_DOWN, __ldg(&a.layers[kLayers - 1].expect[PH_DOWN]))) {
+            drain();
+            return;
+        }
+        for (int i = tid; i < kHidden; i += kMegaThreads) {
+            const float v = __ldcg(a.hidden + i);
+            xv[i] = v;
+            a.hidden_log[(int64_t)pos * kHidden + i] = v;
+        }
+        __syncthreads();
+        if (a.out_norm) {
+            for (int i = tid; i < kHidden; i += kMegaThreads) sq[i] = __fmul_rn(xv[i], xv[i]);
+            __syncthreads();
+            if (tid == 0) ms.scale = rms_scale(sq, kHidden);
+            __syncthreads();
+        } else if (tid == 0) {
+            ms.scale = 1.0f;
+        }
+        __syncthreads();
+        for (int i = tid; i < kHidden; i += kMegaThreads)
+            a.xn[i] = a.out_norm ? __fmul_rn(__fmul_rn(xv[i], __ldg(a.out_norm + i)), ms.scale) : xv[i];
+        if (tid == 0) {
+            *a.pos_dev = pos + 1;
+            *a.key = 0;
+        }
+    }
+    drain();
+}
+
+// Contiguous share [lo, hi) of n items for part i of parts.
+inline void split(int64_t n, int parts, int i, int64_t* lo, int64_t* hi)
+{
+    *lo = n * i / parts;
+    *hi = n * (i + 1) / parts;
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------ host --
+struct MegaState {
+    MegaArgs args{};
+    size_t smem = 0;
+    int grid = 0;
+    void* dev_layers = nullptr;
+    void* dev_slots = nullptr;
+    unsigned* dev_zero = nullptr;  // counters | abort flag | partmax
+    size_t zero_bytes = 0;
+};
+
+namespace {
+
+// Adds a copy of `bytes` from src to offset *off of the slot (skipped when empty).
+void add_seg(MegaSlot& sp, const void* src, uint32_t bytes, uint32_t* off)
+{
+    if (!bytes) return;
+    sp.seg[sp.nseg].src = src;
+    sp.seg[sp.nseg].dst = *off;
+    sp.seg[sp.nseg].bytes = bytes;
+    sp.nseg++;
+    *off += bytes;
+    sp.total += bytes;
+}
+
+// A block-quant slot over up to two ranges of 8-row groups [g0, g1) of w.
+int blockq_slot(const tmac_weight_s* w, const std::vector<int>& exc_ptr, const int64_t (&g0)[2],
+                const int64_t (&g1)[2], const int32_t (&out0)[2], int nrange, MegaSlot& sp)
+{
+    sp = MegaSlot{};
+    int64_t rows = 0;
+    for (int r = 0; r < nrange; r++) rows += 8 * (g1[r] - g0[r]);
+    if (rows == 0) return TMAC_OK;
+    sp.kind = w->type == TMAC_TYPE_Q5_0 ? SK_Q5 : (w->type == TMAC_TYPE_Q6_K ? SK_Q6K : SK_Q4K);
+    sp.rows = (uint32_t)rows;
+    uint32_t off = 0;
+    for (int r = 0; r < nrange; r++)
+        add_seg(sp, w->data + g0[r] * w->group_bytes, (uint32_t)((g1[r] - g0[r]) * w->group_bytes), &off);
+    sp.ri_off = off;
+    for (int r = 0; r < nrange; r++)
+        add_seg(sp, w->row_norm + 8 * g0[r], (uint32_t)(32 * (g1[r] - g0[r])), &off);
+    sp.exc_off = off;
+    for (int r = 0; r < nrange; r++) {
+        const int64_t e0 = exc_ptr[std::min<int64_t>(8 * g0[r], w->rows)];
+        const int64_t e1 = exc_ptr[std::min<int64_t>(8 * g1[r], w->rows)];
+        add_seg(sp, static_cast<const int4*>(w->exc) + e0, (uint32_t)(16 * (e1 - e0)), &off);
+        sp.exc_n += (uint32_t)(e1 - e0);
+    }
+    for (int r = 0; r < 2; r++) {
+        sp.row0[r] = r < nrange ? (int32_t)(8 * g0[r]) : 0;
+        sp.out0[r] = r < nrange ? out0[r] : 0;
+    }
+    sp.ngate = (uint32_t)(8 * (g1[0] - g0[0]));
+    return TMAC_OK;
+}
+
+int host_exc_ptr(const tmac_weight_s* w, std::vector<int>& out)
+{
+    out.assign((size_t)w->rows + 1, 0);
+    TMAC_CUDA_TRY(cudaMemcpy(out.data(), w->exc_ptr, (w->rows + 1) * sizeof(int), cudaMemcpyDeviceToHost));
+    return TMAC_OK;
+}
+
+const tmac_weight_s* find_mat(tmac_model_s* m, const std::string& name)
+{
+    auto it = m->mats.find(name);
+    return it == m->mats.end() ? nullptr : it->second;
+}
+
+bool native_blockq(const tmac_weight_s* w, int type, int64_t rows, int64_t cols)
+{
+    if (!w || w->mode != TMAC_MODE_NATIVE || w->type != type || w->rows != rows || w->cols != cols || !w->exc ||
+        !w->exc_ptr)
+        return false;
+    int64_t gb = 0;
+    if (type == TMAC_TYPE_Q5_0) gb = Geo<TMAC_TYPE_Q5_0>::group_bytes(cols / 32);
+    else if (type == TMAC_TYPE_Q4_K) gb = Geo<TMAC_TYPE_Q4_K>::group_bytes(cols / 256);
+    else gb = Geo<TMAC_TYPE_Q6_K>::group_bytes(cols / 256);
+    return w->group_bytes == gb && w->groups == (rows + 7) / 8;
+}
+
+}  // namespace
+
+void mega_free(MegaState* st)
+{
+    if (!st) return;
+    if (st->dev_layers) cudaFree(st->dev_layers);
+    if (st->dev_slots) cudaFree(st->dev_slots);
+    if (st->dev_zero) cudaFree(st->dev_zero);
+    delete st;
+}
+
+// Builds the copy plans of every CTA; returns TMAC_OK with *out = nullptr when
+// the model cannot run on the persistent kernel (a matrix off its FPGA-core
+// path, another shape, or shared memory too small), so the caller keeps the
+// per-kernel engine.
+int mega_prepare(tmac_model_s* m, MegaState** out)
+{
+    *out = nullptr;
+    if (m->max_seq > 1024) return TMAC_OK;
+    const int G = num_sms(m->device);
+    if (G < 2 * kHeads) return TMAC_OK;
+    std::vector<MegaLayer> layers(kLayers);
+    std::vector<MegaSlot> slots((size_t)G * kLayers * kSlots);
+    uint32_t slot_bytes[kSlots] = {0, 0, 0, 0};
+    uint32_t max_rows = 32;
+    std::vector<int> ep_a, ep_o, ep_g, ep_d;
+    for (int l = 0; l < kLayers; l++) {
+        MegaLayer& L = layers[l];
+        L.attn_norm = vec_or_null(m, lname(l, "attn_norm.weight"));
+        L.ffn_norm = vec_or_null(m, lname(l, "ffn_norm.weight"));
+        L.bq = vec_or_null(m, lname(l, "attn_q.bias"));
+        L.bk = vec_or_null(m, lname(l, "attn_k.bias"));
+        L.bv = vec_or_null(m, lname(l, "attn_v.bias"));
+        L.kc = m->kcache + (int64_t)l * m->max_seq * kKvDim;
+        L.vc = m->vcache + (int64_t)l * m->max_seq * kKvDim;
+        if (!L.attn_norm || !L.ffn_norm) return TMAC_OK;
+        const tmac_weight_s* qkv = find_mat(m, lname(l, "attn_qkv"));
+        const tmac_weight_s* qk = find_mat(m, lname(l, "attn_qk"));
+        const tmac_weight_s* v8 = find_mat(m, lname(l, "attn_v.weight"));
+        const tmac_weight_s* wo = find_mat(m, lname(l, "attn_output.weight"));
+        const tmac_weight_s* gu = find_mat(m, lname(l, "ffn_gate_up"));
+        const tmac_weight_s* wd = find_mat(m, lname(l, "ffn_down.weight"));
+        const bool q5_layer = qkv != nullptr;
+        if (q5_layer) {
+            if (!native_blockq(qkv, TMAC_TYPE_Q5_0, kHidden + 2 * kKvDim, kHidden)) return TMAC_OK;
+        } else {
+            if (!native_blockq(qk, TMAC_TYPE_Q5_0, kHidden + kKvDim, kHidden)) return TMAC_OK;
+            if (!v8 || v8->mode != TMAC_MODE_NATIVE || v8->type != TMAC_TYPE_Q8_0 || v8->rows != kKvDim ||
+                v8->cols != kHidden || v8->groups != kKvDim / 32 || v8->group_bytes != (kHidden / 64) * 2176 + 128)
+                return TMAC_OK;
+        }
+        if (!native_blockq(wo, TMAC_TYPE_Q5_0, kHidden, kHidden) ||
+            !native_blockq(gu, TMAC_TYPE_Q5_0, 2 * kInter, kHidden) ||
+            !(native_blockq(wd, TMAC_TYPE_Q4_K, kHidden, kInter) || native_blockq(wd, TMAC_TYPE_Q6_K, kHidden, kInter)))
+            return TMAC_OK;
+        uint32_t expect[kPhases] = {0, (uint32_t)kHeads, 0, 0, 0};
+        int rc;
+        if ((rc = host_exc_ptr(q5_layer ? qkv : qk, ep_a)) || (rc = host_exc_ptr(wo, ep_o)) ||
+            (rc = host_exc_ptr(gu, ep_g)) || (rc = host_exc_ptr(wd, ep_d)))
+            return rc;
+        for (int c = 0; c < G; c++) {
+            MegaSlot* sp = &slots[((size_t)c * kLayers + l) * kSlots];
+            int64_t a0[2] = {0, 0}, a1[2] = {0, 0};
+            int32_t o0[2] = {0, 0};
+            // A: q|k|v rows (Q8_0 layers: q|k over the first G - 4 CTAs, the four
+            // 32-row attn_v groups on the last four)
+            if (q5_layer) {
+                split(qkv->groups, G, c, &a0[0], &a1[0]);
+                o0[0] = (int32_t)(8 * a0[0]);
+                if ((rc = blockq_slot(qkv, ep_a, a0, a1, o0, 1, sp[0]))) return rc;
+            } else if (c < G - 4) {
+                split(qk->groups, G - 4, c, &a0[0], &a1[0]);
+                o0[0] = (int32_t)(8 * a0[0]);
+                if ((rc = blockq_slot(qk, ep_a, a0, a1, o0, 1, sp[0]))) return rc;
+            } else {
+                const int gi = c - (G - 4);
+                MegaSlot& s0 = sp[0];
+                s0 = MegaSlot{};
+                s0.kind = SK_Q8;
+                s0.rows = 32;
+                uint32_t off = 0;
+                add_seg(s0, v8->data + gi * v8->group_bytes, (uint32_t)v8->group_bytes, &off);
+                s0.out0[0] = kHidden + kKvDim + 32 * gi;
+            }
+            // C: attn_output rows
+            split(wo->groups, G, c, &a0[0], &a1[0]);
+            o0[0] = (int32_t)(8 * a0[0]);
+            if ((rc = blockq_slot(wo, ep_o, a0, a1, o0, 1, sp[1]))) return rc;
+            // D: gate groups [p0, p1) with the up groups holding the same rows
+            int64_t p0, p1;
+            split(gu->groups / 2, G, c, &p0, &p1);
+            a0[0] = p0;
+            a1[0] = p1;
+            a0[1] = gu->groups / 2 + p0;
+            a1[1] = gu->groups / 2 + p1;
+            o0[0] = (int32_t)(8 * p0);
+            o0[1] = 0;
+            if ((rc = blockq_slot(gu, ep_g, a0, a1, o0, 2, sp[2]))) return rc;
+            // E: ffn_down rows
+            split(wd->groups, G, c, &a0[0], &a1[0]);
+            o0[0] = (int32_t)(8 * a0[0]);
+            if ((rc = blockq_slot(wd, ep_d, a0, a1, o0, 1, sp[3]))) return rc;
+            const uint32_t phases[kSlots] = {PH_QKV, PH_O, PH_GU, PH_DOWN};
+            for (int s = 0; s < kSlots; s++) {
+                if (sp[s].kind != SK_NONE) expect[phases[s]]++;
+                slot_bytes[s] = std::max(slot_bytes[s], (sp[s].total + 127) / 128 * 128);
+                max_rows = std::max(max_rows, sp[s].rows);
+            }
+        }
+        memcpy(L.expect, expect, sizeof(expect));
+    }
+    // shared-memory layout
+    MegaArgs a{};
+    size_t off = 0;
+    for (int s = 0; s < kSlots; s++) {
+        a.slot_off[s] = (uint32_t)off;
+        off += slot_bytes[s];
+    }
+    a.plan_off = (uint32_t)off;
+    off += (size_t)kLayers * kSlots * sizeof(MegaSlot);
+    a.x_off = (uint32_t)off;
+    off += 2 * kInter;
+    a.norm_off = (uint32_t)off;
+    off += 2 * kHidden * sizeof(float);
+    a.att_off = (uint32_t)off;
+    off += (attn_scratch_bytes(m->max_seq) + 127) / 128 * 128;
+    a.acc_off = (uint32_t)off;
+    a.max_rows = max_rows;
+    off += ((size_t)max_rows * 12 + 15) / 16 * 16 + (size_t)(kHidden / 64) * 32 * 8;
+    off = (off + 127) / 128 * 128;
+    a.misc_off = (uint32_t)off;
+    off += (sizeof(MegaMisc) + 127) / 128 * 128;
+    if (off > kMaxSmemBytes) return TMAC_OK;
+    int coop = 0;
+    TMAC_CUDA_TRY(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, m->device));
+    if (!coop) return TMAC_OK;
+    TMAC_CUDA_TRY(cudaFuncSetAttribute(decode_mega_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)off));
+    int per_sm = 0;
+    TMAC_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_mega_kernel, kMegaThreads, off));
+    if (per_sm < 1) return TMAC_OK;
+
+    MegaState* st = new MegaState();
+    st->smem = off;
+    st->grid = G;
+    st->zero_bytes = ((size_t)kLayers * kPhases + 1 + G) * sizeof(unsigned);
+    cudaError_t e = cudaMalloc(&st->dev_layers, layers.size() * sizeof(MegaLayer));
+    if (e == cudaSuccess) e = cudaMalloc(&st->dev_slots, slots.size() * sizeof(MegaSlot));
+    if (e == cudaSuccess) e = cudaMalloc(&st->dev_zero, st->zero_bytes);
+    if (e == cudaSuccess)
+        e = cudaMemcpy(st->dev_layers, layers.data(), layers.size() * sizeof(MegaLayer), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess)
+        e = cudaMemcpy(st->dev_slots, slots.data(), slots.size() * sizeof(MegaSlot), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemset(st->dev_zero, 0, st->zero_bytes);
+    if (e != cudaSuccess) {
+        mega_free(st);
+        return cuda_fail(e, "decode kernel set-up");
+    }
+    a.layers = static_cast<const MegaLayer*>(st->dev_layers);
+    a.slots = static_cast<const MegaSlot*>(st->dev_slots);
+    a.emb = m->emb_raw;
+    a.key = m->key;
+    a.token_log = m->token_log;
+    a.tokens = m->tokens;
+    a.pos_dev = m->pos_dev;
+    a.hidden = m->hidden;
+    a.qkv = m->q;
+    a.ctx = m->ctx;
+    a.hbuf = m->gate;
+    a.xn = m->xn;
+    a.hidden_log = m->hidden_log;
+    a.rope_c = m->rope_c;
+    a.rope_s = m->rope_s;
+    a.out_norm = vec_or_null(m, "output_norm.weight");
+    a.counters = st->dev_zero;
+    a.abort_flag = reinterpret_cast<int*>(st->dev_zero + kLayers * kPhases);
+    a.partmax = reinterpret_cast<float*>(st->dev_zero + kLayers * kPhases + 1);
+    a.err = device_error_word(m->device);
+    a.max_seq = m->max_seq;
+    a.head_cta0 = G - kHeads;
+    st->args = a;
+    *out = st;
+    return TMAC_OK;
+}
+
+// One token: counters cleared, then the persistent kernel (cooperative launch,
+// so every CTA is resident before any waits on another).
+int mega_launch(MegaState* st, int n_prompt, cudaStream_t s)
+{
+    TMAC_CUDA_TRY(cudaMemsetAsync(st->dev_zero, 0, st->zero_bytes, s));
+    MegaArgs a = st->args;
+    a.n_prompt = n_prompt;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(st->grid);
+    cfg.blockDim = dim3(kMegaThreads);
+    cfg.dynamicSmemBytes = st->smem;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeCooperative;
+    at[0].val.cooperative = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    TMAC_CUDA_TRY(cudaLaunchKernelEx(&cfg, decode_mega_kernel, a));
+    return TMAC_OK;
+}
+
+}  // namespace tmac

@@ -29,6 +29,7 @@ struct HostTensor {
 };
 
 struct PrefillState;  // prefill.cu
+struct MegaState;     // decode_mega.cu
 
 }  // namespace tmac
 
@@ -58,6 +59,9 @@ struct tmac_model_s {
     int graph_n_prompt = -1;
     std::vector<void*> allocs;
     tmac::PrefillState* prefill = nullptr;  // batched prefill buffers (prefill.cu)
+    tmac::MegaState* mega = nullptr;        // persistent decode kernel (decode_mega.cu)
+    int mega_state = 0;                     // 0 not tried, 1 ready, -1 not applicable
+    int last_engine = -1;                   // tmac_model_decode_engine
 };
 
 namespace tmac {
@@ -84,5 +88,9 @@ inline const float* vec_or_null(tmac_model_s* m, const std::string& name)
 }
 
 void prefill_free(tmac_model_s* m);
+// Persistent decode kernel: *out stays nullptr when the model does not qualify.
+int mega_prepare(tmac_model_s* m, MegaState** out);
+int mega_launch(MegaState* st, int n_prompt, cudaStream_t s);
+void mega_free(MegaState* st);
 
 }  // namespace tmac
