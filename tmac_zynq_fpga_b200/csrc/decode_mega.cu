@@ -98,6 +98,7 @@ struct MegaArgs {
     int* err;
     int max_seq;
     int head_cta0;
+    int emb_cta;  // a CTA with layer-0 q|k|v work: it writes the embedding to hidden
 };
 
 struct MegaMisc {
@@ -307,6 +308,28 @@ TMAC_DEV void mega_block_sums(const uint8_t* xpl, int n, int* sx)
     __syncthreads();
 }
 
+#ifdef TMAC_TRACE
+// Diagnostic build only (-DTMAC_TRACE): %globaltimer stamps of each CTA's phase
+// boundaries, read back with tmac_trace_read_mega.
+__device__ unsigned long long g_mega_trace[160][kLayers][8];
+__device__ float g_mega_dbg[4][1152];
+#define MEGA_DBG(k, src, n)                                                                           \
+    do {                                                                                              \
+        if (l == 0) for (int i_ = threadIdx.x; i_ < (n); i_ += blockDim.x) g_mega_dbg[k][i_] = __ldcg((src) + i_); \
+    } while (0)
+#define MEGA_STAMP(l, i)                                                                 \
+    do {                                                                                 \
+        if (threadIdx.x == 0 && blockIdx.x < 160) g_mega_trace[blockIdx.x][l][i] = global_timer_ns(); \
+    } while (0)
+#else
+#define MEGA_STAMP(l, i) \
+    do {                 \
+    } while (0)
+#define MEGA_DBG(k, src, n) \
+    do {                    \
+    } while (0)
+#endif
+
 __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaArgs a)
 {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -387,13 +410,18 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaArgs a
         __syncthreads();
         return !ms.abort;
     };
-    // End of a phase with a slot: arrive, then refill the slot for layer l + 1.
+    // Thread 0: fill `slot` with layer l + 1's weights once its layer-l use is
+    // over -- whether or not this CTA had layer-l work in it (the splits differ
+    // between layers, e.g. q|k|v of the Q5_0 and the Q8_0 layers).
+    auto refill = [&](int l, int slot) {
+        if (tid == 0 && l + 1 < kLayers && ms.armed[slot] == ms.waited[slot])
+            issue_slot(plans[(l + 1) * kSlots + slot], slot_base[slot], ms, slot);
+    };
+    // End of a phase: arrive, then refill the phase's slot.
     auto finish = [&](int l, int ph, int slot) {
         __syncthreads();
-        if (tid == 0) {
-            red_release_gpu(&cnt[l * kPhases + ph]);
-            if (slot >= 0 && l + 1 < kLayers) issue_slot(plans[(l + 1) * kSlots + slot], slot_base[slot], ms, slot);
-        }
+        if (tid == 0) red_release_gpu(&cnt[l * kPhases + ph]);
+        if (slot >= 0) refill(l, slot);
     };
 
     if (ms.abort) {
@@ -403,6 +431,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaArgs a
 
     for (int l = 0; l < kLayers; l++) {
         const MegaLayer& L = a.layers[l];
+        MEGA_STAMP(l, 0);
         // ------------------------------------------------ A: q|k|v rows
         const MegaSlot& pa = plans[l * kSlots + 0];
         if (pa.kind != SK_NONE) {
@@ -413,50 +442,97 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaArgs a
                     const uint8_t* b = a.emb + (idx / 32) * 34;
                     const float v = __fmul_rn((float)(int8_t)b[2 + idx % 32], f16_bits_to_f32(ld_u16_unaligned(b)));
                     xv[i] = v;
-                    if (cta == 0) a.hidden[i] = v;
+                    if (cta == a.emb_cta) a.hidden[i] = v;
                 }
             } else {
                 if (!wait_phase(l - 1, PH_DOWN, __ldg(&a.layers[l - 1].expect[PH_DOWN]))) break;
                 for (int i = tid; i < kHidden; i += kMegaThreads) xv[i] = __ldcg(a.hidden + i);
             }
             __syncthreads();
+            MEGA_STAMP(l, 1);
             mega_norm_quantize(xv, sq, L.attn_norm, kHidden, xpl, ms);
             if (pa.kind == SK_Q8) mega_block_sums(xpl, kHidden, ms.sx);
+            MEGA_STAMP(l, 2);
             if (!wait_slot(0)) break;
             if (pa.kind == SK_Q8) mega_q8(slot_base[0], kHidden, xpl, ms.sx, ms.xs, tsum, yv);
             else mega_blockq<TMAC_TYPE_Q5_0>(slot_base[0], pa, kHidden, xpl, ms.xs, acc_lo, acc_hi, yv);
             for (int t = tid; t < (int)pa.rows; t += kMegaThreads) a.qkv[pa.out0[0] + t] = yv[t];
             finish(l, PH_QKV, 0);
+            MEGA_STAMP(l, 3);
+        } else {
+            refill(l, 0);
         }
         // ------------------------------------------------ B: attention of one head
         const int h = cta - a.head_cta0;
         if (h >= 0 && h < kHeads) {
             if (!wait_phase(l, PH_QKV, __ldg(&L.expect[PH_QKV]))) break;
+            if (h == 0) MEGA_DBG(1, a.qkv, 1152);
             if (tid < kAttnThreads)
                 rope_attention_head(h, a.qkv, a.qkv + kHidden, a.qkv + kHidden + kKvDim, L.bq, L.bk, L.bv, a.rope_c,
                                     a.rope_s, pos, L.kc, L.vc, a.ctx, a.max_seq, att, ms.attn, 1);
+#ifdef TMAC_TRACE
+            __syncthreads();
+            if (l == 0 && h == 0 && tid == 0) {
+                g_mega_dbg[0][0] = (float)pos;
+                g_mega_dbg[0][1] = att[0];
+                g_mega_dbg[0][2] = ms.attn.log_sum;
+                g_mega_dbg[0][3] = ms.attn.q[0];
+                g_mega_dbg[0][4] = ms.attn.k[0];
+                g_mega_dbg[0][5] = ms.attn.v[0];
+                g_mega_dbg[0][6] = (float)a.max_seq;
+                g_mega_dbg[0][7] = att[1];
+                g_mega_dbg[0][8] = att[2 * a.max_seq];
+                for (int i = 0; i < 64; i++) g_mega_dbg[0][64 + i] = __ldcg(a.ctx + i);
+            }
+            if (l == 0 && tid == 0) g_mega_dbg[3][1010 + h] = (float)(global_timer_ns() & 0xFFFFFF);
+#endif
             finish(l, PH_ATTN, -1);
+            MEGA_STAMP(l, 4);
         }
         // ------------------------------------------------ C: attn_output + residual
         const MegaSlot& pc = plans[l * kSlots + 1];
         if (pc.kind != SK_NONE) {
             if (!wait_phase(l, PH_ATTN, kHeads)) break;
+            if (cta == (int)gridDim.x - 1) MEGA_DBG(2, a.ctx, kHidden);
+#ifdef TMAC_TRACE
+            if (l == 0 && cta == (int)gridDim.x - 1 && tid == 0) {
+                g_mega_dbg[3][1000] = (float)ld_acquire_gpu(&cnt[l * kPhases + PH_ATTN]);
+                g_mega_dbg[3][1001] = (float)(global_timer_ns() & 0xFFFFFF);
+                g_mega_dbg[3][1002] = (float)ld_acquire_gpu(&cnt[l * kPhases + PH_QKV]);
+                g_mega_dbg[3][1003] = (float)(l * kPhases + PH_ATTN);
+            }
+#endif
             float mx = 0.0f;
             for (int i = tid; i < kHidden; i += kMegaThreads) mx = fmaxf(mx, fabsf(__ldcg(a.ctx + i)));
             mx = block_max(mx, ms.red, kMegaThreads);
             mega_quantize(a.ctx, kHidden, mx, xpl, ms);
             if (!wait_slot(1)) break;
             mega_blockq<TMAC_TYPE_Q5_0>(slot_base[1], pc, kHidden, xpl, ms.xs, acc_lo, acc_hi, yv);
+#ifdef TMAC_TRACE
+            if (l == 0 && cta == (int)gridDim.x - 1 && tid == 0) {
+                for (int i = 0; i < 8; i++) g_mega_dbg[2][900 + i] = yv[i];
+                g_mega_dbg[2][908] = ms.xs;
+                g_mega_dbg[2][909] = (float)pc.out0[0];
+                g_mega_dbg[2][910] = (float)pc.rows;
+                g_mega_dbg[2][911] = (float)pc.exc_n;
+                for (int i = 0; i < 64; i++) g_mega_dbg[2][912 + i] = (float)((int)(int8_t)xpl[i] * 256 + xpl[kHidden + i]);
+                for (int i = 0; i < 8; i++) g_mega_dbg[2][980 + i] = reinterpret_cast<const float*>(slot_base[1] + pc.ri_off)[i];
+            }
+#endif
             for (int t = tid; t < (int)pc.rows; t += kMegaThreads) {
                 float* hp = a.hidden + pc.out0[0] + t;
                 *hp = __fadd_rn(__ldcg(hp), yv[t]);
             }
             finish(l, PH_O, 1);
+            MEGA_STAMP(l, 5);
+        } else {
+            refill(l, 1);
         }
         // ------------------------------------------------ D: gate|up + silu
         const MegaSlot& pd = plans[l * kSlots + 2];
         if (pd.kind != SK_NONE) {
             if (!wait_phase(l, PH_O, __ldg(&L.expect[PH_O]))) break;
+            if (cta == (int)gridDim.x - 1) MEGA_DBG(3, a.hidden, kHidden);
             for (int i = tid; i < kHidden; i += kMegaThreads) xv[i] = __ldcg(a.hidden + i);
             __syncthreads();
             mega_norm_quantize(xv, sq, L.ffn_norm, kHidden, xpl, ms);
@@ -472,6 +548,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaArgs a
             mx = block_max(mx, ms.red, kMegaThreads);
             if (tid == 0) a.partmax[cta] = mx;
             finish(l, PH_GU, 2);
+            MEGA_STAMP(l, 6);
+        } else {
+            refill(l, 2);
         }
         // ------------------------------------------------ E: ffn_down + residual
         const MegaSlot& pe = plans[l * kSlots + 3];
@@ -491,6 +570,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaArgs a
                 *hp = __fadd_rn(__ldcg(hp), yv[t]);
             }
             finish(l, PH_DOWN, 3);
+            MEGA_STAMP(l, 7);
+        } else {
+            refill(l, 3);
         }
     }
     if (ms.abort) {
@@ -798,6 +880,11 @@ int mega_prepare(tmac_model_s* m, MegaState** out)
     a.err = device_error_word(m->device);
     a.max_seq = m->max_seq;
     a.head_cta0 = G - kHeads;
+    // the embedding reaches hidden through a CTA that signals layer 0's q|k|v
+    // phase, which every later reader of hidden waits for (directly or not)
+    a.emb_cta = -1;
+    for (int c = 0; c < G && a.emb_cta < 0; c++)
+        if (slots[(size_t)c * kLayers * kSlots].kind != SK_NONE) a.emb_cta = c;
     st->args = a;
     *out = st;
     return TMAC_OK;
@@ -825,3 +912,14 @@ int mega_launch(MegaState* st, int n_prompt, cudaStream_t s)
 }
 
 }  // namespace tmac
+
+#ifdef TMAC_TRACE
+extern "C" int tmac_trace_read_mega(unsigned long long* out)
+{
+    return (int)cudaMemcpyFromSymbol(out, tmac::g_mega_trace, sizeof(tmac::g_mega_trace));
+}
+extern "C" int tmac_trace_read_mega_dbg(float* out)
+{
+    return (int)cudaMemcpyFromSymbol(out, tmac::g_mega_dbg, sizeof(tmac::g_mega_dbg));
+}
+#endif

@@ -60,6 +60,8 @@ __host__ __device__ constexpr size_t attn_scratch_bytes(int nscore)
 // order, log-sum-exp weights, context accumulated in position order.  The
 // current position's k/v come from shared memory, so the append needs no
 // ordering against the other heads.  `sc` holds attn_scratch_bytes(nscore).
+// Activations and the KV cache are read at L2 (ld.global.cg): other CTAs of a
+// persistent kernel write them while this CTA may hold older copies in L1.
 TMAC_DEV void rope_attention_head(int h, const float* __restrict__ q, const float* __restrict__ k,
                                   const float* __restrict__ v, const float* __restrict__ bq,
                                   const float* __restrict__ bk, const float* __restrict__ bv,
@@ -77,13 +79,13 @@ TMAC_DEV void rope_attention_head(int h, const float* __restrict__ q, const floa
         const bool isk = j & 1;
         const float* vec = isk ? k + kvh * kHeadDim : q + h * kHeadDim;
         const float* b = isk ? (bk ? bk + kvh * kHeadDim : nullptr) : (bq ? bq + h * kHeadDim : nullptr);
-        const float x0 = __fadd_rn(vec[d], b ? b[d] : 0.0f), x1 = __fadd_rn(vec[d + 1], b ? b[d + 1] : 0.0f);
+        const float x0 = __fadd_rn(__ldcg(vec + d), b ? b[d] : 0.0f), x1 = __fadd_rn(__ldcg(vec + d + 1), b ? b[d + 1] : 0.0f);
         const float y0 = __fsub_rn(__fmul_rn(x0, c[pr]), __fmul_rn(x1, sv[pr]));
         const float y1 = __fadd_rn(__fmul_rn(x0, sv[pr]), __fmul_rn(x1, c[pr]));
         float* dst = isk ? sh.k : sh.q;
         dst[d] = y0;
         dst[d + 1] = y1;
-        sh.v[j] = __fadd_rn(v[kvh * kHeadDim + j], bv ? bv[kvh * kHeadDim + j] : 0.0f);
+        sh.v[j] = __fadd_rn(__ldcg(v + kvh * kHeadDim + j), bv ? bv[kvh * kHeadDim + j] : 0.0f);
     }
     named_bar_sync(bar, kAttnThreads);
     if (h % (kHeads / kKvHeads) == 0 && tid < kHeadDim) {
@@ -98,7 +100,7 @@ TMAC_DEV void rope_attention_head(int h, const float* __restrict__ q, const floa
         named_bar_sync(bar, kAttnThreads);
         for (int i = tid; i < rows * kHeadDim; i += kAttnThreads) {
             const int r = i / kHeadDim, d = i % kHeadDim, p = c0 + r;
-            kv[r * (kHeadDim + 1) + d] = (p == pos) ? sh.k[d] : kc[(int64_t)p * kKvDim + kvh * kHeadDim + d];
+            kv[r * (kHeadDim + 1) + d] = (p == pos) ? sh.k[d] : __ldcg(kc + (int64_t)p * kKvDim + kvh * kHeadDim + d);
         }
         named_bar_sync(bar, kAttnThreads);
         for (int r = tid; r < rows; r += kAttnThreads) {
@@ -135,7 +137,7 @@ TMAC_DEV void rope_attention_head(int h, const float* __restrict__ q, const floa
         named_bar_sync(bar, kAttnThreads);
         for (int i = tid; i < rows * kHeadDim; i += kAttnThreads) {
             const int r = i / kHeadDim, d = i % kHeadDim, p = c0 + r;
-            kv[r * (kHeadDim + 1) + d] = (p == pos) ? sh.v[d] : vc[(int64_t)p * kKvDim + kvh * kHeadDim + d];
+            kv[r * (kHeadDim + 1) + d] = (p == pos) ? sh.v[d] : __ldcg(vc + (int64_t)p * kKvDim + kvh * kHeadDim + d);
         }
         named_bar_sync(bar, kAttnThreads);
         if (tid < kHeadDim)
