@@ -149,7 +149,7 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(float* __restrict__ x, con
     for (int i = threadIdx.x; i < n; i += blockDim.x) store_xq(xq, xp, n, i, quantize_one(xsh[i], s));
 }
 
-// One CTA of 256 threads per query head (rope_attention_head, decode_ops.cuh).
+// One CTA of 256 threads per query head (attention_prefetch + attention_head, decode_ops.cuh).
 __global__ void __launch_bounds__(256) rope_attention_kernel(
     const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
     const float* __restrict__ bq, const float* __restrict__ bk, const float* __restrict__ bv,
@@ -161,7 +161,8 @@ __global__ void __launch_bounds__(256) rope_attention_kernel(
     extern __shared__ float sc[];  // [nsc] scores, then weights; [nsc] exp terms; K/V staging
     __shared__ AttnShared sh;
     if (pos_dev) pos = *pos_dev;
-    rope_attention_head(blockIdx.x, q, k, v, bq, bk, bv, cs, sn, pos, kc, vc, ctx, nscore, sc, sh, 1);
+    attention_prefetch(blockIdx.x, kc, vc, pos, nscore, sc);
+    attention_head(blockIdx.x, q, k, v, bq, bk, bv, cs, sn, pos, kc, vc, ctx, nscore, sc, sh, 1);
 }
 
 // silu(gate) * up (:459-461, :1697-1700), then the quantisation ffn_down's
@@ -484,6 +485,9 @@ int tmac_model_finalize(tmac_model_t m)
     TMAC_CUDA_TRY(cudaMemcpy(m->rope_s, sn.data(), sn.size() * sizeof(float), cudaMemcpyHostToDevice));
     TMAC_CUDA_TRY(cudaMemset(m->kcache, 0, kv * sizeof(float)));
     TMAC_CUDA_TRY(cudaMemset(m->vcache, 0, kv * sizeof(float)));
+    // the attention's score slots grow with the KV cache (above 48 KB past ~1400 positions)
+    TMAC_CUDA_TRY(cudaFuncSetAttribute(rope_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)attn_scratch_bytes(m->max_seq)));
     m->host.clear();
     m->final = true;
     return TMAC_OK;

@@ -18,7 +18,7 @@
 //      as rms_norm :447-454) -> x_q; q|k|v rows of this CTA (Q5_0 groups, or
 //      one 32-row Q8_0 attn_v group in the Q8_0 layers)
 //   B  CTA head_cta0 + h, h < 14: bias + RoPE + KV append + attention of query
-//      head h (rope_attention_head)
+//      head h (attention_prefetch before the wait, then attention_head)
 //   C  ctx -> x_q; attn_output rows; hidden[r] += y[r]
 //   D  ffn_norm -> x_q; gate rows and the matching up rows; h = silu(g) * u,
 //      per-CTA max |h|
@@ -258,12 +258,14 @@ TMAC_DEV void mega_q8(const uint8_t* rec, int cols, const uint8_t* xpl, const in
 // then x_q of the result as byte planes xpl[0..n) (high) / xpl[n..2n) (low) and
 // x_scale in ms.xs.  All threads.
 TMAC_DEV void mega_norm_quantize(float* xv, float* sq, const float* __restrict__ w, int n, uint8_t* xpl,
-                                 MegaMisc& ms)
+                                 MegaMisc& ms, unsigned long long* stamps = nullptr)
 {
     const int tid = threadIdx.x;
     for (int i = tid; i < n; i += kMegaThreads) sq[i] = __fmul_rn(xv[i], xv[i]);
     __syncthreads();
+    if (stamps && tid == 0) stamps[0] = global_timer_ns();
     if (tid == 0) ms.scale = rms_scale(sq, n);
+    if (stamps && tid == 0) stamps[1] = global_timer_ns();
     __syncthreads();
     const float scale = ms.scale;
     float mx = 0.0f;
@@ -283,18 +285,39 @@ TMAC_DEV void mega_norm_quantize(float* xv, float* sq, const float* __restrict__
     __syncthreads();
 }
 
-// x_q of v[0..n) with x_scale from max_abs (tmac_gguf.cpp:889-896).
-TMAC_DEV void mega_quantize(const float* v, int n, float max_abs, uint8_t* xpl, MegaMisc& ms)
+// x_q of v[0..n) (global, written by other CTAs) with x_scale from the maximum
+// of |v| and of extra[0..n_extra) (tmac_gguf.cpp:889-896).  Every value is
+// loaded once into registers, so the phase pays one round trip to L2 for its
+// activations.
+constexpr int kMaxQuant = 7;
+TMAC_DEV void mega_quantize(const float* v, int n, const float* extra, int n_extra, uint8_t* xpl, MegaMisc& ms)
 {
-    const float s = x_scale_from_max(max_abs);
-    if (threadIdx.x == 0) ms.xs = s;
-    for (int i = threadIdx.x; i < n; i += kMegaThreads) {
-        const int16_t q = quantize_one(__ldcg(v + i), s);
-        xpl[i] = (uint8_t)((uint16_t)q >> 8);
-        xpl[n + i] = (uint8_t)(q & 0xFF);
+    const int tid = threadIdx.x;
+    float r[kMaxQuant];
+    float mx = 0.0f;
+#pragma unroll
+    for (int k = 0; k < kMaxQuant; k++) {
+        const int i = tid + k * kMegaThreads;
+        r[k] = i < n ? __ldcg(v + i) : 0.0f;
+    }
+    for (int i = tid; i < n_extra; i += kMegaThreads) mx = fmaxf(mx, __ldcg(extra + i));
+#pragma unroll
+    for (int k = 0; k < kMaxQuant; k++) mx = fmaxf(mx, fabsf(r[k]));
+    mx = block_max(mx, ms.red, kMegaThreads);
+    const float s = x_scale_from_max(mx);
+    if (tid == 0) ms.xs = s;
+#pragma unroll
+    for (int k = 0; k < kMaxQuant; k++) {
+        const int i = tid + k * kMegaThreads;
+        if (i < n) {
+            const int16_t q = quantize_one(r[k], s);
+            xpl[i] = (uint8_t)((uint16_t)q >> 8);
+            xpl[n + i] = (uint8_t)(q & 0xFF);
+        }
     }
     __syncthreads();
 }
+static_assert(kInter <= kMaxQuant * kMegaThreads, "h fits the registers of mega_quantize");
 
 // x_q sums of every 32-column block (the Q8_0 dot products' correction term).
 TMAC_DEV void mega_block_sums(const uint8_t* xpl, int n, int* sx)
@@ -310,24 +333,22 @@ TMAC_DEV void mega_block_sums(const uint8_t* xpl, int n, int* sx)
 
 #ifdef TMAC_TRACE
 // Diagnostic build only (-DTMAC_TRACE): %globaltimer stamps of each CTA's phase
-// boundaries, read back with tmac_trace_read_mega.
-__device__ unsigned long long g_mega_trace[160][kLayers][8];
-__device__ float g_mega_dbg[4][1152];
-#define MEGA_DBG(k, src, n)                                                                           \
-    do {                                                                                              \
-        if (l == 0) for (int i_ = threadIdx.x; i_ < (n); i_ += blockDim.x) g_mega_dbg[k][i_] = __ldcg((src) + i_); \
-    } while (0)
+// boundaries and of each head's attention steps, read back with
+// tmac_trace_read_mega / tmac_trace_read_att.
+__device__ unsigned long long g_mega_trace[160][kLayers][20];
+__device__ unsigned long long g_att_trace[kHeads][kLayers][8];
 #define MEGA_STAMP(l, i)                                                                 \
     do {                                                                                 \
         if (threadIdx.x == 0 && blockIdx.x < 160) g_mega_trace[blockIdx.x][l][i] = global_timer_ns(); \
     } while (0)
+#define MEGA_ATT_STAMPS(h, l) (&g_att_trace[h][l][0])
+#define MEGA_NORM_STAMPS(l) (&g_mega_trace[blockIdx.x][l][17])
 #else
 #define MEGA_STAMP(l, i) \
     do {                 \
     } while (0)
-#define MEGA_DBG(k, src, n) \
-    do {                    \
-    } while (0)
+#define MEGA_ATT_STAMPS(h, l) nullptr
+#define MEGA_NORM_STAMPS(l) nullptr
 #endif
 
 __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaArgs a)
@@ -388,6 +409,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaArgs a
 
     // A wait that failed anywhere ends the token: drain this CTA's copies, return.
     auto drain = [&]() {
+        cp_async_wait_all();  // attention prefetches of this thread
         if (tid == 0)
             for (int s = 0; s < kSlots; s++)
                 for (; ms.waited[s] < ms.armed[s]; ms.waited[s]++) mbar_wait_bounded(&ms.bar[s], ms.waited[s] & 1, nullptr);
@@ -446,85 +468,51 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaArgs a
                 }
             } else {
                 if (!wait_phase(l - 1, PH_DOWN, __ldg(&a.layers[l - 1].expect[PH_DOWN]))) break;
+                MEGA_STAMP(l, 1);
                 for (int i = tid; i < kHidden; i += kMegaThreads) xv[i] = __ldcg(a.hidden + i);
             }
             __syncthreads();
-            MEGA_STAMP(l, 1);
-            mega_norm_quantize(xv, sq, L.attn_norm, kHidden, xpl, ms);
+            mega_norm_quantize(xv, sq, L.attn_norm, kHidden, xpl, ms, MEGA_NORM_STAMPS(l));
             if (pa.kind == SK_Q8) mega_block_sums(xpl, kHidden, ms.sx);
             MEGA_STAMP(l, 2);
             if (!wait_slot(0)) break;
+            MEGA_STAMP(l, 3);
             if (pa.kind == SK_Q8) mega_q8(slot_base[0], kHidden, xpl, ms.sx, ms.xs, tsum, yv);
             else mega_blockq<TMAC_TYPE_Q5_0>(slot_base[0], pa, kHidden, xpl, ms.xs, acc_lo, acc_hi, yv);
             for (int t = tid; t < (int)pa.rows; t += kMegaThreads) a.qkv[pa.out0[0] + t] = yv[t];
             finish(l, PH_QKV, 0);
-            MEGA_STAMP(l, 3);
+            MEGA_STAMP(l, 4);
         } else {
             refill(l, 0);
         }
         // ------------------------------------------------ B: attention of one head
         const int h = cta - a.head_cta0;
         if (h >= 0 && h < kHeads) {
+            // earlier positions' K / V rows do not depend on this step: their
+            // copies overlap the wait for q|k|v
+            if (tid < kAttnThreads) attention_prefetch(h, L.kc, L.vc, pos, a.max_seq, att);
             if (!wait_phase(l, PH_QKV, __ldg(&L.expect[PH_QKV]))) break;
-            if (h == 0) MEGA_DBG(1, a.qkv, 1152);
+            MEGA_STAMP(l, 5);
             if (tid < kAttnThreads)
-                rope_attention_head(h, a.qkv, a.qkv + kHidden, a.qkv + kHidden + kKvDim, L.bq, L.bk, L.bv, a.rope_c,
-                                    a.rope_s, pos, L.kc, L.vc, a.ctx, a.max_seq, att, ms.attn, 1);
-#ifdef TMAC_TRACE
-            __syncthreads();
-            if (l == 0 && h == 0 && tid == 0) {
-                g_mega_dbg[0][0] = (float)pos;
-                g_mega_dbg[0][1] = att[0];
-                g_mega_dbg[0][2] = ms.attn.log_sum;
-                g_mega_dbg[0][3] = ms.attn.q[0];
-                g_mega_dbg[0][4] = ms.attn.k[0];
-                g_mega_dbg[0][5] = ms.attn.v[0];
-                g_mega_dbg[0][6] = (float)a.max_seq;
-                g_mega_dbg[0][7] = att[1];
-                g_mega_dbg[0][8] = att[2 * a.max_seq];
-                for (int i = 0; i < 64; i++) g_mega_dbg[0][64 + i] = __ldcg(a.ctx + i);
-            }
-            if (l == 0 && tid == 0) g_mega_dbg[3][1010 + h] = (float)(global_timer_ns() & 0xFFFFFF);
-#endif
+                attention_head(h, a.qkv, a.qkv + kHidden, a.qkv + kHidden + kKvDim, L.bq, L.bk, L.bv, a.rope_c,
+                               a.rope_s, pos, L.kc, L.vc, a.ctx, a.max_seq, att, ms.attn, 1, MEGA_ATT_STAMPS(h, l));
             finish(l, PH_ATTN, -1);
-            MEGA_STAMP(l, 4);
+            MEGA_STAMP(l, 6);
         }
         // ------------------------------------------------ C: attn_output + residual
         const MegaSlot& pc = plans[l * kSlots + 1];
         if (pc.kind != SK_NONE) {
             if (!wait_phase(l, PH_ATTN, kHeads)) break;
-            if (cta == (int)gridDim.x - 1) MEGA_DBG(2, a.ctx, kHidden);
-#ifdef TMAC_TRACE
-            if (l == 0 && cta == (int)gridDim.x - 1 && tid == 0) {
-                g_mega_dbg[3][1000] = (float)ld_acquire_gpu(&cnt[l * kPhases + PH_ATTN]);
-                g_mega_dbg[3][1001] = (float)(global_timer_ns() & 0xFFFFFF);
-                g_mega_dbg[3][1002] = (float)ld_acquire_gpu(&cnt[l * kPhases + PH_QKV]);
-                g_mega_dbg[3][1003] = (float)(l * kPhases + PH_ATTN);
-            }
-#endif
-            float mx = 0.0f;
-            for (int i = tid; i < kHidden; i += kMegaThreads) mx = fmaxf(mx, fabsf(__ldcg(a.ctx + i)));
-            mx = block_max(mx, ms.red, kMegaThreads);
-            mega_quantize(a.ctx, kHidden, mx, xpl, ms);
+            MEGA_STAMP(l, 7);
+            // this CTA's rows of hidden, loaded together with ctx (one round trip)
+            const float hres = tid < (int)pc.rows ? __ldcg(a.hidden + pc.out0[0] + tid) : 0.0f;
+            mega_quantize(a.ctx, kHidden, nullptr, 0, xpl, ms);
+            MEGA_STAMP(l, 8);
             if (!wait_slot(1)) break;
             mega_blockq<TMAC_TYPE_Q5_0>(slot_base[1], pc, kHidden, xpl, ms.xs, acc_lo, acc_hi, yv);
-#ifdef TMAC_TRACE
-            if (l == 0 && cta == (int)gridDim.x - 1 && tid == 0) {
-                for (int i = 0; i < 8; i++) g_mega_dbg[2][900 + i] = yv[i];
-                g_mega_dbg[2][908] = ms.xs;
-                g_mega_dbg[2][909] = (float)pc.out0[0];
-                g_mega_dbg[2][910] = (float)pc.rows;
-                g_mega_dbg[2][911] = (float)pc.exc_n;
-                for (int i = 0; i < 64; i++) g_mega_dbg[2][912 + i] = (float)((int)(int8_t)xpl[i] * 256 + xpl[kHidden + i]);
-                for (int i = 0; i < 8; i++) g_mega_dbg[2][980 + i] = reinterpret_cast<const float*>(slot_base[1] + pc.ri_off)[i];
-            }
-#endif
-            for (int t = tid; t < (int)pc.rows; t += kMegaThreads) {
-                float* hp = a.hidden + pc.out0[0] + t;
-                *hp = __fadd_rn(__ldcg(hp), yv[t]);
-            }
+            if (tid < (int)pc.rows) a.hidden[pc.out0[0] + tid] = __fadd_rn(hres, yv[tid]);
             finish(l, PH_O, 1);
-            MEGA_STAMP(l, 5);
+            MEGA_STAMP(l, 9);
         } else {
             refill(l, 1);
         }
@@ -532,12 +520,14 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaArgs a
         const MegaSlot& pd = plans[l * kSlots + 2];
         if (pd.kind != SK_NONE) {
             if (!wait_phase(l, PH_O, __ldg(&L.expect[PH_O]))) break;
-            if (cta == (int)gridDim.x - 1) MEGA_DBG(3, a.hidden, kHidden);
+            MEGA_STAMP(l, 10);
             for (int i = tid; i < kHidden; i += kMegaThreads) xv[i] = __ldcg(a.hidden + i);
             __syncthreads();
             mega_norm_quantize(xv, sq, L.ffn_norm, kHidden, xpl, ms);
+            MEGA_STAMP(l, 11);
             if (!wait_slot(2)) break;
             mega_blockq<TMAC_TYPE_Q5_0>(slot_base[2], pd, kHidden, xpl, ms.xs, acc_lo, acc_hi, yv);
+            MEGA_STAMP(l, 12);
             const int n = (int)pd.ngate;
             float mx = 0.0f;
             for (int t = tid; t < n; t += kMegaThreads) {
@@ -548,29 +538,28 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaArgs a
             mx = block_max(mx, ms.red, kMegaThreads);
             if (tid == 0) a.partmax[cta] = mx;
             finish(l, PH_GU, 2);
-            MEGA_STAMP(l, 6);
+            MEGA_STAMP(l, 13);
         } else {
             refill(l, 2);
         }
         // ------------------------------------------------ E: ffn_down + residual
         const MegaSlot& pe = plans[l * kSlots + 3];
         if (pe.kind != SK_NONE) {
+            // hidden is final since the attn_output phase this CTA waited for in
+            // D (every CTA has gate|up rows): read this CTA's rows before the wait
+            const float hres = tid < (int)pe.rows ? __ldcg(a.hidden + pe.out0[0] + tid) : 0.0f;
             if (!wait_phase(l, PH_GU, __ldg(&L.expect[PH_GU]))) break;
-            float mx = 0.0f;
-            for (int i = tid; i < (int)gridDim.x; i += kMegaThreads) mx = fmaxf(mx, __ldcg(a.partmax + i));
-            mx = block_max(mx, ms.red, kMegaThreads);
-            mega_quantize(a.hbuf, kInter, mx, xpl, ms);
+            MEGA_STAMP(l, 14);
+            mega_quantize(a.hbuf, kInter, a.partmax, (int)gridDim.x, xpl, ms);
+            MEGA_STAMP(l, 15);
             if (!wait_slot(3)) break;
             if (pe.kind == SK_Q6K)
                 mega_blockq<TMAC_TYPE_Q6_K>(slot_base[3], pe, kInter, xpl, ms.xs, acc_lo, acc_hi, yv);
             else
                 mega_blockq<TMAC_TYPE_Q4_K>(slot_base[3], pe, kInter, xpl, ms.xs, acc_lo, acc_hi, yv);
-            for (int t = tid; t < (int)pe.rows; t += kMegaThreads) {
-                float* hp = a.hidden + pe.out0[0] + t;
-                *hp = __fadd_rn(__ldcg(hp), yv[t]);
-            }
+            if (tid < (int)pe.rows) a.hidden[pe.out0[0] + tid] = __fadd_rn(hres, yv[tid]);
             finish(l, PH_DOWN, 3);
-            MEGA_STAMP(l, 7);
+            MEGA_STAMP(l, 16);
         } else {
             refill(l, 3);
         }
@@ -803,6 +792,7 @@ int mega_prepare(tmac_model_s* m, MegaState** out)
             split(wd->groups, G, c, &a0[0], &a1[0]);
             o0[0] = (int32_t)(8 * a0[0]);
             if ((rc = blockq_slot(wd, ep_d, a0, a1, o0, 1, sp[3]))) return rc;
+            if (sp[2].kind == SK_NONE) return TMAC_OK;  // phase E relies on every CTA taking part in D
             const uint32_t phases[kSlots] = {PH_QKV, PH_O, PH_GU, PH_DOWN};
             for (int s = 0; s < kSlots; s++) {
                 if (sp[s].kind != SK_NONE) expect[phases[s]]++;
@@ -918,8 +908,8 @@ extern "C" int tmac_trace_read_mega(unsigned long long* out)
 {
     return (int)cudaMemcpyFromSymbol(out, tmac::g_mega_trace, sizeof(tmac::g_mega_trace));
 }
-extern "C" int tmac_trace_read_mega_dbg(float* out)
+extern "C" int tmac_trace_read_att(unsigned long long* out)
 {
-    return (int)cudaMemcpyFromSymbol(out, tmac::g_mega_dbg, sizeof(tmac::g_mega_dbg));
+    return (int)cudaMemcpyFromSymbol(out, tmac::g_att_trace, sizeof(tmac::g_att_trace));
 }
 #endif

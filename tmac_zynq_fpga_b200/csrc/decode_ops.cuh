@@ -36,7 +36,8 @@ TMAC_DEV float rms_scale(const float* sq, int n)
 // silu(g) * u (:459-461, :1697-1700).
 TMAC_DEV float silu_mul(float g, float u) { return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf_ref(-g))), u); }
 
-constexpr int kAttnChunk = 128;   // K/V rows staged in shared memory at a time
+constexpr int kAttnChunk = 64;    // K/V rows in shared memory at a time
+constexpr int kAttnStride = 68;   // floats per staged row (16-byte aligned rows)
 constexpr int kAttnThreads = 256; // threads of one head's attention
 
 struct AttnShared {
@@ -45,35 +46,70 @@ struct AttnShared {
     float log_sum;
 };
 
-// Bytes of the dynamic scratch `sc` that rope_attention_head needs for nscore
-// score slots.
+// Bytes of the dynamic scratch `sc` that the attention needs for nscore score
+// slots: scores | exp terms | K rows | V rows.
 __host__ __device__ constexpr size_t attn_scratch_bytes(int nscore)
 {
-    return (2 * (size_t)nscore + kAttnChunk * (kHeadDim + 1)) * sizeof(float);
+    return (2 * (size_t)nscore + 2 * kAttnChunk * kAttnStride) * sizeof(float);
+}
+
+TMAC_DEV void cp_async16(void* dst, const void* src)
+{
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+TMAC_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+TMAC_DEV void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// First half of a query head's attention, threads 0..255: start copying the
+// K and V rows of KV head kvh(h) for positions [0, min(pos, 64)) -- written by
+// earlier steps, so they do not depend on this step's q / k / v -- into the
+// K / V row buffers of `sc` (asynchronous; attention_head waits for them).
+TMAC_DEV void attention_prefetch(int h, const float* __restrict__ kc, const float* __restrict__ vc, int pos,
+                                 int nscore, float* sc)
+{
+    const int kvh = h / (kHeads / kKvHeads);
+    const int n = min(pos, kAttnChunk);
+    float* kb = sc + 2 * nscore;
+    float* vb = kb + kAttnChunk * kAttnStride;
+    for (int i = threadIdx.x; i < n * (kHeadDim / 4); i += kAttnThreads) {
+        const int r = i / (kHeadDim / 4), d4 = i % (kHeadDim / 4);
+        const int64_t g = (int64_t)r * kKvDim + kvh * kHeadDim + 4 * d4;
+        cp_async16(kb + r * kAttnStride + 4 * d4, kc + g);
+        cp_async16(vb + r * kAttnStride + 4 * d4, vc + g);
+    }
+    cp_async_commit();
 }
 
 // Query head h, run by threads 0..255 of a CTA (they synchronise on named
-// barrier `bar`): q/k/v bias add (:1591-1614), RoPE on the head's q and its KV
-// head's k (:1528-1554), KV-cache append by the first query head of each KV
-// group (:1622-1623), then attention over positions 0..pos (:1625-1660):
-// scores q.k in d order / sqrtf(64), max, exp terms, their sum in position
-// order, log-sum-exp weights, context accumulated in position order.  The
-// current position's k/v come from shared memory, so the append needs no
-// ordering against the other heads.  `sc` holds attn_scratch_bytes(nscore).
-// Activations and the KV cache are read at L2 (ld.global.cg): other CTAs of a
-// persistent kernel write them while this CTA may hold older copies in L1.
-TMAC_DEV void rope_attention_head(int h, const float* __restrict__ q, const float* __restrict__ k,
-                                  const float* __restrict__ v, const float* __restrict__ bq,
-                                  const float* __restrict__ bk, const float* __restrict__ bv,
-                                  const float* __restrict__ cs, const float* __restrict__ sn, int pos,
-                                  float* __restrict__ kc, float* __restrict__ vc, float* __restrict__ ctx, int nscore,
-                                  float* sc, AttnShared& sh, int bar)
+// barrier `bar`) after attention_prefetch: q/k/v bias add (:1591-1614), RoPE on
+// the head's q and its KV head's k (:1528-1554), KV-cache append by the first
+// query head of each KV group (:1622-1623), then attention over positions
+// 0..pos (:1625-1660): scores q.k in d order / sqrtf(64), max, exp terms, their
+// sum in position order, log-sum-exp weights, context accumulated in position
+// order.  The current position's k/v come from shared memory, so the append
+// needs no ordering against the other heads.  `sc` holds
+// attn_scratch_bytes(nscore).  Activations and KV rows past the prefetched
+// chunk are read at L2 (ld.global.cg): other CTAs of a persistent kernel write
+// them while this CTA may hold older copies in L1.  stamps (diagnostics only):
+// 8 %globaltimer values of the steps, or nullptr.
+TMAC_DEV void attention_head(int h, const float* __restrict__ q, const float* __restrict__ k,
+                             const float* __restrict__ v, const float* __restrict__ bq, const float* __restrict__ bk,
+                             const float* __restrict__ bv, const float* __restrict__ cs, const float* __restrict__ sn,
+                             int pos, float* __restrict__ kc, float* __restrict__ vc, float* __restrict__ ctx,
+                             int nscore, float* sc, AttnShared& sh, int bar, unsigned long long* stamps = nullptr)
 {
+#define ATT_STAMP(i)                                                  \
+    do {                                                              \
+        if (stamps && threadIdx.x == 0) stamps[i] = global_timer_ns(); \
+    } while (0)
+    ATT_STAMP(0);
     const int tid = threadIdx.x;
     const int nsc = nscore;
     const int kvh = h / (kHeads / kKvHeads);
     const float* c = cs + (int64_t)pos * (kHeadDim / 2);
     const float* sv = sn + (int64_t)pos * (kHeadDim / 2);
+    float* kb = sc + 2 * nsc;  // [kAttnChunk][kAttnStride]
+    float* vb = kb + kAttnChunk * kAttnStride;
     if (tid < kHeadDim) {  // thread j: pair j/2 of q (j even) or of k (j odd)
         const int j = tid, pr = j >> 1, d = 2 * pr;
         const bool isk = j & 1;
@@ -87,30 +123,34 @@ TMAC_DEV void rope_attention_head(int h, const float* __restrict__ q, const floa
         dst[d + 1] = y1;
         sh.v[j] = __fadd_rn(__ldcg(v + kvh * kHeadDim + j), bv ? bv[kvh * kHeadDim + j] : 0.0f);
     }
+    cp_async_wait_all();  // the prefetched K / V rows of positions [0, min(pos, 64))
     named_bar_sync(bar, kAttnThreads);
+    ATT_STAMP(1);
     if (h % (kHeads / kKvHeads) == 0 && tid < kHeadDim) {
         kc[(int64_t)pos * kKvDim + kvh * kHeadDim + tid] = sh.k[tid];
         vc[(int64_t)pos * kKvDim + kvh * kHeadDim + tid] = sh.v[tid];
     }
-    // scores: K rows of this KV head staged in shared memory, 128 positions at a
-    // time (rows padded to 65 floats), one position per thread, d in order
-    float* kv = sc + 2 * nsc;  // [kAttnChunk][kHeadDim + 1]
+    // scores, 64 positions at a time, one position per thread, d in order; the
+    // first chunk's earlier rows were prefetched, later chunks are staged here
     for (int c0 = 0; c0 <= pos; c0 += kAttnChunk) {
         const int rows = min(kAttnChunk, pos + 1 - c0);
-        named_bar_sync(bar, kAttnThreads);
+        if (c0 > 0) named_bar_sync(bar, kAttnThreads);
         for (int i = tid; i < rows * kHeadDim; i += kAttnThreads) {
             const int r = i / kHeadDim, d = i % kHeadDim, p = c0 + r;
-            kv[r * (kHeadDim + 1) + d] = (p == pos) ? sh.k[d] : __ldcg(kc + (int64_t)p * kKvDim + kvh * kHeadDim + d);
+            if (p == pos) kb[r * kAttnStride + d] = sh.k[d];
+            else if (c0 > 0) kb[r * kAttnStride + d] = __ldcg(kc + (int64_t)p * kKvDim + kvh * kHeadDim + d);
         }
         named_bar_sync(bar, kAttnThreads);
+        ATT_STAMP(2);
         for (int r = tid; r < rows; r += kAttnThreads) {
-            const float* kp = kv + r * (kHeadDim + 1);
+            const float* kp = kb + r * kAttnStride;
             float sum = 0.0f;
             for (int d = 0; d < kHeadDim; d++) sum = __fadd_rn(sum, __fmul_rn(sh.q[d], kp[d]));
             sc[c0 + r] = __fdiv_rn(sum, 8.0f);  // / sqrtf(64)
         }
     }
     named_bar_sync(bar, kAttnThreads);
+    ATT_STAMP(3);
     // max (order-free), the exp terms in parallel, their sum in position order
     float mx = -INFINITY;
     for (int p = tid; p <= pos; p += kAttnThreads) mx = fmaxf(mx, sc[p]);
@@ -128,22 +168,28 @@ TMAC_DEV void rope_attention_head(int h, const float* __restrict__ q, const floa
         sh.log_sum = __fadd_rn(logf_ref(es), mx);
     }
     named_bar_sync(bar, kAttnThreads);
+    ATT_STAMP(4);
     for (int p = tid; p <= pos; p += kAttnThreads) sc[p] = expf_ref(__fsub_rn(sc[p], sh.log_sum));
     named_bar_sync(bar, kAttnThreads);
-    // context: V rows staged the same way, positions in order
+    ATT_STAMP(5);
+    // context: V rows (first chunk prefetched), positions in order
     float a = 0.0f;
     for (int c0 = 0; c0 <= pos; c0 += kAttnChunk) {
         const int rows = min(kAttnChunk, pos + 1 - c0);
-        named_bar_sync(bar, kAttnThreads);
+        if (c0 > 0) named_bar_sync(bar, kAttnThreads);
         for (int i = tid; i < rows * kHeadDim; i += kAttnThreads) {
             const int r = i / kHeadDim, d = i % kHeadDim, p = c0 + r;
-            kv[r * (kHeadDim + 1) + d] = (p == pos) ? sh.v[d] : __ldcg(vc + (int64_t)p * kKvDim + kvh * kHeadDim + d);
+            if (p == pos) vb[r * kAttnStride + d] = sh.v[d];
+            else if (c0 > 0) vb[r * kAttnStride + d] = __ldcg(vc + (int64_t)p * kKvDim + kvh * kHeadDim + d);
         }
         named_bar_sync(bar, kAttnThreads);
+        ATT_STAMP(6);
         if (tid < kHeadDim)
-            for (int r = 0; r < rows; r++) a = __fadd_rn(a, __fmul_rn(sc[c0 + r], kv[r * (kHeadDim + 1) + tid]));
+            for (int r = 0; r < rows; r++) a = __fadd_rn(a, __fmul_rn(sc[c0 + r], vb[r * kAttnStride + tid]));
     }
     if (tid < kHeadDim) ctx[h * kHeadDim + tid] = a;
+    ATT_STAMP(7);
+#undef ATT_STAMP
 }
 
 }  // namespace tmac
