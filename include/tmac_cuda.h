@@ -203,9 +203,11 @@ int tmac_reserve(int device, int64_t max_batch, int64_t max_cols);
  * for bit: every row is quantised like one GEMV call, the products are the
  * reference's exact int16 weights times x_q (tcgen05 int8 MMAs on byte planes),
  * row_acc (optional, int64 [m][rows]) the integer row sums.  NATIVE Q5_0 /
- * Q4_K / Q6_K weights; cols a multiple of 16, at most 32768.  The first call on
- * a weight decodes its int16 planes (2 bytes per weight, kept with the weight).
- * Device pointers; asynchronous on `stream`. */
+ * Q4_K / Q6_K weights, and NATIVE Q8_0 (matmul_fpga_q8 per row: one GEMM per
+ * 64-column tile, folded into y in tile order; row_acc must be NULL); cols a
+ * multiple of 16, at most 32768.  The first call on a weight decodes its int16
+ * planes (2 bytes per weight, kept with the weight).  Device pointers;
+ * asynchronous on `stream`. */
 int tmac_gemm(tmac_weight_t w, const float* x, float* y, int64_t* row_acc, int m, void* stream);
 
 /* Measurement aid (no reference counterpart): dense int8 tensor-core rate of

@@ -247,6 +247,14 @@ int ref_phaseb_run(uint32_t desc_off, int64_t* acc, int64_t cap)
 // compares against the drivers' y (|err| <= 2); returns the error count.
 int ref_phaseb_verify(void) { return phaseb_verify(); }
 
+// phaseb_dump_files (tmac_gguf.cpp:597-708) on the chain built so far: writes
+// the reference's testbench files /tmp/tb_phaseb.bin and /tmp/tb_phaseb.hdr.
+int ref_phaseb_dump(void)
+{
+    phaseb_dump_files();
+    return 0;
+}
+
 }  // extern "C"
 
 // ---------------------------------------------------------------------------

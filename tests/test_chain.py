@@ -189,3 +189,28 @@ def test_gpu_dump_files_equal_the_oracle():
     b, h = oracle.phaseb_dump_bytes(room, base, head, desc_base, base)
     assert open(bp, "rb").read() == b
     assert open(hp, "rb").read() == h
+
+
+@needs_ref
+def test_dump_format_equals_the_reference_dump_files():
+    """The Phase-B testbench files written by the reference's own
+    phaseb_dump_files (tmac_gguf.cpp:597-708, run through oracle/_ref; it writes
+    fixed /tmp paths) are byte-identical to the oracle's restatement, which the
+    GPU test above pins tmac_phaseb_dump to.  Covers the 20-byte header entries
+    (the code, not the 24 its comment states) and the DDR image."""
+    ms = [(synth.Q5_0, synth.make_weights(synth.Q5_0, 16, 896, seed=61), 16, 896,
+           synth.make_activations(896, seed=61)[0]),
+          (synth.Q6_K, synth.make_weights(synth.Q6_K, 64, 512, seed=62), 64, 512,
+           synth.make_activations(512, seed=62)[0]),
+          (synth.Q4_K, synth.make_weights(synth.Q4_K, 56, 256, seed=63), 56, 256,
+           synth.make_activations(256, seed=63)[0])]
+    arena, base, head, _ = oracle.ref_build_chain(ms)
+    ndesc = len(oracle.walk_chain(arena, base, head))
+    desc_base = (base + arena.nbytes + 31) & ~31
+    room = np.concatenate([arena, np.zeros(desc_base - base - arena.nbytes + 32 * ndesc, np.uint8)])
+    b, h = oracle.phaseb_dump_bytes(room, base, head, desc_base, base)
+    R = oracle.ref()
+    R.ref_phaseb_dump.restype = ctypes.c_int
+    assert R.ref_phaseb_dump() == 0
+    assert open("/tmp/tb_phaseb.bin", "rb").read() == b
+    assert open("/tmp/tb_phaseb.hdr", "rb").read() == h

@@ -70,3 +70,45 @@ def test_prefill_long_odd_length_matches_decode(mdl):
         np.testing.assert_array_equal(hid[0, p], h[0], err_msg=f"position {p}")
     toks, _ = mdl.generate(a, 1)
     assert nxt[0] == toks[0]
+
+
+def test_prefill_64x512_matches_decode_at_full_size():
+    """The benchmark's batched prefill, 64 sequences x 512 seeded tokens (M =
+    32768 rows per projection): for three sequences, the hidden states at
+    positions 0, 255 and 511 equal the decode engine's after feeding the same
+    tokens (bit for bit), and so does the greedy next token."""
+    m = tm.Model(model.default_model_path(0), switches=tm.SW_ALL, max_seq=513)
+    try:
+        toks = np.random.default_rng(0).integers(0, model.VOCAB, size=(64, 512)).astype(np.int32)
+        nxt, hid = m.prefill(toks, want_hidden=True)
+        for s in (0, 31, 63):
+            for p in (0, 255):
+                _, h = m.generate(toks[s, :p + 1], 0, want_hidden=True)
+                np.testing.assert_array_equal(hid[s, p].view(np.int32), h[0].view(np.int32),
+                                              err_msg=f"sequence {s} position {p}")
+            t, h = m.generate(toks[s], 1, want_hidden=True)
+            np.testing.assert_array_equal(hid[s, 511].view(np.int32), h[0].view(np.int32),
+                                          err_msg=f"sequence {s} position 511")
+            assert nxt[s] == t[0], f"sequence {s}"
+    finally:
+        m.free()
+
+
+PREFILL_FIX = os.path.join(HERE, "golden", "prefill_2x64_seed0.npz")
+HIDDEN_RTOL = 5e-4  # as test_decode_gpu.py: the context ops' expf/logf against glibc
+
+
+@pytest.mark.skipif(not os.path.exists(PREFILL_FIX), reason="prefill fixture missing")
+def test_prefill_matches_reference_process_prompt(mdl):
+    """Two 64-token sequences of the benchmark's prefill workload against the
+    reference engine's own process_prompt + one greedy step (fixture from
+    oracle/_ref, tests/golden/make_prefill_golden.py): the hidden state after
+    the last prompt position within HIDDEN_RTOL, the next token identical."""
+    g = np.load(PREFILL_FIX)
+    toks = g["tokens"]
+    nxt, hid = mdl.prefill(toks, want_hidden=True)
+    for s in range(len(toks)):
+        ref = g["hidden"][s]
+        err = np.abs(hid[s, -1] - ref).max() / np.abs(ref).max()
+        assert err < HIDDEN_RTOL, f"sequence {s}: relative hidden error {err:.3g}"
+        assert nxt[s] == g["next_token"][s], f"sequence {s}"

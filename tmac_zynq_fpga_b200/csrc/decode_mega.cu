@@ -335,7 +335,7 @@ TMAC_DEV void mega_block_sums(const uint8_t* xpl, int n, int* sx)
 // Diagnostic build only (-DTMAC_TRACE): %globaltimer stamps of each CTA's phase
 // boundaries and of each head's attention steps, read back with
 // tmac_trace_read_mega / tmac_trace_read_att.
-__device__ unsigned long long g_mega_trace[160][kLayers][20];
+__device__ unsigned long long g_mega_trace[160][kLayers][24];
 __device__ unsigned long long g_att_trace[kHeads][kLayers][8];
 #define MEGA_STAMP(l, i)                                                                 \
     do {                                                                                 \
@@ -496,6 +496,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaArgs a
             if (tid < kAttnThreads)
                 attention_head(h, a.qkv, a.qkv + kHidden, a.qkv + kHidden + kKvDim, L.bq, L.bk, L.bv, a.rope_c,
                                a.rope_s, pos, L.kc, L.vc, a.ctx, a.max_seq, att, ms.attn, 1, MEGA_ATT_STAMPS(h, l));
+            MEGA_STAMP(l, 23);
             finish(l, PH_ATTN, -1);
             MEGA_STAMP(l, 6);
         }
@@ -509,7 +510,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaArgs a
             mega_quantize(a.ctx, kHidden, nullptr, 0, xpl, ms);
             MEGA_STAMP(l, 8);
             if (!wait_slot(1)) break;
+            MEGA_STAMP(l, 21);
             mega_blockq<TMAC_TYPE_Q5_0>(slot_base[1], pc, kHidden, xpl, ms.xs, acc_lo, acc_hi, yv);
+            MEGA_STAMP(l, 22);
             if (tid < (int)pc.rows) a.hidden[pc.out0[0] + tid] = __fadd_rn(hres, yv[tid]);
             finish(l, PH_O, 1);
             MEGA_STAMP(l, 9);
@@ -553,10 +556,12 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaArgs a
             mega_quantize(a.hbuf, kInter, a.partmax, (int)gridDim.x, xpl, ms);
             MEGA_STAMP(l, 15);
             if (!wait_slot(3)) break;
+            MEGA_STAMP(l, 19);
             if (pe.kind == SK_Q6K)
                 mega_blockq<TMAC_TYPE_Q6_K>(slot_base[3], pe, kInter, xpl, ms.xs, acc_lo, acc_hi, yv);
             else
                 mega_blockq<TMAC_TYPE_Q4_K>(slot_base[3], pe, kInter, xpl, ms.xs, acc_lo, acc_hi, yv);
+            MEGA_STAMP(l, 20);
             if (tid < (int)pe.rows) a.hidden[pe.out0[0] + tid] = __fadd_rn(hres, yv[tid]);
             finish(l, PH_DOWN, 3);
             MEGA_STAMP(l, 16);

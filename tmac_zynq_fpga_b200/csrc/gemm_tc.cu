@@ -397,8 +397,50 @@ int gemm_planes(const GemmOperands& op, cudaStream_t s)
     return TMAC_OK;
 }
 
+// NATIVE Q8_0 (matmul_fpga_q8 per row, tmac_gguf.cpp:948-1085): the int16
+// products deq = (q * cs) >> 8 as byte planes (decoded on first use, kept with
+// the weight), one GEMM per 64-column tile folding y = (float)(y + acc * x_scale
+// * row_scale) in tile order from y = 0, as the Q8_0 GEMV does.
+int launch_gemm_q8(tmac_weight_s* w, const float* x, float* y, int M, cudaStream_t s)
+{
+    if (!w->gwh) {
+        const size_t n = (size_t)(w->rows * w->cols);
+        TMAC_CUDA_TRY(cudaMalloc(&w->gwh, n));
+        TMAC_CUDA_TRY(cudaMalloc(&w->gwl, n));
+        int rc = q8_planes(w, reinterpret_cast<int8_t*>(w->gwh), reinterpret_cast<uint8_t*>(w->gwl), s);
+        if (rc) return rc;
+    }
+    GemmWorkspace* ws = nullptr;
+    int rc;
+    if ((rc = gemm_workspace(w->device, M, w->cols, &ws))) return rc;
+    if ((rc = quantize_rows(x, w->cols, M, ws->xh, ws->xl, ws->xs, s))) return rc;
+    TMAC_CUDA_TRY(cudaMemsetAsync(y, 0, (size_t)M * w->rows * sizeof(float), s));
+    for (int64_t k0 = 0; k0 < w->cols; k0 += 64) {
+        GemmOperands op;
+        op.xh = reinterpret_cast<const uint8_t*>(ws->xh);
+        op.xl = ws->xl;
+        op.x_stride = w->cols;
+        op.xs = ws->xs;
+        op.M = M;
+        op.wh = reinterpret_cast<const uint8_t*>(w->gwh);
+        op.wl = reinterpret_cast<const uint8_t*>(w->gwl);
+        op.w_stride = w->cols;
+        op.N = (int)w->rows;
+        op.K = std::min<int64_t>(64, w->cols - k0);
+        op.k_off = k0;
+        op.row_param = w->row_norm;
+        op.mode = 1;
+        op.y = y;
+        op.y_stride = w->rows;
+        op.device = w->device;
+        if ((rc = gemm_planes(op, s))) return rc;
+    }
+    return TMAC_OK;
+}
+
 int launch_gemm(tmac_weight_s* w, const float* x, float* y, int64_t* acc_out, int M, cudaStream_t s)
 {
+    if (w->type == TMAC_TYPE_Q8_0) return launch_gemm_q8(w, x, y, M, s);
     int rc = gemm_prepare(w, s);
     if (rc) return rc;
     GemmWorkspace* ws = nullptr;
@@ -435,8 +477,10 @@ extern "C" int tmac_gemm(tmac_weight_t w, const float* x, float* y, int64_t* row
     if (!w) return fail(TMAC_ERR_INVALID, "NULL weight handle");
     if (!x || !y) return fail(TMAC_ERR_INVALID, "NULL x or y");
     if (m <= 0) return fail(TMAC_ERR_SHAPE, "m must be positive");
-    if (w->mode != TMAC_MODE_NATIVE || w->type == TMAC_TYPE_Q8_0)
-        return fail(TMAC_ERR_TYPE, "tmac_gemm: NATIVE Q5_0 / Q4_K / Q6_K weights only");
+    if (w->mode != TMAC_MODE_NATIVE)
+        return fail(TMAC_ERR_TYPE, "tmac_gemm: NATIVE Q5_0 / Q8_0 / Q4_K / Q6_K weights only");
+    if (w->type == TMAC_TYPE_Q8_0 && row_acc)
+        return fail(TMAC_ERR_TYPE, "tmac_gemm: no integer row sums for Q8_0 (its rows fold 64-column tiles in fp64)");
     if (w->cols % 16 || w->cols > 32768) return fail(TMAC_ERR_SHAPE, "tmac_gemm: cols must be a multiple of 16, <= 32768");
     DeviceGuard dg(w->device);
     if (!dg.ok) return fail(TMAC_ERR_CUDA, "cudaSetDevice failed");
