@@ -158,7 +158,7 @@ __global__ void __launch_bounds__(256) rope_attention_kernel(
 {
     pdl_launch();
     pdl_wait();
-    extern __shared__ float sc[];  // [nsc] scores, then weights; [nsc] exp terms; K/V staging
+    extern __shared__ __align__(16) float sc[];  // [nsc] scores, then weights; [nsc] exp terms; K/V staging
     __shared__ AttnShared sh;
     if (pos_dev) pos = *pos_dev;
     attention_prefetch(blockIdx.x, kc, vc, pos, nscore, sc);

@@ -46,11 +46,15 @@ struct AttnShared {
     float log_sum;
 };
 
+// Floats of the score and exp-term slots for nscore positions, rounded so that
+// the K / V row buffers after them start 16-byte aligned (cp.async targets).
+__host__ __device__ constexpr int attn_score_floats(int nscore) { return (2 * nscore + 3) / 4 * 4; }
+
 // Bytes of the dynamic scratch `sc` that the attention needs for nscore score
 // slots: scores | exp terms | K rows | V rows.
 __host__ __device__ constexpr size_t attn_scratch_bytes(int nscore)
 {
-    return (2 * (size_t)nscore + 2 * kAttnChunk * kAttnStride) * sizeof(float);
+    return ((size_t)attn_score_floats(nscore) + 2 * kAttnChunk * kAttnStride) * sizeof(float);
 }
 
 TMAC_DEV void cp_async16(void* dst, const void* src)
@@ -69,7 +73,7 @@ TMAC_DEV void attention_prefetch(int h, const float* __restrict__ kc, const floa
 {
     const int kvh = h / (kHeads / kKvHeads);
     const int n = min(pos, kAttnChunk);
-    float* kb = sc + 2 * nscore;
+    float* kb = sc + attn_score_floats(nscore);
     float* vb = kb + kAttnChunk * kAttnStride;
     for (int i = threadIdx.x; i < n * (kHeadDim / 4); i += kAttnThreads) {
         const int r = i / (kHeadDim / 4), d4 = i % (kHeadDim / 4);
@@ -108,7 +112,7 @@ TMAC_DEV void attention_head(int h, const float* __restrict__ q, const float* __
     const int kvh = h / (kHeads / kKvHeads);
     const float* c = cs + (int64_t)pos * (kHeadDim / 2);
     const float* sv = sn + (int64_t)pos * (kHeadDim / 2);
-    float* kb = sc + 2 * nsc;  // [kAttnChunk][kAttnStride]
+    float* kb = sc + attn_score_floats(nsc);  // [kAttnChunk][kAttnStride]
     float* vb = kb + kAttnChunk * kAttnStride;
     if (tid < kHeadDim) {  // thread j: pair j/2 of q (j even) or of k (j odd)
         const int j = tid, pr = j >> 1, d = 2 * pr;
