@@ -500,6 +500,9 @@ def main():
     ap.add_argument("--no-model", action="store_true", help="skip the decode / prefill measurements")
     ap.add_argument("--no-pdl", action="store_true",
                     help="launch each step's kernel after the previous one ends (no programmatic dependent launch)")
+    ap.add_argument("--full-logits", action="store_true",
+                    help="N > 1: every step also all-gathers the logits shards (NCCL) so each rank holds the "
+                         "whole vector, as get_logits_q8 returns it")
     ap.add_argument("--collective", choices=["fused", "peer", "nccl"], default="fused",
                     help="top-1 merge across ranks: inside the logits GEMV over NVLink peer memory, "
                          "a separate peer-memory exchange kernel, or an NCCL all-reduce")
@@ -567,19 +570,25 @@ def main():
             except Exception as e:  # keep NCCL
                 merge_kind = f"nccl int64 MAX all-reduce (peer exchange unavailable: {e})"
 
+    gather = world > 1 and args.full_logits
+    y_full = torch.empty(VOCAB, dtype=torch.float32, device="cuda") if gather else None
+
     def step(i):
         # logits of this rank's vocab shard + their top-1 key, then the global
-        # greedy token on every rank
+        # greedy token on every rank (and, with --full-logits, the whole vector)
         w = weights[i % ncopies]
         if fused:
             merge.gemv_top1(w, x, y, key, r0, stream)
-            return
-        w.gemv_top1(x, y, key, index_base=r0, stream=stream)
-        if world > 1:
-            if merge is not None:
-                merge(key, stream)
-            else:
-                dist.all_reduce(key, op=dist.ReduceOp.MAX)
+        else:
+            w.gemv_top1(x, y, key, index_base=r0, stream=stream)
+            if world > 1:
+                if merge is not None:
+                    merge(key, stream)
+                else:
+                    dist.all_reduce(key, op=dist.ReduceOp.MAX)
+        if gather:
+            from tmac_zynq_fpga_b200 import shard as _shard
+            _shard.gather_logits(y, VOCAB, out=y_full)
 
     # consecutive steps' kernels: the next one's prologue and weight copies may
     # start while the previous one finishes (tmac_set_pdl; results unchanged)
@@ -660,7 +669,8 @@ def main():
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "int16/int64", "data": "synthetic",
             "config": {"workload": WORKLOAD, "rows": VOCAB, "cols": HIDDEN, "batch": 1,
-                       "step": "shard logits GEMV with fused top-1 key" + (f" + {merge_kind}" if world > 1 else ""),
+                       "step": "shard logits GEMV with fused top-1 key" + (f" + {merge_kind}" if world > 1 else "")
+                               + (" + NCCL all-gather of the logits shards" if gather else ""),
                        "greedy_token": tok,
                        "parallelism": f"vocab-row shards x{world}", "shard_rows": rows,
                        "launch": "back-to-back, no programmatic dependent launch" if args.no_pdl else

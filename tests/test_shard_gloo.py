@@ -95,3 +95,29 @@ def test_two_rank_sequence_sharded_prefill_gathers_in_batch_order(n_seq):
     toks = np.random.default_rng(3).integers(0, 151936, size=(n_seq, 16))
     expect = (toks.sum(axis=1) * 7919 % 151936).astype(np.int32).tolist()
     assert out[0] == expect and out[1] == expect
+
+
+def _logits_rank(rank, world, port, rows, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    w = synth.make_weights(synth.Q8_0, rows, COLS, seed=9)
+    x = synth.make_activations(COLS, seed=9)[0]
+    r0, r1 = shard.shard_bounds(rows, world, rank)
+    y = oracle.gemv(synth.Q8_0, w[r0 * 28 * 34: r1 * 28 * 34], r1 - r0, COLS, x).y
+    full = shard.gather_logits(torch.from_numpy(y), rows)
+    out[rank] = full.numpy().tobytes()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("rows", [2048, 2047])
+def test_two_rank_full_logits_gather(rows):
+    """Every rank ends with the whole logits vector, bit-identical to the
+    unsharded GEMV (even and uneven shards)."""
+    world = 2
+    out = mp.Manager().dict()
+    mp.spawn(_logits_rank, args=(world, _free_port(), rows, out), nprocs=world, join=True)
+    w = synth.make_weights(synth.Q8_0, rows, COLS, seed=9)
+    x = synth.make_activations(COLS, seed=9)[0]
+    y = oracle.gemv(synth.Q8_0, w, rows, COLS, x).y
+    for r in range(world):
+        assert out[r] == y.tobytes()

@@ -45,6 +45,35 @@ def all_reduce_top1(key_tensor, group=None):
     return key_tensor
 
 
+def gather_logits(local, rows: int, out=None, group=None):
+    """The full logits vector on every rank from each rank's vocab shard
+    (get_logits_q8 returns all rows, sim/tmac_gguf.cpp:1820-1845): one
+    all-gather of the shards, padded to the largest shard.  `local` is this
+    rank's shard (a torch tensor on the process group's device, float32);
+    returns (and fills `out`, if given) a float32 tensor [rows]."""
+    import torch
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    most = -(-rows // world)
+    if local.numel() == most:
+        buf = local.contiguous()
+    else:
+        buf = torch.zeros(most, dtype=torch.float32, device=local.device)
+        buf[: local.numel()] = local
+    flat = torch.empty(world * most, dtype=torch.float32, device=local.device)
+    dist.all_gather_into_tensor(flat, buf, group=group)
+    if out is None:
+        out = torch.empty(rows, dtype=torch.float32, device=local.device)
+    if all(shard_bounds(rows, world, r)[1] - shard_bounds(rows, world, r)[0] == most for r in range(world)):
+        out.copy_(flat[:rows])
+    else:
+        parts = flat.view(world, most)
+        for r in range(world):
+            r0, r1 = shard_bounds(rows, world, r)
+            out[r0:r1] = parts[r, : r1 - r0]
+    return out
+
+
 # ------------------------------------------------------------------ prefill
 # The multi-sequence prefill batch shards by sequence: rank r prefills sequences
 # [s0, s1) of the batch with tmac_model_prefill on its own GPU.  Sequences are
