@@ -9,8 +9,11 @@
 // does not wait for the activations: each CTA owns a fixed share of every
 // projection's 8-row groups and bulk-copies its share of layer l + 1 into
 // shared memory while layer l computes, so a projection phase only decodes
-// from shared memory.  Phases hand activations over through global memory and
-// per-(layer, phase) arrival counters (release / acquire at GPU scope).
+// from shared memory.  Phases hand activations over through global memory:
+// every value is stored together with the tag of the phase that produced it
+// (one 8-byte store, so value and tag are seen together), and a reader polls
+// the values it needs until their tags are current -- no separate flag, so a
+// hand-over costs one L2 round trip once the data is there.
 //
 // Phases of layer l (weights of phases A, C, D, E are the four shared-memory
 // slots of this CTA):
@@ -30,7 +33,12 @@
 // operation order as the per-kernel engine, so both engines give identical
 // hidden states, bit for bit (tests/test_decode_gpu.py checks it).
 //
-// Waits: every spin on an arrival counter and every bulk-copy barrier wait is
+// Buffer reuse: a phase overwrites a tagged buffer only after every reader of
+// its previous contents has finished, which the data dependencies guarantee
+// (e.g. q|k|v of layer l + 1 needs hidden after layer l's ffn_down, which needs
+// h from every CTA, each of which computed it after its layer-l attention).
+//
+// Waits: every poll of tagged values and every bulk-copy barrier wait is
 // bounded (tmac_set_wait_limit_ns); on expiry the kernel records
 // TMAC_ERR_TIMEOUT, raises an abort flag that the other CTAs' waits see, waits
 // (bounded) for its own copies in flight and returns.
@@ -50,8 +58,6 @@ constexpr int kMegaThreads = 768;
 constexpr int kMegaWarps = kMegaThreads / 32;
 constexpr int kSlots = 4;  // weight slots: q|k|v, attn_output, gate|up, ffn_down
 constexpr int kMaxSeg = 6;
-constexpr int kPhases = 5;  // arrival counters per layer
-enum : uint32_t { PH_QKV = 0, PH_ATTN = 1, PH_O = 2, PH_GU = 3, PH_DOWN = 4 };
 enum : uint32_t { SK_NONE = 0, SK_Q5 = 1, SK_Q8 = 2, SK_Q4K = 3, SK_Q6K = 4 };
 constexpr size_t kMaxSmemBytes = 227 * 1024;
 
@@ -75,8 +81,6 @@ static_assert(sizeof(MegaSlot) % 16 == 0, "slots are bulk-copied");
 struct MegaLayer {
     const float *attn_norm, *ffn_norm, *bq, *bk, *bv;
     float *kc, *vc;
-    uint32_t expect[kPhases];  // CTAs that signal each phase
-    uint32_t pad;
 };
 
 struct MegaArgs {
@@ -90,11 +94,14 @@ struct MegaArgs {
     int* tokens;
     int* pos_dev;
     int n_prompt;
-    float *hidden, *qkv, *ctx, *hbuf, *xn, *hidden_log;
+    float *hidden, *xn, *hidden_log;
     const float *rope_c, *rope_s, *out_norm;
-    unsigned* counters;  // [kLayers][kPhases], then the abort flag, then partmax[grid]; zeroed per launch
-    int* abort_flag;
-    float* partmax;
+    // Activations handed between CTAs, each value stored with the tag of the
+    // phase that wrote it (tag << 32 | float bits, one 8-byte store): a reader
+    // polls the values it needs until their tags are the expected ones.
+    unsigned long long *hid_t, *qkv_t, *ctx_t, *h_t, *pm_t;
+    uint32_t epoch;  // this launch's tag base (128 tags per launch)
+    int* abort_flag;  // zeroed per launch
     int* err;
     int max_seq;
     int head_cta0;
@@ -112,34 +119,104 @@ struct MegaMisc {
     AttnShared attn;
 };
 
-// --------------------------------------------------------------- sync bits --
-TMAC_DEV uint32_t ld_acquire_gpu(const unsigned* p)
+// --------------------------------------------------------- tagged values --
+// Tags of one launch: EMB for the embedding in hidden, then five per layer.
+enum : uint32_t { TG_QKV = 0, TG_CTX = 1, TG_HID_C = 2, TG_H = 3, TG_HID_E = 4 };
+TMAC_DEV uint32_t tag_of(uint32_t epoch, int l, uint32_t ph) { return epoch * 128u + 1u + (uint32_t)l * 5u + ph; }
+TMAC_DEV uint32_t tag_emb(uint32_t epoch) { return epoch * 128u; }
+
+// One value with its tag, as one single-copy-atomic 8-byte store at L2.
+TMAC_DEV void st_tagged(unsigned long long* p, float v, uint32_t tag)
 {
-    uint32_t v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
+    const unsigned long long u = ((unsigned long long)tag << 32) | __float_as_uint(v);
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(u) : "memory");
 }
-TMAC_DEV void red_release_gpu(unsigned* p)
+TMAC_DEV unsigned long long ld_tagged(const unsigned long long* p)
 {
-    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(p) : "memory");
+    unsigned long long u;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(u) : "l"(p) : "memory");
+    return u;
 }
 
-// Thread 0: wait until *cnt >= target (bounded; false on timeout or abort).
-TMAC_DEV bool grid_wait(const unsigned* cnt, unsigned target, int* abort_g, int* err)
+// One more value a thread waits for beside its share of the main array:
+// thread tid < n takes src[tid] once its tag equals `tag`.
+struct PollExtra {
+    const unsigned long long* src = nullptr;
+    int n = 0;
+    uint32_t tag = 0;
+    float* out = nullptr;
+};
+
+// All threads: r[k] = value src[tid + k * kMegaThreads] (k < K, index < n) once
+// its tag equals `tag`, and the extras likewise, all in the same polling loop
+// (one L2 round trip when everything is already there).  Bounded: false (and
+// ms.abort) on timeout or another CTA's abort.
+template <int K>
+TMAC_DEV bool poll_regs(const unsigned long long* src, int n, uint32_t tag, float (&r)[K], MegaMisc& ms,
+                        int* abort_g, int* err, PollExtra e0 = PollExtra(), PollExtra e1 = PollExtra())
 {
-    if (ld_acquire_gpu(cnt) >= target) return true;
-    const uint64_t t0 = global_timer_ns();
-    for (uint32_t it = 1;; it++) {
-        if (ld_acquire_gpu(cnt) >= target) return true;
-        if ((it & 31u) == 0) {
-            if (*(volatile int*)abort_g) return false;
-            if (global_timer_ns() - t0 > wait_limit_ns()) {
-                if (err) atomicExch(err, (int)TMAC_ERR_TIMEOUT);
-                atomicExch(abort_g, 1);
-                return false;
+    const int tid = threadIdx.x;
+    uint32_t todo = 0;
+#pragma unroll
+    for (int k = 0; k < K; k++)
+        if (tid + k * kMegaThreads < n) todo |= 1u << k;
+    if (tid < e0.n) todo |= 1u << 30;
+    if (tid < e1.n) todo |= 1u << 31;
+    uint64_t t0 = 0;
+    for (uint32_t it = 0;; it++) {
+#pragma unroll
+        for (int k = 0; k < K; k++) {
+            if (todo & (1u << k)) {
+                const unsigned long long u = ld_tagged(src + tid + k * kMegaThreads);
+                if ((uint32_t)(u >> 32) == tag) {
+                    r[k] = __uint_as_float((uint32_t)u);
+                    todo &= ~(1u << k);
+                }
             }
         }
+        if (todo & (1u << 30)) {
+            const unsigned long long u = ld_tagged(e0.src + tid);
+            if ((uint32_t)(u >> 32) == e0.tag) {
+                *e0.out = __uint_as_float((uint32_t)u);
+                todo &= ~(1u << 30);
+            }
+        }
+        if (todo & (1u << 31)) {
+            const unsigned long long u = ld_tagged(e1.src + tid);
+            if ((uint32_t)(u >> 32) == e1.tag) {
+                *e1.out = __uint_as_float((uint32_t)u);
+                todo &= ~(1u << 31);
+            }
+        }
+        if (__syncthreads_and(todo == 0)) return true;
+        if ((it & 15u) == 15u) {
+            if (tid == 0) {
+                if (t0 == 0) t0 = global_timer_ns();
+                if (*(volatile int*)abort_g) {
+                    ms.abort = 1;
+                } else if (global_timer_ns() - t0 > wait_limit_ns()) {
+                    if (err) atomicExch(err, (int)TMAC_ERR_TIMEOUT);
+                    atomicExch(abort_g, 1);
+                    ms.abort = 1;
+                }
+            }
+            __syncthreads();
+            if (ms.abort) return false;
+        }
     }
+}
+
+// All threads: dst[i] = value of src[i] for i < n (n <= kMegaThreads * 2),
+// waiting for `tag` as poll_regs.
+TMAC_DEV bool poll_smem(const unsigned long long* src, int n, uint32_t tag, float* dst, MegaMisc& ms, int* abort_g,
+                        int* err)
+{
+    float r[2];
+    if (!poll_regs<2>(src, n, tag, r, ms, abort_g, err)) return false;
+    for (int k = 0; k < 2; k++)
+        if (threadIdx.x + k * kMegaThreads < n) dst[threadIdx.x + k * kMegaThreads] = r[k];
+    __syncthreads();
+    return true;
 }
 
 // Thread 0: the copies of one slot for one layer.
@@ -285,29 +362,17 @@ TMAC_DEV void mega_norm_quantize(float* xv, float* sq, const float* __restrict__
     __syncthreads();
 }
 
-// x_q of v[0..n) (global, written by other CTAs) with x_scale from the maximum
-// of |v| and of extra[0..n_extra) (tmac_gguf.cpp:889-896).  Every value is
-// loaded once into registers, so the phase pays one round trip to L2 for its
-// activations.
+// x_q of the values r[k] (index tid + k * kMegaThreads < n) with x_scale from
+// max_abs (tmac_gguf.cpp:889-896); planes xpl[0..n) high, [n..2n) low.
 constexpr int kMaxQuant = 7;
-TMAC_DEV void mega_quantize(const float* v, int n, const float* extra, int n_extra, uint8_t* xpl, MegaMisc& ms)
+template <int K>
+TMAC_DEV void mega_quantize(const float (&r)[K], int n, float max_abs, uint8_t* xpl, MegaMisc& ms)
 {
     const int tid = threadIdx.x;
-    float r[kMaxQuant];
-    float mx = 0.0f;
-#pragma unroll
-    for (int k = 0; k < kMaxQuant; k++) {
-        const int i = tid + k * kMegaThreads;
-        r[k] = i < n ? __ldcg(v + i) : 0.0f;
-    }
-    for (int i = tid; i < n_extra; i += kMegaThreads) mx = fmaxf(mx, __ldcg(extra + i));
-#pragma unroll
-    for (int k = 0; k < kMaxQuant; k++) mx = fmaxf(mx, fabsf(r[k]));
-    mx = block_max(mx, ms.red, kMegaThreads);
-    const float s = x_scale_from_max(mx);
+    const float s = x_scale_from_max(max_abs);
     if (tid == 0) ms.xs = s;
 #pragma unroll
-    for (int k = 0; k < kMaxQuant; k++) {
+    for (int k = 0; k < K; k++) {
         const int i = tid + k * kMegaThreads;
         if (i < n) {
             const int16_t q = quantize_one(r[k], s);
@@ -405,7 +470,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaArgs a
     }
     __syncthreads();
     const int pos = ms.pos;
-    unsigned* cnt = a.counters;
+    const uint32_t ep = a.epoch;
 
     // A wait that failed anywhere ends the token: drain this CTA's copies, return.
     auto drain = [&]() {
@@ -426,12 +491,6 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaArgs a
         if (!go && tid == 0) atomicExch(a.abort_flag, 1);
         return go;
     };
-    // Thread 0 waits for a phase's arrivals; everyone learns the outcome.
-    auto wait_phase = [&](int l, int ph, unsigned target) -> bool {
-        if (tid == 0 && !grid_wait(&cnt[l * kPhases + ph], target, a.abort_flag, a.err)) ms.abort = 1;
-        __syncthreads();
-        return !ms.abort;
-    };
     // Thread 0: fill `slot` with layer l + 1's weights once its layer-l use is
     // over -- whether or not this CTA had layer-l work in it (the splits differ
     // between layers, e.g. q|k|v of the Q5_0 and the Q8_0 layers).
@@ -439,10 +498,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaArgs a
         if (tid == 0 && l + 1 < kLayers && ms.armed[slot] == ms.waited[slot])
             issue_slot(plans[(l + 1) * kSlots + slot], slot_base[slot], ms, slot);
     };
-    // End of a phase: arrive, then refill the phase's slot.
-    auto finish = [&](int l, int ph, int slot) {
+    // End of a phase: every value is stored; refill the phase's slot.
+    auto finish = [&](int l, int slot) {
         __syncthreads();
-        if (tid == 0) red_release_gpu(&cnt[l * kPhases + ph]);
         if (slot >= 0) refill(l, slot);
     };
 
@@ -464,14 +522,13 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaArgs a
                     const uint8_t* b = a.emb + (idx / 32) * 34;
                     const float v = __fmul_rn((float)(int8_t)b[2 + idx % 32], f16_bits_to_f32(ld_u16_unaligned(b)));
                     xv[i] = v;
-                    if (cta == a.emb_cta) a.hidden[i] = v;
+                    if (cta == a.emb_cta) st_tagged(a.hid_t + i, v, tag_emb(ep));
                 }
+                __syncthreads();
             } else {
-                if (!wait_phase(l - 1, PH_DOWN, __ldg(&a.layers[l - 1].expect[PH_DOWN]))) break;
+                if (!poll_smem(a.hid_t, kHidden, tag_of(ep, l - 1, TG_HID_E), xv, ms, a.abort_flag, a.err)) break;
                 MEGA_STAMP(l, 1);
-                for (int i = tid; i < kHidden; i += kMegaThreads) xv[i] = __ldcg(a.hidden + i);
             }
-            __syncthreads();
             mega_norm_quantize(xv, sq, L.attn_norm, kHidden, xpl, ms, MEGA_NORM_STAMPS(l));
             if (pa.kind == SK_Q8) mega_block_sums(xpl, kHidden, ms.sx);
             MEGA_STAMP(l, 2);
@@ -479,8 +536,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaArgs a
             MEGA_STAMP(l, 3);
             if (pa.kind == SK_Q8) mega_q8(slot_base[0], kHidden, xpl, ms.sx, ms.xs, tsum, yv);
             else mega_blockq<TMAC_TYPE_Q5_0>(slot_base[0], pa, kHidden, xpl, ms.xs, acc_lo, acc_hi, yv);
-            for (int t = tid; t < (int)pa.rows; t += kMegaThreads) a.qkv[pa.out0[0] + t] = yv[t];
-            finish(l, PH_QKV, 0);
+            for (int t = tid; t < (int)pa.rows; t += kMegaThreads)
+                st_tagged(a.qkv_t + pa.out0[0] + t, yv[t], tag_of(ep, l, TG_QKV));
+            finish(l, 0);
             MEGA_STAMP(l, 4);
         } else {
             refill(l, 0);
@@ -491,30 +549,82 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaArgs a
             // earlier positions' K / V rows do not depend on this step: their
             // copies overlap the wait for q|k|v
             if (tid < kAttnThreads) attention_prefetch(h, L.kc, L.vc, pos, a.max_seq, att);
-            if (!wait_phase(l, PH_QKV, __ldg(&L.expect[PH_QKV]))) break;
+            // the head's q, its KV head's k and v (192 values) into sq
+            const int kvh = h / (kHeads / kKvHeads);
+            float r[1];
+            const int src = tid < kHeadDim ? h * kHeadDim + tid
+                                           : (tid < 2 * kHeadDim ? kHidden + kvh * kHeadDim + tid - kHeadDim
+                                                                 : kHidden + kKvDim + kvh * kHeadDim + tid - 2 * kHeadDim);
+            r[0] = 0.0f;
+            {
+                const int n = tid < 3 * kHeadDim ? 1 : 0;  // threads 0..191 each wait for one value
+                uint32_t todo = n;
+                uint64_t t0 = 0;
+                bool ok = true;
+                for (uint32_t it = 0;; it++) {
+                    if (todo) {
+                        const unsigned long long u = ld_tagged(a.qkv_t + src);
+                        if ((uint32_t)(u >> 32) == tag_of(ep, l, TG_QKV)) {
+                            r[0] = __uint_as_float((uint32_t)u);
+                            todo = 0;
+                        }
+                    }
+                    if (__syncthreads_and(todo == 0)) break;
+                    if ((it & 15u) == 15u) {
+                        if (tid == 0) {
+                            if (t0 == 0) t0 = global_timer_ns();
+                            if (*(volatile int*)a.abort_flag) {
+                                ms.abort = 1;
+                            } else if (global_timer_ns() - t0 > wait_limit_ns()) {
+                                atomicExch(a.err, (int)TMAC_ERR_TIMEOUT);
+                                atomicExch(a.abort_flag, 1);
+                                ms.abort = 1;
+                            }
+                        }
+                        __syncthreads();
+                        if (ms.abort) {
+                            ok = false;
+                            break;
+                        }
+                    }
+                }
+                if (!ok) break;
+            }
+            if (tid < 3 * kHeadDim) sq[tid] = r[0];
+            __syncthreads();
             MEGA_STAMP(l, 5);
             if (tid < kAttnThreads)
-                attention_head(h, a.qkv, a.qkv + kHidden, a.qkv + kHidden + kKvDim, L.bq, L.bk, L.bv, a.rope_c,
-                               a.rope_s, pos, L.kc, L.vc, a.ctx, a.max_seq, att, ms.attn, 1, MEGA_ATT_STAMPS(h, l));
+                attention_head(h, sq, sq + kHeadDim, sq + 2 * kHeadDim, L.bq, L.bk, L.bv, a.rope_c, a.rope_s, pos,
+                               L.kc, L.vc, sq + 3 * kHeadDim, a.max_seq, att, ms.attn, 1, MEGA_ATT_STAMPS(h, l));
+            __syncthreads();
+            if (tid < kHeadDim) st_tagged(a.ctx_t + h * kHeadDim + tid, sq[3 * kHeadDim + tid], tag_of(ep, l, TG_CTX));
             MEGA_STAMP(l, 23);
-            finish(l, PH_ATTN, -1);
+            finish(l, -1);
             MEGA_STAMP(l, 6);
         }
         // ------------------------------------------------ C: attn_output + residual
         const MegaSlot& pc = plans[l * kSlots + 1];
         if (pc.kind != SK_NONE) {
-            if (!wait_phase(l, PH_ATTN, kHeads)) break;
+            // ctx, and this CTA's rows of hidden for the residual, in one polling loop
+            float r[2], hres = 0.0f;
+            PollExtra ex;
+            ex.src = a.hid_t + pc.out0[0];
+            ex.n = (int)pc.rows;
+            ex.tag = l == 0 ? tag_emb(ep) : tag_of(ep, l - 1, TG_HID_E);
+            ex.out = &hres;
+            if (!poll_regs<2>(a.ctx_t, kHidden, tag_of(ep, l, TG_CTX), r, ms, a.abort_flag, a.err, ex)) break;
             MEGA_STAMP(l, 7);
-            // this CTA's rows of hidden, loaded together with ctx (one round trip)
-            const float hres = tid < (int)pc.rows ? __ldcg(a.hidden + pc.out0[0] + tid) : 0.0f;
-            mega_quantize(a.ctx, kHidden, nullptr, 0, xpl, ms);
+            float mx = fmaxf(fabsf(r[0]), tid + kMegaThreads < kHidden ? fabsf(r[1]) : 0.0f);
+            mx = block_max(mx, ms.red, kMegaThreads);
+            mega_quantize<2>(r, kHidden, mx, xpl, ms);
             MEGA_STAMP(l, 8);
             if (!wait_slot(1)) break;
             MEGA_STAMP(l, 21);
             mega_blockq<TMAC_TYPE_Q5_0>(slot_base[1], pc, kHidden, xpl, ms.xs, acc_lo, acc_hi, yv);
             MEGA_STAMP(l, 22);
-            if (tid < (int)pc.rows) a.hidden[pc.out0[0] + tid] = __fadd_rn(hres, yv[tid]);
-            finish(l, PH_O, 1);
+            if (tid < (int)pc.rows)
+                st_tagged(a.hid_t + pc.out0[0] + tid, __fadd_rn(hres, yv[tid]), tag_of(ep, l, TG_HID_C));
+            finish(l, 1);
             MEGA_STAMP(l, 9);
         } else {
             refill(l, 1);
@@ -522,10 +632,8 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaArgs a
         // ------------------------------------------------ D: gate|up + silu
         const MegaSlot& pd = plans[l * kSlots + 2];
         if (pd.kind != SK_NONE) {
-            if (!wait_phase(l, PH_O, __ldg(&L.expect[PH_O]))) break;
+            if (!poll_smem(a.hid_t, kHidden, tag_of(ep, l, TG_HID_C), xv, ms, a.abort_flag, a.err)) break;
             MEGA_STAMP(l, 10);
-            for (int i = tid; i < kHidden; i += kMegaThreads) xv[i] = __ldcg(a.hidden + i);
-            __syncthreads();
             mega_norm_quantize(xv, sq, L.ffn_norm, kHidden, xpl, ms);
             MEGA_STAMP(l, 11);
             if (!wait_slot(2)) break;
@@ -535,12 +643,12 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaArgs a
             float mx = 0.0f;
             for (int t = tid; t < n; t += kMegaThreads) {
                 const float v = silu_mul(yv[t], yv[n + t]);
-                a.hbuf[pd.out0[0] + t] = v;
+                st_tagged(a.h_t + pd.out0[0] + t, v, tag_of(ep, l, TG_H));
                 mx = fmaxf(mx, fabsf(v));
             }
             mx = block_max(mx, ms.red, kMegaThreads);
-            if (tid == 0) a.partmax[cta] = mx;
-            finish(l, PH_GU, 2);
+            if (tid == 0) st_tagged(a.pm_t + cta, mx, tag_of(ep, l, TG_H));
+            finish(l, 2);
             MEGA_STAMP(l, 13);
         } else {
             refill(l, 2);
@@ -548,12 +656,23 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaArgs a
         // ------------------------------------------------ E: ffn_down + residual
         const MegaSlot& pe = plans[l * kSlots + 3];
         if (pe.kind != SK_NONE) {
-            // hidden is final since the attn_output phase this CTA waited for in
-            // D (every CTA has gate|up rows): read this CTA's rows before the wait
-            const float hres = tid < (int)pe.rows ? __ldcg(a.hidden + pe.out0[0] + tid) : 0.0f;
-            if (!wait_phase(l, PH_GU, __ldg(&L.expect[PH_GU]))) break;
+            // h, the per-CTA maxima and this CTA's rows of hidden, in one polling loop
+            float r[kMaxQuant], pm = 0.0f, hres = 0.0f;
+            PollExtra ex0, ex1;
+            ex0.src = a.pm_t;
+            ex0.n = (int)gridDim.x;
+            ex0.tag = tag_of(ep, l, TG_H);
+            ex0.out = &pm;
+            ex1.src = a.hid_t + pe.out0[0];
+            ex1.n = (int)pe.rows;
+            ex1.tag = tag_of(ep, l, TG_HID_C);
+            ex1.out = &hres;
+            if (!poll_regs<kMaxQuant>(a.h_t, kInter, tag_of(ep, l, TG_H), r, ms, a.abort_flag, a.err, ex0, ex1)) break;
             MEGA_STAMP(l, 14);
-            mega_quantize(a.hbuf, kInter, a.partmax, (int)gridDim.x, xpl, ms);
+            // x_scale from the maximum of the per-CTA maxima (every CTA has gate|up rows)
+            float mx = tid < (int)gridDim.x ? pm : 0.0f;
+            mx = block_max(mx, ms.red, kMegaThreads);
+            mega_quantize<kMaxQuant>(r, kInter, mx, xpl, ms);
             MEGA_STAMP(l, 15);
             if (!wait_slot(3)) break;
             MEGA_STAMP(l, 19);
@@ -562,8 +681,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaArgs a
             else
                 mega_blockq<TMAC_TYPE_Q4_K>(slot_base[3], pe, kInter, xpl, ms.xs, acc_lo, acc_hi, yv);
             MEGA_STAMP(l, 20);
-            if (tid < (int)pe.rows) a.hidden[pe.out0[0] + tid] = __fadd_rn(hres, yv[tid]);
-            finish(l, PH_DOWN, 3);
+            if (tid < (int)pe.rows)
+                st_tagged(a.hid_t + pe.out0[0] + tid, __fadd_rn(hres, yv[tid]), tag_of(ep, l, TG_HID_E));
+            finish(l, 3);
             MEGA_STAMP(l, 16);
         } else {
             refill(l, 3);
@@ -573,19 +693,17 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaArgs a
         drain();
         return;
     }
-    // ---- end of the token (CTA 0): hidden log, output_norm for the logits GEMV,
-    // next position, key cleared for the next step's top-1
+    // ---- end of the token (CTA 0): hidden state and its log, output_norm for
+    // the logits GEMV, next position, key cleared for the next step's top-1
     if (cta == 0) {
-        if (!wait_phase(kLayers - 1, PH_DOWN, __ldg(&a.layers[kLayers - 1].expect[PH_DOWN]))) {
+        if (!poll_smem(a.hid_t, kHidden, tag_of(ep, kLayers - 1, TG_HID_E), xv, ms, a.abort_flag, a.err)) {
             drain();
             return;
         }
         for (int i = tid; i < kHidden; i += kMegaThreads) {
-            const float v = __ldcg(a.hidden + i);
-            xv[i] = v;
-            a.hidden_log[(int64_t)pos * kHidden + i] = v;
+            a.hidden[i] = xv[i];
+            a.hidden_log[(int64_t)pos * kHidden + i] = xv[i];
         }
-        __syncthreads();
         if (a.out_norm) {
             for (int i = tid; i < kHidden; i += kMegaThreads) sq[i] = __fmul_rn(xv[i], xv[i]);
             __syncthreads();
@@ -621,8 +739,9 @@ struct MegaState {
     int grid = 0;
     void* dev_layers = nullptr;
     void* dev_slots = nullptr;
-    unsigned* dev_zero = nullptr;  // counters | abort flag | partmax
-    size_t zero_bytes = 0;
+    int* dev_abort = nullptr;                // cleared before every launch
+    unsigned long long* dev_tagged = nullptr;  // hidden | q|k|v | ctx | h | per-CTA max |h|
+    uint32_t epoch = 0;                        // tag base of the last launch
 };
 
 namespace {
@@ -702,7 +821,8 @@ void mega_free(MegaState* st)
     if (!st) return;
     if (st->dev_layers) cudaFree(st->dev_layers);
     if (st->dev_slots) cudaFree(st->dev_slots);
-    if (st->dev_zero) cudaFree(st->dev_zero);
+    if (st->dev_abort) cudaFree(st->dev_abort);
+    if (st->dev_tagged) cudaFree(st->dev_tagged);
     delete st;
 }
 
@@ -750,7 +870,6 @@ int mega_prepare(tmac_model_s* m, MegaState** out)
             !native_blockq(gu, TMAC_TYPE_Q5_0, 2 * kInter, kHidden) ||
             !(native_blockq(wd, TMAC_TYPE_Q4_K, kHidden, kInter) || native_blockq(wd, TMAC_TYPE_Q6_K, kHidden, kInter)))
             return TMAC_OK;
-        uint32_t expect[kPhases] = {0, (uint32_t)kHeads, 0, 0, 0};
         int rc;
         if ((rc = host_exc_ptr(q5_layer ? qkv : qk, ep_a)) || (rc = host_exc_ptr(wo, ep_o)) ||
             (rc = host_exc_ptr(gu, ep_g)) || (rc = host_exc_ptr(wd, ep_d)))
@@ -798,14 +917,11 @@ int mega_prepare(tmac_model_s* m, MegaState** out)
             o0[0] = (int32_t)(8 * a0[0]);
             if ((rc = blockq_slot(wd, ep_d, a0, a1, o0, 1, sp[3]))) return rc;
             if (sp[2].kind == SK_NONE) return TMAC_OK;  // phase E relies on every CTA taking part in D
-            const uint32_t phases[kSlots] = {PH_QKV, PH_O, PH_GU, PH_DOWN};
             for (int s = 0; s < kSlots; s++) {
-                if (sp[s].kind != SK_NONE) expect[phases[s]]++;
                 slot_bytes[s] = std::max(slot_bytes[s], (sp[s].total + 127) / 128 * 128);
                 max_rows = std::max(max_rows, sp[s].rows);
             }
         }
-        memcpy(L.expect, expect, sizeof(expect));
     }
     // shared-memory layout
     MegaArgs a{};
@@ -840,15 +956,16 @@ int mega_prepare(tmac_model_s* m, MegaState** out)
     MegaState* st = new MegaState();
     st->smem = off;
     st->grid = G;
-    st->zero_bytes = ((size_t)kLayers * kPhases + 1 + G) * sizeof(unsigned);
+    const size_t n_tagged = (size_t)kHidden + kHidden + 2 * kKvDim + kHidden + kInter + G;
     cudaError_t e = cudaMalloc(&st->dev_layers, layers.size() * sizeof(MegaLayer));
     if (e == cudaSuccess) e = cudaMalloc(&st->dev_slots, slots.size() * sizeof(MegaSlot));
-    if (e == cudaSuccess) e = cudaMalloc(&st->dev_zero, st->zero_bytes);
+    if (e == cudaSuccess) e = cudaMalloc(&st->dev_abort, sizeof(int));
+    if (e == cudaSuccess) e = cudaMalloc(&st->dev_tagged, n_tagged * sizeof(unsigned long long));
     if (e == cudaSuccess)
         e = cudaMemcpy(st->dev_layers, layers.data(), layers.size() * sizeof(MegaLayer), cudaMemcpyHostToDevice);
     if (e == cudaSuccess)
         e = cudaMemcpy(st->dev_slots, slots.data(), slots.size() * sizeof(MegaSlot), cudaMemcpyHostToDevice);
-    if (e == cudaSuccess) e = cudaMemset(st->dev_zero, 0, st->zero_bytes);
+    if (e == cudaSuccess) e = cudaMemset(st->dev_tagged, 0, n_tagged * sizeof(unsigned long long));  // tag 0: never current
     if (e != cudaSuccess) {
         mega_free(st);
         return cuda_fail(e, "decode kernel set-up");
@@ -861,17 +978,17 @@ int mega_prepare(tmac_model_s* m, MegaState** out)
     a.tokens = m->tokens;
     a.pos_dev = m->pos_dev;
     a.hidden = m->hidden;
-    a.qkv = m->q;
-    a.ctx = m->ctx;
-    a.hbuf = m->gate;
     a.xn = m->xn;
     a.hidden_log = m->hidden_log;
     a.rope_c = m->rope_c;
     a.rope_s = m->rope_s;
     a.out_norm = vec_or_null(m, "output_norm.weight");
-    a.counters = st->dev_zero;
-    a.abort_flag = reinterpret_cast<int*>(st->dev_zero + kLayers * kPhases);
-    a.partmax = reinterpret_cast<float*>(st->dev_zero + kLayers * kPhases + 1);
+    a.abort_flag = st->dev_abort;
+    a.hid_t = st->dev_tagged;
+    a.qkv_t = a.hid_t + kHidden;
+    a.ctx_t = a.qkv_t + kHidden + 2 * kKvDim;
+    a.h_t = a.ctx_t + kHidden;
+    a.pm_t = a.h_t + kInter;
     a.err = device_error_word(m->device);
     a.max_seq = m->max_seq;
     a.head_cta0 = G - kHeads;
@@ -885,13 +1002,18 @@ int mega_prepare(tmac_model_s* m, MegaState** out)
     return TMAC_OK;
 }
 
-// One token: counters cleared, then the persistent kernel (cooperative launch,
+// One token: abort flag cleared, then the persistent kernel (cooperative launch,
 // so every CTA is resident before any waits on another).
 int mega_launch(MegaState* st, int n_prompt, cudaStream_t s)
 {
-    TMAC_CUDA_TRY(cudaMemsetAsync(st->dev_zero, 0, st->zero_bytes, s));
+    TMAC_CUDA_TRY(cudaMemsetAsync(st->dev_abort, 0, sizeof(int), s));
     MegaArgs a = st->args;
     a.n_prompt = n_prompt;
+    // tags of this launch: values of earlier launches never match them (the
+    // 25-bit epoch wraps after 2^25 tokens, long after any value is rewritten)
+    st->epoch = (st->epoch + 1) & 0x1FFFFFFu;
+    if (st->epoch == 0) st->epoch = 1;
+    a.epoch = st->epoch;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(st->grid);
     cfg.blockDim = dim3(kMegaThreads);

@@ -92,14 +92,15 @@ TMAC_DEV void attention_prefetch(int h, const float* __restrict__ kc, const floa
 // sum in position order, log-sum-exp weights, context accumulated in position
 // order.  The current position's k/v come from shared memory, so the append
 // needs no ordering against the other heads.  `sc` holds
-// attn_scratch_bytes(nscore).  Activations and KV rows past the prefetched
-// chunk are read at L2 (ld.global.cg): other CTAs of a persistent kernel write
-// them while this CTA may hold older copies in L1.  stamps (diagnostics only):
-// 8 %globaltimer values of the steps, or nullptr.
-TMAC_DEV void attention_head(int h, const float* __restrict__ q, const float* __restrict__ k,
-                             const float* __restrict__ v, const float* __restrict__ bq, const float* __restrict__ bk,
+// attn_scratch_bytes(nscore).  q_head / k_head / v_head: the head's 64 q values
+// and its KV head's k and v (global or shared memory); ctx_head: its 64 context
+// outputs.  KV rows past the prefetched chunk are read at L2 (ld.global.cg):
+// other CTAs of a persistent kernel write them while this CTA may hold older
+// copies in L1.  stamps (diagnostics only): 8 %globaltimer values, or nullptr.
+TMAC_DEV void attention_head(int h, const float* q_head, const float* k_head, const float* v_head,
+                             const float* __restrict__ bq, const float* __restrict__ bk,
                              const float* __restrict__ bv, const float* __restrict__ cs, const float* __restrict__ sn,
-                             int pos, float* __restrict__ kc, float* __restrict__ vc, float* __restrict__ ctx,
+                             int pos, float* __restrict__ kc, float* __restrict__ vc, float* ctx_head,
                              int nscore, float* sc, AttnShared& sh, int bar, unsigned long long* stamps = nullptr)
 {
 #define ATT_STAMP(i)                                                  \
@@ -117,15 +118,15 @@ TMAC_DEV void attention_head(int h, const float* __restrict__ q, const float* __
     if (tid < kHeadDim) {  // thread j: pair j/2 of q (j even) or of k (j odd)
         const int j = tid, pr = j >> 1, d = 2 * pr;
         const bool isk = j & 1;
-        const float* vec = isk ? k + kvh * kHeadDim : q + h * kHeadDim;
+        const float* vec = isk ? k_head : q_head;
         const float* b = isk ? (bk ? bk + kvh * kHeadDim : nullptr) : (bq ? bq + h * kHeadDim : nullptr);
-        const float x0 = __fadd_rn(__ldcg(vec + d), b ? b[d] : 0.0f), x1 = __fadd_rn(__ldcg(vec + d + 1), b ? b[d + 1] : 0.0f);
+        const float x0 = __fadd_rn(vec[d], b ? b[d] : 0.0f), x1 = __fadd_rn(vec[d + 1], b ? b[d + 1] : 0.0f);
         const float y0 = __fsub_rn(__fmul_rn(x0, c[pr]), __fmul_rn(x1, sv[pr]));
         const float y1 = __fadd_rn(__fmul_rn(x0, sv[pr]), __fmul_rn(x1, c[pr]));
         float* dst = isk ? sh.k : sh.q;
         dst[d] = y0;
         dst[d + 1] = y1;
-        sh.v[j] = __fadd_rn(__ldcg(v + kvh * kHeadDim + j), bv ? bv[kvh * kHeadDim + j] : 0.0f);
+        sh.v[j] = __fadd_rn(v_head[j], bv ? bv[kvh * kHeadDim + j] : 0.0f);
     }
     cp_async_wait_all();  // the prefetched K / V rows of positions [0, min(pos, 64))
     named_bar_sync(bar, kAttnThreads);
@@ -191,7 +192,7 @@ TMAC_DEV void attention_head(int h, const float* __restrict__ q, const float* __
         if (tid < kHeadDim)
             for (int r = 0; r < rows; r++) a = __fadd_rn(a, __fmul_rn(sc[c0 + r], vb[r * kAttnStride + tid]));
     }
-    if (tid < kHeadDim) ctx[h * kHeadDim + tid] = a;
+    if (tid < kHeadDim) ctx_head[tid] = a;
     ATT_STAMP(7);
 #undef ATT_STAMP
 }
