@@ -343,8 +343,10 @@ def model_extras(world=1, rank=0):
                                "bytes": f"{fwd} forwards x {LAYER_BYTES} B of layer weights + {n} x "
                                         f"{LOGITS_BYTES} B of logits weights + KV reads 24576 B x (pos + 1)"},
                   "tokens_match_reference": bool(np.array_equal(toks, ref)),
+                  "engine": {1: "persistent kernel (one cooperative launch per token) + logits GEMV",
+                             0: "per-kernel engine (CUDA graphs)"}.get(m.decode_engine(), "unknown"),
                   "config": "Qwen2-0.5B-shaped decode: 24 layers, mixed Q5_0/Q8_0/Q4_K/Q6_K, 512-slot KV, "
-                            "greedy, CUDA graphs",
+                            "greedy",
                   "api": "tmac_model_generate"}
     rng = np.random.default_rng(0)
     ptoks = rng.integers(0, VOCAB, size=(64, 512)).astype(np.int32)

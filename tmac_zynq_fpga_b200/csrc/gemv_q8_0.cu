@@ -360,10 +360,10 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemv_kernel(Q8Args a)
         const int s0 = i % L.stages, b0 = i % kAccBufs;
         const int s1 = (i + 1) % L.stages, b1 = (i + 1) % kAccBufs;
         if (*abort_flag || !mbar_wait_sleep(&full[s0], (i / L.stages) & 1, a.err) ||
-            (i >= kAccBufs && !mbar_wait_bounded(&acc_empty[b0], ((i / kAccBufs) & 1) ^ 1, a.err)) ||
+            (i >= kAccBufs && !mbar_wait_sleep(&acc_empty[b0], ((i / kAccBufs) & 1) ^ 1, a.err)) ||
             (two && (!mbar_wait_sleep(&full[s1], ((i + 1) / L.stages) & 1, a.err) ||
                      (i + 1 >= kAccBufs &&
-                      !mbar_wait_bounded(&acc_empty[b1], (((i + 1) / kAccBufs) & 1) ^ 1, a.err))))) {
+                      !mbar_wait_sleep(&acc_empty[b1], (((i + 1) / kAccBufs) & 1) ^ 1, a.err))))) {
             *abort_flag = 1;
             break;
         }
