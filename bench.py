@@ -503,8 +503,9 @@ def main():
     ap.add_argument("--no-pdl", action="store_true",
                     help="launch each step's kernel after the previous one ends (no programmatic dependent launch)")
     ap.add_argument("--full-logits", action="store_true",
-                    help="N > 1: every step also all-gathers the logits shards (NCCL) so each rank holds the "
-                         "whole vector, as get_logits_q8 returns it")
+                    help="N > 1: every rank also ends each step with the whole logits vector, as "
+                         "get_logits_q8 returns it: stored over NVLink by the GEMV itself with the fused "
+                         "exchange, else an NCCL all-gather")
     ap.add_argument("--collective", choices=["fused", "peer", "nccl"], default="fused",
                     help="top-1 merge across ranks: inside the logits GEMV over NVLink peer memory, "
                          "a separate peer-memory exchange kernel, or an NCCL all-reduce")
@@ -553,7 +554,9 @@ def main():
         if args.collective in ("fused", "peer"):
             from tmac_zynq_fpga_b200 import shard
             try:
-                xchg = shard.PeerTop1(local)
+                # --full-logits with the fused exchange: the GEMV also stores its rows
+                # into every rank's full-logits vector over NVLink (no NCCL all-gather)
+                xchg = shard.PeerTop1(local, vocab=VOCAB if (args.full_logits and args.collective == "fused") else 0)
                 weights[0].gemv_top1(x, y, key, index_base=r0, stream=stream)
                 ref = key.clone()
                 dist.all_reduce(ref, op=dist.ReduceOp.MAX)
@@ -572,7 +575,8 @@ def main():
             except Exception as e:  # keep NCCL
                 merge_kind = f"nccl int64 MAX all-reduce (peer exchange unavailable: {e})"
 
-    gather = world > 1 and args.full_logits
+    peer_full = fused and merge is not None and merge.vocab > 0
+    gather = world > 1 and args.full_logits and not peer_full
     y_full = torch.empty(VOCAB, dtype=torch.float32, device="cuda") if gather else None
 
     def step(i):
@@ -672,7 +676,9 @@ def main():
             "scaling": "strong", "vs_baseline": None, "dtype": "int16/int64", "data": "synthetic",
             "config": {"workload": WORKLOAD, "rows": VOCAB, "cols": HIDDEN, "batch": 1,
                        "step": "shard logits GEMV with fused top-1 key" + (f" + {merge_kind}" if world > 1 else "")
-                               + (" + NCCL all-gather of the logits shards" if gather else ""),
+                               + (" + NCCL all-gather of the logits shards" if gather else "")
+                               + (" + full logits stored into every rank over NVLink inside the GEMV"
+                                  if peer_full else ""),
                        "greedy_token": tok,
                        "parallelism": f"vocab-row shards x{world}", "shard_rows": rows,
                        "launch": "back-to-back, no programmatic dependent launch" if args.no_pdl else

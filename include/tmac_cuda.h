@@ -263,6 +263,17 @@ int tmac_xchg_top1(tmac_xchg_t x, uint64_t* key, void* stream);
  * same sequence of calls. */
 int tmac_xchg_gemv_top1(tmac_xchg_t x, tmac_weight_t w, const float* in, float* y, uint64_t* key,
                         int64_t index_base, void* stream);
+/* The same exchange with the full logits on every rank (get_logits_q8 returns
+ * the whole vector, sim/tmac_gguf.cpp:1820-1845): created with the vocabulary
+ * size, each rank's buffer also holds two full-logits vectors (by step
+ * parity), and tmac_xchg_gemv_top1 on a NATIVE Q8_0 shard stores every row it
+ * computes into all ranks' vectors over NVLink peer memory, inside the same
+ * launch, before the step's key is published.  tmac_xchg_logits gives the
+ * device address of this rank's full vector for the last step enqueued; read
+ * it (stream-ordered) before the next exchange call on that stream, which lets
+ * the other ranks write the next step. */
+int tmac_xchg_create_logits(int device, int world, int rank, int64_t vocab, tmac_xchg_t* out);
+int tmac_xchg_logits(tmac_xchg_t x, float** logits);
 int tmac_xchg_free(tmac_xchg_t x);
 
 /* ------------------------------------------------------------------------ */

@@ -139,7 +139,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _rank_main(rank, world, port, rows, cols, fused, out):
+def _rank_main(rank, world, port, rows, cols, fused, out, full=False):
     import torch
     import torch.distributed as dist
     from tmac_zynq_fpga_b200 import shard
@@ -152,8 +152,8 @@ def _rank_main(rank, world, port, rows, cols, fused, out):
         r0, r1 = rank * rows // world, (rank + 1) * rows // world
         blk = (cols // 32) * Q8_BLOCK_BYTES
         w = tm.Weight(synth.Q8_0, r1 - r0, cols, raw[r0 * blk:r1 * blk], device=rank)
-        xchg = shard.PeerTop1(rank)
-        keys = []
+        xchg = shard.PeerTop1(rank, vocab=rows if full else 0)
+        keys, fulls = [], []
         for step in range(8):
             x = torch.from_numpy(synth.make_activations(cols, seed=50 + step) * (1 + step)).cuda()
             y = torch.empty(r1 - r0, device="cuda")
@@ -165,8 +165,10 @@ def _rank_main(rank, world, port, rows, cols, fused, out):
                 xchg(key)
             torch.cuda.synchronize()
             keys.append(key.item())
+            if full:
+                fulls.append(xchg.logits().cpu().numpy().copy())
         assert tm.device_error(rank) == 0
-        out.put((rank, keys))
+        out.put((rank, (keys, fulls) if full else keys))
         dist.barrier()
         xchg.free()
     finally:
@@ -204,3 +206,75 @@ def test_two_ranks_merge_to_global_argmax(fused):
         key = torch.zeros(1, dtype=torch.int64, device="cuda")
         w.gemv_top1(x, y, key)
         assert got[0][step] == got[1][step] == key.item(), step
+
+
+def test_two_ranks_full_logits_over_peer_memory():
+    """The fused exchange with the full logits (tmac_xchg_create_logits): each
+    rank's shard GEMV also stores its rows into both ranks' full vectors over
+    NVLink, so after every step both ranks hold the whole logits vector, bit
+    for bit the unsharded GEMV's, and the same greedy key."""
+    torch = pytest.importorskip("torch")
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    rows, cols = 20000, 896
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, rows, cols, True, q, True)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = {}
+    try:
+        for _ in range(2):
+            r, res = q.get(timeout=300)
+            got[r] = res
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    assert all(p.exitcode == 0 for p in procs)
+    w = tm.Weight(synth.Q8_0, rows, cols, synth.make_weights(synth.Q8_0, rows, cols, seed=77))
+    for step in range(8):
+        x = torch.from_numpy(synth.make_activations(cols, seed=50 + step) * (1 + step)).cuda()
+        y = torch.empty(rows, device="cuda")
+        key = torch.zeros(1, dtype=torch.int64, device="cuda")
+        w.gemv_top1(x, y, key)
+        yh = y.cpu().numpy()
+        for r in range(2):
+            keys, fulls = got[r]
+            assert keys[step] == key.item(), step
+            np.testing.assert_array_equal(fulls[step].view(np.int32), yh.view(np.int32), err_msg=f"rank {r} step {step}")
+
+
+def test_one_rank_full_logits_buffer():
+    """World 1: the full-logits buffer of each step equals y (both parities)."""
+    torch = pytest.importorskip("torch")
+    from tmac_zynq_fpga_b200 import shard
+    L = tm.lib()
+    rows, cols = 3000, 896
+    w = tm.Weight(synth.Q8_0, rows, cols, synth.make_weights(synth.Q8_0, rows, cols, seed=41))
+    h = ctypes.c_void_p()
+    L.tmac_xchg_create_logits.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int64,
+                                          ctypes.POINTER(ctypes.c_void_p)]
+    tm.check(L.tmac_xchg_create_logits(0, 1, 0, rows, ctypes.byref(h)))
+    try:
+        buf = (ctypes.c_uint8 * 64)()
+        tm.check(L.tmac_xchg_ipc_handle(h, buf))
+        tm.check(L.tmac_xchg_open(h, bytes(buf)))
+        p = ctypes.c_void_p()
+        L.tmac_xchg_logits.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]
+        assert L.tmac_xchg_logits(h, ctypes.byref(p)) != 0  # no step yet
+        for step in range(3):
+            x = torch.from_numpy(synth.make_activations(cols, seed=60 + step)).cuda()
+            y = torch.empty(rows, device="cuda")
+            key = torch.zeros(1, dtype=torch.int64, device="cuda")
+            tm.check(L.tmac_xchg_gemv_top1(h, w.handle, x.data_ptr(), y.data_ptr(), key.data_ptr(), 0, None))
+            tm.check(L.tmac_xchg_logits(h, ctypes.byref(p)))
+            full = shard.device_view(p.value, rows).cpu().numpy()
+            np.testing.assert_array_equal(full.view(np.int32), y.cpu().numpy().view(np.int32))
+        assert tm.device_error(0) == 0
+    finally:
+        L.tmac_xchg_free(h)
+        w.free()

@@ -267,6 +267,10 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemv_kernel(Q8Args a)
             }
             if (r < a.rows) {
                 a.y[r] = yr;
+                if (a.xg.vocab) {  // this row of the full logits in every rank (NVLink peer stores)
+                    const uint64_t step = *a.xg.step + 1;
+                    for (int q = 0; q < a.xg.world; q++) xchg_logits(a.xg, q, step)[a.index_base + r] = yr;
+                }
                 if (a.row_acc) a.row_acc[r] = rsum;
                 const unsigned long long k = top1_key(yr, a.index_base + r);
                 best = k > best ? k : best;

@@ -37,6 +37,8 @@ XchgDev xchg_dev(const tmac_xchg_s* x)
     d.counter = x->counter;
     d.world = x->world;
     d.rank = x->rank;
+    d.vocab = x->vocab;
+    d.logits_off = x->logits_off;
     return d;
 }
 
@@ -99,16 +101,26 @@ extern "C" {
 
 int tmac_xchg_create(int device, int world, int rank, tmac_xchg_t* out)
 {
+    return tmac_xchg_create_logits(device, world, rank, 0, out);
+}
+
+int tmac_xchg_create_logits(int device, int world, int rank, int64_t vocab, tmac_xchg_t* out)
+{
     if (!out) return fail(TMAC_ERR_INVALID, "NULL output");
     *out = nullptr;
     if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world) return fail(TMAC_ERR_SHAPE, "bad world / rank");
+    if (vocab < 0 || vocab > 0x7FFFFFFF) return fail(TMAC_ERR_SHAPE, "bad vocabulary size");
     DeviceGuard dg(device);
     if (!dg.ok) return fail(TMAC_ERR_CUDA, "cudaSetDevice failed");
     tmac_xchg_s* x = new tmac_xchg_s();
     x->device = device;
     x->world = world;
     x->rank = rank;
-    const size_t bytes = (size_t)4 * world * sizeof(uint64_t);
+    x->vocab = vocab;
+    x->logits_off = ((size_t)4 * world * sizeof(uint64_t) + 255) / 256 * 256;
+    // keys | tags, then (vocab > 0) the full logits of the two step parities:
+    // one allocation, so one IPC handle maps everything a peer writes
+    const size_t bytes = vocab ? x->logits_off + (size_t)2 * vocab * sizeof(float) : (size_t)4 * world * sizeof(uint64_t);
     cudaError_t e = cudaMalloc(&x->buf, bytes);
     if (e == cudaSuccess) e = cudaMemset(x->buf, 0, bytes);
     if (e == cudaSuccess) e = cudaMalloc(&x->step, sizeof(uint64_t));
@@ -187,6 +199,7 @@ int tmac_xchg_top1(tmac_xchg_t x, uint64_t* key, void* stream)
     TMAC_CUDA_TRY(launch_k(xchg_top1_kernel, dim3(1), dim3(threads), 0, (cudaStream_t)stream,
                            reinterpret_cast<unsigned long long*>(key), xchg_dev(x), device_error_word(x->device)));
     TMAC_CUDA_TRY(cudaGetLastError());
+    x->host_steps++;
     return TMAC_OK;
 }
 
@@ -198,14 +211,28 @@ int tmac_xchg_gemv_top1(tmac_xchg_t x, tmac_weight_t w, const float* in, float* 
         if (!x->peer[r]) return fail(TMAC_ERR_INVALID, "tmac_xchg_open has not mapped every rank");
     if (w->device != x->device) return fail(TMAC_ERR_INVALID, "weight and exchange on different devices");
     if (!(w->mode == TMAC_MODE_NATIVE && w->type == TMAC_TYPE_Q8_0)) {
+        if (x->vocab) return fail(TMAC_ERR_TYPE, "the full-logits exchange needs a NATIVE Q8_0 logits weight");
         const int rc = tmac_gemv_top1(w, in, y, key, index_base, 1, stream);
         return rc ? rc : tmac_xchg_top1(x, key, stream);
     }
     if (index_base < 0 || index_base + w->rows > 0x7FFFFFFF) return fail(TMAC_ERR_SHAPE, "bad index range");
+    if (x->vocab && index_base + w->rows > x->vocab) return fail(TMAC_ERR_SHAPE, "shard rows beyond the vocabulary");
     DeviceGuard dg(x->device);
     const XchgDev d = xchg_dev(x);
-    return launch_q8_0(w, in, y, nullptr, nullptr, 1, (cudaStream_t)stream,
-                       reinterpret_cast<unsigned long long*>(key), index_base, nullptr, nullptr, &d);
+    const int rc = launch_q8_0(w, in, y, nullptr, nullptr, 1, (cudaStream_t)stream,
+                               reinterpret_cast<unsigned long long*>(key), index_base, nullptr, nullptr, &d);
+    if (!rc) x->host_steps++;
+    return rc;
+}
+
+int tmac_xchg_logits(tmac_xchg_t x, float** logits)
+{
+    if (!x || !logits) return fail(TMAC_ERR_INVALID, "NULL argument");
+    if (!x->vocab) return fail(TMAC_ERR_INVALID, "exchange created without a logits buffer");
+    if (!x->host_steps) return fail(TMAC_ERR_INVALID, "no exchange step has run yet");
+    *logits = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(x->buf) + x->logits_off) +
+              (x->host_steps & 1) * x->vocab;
+    return TMAC_OK;
 }
 
 int tmac_xchg_free(tmac_xchg_t x)

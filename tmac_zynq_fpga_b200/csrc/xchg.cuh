@@ -22,6 +22,9 @@ struct tmac_xchg_s {
     unsigned* counter = nullptr;            // fused GEMV: CTAs finished
     std::vector<uint64_t*> peer;       // every rank's buffer as mapped here (own = buf)
     std::vector<char> ipc_mapped;      // peer[r] came from cudaIpcOpenMemHandle
+    int64_t vocab = 0;                 // > 0: full logits [2][vocab] floats after the keys
+    size_t logits_off = 0;             // byte offset of the logits in every rank's buffer
+    uint64_t host_steps = 0;           // exchange steps enqueued so far
     uint64_t** peer_dev = nullptr;     // the same table on the device
 };
 
@@ -34,7 +37,17 @@ struct XchgDev {
     unsigned long long* partial = nullptr;
     unsigned* counter = nullptr;
     int world = 0, rank = 0;
+    int64_t vocab = 0;       // > 0: every rank's full-logits buffers are written too
+    size_t logits_off = 0;   // their byte offset in each rank's exchange buffer
 };
+
+// Full-logits buffer of rank q for the step about to run (its parity half):
+// the logits GEMV stores its shard there in every rank, so each rank ends
+// the step holding the whole vector.
+TMAC_DEV float* xchg_logits(const XchgDev& x, int q, uint64_t step)
+{
+    return reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(x.peers[q]) + x.logits_off) + (step & 1) * x.vocab;
+}
 
 TMAC_DEV void st_release_sys(uint64_t* p, uint64_t v)
 {
@@ -107,6 +120,10 @@ TMAC_DEV void top1_cta_finish(const XchgDev& xg, unsigned long long* top1, unsig
     if (lane == 0) slots[slot] = best;
     asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(bar_threads) : "memory");
     if (!(leader_warp && lane == 0)) return;
+    // full logits: the peer stores of the CTA's warps (ordered before this
+    // thread by the barrier) reach the other GPUs before the key that the last
+    // CTA publishes with a system-scope release
+    if (xg.vocab) __threadfence_system();
     unsigned long long m = 0;
     for (int w = 0; w < bar_threads / 32; w++) m = slots[w] > m ? slots[w] : m;
     if (!xg.partial) {

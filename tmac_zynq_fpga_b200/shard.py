@@ -74,6 +74,15 @@ def gather_logits(local, rows: int, out=None, group=None):
     return out
 
 
+def device_view(ptr: int, n: int):
+    """A float32 CUDA tensor over n floats at device address ptr (no copy)."""
+    import torch
+
+    class _View:
+        __cuda_array_interface__ = {"shape": (n,), "typestr": "<f4", "data": (int(ptr), False), "version": 3}
+    return torch.as_tensor(_View(), device="cuda")
+
+
 # ------------------------------------------------------------------ prefill
 # The multi-sequence prefill batch shards by sequence: rank r prefills sequences
 # [s0, s1) of the batch with tmac_model_prefill on its own GPU.  Sequences are
@@ -111,14 +120,17 @@ class PeerTop1:
     logits GEMV itself (gemv_top1).  Setup shares
     the CUDA IPC handles of the buffers over the process group."""
 
-    def __init__(self, device: int, group=None):
+    def __init__(self, device: int, group=None, vocab: int = 0):
         import ctypes
         import torch.distributed as dist
         from . import lib, check, _P
         self._lib = lib()
         world, rank = dist.get_world_size(group), dist.get_rank(group)
         self.handle = _P()
-        check(self._lib.tmac_xchg_create(device, world, rank, ctypes.byref(self.handle)))
+        self.vocab = int(vocab)
+        f = self._lib.tmac_xchg_create_logits
+        f.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int64, ctypes.POINTER(_P)]
+        check(f(device, world, rank, self.vocab, ctypes.byref(self.handle)))
         buf = (ctypes.c_uint8 * 64)()
         check(self._lib.tmac_xchg_ipc_handle(self.handle, buf))
         handles = [None] * world
@@ -142,6 +154,19 @@ class PeerTop1:
         check(self._lib.tmac_xchg_gemv_top1(self.handle, weight.handle, x.data_ptr(), y.data_ptr(),
                                             key_tensor.data_ptr(), int(index_base), s))
         return key_tensor
+
+    def logits(self):
+        """This rank's full logits vector of the last step (created with vocab > 0;
+        tmac_xchg_logits) as a float32 CUDA tensor viewing the exchange buffer:
+        valid until the next exchange call."""
+        import ctypes
+        import torch
+        from . import check
+        p = ctypes.c_void_p()
+        f = self._lib.tmac_xchg_logits
+        f.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]
+        check(f(self.handle, ctypes.byref(p)))
+        return device_view(p.value, self.vocab)
 
     def free(self):
         if getattr(self, "handle", None):
