@@ -502,8 +502,10 @@ def main():
     ap.add_argument("--no-model", action="store_true", help="skip the decode / prefill measurements")
     ap.add_argument("--no-pdl", action="store_true",
                     help="launch each step's kernel after the previous one ends (no programmatic dependent launch)")
-    ap.add_argument("--full-logits", action="store_true",
-                    help="N > 1: every rank also ends each step with the whole logits vector, as "
+    ap.add_argument("--top1-only", dest="full_logits", action="store_false",
+                    help="N > 1: only the global greedy token on every rank, not the whole logits vector")
+    ap.add_argument("--full-logits", dest="full_logits", action="store_true", default=True,
+                    help="(default) N > 1: every rank also ends each step with the whole logits vector, as "
                          "get_logits_q8 returns it: stored over NVLink by the GEMV itself with the fused "
                          "exchange, else an NCCL all-gather")
     ap.add_argument("--collective", choices=["fused", "peer", "nccl"], default="fused",
