@@ -239,6 +239,11 @@ TMAC_DEV void named_bar_sync(int id, int nthreads)
 {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
+// Arrive without waiting (producer side of a named barrier some other warps sync on).
+TMAC_DEV void named_bar_arrive(int id, int nthreads)
+{
+    asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
 
 // Launches with programmatic stream serialisation while the calling thread has
 // PDL enabled (the decode engine enables it around its graph capture).

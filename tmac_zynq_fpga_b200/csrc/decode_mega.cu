@@ -99,7 +99,7 @@ struct MegaArgs {
     // Activations handed between CTAs, each value stored with the tag of the
     // phase that wrote it (tag << 32 | float bits, one 8-byte store): a reader
     // polls the values it needs until their tags are the expected ones.
-    unsigned long long *hid_t, *qkv_t, *ctx_t, *h_t, *pm_t;
+    unsigned long long *hid_t, *qkv_t, *ctx_t, *h_t;
     uint32_t epoch;  // this launch's tag base (128 tags per launch)
     int* abort_flag;  // zeroed per launch
     int* err;
@@ -238,7 +238,7 @@ TMAC_DEV void issue_slot(const MegaSlot& sp, uint8_t* base, MegaMisc& ms, int sl
 // yv[rr] = (float)((double)acc * x_scale / (double)row_inv).
 template <int TYPE>
 TMAC_DEV void mega_blockq(const uint8_t* wsm, const MegaSlot& sp, int cols, const uint8_t* xpl, float xs,
-                          uint32_t* acc_lo, uint32_t* acc_hi, float* yv)
+                          uint32_t* acc_lo, uint32_t* acc_hi, float* yv, unsigned long long* stamps = nullptr)
 {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int64_t cpr = cols / 32, nblk = cols / Geo<TYPE>::kBlockVals;
@@ -258,7 +258,9 @@ TMAC_DEV void mega_blockq(const uint8_t* wsm, const MegaSlot& sp, int cols, cons
     const uint32_t wsm_a = smem_addr(wsm);
     long long acc = 0;
     int slot = items ? it0 / steps : 0, s = items ? it0 % steps : 0;
+    if (stamps && lane == 0 && warp == 0) stamps[4] = global_timer_ns();
     for (int it = it0; it < it1; it++) {
+        if (stamps && lane == 0 && warp == 0 && it - it0 < 6) stamps[5 + 2 * (it - it0)] = global_timer_ns();
         const int rr = q5 ? slot * 8 + r_lane : slot;
         const SharedBytes G{wsm_a + (uint32_t)(rr >> 3) * (uint32_t)group_bytes};
         const int r = rr & 7;
@@ -271,6 +273,7 @@ TMAC_DEV void mega_blockq(const uint8_t* wsm, const MegaSlot& sp, int cols, cons
             fast_values<TYPE>(c, ri, vw);
             acc += chunk_dot(vw, xpl + ch * 32, xpl + cols + ch * 32);
         }
+        if (stamps && lane == 0 && warp == 0 && it - it0 < 6) stamps[6 + 2 * (it - it0)] = (unsigned long long)(acc & 1) + global_timer_ns();
         if (++s == steps || it + 1 == it1) {
             long long v = acc;
             for (int o = q5 ? 8 : 1; o < 32; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -282,6 +285,7 @@ TMAC_DEV void mega_blockq(const uint8_t* wsm, const MegaSlot& sp, int cols, cons
             }
         }
     }
+    if (stamps && threadIdx.x == 0) stamps[0] = global_timer_ns();
     // exceptions: (v - v') * x_q[col] for the entries of this slot's rows
     const int n1 = (int)sp.ngate;
     for (int t = tid; t < (int)sp.exc_n; t += kMegaThreads) {
@@ -290,11 +294,13 @@ TMAC_DEV void mega_blockq(const uint8_t* wsm, const MegaSlot& sp, int cols, cons
         acc_add(&acc_lo[rr], &acc_hi[rr], (long long)ex.z * xq_at(xpl, cols, 0, ex.y));
     }
     __syncthreads();
+    if (stamps && threadIdx.x == 0) stamps[1] = global_timer_ns();
     for (int t = tid; t < rows_cta; t += kMegaThreads) {
         const long long tot = (long long)(((unsigned long long)acc_hi[t] << 32) | acc_lo[t]);
         yv[t] = (float)__ddiv_rn(__dmul_rn((double)tot, (double)xs), (double)ri_s[t]);
     }
     __syncthreads();
+    if (stamps && threadIdx.x == 0) stamps[2] = global_timer_ns();
 }
 
 // One 32-row Q8_0 record (gemv_q8_0.cu layout): tile t on warp t (lane = row),
@@ -331,31 +337,106 @@ TMAC_DEV void mega_q8(const uint8_t* rec, int cols, const uint8_t* xpl, const in
     __syncthreads();
 }
 
-// rms_norm of xv[0..n) with weights w (the order of rmsnorm_kernel, decode.cu),
-// then x_q of the result as byte planes xpl[0..n) (high) / xpl[n..2n) (low) and
-// x_scale in ms.xs.  All threads.
-TMAC_DEV void mega_norm_quantize(float* xv, float* sq, const float* __restrict__ w, int n, uint8_t* xpl,
-                                 MegaMisc& ms, unsigned long long* stamps = nullptr)
+// In-order sum of the kHidden squares, speculated by segment.  The sum
+// s_{i+1} = fl(s_i + p_i) is split into kSumSegs segments.  The running sum at
+// the start of segment k is estimated as fl(exact prefix sum) (double sums of
+// the segments), and 64 threads run segment k from the 64 floats nearest that
+// estimate (one each).  One thread runs segment 0 from 0 and then links: the
+// true start of segment k is the end of segment k - 1; the candidate that
+// started from exactly that float holds the true end of segment k.  A start
+// outside the candidates' range is summed again in order (never wrong, only
+// slower), so the result is the sequential sum bit for bit.
+constexpr int kSumSegs = 8;
+constexpr int kSegLen = kHidden / kSumSegs;
+constexpr int kSumWarps = 2 * (kSumSegs - 1) + 1;  // two candidate warps per later segment + the linking warp
+constexpr int kSumBar = 3;                          // named barrier of the kSumWarps warps
+constexpr int kNormBar = 2;                         // linking warp + the warps forming x * w
+constexpr int kNormBarThreads = 32 + (kMegaWarps - kSumWarps) * 32;
+static_assert(kHidden % (kSumSegs * 16) == 0, "segments of whole 16-value batches");
+static_assert(kSumWarps < kMegaWarps, "warps left for x * w");
+
+// Float estimate of the running sum at the start of segment k (same arithmetic
+// in every thread that asks).
+TMAC_DEV float seg_start_estimate(const double* seg_sum, int k)
 {
-    const int tid = threadIdx.x;
+    double e = 0.0;
+    for (int i = 0; i < k; i++) e += seg_sum[i];
+    return (float)e;
+}
+
+// rms_norm of xv[0..kHidden) with weights w (the order of rmsnorm_kernel,
+// decode.cu), then x_q of the result as byte planes xpl[0..n) (high) /
+// xpl[n..2n) (low) and x_scale in ms.xs.  All threads; scratch: 2 KB of shared
+// memory.  While warps 0..kSumWarps-1 run the sum of squares, the other warps
+// form xw = fl(x * w) and max |xw|: the normed value is fl(xw * scale), and
+// because rounding is monotonic, max |fl(xw * scale)| = fl(max |xw| * scale).
+TMAC_DEV void mega_norm_quantize(float* xv, float* sq, const float* __restrict__ w, int n, uint8_t* xpl,
+                                 MegaMisc& ms, float* scratch, unsigned long long* stamps = nullptr)
+{
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     for (int i = tid; i < n; i += kMegaThreads) sq[i] = __fmul_rn(xv[i], xv[i]);
     __syncthreads();
-    if (stamps && tid == 0) stamps[0] = global_timer_ns();
-    if (tid == 0) ms.scale = rms_scale(sq, n);
-    if (stamps && tid == 0) stamps[1] = global_timer_ns();
-    __syncthreads();
-    const float scale = ms.scale;
-    float mx = 0.0f;
-    for (int i = tid; i < n; i += kMegaThreads) {
-        const float v = __fmul_rn(__fmul_rn(xv[i], __ldg(w + i)), scale);
-        xv[i] = v;
-        mx = fmaxf(mx, fabsf(v));
+    float* seg_end = scratch;                                                  // [kSumSegs - 1][64]
+    double* seg_sum = reinterpret_cast<double*>(scratch + (kSumSegs - 1) * 64);  // [kSumSegs]
+    int* est_bits = reinterpret_cast<int*>(seg_sum + kSumSegs);                   // [kSumSegs] estimates' bits
+    if (warp < kSumWarps) {
+        if (warp < kSumSegs) {
+            double v = 0.0;
+            for (int i = lane; i < kSegLen; i += 32) v += (double)sq[warp * kSegLen + i];
+            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            if (lane == 0) seg_sum[warp] = v;
+        }
+        named_bar_sync(kSumBar, kSumWarps * 32);
+        if (warp < kSumWarps - 1) {
+            const int k = 1 + (warp >> 1);
+            const int j = (warp & 1) * 32 + lane - 32;  // candidate: estimate + j ulps
+            const int est = __float_as_int(seg_start_estimate(seg_sum, k));
+            if ((warp & 1) == 0 && lane == 0) est_bits[k] = est;
+            const int bits = est + j;
+            seg_end[(k - 1) * 64 + j + 32] =
+                bits >= 0 ? seq_sum_from(__int_as_float(bits), sq + k * kSegLen, kSegLen) : __int_as_float(0x7FC00000);
+            named_bar_arrive(kSumBar, kSumWarps * 32);
+        } else {
+            float s = 0.0f;
+            if (lane == 0) {
+                if (stamps) stamps[0] = global_timer_ns();
+                s = seq_sum_from(0.0f, sq, kSegLen);
+                if (stamps) stamps[2] = global_timer_ns();
+            }
+            named_bar_sync(kSumBar, kSumWarps * 32);
+            if (lane == 0) {
+                if (stamps) stamps[3] = global_timer_ns();
+                for (int k = 1; k < kSumSegs; k++) {
+                    const int j = __float_as_int(s) - est_bits[k];
+                    s = (j >= -32 && j < 32) ? seg_end[(k - 1) * 64 + j + 32] : seq_sum_from(s, sq + k * kSegLen, kSegLen);
+                }
+                ms.scale = rms_scale_from_sum(s, n);
+                if (stamps) stamps[1] = global_timer_ns();
+            }
+            named_bar_sync(kNormBar, kNormBarThreads);
+            if (lane == 0) {
+                float mx = 0.0f;
+                for (int i = kSumWarps; i < kMegaWarps; i++) mx = fmaxf(mx, ms.red[i]);
+                ms.xs = x_scale_from_max(__fmul_rn(mx, ms.scale));
+            }
+        }
+    } else {
+        float mx = 0.0f;
+        for (int i = tid - kSumWarps * 32; i < n; i += kMegaThreads - kSumWarps * 32) {
+            const float v = __fmul_rn(xv[i], __ldg(w + i));
+            xv[i] = v;
+            mx = fmaxf(mx, fabsf(v));
+        }
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        if (lane == 0) ms.red[warp] = mx;
+        named_bar_arrive(kNormBar, kNormBarThreads);
     }
-    mx = block_max(mx, ms.red, kMegaThreads);
-    const float s = x_scale_from_max(mx);
-    if (tid == 0) ms.xs = s;
+    __syncthreads();
+    const float scale = ms.scale, s = ms.xs;
     for (int i = tid; i < n; i += kMegaThreads) {
-        const int16_t q = quantize_one(xv[i], s);
+        const float v = __fmul_rn(xv[i], scale);
+        xv[i] = v;
+        const int16_t q = quantize_one(v, s);
         xpl[i] = (uint8_t)((uint16_t)q >> 8);
         xpl[n + i] = (uint8_t)(q & 0xFF);
     }
@@ -402,18 +483,22 @@ TMAC_DEV void mega_block_sums(const uint8_t* xpl, int n, int* sx)
 // tmac_trace_read_mega / tmac_trace_read_att.
 __device__ unsigned long long g_mega_trace[160][kLayers][24];
 __device__ unsigned long long g_att_trace[kHeads][kLayers][8];
+__device__ unsigned long long g_bq_trace[160][kLayers][4][20];
+__device__ unsigned long long g_norm_trace[160][kLayers][2][8];
 #define MEGA_STAMP(l, i)                                                                 \
     do {                                                                                 \
         if (threadIdx.x == 0 && blockIdx.x < 160) g_mega_trace[blockIdx.x][l][i] = global_timer_ns(); \
     } while (0)
 #define MEGA_ATT_STAMPS(h, l) (&g_att_trace[h][l][0])
-#define MEGA_NORM_STAMPS(l) (&g_mega_trace[blockIdx.x][l][17])
+#define MEGA_NORM_STAMPS(l, i) (blockIdx.x < 160 ? &g_norm_trace[blockIdx.x][l][i][0] : nullptr)
+#define MEGA_BQ_STAMPS(l, ph) (blockIdx.x < 160 ? &g_bq_trace[blockIdx.x][l][ph][0] : nullptr)
 #else
 #define MEGA_STAMP(l, i) \
     do {                 \
     } while (0)
 #define MEGA_ATT_STAMPS(h, l) nullptr
-#define MEGA_NORM_STAMPS(l) nullptr
+#define MEGA_NORM_STAMPS(l, i) nullptr
+#define MEGA_BQ_STAMPS(l, ph) nullptr
 #endif
 
 __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaArgs a)
@@ -529,13 +614,13 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaArgs a
                 if (!poll_smem(a.hid_t, kHidden, tag_of(ep, l - 1, TG_HID_E), xv, ms, a.abort_flag, a.err)) break;
                 MEGA_STAMP(l, 1);
             }
-            mega_norm_quantize(xv, sq, L.attn_norm, kHidden, xpl, ms, MEGA_NORM_STAMPS(l));
+            mega_norm_quantize(xv, sq, L.attn_norm, kHidden, xpl, ms, att, MEGA_NORM_STAMPS(l, 0));
             if (pa.kind == SK_Q8) mega_block_sums(xpl, kHidden, ms.sx);
             MEGA_STAMP(l, 2);
             if (!wait_slot(0)) break;
             MEGA_STAMP(l, 3);
             if (pa.kind == SK_Q8) mega_q8(slot_base[0], kHidden, xpl, ms.sx, ms.xs, tsum, yv);
-            else mega_blockq<TMAC_TYPE_Q5_0>(slot_base[0], pa, kHidden, xpl, ms.xs, acc_lo, acc_hi, yv);
+            else mega_blockq<TMAC_TYPE_Q5_0>(slot_base[0], pa, kHidden, xpl, ms.xs, acc_lo, acc_hi, yv, MEGA_BQ_STAMPS(l, 0));
             for (int t = tid; t < (int)pa.rows; t += kMegaThreads)
                 st_tagged(a.qkv_t + pa.out0[0] + t, yv[t], tag_of(ep, l, TG_QKV));
             finish(l, 0);
@@ -620,7 +705,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaArgs a
             MEGA_STAMP(l, 8);
             if (!wait_slot(1)) break;
             MEGA_STAMP(l, 21);
-            mega_blockq<TMAC_TYPE_Q5_0>(slot_base[1], pc, kHidden, xpl, ms.xs, acc_lo, acc_hi, yv);
+            mega_blockq<TMAC_TYPE_Q5_0>(slot_base[1], pc, kHidden, xpl, ms.xs, acc_lo, acc_hi, yv, MEGA_BQ_STAMPS(l, 1));
             MEGA_STAMP(l, 22);
             if (tid < (int)pc.rows)
                 st_tagged(a.hid_t + pc.out0[0] + tid, __fadd_rn(hres, yv[tid]), tag_of(ep, l, TG_HID_C));
@@ -634,20 +719,14 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaArgs a
         if (pd.kind != SK_NONE) {
             if (!poll_smem(a.hid_t, kHidden, tag_of(ep, l, TG_HID_C), xv, ms, a.abort_flag, a.err)) break;
             MEGA_STAMP(l, 10);
-            mega_norm_quantize(xv, sq, L.ffn_norm, kHidden, xpl, ms);
+            mega_norm_quantize(xv, sq, L.ffn_norm, kHidden, xpl, ms, att, MEGA_NORM_STAMPS(l, 1));
             MEGA_STAMP(l, 11);
             if (!wait_slot(2)) break;
-            mega_blockq<TMAC_TYPE_Q5_0>(slot_base[2], pd, kHidden, xpl, ms.xs, acc_lo, acc_hi, yv);
+            mega_blockq<TMAC_TYPE_Q5_0>(slot_base[2], pd, kHidden, xpl, ms.xs, acc_lo, acc_hi, yv, MEGA_BQ_STAMPS(l, 2));
             MEGA_STAMP(l, 12);
             const int n = (int)pd.ngate;
-            float mx = 0.0f;
-            for (int t = tid; t < n; t += kMegaThreads) {
-                const float v = silu_mul(yv[t], yv[n + t]);
-                st_tagged(a.h_t + pd.out0[0] + t, v, tag_of(ep, l, TG_H));
-                mx = fmaxf(mx, fabsf(v));
-            }
-            mx = block_max(mx, ms.red, kMegaThreads);
-            if (tid == 0) st_tagged(a.pm_t + cta, mx, tag_of(ep, l, TG_H));
+            for (int t = tid; t < n; t += kMegaThreads)
+                st_tagged(a.h_t + pd.out0[0] + t, silu_mul(yv[t], yv[n + t]), tag_of(ep, l, TG_H));
             finish(l, 2);
             MEGA_STAMP(l, 13);
         } else {
@@ -656,30 +735,30 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaArgs a
         // ------------------------------------------------ E: ffn_down + residual
         const MegaSlot& pe = plans[l * kSlots + 3];
         if (pe.kind != SK_NONE) {
-            // h, the per-CTA maxima and this CTA's rows of hidden, in one polling loop
-            float r[kMaxQuant], pm = 0.0f, hres = 0.0f;
-            PollExtra ex0, ex1;
-            ex0.src = a.pm_t;
-            ex0.n = (int)gridDim.x;
-            ex0.tag = tag_of(ep, l, TG_H);
-            ex0.out = &pm;
+            // h and this CTA's rows of hidden, in one polling loop
+            float r[kMaxQuant], hres = 0.0f;
+            PollExtra ex1;
             ex1.src = a.hid_t + pe.out0[0];
             ex1.n = (int)pe.rows;
             ex1.tag = tag_of(ep, l, TG_HID_C);
             ex1.out = &hres;
-            if (!poll_regs<kMaxQuant>(a.h_t, kInter, tag_of(ep, l, TG_H), r, ms, a.abort_flag, a.err, ex0, ex1)) break;
+            if (!poll_regs<kMaxQuant>(a.h_t, kInter, tag_of(ep, l, TG_H), r, ms, a.abort_flag, a.err, PollExtra(), ex1))
+                break;
             MEGA_STAMP(l, 14);
-            // x_scale from the maximum of the per-CTA maxima (every CTA has gate|up rows)
-            float mx = tid < (int)gridDim.x ? pm : 0.0f;
+            // x_scale from max |h| over the values just polled
+            float mx = 0.0f;
+#pragma unroll
+            for (int k = 0; k < kMaxQuant; k++)
+                if (tid + k * kMegaThreads < kInter) mx = fmaxf(mx, fabsf(r[k]));
             mx = block_max(mx, ms.red, kMegaThreads);
             mega_quantize<kMaxQuant>(r, kInter, mx, xpl, ms);
             MEGA_STAMP(l, 15);
             if (!wait_slot(3)) break;
             MEGA_STAMP(l, 19);
             if (pe.kind == SK_Q6K)
-                mega_blockq<TMAC_TYPE_Q6_K>(slot_base[3], pe, kInter, xpl, ms.xs, acc_lo, acc_hi, yv);
+                mega_blockq<TMAC_TYPE_Q6_K>(slot_base[3], pe, kInter, xpl, ms.xs, acc_lo, acc_hi, yv, MEGA_BQ_STAMPS(l, 3));
             else
-                mega_blockq<TMAC_TYPE_Q4_K>(slot_base[3], pe, kInter, xpl, ms.xs, acc_lo, acc_hi, yv);
+                mega_blockq<TMAC_TYPE_Q4_K>(slot_base[3], pe, kInter, xpl, ms.xs, acc_lo, acc_hi, yv, MEGA_BQ_STAMPS(l, 3));
             MEGA_STAMP(l, 20);
             if (tid < (int)pe.rows)
                 st_tagged(a.hid_t + pe.out0[0] + tid, __fadd_rn(hres, yv[tid]), tag_of(ep, l, TG_HID_E));
@@ -740,7 +819,7 @@ struct MegaState {
     void* dev_layers = nullptr;
     void* dev_slots = nullptr;
     int* dev_abort = nullptr;                // cleared before every launch
-    unsigned long long* dev_tagged = nullptr;  // hidden | q|k|v | ctx | h | per-CTA max |h|
+    unsigned long long* dev_tagged = nullptr;  // hidden | q|k|v | ctx | h
     uint32_t epoch = 0;                        // tag base of the last launch
 };
 
@@ -956,7 +1035,7 @@ int mega_prepare(tmac_model_s* m, MegaState** out)
     MegaState* st = new MegaState();
     st->smem = off;
     st->grid = G;
-    const size_t n_tagged = (size_t)kHidden + kHidden + 2 * kKvDim + kHidden + kInter + G;
+    const size_t n_tagged = (size_t)kHidden + kHidden + 2 * kKvDim + kHidden + kInter;
     cudaError_t e = cudaMalloc(&st->dev_layers, layers.size() * sizeof(MegaLayer));
     if (e == cudaSuccess) e = cudaMalloc(&st->dev_slots, slots.size() * sizeof(MegaSlot));
     if (e == cudaSuccess) e = cudaMalloc(&st->dev_abort, sizeof(int));
@@ -988,7 +1067,6 @@ int mega_prepare(tmac_model_s* m, MegaState** out)
     a.qkv_t = a.hid_t + kHidden;
     a.ctx_t = a.qkv_t + kHidden + 2 * kKvDim;
     a.h_t = a.ctx_t + kHidden;
-    a.pm_t = a.h_t + kInter;
     a.err = device_error_word(m->device);
     a.max_seq = m->max_seq;
     a.head_cta0 = G - kHeads;
@@ -1034,6 +1112,14 @@ int mega_launch(MegaState* st, int n_prompt, cudaStream_t s)
 extern "C" int tmac_trace_read_mega(unsigned long long* out)
 {
     return (int)cudaMemcpyFromSymbol(out, tmac::g_mega_trace, sizeof(tmac::g_mega_trace));
+}
+extern "C" int tmac_trace_read_bq(unsigned long long* out)
+{
+    return (int)cudaMemcpyFromSymbol(out, tmac::g_bq_trace, sizeof(tmac::g_bq_trace));
+}
+extern "C" int tmac_trace_read_norm(unsigned long long* out)
+{
+    return (int)cudaMemcpyFromSymbol(out, tmac::g_norm_trace, sizeof(tmac::g_norm_trace));
 }
 extern "C" int tmac_trace_read_att(unsigned long long* out)
 {

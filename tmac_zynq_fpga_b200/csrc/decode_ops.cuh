@@ -9,6 +9,46 @@
 
 namespace tmac {
 
+// rms_norm's scale (:447-454) from the in-order sum of the squares.
+TMAC_DEV float rms_scale_from_sum(float sum, int n)
+{
+    const float mean = __fdiv_rn(sum, (float)n);
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, 1e-6f)));
+}
+
+// s + p[0] + p[1] + ... + p[m-1], each add rounded in turn (p 16-byte aligned,
+// m a multiple of 16).
+TMAC_DEV float seq_sum_from(float s, const float* p, int m)
+{
+    const float4* p4 = reinterpret_cast<const float4*>(p);
+    int i = 0;
+    for (; i + 32 <= m; i += 32) {
+        float4 f[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) f[u] = p4[i / 4 + u];
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            s = __fadd_rn(s, f[u].x);
+            s = __fadd_rn(s, f[u].y);
+            s = __fadd_rn(s, f[u].z);
+            s = __fadd_rn(s, f[u].w);
+        }
+    }
+    for (; i < m; i += 16) {
+        float4 f[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) f[u] = p4[i / 4 + u];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            s = __fadd_rn(s, f[u].x);
+            s = __fadd_rn(s, f[u].y);
+            s = __fadd_rn(s, f[u].z);
+            s = __fadd_rn(s, f[u].w);
+        }
+    }
+    return s;
+}
+
 // rms_norm's scale (:447-454): 1 / sqrtf(sum / n + 1e-6) with the sum of the
 // squares sq[0..n) taken in order (sq 16-byte aligned; one thread).
 TMAC_DEV float rms_scale(const float* sq, int n)
@@ -29,8 +69,7 @@ TMAC_DEV float rms_scale(const float* sq, int n)
         }
     }
     for (; i < n; i++) sum = __fadd_rn(sum, sq[i]);
-    const float mean = __fdiv_rn(sum, (float)n);
-    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, 1e-6f)));
+    return rms_scale_from_sum(sum, n);
 }
 
 // silu(g) * u (:459-461, :1697-1700).
