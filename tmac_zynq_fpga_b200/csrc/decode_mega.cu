@@ -147,13 +147,19 @@ struct PollExtra {
     float* out = nullptr;
 };
 
+struct NoHook {
+    TMAC_DEV void operator()() const {}
+};
+
 // All threads: r[k] = value src[tid + k * kMegaThreads] (k < K, index < n) once
 // its tag equals `tag`, and the extras likewise, all in the same polling loop
-// (one L2 round trip when everything is already there).  Bounded: false (and
-// ms.abort) on timeout or another CTA's abort.
-template <int K>
+// (one L2 round trip when everything is already there).  hook() runs once in
+// every thread while the first round of loads is in flight.  Bounded: false
+// (and ms.abort) on timeout or another CTA's abort.
+template <int K, class Hook = NoHook>
 TMAC_DEV bool poll_regs(const unsigned long long* src, int n, uint32_t tag, float (&r)[K], MegaMisc& ms,
-                        int* abort_g, int* err, PollExtra e0 = PollExtra(), PollExtra e1 = PollExtra())
+                        int* abort_g, int* err, PollExtra e0 = PollExtra(), PollExtra e1 = PollExtra(),
+                        const Hook& hook = Hook())
 {
     const int tid = threadIdx.x;
     uint32_t todo = 0;
@@ -164,29 +170,28 @@ TMAC_DEV bool poll_regs(const unsigned long long* src, int n, uint32_t tag, floa
     if (tid < e1.n) todo |= 1u << 31;
     uint64_t t0 = 0;
     for (uint32_t it = 0;; it++) {
+        // loads first, then the hook, then the tag checks: the hook's work
+        // overlaps this thread's loads in flight
+        unsigned long long u[K], u0 = 0, u1 = 0;
+#pragma unroll
+        for (int k = 0; k < K; k++) u[k] = (todo & (1u << k)) ? ld_tagged(src + tid + k * kMegaThreads) : 0ull;
+        if (todo & (1u << 30)) u0 = ld_tagged(e0.src + tid);
+        if (todo & (1u << 31)) u1 = ld_tagged(e1.src + tid);
+        if (it == 0) hook();
 #pragma unroll
         for (int k = 0; k < K; k++) {
-            if (todo & (1u << k)) {
-                const unsigned long long u = ld_tagged(src + tid + k * kMegaThreads);
-                if ((uint32_t)(u >> 32) == tag) {
-                    r[k] = __uint_as_float((uint32_t)u);
-                    todo &= ~(1u << k);
-                }
+            if ((todo & (1u << k)) && (uint32_t)(u[k] >> 32) == tag) {
+                r[k] = __uint_as_float((uint32_t)u[k]);
+                todo &= ~(1u << k);
             }
         }
-        if (todo & (1u << 30)) {
-            const unsigned long long u = ld_tagged(e0.src + tid);
-            if ((uint32_t)(u >> 32) == e0.tag) {
-                *e0.out = __uint_as_float((uint32_t)u);
-                todo &= ~(1u << 30);
-            }
+        if ((todo & (1u << 30)) && (uint32_t)(u0 >> 32) == e0.tag) {
+            *e0.out = __uint_as_float((uint32_t)u0);
+            todo &= ~(1u << 30);
         }
-        if (todo & (1u << 31)) {
-            const unsigned long long u = ld_tagged(e1.src + tid);
-            if ((uint32_t)(u >> 32) == e1.tag) {
-                *e1.out = __uint_as_float((uint32_t)u);
-                todo &= ~(1u << 31);
-            }
+        if ((todo & (1u << 31)) && (uint32_t)(u1 >> 32) == e1.tag) {
+            *e1.out = __uint_as_float((uint32_t)u1);
+            todo &= ~(1u << 31);
         }
         if (__syncthreads_and(todo == 0)) return true;
         if ((it & 15u) == 15u) {
@@ -208,11 +213,12 @@ TMAC_DEV bool poll_regs(const unsigned long long* src, int n, uint32_t tag, floa
 
 // All threads: dst[i] = value of src[i] for i < n (n <= kMegaThreads * 2),
 // waiting for `tag` as poll_regs.
+template <class Hook = NoHook>
 TMAC_DEV bool poll_smem(const unsigned long long* src, int n, uint32_t tag, float* dst, MegaMisc& ms, int* abort_g,
-                        int* err)
+                        int* err, const Hook& hook = Hook())
 {
     float r[2];
-    if (!poll_regs<2>(src, n, tag, r, ms, abort_g, err)) return false;
+    if (!poll_regs<2>(src, n, tag, r, ms, abort_g, err, PollExtra(), PollExtra(), hook)) return false;
     for (int k = 0; k < 2; k++)
         if (threadIdx.x + k * kMegaThreads < n) dst[threadIdx.x + k * kMegaThreads] = r[k];
     __syncthreads();
@@ -230,6 +236,23 @@ TMAC_DEV void issue_slot(const MegaSlot& sp, uint8_t* base, MegaMisc& ms, int sl
             bulk_g2s(base + sp.seg[s].dst + off, src + off, min(32768u, sp.seg[s].bytes - off), &ms.bar[slot]);
     }
     ms.armed[slot]++;
+}
+
+// Warp 0: the same copies, one segment per lane -- a bulk copy takes its
+// issuing thread ~0.15 us, so the segments are issued side by side.
+TMAC_DEV void issue_slot_warp(const MegaSlot& sp, uint8_t* base, MegaMisc& ms, int slot, int lane)
+{
+    if (sp.kind == SK_NONE || sp.total == 0) return;
+    if (lane == 0) mbar_arrive_expect_tx(&ms.bar[slot], sp.total);
+    __syncwarp();
+    for (uint32_t sg = lane; sg < sp.nseg; sg += 32) {
+        const uint8_t* src = static_cast<const uint8_t*>(sp.seg[sg].src);
+        for (uint32_t off = 0; off < sp.seg[sg].bytes; off += 32768u)
+            bulk_g2s(base + sp.seg[sg].dst + off, src + off, min(32768u, sp.seg[sg].bytes - off), &ms.bar[slot]);
+    }
+    __syncwarp();
+    if (lane == 0) ms.armed[slot]++;
+    __syncwarp();
 }
 
 // ---------------------------------------------------------------- compute --
@@ -492,6 +515,9 @@ __device__ unsigned long long g_norm_trace[160][kLayers][2][8];
 #define MEGA_ATT_STAMPS(h, l) (&g_att_trace[h][l][0])
 #define MEGA_NORM_STAMPS(l, i) (blockIdx.x < 160 ? &g_norm_trace[blockIdx.x][l][i][0] : nullptr)
 #define MEGA_BQ_STAMPS(l, ph) (blockIdx.x < 160 ? &g_bq_trace[blockIdx.x][l][ph][0] : nullptr)
+#define MEGA_ISSUE_T0() const unsigned long long it0_ = global_timer_ns()
+#define MEGA_ISSUE_T1(l, s) do { if (blockIdx.x < 160) { g_bq_trace[blockIdx.x][l][s][18] = global_timer_ns() - it0_; g_bq_trace[blockIdx.x][l][s][19] = plans[(l + 1) * kSlots + s].nseg; } } while (0)
+#define MEGA_BQ_MARK(l, ph, i) do { if (threadIdx.x == 0 && blockIdx.x < 160) g_bq_trace[blockIdx.x][l][ph][i] = global_timer_ns(); } while (0)
 #else
 #define MEGA_STAMP(l, i) \
     do {                 \
@@ -499,6 +525,9 @@ __device__ unsigned long long g_norm_trace[160][kLayers][2][8];
 #define MEGA_ATT_STAMPS(h, l) nullptr
 #define MEGA_NORM_STAMPS(l, i) nullptr
 #define MEGA_BQ_STAMPS(l, ph) nullptr
+#define MEGA_BQ_MARK(l, ph, i) do { } while (0)
+#define MEGA_ISSUE_T0() do { } while (0)
+#define MEGA_ISSUE_T1(l, s) do { } while (0)
 #endif
 
 __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaArgs a)
@@ -564,8 +593,39 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaArgs a
             for (int s = 0; s < kSlots; s++)
                 for (; ms.waited[s] < ms.armed[s]; ms.waited[s]++) mbar_wait_bounded(&ms.bar[s], ms.waited[s] & 1, nullptr);
     };
+    // Fill `slot` with layer l + 1's weights once its layer-l use is over --
+    // whether or not this CTA had layer-l work in it (the splits differ between
+    // layers, e.g. q|k|v of the Q5_0 and the Q8_0 layers).  Issuing the bulk
+    // copies takes thread 0 a while, so refill() only notes the slot, and
+    // flush() issues the noted copies while the next poll's first loads are in
+    // flight (every phase polls before it waits for a slot; wait_slot flushes
+    // too).
+    uint32_t pend_mask = 0;
+    int pend_l[kSlots];
+    auto refill = [&](int l, int slot) {
+        if (tid < 32) {
+            pend_mask |= 1u << slot;
+            pend_l[slot] = l;
+        }
+    };
+    auto flush = [&]() {
+        if (tid < 32 && pend_mask) {
+            for (int s = 0; s < kSlots; s++)
+                if ((pend_mask >> s) & 1u) {
+                    const int l = pend_l[s];
+                    if (l + 1 < kLayers && ms.armed[s] == ms.waited[s]) {
+                        MEGA_ISSUE_T0();
+                        issue_slot_warp(plans[(l + 1) * kSlots + s], slot_base[s], ms, s, tid);
+                        if (tid == 0) MEGA_ISSUE_T1(l, s);
+                    }
+                }
+            pend_mask = 0;
+        }
+    };
+    const auto hook = [&]() { flush(); };
     // All threads: wait for this layer's copies of `slot`.
     auto wait_slot = [&](int slot) -> bool {
+        flush();
         const uint32_t par = ms.waited[slot] & 1;
         const bool ok = mbar_wait_sleep(&ms.bar[slot], par, a.err);
         if (!ok) ms.abort = 1;
@@ -575,13 +635,6 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaArgs a
         __syncthreads();
         if (!go && tid == 0) atomicExch(a.abort_flag, 1);
         return go;
-    };
-    // Thread 0: fill `slot` with layer l + 1's weights once its layer-l use is
-    // over -- whether or not this CTA had layer-l work in it (the splits differ
-    // between layers, e.g. q|k|v of the Q5_0 and the Q8_0 layers).
-    auto refill = [&](int l, int slot) {
-        if (tid == 0 && l + 1 < kLayers && ms.armed[slot] == ms.waited[slot])
-            issue_slot(plans[(l + 1) * kSlots + slot], slot_base[slot], ms, slot);
     };
     // End of a phase: every value is stored; refill the phase's slot.
     auto finish = [&](int l, int slot) {
@@ -611,7 +664,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaArgs a
                 }
                 __syncthreads();
             } else {
-                if (!poll_smem(a.hid_t, kHidden, tag_of(ep, l - 1, TG_HID_E), xv, ms, a.abort_flag, a.err)) break;
+                if (!poll_smem(a.hid_t, kHidden, tag_of(ep, l - 1, TG_HID_E), xv, ms, a.abort_flag, a.err, hook)) break;
                 MEGA_STAMP(l, 1);
             }
             mega_norm_quantize(xv, sq, L.attn_norm, kHidden, xpl, ms, att, MEGA_NORM_STAMPS(l, 0));
@@ -623,6 +676,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaArgs a
             else mega_blockq<TMAC_TYPE_Q5_0>(slot_base[0], pa, kHidden, xpl, ms.xs, acc_lo, acc_hi, yv, MEGA_BQ_STAMPS(l, 0));
             for (int t = tid; t < (int)pa.rows; t += kMegaThreads)
                 st_tagged(a.qkv_t + pa.out0[0] + t, yv[t], tag_of(ep, l, TG_QKV));
+            MEGA_BQ_MARK(l, 0, 3);
+            __syncthreads();
+            MEGA_BQ_MARK(l, 0, 17);
             finish(l, 0);
             MEGA_STAMP(l, 4);
         } else {
@@ -647,12 +703,11 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaArgs a
                 uint64_t t0 = 0;
                 bool ok = true;
                 for (uint32_t it = 0;; it++) {
-                    if (todo) {
-                        const unsigned long long u = ld_tagged(a.qkv_t + src);
-                        if ((uint32_t)(u >> 32) == tag_of(ep, l, TG_QKV)) {
-                            r[0] = __uint_as_float((uint32_t)u);
-                            todo = 0;
-                        }
+                    const unsigned long long u = todo ? ld_tagged(a.qkv_t + src) : 0ull;
+                    if (it == 0) flush();  // while the load is in flight
+                    if (todo && (uint32_t)(u >> 32) == tag_of(ep, l, TG_QKV)) {
+                        r[0] = __uint_as_float((uint32_t)u);
+                        todo = 0;
                     }
                     if (__syncthreads_and(todo == 0)) break;
                     if ((it & 15u) == 15u) {
@@ -697,7 +752,8 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaArgs a
             ex.n = (int)pc.rows;
             ex.tag = l == 0 ? tag_emb(ep) : tag_of(ep, l - 1, TG_HID_E);
             ex.out = &hres;
-            if (!poll_regs<2>(a.ctx_t, kHidden, tag_of(ep, l, TG_CTX), r, ms, a.abort_flag, a.err, ex)) break;
+            if (!poll_regs<2>(a.ctx_t, kHidden, tag_of(ep, l, TG_CTX), r, ms, a.abort_flag, a.err, ex, PollExtra(), hook))
+                break;
             MEGA_STAMP(l, 7);
             float mx = fmaxf(fabsf(r[0]), tid + kMegaThreads < kHidden ? fabsf(r[1]) : 0.0f);
             mx = block_max(mx, ms.red, kMegaThreads);
@@ -709,6 +765,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaArgs a
             MEGA_STAMP(l, 22);
             if (tid < (int)pc.rows)
                 st_tagged(a.hid_t + pc.out0[0] + tid, __fadd_rn(hres, yv[tid]), tag_of(ep, l, TG_HID_C));
+            MEGA_BQ_MARK(l, 1, 3);
+            __syncthreads();
+            MEGA_BQ_MARK(l, 1, 17);
             finish(l, 1);
             MEGA_STAMP(l, 9);
         } else {
@@ -717,7 +776,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaArgs a
         // ------------------------------------------------ D: gate|up + silu
         const MegaSlot& pd = plans[l * kSlots + 2];
         if (pd.kind != SK_NONE) {
-            if (!poll_smem(a.hid_t, kHidden, tag_of(ep, l, TG_HID_C), xv, ms, a.abort_flag, a.err)) break;
+            if (!poll_smem(a.hid_t, kHidden, tag_of(ep, l, TG_HID_C), xv, ms, a.abort_flag, a.err, hook)) break;
             MEGA_STAMP(l, 10);
             mega_norm_quantize(xv, sq, L.ffn_norm, kHidden, xpl, ms, att, MEGA_NORM_STAMPS(l, 1));
             MEGA_STAMP(l, 11);
@@ -727,6 +786,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaArgs a
             const int n = (int)pd.ngate;
             for (int t = tid; t < n; t += kMegaThreads)
                 st_tagged(a.h_t + pd.out0[0] + t, silu_mul(yv[t], yv[n + t]), tag_of(ep, l, TG_H));
+            MEGA_BQ_MARK(l, 2, 3);
+            __syncthreads();
+            MEGA_BQ_MARK(l, 2, 17);
             finish(l, 2);
             MEGA_STAMP(l, 13);
         } else {
@@ -742,7 +804,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaArgs a
             ex1.n = (int)pe.rows;
             ex1.tag = tag_of(ep, l, TG_HID_C);
             ex1.out = &hres;
-            if (!poll_regs<kMaxQuant>(a.h_t, kInter, tag_of(ep, l, TG_H), r, ms, a.abort_flag, a.err, PollExtra(), ex1))
+            if (!poll_regs<kMaxQuant>(a.h_t, kInter, tag_of(ep, l, TG_H), r, ms, a.abort_flag, a.err, PollExtra(), ex1, hook))
                 break;
             MEGA_STAMP(l, 14);
             // x_scale from max |h| over the values just polled
@@ -762,6 +824,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaArgs a
             MEGA_STAMP(l, 20);
             if (tid < (int)pe.rows)
                 st_tagged(a.hid_t + pe.out0[0] + tid, __fadd_rn(hres, yv[tid]), tag_of(ep, l, TG_HID_E));
+            MEGA_BQ_MARK(l, 3, 3);
+            __syncthreads();
+            MEGA_BQ_MARK(l, 3, 17);
             finish(l, 3);
             MEGA_STAMP(l, 16);
         } else {
