@@ -133,6 +133,13 @@ int64_t tmac_units_per_row(int type, int mode, int64_t cols);
  *              partial sums (see tmac_units_per_row).
  *   stream:    cudaStream_t of the weight's device (NULL = default stream).
  * Asynchronous: returns after enqueueing.
+ * NATIVE Q5_0 / Q4_K / Q6_K with 8 <= batch <= 64, no unit_acc and cols a
+ * multiple of 16 run on the tensor cores (the split-K path of tmac_gemm), with
+ * the same results bit for bit.  The first such call on a weight decodes its
+ * int16 planes (2 bytes per weight, kept with the weight) and may grow the
+ * per-device workspaces, so before CUDA-graph capture make one call per weight
+ * at the largest batch the graph uses.  Calls on one device share the
+ * workspaces: order them on one stream.
  */
 int tmac_gemv(tmac_weight_t w, const float* x, float* y, int batch, void* stream);
 int tmac_gemv_acc(tmac_weight_t w, const float* x, float* y, int64_t* row_acc, int64_t* unit_acc,

@@ -9,6 +9,17 @@ identical to tmac_gemv with batch m, bit for bit, including partial tiles
 import numpy as np
 import pytest
 
+
+def per_row_gemv(w, x, m, rows):
+    """The reference for tmac_gemm: one batch-1 CUDA-core GEMV per activation
+    row (tmac_gemv itself sends batches of 8..64 to the tensor cores)."""
+    import torch
+    y = torch.empty((m, rows), device="cuda")
+    acc = torch.zeros((m, rows), dtype=torch.int64, device="cuda")
+    for i in range(m):
+        w.gemv(x[i], y[i], batch=1, row_acc=acc[i])
+    return y, acc
+
 import tmac_zynq_fpga_b200 as tm
 from tmac_zynq_fpga_b200 import synth
 
@@ -29,13 +40,49 @@ def test_gemm_matches_gemv(qtype, rows, cols, m):
         y = torch.full((m, rows), float("nan"), device="cuda")
         acc = torch.zeros((m, rows), dtype=torch.int64, device="cuda")
         w.gemm(x, y, m, row_acc=acc)
-        y_ref = torch.empty((m, rows), device="cuda")
-        acc_ref = torch.zeros((m, rows), dtype=torch.int64, device="cuda")
-        w.gemv(x, y_ref, batch=m, row_acc=acc_ref)
+        if m <= 64:
+            y_ref, acc_ref = per_row_gemv(w, x, m, rows)
+        else:
+            y_ref = torch.empty((m, rows), device="cuda")
+            acc_ref = torch.zeros((m, rows), dtype=torch.int64, device="cuda")
+            w.gemv(x, y_ref, batch=m, row_acc=acc_ref)
         torch.cuda.synchronize()
         assert tm.device_error(0) == 0
         assert torch.equal(acc, acc_ref)
         assert torch.equal(y.view(torch.int32), y_ref.view(torch.int32))
+    finally:
+        w.free()
+
+
+SKINNY = [(synth.Q4_K, 896, 4864, 16), (synth.Q6_K, 896, 4864, 16), (synth.Q5_0, 200, 96, 5),
+          (synth.Q5_0, 1152, 896, 33), (synth.Q4_K, 896, 4864, 64), (synth.Q5_0, 4864, 896, 1)]
+
+
+@pytest.mark.parametrize("qtype,rows,cols,m", SKINNY)
+def test_skinny_split_k_matches_gemv(qtype, rows, cols, m):
+    """m <= 64 rows: weights as the 128-row MMA operand, the batch as N, K split
+    across CTAs with int64 partial sums in a workspace that the last CTA of each
+    row tile drains and zeroes -- three calls in a row must all match."""
+    torch = pytest.importorskip("torch")
+    w = tm.Weight(qtype, rows, cols, synth.make_weights(qtype, rows, cols, seed=111))
+    try:
+        for call in range(3):
+            x = torch.from_numpy(synth.make_activations(cols, batch=m, seed=112 + call)).cuda()
+            if m > 3:
+                x[3] *= 1000.0
+                x[m - 1] = 0.0
+            y = torch.full((m, rows), float("nan"), device="cuda")
+            acc = torch.zeros((m, rows), dtype=torch.int64, device="cuda")
+            w.gemm(x, y, m, row_acc=acc)
+            y_ref, acc_ref = per_row_gemv(w, x, m, rows)
+            # tmac_gemv at this batch (tensor cores from batch 8) agrees as well
+            y_b = torch.empty((m, rows), device="cuda")
+            w.gemv(x, y_b, batch=m)
+            torch.cuda.synchronize()
+            assert tm.device_error(0) == 0
+            assert torch.equal(y_b.view(torch.int32), y_ref.view(torch.int32)), call
+            assert torch.equal(acc, acc_ref), call
+            assert torch.equal(y.view(torch.int32), y_ref.view(torch.int32)), call
     finally:
         w.free()
 

@@ -151,3 +151,27 @@ def test_quantize_once_matches_gemv(qtype, rows, cols, batch):
         assert np.float32(xs[b].item()) == xs_o
         np.testing.assert_array_equal(xq[b].cpu().numpy(), xq_o)
     w.free()
+
+
+@pytest.mark.parametrize("qtype,rows,cols,batch", [(tm.Q4_K, 896, 4864, 16), (tm.Q6_K, 896, 4864, 8),
+                                                   (tm.Q5_0, 4864, 896, 64), (tm.Q5_0, 200, 96, 9)])
+def test_tensor_core_batches_equal_the_oracle(qtype, rows, cols, batch):
+    """Batches of 8..64 without per-unit sums run on the tensor cores (split-K
+    tcgen05 kernel); y and the int64 row sums must still equal the oracle."""
+    raw = synth.make_weights(qtype, rows, cols, seed=rows + batch)
+    x = synth.make_activations(cols, batch=batch, seed=batch)
+    w = tm.Weight(qtype, rows, cols, raw)
+    try:
+        xt = torch.from_numpy(x).cuda()
+        y = torch.empty((batch, rows), dtype=torch.float32, device="cuda")
+        ra = torch.zeros((batch, rows), dtype=torch.int64, device="cuda")
+        w.gemv(xt, y, batch=batch, row_acc=ra)
+        torch.cuda.synchronize()
+        assert tm.device_error(w.device) == 0
+        y, ra = y.cpu().numpy(), ra.cpu().numpy()
+        for b in range(0, batch, max(1, batch // 4)):
+            o = oracle.gemv(qtype, raw, rows, cols, x[b], path=oracle.PATH_NATIVE)
+            np.testing.assert_array_equal(y[b].view(np.int32), o.y.view(np.int32), err_msg=f"y bits differ (batch {b})")
+            np.testing.assert_array_equal(ra[b], o.row_acc, err_msg="int64 row sums differ")
+    finally:
+        w.free()

@@ -319,6 +319,8 @@ int blockq_planes(const tmac_weight_s* w, int8_t* wh, uint8_t* wl, cudaStream_t 
 // Tensor-core GEMM (gemm_tc.cu): Y[m][rows] = the GEMV of each of m fp32 rows.
 int gemm_prepare(tmac_weight_s* w, cudaStream_t s);
 int launch_gemm(tmac_weight_s* w, const float* x, float* y, int64_t* acc_out, int M, cudaStream_t s);
+// Batches tmac_gemv sends to the tensor cores (NATIVE Q5_0 / Q4_K / Q6_K).
+constexpr int kTcMinBatch = 8, kTcMaxBatch = 64;
 // Activation rows -> x_scale and byte planes (x_q = 256*xh + xl).
 int quantize_rows(const float* x, int64_t K, int M, int8_t* xh, uint8_t* xl, float* xs, cudaStream_t s);
 // One GEMM over byte planes: columns [k_off, k_off + K) of X [M][x_stride] and

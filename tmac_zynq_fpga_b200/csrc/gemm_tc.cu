@@ -258,6 +258,221 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+// ------------------------------------------------- skinny batches, split K --
+// M <= 64 activation rows (a batched GEMV): the weights are the 128-row MMA
+// operand and the batch the N operand (16..64 columns), and K is split across
+// CTAs so that ~one CTA per SM streams its share of the weight planes once.
+// CTA (mt, ks) accumulates k-blocks [ks * kchunk, ...) of weight rows
+// [128 mt, 128 mt + 128) in TMEM, adds its int64 partial sums into a zeroed
+// workspace with atomics (integer sums: the order does not matter), and the
+// last CTA of the row tile (counter) takes the totals -- atomicExch leaves the
+// workspace zeroed for the next call -- and forms y as the GEMM epilogue does.
+constexpr int SK_BM = 128, SK_STAGES = 4, SK_MAXNB = 64;
+constexpr int kSkThreads = 6 * 32;  // warp 0 TMA, warp 1 MMA + TMEM, warps 2..5 epilogue (TMEM lane quarters 2,3,0,1)
+
+struct SkArgs {
+    const float* xs;           // [batch] x_scale
+    const float* ri;           // [rows] row_inv
+    const double* rinv;        // [rows] RN(1 / row_inv)
+    float* y;                  // [batch][rows]
+    int64_t* acc_out;          // optional [batch][rows]
+    unsigned long long* ws;    // [batch][rows] zeroed int64 sums
+    unsigned* cnt;             // [tiles_m] zeroed arrival counters
+    int rows, batch, NB, KB, kchunk, ksplit;
+    int* err;
+};
+
+#ifdef TMAC_TRACE
+__device__ unsigned long long g_sk_trace[160][8];
+__device__ unsigned long long g_q_trace[64][4];
+#define SK_STAMP(i) do { if (blockIdx.x < 160) g_sk_trace[blockIdx.x][i] = global_timer_ns(); } while (0)
+#else
+#define SK_STAMP(i) do { } while (0)
+#endif
+
+__host__ __device__ constexpr uint32_t sk_stage_bytes(int NB) { return 2u * SK_BM * BK + 2u * (uint32_t)NB * BK; }
+__host__ __device__ constexpr uint32_t sk_tmem_cols(int NB) { return 3 * NB <= 64 ? 64u : (3 * NB <= 128 ? 128u : 256u); }
+
+__global__ void __launch_bounds__(kSkThreads, 1)
+    gemv_tc_splitk_kernel(const __grid_constant__ CUtensorMap tm_wh, const __grid_constant__ CUtensorMap tm_wl,
+                          const __grid_constant__ CUtensorMap tm_xh, const __grid_constant__ CUtensorMap tm_xl, SkArgs a)
+{
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    const uint32_t stage_bytes = sk_stage_bytes(a.NB), tile_w = SK_BM * BK, tile_x = (uint32_t)a.NB * BK;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + SK_STAGES * stage_bytes);
+    uint64_t* empty = full + SK_STAGES;
+    uint64_t* tfull = empty + SK_STAGES;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfull + 1);
+    volatile int* flags = reinterpret_cast<volatile int*>(tmem_slot + 1);  // [0] abort, [1] last CTA of the tile
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int mt = blockIdx.x / a.ksplit, ks = blockIdx.x % a.ksplit;
+    const int kb0 = ks * a.kchunk, nkb = min(a.KB, kb0 + a.kchunk) - kb0;
+    const uint32_t tcols = sk_tmem_cols(a.NB);
+
+    if (threadIdx.x == 0) {
+        SK_STAMP(0);
+        for (int i = 0; i < SK_STAGES; i++) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 1);
+        }
+        mbar_init(tfull, 1);
+        flags[0] = 0;
+        flags[1] = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, tcols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    pdl_launch();  // the next kernel's writes of the x planes wait for this grid (its pdl_wait)
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // the weight planes of the first stages do not depend on the preceding
+            // kernel: their copies start before the wait for the x planes
+            const int pre = min(nkb, SK_STAGES);
+            for (int i = 0; i < pre; i++) {
+                uint8_t* st = smem + i * stage_bytes;
+                const int kx = (kb0 + i) * BK;
+                mbar_arrive_expect_tx(&full[i], stage_bytes);
+                tma_load_2d(st, &tm_wh, kx, mt * SK_BM, &full[i]);
+                tma_load_2d(st + tile_w, &tm_wl, kx, mt * SK_BM, &full[i]);
+            }
+            SK_STAMP(1);
+            pdl_wait();  // x planes come from the preceding quantisation kernel
+            SK_STAMP(2);
+            for (int i = 0; i < nkb; i++) {
+                const int s = i % SK_STAGES;
+                uint8_t* st = smem + s * stage_bytes;
+                const int kx = (kb0 + i) * BK;
+                if (i >= pre) {
+                    if (!mbar_wait_bounded(&empty[s], ((i / SK_STAGES) - 1) & 1, a.err)) {
+                        flags[0] = 1;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&full[s], stage_bytes);
+                    tma_load_2d(st, &tm_wh, kx, mt * SK_BM, &full[s]);
+                    tma_load_2d(st + tile_w, &tm_wl, kx, mt * SK_BM, &full[s]);
+                }
+                tma_load_2d(st + 2 * tile_w, &tm_xh, kx, 0, &full[s]);
+                tma_load_2d(st + 2 * tile_w + tile_x, &tm_xl, kx, 0, &full[s]);
+            }
+        } else {
+            pdl_wait();
+        }
+    } else if (warp == 1) {
+        pdl_wait();
+        if (lane == 0) {
+            const uint32_t NB = (uint32_t)a.NB;
+            const uint32_t kHH = idesc_i8_mn(1, 1, SK_BM, NB), kHL = idesc_i8_mn(1, 0, SK_BM, NB);
+            const uint32_t kLH = idesc_i8_mn(0, 1, SK_BM, NB), kLL = idesc_i8_mn(0, 0, SK_BM, NB);
+            for (int i = 0; i < nkb; i++) {
+                const int s = i % SK_STAGES;
+                if (flags[0] || !mbar_wait_bounded(&full[s], (i / SK_STAGES) & 1, a.err)) {
+                    flags[0] = 1;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t st = smem_addr(smem + s * stage_bytes);
+#pragma unroll
+                for (int kk = 0; kk < BK / 32; kk++) {
+                    const uint64_t wh = desc_sw128(st + kk * 32), wl = desc_sw128(st + tile_w + kk * 32);
+                    const uint64_t xh = desc_sw128(st + 2 * tile_w + kk * 32);
+                    const uint64_t xl = desc_sw128(st + 2 * tile_w + tile_x + kk * 32);
+                    const uint32_t acc = (i | kk) != 0;
+                    mma_i8(tmem, wh, xh, kHH, acc);
+                    mma_i8(tmem + NB, wh, xl, kHL, acc);
+                    mma_i8(tmem + NB, wl, xh, kLH, 1u);
+                    mma_i8(tmem + 2 * NB, wl, xl, kLL, acc);
+                }
+                mma_commit(&empty[s]);
+            }
+            mma_commit(tfull);  // completes when every MMA issued above has
+        }
+    } else {
+        pdl_wait();  // x_scale is read by the last CTA's epilogue
+        // epilogue: TMEM lane = weight row of the tile, columns = batch entries
+        const int q = warp & 3;
+        const int row = mt * SK_BM + q * 32 + lane;
+        bool ok = !flags[0] && mbar_wait_bounded(tfull, 0, a.err);
+        ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld below is warp-collective
+        if (ok) {
+            tc_fence_after();
+            if (q == 0 && lane == 0) SK_STAMP(3);
+            const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16);
+            for (int c = 0; c < a.NB; c += 8) {
+                uint32_t hh[8], md[8], ll[8];
+                tmem_ld8(taddr + c, hh);
+                tmem_ld8(taddr + a.NB + c, md);
+                tmem_ld8(taddr + 2 * a.NB + c, ll);
+                tmem_wait_ld();
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    const int b = c + j;
+                    if (b < a.batch && row < a.rows) {
+                        const long long part = (long long)(int32_t)hh[j] * 65536 + (long long)(int32_t)md[j] * 256 +
+                                               (long long)(int32_t)ll[j];
+                        atomicAdd(a.ws + (int64_t)b * a.rows + row, (unsigned long long)part);
+                    }
+                }
+            }
+        } else {
+            flags[0] = 1;
+        }
+        __threadfence();
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        SK_STAMP(4);
+        flags[1] = (atomicAdd(a.cnt + mt, 1u) == (unsigned)(a.ksplit - 1)) ? 1 : 0;
+        SK_STAMP(5);
+    }
+    __syncthreads();
+    if (flags[1]) {
+        __threadfence();
+        if (warp >= 2) {
+            const int q = warp & 3;
+            const int row = mt * SK_BM + q * 32 + lane;
+            if (row < a.rows) {
+                const double rinv = a.rinv[row];
+                const float ri = a.ri[row];
+                // every other CTA's atomics on these sums were performed before its
+                // counter increment: plain L2 loads, issued 16 at a time, see the
+                // totals; the stores of 0 leave the workspace clean for the next call
+                for (int b0 = 0; b0 < a.batch; b0 += 16) {
+                    long long acc[16];
+#pragma unroll
+                    for (int j = 0; j < 16; j++)
+                        acc[j] = b0 + j < a.batch ? (long long)__ldcg(a.ws + (int64_t)(b0 + j) * a.rows + row) : 0;
+#pragma unroll
+                    for (int j = 0; j < 16; j++) {
+                        const int b = b0 + j;
+                        if (b < a.batch) {
+                            a.ws[(int64_t)b * a.rows + row] = 0ull;
+                            const double p = __dmul_rn((double)acc[j], (double)a.xs[b]);
+                            a.y[(int64_t)b * a.rows + row] = quotient_f32(p, rinv, ri);
+                            if (a.acc_out) a.acc_out[(int64_t)b * a.rows + row] = acc[j];
+                        }
+                    }
+                }
+            }
+        }
+        if (threadIdx.x == 0) a.cnt[mt] = 0;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        SK_STAMP(6);
+    }
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, tcols);
+    }
+}
+
 __global__ void rinv_kernel(const float* __restrict__ ri, int64_t n, double* __restrict__ out)
 {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -265,14 +480,24 @@ __global__ void rinv_kernel(const float* __restrict__ ri, int64_t n, double* __r
 }
 
 // Activation rows -> x_scale and byte planes (one CTA per row, tmac_gguf.cpp:889-896).
-__global__ void __launch_bounds__(256) quantize_rows_kernel(const float* __restrict__ x, int64_t K,
+#ifndef TMAC_QUANT_THREADS
+#define TMAC_QUANT_THREADS 1024
+#endif
+constexpr int kQuantThreads = TMAC_QUANT_THREADS;
+__global__ void __launch_bounds__(kQuantThreads) quantize_rows_kernel(const float* __restrict__ x, int64_t K,
                                                             int8_t* __restrict__ xh, uint8_t* __restrict__ xl,
                                                             float* __restrict__ xs)
 
 {
-    __shared__ float red[8];
+    __shared__ float red[kQuantThreads / 32];
+#ifdef TMAC_TRACE
+    if (threadIdx.x == 0 && blockIdx.x < 64) g_q_trace[blockIdx.x][0] = global_timer_ns();
+#endif
     pdl_launch();
     pdl_wait();
+#ifdef TMAC_TRACE
+    if (threadIdx.x == 0 && blockIdx.x < 64) g_q_trace[blockIdx.x][1] = global_timer_ns();
+#endif
     const float* xr = x + (int64_t)blockIdx.x * K;
     float mx = 0.0f;
     for (int64_t j = threadIdx.x; j < K; j += blockDim.x) mx = fmaxf(mx, fabsf(xr[j]));
@@ -284,6 +509,10 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const float* __restr
         xh[(int64_t)blockIdx.x * K + j] = (int8_t)(q >> 8);
         xl[(int64_t)blockIdx.x * K + j] = (uint8_t)(q & 0xFF);
     }
+#ifdef TMAC_TRACE
+    __syncthreads();
+    if (threadIdx.x == 0 && blockIdx.x < 64) g_q_trace[blockIdx.x][2] = global_timer_ns();
+#endif
 }
 
 // ------------------------------------------------------------------ host --
@@ -302,6 +531,13 @@ int encode_plane_map(CUtensorMap* tm, const void* base, int64_t rows, int64_t K,
     if (r != CUDA_SUCCESS) return fail(TMAC_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
     return TMAC_OK;
 }
+
+struct SkWorkspace {
+    unsigned long long* acc = nullptr;  // zeroed between calls
+    unsigned* cnt = nullptr;
+    size_t acc_cap = 0, cnt_cap = 0;
+};
+std::vector<SkWorkspace> g_sk_ws;
 
 struct GemmWorkspace {
     int8_t* xh = nullptr;
@@ -339,6 +575,31 @@ int gemm_workspace(int device, int64_t M, int64_t K, GemmWorkspace** out)
     return TMAC_OK;
 }
 
+int sk_workspace(int device, size_t nacc, size_t ncnt, SkWorkspace** out)
+{
+    // the caller holds g_gemm_mutex
+    if ((int)g_sk_ws.size() <= device) g_sk_ws.resize(device + 1);
+    SkWorkspace& w = g_sk_ws[device];
+    if (w.acc_cap < nacc) {
+        if (w.acc) cudaFree(w.acc);
+        w.acc = nullptr;
+        w.acc_cap = 0;
+        TMAC_CUDA_TRY(cudaMalloc(&w.acc, nacc * sizeof(unsigned long long)));
+        TMAC_CUDA_TRY(cudaMemset(w.acc, 0, nacc * sizeof(unsigned long long)));
+        w.acc_cap = nacc;
+    }
+    if (w.cnt_cap < ncnt) {
+        if (w.cnt) cudaFree(w.cnt);
+        w.cnt = nullptr;
+        w.cnt_cap = 0;
+        TMAC_CUDA_TRY(cudaMalloc(&w.cnt, ncnt * sizeof(unsigned)));
+        TMAC_CUDA_TRY(cudaMemset(w.cnt, 0, ncnt * sizeof(unsigned)));
+        w.cnt_cap = ncnt;
+    }
+    *out = &w;
+    return TMAC_OK;
+}
+
 }  // namespace
 
 // Exact int16 planes of the weight, decoded on first use.
@@ -358,7 +619,7 @@ int gemm_prepare(tmac_weight_s* w, cudaStream_t s)
 
 int quantize_rows(const float* x, int64_t K, int M, int8_t* xh, uint8_t* xl, float* xs, cudaStream_t s)
 {
-    TMAC_CUDA_TRY(launch_k(quantize_rows_kernel, dim3(M), dim3(256), 0, s, x, K, xh, xl, xs));
+    TMAC_CUDA_TRY(launch_k(quantize_rows_kernel, dim3(M), dim3(kQuantThreads), 0, s, x, K, xh, xl, xs));
     TMAC_CUDA_TRY(cudaGetLastError());
     return TMAC_OK;
 }
@@ -438,6 +699,61 @@ int launch_gemm_q8(tmac_weight_s* w, const float* x, float* y, int M, cudaStream
     return TMAC_OK;
 }
 
+// M <= SK_MAXNB rows: gemv_tc_splitk_kernel over the quantised rows in ws.
+int launch_gemm_skinny(tmac_weight_s* w, GemmWorkspace* ws, float* y, int64_t* acc_out, int M, cudaStream_t s)
+{
+    const int NB = (M + 15) / 16 * 16;
+    const int tiles_m = (int)((w->rows + SK_BM - 1) / SK_BM);
+    const int KB = (int)((w->cols + BK - 1) / BK);
+#ifndef TMAC_SK_DIV
+#define TMAC_SK_DIV 1
+#endif
+    const int target = std::max(1, num_sms(w->device) / tiles_m / TMAC_SK_DIV);
+    const int kchunk = (KB + target - 1) / target;
+    const int ksplit = (KB + kchunk - 1) / kchunk;
+    SkWorkspace* sk = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_gemm_mutex);
+        int rc = sk_workspace(w->device, (size_t)M * (size_t)w->rows, (size_t)tiles_m, &sk);
+        if (rc) return rc;
+    }
+    alignas(64) CUtensorMap tm[4];
+    int rc;
+    const uint8_t* wh = reinterpret_cast<const uint8_t*>(w->gwh);
+    const uint8_t* wl = reinterpret_cast<const uint8_t*>(w->gwl);
+    if ((rc = encode_plane_map(&tm[0], wh, w->rows, w->cols, w->cols, SK_BM)) ||
+        (rc = encode_plane_map(&tm[1], wl, w->rows, w->cols, w->cols, SK_BM)) ||
+        (rc = encode_plane_map(&tm[2], reinterpret_cast<const uint8_t*>(ws->xh), M, w->cols, w->cols, (uint32_t)NB)) ||
+        (rc = encode_plane_map(&tm[3], ws->xl, M, w->cols, w->cols, (uint32_t)NB)))
+        return rc;
+    const size_t smem = SK_STAGES * (size_t)sk_stage_bytes(NB) + 1024 + 256;
+    static bool attr[64] = {};
+    if (!attr[w->device & 63]) {
+        TMAC_CUDA_TRY(cudaFuncSetAttribute(gemv_tc_splitk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)(SK_STAGES * (size_t)sk_stage_bytes(SK_MAXNB) + 1024 + 256)));
+        attr[w->device & 63] = true;
+    }
+    SkArgs a;
+    a.xs = ws->xs;
+    a.ri = w->row_norm;
+    a.rinv = reinterpret_cast<const double*>(w->grinv);
+    a.y = y;
+    a.acc_out = acc_out;
+    a.ws = sk->acc;
+    a.cnt = sk->cnt;
+    a.rows = (int)w->rows;
+    a.batch = M;
+    a.NB = NB;
+    a.KB = KB;
+    a.kchunk = kchunk;
+    a.ksplit = ksplit;
+    a.err = device_error_word(w->device);
+    TMAC_CUDA_TRY(launch_k(gemv_tc_splitk_kernel, dim3((unsigned)(tiles_m * ksplit)), dim3(kSkThreads), smem, s,
+                           tm[0], tm[1], tm[2], tm[3], a));
+    TMAC_CUDA_TRY(cudaGetLastError());
+    return TMAC_OK;
+}
+
 int launch_gemm(tmac_weight_s* w, const float* x, float* y, int64_t* acc_out, int M, cudaStream_t s)
 {
     if (w->type == TMAC_TYPE_Q8_0) return launch_gemm_q8(w, x, y, M, s);
@@ -446,6 +762,7 @@ int launch_gemm(tmac_weight_s* w, const float* x, float* y, int64_t* acc_out, in
     GemmWorkspace* ws = nullptr;
     if ((rc = gemm_workspace(w->device, M, w->cols, &ws))) return rc;
     if ((rc = quantize_rows(x, w->cols, M, ws->xh, ws->xl, ws->xs, s))) return rc;
+    if (M <= SK_MAXNB) return launch_gemm_skinny(w, ws, y, acc_out, M, s);
     GemmOperands op;
     op.xh = reinterpret_cast<const uint8_t*>(ws->xh);
     op.xl = ws->xl;
@@ -471,6 +788,17 @@ int launch_gemm(tmac_weight_s* w, const float* x, float* y, int64_t* acc_out, in
 }  // namespace tmac
 
 using namespace tmac;
+
+#ifdef TMAC_TRACE
+extern "C" int tmac_trace_read_sk(unsigned long long* out)
+{
+    return (int)cudaMemcpyFromSymbol(out, tmac::g_sk_trace, sizeof(tmac::g_sk_trace));
+}
+extern "C" int tmac_trace_read_q(unsigned long long* out)
+{
+    return (int)cudaMemcpyFromSymbol(out, tmac::g_q_trace, sizeof(tmac::g_q_trace));
+}
+#endif
 
 extern "C" int tmac_gemm(tmac_weight_t w, const float* x, float* y, int64_t* row_acc, int m, void* stream)
 {
