@@ -121,6 +121,22 @@ TMAC_DEV float x_scale_from_max(float mx) { return (mx < 1e-10f) ? 1.0f : __fdiv
 // x_q of tmac_gguf.cpp:894-896.
 TMAC_DEV int16_t quantize_one(float x, float xs) { return (int16_t)(int)roundf(__fdiv_rn(x, xs)); }
 
+// (float)(p / ri) with p / ri rounded to double first, as the GEMV computes it
+// (__ddiv_rn then the float conversion).  p * RN(1/ri) is within 2 double ulps
+// of the double quotient; unless its 29 bits below float precision lie within
+// 16 units of the float rounding midpoint (or the value is outside the normal
+// float range) both round to the same float, else the exact division decides.
+TMAC_DEV float quotient_f32(double p, double rinv, float ri)
+{
+    const double q = __dmul_rn(p, rinv);
+    const long long bits = __double_as_longlong(q);
+    const int exp = (int)((bits >> 52) & 0x7FF);
+    const int low = (int)(bits & 0x1FFFFFFF);
+    const bool near_mid = abs(low - 0x10000000) <= 16;
+    if (near_mid || exp < 1023 - 120 || exp > 1023 + 120) return (float)__ddiv_rn(p, (double)ri);
+    return (float)q;
+}
+
 // ----------------------------------------------------- mbarrier / bulk copy
 TMAC_DEV uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 

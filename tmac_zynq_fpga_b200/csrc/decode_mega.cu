@@ -58,6 +58,12 @@ constexpr int kMegaThreads = 768;
 constexpr int kMegaWarps = kMegaThreads / 32;
 constexpr int kSlots = 4;  // weight slots: q|k|v, attn_output, gate|up, ffn_down
 constexpr int kMaxSeg = 6;
+// Per-row constants of a block-quant matrix as the slots carry them: row_inv
+// and RN(1 / row_inv) in double for the epilogue (quotient_f32).
+struct RowConst {
+    float ri, pad;
+    double rinv;
+};
 enum : uint32_t { SK_NONE = 0, SK_Q5 = 1, SK_Q8 = 2, SK_Q4K = 3, SK_Q6K = 4 };
 constexpr size_t kMaxSmemBytes = 227 * 1024;
 
@@ -72,7 +78,7 @@ struct MegaSeg {
 struct MegaSlot {
     MegaSeg seg[kMaxSeg];
     uint32_t total, nseg, kind, rows;  // expect-tx bytes, copies, SK_*, local rows
-    uint32_t ri_off, exc_off, exc_n, ngate;  // ngate: local rows of range 0
+    uint32_t ri_off, exc_off, exc_n, ngate;  // ngate: local rows of range 0; ri_off: RowConst[rows]
     int32_t row0[2];   // first weight row of each range
     int32_t out0[2];   // output index of each range's first row
 };
@@ -267,7 +273,7 @@ TMAC_DEV void mega_blockq(const uint8_t* wsm, const MegaSlot& sp, int cols, cons
     const int64_t cpr = cols / 32, nblk = cols / Geo<TYPE>::kBlockVals;
     const int64_t group_bytes = Geo<TYPE>::group_bytes(nblk);
     const int rows_cta = (int)sp.rows, ng = rows_cta / 8;
-    const float* ri_s = reinterpret_cast<const float*>(wsm + sp.ri_off);
+    const RowConst* rc_s = reinterpret_cast<const RowConst*>(wsm + sp.ri_off);
     const int4* exc_s = reinterpret_cast<const int4*>(wsm + sp.exc_off);
     for (int t = tid; t < rows_cta; t += kMegaThreads) acc_lo[t] = acc_hi[t] = 0;
     __syncthreads();
@@ -287,7 +293,7 @@ TMAC_DEV void mega_blockq(const uint8_t* wsm, const MegaSlot& sp, int cols, cons
         const int rr = q5 ? slot * 8 + r_lane : slot;
         const SharedBytes G{wsm_a + (uint32_t)(rr >> 3) * (uint32_t)group_bytes};
         const int r = rr & 7;
-        const float ri = ri_s[rr];
+        const float ri = rc_s[rr].ri;
         const uint32_t ch = q5 ? (uint32_t)(4 * s + l_lane) : (uint32_t)(4 * s + (lane >> 3)) * 8 + (lane & 7);
         if (ch < cpr) {
             Chunk c;
@@ -320,7 +326,7 @@ TMAC_DEV void mega_blockq(const uint8_t* wsm, const MegaSlot& sp, int cols, cons
     if (stamps && threadIdx.x == 0) stamps[1] = global_timer_ns();
     for (int t = tid; t < rows_cta; t += kMegaThreads) {
         const long long tot = (long long)(((unsigned long long)acc_hi[t] << 32) | acc_lo[t]);
-        yv[t] = (float)__ddiv_rn(__dmul_rn((double)tot, (double)xs), (double)ri_s[t]);
+        yv[t] = quotient_f32(__dmul_rn((double)tot, (double)xs), rc_s[t].rinv, rc_s[t].ri);
     }
     __syncthreads();
     if (stamps && threadIdx.x == 0) stamps[2] = global_timer_ns();
@@ -886,6 +892,7 @@ struct MegaState {
     int* dev_abort = nullptr;                // cleared before every launch
     unsigned long long* dev_tagged = nullptr;  // hidden | q|k|v | ctx | h
     uint32_t epoch = 0;                        // tag base of the last launch
+    std::vector<void*> rowc;                   // RowConst arrays of the block-quant matrices
 };
 
 namespace {
@@ -903,8 +910,8 @@ void add_seg(MegaSlot& sp, const void* src, uint32_t bytes, uint32_t* off)
 }
 
 // A block-quant slot over up to two ranges of 8-row groups [g0, g1) of w.
-int blockq_slot(const tmac_weight_s* w, const std::vector<int>& exc_ptr, const int64_t (&g0)[2],
-                const int64_t (&g1)[2], const int32_t (&out0)[2], int nrange, MegaSlot& sp)
+int blockq_slot(const tmac_weight_s* w, const RowConst* rowc, const std::vector<int>& exc_ptr,
+                const int64_t (&g0)[2], const int64_t (&g1)[2], const int32_t (&out0)[2], int nrange, MegaSlot& sp)
 {
     sp = MegaSlot{};
     int64_t rows = 0;
@@ -917,7 +924,7 @@ int blockq_slot(const tmac_weight_s* w, const std::vector<int>& exc_ptr, const i
         add_seg(sp, w->data + g0[r] * w->group_bytes, (uint32_t)((g1[r] - g0[r]) * w->group_bytes), &off);
     sp.ri_off = off;
     for (int r = 0; r < nrange; r++)
-        add_seg(sp, w->row_norm + 8 * g0[r], (uint32_t)(32 * (g1[r] - g0[r])), &off);
+        add_seg(sp, rowc + 8 * g0[r], (uint32_t)(8 * sizeof(RowConst) * (g1[r] - g0[r])), &off);
     sp.exc_off = off;
     for (int r = 0; r < nrange; r++) {
         const int64_t e0 = exc_ptr[std::min<int64_t>(8 * g0[r], w->rows)];
@@ -930,6 +937,31 @@ int blockq_slot(const tmac_weight_s* w, const std::vector<int>& exc_ptr, const i
         sp.out0[r] = r < nrange ? out0[r] : 0;
     }
     sp.ngate = (uint32_t)(8 * (g1[0] - g0[0]));
+    return TMAC_OK;
+}
+
+__global__ void rowconst_kernel(const float* __restrict__ ri, const double* __restrict__ rinv, int64_t n,
+                                RowConst* __restrict__ out)
+{
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) out[i] = RowConst{ri[i], 0.0f, rinv[i]};
+}
+
+// The RowConst array of w (rows padded to whole groups), made once per weight.
+int row_consts(const tmac_weight_s* w, std::map<const tmac_weight_s*, RowConst*>& made, const RowConst** out)
+{
+    auto it = made.find(w);
+    if (it != made.end()) {
+        *out = it->second;
+        return TMAC_OK;
+    }
+    const int64_t n = w->groups * 8;
+    RowConst* p = nullptr;
+    TMAC_CUDA_TRY(cudaMalloc(&p, (size_t)n * sizeof(RowConst)));
+    made[w] = p;
+    rowconst_kernel<<<(unsigned)((n + 255) / 256), 256>>>(w->row_norm, static_cast<const double*>(w->grinv), n, p);
+    TMAC_CUDA_TRY(cudaGetLastError());
+    *out = p;
     return TMAC_OK;
 }
 
@@ -949,7 +981,7 @@ const tmac_weight_s* find_mat(tmac_model_s* m, const std::string& name)
 bool native_blockq(const tmac_weight_s* w, int type, int64_t rows, int64_t cols)
 {
     if (!w || w->mode != TMAC_MODE_NATIVE || w->type != type || w->rows != rows || w->cols != cols || !w->exc ||
-        !w->exc_ptr)
+        !w->exc_ptr || !w->grinv)
         return false;
     int64_t gb = 0;
     if (type == TMAC_TYPE_Q5_0) gb = Geo<TMAC_TYPE_Q5_0>::group_bytes(cols / 32);
@@ -967,6 +999,7 @@ void mega_free(MegaState* st)
     if (st->dev_slots) cudaFree(st->dev_slots);
     if (st->dev_abort) cudaFree(st->dev_abort);
     if (st->dev_tagged) cudaFree(st->dev_tagged);
+    for (void* p : st->rowc) cudaFree(p);
     delete st;
 }
 
@@ -985,6 +1018,14 @@ int mega_prepare(tmac_model_s* m, MegaState** out)
     uint32_t slot_bytes[kSlots] = {0, 0, 0, 0};
     uint32_t max_rows = 32;
     std::vector<int> ep_a, ep_o, ep_g, ep_d;
+    std::map<const tmac_weight_s*, RowConst*> rowc;  // handed to the state on success, else freed
+    struct FreeRowc {
+        std::map<const tmac_weight_s*, RowConst*>* m;
+        ~FreeRowc()
+        {
+            for (auto& kv : *m) cudaFree(kv.second);
+        }
+    } free_rowc{&rowc};
     for (int l = 0; l < kLayers; l++) {
         MegaLayer& L = layers[l];
         L.attn_norm = vec_or_null(m, lname(l, "attn_norm.weight"));
@@ -1018,6 +1059,10 @@ int mega_prepare(tmac_model_s* m, MegaState** out)
         if ((rc = host_exc_ptr(q5_layer ? qkv : qk, ep_a)) || (rc = host_exc_ptr(wo, ep_o)) ||
             (rc = host_exc_ptr(gu, ep_g)) || (rc = host_exc_ptr(wd, ep_d)))
             return rc;
+        const RowConst *rc_a = nullptr, *rc_o = nullptr, *rc_g = nullptr, *rc_d = nullptr;
+        if ((rc = row_consts(q5_layer ? qkv : qk, rowc, &rc_a)) || (rc = row_consts(wo, rowc, &rc_o)) ||
+            (rc = row_consts(gu, rowc, &rc_g)) || (rc = row_consts(wd, rowc, &rc_d)))
+            return rc;
         for (int c = 0; c < G; c++) {
             MegaSlot* sp = &slots[((size_t)c * kLayers + l) * kSlots];
             int64_t a0[2] = {0, 0}, a1[2] = {0, 0};
@@ -1027,11 +1072,11 @@ int mega_prepare(tmac_model_s* m, MegaState** out)
             if (q5_layer) {
                 split(qkv->groups, G, c, &a0[0], &a1[0]);
                 o0[0] = (int32_t)(8 * a0[0]);
-                if ((rc = blockq_slot(qkv, ep_a, a0, a1, o0, 1, sp[0]))) return rc;
+                if ((rc = blockq_slot(qkv, rc_a, ep_a, a0, a1, o0, 1, sp[0]))) return rc;
             } else if (c < G - 4) {
                 split(qk->groups, G - 4, c, &a0[0], &a1[0]);
                 o0[0] = (int32_t)(8 * a0[0]);
-                if ((rc = blockq_slot(qk, ep_a, a0, a1, o0, 1, sp[0]))) return rc;
+                if ((rc = blockq_slot(qk, rc_a, ep_a, a0, a1, o0, 1, sp[0]))) return rc;
             } else {
                 const int gi = c - (G - 4);
                 MegaSlot& s0 = sp[0];
@@ -1045,7 +1090,7 @@ int mega_prepare(tmac_model_s* m, MegaState** out)
             // C: attn_output rows
             split(wo->groups, G, c, &a0[0], &a1[0]);
             o0[0] = (int32_t)(8 * a0[0]);
-            if ((rc = blockq_slot(wo, ep_o, a0, a1, o0, 1, sp[1]))) return rc;
+            if ((rc = blockq_slot(wo, rc_o, ep_o, a0, a1, o0, 1, sp[1]))) return rc;
             // D: gate groups [p0, p1) with the up groups holding the same rows
             int64_t p0, p1;
             split(gu->groups / 2, G, c, &p0, &p1);
@@ -1055,11 +1100,11 @@ int mega_prepare(tmac_model_s* m, MegaState** out)
             a1[1] = gu->groups / 2 + p1;
             o0[0] = (int32_t)(8 * p0);
             o0[1] = 0;
-            if ((rc = blockq_slot(gu, ep_g, a0, a1, o0, 2, sp[2]))) return rc;
+            if ((rc = blockq_slot(gu, rc_g, ep_g, a0, a1, o0, 2, sp[2]))) return rc;
             // E: ffn_down rows
             split(wd->groups, G, c, &a0[0], &a1[0]);
             o0[0] = (int32_t)(8 * a0[0]);
-            if ((rc = blockq_slot(wd, ep_d, a0, a1, o0, 1, sp[3]))) return rc;
+            if ((rc = blockq_slot(wd, rc_d, ep_d, a0, a1, o0, 1, sp[3]))) return rc;
             if (sp[2].kind == SK_NONE) return TMAC_OK;  // phase E relies on every CTA taking part in D
             for (int s = 0; s < kSlots; s++) {
                 slot_bytes[s] = std::max(slot_bytes[s], (sp[s].total + 127) / 128 * 128);
@@ -1110,10 +1155,13 @@ int mega_prepare(tmac_model_s* m, MegaState** out)
     if (e == cudaSuccess)
         e = cudaMemcpy(st->dev_slots, slots.data(), slots.size() * sizeof(MegaSlot), cudaMemcpyHostToDevice);
     if (e == cudaSuccess) e = cudaMemset(st->dev_tagged, 0, n_tagged * sizeof(unsigned long long));  // tag 0: never current
+    if (e == cudaSuccess) e = cudaStreamSynchronize(nullptr);  // the RowConst arrays are filled
     if (e != cudaSuccess) {
         mega_free(st);
         return cuda_fail(e, "decode kernel set-up");
     }
+    for (auto& kv : rowc) st->rowc.push_back(kv.second);
+    rowc.clear();
     a.layers = static_cast<const MegaLayer*>(st->dev_layers);
     a.slots = static_cast<const MegaSlot*>(st->dev_slots);
     a.emb = m->emb_raw;

@@ -58,22 +58,6 @@ __host__ __device__ constexpr uint32_t idesc_i8(uint32_t a_signed, uint32_t b_si
     return (2u << 4) | (a_signed << 7) | (b_signed << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
 }
 
-// (float)(p / ri) with p / ri rounded to double first, as the GEMV computes it
-// (__ddiv_rn then the float conversion).  p * RN(1/ri) is within 2 double ulps
-// of the double quotient; unless its 29 bits below float precision lie within
-// 16 units of the float rounding midpoint (or the value is outside the normal
-// float range) both round to the same float, else the exact division decides.
-TMAC_DEV float quotient_f32(double p, double rinv, float ri)
-{
-    const double q = __dmul_rn(p, rinv);
-    const long long bits = __double_as_longlong(q);
-    const int exp = (int)((bits >> 52) & 0x7FF);
-    const int low = (int)(bits & 0x1FFFFFFF);
-    const bool near_mid = abs(low - 0x10000000) <= 16;
-    if (near_mid || exp < 1023 - 120 || exp > 1023 + 120) return (float)__ddiv_rn(p, (double)ri);
-    return (float)q;
-}
-
 // ----------------------------------------------------------------- kernel --
 // Persistent: CTA c takes tiles c, c + grid, ...; tile i -> (m tile i / tiles_n,
 // n tile i % tiles_n), so the tiles in flight share few activation tiles, which
@@ -473,11 +457,6 @@ __global__ void __launch_bounds__(kSkThreads, 1)
     }
 }
 
-__global__ void rinv_kernel(const float* __restrict__ ri, int64_t n, double* __restrict__ out)
-{
-    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < n) out[i] = __ddiv_rn(1.0, (double)ri[i]);
-}
 
 // Activation rows -> x_scale and byte planes (one CTA per row, tmac_gguf.cpp:889-896).
 #ifndef TMAC_QUANT_THREADS
@@ -611,9 +590,7 @@ int gemm_prepare(tmac_weight_s* w, cudaStream_t s)
     TMAC_CUDA_TRY(cudaMalloc(&w->gwl, n));
     int rc = blockq_planes(w, reinterpret_cast<int8_t*>(w->gwh), reinterpret_cast<uint8_t*>(w->gwl), s);
     if (rc) return rc;
-    TMAC_CUDA_TRY(cudaMalloc(&w->grinv, (size_t)w->rows * sizeof(double)));
-    rinv_kernel<<<(unsigned)((w->rows + 255) / 256), 256, 0, s>>>(w->row_norm, w->rows, reinterpret_cast<double*>(w->grinv));
-    TMAC_CUDA_TRY(cudaGetLastError());
+    if (!w->grinv) return fail(TMAC_ERR_INVALID, "gemm_prepare: weight has no row reciprocals");
     return TMAC_OK;
 }
 

@@ -167,6 +167,7 @@ __global__ void planes_kernel(const uint8_t* __restrict__ data, const float* __r
 struct BqArgs {
     const uint8_t* data;     // grouped layout
     const float* row_inv;
+    const double* rinv;      // RN(1 / row_inv)
     int64_t rows, cols, groups, group_bytes;
     int gpc;                 // groups per CTA
     const float* x;          // [nb][cols] fp32 activations, or
@@ -242,6 +243,11 @@ __global__ void __launch_bounds__(NB == 1 ? 1024 : 512) blockq_gemv_kernel(BqArg
     float* red = reinterpret_cast<float*>(smem + L.red);
     uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L.bar);  // [0] weights, [1] activations, [2] exceptions
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    // the epilogue's reciprocal of this thread's first (row, vector), loaded now
+    // so that its latency hides behind the main loop
+    const double rinv0 = NB == 1 && (int)threadIdx.x < rows_cta && row0 + (int)threadIdx.x < a.rows
+                             ? __ldg(a.rinv + row0 + (int)threadIdx.x)
+                             : 0.0;
 
     BQ_STAMP(0);
     // ---- prologue: everything here depends on the weights only.  Thread 0
@@ -476,8 +482,8 @@ __global__ void __launch_bounds__(NB == 1 ? 1024 : 512) blockq_gemv_kernel(BqArg
         const int64_t row = row0 + rr;
         if (row >= a.rows) continue;
         const long long tot = (long long)(((unsigned long long)acc_hi[rr * nb + b] << 32) | acc_lo[rr * nb + b]);
-        const double v = __ddiv_rn(__dmul_rn((double)tot, (double)xs_s[b]), (double)ri_s[rr]);
-        a.y[(int64_t)b * a.rows + row] = (float)v;
+        const double rv = (NB == 1 && t == (int)threadIdx.x) ? rinv0 : __ldg(a.rinv + row);
+        a.y[(int64_t)b * a.rows + row] = quotient_f32(__dmul_rn((double)tot, (double)xs_s[b]), rv, ri_s[rr]);
         if (a.row_acc) a.row_acc[(int64_t)b * a.rows + row] = tot;
     }
 #ifdef TMAC_TRACE
@@ -535,6 +541,7 @@ int launch_type(const tmac_weight_s* w, const float* x, const int16_t* xq, const
         BqArgs a;
         a.data = w->data;
         a.row_inv = w->row_norm;
+        a.rinv = reinterpret_cast<const double*>(w->grinv);
         a.rows = w->rows;
         a.cols = cols;
         a.groups = w->groups;
@@ -564,6 +571,13 @@ int launch_type(const tmac_weight_s* w, const float* x, const int16_t* xq, const
     return TMAC_OK;
 }
 
+// RN(1 / row_inv) in double for the epilogue (quotient_f32); rows padded to groups.
+__global__ void rinv_kernel(const float* __restrict__ ri, int64_t n, double* __restrict__ out)
+{
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) out[i] = __ddiv_rn(1.0, (double)ri[i]);
+}
+
 template <int TYPE>
 int register_type(tmac_weight_s* w, const uint8_t* d_raw, cudaStream_t s)
 {
@@ -574,6 +588,10 @@ int register_type(tmac_weight_s* w, const uint8_t* d_raw, cudaStream_t s)
     const int wpb = 8;
     const unsigned rgrid = (unsigned)((rows + wpb - 1) / wpb);
     row_inv_kernel<TYPE><<<rgrid, wpb * 32, 0, s>>>(d_raw, rows, w->cols, w->row_norm);
+    TMAC_CUDA_TRY(cudaGetLastError());
+    const int64_t prow = (rows + 7) / 8 * 8;
+    TMAC_CUDA_TRY(cudaMalloc(&w->grinv, (size_t)prow * sizeof(double)));
+    rinv_kernel<<<(unsigned)((prow + 255) / 256), 256, 0, s>>>(w->row_norm, prow, reinterpret_cast<double*>(w->grinv));
     TMAC_CUDA_TRY(cudaGetLastError());
 
     w->groups = (rows + 7) / 8;
