@@ -161,10 +161,10 @@ __global__ void __launch_bounds__(256) rope_attention_kernel(
     extern __shared__ __align__(16) float sc[];  // [nsc] scores, then weights; [nsc] exp terms; K/V staging
     __shared__ AttnShared sh;
     if (pos_dev) pos = *pos_dev;
-    attention_prefetch(blockIdx.x, kc, vc, pos, nscore, sc);
+    attention_prefetch(blockIdx.x, kc, vc, pos, nscore, sc, bq, bk, bv, cs, sn, sh);
     const int h = blockIdx.x, kvh = h / (kHeads / kKvHeads);
-    attention_head(h, q + h * kHeadDim, k + kvh * kHeadDim, v + kvh * kHeadDim, bq, bk, bv, cs, sn, pos, kc, vc,
-                   ctx + h * kHeadDim, nscore, sc, sh, 1);
+    attention_head(h, q + h * kHeadDim, k + kvh * kHeadDim, v + kvh * kHeadDim, pos, kc, vc, ctx + h * kHeadDim,
+                   nscore, sc, sh, 1);
 }
 
 // silu(gate) * up (:459-461, :1697-1700), then the quantisation ffn_down's

@@ -695,7 +695,8 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaArgs a
         if (h >= 0 && h < kHeads) {
             // earlier positions' K / V rows do not depend on this step: their
             // copies overlap the wait for q|k|v
-            if (tid < kAttnThreads) attention_prefetch(h, L.kc, L.vc, pos, a.max_seq, att);
+            if (tid < kAttnThreads)
+                attention_prefetch(h, L.kc, L.vc, pos, a.max_seq, att, L.bq, L.bk, L.bv, a.rope_c, a.rope_s, ms.attn);
             // the head's q, its KV head's k and v (192 values) into sq
             const int kvh = h / (kHeads / kKvHeads);
             float r[1];
@@ -740,8 +741,8 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaArgs a
             __syncthreads();
             MEGA_STAMP(l, 5);
             if (tid < kAttnThreads)
-                attention_head(h, sq, sq + kHeadDim, sq + 2 * kHeadDim, L.bq, L.bk, L.bv, a.rope_c, a.rope_s, pos,
-                               L.kc, L.vc, sq + 3 * kHeadDim, a.max_seq, att, ms.attn, 1, MEGA_ATT_STAMPS(h, l));
+                attention_head(h, sq, sq + kHeadDim, sq + 2 * kHeadDim, pos, L.kc, L.vc, sq + 3 * kHeadDim, a.max_seq,
+                               att, ms.attn, 1, MEGA_ATT_STAMPS(h, l));
             __syncthreads();
             if (tid < kHeadDim) st_tagged(a.ctx_t + h * kHeadDim + tid, sq[3 * kHeadDim + tid], tag_of(ep, l, TG_CTX));
             MEGA_STAMP(l, 23);

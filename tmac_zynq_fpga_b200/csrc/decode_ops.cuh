@@ -80,6 +80,9 @@ constexpr int kAttnStride = 68;   // floats per staged row (16-byte aligned rows
 constexpr int kAttnThreads = 256; // threads of one head's attention
 
 struct AttnShared {
+    // the head's q bias, its KV head's k and v biases, and the RoPE cos / sin of
+    // the position (64 + 64 + 64 + 32 + 32), staged by attention_prefetch
+    alignas(16) float pre[3 * kHeadDim + kHeadDim];
     float red[kAttnThreads / 32];
     float q[kHeadDim], k[kHeadDim], v[kHeadDim];
     float log_sum;
@@ -108,9 +111,27 @@ TMAC_DEV void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memor
 // earlier steps, so they do not depend on this step's q / k / v -- into the
 // K / V row buffers of `sc` (asynchronous; attention_head waits for them).
 TMAC_DEV void attention_prefetch(int h, const float* __restrict__ kc, const float* __restrict__ vc, int pos,
-                                 int nscore, float* sc)
+                                 int nscore, float* sc, const float* __restrict__ bq, const float* __restrict__ bk,
+                                 const float* __restrict__ bv, const float* __restrict__ cs,
+                                 const float* __restrict__ sn, AttnShared& sh)
 {
     const int kvh = h / (kHeads / kKvHeads);
+    // biases and RoPE terms: they do not depend on this step's q / k / v
+    if (threadIdx.x < 64) {
+        const int i = threadIdx.x, part = i >> 4, c4 = (i & 15) * 4;
+        const float* src = part == 0   ? (bq ? bq + h * kHeadDim : nullptr)
+                           : part == 1 ? (bk ? bk + kvh * kHeadDim : nullptr)
+                           : part == 2 ? (bv ? bv + kvh * kHeadDim : nullptr)
+                                       : nullptr;
+        float* dst = sh.pre + part * kHeadDim + c4;
+        if (part < 3) {
+            if (src) cp_async16(dst, src + c4);
+            else dst[0] = dst[1] = dst[2] = dst[3] = 0.0f;
+        } else {  // 8 chunks of cos, 8 of sin
+            const float* tab = c4 < 32 ? cs : sn;
+            cp_async16(dst, tab + (int64_t)pos * (kHeadDim / 2) + (c4 & 31));
+        }
+    }
     const int n = min(pos, kAttnChunk);
     float* kb = sc + attn_score_floats(nscore);
     float* vb = kb + kAttnChunk * kAttnStride;
@@ -124,7 +145,8 @@ TMAC_DEV void attention_prefetch(int h, const float* __restrict__ kc, const floa
 }
 
 // Query head h, run by threads 0..255 of a CTA (they synchronise on named
-// barrier `bar`) after attention_prefetch: q/k/v bias add (:1591-1614), RoPE on
+// barrier `bar`) after attention_prefetch (which staged the biases and RoPE
+// terms in sh.pre): q/k/v bias add (:1591-1614), RoPE on
 // the head's q and its KV head's k (:1528-1554), KV-cache append by the first
 // query head of each KV group (:1622-1623), then attention over positions
 // 0..pos (:1625-1660): scores q.k in d order / sqrtf(64), max, exp terms, their
@@ -137,8 +159,6 @@ TMAC_DEV void attention_prefetch(int h, const float* __restrict__ kc, const floa
 // other CTAs of a persistent kernel write them while this CTA may hold older
 // copies in L1.  stamps (diagnostics only): 8 %globaltimer values, or nullptr.
 TMAC_DEV void attention_head(int h, const float* q_head, const float* k_head, const float* v_head,
-                             const float* __restrict__ bq, const float* __restrict__ bk,
-                             const float* __restrict__ bv, const float* __restrict__ cs, const float* __restrict__ sn,
                              int pos, float* __restrict__ kc, float* __restrict__ vc, float* ctx_head,
                              int nscore, float* sc, AttnShared& sh, int bar, unsigned long long* stamps = nullptr)
 {
@@ -150,24 +170,24 @@ TMAC_DEV void attention_head(int h, const float* q_head, const float* k_head, co
     const int tid = threadIdx.x;
     const int nsc = nscore;
     const int kvh = h / (kHeads / kKvHeads);
-    const float* c = cs + (int64_t)pos * (kHeadDim / 2);
-    const float* sv = sn + (int64_t)pos * (kHeadDim / 2);
     float* kb = sc + attn_score_floats(nsc);  // [kAttnChunk][kAttnStride]
     float* vb = kb + kAttnChunk * kAttnStride;
+    cp_async_wait_all();  // biases, RoPE terms and K / V rows of positions [0, min(pos, 64))
+    named_bar_sync(bar, kAttnThreads);
     if (tid < kHeadDim) {  // thread j: pair j/2 of q (j even) or of k (j odd)
         const int j = tid, pr = j >> 1, d = 2 * pr;
         const bool isk = j & 1;
         const float* vec = isk ? k_head : q_head;
-        const float* b = isk ? (bk ? bk + kvh * kHeadDim : nullptr) : (bq ? bq + h * kHeadDim : nullptr);
-        const float x0 = __fadd_rn(vec[d], b ? b[d] : 0.0f), x1 = __fadd_rn(vec[d + 1], b ? b[d + 1] : 0.0f);
-        const float y0 = __fsub_rn(__fmul_rn(x0, c[pr]), __fmul_rn(x1, sv[pr]));
-        const float y1 = __fadd_rn(__fmul_rn(x0, sv[pr]), __fmul_rn(x1, c[pr]));
+        const float* b = sh.pre + (isk ? kHeadDim : 0);
+        const float c = sh.pre[3 * kHeadDim + pr], sv = sh.pre[3 * kHeadDim + kHeadDim / 2 + pr];
+        const float x0 = __fadd_rn(vec[d], b[d]), x1 = __fadd_rn(vec[d + 1], b[d + 1]);
+        const float y0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sv));
+        const float y1 = __fadd_rn(__fmul_rn(x0, sv), __fmul_rn(x1, c));
         float* dst = isk ? sh.k : sh.q;
         dst[d] = y0;
         dst[d + 1] = y1;
-        sh.v[j] = __fadd_rn(v_head[j], bv ? bv[kvh * kHeadDim + j] : 0.0f);
+        sh.v[j] = __fadd_rn(v_head[j], sh.pre[2 * kHeadDim + j]);
     }
-    cp_async_wait_all();  // the prefetched K / V rows of positions [0, min(pos, 64))
     named_bar_sync(bar, kAttnThreads);
     ATT_STAMP(1);
     if (h % (kHeads / kKvHeads) == 0 && tid < kHeadDim) {
