@@ -213,7 +213,10 @@ int tmac_reserve(int device, int64_t max_batch, int64_t max_cols);
  * Q4_K / Q6_K weights, and NATIVE Q8_0 (matmul_fpga_q8 per row: one GEMM per
  * 64-column tile, folded into y in tile order; row_acc must be NULL); cols a
  * multiple of 16, at most 32768.  The first call on a weight decodes its int16
- * planes (2 bytes per weight, kept with the weight).  Device pointers;
+ * planes (2 bytes per weight, kept with the weight).  For m <= 64 (Q5_0 / Q4_K /
+ * Q6_K) the weights are the 128-row MMA operand and K is split across the SMs,
+ * with int64 partial sums in a per-device workspace that the call leaves zeroed;
+ * calls on one device must then be ordered on one stream.  Device pointers;
  * asynchronous on `stream`. */
 int tmac_gemm(tmac_weight_t w, const float* x, float* y, int64_t* row_acc, int m, void* stream);
 
