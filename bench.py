@@ -500,6 +500,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-model", action="store_true", help="skip the decode / prefill measurements")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="issue the timed steps one by one from Python instead of replaying a CUDA graph of them")
     ap.add_argument("--no-pdl", action="store_true",
                     help="launch each step's kernel after the previous one ends (no programmatic dependent launch)")
     ap.add_argument("--top1-only", dest="full_logits", action="store_false",
@@ -581,14 +583,15 @@ def main():
     gather = world > 1 and args.full_logits and not peer_full
     y_full = torch.empty(VOCAB, dtype=torch.float32, device="cuda") if gather else None
 
-    def step(i):
+    def step(i, st=None):
         # logits of this rank's vocab shard + their top-1 key, then the global
         # greedy token on every rank (and, with --full-logits, the whole vector)
+        st = stream if st is None else st
         w = weights[i % ncopies]
         if fused:
-            merge.gemv_top1(w, x, y, key, r0, stream)
+            merge.gemv_top1(w, x, y, key, r0, st)
         else:
-            w.gemv_top1(x, y, key, index_base=r0, stream=stream)
+            w.gemv_top1(x, y, key, index_base=r0, stream=st)
             if world > 1:
                 if merge is not None:
                     merge(key, stream)
@@ -606,6 +609,22 @@ def main():
     torch.cuda.synchronize()
     if tm.device_error(local) != 0:
         raise SystemExit("a kernel recorded a device-side error during warm-up")
+    # The timed steps run as replays of a CUDA graph of G consecutive steps (one
+    # kernel launch each, programmatic dependent launch between them) when a
+    # step is a single launch: at N > 1 a shard's GEMV takes a few microseconds,
+    # less than issuing it from Python.  G is even (the exchange alternates
+    # buffer halves by step parity) and divides K, so exactly K steps are timed.
+    graph, G = None, 0
+    if not args.no_graph and (world == 1 or (fused and not gather)):
+        G = next((g for g in range(64, 1, -1) if g % 2 == 0 and args.steps % g == 0), 0)
+        if G:
+            cap = torch.cuda.Stream()
+            cap.wait_stream(stream)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=cap):
+                for i in range(G):
+                    step(i, cap)
+            torch.cuda.synchronize()
     sampler = ClockSampler(local)
     sampler.start()
     time.sleep(0.3)
@@ -614,8 +633,12 @@ def main():
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record(stream)
-    for i in range(args.steps):
-        step(i)
+    if graph is not None:
+        for _ in range(args.steps // G):
+            graph.replay()  # on the current stream
+    else:
+        for i in range(args.steps):
+            step(i)
     ev1.record(stream)
     torch.cuda.synchronize()
     if world > 1:
@@ -683,8 +706,10 @@ def main():
                                   if peer_full else ""),
                        "greedy_token": tok,
                        "parallelism": f"vocab-row shards x{world}", "shard_rows": rows,
-                       "launch": "back-to-back, no programmatic dependent launch" if args.no_pdl else
-                                 "programmatic dependent launch between steps (tmac_set_pdl)",
+                       "launch": ("back-to-back, no programmatic dependent launch" if args.no_pdl else
+                                  "programmatic dependent launch between steps (tmac_set_pdl)")
+                                 + (f"; CUDA graph of {G} steps replayed {args.steps // G} times" if graph is not None
+                                    else "; steps issued one by one"),
                        "l2": f"inputs larger than L2: {ncopies} rotating weight copies of "
                              f"{per_copy / 1e6:.1f} MB per rank"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk, "unit": "GB/s",
