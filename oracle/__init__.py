@@ -18,6 +18,9 @@ REF_PATH = os.path.join(HERE, "_ref", "libtmac_ref.so")
 # (tmac_zynq_fpga_b200/host/matmul_fpga_binding.cpp): not a checker, the
 # drop-in under test.  Loading it touches no GPU; its drivers need one.
 REF_SHIM_PATH = os.path.join(HERE, "_ref", "libtmac_ref_shim.so")
+# The reference with only MAX_SEQ_LEN (sim/tmac_gguf.cpp:148) raised to 512, for
+# decode fixtures that fill the 512-position cache (oracle/Makefile, ref512).
+REF_SEQ512_PATH = os.path.join(HERE, "_ref", "libtmac_ref_seq512.so")
 
 PATH_NATIVE, PATH_INT16, PATH_F32 = 0, 1, 2
 
@@ -69,6 +72,14 @@ def ref_available():
 def ref_shim():
     """The reference engine re-pointed at libtmac_cuda.so (see REF_SHIM_PATH)."""
     R = ctypes.CDLL(REF_SHIM_PATH)
+    R.ref_decode.restype = ctypes.c_int
+    R.ref_decode.argtypes = [ctypes.c_char_p, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P, _P, _P]
+    return R
+
+
+def ref_seq512():
+    """The reference engine built with a 512-position KV cache (REF_SEQ512_PATH)."""
+    R = ctypes.CDLL(REF_SEQ512_PATH)
     R.ref_decode.restype = ctypes.c_int
     R.ref_decode.argtypes = [ctypes.c_char_p, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P, _P, _P]
     return R

@@ -95,3 +95,29 @@ def test_reference_engine_on_the_binding_is_bit_identical():
     np.testing.assert_array_equal(toks, g["tokens"])
     np.testing.assert_array_equal(logit.view(np.int32), g["logit"].view(np.int32))
     np.testing.assert_array_equal(hidden.view(np.int32), g["hidden"].view(np.int32))
+
+
+FIX512 = os.path.join(HERE, "golden", "decode_greedy_seed0_pos512.npz")
+HIDDEN_RTOL_512 = 5e-4  # same bar as the 8-token prompt, over 448 prompt positions + 64 steps
+
+
+@pytest.mark.skipif(not os.path.exists(FIX512), reason="512-position decode fixture missing")
+def test_full_512_position_cache_matches_reference():
+    """The configuration's whole KV cache: a 448-token prompt and 64 greedy steps,
+    positions 0..511.  The fixture comes from the reference engine compiled with
+    only MAX_SEQ_LEN (sim/tmac_gguf.cpp:148) raised from 256 to 512, since the
+    unmodified reference stops at position 256.  Bar: the 64 greedy tokens
+    identical, the hidden state after the prompt and after every step within the
+    relative tolerance of the short-prompt test."""
+    g = np.load(FIX512)
+    m = tm.Model(model.default_model_path(int(g["model_seed"])), switches=tm.SW_ALL, max_seq=512)
+    try:
+        toks, hid = m.generate(g["prompt"], len(g["tokens"]), want_hidden=True)
+        assert m.decode_engine() == 1, "the persistent decode kernel did not run"
+    finally:
+        m.free()
+    ref = g["hidden"]
+    err = np.abs(hid - ref).max(axis=1) / np.abs(ref).max(axis=1)
+    print(f"512-position decode: max relative hidden error {err.max():.3g}")
+    np.testing.assert_array_equal(toks, g["tokens"])
+    assert err.max() < HIDDEN_RTOL_512, f"max relative hidden error {err.max():.3g} (per step {np.round(err, 6)})"
