@@ -21,6 +21,7 @@ REF_SHIM_PATH = os.path.join(HERE, "_ref", "libtmac_ref_shim.so")
 # The reference with only MAX_SEQ_LEN (sim/tmac_gguf.cpp:148) raised to 512, for
 # decode fixtures that fill the 512-position cache (oracle/Makefile, ref512).
 REF_SEQ512_PATH = os.path.join(HERE, "_ref", "libtmac_ref_seq512.so")
+REF_SHIM_SEQ512_PATH = os.path.join(HERE, "_ref", "libtmac_ref_shim_seq512.so")
 
 PATH_NATIVE, PATH_INT16, PATH_F32 = 0, 1, 2
 
@@ -69,9 +70,10 @@ def ref_available():
     return os.path.exists(REF_PATH)
 
 
-def ref_shim():
-    """The reference engine re-pointed at libtmac_cuda.so (see REF_SHIM_PATH)."""
-    R = ctypes.CDLL(REF_SHIM_PATH)
+def ref_shim(path=REF_SHIM_PATH):
+    """The reference engine re-pointed at libtmac_cuda.so (see REF_SHIM_PATH;
+    REF_SHIM_SEQ512_PATH for the 512-position build)."""
+    R = ctypes.CDLL(path)
     R.ref_decode.restype = ctypes.c_int
     R.ref_decode.argtypes = [ctypes.c_char_p, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P, _P, _P]
     return R

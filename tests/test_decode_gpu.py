@@ -121,3 +121,24 @@ def test_full_512_position_cache_matches_reference():
     print(f"512-position decode: max relative hidden error {err.max():.3g}")
     np.testing.assert_array_equal(toks, g["tokens"])
     assert err.max() < HIDDEN_RTOL_512, f"max relative hidden error {err.max():.3g} (per step {np.round(err, 6)})"
+
+
+@pytest.mark.skipif(not (os.path.exists(FIX512) and os.path.exists(oracle.REF_SHIM_SEQ512_PATH)),
+                    reason="512-position fixture or oracle/_ref/libtmac_ref_shim_seq512.so missing")
+def test_reference_engine_on_the_binding_at_512_positions():
+    """The drop-in over the whole 512-position cache: the reference's decode loop
+    (512-position build) with its matmul_fpga_* drivers on libtmac_cuda.so gives
+    the fixture's tokens, logits and hidden states bit for bit."""
+    g = np.load(FIX512)
+    R = oracle.ref_shim(oracle.REF_SHIM_SEQ512_PATH)
+    prompt = g["prompt"].astype(np.int32)
+    n_gen = len(g["tokens"])
+    toks = np.zeros(n_gen, np.int32)
+    logit = np.zeros(n_gen, np.float32)
+    hidden = np.zeros((n_gen + 1, model.HIDDEN), np.float32)
+    n = R.ref_decode(model.default_model_path(0).encode(), prompt.ctypes.data, len(prompt), n_gen, 1,
+                     toks.ctypes.data, logit.ctypes.data, hidden.ctypes.data)
+    assert n == n_gen
+    np.testing.assert_array_equal(toks, g["tokens"])
+    np.testing.assert_array_equal(logit.view(np.int32), g["logit"].view(np.int32))
+    np.testing.assert_array_equal(hidden.view(np.int32), g["hidden"].view(np.int32))
