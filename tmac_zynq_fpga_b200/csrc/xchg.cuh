@@ -85,22 +85,45 @@ TMAC_DEV bool xchg_read(const XchgDev& x, int t, uint64_t step, unsigned long lo
     return true;
 }
 
-// One thread: publish to every rank, then the maximum of every rank's key
-// (*out unchanged and TMAC_ERR_TIMEOUT recorded if a rank does not arrive).
-TMAC_DEV void xchg_top1_thread(const XchgDev& x, unsigned long long k, unsigned long long* out, int* err)
+TMAC_DEV void st_relaxed_sys(uint64_t* p, uint64_t v)
 {
-    const uint64_t step = *x.step + 1;
-    for (int t = 0; t < x.world; t++) xchg_publish(x, t, step, k);
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// One warp (all 32 lanes): publish `k` to every rank, then the maximum of every
+// rank's key (*out unchanged and TMAC_ERR_TIMEOUT recorded if a rank does not
+// arrive).  Lane t serves ranks t, t + 32, ...: the key stores, ONE
+// system-scope fence, then relaxed tag stores (a release pattern for every
+// tag), and the tags of all ranks are polled at once.  A release store per rank
+// from one thread would pay one system-scope fence per rank, in sequence.
+TMAC_DEV void xchg_top1_warp(const XchgDev& x, unsigned long long k, unsigned long long* out, int* err)
+{
+    const int lane = threadIdx.x & 31;
+    uint64_t step = 0;
+    if (lane == 0) step = *x.step + 1;
+    step = __shfl_sync(0xffffffffu, step, 0);
+    k = __shfl_sync(0xffffffffu, k, 0);
+    const int half = (int)(step & 1);
+    for (int t = lane; t < x.world; t += 32) x.peers[t][half * x.world + x.rank] = k;
+    __threadfence_system();
+    for (int t = lane; t < x.world; t += 32) st_relaxed_sys(x.peers[t] + 2 * x.world + half * x.world + x.rank, step);
     unsigned long long m = 0;
     bool ok = true;
-    for (int t = 0; t < x.world && ok; t++) {
+    for (int t = lane; t < x.world && ok; t += 32) {
         unsigned long long v = 0;
         ok = xchg_read(x, t, step, &v);
         m = v > m ? v : m;
     }
-    if (ok) *out = m;
-    else if (err) atomicExch(err, (int)TMAC_ERR_TIMEOUT);
-    *x.step = step;
+    ok = __all_sync(0xffffffffu, ok);
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long v = __shfl_xor_sync(0xffffffffu, m, o);
+        m = v > m ? v : m;
+    }
+    if (lane == 0) {
+        if (ok) *out = m;
+        else if (err) atomicExch(err, (int)TMAC_ERR_TIMEOUT);
+        *x.step = step;
+    }
 }
 
 // End of a GEMV CTA that tracks the top-1 key of its rows: every warp of the
@@ -119,30 +142,36 @@ TMAC_DEV void top1_cta_finish(const XchgDev& xg, unsigned long long* top1, unsig
     const int lane = threadIdx.x & 31;
     if (lane == 0) slots[slot] = best;
     asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(bar_threads) : "memory");
-    if (!(leader_warp && lane == 0)) return;
-    // full logits: the peer stores of the CTA's warps (ordered before this
-    // thread by the barrier) reach the other GPUs before the key that the last
-    // CTA publishes with a system-scope release
-    if (xg.vocab) __threadfence_system();
-    unsigned long long m = 0;
-    for (int w = 0; w < bar_threads / 32; w++) m = slots[w] > m ? slots[w] : m;
-    if (!xg.partial) {
-        if (m) atomicMax(top1, m);
-        return;
+    if (!leader_warp) return;
+    unsigned done = 0;
+    unsigned long long k = 0;
+    if (lane == 0) {
+        // full logits: the peer stores of the CTA's warps (ordered before this
+        // thread by the barrier) reach the other GPUs before the key that the
+        // last CTA publishes with a system-scope release pattern
+        if (xg.vocab) __threadfence_system();
+        unsigned long long m = 0;
+        for (int w = 0; w < bar_threads / 32; w++) m = slots[w] > m ? slots[w] : m;
+        if (!xg.partial) {
+            if (m) atomicMax(top1, m);
+        } else {
+            if (m) atomicMax(xg.partial, m);
+            // acquire-release count: each CTA's max is ordered before its
+            // increment, and the CTA that sees the last increment sees every max
+            asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(done) : "l"(xg.counter) : "memory");
+            if (done == gridDim.x - 1) {
+                k = atomicExch(xg.partial, 0ull);
+                atomicExch(xg.counter, 0u);
+                if (!xg.peers) *top1 = k;
+            }
+        }
     }
-    if (m) atomicMax(xg.partial, m);
-    // acquire-release count: each CTA's max is ordered before its increment,
-    // and the CTA that sees the last increment sees every max
-    unsigned done;
-    asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(done) : "l"(xg.counter) : "memory");
-    if (done == gridDim.x - 1) {
-        const unsigned long long k = atomicExch(xg.partial, 0ull);
-        atomicExch(xg.counter, 0u);
-        if (xg.peers)
-            xchg_top1_thread(xg, k, top1, err);
-        else
-            *top1 = k;
-    }
+    if (!xg.partial || !xg.peers) return;
+    done = __shfl_sync(0xffffffffu, done, 0);
+    if (done != gridDim.x - 1) return;
+    // what lane 0 acquired is ordered before the other lanes' exchange stores
+    __syncwarp();
+    xchg_top1_warp(xg, k, top1, err);
 }
 
 XchgDev xchg_dev(const tmac_xchg_s* x);  // xchg.cu
