@@ -183,6 +183,7 @@ struct Q8Args {
     int* err;
 };
 
+template <bool kPeers>
 __global__ void __launch_bounds__(kThreads, 1) q8_gemv_kernel(Q8Args a)
 {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -288,7 +289,10 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemv_kernel(Q8Args a)
                 const unsigned long long k = __shfl_xor_sync(0xffffffffu, best, o);
                 best = k > best ? k : best;
             }
-            top1_cta_finish(a.xg, a.top1, best, top1_slots, f, f == 0, 2, kFoldWarps * 32, a.err);
+            if constexpr (kPeers)
+                top1_cta_finish_peers(a.xg, a.top1, best, top1_slots, f, f == 0, 2, kFoldWarps * 32, a.err);
+            else
+                top1_cta_finish(a.xg, a.top1, best, top1_slots, f, f == 0, 2, kFoldWarps * 32, a.err);
         }
         return;
     }
@@ -489,7 +493,10 @@ int launch_q8_0(const tmac_weight_s* w, const float* x, float* y, int64_t* row_a
     const size_t smem = q8_smem_bytes(L);
     static bool attr_set[64] = {};
     if (!attr_set[w->device & 63]) {
-        TMAC_CUDA_TRY(cudaFuncSetAttribute(q8_gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemLimit));
+        TMAC_CUDA_TRY(cudaFuncSetAttribute(q8_gemv_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)kSmemLimit));
+        TMAC_CUDA_TRY(cudaFuncSetAttribute(q8_gemv_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)kSmemLimit));
         attr_set[w->device & 63] = true;
     }
     const int grid = (int)std::min<int64_t>(L.groups, num_sms(w->device));
@@ -514,7 +521,11 @@ int launch_q8_0(const tmac_weight_s* w, const float* x, float* y, int64_t* row_a
             a.xg.counter = reinterpret_cast<unsigned*>(a.xg.partial + 1);
         }
         a.err = device_error_word(w->device);
-        TMAC_CUDA_TRY(launch_k(q8_gemv_kernel, dim3(grid), dim3(kThreads), smem, s, a));
+        // the exchange across ranks is a separate instantiation (see top1_cta_finish)
+        if (a.xg.peers)
+            TMAC_CUDA_TRY(launch_k(q8_gemv_kernel<true>, dim3(grid), dim3(kThreads), smem, s, a));
+        else
+            TMAC_CUDA_TRY(launch_k(q8_gemv_kernel<false>, dim3(grid), dim3(kThreads), smem, s, a));
         TMAC_CUDA_TRY(cudaGetLastError());
     }
     return TMAC_OK;

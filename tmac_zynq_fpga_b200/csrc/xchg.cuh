@@ -126,6 +126,24 @@ TMAC_DEV void xchg_top1_warp(const XchgDev& x, unsigned long long k, unsigned lo
     }
 }
 
+// One thread: publish to every rank, then the maximum of every rank's key
+// (*out unchanged and TMAC_ERR_TIMEOUT recorded if a rank does not arrive).
+TMAC_DEV void xchg_top1_thread(const XchgDev& x, unsigned long long k, unsigned long long* out, int* err)
+{
+    const uint64_t step = *x.step + 1;
+    for (int t = 0; t < x.world; t++) xchg_publish(x, t, step, k);
+    unsigned long long m = 0;
+    bool ok = true;
+    for (int t = 0; t < x.world && ok; t++) {
+        unsigned long long v = 0;
+        ok = xchg_read(x, t, step, &v);
+        m = v > m ? v : m;
+    }
+    if (ok) *out = m;
+    else if (err) atomicExch(err, (int)TMAC_ERR_TIMEOUT);
+    *x.step = step;
+}
+
 // End of a GEMV CTA that tracks the top-1 key of its rows: every warp of the
 // `bar_threads` (named barrier `bar_id`) calls it with its warp-reduced key;
 // `slots` is shared memory for one key per calling warp, `slot` this warp's.
@@ -142,6 +160,43 @@ TMAC_DEV void top1_cta_finish(const XchgDev& xg, unsigned long long* top1, unsig
     const int lane = threadIdx.x & 31;
     if (lane == 0) slots[slot] = best;
     asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(bar_threads) : "memory");
+    if (!(leader_warp && lane == 0)) return;
+    // full logits: the peer stores of the CTA's warps (ordered before this
+    // thread by the barrier) reach the other GPUs before the key that the last
+    // CTA publishes with a system-scope release
+    if (xg.vocab) __threadfence_system();
+    unsigned long long m = 0;
+    for (int w = 0; w < bar_threads / 32; w++) m = slots[w] > m ? slots[w] : m;
+    if (!xg.partial) {
+        if (m) atomicMax(top1, m);
+        return;
+    }
+    if (m) atomicMax(xg.partial, m);
+    // acquire-release count: each CTA's max is ordered before its increment,
+    // and the CTA that sees the last increment sees every max
+    unsigned done;
+    asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(done) : "l"(xg.counter) : "memory");
+    if (done == gridDim.x - 1) {
+        const unsigned long long k = atomicExch(xg.partial, 0ull);
+        atomicExch(xg.counter, 0u);
+        if (xg.peers)
+            xchg_top1_thread(xg, k, top1, err);
+        else
+            *top1 = k;
+    }
+}
+
+// The same end of a GEMV CTA for the fused exchange across ranks (xg.peers
+// and xg.partial set): the last CTA's whole leader warp publishes this rank's
+// key and merges every rank's (xchg_top1_warp).  A separate function, so the
+// kernel without peers carries none of the warp exchange code.
+TMAC_DEV void top1_cta_finish_peers(const XchgDev& xg, unsigned long long* top1, unsigned long long best,
+                                    unsigned long long* slots, int slot, bool leader_warp, int bar_id,
+                                    int bar_threads, int* err)
+{
+    const int lane = threadIdx.x & 31;
+    if (lane == 0) slots[slot] = best;
+    asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(bar_threads) : "memory");
     if (!leader_warp) return;
     unsigned done = 0;
     unsigned long long k = 0;
@@ -152,21 +207,13 @@ TMAC_DEV void top1_cta_finish(const XchgDev& xg, unsigned long long* top1, unsig
         if (xg.vocab) __threadfence_system();
         unsigned long long m = 0;
         for (int w = 0; w < bar_threads / 32; w++) m = slots[w] > m ? slots[w] : m;
-        if (!xg.partial) {
-            if (m) atomicMax(top1, m);
-        } else {
-            if (m) atomicMax(xg.partial, m);
-            // acquire-release count: each CTA's max is ordered before its
-            // increment, and the CTA that sees the last increment sees every max
-            asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(done) : "l"(xg.counter) : "memory");
-            if (done == gridDim.x - 1) {
-                k = atomicExch(xg.partial, 0ull);
-                atomicExch(xg.counter, 0u);
-                if (!xg.peers) *top1 = k;
-            }
+        if (m) atomicMax(xg.partial, m);
+        asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(done) : "l"(xg.counter) : "memory");
+        if (done == gridDim.x - 1) {
+            k = atomicExch(xg.partial, 0ull);
+            atomicExch(xg.counter, 0u);
         }
     }
-    if (!xg.partial || !xg.peers) return;
     done = __shfl_sync(0xffffffffu, done, 0);
     if (done != gridDim.x - 1) return;
     // what lane 0 acquired is ordered before the other lanes' exchange stores
