@@ -654,6 +654,44 @@ def main():
     kernel_us = ms / args.steps * 1e3  # one launch per step on this rank
     tm.lib().tmac_set_pdl(prev_pdl)
 
+    # At N > 1: this rank's shard GEMV alone (fused top-1 key, no exchange), timed
+    # the same way, so the line shows what the exchange adds to the step.
+    shard_alone = None
+    if world > 1:
+        la_us, la_failed, la_note = 0.0, 0.0, ""
+        la_pdl = tm.lib().tmac_set_pdl(0 if args.no_pdl else 1)  # as in the timed steps
+        try:
+            key_l = torch.zeros(1, dtype=torch.int64, device="cuda")
+            cap_l = torch.cuda.Stream()
+            cap_l.wait_stream(stream)
+            with torch.cuda.stream(cap_l):
+                for i in range(args.warmup):
+                    weights[i % ncopies].gemv_top1(x, y, key_l, index_base=r0, stream=cap_l)
+            torch.cuda.synchronize()
+            g_l = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g_l, stream=cap_l):
+                for i in range(50):
+                    weights[i % ncopies].gemv_top1(x, y, key_l, index_base=r0, stream=cap_l)
+            torch.cuda.synchronize()
+            g_l.replay()
+            torch.cuda.synchronize()
+            l0, l1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            l0.record(stream)
+            for _ in range(20):
+                g_l.replay()
+            l1.record(stream)
+            torch.cuda.synchronize()
+            la_us = l0.elapsed_time(l1) / 1000 * 1e3
+        except Exception as ex:  # reported, never fatal: the step above is the measurement
+            la_failed, la_note = 1.0, str(ex)[:200]
+        tm.lib().tmac_set_pdl(la_pdl)
+        la = torch.tensor([la_us, la_failed], dtype=torch.float64, device="cuda")
+        dist.all_reduce(la, op=dist.ReduceOp.MAX)
+        shard_alone = ({"error": la_note or "failed on another rank"} if la[1].item() > 0 else
+                       {"us_per_step": float(la[0].item()), "steps": 1000,
+                        "what": "this rank's shard GEMV with its top-1 key, no exchange (CUDA graph of 50, "
+                                "max over ranks); the step minus this is the exchange's cost"})
+
     # e2e: the public host-buffer entry (tmac_gemv_host): H2D x, GEMV, D2H y per step.
     xh = torch.from_numpy(synth.make_activations(HIDDEN, seed=0)).pin_memory()
     yh = torch.empty(rows, dtype=torch.float32).pin_memory()
@@ -720,6 +758,7 @@ def main():
                     "d2h_bytes_per_step": rows * 4, "api": "tmac_gemv_host", "steps": e2e_steps},
             "gpu_launches": args.steps * (2 if (merge is not None and not fused) else 1),
             "clocks": clocks,
+            "shard_alone": shard_alone,
             "decode": decode,
             "gemv_shapes": shapes,
             "prefill": prefill,
